@@ -1,0 +1,409 @@
+"""Benchmark: int8 TOPS of the W8A8 linear path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl xdna|reference] [--workload cfg2|square]
+
+One step = one pass of the hot path over one batch: BASELINE config 2's Qwen3-0.6B projection set at
+M = 8192 rows, bf16 activations, W8A8 -- xdna::linear_cat q/k/v (N = 2048+1024+1024, K = 1024),
+xdna::linear_cat gate/up (N = 2x3072, K = 1024) and xdna::linear down (N = 1024, K = 3072). Each op is
+our quantise kernel followed by our tcgen05 int8 GEMM with the dequantising epilogue. Metric: int8
+TOPS = 2*M*sum(N*K) per step / step time, whole job (all ranks).
+
+  value      device time of the K steps (CUDA events on the launching stream), inputs resident in HBM,
+             L2 flushed (a 256 MiB write) between steps, outside the events;
+  e2e        the same steps through the public API (torch.compile(backend="xdna")) with the inputs
+             copied from pinned host memory and every output copied back, inside the timed region;
+  roofline   the GEMM kernel alone: its algorithmic int8 ops per launch / its event-timed duration,
+             against the int8 peak (2x the measured dense bf16 cuBLAS rate in MEASURED_PEAKS.json --
+             B200's dense int8 rate is twice its bf16 rate);
+  cpu_baseline  the reference's CPU route (torch._int_mm + its eager quantise / dequantise ops),
+             restated in oracle/reference_cpu.py, on a bounded row sample, all host threads.
+
+--impl reference times only that CPU route, on rank 0, and prints its own line.
+Multi-GPU (torchrun): the linear does not shard (replicas only): every rank runs the whole workload,
+value = ranks x units / max-over-ranks time.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "torch-xdna_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+D, NQ, NKV, INTER = 1024, 2048, 1024, 3072
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="xdna", choices=["xdna", "reference"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "square"])
+    ap.add_argument("--rows", type=int, default=8192)
+    ap.add_argument("--cpu-rows", type=int, default=1024, help="row sample of the CPU baseline")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_init(n):
+    if n <= 1 and "RANK" not in os.environ:
+        return 0, 1
+    import datetime
+
+    import torch.distributed as dist
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return rank, world
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- workload
+class ProjectionSet(torch.nn.Module):
+    """The projections of one Qwen3-0.6B layer: q/k/v and gate/up share an input, down reads the MLP act."""
+
+    def __init__(self):
+        super().__init__()
+        self.q = torch.nn.Linear(D, NQ, bias=False)
+        self.k = torch.nn.Linear(D, NKV, bias=False)
+        self.v = torch.nn.Linear(D, NKV, bias=False)
+        self.gate = torch.nn.Linear(D, INTER, bias=False)
+        self.up = torch.nn.Linear(D, INTER, bias=False)
+        self.down = torch.nn.Linear(INTER, D, bias=False)
+
+    def forward(self, x, act):
+        return self.q(x), self.k(x), self.v(x), self.gate(x), self.up(x), self.down(act)
+
+
+def gemm_shapes(workload, rows):
+    if workload == "square":
+        return [(4096, 4096, 4096)]
+    return [(rows, NQ + 2 * NKV, D), (rows, 2 * INTER, D), (rows, D, INTER)]
+
+
+def make_model(dev):
+    g = torch.Generator().manual_seed(0)
+    m = ProjectionSet()
+    for p in m.parameters():
+        p.data = (torch.randn(p.shape, generator=g) * 0.02)
+    return m.to(dev, torch.bfloat16).eval()
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) of this GPU's clocks and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [num(r[0]) for r in self.rows if num(r[0])]
+        mx = [num(r[1]) for r in self.rows if num(r[1])]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[4:8]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------- the CPU baseline (reference route)
+def cpu_baseline(workload, rows_sample, budget_s=12.0):
+    """The reference's CPU route on a bounded row sample (oracle/reference_cpu.py), all host threads."""
+    from oracle import reference_cpu as rc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(1)
+    shapes = gemm_shapes(workload, rows_sample)
+    ops = []
+    for (m, n, k) in shapes:
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        w_kn, sw = rc.quant_weight(w)
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        ops.append((x, w_kn, sw))
+    with torch.no_grad():
+        for x, w_kn, sw in ops:           # warm-up
+            rc.linear_int8(x, w_kn, sw)
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            for x, w_kn, sw in ops:
+                rc.linear_int8(x, w_kn, sw)
+            times.append(time.perf_counter() - t0)
+    step = statistics.median(times)
+    work = sum(2 * m * n * k for m, n, k in shapes)
+    return {"value": round(work / step / 1e12, 4), "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{workload} projection set at {rows_sample} rows (of the workload's rows), "
+                      f"median of {len(times)} passes; torch._int_mm + eager quantise/dequantise (reference route)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    rows = args.cpu_rows if args.workload == "cfg2" else 4096
+    cb = cpu_baseline(args.workload, rows, budget_s=max(5.0, 0.5 * (args.steps + args.warmup)))
+    line = {"impl": "reference", "metric": metric_name(args.workload), "value": cb["value"], "unit": "TOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": config_of(args), "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(workload):
+    return "int8 TOPS/GPU, W8A8 linear (BASELINE config 2" + (" square 4096^3)" if workload == "square" else
+                                                               " Qwen3-0.6B projection set)")
+
+
+def config_of(args):
+    if args.workload == "square":
+        return {"workload": "cfg2 square int8 GEMM M=N=K=4096 (quantise + GEMM + dequantise to bf16)",
+                "l2": "flushed between steps"}
+    return {"workload": f"cfg2 Qwen3-0.6B projection set, W8A8, M={args.rows} rows bf16: linear_cat qkv "
+                        f"(N=4096,K=1024) + linear_cat gate/up (N=6144,K=1024) + linear down (N=1024,K=3072)",
+            "global_batch": args.rows, "parallelism": "replicas", "l2": "flushed between steps (256 MiB write)"}
+
+
+# ---------------------------------------------------------------- the B200 arm
+def run_xdna(args, rank, world):
+    import torch_xdna
+    from torch_xdna import kernels
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if not torch_xdna.gpu_available():
+        raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
+    torch.manual_seed(0)
+    cfg = torch_xdna.Config(verify="first", fallback="eager")
+    cid = torch_xdna.ops.config_id(cfg)
+    model = make_model(dev)
+    R = args.rows
+    x = torch.randn(R, D, device=dev).to(torch.bfloat16)
+    act = torch.randn(R, INTER, device=dev).to(torch.bfloat16)
+    if args.workload == "square":
+        w_sq = (torch.randn(4096, 4096, device=dev) * 0.02).to(torch.bfloat16)
+        x = torch.randn(4096, 4096, device=dev).to(torch.bfloat16)
+    shapes = gemm_shapes(args.workload, R)
+    work = sum(2 * m * n * k for m, n, k in shapes)
+
+    qkv = [model.q.weight, model.k.weight, model.v.weight]
+    gu = [model.gate.weight, model.up.weight]
+
+    def step():
+        if args.workload == "square":
+            return [torch.ops.xdna.linear(x, w_sq, None, False, cid)]
+        return [torch.ops.xdna.linear_cat(x, qkv, [None] * 3, cid), torch.ops.xdna.linear_cat(x, gu, [None] * 2, cid),
+                torch.ops.xdna.linear(act, model.down.weight, None, False, cid)]
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            step()
+        barrier(world)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        torch_xdna.stats.reset()
+        with ClockSampler(dev.index) as clocks:
+            barrier(world)
+            for i in range(args.steps):
+                flush.fill_(i & 0xFF)
+                starts[i].record(stream)
+                step()
+                ends[i].record(stream)
+            barrier(world)
+        launches = torch_xdna.stats.launches
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_s = max_over_ranks(sum(step_ms) / 1e3, world)
+    value = world * work * args.steps / total_s / 1e12
+
+    # ---- roofline: the GEMM kernel alone (same shapes, same stream), event-timed per launch
+    roof = gemm_roofline(shapes, dev, args.steps, flush)
+    # ---- e2e through torch.compile(backend="xdna") with host buffers
+    e2e = e2e_measure(args, model, dev, world, work)
+    # ---- CPU baseline (rank 0, one GPU only)
+    cb = cpu_baseline(args.workload, args.cpu_rows if args.workload == "cfg2" else 1024) \
+        if (rank == 0 and world == 1) else None
+    if kernels.take_device_error() != (0, 0):
+        raise SystemExit("a kernel recorded a device-side timeout")
+    if rank == 0:
+        line = {"metric": metric_name(args.workload), "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
+                "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(total_s * 1e3 / args.steps, 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)", "config": config_of(args),
+                "gpu_launches": launches, "roofline": roof, "e2e": e2e, "clocks": clocks.summary()}
+        if cb is not None:
+            line["cpu_baseline"] = cb
+        print(json.dumps(line), flush=True)
+
+
+def int8_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return 2 * float(d["bf16_tflops"]), "2x measured dense bf16 cuBLAS burst (MEASURED_PEAKS.json)"
+    return 2 * 1590.0, "2x fallback dense bf16 1.59 PFLOP/s"
+
+
+def gemm_roofline(shapes, dev, steps, flush):
+    """Algorithmic int8 ops per launch of the GEMM kernel / its CUDA-event duration, summed over the
+    workload's GEMMs; inputs pre-quantised, L2 flushed before every launch."""
+    from torch_xdna import kernels
+
+    cases = []
+    for (m, n, k) in shapes:
+        xq = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev)
+        wq = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev)
+        sx = torch.rand(m, device=dev) * 0.01
+        sw = torch.rand(n, device=dev) * 0.01
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        cases.append((xq, wq, k, y, sx, sw))
+    stream = torch.cuda.current_stream()
+    for c in cases:
+        for _ in range(3):
+            kernels.gemm_i8(c[0], c[1], c[2], c[3], c[4], c[5])
+    total_ms, total_ops = 0.0, 0
+    reps = max(5, steps)
+    for (m, n, k), c in zip(shapes, cases):
+        ms = []
+        for _ in range(reps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            kernels.gemm_i8(c[0], c[1], c[2], c[3], c[4], c[5])
+            e.record(stream)
+            e.synchronize()
+            ms.append(s.elapsed_time(e))
+        total_ms += statistics.median(ms)
+        total_ops += 2 * m * n * k
+    torch.cuda.synchronize()
+    peak, src = int8_peak()
+    achieved = total_ops / (total_ms / 1e3) / 1e12
+    return {"bound": "tensor", "kernel": "umma_gemm_kernel (gemm_i8, dequantising epilogue, bf16 out)",
+            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
+            "frac": round(achieved / peak, 4), "peak_source": src, "traffic": None,
+            "per_launch_ms": round(total_ms / len(shapes), 4)}
+
+
+def e2e_measure(args, model, dev, world, work):
+    """The step through torch.compile(backend="xdna"): pinned host inputs copied in, outputs copied out."""
+    import torch_xdna
+
+    if args.workload == "square":
+        return None
+    torch._dynamo.reset()
+    comp = torch.compile(model, backend="xdna", options={"fallback": "eager", "verify": "off"})
+    R = args.rows
+    hx = torch.randn(R, D).to(torch.bfloat16).pin_memory()
+    ha = torch.randn(R, INTER).to(torch.bfloat16).pin_memory()
+    outs_n = [NQ, NKV, NKV, INTER, INTER, D]
+    houts = [torch.empty(R, n, dtype=torch.bfloat16).pin_memory() for n in outs_n]
+    stream = torch.cuda.current_stream()
+
+    def one():
+        x = hx.to(dev, non_blocking=True)
+        a = ha.to(dev, non_blocking=True)
+        ys = comp(x, a)
+        for h, y in zip(houts, ys):
+            h.copy_(y, non_blocking=True)
+
+    with torch.no_grad():
+        for _ in range(3):
+            one()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = max(3, args.steps // 2)
+        s.record(stream)
+        for _ in range(steps):
+            one()
+        e.record(stream)
+        barrier(world)
+    sec = max_over_ranks(s.elapsed_time(e) / 1e3, world)
+    h2d = (hx.numel() + ha.numel()) * 2
+    d2h = sum(h.numel() for h in houts) * 2
+    return {"value": round(world * work * steps / sec / 1e12, 2), "unit": "TOPS", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "api": "torch.compile(backend='xdna', fallback='eager')"}
+
+
+def main():
+    args = parse()
+    rank, world = dist_init(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_xdna(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

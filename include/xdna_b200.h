@@ -1,0 +1,123 @@
+/* xdna_b200.h -- C ABI of libxdna_b200.so, the B200 (sm_100a) kernels behind torch_xdna's custom ops.
+ *
+ * Conventions (every entry point):
+ *   - returns XDNA_OK (0) or a negative XDNA_ERR_* code; xdna_last_error() then describes the
+ *     failure (thread-local, valid until the next call on the same thread);
+ *   - every pointer is caller-owned device memory on the current CUDA device, except where a
+ *     comment says "host";
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); calls only enqueue work and
+ *     never synchronise, except xdna_take_device_error();
+ *   - no entry point allocates device memory on its hot path; the only allocation the library
+ *     ever makes is nothing -- scratch is passed in by the caller;
+ *   - leading dimensions (`ld*`) are in elements; int8 operands read by TMA need their row
+ *     pitch in bytes to be a multiple of 16 and their base 16-byte aligned.
+ *
+ * The reference (AyaSakura-comp/torch-xdna) reaches its device through Python calls into
+ * Triton-XDNA; each entry point below names the reference call it replaces.
+ */
+#ifndef XDNA_B200_H
+#define XDNA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status codes */
+#define XDNA_OK 0
+#define XDNA_ERR_INVALID (-1)     /* bad argument: shape, stride, alignment, dtype, mode */
+#define XDNA_ERR_UNSUPPORTED (-2) /* a valid request this build does not implement */
+#define XDNA_ERR_CUDA (-3)        /* a CUDA runtime or driver call failed */
+#define XDNA_ERR_TIMEOUT (-4)     /* a bounded device-side wait gave up; the kernel returned early */
+#define XDNA_ERR_DEVICE (-5)      /* the current device is not an sm_100 (B200-class) GPU */
+
+/* ------------------------------------------------------------------ element types */
+#define XDNA_F32 0
+#define XDNA_BF16 1
+#define XDNA_F16 2
+#define XDNA_I32 3
+#define XDNA_I8 4
+#define XDNA_U8 5
+
+/* ------------------------------------------------------------------ conv3x3 modes */
+#define XDNA_CONV_Q 0         /* q = sat((acc + 2^(shift-1)) >> shift) as int8, or uint8 [0,255] with relu, NCHW */
+#define XDNA_CONV_DEQUANT 1   /* y = float(q) * (scale[co] * sx[n]) (+ bias[co]) in out_dtype, NCHW */
+#define XDNA_CONV_CALIBRATE 2 /* *acc_max = max over the sums of image 0 of (relu ? max(acc,0) : |acc|) */
+
+/* Last error of this thread, as text. */
+const char* xdna_last_error(void);
+
+/* ABI version of this library (bumped when a signature changes). */
+int xdna_abi_version(void);
+
+/* XDNA_OK when `device` is an sm_100 GPU this library's kernels run on. */
+int xdna_device_check(int device);
+
+/* Reads and clears the device-side error word that bounded waits write (code, site). Synchronises
+ * `stream`. *code is XDNA_OK when no kernel recorded an error since the last call. */
+int xdna_take_device_error(int* code, int* site, void* stream);
+
+/* ------------------------------------------------------------------ W8A8 linear
+ * Per-row symmetric int8 quantisation: for each row r of x [rows, cols] (leading dim ldx, dtype
+ * f32 / bf16 / f16): scale[r] = max(max_c |x[r,c]|, 1e-8) / 127 (the max taken in x's dtype),
+ * xq[r,c] = clamp(round_half_even(float(x[r,c]) / scale[r]), -127, 127). IEEE division, no FMA.
+ * Replaces R:torch_xdna/runtime.py:145-148 (_quant_rows), the quantise ops of
+ * R:torch_xdna/runtime.py:366-368 (linear_int8) and the weight quantisation of QWeight
+ * R:torch_xdna/runtime.py:59-66 (a weight is quantised as rows of [N, K]). */
+int xdna_quant_rows_i8(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx, int8_t* xq,
+                       int64_t ldq, float* scale, void* stream);
+
+/* acc[M,N] = xq[M,K] . wq[N,K]^T in int32 on the tcgen05 tensor cores (both operands K-major).
+ * y_dtype XDNA_I32: y receives acc (sx, sw, bias ignored).
+ * y_dtype XDNA_F32 / XDNA_BF16 / XDNA_F16: y = (float(acc) * sx[m]) * sw[n] (+ float(bias[n])),
+ *   rounded once to y_dtype (round to nearest even) -- the reference's dequantise order.
+ * bias may be NULL; bias_dtype is its element type.
+ * Replaces kernels.mm_i8 R:torch_xdna/kernels.py:172-192 as called by _npu_acc
+ * R:torch_xdna/runtime.py:191-209 (and the CPU route torch._int_mm, R:torch_xdna/runtime.py:162-163),
+ * fused with the dequantisation of R:torch_xdna/runtime.py:350-353, :370-374 and :429-432. */
+int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                 const float* sx, const float* sw, const void* bias, int bias_dtype, void* y, int y_dtype,
+                 int64_t ldy, void* stream);
+
+/* ------------------------------------------------------------------ conv3x3
+ * The implicit-GEMM conv reads activations as a zero-bordered NHWC int8 tensor
+ * xp [N, H+2, W+2, Cp] (Cp = channels rounded up to a multiple of 16, pad channels zero), and
+ * weights as wp [Co, 9, Cp] int8 (tap = 3*ky + kx, pad channels zero). */
+
+/* Per-image quantisation fused with the layout change: for image n of x [N, C, H, W] (NCHW,
+ * contiguous, f32 / bf16 / f16): sx[n] = max(max |x[n]|, 1e-8) / 127, and xp gets
+ * clamp(round_half_even(float(x) / sx[n]), -127, 127) inside a zero border.
+ * amax_scratch: N uint32 words of scratch this call clears and uses.
+ * Replaces the quantise ops of conv3x3_int8, R:torch_xdna/conv.py:45-46, and the host-side
+ * NCHW -> NPU layout packing of Triton-XDNA's conv3x3 host code. */
+int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,
+                         int64_t Cp, float* sx, uint32_t* amax_scratch, void* stream);
+
+/* NCHW int8 xq [N, C, H, W] (the xdna::conv3x3 op's input) -> bordered NHWC xp as above. */
+int xdna_conv_pack_input(const int8_t* xq, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp, int64_t Cp,
+                         void* stream);
+
+/* int8 weights wq [Co, Ci, 3, 3] (contiguous) -> wp [Co, 9, Cp]. */
+int xdna_conv_pack_weight(const int8_t* wq, int64_t Co, int64_t Ci, int8_t* wp, int64_t Cp, void* stream);
+
+/* 3x3 / stride 1 / padding 1 conv of xp by wp on the int8 tensor cores, int32 sums, and one of the
+ * epilogues XDNA_CONV_Q / XDNA_CONV_DEQUANT / XDNA_CONV_CALIBRATE (see above). Rounding of the
+ * requantise is round half up via an arithmetic shift, then saturation: [-128,127] int8, or
+ * [0,255] uint8 when relu != 0. Output `out` is NCHW [N, Co, H, W] in out_dtype (XDNA_I8 / XDNA_U8
+ * for XDNA_CONV_Q; XDNA_F32 / XDNA_BF16 / XDNA_F16 for XDNA_CONV_DEQUANT). For XDNA_CONV_CALIBRATE
+ * only image 0 is computed and acc_max (one int32, cleared by this call) receives the maximum.
+ * Replaces tl.extra.npu.conv3x3.Conv3x3(...)(xq) as used by ConvLayer.npu
+ * R:torch_xdna/conv.py:334-340,350-359, the CPU integers ConvLayer.cpu R:torch_xdna/conv.py:345-348,
+ * the calibration sums of ConvLayer.calibrate R:torch_xdna/conv.py:327-332, and (DEQUANT) the
+ * dequantise ops of conv3x3_int8 R:torch_xdna/conv.py:47-50. */
+int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, int64_t Cp, int64_t Co, int64_t H,
+                    int64_t W, int mode, int shift, int relu, const float* scale, const float* sx, const void* bias,
+                    int bias_dtype, void* out, int out_dtype, int32_t* acc_max, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XDNA_B200_H */

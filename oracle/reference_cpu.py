@@ -1,0 +1,66 @@
+"""The reference's CPU route, restated with the same torch CPU calls -- TEST / BASELINE INFRASTRUCTURE.
+
+Used as `bench.py --impl reference` and as the cpu_baseline leg: it times what the reference runs with
+policy="cpu" on the host cores (torch._int_mm on oneDNN, eager quantise / dequantise ops; the conv's
+exact fp conv of the integers), because the reference package itself is not present on the GPU box.
+Only tests/, __graft_entry__.smoke() and bench.py's baseline legs may import this module.
+Pinned against the reference's golden vectors by tests/test_oracle.py::test_reference_cpu_port_*.
+"""
+
+import math
+
+import torch
+
+
+def quant_rows(x2d):
+    """R:torch_xdna/runtime.py:366-368."""
+    sx = x2d.abs().amax(dim=1, keepdim=True).float().clamp(min=1e-8) / 127
+    xq = torch.round(x2d.float() / sx).clamp(-127, 127).to(torch.int8)
+    return xq, sx
+
+
+def quant_weight(w):
+    """QWeight, R:torch_xdna/runtime.py:59-66: (w_kn [K, N] int8 for torch._int_mm, sw [N])."""
+    wf = w.detach().float()
+    sw = wf.abs().amax(dim=1).clamp(min=1e-8) / 127
+    q = torch.round(wf / sw[:, None]).clamp(-127, 127).to(torch.int8)
+    return q.t().contiguous(), sw
+
+
+def linear_int8(x, w_kn, sw, bias=None):
+    """The W8A8 linear of R:torch_xdna/runtime.py:366-374 with a quantised weight."""
+    x2 = x.reshape(-1, x.shape[-1])
+    xq, sx = quant_rows(x2)
+    acc = torch._int_mm(xq, w_kn)
+    y = acc.float() * sx * sw
+    if bias is not None:
+        y = y + bias.float()
+    return y.to(x.dtype).reshape(*x.shape[:-1], y.shape[-1])
+
+
+def conv_layer(weight, relu):
+    """ConvLayer weights, R:torch_xdna/conv.py:314-319."""
+    wf = weight.detach().float()
+    sw = wf.abs().amax(dim=(1, 2, 3)).clamp(min=1e-8) / 127
+    wq = torch.round(wf / sw[:, None, None, None]).clamp(-127, 127).to(torch.int8)
+    dt = torch.float32 if 127 * float(wq.abs().sum(dim=(1, 2, 3)).max()) < 2 ** 24 else torch.float64
+    return dict(wq=wq, sw=sw, dt=dt, relu=relu, shift=None)
+
+
+def conv3x3_int8(x, layer, bias=None):
+    """conv3x3_int8 on the CPU route, R:torch_xdna/conv.py:43-51,327-348."""
+    sx = x.abs().amax(dim=(1, 2, 3), keepdim=True).float().clamp(min=1e-8) / 127
+    xq = torch.round(x.float() / sx).clamp(-127, 127).to(torch.int8)
+    acc = torch.nn.functional.conv2d(xq.to(layer["dt"]), layer["wq"].to(layer["dt"]), padding=1).to(torch.int32)
+    if layer["shift"] is None:
+        a0 = acc[0]
+        top = float(a0.clamp(min=0).max()) if layer["relu"] else float(a0.abs().max())
+        layer["shift"] = min(31, max(1, math.ceil(math.log2(max(top * 1.25, 1.0) / (255 if layer["relu"] else 127)))))
+    s = layer["shift"]
+    q = (acc + (1 << (s - 1))) >> s
+    q = q.clamp_(0, 255).to(torch.uint8) if layer["relu"] else q.clamp_(-128, 127).to(torch.int8)
+    scale = layer["sw"] * 2.0 ** s
+    y = q.float() * (scale.view(1, -1, 1, 1) * sx)
+    if bias is not None:
+        y = y + bias.float().view(1, -1, 1, 1)
+    return y.to(x.dtype)

@@ -1,0 +1,167 @@
+"""Host logic without a GPU: the FX pass (which nodes become which xdna:: op), shared-input fusion, the
+conv pass and its ReLU fusion, Config validation, and the loud failure without a B200
+(mirrors R:tests/test_backend.py case_fusion / case_conv_pass / case_no_npu, by graph inspection)."""
+
+import copy
+
+import pytest
+import torch
+
+import torch_xdna
+from torch_xdna import kernels
+from torch_xdna.conv import conv3x3_int8
+
+
+def capture_graphs(model, x, cfg):
+    """Run Dynamo on `model` and return the rewritten FX graphs (the model itself runs eagerly)."""
+    graphs = []
+
+    def backend(gm, example_inputs):
+        original = torch.fx.GraphModule(gm, copy.deepcopy(gm.graph))
+        torch_xdna.offload_gemms(gm, example_inputs, cfg)
+        graphs.append(gm)
+        return original.forward
+
+    torch._dynamo.reset()
+    with torch.no_grad():
+        torch.compile(model, backend=backend)(x)
+    return graphs
+
+
+def call_targets(gm):
+    return [n.target for n in gm.graph.nodes if n.op == "call_function"]
+
+
+class Net(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.a = torch.nn.Linear(200, 300)
+        self.b = torch.nn.Linear(300, 1024, bias=False)
+        self.w = torch.nn.Parameter(torch.randn(1024, 520) * 0.03)
+
+    def forward(self, x):
+        h = torch.nn.functional.gelu(self.a(x))
+        h = torch.nn.functional.silu(self.b(h))
+        return h @ self.w
+
+
+class Attn(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.q = torch.nn.Linear(256, 256)
+        self.k = torch.nn.Linear(256, 128, bias=False)
+        self.v = torch.nn.Linear(256, 128)
+        self.o = torch.nn.Linear(256, 256)
+
+    def forward(self, x):
+        q, k, v = self.q(x), self.k(x), self.v(x)
+        return self.o(q * torch.cat([k, v], -1).sigmoid())
+
+
+class CNN(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.c1 = torch.nn.Conv2d(64, 128, 3, padding=1)
+        self.c2 = torch.nn.Conv2d(128, 128, 3, padding=1, bias=False)
+        self.c3 = torch.nn.Conv2d(128, 32, 3, padding="same")
+        self.down = torch.nn.Conv2d(32, 32, 3, stride=2, padding=1)
+
+    def forward(self, x):
+        h = torch.relu(self.c1(x))
+        h = torch.relu(self.c2(h))
+        return self.down(self.c3(h))
+
+
+class AddmmNet(torch.nn.Module):
+    """HF Conv1D-style b + x @ W, plus a GEMM between two activations that must stay."""
+
+    def __init__(self):
+        super().__init__()
+        self.w = torch.nn.Parameter(torch.randn(64, 96))
+        self.b = torch.nn.Parameter(torch.randn(96))
+
+    def forward(self, x):
+        h = torch.addmm(self.b, x, self.w)
+        return h @ h.t()
+
+
+def test_linear_patterns_rewritten():
+    (gm,) = capture_graphs(Net().eval(), torch.randn(37, 200), torch_xdna.Config())
+    targets = call_targets(gm)
+    lin = [n for n in gm.graph.nodes if n.op == "call_function" and n.target is torch.ops.xdna.linear.default]
+    assert len(lin) == 3
+    assert [n.args[3] for n in lin] == [False, False, True]      # F.linear, F.linear, h @ W
+    assert torch.nn.functional.linear not in targets
+
+
+def test_addmm_rewritten_activation_gemm_left():
+    (gm,) = capture_graphs(AddmmNet(), torch.randn(8, 64), torch_xdna.Config())
+    lin = [n for n in gm.graph.nodes if n.op == "call_function" and n.target is torch.ops.xdna.linear.default]
+    assert len(lin) == 1 and lin[0].args[3] is True and lin[0].args[2] is not None
+    remaining = [n for n in gm.graph.nodes if n.op in ("call_function", "call_method")
+                 and (n.target in (torch.matmul, torch.mm) or n.target in ("matmul", "mm", "__matmul__")
+                      or getattr(n.target, "__name__", "") == "matmul")]
+    assert remaining, "the activation x activation GEMM must not be offloaded"
+
+
+def test_shared_input_fusion():
+    (gm,) = capture_graphs(Attn().eval(), torch.randn(20, 256), torch_xdna.Config())
+    targets = call_targets(gm)
+    assert targets.count(torch.ops.xdna.linear_cat.default) == 1
+    assert targets.count(torch.ops.xdna.linear.default) == 1        # o
+    assert targets.count(torch.narrow) == 3
+    cat = next(n for n in gm.graph.nodes if n.target is torch.ops.xdna.linear_cat.default)
+    assert len(cat.args[1]) == 3 and [b is None for b in cat.args[2]] == [False, True, False]
+    (gm2,) = capture_graphs(Attn().eval(), torch.randn(20, 256), torch_xdna.Config(fuse=False))
+    assert call_targets(gm2).count(torch.ops.xdna.linear.default) == 4
+
+
+def test_conv_pass_which_convs_and_relu():
+    """3 of 4 convs rewritten; only the bias-free conv's ReLU fused; stride 2 left alone
+    (R:tests/test_backend.py:220-240)."""
+    (gm,) = capture_graphs(CNN().eval(), torch.randn(1, 64, 16, 64), torch_xdna.Config(policy="npu"))
+    nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
+    convs = [n for n in nodes if n.target is conv3x3_int8]
+    assert [n.args[3] for n in convs] == [False, True, False], [n.args for n in convs]
+    assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes) == 1
+    assert sum(n.target is torch.conv2d for n in nodes) == 1
+
+
+def test_policy_cpu_rewrites_nothing_and_runs():
+    torch._dynamo.reset()
+    net = Net().eval()
+    x = torch.randn(5, 200)
+    m = torch.compile(net, backend="xdna", options={"policy": "cpu", "fallback": "eager"})
+    with torch.no_grad():
+        assert torch.equal(m(x), net(x))
+
+
+def test_config_validation():
+    c = torch_xdna.Config().merged({"row_buckets": [512, 128], "policy": "npu"})
+    assert c.row_buckets == (128, 512) and c.policy == "npu"
+    with pytest.raises(AssertionError, match="unknown xdna options"):
+        torch_xdna.Config().merged({"polcy": "npu"})
+    with pytest.raises(AssertionError):
+        torch_xdna.Config(policy="gpu")
+    with pytest.raises(AssertionError):
+        torch_xdna.Config(verify="sometimes")
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the behaviour without a GPU")
+def test_no_gpu_fails_loudly():
+    assert not torch_xdna.gpu_available()
+    assert kernels.unavailable_reason()
+    torch._dynamo.reset()
+    m = torch.compile(Net().eval(), backend="xdna")
+    with pytest.raises(Exception, match="B200|CUDA"):
+        with torch.no_grad():
+            m(torch.randn(4, 200))
+    with pytest.raises(kernels.XdnaUnavailable):
+        kernels.require()
+
+
+def test_report_formats():
+    torch_xdna.stats.reset()
+    s = torch_xdna.report()
+    assert s.startswith("B200 available:")
+    assert '"calls"' in torch_xdna.report(as_json=True)

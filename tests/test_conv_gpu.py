@@ -1,0 +1,149 @@
+"""int8 conv3x3 on the B200 vs the oracle (bit-exact): calibration shift, requantised integers (int8 /
+uint8 with ReLU), the fused quantise -> conv -> dequantise, the backend's conv pass, and the golden
+digests recorded from the reference's CPU integers."""
+
+import numpy as np
+import pytest
+import torch
+
+import make_golden as mg
+from oracle import xdna_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def t(a, dev, dtype=None):
+    x = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return x.to(dtype) if dtype is not None else x
+
+
+def _cid(**kw):
+    import torch_xdna
+
+    return torch_xdna.ops.config_id(torch_xdna.Config(**kw))
+
+
+@pytest.mark.parametrize("name", [c[0] for c in mg.CONV_CASES])
+def test_conv_op_matches_reference_digests(cuda, golden, name):
+    manifest, _ = golden
+    ent = manifest["conv"][name]
+    x, w, b = mg.conv_inputs(ent["seed"], ent["N"], ent["Ci"], ent["Co"], ent["H"], ent["W"], bias=ent["bias"])
+    xq, sx = orc.conv_quant(x)
+    weight = torch.nn.Parameter(t(w, cuda))
+    q, scale = torch.ops.xdna.conv3x3(t(xq, cuda), weight, ent["relu"], _cid(verify="off"))
+    from torch_xdna import conv as xconv
+
+    layer = xconv._layer(weight, ent["H"], ent["W"], ent["relu"])
+    assert layer.shift == ent["shift"], (layer.shift, ent["shift"])
+    assert mg.sha(q.cpu().numpy()) == ent["q_sha"], "requantised integers differ from the reference's"
+    assert mg.sha(scale.cpu().numpy()) == ent["scale_sha"]
+    # the fused path (quantise + conv + dequantise) on the same layer
+    y = torch.ops.xdna.conv3x3_fused(t(x, cuda), weight, t(b, cuda) if b is not None else None, ent["relu"],
+                                     _cid(verify="off"))
+    assert mg.sha(y.cpu().numpy()) == ent["y_sha"], "dequantised output differs from the reference's"
+
+
+@pytest.mark.parametrize("relu", [False, True])
+@pytest.mark.parametrize("n,ci,co,h,w", [(1, 256, 256, 64, 64), (2, 3, 64, 13, 37), (2, 64, 48, 13, 37),
+                                         (1, 16, 16, 1, 1), (3, 130, 20, 7, 129), (1, 512, 512, 14, 14),
+                                         (2, 64, 64, 224, 224)])
+def test_conv_q_bitexact_vs_oracle(cuda, relu, n, ci, co, h, w):
+    x, wt, _ = mg.conv_inputs(n * 1000 + ci + co + h, n, ci, co, h, w)
+    want = orc.conv3x3_int8(x, wt, None, relu=relu)
+    weight = torch.nn.Parameter(t(wt, cuda))
+    q, scale = torch.ops.xdna.conv3x3(t(want["xq"], cuda), weight, relu, _cid(verify="off"))
+    from torch_xdna import conv as xconv
+
+    assert xconv._layer(weight, h, w, relu).shift == want["shift"]
+    got = q.cpu().numpy()
+    bad = int((got != want["q"]).sum())
+    assert bad == 0, f"{bad} of {got.size} requantised values differ"
+    assert np.array_equal(scale.cpu().numpy(), want["scale"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_conv_fused_dequant_bitexact(cuda, dtype):
+    x, wt, b = mg.conv_inputs(5, 2, 96, 80, 30, 50, bias=True)
+    xd = orc.cast(x, "bfloat16") if dtype == torch.bfloat16 else x
+    want = orc.conv3x3_int8(xd, wt, b, relu=False, x_dtype="bfloat16" if dtype == torch.bfloat16 else "float32")
+    weight = torch.nn.Parameter(t(wt, cuda))
+    y = torch.ops.xdna.conv3x3_fused(t(xd, cuda, dtype), weight, t(b, cuda), False, _cid(verify="off"))
+    assert np.array_equal(y.float().cpu().numpy(), want["y"])
+
+
+def test_cfg3_chain_matches_reference(cuda, golden):
+    """4 x (conv3x3 256->256 + fused ReLU) on 1x256x64x64; shifts and every layer's
+    integers equal the reference's."""
+    manifest, _ = golden
+    ent = manifest["conv"]["cfg3_chain"]
+    g = mg.rng(ent["seed"])
+    x = g.standard_normal((1, 256, 64, 64), dtype=np.float32)
+    ws = [g.standard_normal((256, 256, 3, 3), dtype=np.float32) * np.float32(np.sqrt(2.0 / (256 * 9)))
+          for _ in range(4)]
+    from torch_xdna import conv as xconv
+
+    h = t(x, cuda)
+    cid = _cid(verify="off")
+    for i, w in enumerate(ws):
+        weight = torch.nn.Parameter(t(w, cuda))
+        h = torch.ops.xdna.conv3x3_fused(h, weight, None, True, cid)
+        assert xconv._layer(weight, 64, 64, True).shift == ent["shifts"][i]
+    assert mg.sha(h.cpu().numpy()) == ent["y_sha"]
+
+
+def test_conv_verify_first(cuda):
+    import torch_xdna
+
+    torch_xdna.stats.reset()
+    x, wt, _ = mg.conv_inputs(9, 1, 32, 32, 20, 20)
+    weight = torch.nn.Parameter(t(wt, cuda))
+    cid = _cid(verify="first")
+    torch.ops.xdna.conv3x3_fused(t(x, cuda), weight, None, True, cid)
+    torch.ops.xdna.conv3x3_fused(t(x, cuda), weight, None, True, cid)
+    checks = torch_xdna.stats.as_dict()["checks"]
+    assert len(checks) == 1 and "bitwise" in checks[0][1]
+
+
+class CNN(torch.nn.Module):
+    """R:tests/test_backend.py:203-217: bias + ReLU, bias-free + ReLU (fused), "same", a stride-2 conv."""
+
+    def __init__(self):
+        super().__init__()
+        self.c1 = torch.nn.Conv2d(64, 128, 3, padding=1)
+        self.c2 = torch.nn.Conv2d(128, 128, 3, padding=1, bias=False)
+        self.c3 = torch.nn.Conv2d(128, 32, 3, padding="same")
+        self.down = torch.nn.Conv2d(32, 32, 3, stride=2, padding=1)
+
+    def forward(self, x):
+        h = torch.relu(self.c1(x))
+        h = torch.relu(self.c2(h))
+        return self.down(self.c3(h))
+
+
+def test_compiled_cnn(cuda):
+    """3 of 4 convs on the B200 (the stride-2 one stays), close to fp32; each layer's integers equal the
+    oracle's on the same quantised input."""
+    import torch_xdna
+
+    torch.manual_seed(0)
+    net = CNN().eval().to(cuda)
+    x = torch.randn(2, 64, 32, 64, device=cuda)
+    torch._dynamo.reset()
+    torch_xdna.stats.reset()
+    m = torch.compile(net, backend="xdna", options={"fallback": "eager"})
+    with torch.no_grad():
+        y, ref = m(x), net(x)
+    s = torch_xdna.stats.as_dict()
+    assert s["calls"] == {"gpu": 3}, s
+    err = ((y - ref).norm() / ref.norm()).item()
+    assert err < 0.05, err
+    # layer by layer against the oracle (c1 with bias, its ReLU separate; c2 ReLU fused; c3 plain)
+    xs = x.cpu().numpy()
+    r1 = orc.conv3x3_int8(xs, net.c1.weight.detach().cpu().numpy(), net.c1.bias.detach().cpu().numpy(), relu=False)
+    h = np.maximum(r1["y"], 0)
+    r2 = orc.conv3x3_int8(h, net.c2.weight.detach().cpu().numpy(), None, relu=True)
+    r3 = orc.conv3x3_int8(r2["y"], net.c3.weight.detach().cpu().numpy(), net.c3.bias.detach().cpu().numpy(),
+                          relu=False)
+    with torch.no_grad():
+        want = net.down(torch.from_numpy(r3["y"]).to(cuda))
+    assert torch.equal(y, want)

@@ -1,0 +1,145 @@
+// Library-wide entry points and host helpers: last error, device checks, the device error word
+// that bounded waits write, and TMA tensor-map encoding.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+
+#include "host_util.h"
+
+namespace xdna {
+
+// The device error word: code, site, block, count. Written by kernels whose bounded waits ran out;
+// read and cleared by xdna_take_device_error(). A file-scope __device__ array: every GPU that loads
+// the library holds its own copy, and no allocation is needed to reach it.
+__device__ int g_device_error[4];
+
+static thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_mutex;
+int g_sm_count[kMaxDevices];    // 0 = unchecked, -1 = not an sm_100 device
+int* g_err_ptr[kMaxDevices];
+}  // namespace
+
+int check_device(int* sm_count) {
+  int dev = 0;
+  XDNA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(XDNA_ERR_DEVICE, "device ordinal %d out of range", dev);
+  int sms = g_sm_count[dev];
+  if (sms == 0) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    cudaDeviceProp prop;
+    XDNA_CUDA(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10) {
+      g_sm_count[dev] = -1;
+      return fail(XDNA_ERR_DEVICE, "device %d (%s) is sm_%d%d; these kernels need sm_100a (B200)", dev, prop.name,
+                  prop.major, prop.minor);
+    }
+    void* p = nullptr;
+    XDNA_CUDA(cudaGetSymbolAddress(&p, g_device_error));
+    g_err_ptr[dev] = static_cast<int*>(p);
+    g_sm_count[dev] = sms = prop.multiProcessorCount;
+  }
+  if (sms < 0) return fail(XDNA_ERR_DEVICE, "device %d is not an sm_100 GPU", dev);
+  if (sm_count) *sm_count = sms;
+  return XDNA_OK;
+}
+
+int* device_error_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  return g_err_ptr[dev];
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(XDNA_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(e));
+  return XDNA_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int encode_tma(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(XDNA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned16(base)) return fail(XDNA_ERR_INVALID, "%s: base address is not 16-byte aligned", what);
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) {
+    if (strides_bytes[i] % 16 != 0)
+      return fail(XDNA_ERR_INVALID, "%s: row pitch %llu bytes is not a multiple of 16", what,
+                  (unsigned long long)strides_bytes[i]);
+    s[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(XDNA_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return XDNA_OK;
+}
+
+}  // namespace xdna
+
+extern "C" {
+
+const char* xdna_last_error(void) { return xdna::t_last_error.c_str(); }
+
+int xdna_abi_version(void) { return 1; }
+
+int xdna_device_check(int device) {
+  int cur = 0;
+  XDNA_CUDA(cudaGetDevice(&cur));
+  if (cur != device) XDNA_CUDA(cudaSetDevice(device));
+  int rc = xdna::check_device(nullptr);
+  if (cur != device) cudaSetDevice(cur);
+  return rc;
+}
+
+int xdna_take_device_error(int* code, int* site, void* stream) {
+  int rc = xdna::check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  int* word = xdna::device_error_word();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host[4] = {0, 0, 0, 0};
+  XDNA_CUDA(cudaMemcpyAsync(host, word, sizeof(host), cudaMemcpyDeviceToHost, s));
+  XDNA_CUDA(cudaStreamSynchronize(s));
+  if (host[0] != 0) XDNA_CUDA(cudaMemsetAsync(word, 0, sizeof(host), s));
+  XDNA_CUDA(cudaStreamSynchronize(s));
+  if (code) *code = host[0];
+  if (site) *site = host[1];
+  return XDNA_OK;
+}
+
+}  // extern "C"

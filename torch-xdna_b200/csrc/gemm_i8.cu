@@ -1,0 +1,198 @@
+// xdna_gemm_i8 and xdna_conv3x3_i8: host side of the tcgen05 int8 GEMM (umma_gemm.cuh).
+#include <algorithm>
+
+#include "host_util.h"
+#include "umma_gemm.cuh"
+
+namespace xdna {
+
+template <int BN, int LOAD, int EPI>
+static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int sms,
+                       cudaStream_t stream) {
+  constexpr int smem = smem_bytes_for<BN>();
+  auto kern = umma_gemm_kernel<BN, LOAD, EPI, false>;
+  static bool configured[64] = {};  // per instantiation and device
+  int dev = 0;
+  XDNA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    XDNA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const int tiles = args.m_tiles * args.n_tiles;
+  const int grid = std::max(1, std::min(tiles, sms));
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, args);
+  return check_launch("umma_gemm_kernel");
+}
+
+template <int LOAD, int EPI>
+static int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int sms,
+                       cudaStream_t stream) {
+  switch (bn) {
+    case 256:
+      return launch_umma<256, LOAD, EPI>(ta, tb, args, sms, stream);
+    case 128:
+      return launch_umma<128, LOAD, EPI>(ta, tb, args, sms, stream);
+    default:
+      return launch_umma<64, LOAD, EPI>(ta, tb, args, sms, stream);
+  }
+}
+
+// Widest tile that still gives every SM work; 64 for narrow outputs.
+static int choose_bn(int64_t m_tiles, int64_t N, int sms) {
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  if (m_tiles * ((N + 255) / 256) >= sms) return 256;
+  if (m_tiles * ((N + 127) / 128) >= sms) return 128;
+  return N >= 1024 ? 64 : 128;
+}
+
+}  // namespace xdna
+
+using namespace xdna;
+
+extern "C" {
+
+int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                 const float* sx, const float* sw, const void* bias, int bias_dtype, void* y, int y_dtype,
+                 int64_t ldy, void* stream) {
+  int sms = 0;
+  int rc = check_device(&sms);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "gemm_i8: negative size");
+  XDNA_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_i8: size exceeds 2^31");
+  XDNA_CHECK_ARG(ldx >= K && ldw >= K && ldy >= N, "gemm_i8: leading dimension smaller than the row");
+  XDNA_CHECK_ARG(y_dtype == XDNA_I32 || is_float_dtype(y_dtype), "gemm_i8: y_dtype %d unsupported", y_dtype);
+  if (M == 0 || N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(xq && wq && y, "gemm_i8: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) {  // empty sum: zeros (dequantised zeros are bias)
+    if (y_dtype == XDNA_I32 && ldy == N) {
+      XDNA_CUDA(cudaMemsetAsync(y, 0, M * N * sizeof(int32_t), s));
+      return XDNA_OK;
+    }
+    return fail(XDNA_ERR_UNSUPPORTED, "gemm_i8: K == 0 is only supported for a dense int32 output");
+  }
+  if (y_dtype != XDNA_I32) {
+    XDNA_CHECK_ARG(sx && sw, "gemm_i8: dequantised output needs sx and sw");
+    XDNA_CHECK_ARG(bias == nullptr || is_float_dtype(bias_dtype), "gemm_i8: bias dtype %d", bias_dtype);
+  }
+  XDNA_CHECK_ARG(ldx % 16 == 0 && ldw % 16 == 0, "gemm_i8: int8 row pitch must be a multiple of 16 bytes");
+
+  GemmArgs a{};
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.num_kb = static_cast<int>((K + kBKBytes - 1) / kBKBytes);
+  a.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  const int bn = choose_bn(a.m_tiles, N, sms);
+  a.n_tiles = static_cast<int>((N + bn - 1) / bn);
+  a.out = y;
+  a.ldo = ldy;
+  a.out_dtype = y_dtype;
+  const int es = dtype_size(y_dtype);
+  a.vec_ok = aligned16(y) && (ldy * es) % 16 == 0;
+  a.sx = sx;
+  a.sw = sw;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.err = device_error_word();
+
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldx)};
+    const uint32_t box[2] = {kBKBytes, kBM};
+    rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, strides, box, "gemm_i8 activations");
+    if (rc != XDNA_OK) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldw)};
+    const uint32_t box[2] = {kBKBytes, static_cast<uint32_t>(bn)};
+    rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, wq, dims, strides, box, "gemm_i8 weights");
+    if (rc != XDNA_OK) return rc;
+  }
+  if (y_dtype == XDNA_I32) return dispatch_bn<LOAD_GEMM, EPI_I32>(bn, ta, tb, a, sms, s);
+  return dispatch_bn<LOAD_GEMM, EPI_DEQ>(bn, ta, tb, a, sms, s);
+}
+
+int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, int64_t Cp, int64_t Co, int64_t H,
+                    int64_t W, int mode, int shift, int relu, const float* scale, const float* sx, const void* bias,
+                    int bias_dtype, void* out, int out_dtype, int32_t* acc_max, void* stream) {
+  int sms = 0;
+  int rc = check_device(&sms);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && Ci >= 1 && Co >= 1 && H >= 1 && W >= 1, "conv3x3: bad shape");
+  XDNA_CHECK_ARG(Cp >= Ci && Cp % 16 == 0, "conv3x3: Cp must be >= Ci and a multiple of 16");
+  XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE,
+                 "conv3x3: unknown mode %d", mode);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (mode == XDNA_CONV_CALIBRATE) {
+    XDNA_CHECK_ARG(acc_max != nullptr, "conv3x3: calibration needs acc_max");
+    XDNA_CUDA(cudaMemsetAsync(acc_max, 0, sizeof(int32_t), s));
+    if (N == 0) return XDNA_OK;
+    N = 1;  // the shift is fixed from the first image's sums
+  } else {
+    XDNA_CHECK_ARG(shift >= 1 && shift <= 31, "conv3x3: shift %d outside [1, 31]", shift);
+    XDNA_CHECK_ARG(scale != nullptr || mode == XDNA_CONV_Q, "conv3x3: dequantise needs scale");
+    if (mode == XDNA_CONV_Q)
+      XDNA_CHECK_ARG(out_dtype == (relu ? XDNA_U8 : XDNA_I8), "conv3x3: requantised output is %s",
+                     relu ? "uint8 with relu" : "int8 without relu");
+    else
+      XDNA_CHECK_ARG(is_float_dtype(out_dtype) && sx != nullptr, "conv3x3: dequantise needs a float out and sx");
+    if (N == 0) return XDNA_OK;
+    XDNA_CHECK_ARG(out != nullptr, "conv3x3: null output");
+  }
+  XDNA_CHECK_ARG(xp && wp, "conv3x3: null pointer");
+  const int64_t Wp = W + 2, HWp = (H + 2) * (W + 2);
+  const int64_t NP = N * HWp;
+  XDNA_CHECK_ARG(NP < (1ll << 31) && Co * Cp * 9 < (1ll << 31), "conv3x3: problem exceeds 2^31 elements");
+
+  GemmArgs a{};
+  a.M = static_cast<int>(NP);
+  a.N = static_cast<int>(Co);
+  a.cblocks = static_cast<int>((Cp + kBKBytes - 1) / kBKBytes);
+  a.num_kb = 9 * a.cblocks;
+  a.m_tiles = static_cast<int>((NP + kBM - 1) / kBM);
+  const int bn = choose_bn(a.m_tiles, Co, sms);
+  a.n_tiles = static_cast<int>((Co + bn - 1) / bn);
+  a.Wp = static_cast<int>(Wp);
+  a.HWp = static_cast<int>(HWp);
+  a.H = static_cast<int>(H);
+  a.W = static_cast<int>(W);
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.sx = sx;
+  a.sw = scale;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.shift = shift;
+  a.relu = relu ? 1 : 0;
+  a.acc_max = acc_max;
+  a.err = device_error_word();
+
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(NP)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(Cp)};
+    const uint32_t box[2] = {kBKBytes, kBM};
+    rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations");
+    if (rc != XDNA_OK) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(Cp), 9, static_cast<uint64_t>(Co)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(9 * Cp)};
+    const uint32_t box[3] = {kBKBytes, 1, static_cast<uint32_t>(bn)};
+    rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wp, dims, strides, box, "conv3x3 weights");
+    if (rc != XDNA_OK) return rc;
+  }
+  switch (mode) {
+    case XDNA_CONV_Q:
+      return dispatch_bn<LOAD_CONV, EPI_CONV_Q>(bn, ta, tb, a, sms, s);
+    case XDNA_CONV_DEQUANT:
+      return dispatch_bn<LOAD_CONV, EPI_CONV_DEQ>(bn, ta, tb, a, sms, s);
+    default:
+      return dispatch_bn<LOAD_CONV, EPI_CONV_CALIB>(bn, ta, tb, a, sms, s);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,425 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a, shared by the W8A8 linear and the
+// implicit-GEMM conv3x3.
+//
+//   C[m, n] = sum_k A[m, k] * B[n, k]        (A and B K-major; int8 -> int32 or bf16 -> f32)
+//
+// One CTA per SM walks output tiles of 128 x BN. Roles (192 threads):
+//   warp 0        TMA producer: a ring of STAGES shared-memory stages, each one 128-byte-wide
+//                 K block of A (128 rows) and B (BN rows), written with 128-byte swizzle;
+//   warp 1        TMEM allocator and MMA issuer: 4 tcgen05.mma (K = 32 bytes each) per stage into
+//                 one of two TMEM accumulators (2 x BN columns), so the epilogue of tile i
+//                 overlaps the MMAs of tile i+1;
+//   warps 2..5    epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31,
+//                 i.e. output rows), the fused per-mode arithmetic, and global stores.
+//
+// The A operand is either a plain row-major matrix (LOAD_GEMM) or, for the conv, the
+// zero-bordered NHWC activations viewed as a [pixels, Cp] matrix: the K loop runs over 9 taps x
+// channel blocks and a tap is a constant row offset dy*(W+2)+dx into that matrix (LOAD_CONV);
+// TMA's zero fill covers rows before the first / past the last pixel and channels past Cp.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace xdna {
+
+enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1 };
+
+enum EpiMode {
+  EPI_I32 = 0,         // int32 accumulators
+  EPI_DEQ = 1,         // (float(acc) * sx[m]) * sw[n] (+ bias[n]) -> f32 / bf16 / f16
+  EPI_CONV_Q = 2,      // requantised int8 / uint8, NCHW
+  EPI_CONV_DEQ = 3,    // requantised then dequantised, NCHW
+  EPI_CONV_CALIB = 4,  // max of the sums (of image 0) into one int32
+};
+
+struct GemmArgs {
+  int M, N;            // output rows (GEMM rows, or bordered pixels for the conv) and columns
+  int num_kb;          // 128-byte K blocks per tile
+  int m_tiles, n_tiles;
+  // conv geometry
+  int cblocks;         // 128-channel blocks per tap
+  int Wp, HWp;         // W + 2, (H + 2) * (W + 2)
+  int H, W;
+  // epilogue
+  void* out;
+  int64_t ldo;         // leading dimension of `out` in elements (GEMM modes)
+  int out_dtype;
+  int vec_ok;          // `out` rows allow 16-byte vector stores
+  const float* sx;
+  const float* sw;     // per-column weight scale (GEMM) / requantise scale (conv)
+  const void* bias;
+  int bias_dtype;
+  int shift, relu;
+  int* acc_max;
+  int* err;
+};
+
+constexpr int kBM = 128;
+constexpr int kBKBytes = 128;  // one 128-byte swizzle row per operand row per stage
+constexpr int kThreads = 192;
+constexpr int kGroupM = 8;     // tile raster: GROUP_M m-tiles share a column of n-tiles (L2 reuse)
+
+__host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
+  return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+}
+
+template <int BN>
+__host__ __device__ constexpr int stages_for() {
+  return BN >= 256 ? 4 : BN >= 128 ? 6 : 8;
+}
+
+template <int BN>
+__host__ __device__ constexpr int smem_bytes_for() {
+  return stages_for<BN>() * (kBM + BN) * kBKBytes + 1024 /*align*/ + 256 /*barriers*/;
+}
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
+  const int per_group = kGroupM * n_tiles;
+  const int g = t / per_group;
+  const int first = g * kGroupM;
+  const int gm = min(kGroupM, m_tiles - first);
+  const int r = t - g * per_group;
+  mb = first + r % gm;
+  nb = r / gm;
+}
+
+__device__ __forceinline__ float load_as_float(const void* p, int dtype, int i) {
+  if (dtype == XDNA_F32) return static_cast<const float*>(p)[i];
+  if (dtype == XDNA_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+// Store 32 floats (columns c0..c0+31 of one row) in the output dtype, rounding to nearest even.
+__device__ __forceinline__ void store_row32(void* out, int dtype, int64_t off, const float (&v)[32], int valid,
+                                            bool vec) {
+  if (dtype == XDNA_F32) {
+    float* o = static_cast<float*>(out) + off;
+    if (vec && valid == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+      for (int j = 0; j < valid; ++j) o[j] = v[j];
+    }
+  } else if (dtype == XDNA_BF16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + off;
+    if (vec && valid == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 u;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        u.z = *reinterpret_cast<uint32_t*>(&h2);
+        u.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(o + j) = u;
+      }
+    } else {
+      for (int j = 0; j < valid; ++j) o[j] = __float2bfloat16_rn(v[j]);
+    }
+  } else {
+    __half* o = static_cast<__half*>(out) + off;
+    if (vec && valid == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 u;
+        __half2 h0 = __floats2half2_rn(v[j], v[j + 1]);
+        __half2 h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
+        __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]);
+        __half2 h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        u.z = *reinterpret_cast<uint32_t*>(&h2);
+        u.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(o + j) = u;
+      }
+    } else {
+      for (int j = 0; j < valid; ++j) o[j] = __float2half_rn(v[j]);
+    }
+  }
+}
+
+__device__ __forceinline__ void store_one(void* out, int dtype, int64_t off, float v) {
+  if (dtype == XDNA_F32)
+    static_cast<float*>(out)[off] = v;
+  else if (dtype == XDNA_BF16)
+    static_cast<__nv_bfloat16*>(out)[off] = __float2bfloat16_rn(v);
+  else
+    static_cast<__half*>(out)[off] = __float2half_rn(v);
+}
+
+// The requantise of the conv: round half up by an arithmetic shift, then saturate.
+__device__ __forceinline__ int requant(int acc, int shift, int relu) {
+  const int q = (acc + (1 << (shift - 1))) >> shift;
+  return relu ? min(max(q, 0), 255) : min(max(q, -128), 127);
+}
+
+// --------------------------------------------------------------------------- epilogues
+// One thread, one output row `row`, accumulator columns n0..n0+31 in r[].
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int n0, const uint32_t (&r)[32]) {
+  if constexpr (EPI == EPI_I32) {
+    if (row >= a.M) return;
+    int32_t* o = static_cast<int32_t*>(a.out) + static_cast<int64_t>(row) * a.ldo + n0;
+    const int valid = min(32, a.N - n0);
+    if (a.vec_ok && valid == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<int4*>(o + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+    } else {
+      for (int j = 0; j < valid; ++j) o[j] = static_cast<int>(r[j]);
+    }
+  } else if constexpr (EPI == EPI_DEQ) {
+    if (row >= a.M) return;
+    const int valid = min(32, a.N - n0);
+    const float s = a.sx[row];
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j;
+      const float w = n < a.N ? __ldg(a.sw + n) : 0.f;
+      float y = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), s), w);
+      if (a.bias != nullptr && n < a.N) y = __fadd_rn(y, load_as_float(a.bias, a.bias_dtype, n));
+      v[j] = y;
+    }
+    store_row32(a.out, a.out_dtype, static_cast<int64_t>(row) * a.ldo + n0, v, valid, a.vec_ok != 0);
+  } else {
+    // conv: row is a bordered pixel index
+    const int p = row;
+    const int img = p / a.HWp;
+    const int rem = p - img * a.HWp;
+    const int yp = rem / a.Wp;
+    const int xp = rem - yp * a.Wp;
+    const bool valid = p < a.M && yp >= 1 && yp <= a.H && xp >= 1 && xp <= a.W;
+    if constexpr (EPI == EPI_CONV_CALIB) {
+      int best = 0;
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (n0 + j < a.N) {
+            const int acc = static_cast<int>(r[j]);
+            best = max(best, a.relu ? acc : abs(acc));
+          }
+        }
+      }
+      best = __reduce_max_sync(0xffffffffu, best);
+      if (lane_id() == 0 && best > 0) atomicMax(a.acc_max, best);
+    } else {
+      if (!valid) return;
+      const int64_t HW = static_cast<int64_t>(a.H) * a.W;
+      const int64_t base = (static_cast<int64_t>(img) * a.N + n0) * HW + static_cast<int64_t>(yp - 1) * a.W + (xp - 1);
+      const int nvalid = min(32, a.N - n0);
+      if constexpr (EPI == EPI_CONV_Q) {
+        if (a.relu) {
+          uint8_t* o = static_cast<uint8_t*>(a.out) + base;
+          for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<uint8_t>(requant(static_cast<int>(r[j]), a.shift, 1));
+        } else {
+          int8_t* o = static_cast<int8_t*>(a.out) + base;
+          for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<int8_t>(requant(static_cast<int>(r[j]), a.shift, 0));
+        }
+      } else {  // EPI_CONV_DEQ
+        const float s = a.sx[img];
+        for (int j = 0; j < nvalid; ++j) {
+          const int co = n0 + j;
+          const int q = requant(static_cast<int>(r[j]), a.shift, a.relu);
+          float y = __fmul_rn(static_cast<float>(q), __fmul_rn(__ldg(a.sw + co), s));
+          if (a.bias != nullptr) y = __fadd_rn(y, load_as_float(a.bias, a.bias_dtype, co));
+          store_one(a.out, a.out_dtype, base + j * HW, y);
+        }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- the kernel
+template <int BN, int LOAD, int EPI, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+  constexpr int STAGES = stages_for<BN>();
+  constexpr int A_BYTES = kBM * kBKBytes;
+  constexpr int B_BYTES = BN * kBKBytes;
+  constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
+  constexpr uint32_t IDESC = BF16 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN);
+  constexpr int KSTEPS = kBKBytes / 32;  // one MMA consumes 32 bytes of K (32 int8 or 16 bf16)
+  constexpr int K_ELEMS = BF16 ? kBKBytes / 2 : kBKBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total = args.m_tiles * args.n_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_parity[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1, abort_flag, args.err, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + stage, STAGE_TX);
+          if constexpr (LOAD == LOAD_GEMM) {
+            tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, kb * K_ELEMS, mb * kBM);
+            tma_load_2d(smB + stage * B_BYTES, &tmB, full + stage, kb * K_ELEMS, nb * BN);
+          } else {
+            const int tap = kb / args.cblocks;
+            const int cb = kb - tap * args.cblocks;
+            const int dy = tap / 3 - 1;
+            const int dx = tap % 3 - 1;
+            tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, cb * K_ELEMS, mb * kBM + dy * args.Wp + dx);
+            tma_load_3d(smB + stage * B_BYTES, &tmB, full + stage, cb * K_ELEMS, tap, nb * BN);
+          }
+          last_parity[stage] = static_cast<int>(phase);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: the last load of every stage has landed before the CTA may exit (a no-op on the
+      // normal path, where the MMA warp consumed them all).
+      for (int s = 0; s < STAGES; ++s)
+        if (last_parity[s] >= 0) {
+          volatile int never = 0;
+          mbar_wait(full + s, static_cast<uint32_t>(last_parity[s]), &never, args.err, 2);
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int buf = 0;
+      uint32_t bphase = 0;
+      bool issued = false;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        if (!mbar_wait(tempty + buf, bphase ^ 1, abort_flag, args.err, 3)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(full + stage, phase, abort_flag, args.err, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_k_sw128(smem_u32(smA + stage * A_BYTES));
+          const uint64_t db = smem_desc_k_sw128(smem_u32(smB + stage * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < KSTEPS; ++k) {
+            const uint32_t acc = (kb | k) != 0;
+            if constexpr (BF16)
+              umma_f16(d, da + 2 * k, db + 2 * k, IDESC, acc);
+            else
+              umma_i8(d, da + 2 * k, db + 2 * k, IDESC, acc);
+          }
+          umma_commit(empty + stage);
+          issued = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull + buf);
+        if (++buf == 2) {
+          buf = 0;
+          bphase ^= 1;
+        }
+      }
+      // Drain: every MMA this thread issued has completed before TMEM is freed.
+      if (issued) {
+        umma_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never, args.err, 5);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // the TMEM lane quadrant this warp may read
+    int buf = 0;
+    uint32_t bphase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
+      if (!mbar_wait(tfull + buf, bphase, abort_flag, args.err, 6)) break;
+      tc_fence_after();
+      const int row = mb * kBM + q * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = nb * BN + c * 32;
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (n0 < args.N) epilogue_chunk<EPI>(args, row, n0, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + buf);
+      if (++buf == 2) {
+        buf = 0;
+        bphase ^= 1;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace xdna

@@ -1,0 +1,232 @@
+"""torch.compile(model, backend="xdna"): GEMMs, 3x3 convs and Qwen3 stacks on the B200 kernels.
+
+A pass over Dynamo's FX graph (the same patterns as R:torch_xdna/backend.py:59-256):
+
+  F.linear(x, W, b), x @ W / torch.mm / torch.matmul / .mm / .matmul with a 2-D float parameter W,
+  and torch.addmm(b, x, W) (alpha = beta = 1, 1-D parameter bias)   -> xdna::linear
+  xdna::linear nodes (not transposed) that read the same x          -> one xdna::linear_cat + narrows
+  conv2d of a [Co, Ci, 3, 3] parameter, stride 1, padding 1 / "same", dilation 1, groups 1
+                                                                    -> conv3x3_int8 (xdna::conv3x3_fused)
+  a ReLU that is the sole user of such a conv without bias          -> fused into the requantise
+  a transformers Qwen3Model of Qwen3-0.6B's shapes into a linear head
+                                                                    -> xdna::qwen3_stack (stack.py)
+
+The rest of the graph goes to Inductor (fallback="inductor") or runs as written (fallback="eager").
+GEMMs between two activations (attention scores) are not rewritten.
+
+Where the reference decomposes each W8A8 linear into quantise / xdna::linear_i8 / dequantise graph
+ops so that its CPU compiler can fuse them (R:torch_xdna/backend.py:206-226), the B200 build keeps
+xdna::linear / linear_cat whole: the quantise is one HBM-bound kernel and the dequantise is the
+GEMM's epilogue, with the same arithmetic and therefore the same bits.
+"""
+
+import logging
+import operator
+
+import torch
+import torch.nn.functional as F
+
+from . import config as _config
+from . import kernels, ops
+
+log = logging.getLogger("torch_xdna")
+
+LINEAR = {torch._C._nn.linear, F.linear}
+CONV2D = {torch.conv2d, F.conv2d}
+RELU = {torch.relu, F.relu, torch.relu_}
+MATMUL = {operator.matmul, torch.matmul}
+FLOATS = (torch.float32, torch.bfloat16, torch.float16)
+
+
+def _parameter_nodes(gm, example_inputs):
+    """Placeholders that hold parameters or buffers: the weights worth quantising once."""
+    placeholders = [n for n in gm.graph.nodes if n.op == "placeholder"]
+    found = set()
+    for node, value in zip(placeholders, example_inputs):
+        if isinstance(value, torch.nn.Parameter) or "_parameters_" in node.name or "_buffers_" in node.name:
+            found.add(node)
+    return found
+
+
+def _tensor_of(node, attr):
+    if node.op == "get_attr":
+        return attr(node.target)
+    if node.op == "placeholder":
+        return node.meta.get("example_value")
+    return None
+
+
+def offload_gemms(gm: torch.fx.GraphModule, example_inputs, cfg) -> int:
+    """Rewrite offloadable GEMMs and 3x3 convs of `gm` in place; returns how many were rewritten."""
+    params = _parameter_nodes(gm, example_inputs)
+
+    def attr(target):
+        obj = gm
+        for part in target.split("."):
+            obj = getattr(obj, part)
+        return obj
+
+    def is_static(n):
+        return isinstance(n, torch.fx.Node) and (n in params or n.op == "get_attr")
+
+    def is_weight(n):
+        if not is_static(n):
+            return False
+        t = _tensor_of(n, attr)
+        return isinstance(t, torch.Tensor) and t.dim() == 2 and t.dtype in FLOATS
+
+    def is_bias_vector(n):
+        t = n.meta.get("example_value") if isinstance(n, torch.fx.Node) else None
+        return is_static(n) and isinstance(t, torch.Tensor) and t.dim() == 1
+
+    cid = ops.config_id(cfg)
+    count = 0
+    for node in list(gm.graph.nodes):
+        if node.op == "call_function" and node.target in LINEAR:
+            x = node.args[0] if node.args else node.kwargs.get("input")
+            w = node.args[1] if len(node.args) > 1 else node.kwargs.get("weight")
+            b = node.args[2] if len(node.args) > 2 else node.kwargs.get("bias")
+            transposed = False
+        elif (((node.op == "call_function" and node.target in MATMUL | {torch.mm})
+               or (node.op == "call_method" and node.target in ("matmul", "mm", "__matmul__")))
+              and len(node.args) == 2 and not node.kwargs):
+            x, w = node.args            # x @ W with W [K, N]
+            b, transposed = None, True
+        elif (node.op == "call_function" and node.target is torch.addmm and len(node.args) == 3
+              and set(node.kwargs) <= {"beta", "alpha"}
+              and all(node.kwargs.get(k, 1) == 1 for k in ("beta", "alpha"))):
+            b, x, w = node.args         # b + x @ W (HF Conv1D)
+            transposed = True
+            if b is not None and not is_bias_vector(b):
+                continue
+        else:
+            continue
+        if not is_weight(w):
+            continue
+        with gm.graph.inserting_after(node):
+            new = gm.graph.call_function(torch.ops.xdna.linear.default, (x, w, b, transposed, cid))
+        new.meta.update(node.meta)
+        node.replace_all_uses_with(new)
+        gm.graph.erase_node(node)
+        count += 1
+    if cfg.fuse:
+        _fuse_shared_input(gm, cid)
+    count += _offload_convs(gm, params, cid, attr, cfg)
+    gm.graph.lint()
+    gm.recompile()
+    return count
+
+
+def _conv_args(node):
+    """(x, weight, bias, stride, padding, dilation, groups) of a conv2d call."""
+    names = ("input", "weight", "bias", "stride", "padding", "dilation", "groups")
+    defaults = dict(bias=None, stride=1, padding=0, dilation=1, groups=1)
+    args = dict(zip(names, node.args), **node.kwargs)
+    return [args.get(k, defaults.get(k)) for k in names]
+
+
+def _pair(v):
+    return tuple(v) if isinstance(v, (tuple, list)) else (v, v)
+
+
+def _is_relu(n):
+    return (n.op == "call_function" and n.target in RELU) or (n.op == "call_method" and n.target in ("relu", "relu_"))
+
+
+def _offload_convs(gm, params, cid, attr, cfg):
+    """3x3 / stride-1 / padding-1 / groups-1 convs of a parameter weight -> conv3x3_int8
+    (R:torch_xdna/backend.py:130-174). The sole-user ReLU of a bias-free conv is fused."""
+    from .conv import conv3x3_int8, supported
+
+    if not cfg.offload:
+        return 0
+    count = 0
+    for node in list(gm.graph.nodes):
+        if node.op != "call_function" or node.target not in CONV2D:
+            continue
+        x, w, b, stride, padding, dilation, groups = _conv_args(node)
+        if (_pair(stride) != (1, 1) or (padding != "same" and _pair(padding) != (1, 1))
+                or _pair(dilation) != (1, 1) or groups != 1):
+            continue
+        if not (isinstance(w, torch.fx.Node) and (w in params or w.op == "get_attr")):
+            continue
+        wt = _tensor_of(w, attr)
+        xt = x.meta.get("example_value") if isinstance(x, torch.fx.Node) else None
+        if not (isinstance(wt, torch.Tensor) and wt.dim() == 4 and tuple(wt.shape[2:]) == (3, 3)
+                and isinstance(xt, torch.Tensor) and xt.dim() == 4 and xt.dtype in FLOATS):
+            continue
+        if not supported(int(wt.shape[1]), int(wt.shape[0]), int(xt.shape[2]), int(xt.shape[3])):
+            continue
+        users = list(node.users)
+        relu = users[0] if (cfg.fuse and b is None and len(users) == 1 and _is_relu(users[0])) else None
+        last = relu or node
+        with gm.graph.inserting_after(last):
+            new = gm.graph.call_function(conv3x3_int8, (x, w, b, relu is not None, cid))
+        new.meta.update(last.meta)
+        last.replace_all_uses_with(new)
+        if relu is not None:
+            gm.graph.erase_node(relu)
+        gm.graph.erase_node(node)
+        count += 1
+    return count
+
+
+def _out_features(w):
+    t = w.meta.get("example_value") if isinstance(w, torch.fx.Node) else None
+    return int(t.shape[0]) if isinstance(t, torch.Tensor) else None
+
+
+def _fuse_shared_input(gm, cid):
+    """xdna::linear nodes reading the same input (q/k/v, gate/up) -> one xdna::linear_cat + narrows
+    (R:torch_xdna/backend.py:177-203)."""
+    groups = {}
+    for node in gm.graph.nodes:
+        if node.op == "call_function" and node.target is torch.ops.xdna.linear.default and not node.args[3]:
+            groups.setdefault(node.args[0], []).append(node)
+    for x, members in groups.items():
+        if len(members) < 2:
+            continue
+        weights = [m.args[1] for m in members]
+        sizes = [_out_features(w) for w in weights]
+        if None in sizes:
+            continue
+        with gm.graph.inserting_before(members[0]):
+            cat = gm.graph.call_function(torch.ops.xdna.linear_cat.default,
+                                         (x, weights, [m.args[2] for m in members], cid))
+            start = 0
+            for m, n in zip(members, sizes):
+                part = gm.graph.call_function(torch.narrow, (cat, -1, start, n))
+                part.meta.update(m.meta)
+                m.replace_all_uses_with(part)
+                start += n
+        for m in members:
+            gm.graph.erase_node(m)
+
+
+def _compile(gm, example_inputs, cfg):
+    n = offload_gemms(gm, example_inputs, cfg) if cfg.offload else 0
+    if cfg.verbose:
+        log.warning("torch_xdna: %d GEMMs / convs offloaded in a graph of %d nodes (policy=%s, fallback=%s)",
+                    n, len(gm.graph.nodes), cfg.policy, cfg.fallback)
+    if cfg.fallback == "eager":
+        return gm.forward
+    from torch._inductor.compile_fx import compile_fx
+
+    return compile_fx(gm, example_inputs)
+
+
+def xdna_backend(gm: torch.fx.GraphModule, example_inputs, options=None, mode=None):
+    """The torch.compile backend; `options` are torch_xdna.Config fields (R:torch_xdna/backend.py:246-256).
+
+    Unlike the reference there is no CPU route: with offloading on (policy other than "cpu") and no
+    usable B200, compiling raises XdnaUnavailable with the reason instead of falling back."""
+    cfg = _config.config.merged(options)
+    if cfg.offload:
+        kernels.require()
+        if cfg.stacks:
+            from . import stack
+
+            plan = stack.find(gm, example_inputs)
+            if plan is not None:
+                return stack.compile_fused(gm, example_inputs, cfg, ops.config_id(cfg), plan, _compile)
+    return _compile(gm, example_inputs, cfg)

@@ -1,0 +1,187 @@
+"""xdna::conv3x3: 3x3 / stride-1 / padding-1 convolutions of a parameter weight, int8 on the B200.
+
+The math is the reference's (R:torch_xdna/conv.py:1-19):
+
+  weights     int8 per output channel, quantised once
+  activations int8 per image (sx)
+  sums        int32 on the int8 tensor cores (implicit GEMM: K = 9 taps x input channels),
+              requantised in the epilogue by one shift: round half up, saturate to int8, or to
+              [0, 255] with a fused ReLU. The shift is fixed on the layer's first call from the
+              first image's sums with 25% headroom (R:torch_xdna/conv.py:327-332).
+  output      q * sw[co] * 2^shift * sx (+ bias)
+
+Data layout on the device: activations are quantised straight into a zero-bordered NHWC int8
+tensor [N, H+2, W+2, Cp] (Cp = channels rounded up to 16), so each of the 9 taps is a constant row
+offset into a [pixels, Cp] matrix that TMA streams into shared memory; weights are packed once as
+[Co, 9, Cp]. Three kernels per conv3x3_int8 call: per-image max, quantise + layout, and the
+conv with the dequantise (or requantise) in its epilogue.
+"""
+
+import logging
+import math
+import threading
+import time
+import weakref
+
+import torch
+
+from . import kernels
+from .runtime import DEVICE, XdnaResultMismatch, stats
+
+log = logging.getLogger("torch_xdna")
+_lock = threading.RLock()
+_layers = {}            # (id(weight), H, W, relu) -> (weakref to weight, ConvLayer)
+
+
+def supported(ci, co, h, w):
+    """Shapes the B200 conv takes: any channel counts and image size (R:torch_xdna/conv.py:38-40 capped
+    input channels at 512 for the NPU op; kept here so the pass rewrites the same convs)."""
+    return 1 <= ci <= 512 and co >= 1 and h >= 1 and w >= 1
+
+
+def conv3x3_int8(x, weight, bias, relu: bool, cfg_id: int):
+    """relu?(conv2d(x, weight, bias, padding=1)) through int8: what the backend puts in the graph
+    (R:torch_xdna/conv.py:43-51). One custom op: quantise, conv and dequantise run as B200 kernels."""
+    return torch.ops.xdna.conv3x3_fused(x, weight, bias, relu, cfg_id)
+
+
+def channels_padded(c):
+    return kernels.round_up(c, 16)
+
+
+class ConvLayer:
+    """One conv weight at one input size: int8 weights packed for the implicit GEMM, the shift."""
+
+    def __init__(self, weight, h, w, relu):
+        kernels._cuda(weight)
+        co, ci = weight.shape[:2]
+        wf = weight.detach()
+        if wf.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+            wf = wf.float()
+        rows = wf.reshape(co, ci * 9).contiguous()
+        self.wq = torch.empty((co, kernels.round_up(ci * 9, 16)), dtype=torch.int8, device=weight.device)
+        self.sw = torch.empty((co,), dtype=torch.float32, device=weight.device)
+        kernels.quant_rows(rows, self.wq, self.sw)           # R:torch_xdna/conv.py:315-316
+        self.ci, self.co, self.cp = ci, co, channels_padded(ci)
+        wq4 = self.wq[:, :ci * 9].contiguous().view(co, ci, 3, 3)
+        self.wq4 = wq4
+        self.wp = torch.empty((co, 9, self.cp), dtype=torch.int8, device=weight.device)
+        kernels.conv_pack_weight(wq4, self.wp)
+        self.h, self.w, self.relu = h, w, relu
+        self.shift = self.scale = None
+        self.checked = False
+        self.name = f"conv3x3 {ci}->{co} {h}x{w}" + (" relu" if relu else "")
+
+    def calibrate(self, xp):
+        """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:327-332)."""
+        acc_max = torch.empty((1,), dtype=torch.int32, device=xp.device)
+        kernels.conv3x3(xp, self.wp, 1, self.ci, self.co, self.h, self.w, kernels.CONV_CALIBRATE, relu=self.relu,
+                        acc_max=acc_max)
+        stats.launches += 1
+        top = float(int(acc_max.item()))
+        self.shift = min(31, max(1, math.ceil(math.log2(max(top * 1.25, 1.0) / (255 if self.relu else 127)))))
+        self.scale = self.sw * 2.0 ** self.shift
+
+    def q(self, xp, n):
+        out = torch.empty((n, self.co, self.h, self.w), dtype=torch.uint8 if self.relu else torch.int8,
+                          device=xp.device)
+        kernels.conv3x3(xp, self.wp, n, self.ci, self.co, self.h, self.w, kernels.CONV_Q, shift=self.shift,
+                        relu=self.relu, out=out)
+        stats.launches += 1
+        return out
+
+    def dequant(self, xp, n, sx, bias, dtype):
+        out = torch.empty((n, self.co, self.h, self.w), dtype=dtype, device=xp.device)
+        kernels.conv3x3(xp, self.wp, n, self.ci, self.co, self.h, self.w, kernels.CONV_DEQUANT, shift=self.shift,
+                        relu=self.relu, scale=self.scale, sx=sx, bias=bias, out=out)
+        stats.launches += 1
+        return out
+
+    def cpu_integers(self, xq_nchw_cpu):
+        """The reference's CPU integers for the same layer and shift (ConvLayer.cpu,
+        R:torch_xdna/conv.py:342-348), used only to verify launches."""
+        dt = torch.float32 if 127 * float(self.wq4.abs().sum(dim=(1, 2, 3)).max()) < 2 ** 24 else torch.float64
+        acc = torch.nn.functional.conv2d(xq_nchw_cpu.to(dt), self.wq4.cpu().to(dt), padding=1)
+        q = (acc.to(torch.int32) + (1 << (self.shift - 1))) >> self.shift
+        return q.clamp_(0, 255).to(torch.uint8) if self.relu else q.clamp_(-128, 127).to(torch.int8)
+
+
+def _layer(weight, h, w, relu):
+    key = (id(weight), h, w, relu)
+    hit = _layers.get(key)
+    if hit is not None and hit[0]() is weight:
+        return hit[1]
+    layer = ConvLayer(weight, h, w, relu)
+    _layers[key] = (weakref.ref(weight), layer)
+    return layer
+
+
+def _bordered(n, h, w, cp, device):
+    return torch.empty((n, h + 2, w + 2, cp), dtype=torch.int8, device=device)
+
+
+def _verify(cfg, layer, xp, xq_cpu_fn):
+    if cfg.verify == "off" or (cfg.verify == "first" and layer.checked):
+        return
+    n = xp.shape[0]
+    got = layer.q(xp, n).cpu()
+    want = layer.cpu_integers(xq_cpu_fn())
+    if not torch.equal(got, want):
+        raise XdnaResultMismatch(f"{layer.name} disagrees with the CPU integers: "
+                                 f"{int((got != want).sum())} of {want.numel()} values differ")
+    layer.checked = True
+    stats.checks.append((layer.name, "bitwise equal to the CPU integers"))
+
+
+def conv3x3(cfg, xq, weight, relu):
+    """(q, scale) of xdna::conv3x3 for int8 xq [N, Ci, H, W] (R:torch_xdna/conv.py:164-189)."""
+    kernels._cuda(xq, weight)
+    n, ci, h, w = xq.shape
+    co = weight.shape[0]
+    t0 = time.perf_counter()
+    with _lock:
+        layer = _layer(weight, h, w, relu)
+        xp = _bordered(n, h, w, layer.cp, xq.device)
+        kernels.conv_pack_input(xq.contiguous(), xp)
+        stats.launches += 1
+        if layer.shift is None:
+            layer.calibrate(xp)
+        _verify(cfg, layer, xp, lambda: xq.cpu())
+        q = layer.q(xp, n)
+    stats.calls[DEVICE] += 1
+    stats.seconds[DEVICE] += time.perf_counter() - t0
+    stats.macs[DEVICE] += n * co * ci * h * w * 9
+    # a fresh tensor: Inductor may reuse an extern op's output buffer once it is dead
+    return q, layer.scale.clone()
+
+
+def conv3x3_fused(cfg, x, weight, bias, relu):
+    """conv3x3_int8 in three kernels: per-image max, quantise into the bordered NHWC layout, and the
+    conv whose epilogue requantises and dequantises (q * (scale * sx) + bias) straight to x.dtype."""
+    kernels._cuda(x, weight, bias)
+    n, ci, h, w = x.shape
+    co = weight.shape[0]
+    t0 = time.perf_counter()
+    with _lock:
+        layer = _layer(weight, h, w, relu)
+        xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
+        xc = xc.contiguous()
+        xp = _bordered(n, h, w, layer.cp, x.device)
+        sx = torch.empty((n,), dtype=torch.float32, device=x.device)
+        scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
+        kernels.conv_quant(xc, xp, sx, scratch)
+        stats.launches += 2
+        if layer.shift is None:
+            layer.calibrate(xp)
+
+        def xq_cpu():
+            xf = xc.float().cpu()
+            s = xf.abs().amax(dim=(1, 2, 3), keepdim=True).clamp(min=1e-8) / 127
+            return torch.round(xf / s).clamp(-127, 127).to(torch.int8)
+
+        _verify(cfg, layer, xp, xq_cpu)
+        y = layer.dequant(xp, n, sx, bias, x.dtype)
+    stats.calls[DEVICE] += 1
+    stats.seconds[DEVICE] += time.perf_counter() - t0
+    stats.macs[DEVICE] += n * co * ci * h * w * 9
+    return y

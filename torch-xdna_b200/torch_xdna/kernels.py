@@ -1,0 +1,208 @@
+"""The device side: libxdna_b200.so, hand-written sm_100a kernels behind a C ABI (include/xdna_b200.h).
+
+Replaces the reference's Triton-XDNA driver module (R:torch_xdna/kernels.py): `available()`,
+`unavailable_reason()` and `mark_broken()` keep their meaning; the launch functions below replace
+`mm_i8` (R:torch_xdna/kernels.py:172-192) and the Triton-XDNA conv3x3 / qwen3_stack calls.
+
+The library is loaded from this package (lib/libxdna_b200.so, built in-tree by
+__graft_entry__.build() or `make -C torch-xdna_b200/csrc`). There is no CPU fallback: without the
+library or without an sm_100 GPU, every op raises XdnaUnavailable with the reason.
+"""
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libxdna_b200.so"
+ABI_VERSION = 1
+
+# element types (XDNA_F32 ...)
+F32, BF16, F16, I32, I8, U8 = 0, 1, 2, 3, 4, 5
+DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16, torch.int32: I32, torch.int8: I8,
+               torch.uint8: U8}
+# conv3x3 modes
+CONV_Q, CONV_DEQUANT, CONV_CALIBRATE = 0, 1, 2
+# status codes
+ERR_TIMEOUT = -4
+
+_lock = threading.RLock()
+_state = {"lib": None, "ok": None, "error": None}
+
+
+class XdnaUnavailable(RuntimeError):
+    """No B200 or no library: the xdna ops cannot run in this process."""
+
+
+class XdnaError(RuntimeError):
+    """A library call returned an error status."""
+
+    def __init__(self, name, status, message):
+        super().__init__(f"{name} failed ({status}): {message}")
+        self.status = status
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise XdnaUnavailable(f"{LIB_PATH} is not built (run __graft_entry__.build() or make -C torch-xdna_b200/csrc)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    sig = {
+        "xdna_last_error": ([], ctypes.c_char_p),
+        "xdna_abi_version": ([], I),
+        "xdna_device_check": ([I], I),
+        "xdna_take_device_error": ([P, P, P], I),
+        "xdna_quant_rows_i8": ([P, I, I64, I64, I64, P, I64, P, P], I),
+        "xdna_gemm_i8": ([P, I64, P, I64, I64, I64, I64, P, P, P, I, P, I, I64, P], I),
+        "xdna_conv_quant_nhwc": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
+        "xdna_conv_pack_input": ([P, I64, I64, I64, I64, P, I64, P], I),
+        "xdna_conv_pack_weight": ([P, I64, I64, P, I64, P], I),
+        "xdna_conv3x3_i8": ([P, P, I64, I64, I64, I64, I64, I64, I, I, I, P, P, P, I, P, I, P, P], I),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes, fn.restype = args, res
+    if lib.xdna_abi_version() != ABI_VERSION:
+        raise XdnaUnavailable(f"{LIB_PATH} has ABI {lib.xdna_abi_version()}, this package needs {ABI_VERSION}")
+    return lib
+
+
+def lib():
+    """The loaded library; raises XdnaUnavailable (loudly) when it cannot be used."""
+    with _lock:
+        if _state["lib"] is None:
+            try:
+                _state["lib"] = _load()
+            except XdnaUnavailable:
+                raise
+            except OSError as e:
+                raise XdnaUnavailable(f"cannot load {LIB_PATH}: {e}") from e
+        return _state["lib"]
+
+
+def available() -> bool:
+    """True if the xdna ops can run here: the library loads and CUDA device 0 is an sm_100 GPU."""
+    with _lock:
+        if _state["ok"] is None:
+            try:
+                if os.environ.get("TORCH_XDNA_DISABLE_GPU") == "1":
+                    raise XdnaUnavailable("disabled by TORCH_XDNA_DISABLE_GPU=1")
+                if not torch.cuda.is_available():
+                    raise XdnaUnavailable("no CUDA device")
+                L = lib()
+                rc = L.xdna_device_check(torch.cuda.current_device())
+                if rc != 0:
+                    raise XdnaUnavailable(L.xdna_last_error().decode())
+                _state["ok"] = True
+            except Exception as e:  # any missing piece: the ops raise with this reason
+                _state["ok"], _state["error"] = False, f"{type(e).__name__}: {e}"
+        return _state["ok"]
+
+
+def unavailable_reason():
+    return _state["error"]
+
+
+def mark_broken(err: BaseException):
+    """A launch failed unrecoverably: stop accepting calls for the rest of the process."""
+    with _lock:
+        _state["ok"], _state["error"] = False, f"{type(err).__name__}: {err}"
+
+
+def require():
+    if not available():
+        raise XdnaUnavailable(f"torch_xdna needs a B200 (sm_100) and libxdna_b200.so: {unavailable_reason()}")
+    return lib()
+
+
+def device_name() -> str:
+    if not available():
+        return "none"
+    return torch.cuda.get_device_name(torch.cuda.current_device())
+
+
+# ---------------------------------------------------------------- call helpers
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _check(name, rc):
+    if rc != 0:
+        raise XdnaError(name, rc, lib().xdna_last_error().decode())
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise XdnaUnavailable("torch_xdna ops run on CUDA tensors; move the model and inputs to the B200")
+
+
+def take_device_error():
+    """(code, site) recorded by a bounded device wait since the last call; (0, 0) when none. Synchronises."""
+    L = require()
+    code, site = ctypes.c_int(0), ctypes.c_int(0)
+    _check("xdna_take_device_error", L.xdna_take_device_error(ctypes.byref(code), ctypes.byref(site), _stream()))
+    return code.value, site.value
+
+
+def round_up(x, m):
+    return -(-x // m) * m
+
+
+def quant_rows(x2d, xq, scale):
+    """xq[:, :K] / scale[:] = per-row int8 of x2d [R, K] (f32/bf16/f16; unit column stride)."""
+    L = require()
+    _cuda(x2d, xq, scale)
+    R, K = x2d.shape
+    assert x2d.stride(1) == 1 or K <= 1, "rows must be contiguous"
+    _check("xdna_quant_rows_i8", L.xdna_quant_rows_i8(_p(x2d), DTYPE_CODES[x2d.dtype], R, K, max(x2d.stride(0), K),
+                                                      _p(xq), xq.stride(0), _p(scale), _stream()))
+
+
+def gemm_i8(xq, wq, K, y, sx=None, sw=None, bias=None):
+    """y [M, N] = xq[:, :K] . wq[:, :K]^T (int32 y), or its dequantisation in y's float dtype."""
+    L = require()
+    _cuda(xq, wq, y, sx, sw, bias)
+    M, N = y.shape
+    _check("xdna_gemm_i8", L.xdna_gemm_i8(_p(xq), xq.stride(0), _p(wq), wq.stride(0), M, N, K, _p(sx), _p(sw),
+                                          _p(bias), DTYPE_CODES[bias.dtype] if bias is not None else F32,
+                                          _p(y), DTYPE_CODES[y.dtype], y.stride(0), _stream()))
+
+
+def conv_quant(x, xp, sx, scratch):
+    L = require()
+    _cuda(x, xp, sx, scratch)
+    N, C, H, W = x.shape
+    _check("xdna_conv_quant_nhwc", L.xdna_conv_quant_nhwc(_p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp),
+                                                          xp.shape[-1], _p(sx), _p(scratch), _stream()))
+
+
+def conv_pack_input(xq, xp):
+    L = require()
+    _cuda(xq, xp)
+    N, C, H, W = xq.shape
+    _check("xdna_conv_pack_input", L.xdna_conv_pack_input(_p(xq), N, C, H, W, _p(xp), xp.shape[-1], _stream()))
+
+
+def conv_pack_weight(wq, wp):
+    L = require()
+    _cuda(wq, wp)
+    Co, Ci = wq.shape[:2]
+    _check("xdna_conv_pack_weight", L.xdna_conv_pack_weight(_p(wq), Co, Ci, _p(wp), wp.shape[-1], _stream()))
+
+
+def conv3x3(xp, wp, N, Ci, Co, H, W, mode, shift=1, relu=False, scale=None, sx=None, bias=None, out=None,
+            acc_max=None):
+    L = require()
+    _cuda(xp, wp, scale, sx, bias, out, acc_max)
+    Cp = wp.shape[-1]
+    _check("xdna_conv3x3_i8", L.xdna_conv3x3_i8(
+        _p(xp), _p(wp), N, Ci, Cp, Co, H, W, mode, shift, int(bool(relu)), _p(scale), _p(sx), _p(bias),
+        DTYPE_CODES[bias.dtype] if bias is not None else F32, _p(out),
+        DTYPE_CODES[out.dtype] if out is not None else I8, _p(acc_max), _stream()))

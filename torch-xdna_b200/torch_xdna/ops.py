@@ -1,0 +1,100 @@
+"""The custom ops the backend puts in place of offloadable GEMMs, convs and transformer stacks.
+
+Schemas are the reference's, unchanged (R:torch_xdna/ops.py:25-89), so graphs and code that call
+torch.ops.xdna.* keep working; the implementations call the B200 kernels. To the rest of
+torch.compile each op is opaque with a shape function (the fake impl), and Inductor calls it as an
+extern kernel. One op is new: xdna::conv3x3_fused, the whole quantise -> conv -> dequantise of
+conv3x3_int8 as one op, because on the B200 those three steps are kernels of ours rather than
+graph ops for the CPU compiler to fuse.
+"""
+
+from typing import Optional
+
+import torch
+
+from . import conv, runtime, stack
+
+_configs = []  # cfg_id -> Config; op arguments must be plain values (R:torch_xdna/ops.py:14-22)
+
+
+def config_id(cfg) -> int:
+    for i, c in enumerate(_configs):
+        if c == cfg:
+            return i
+    _configs.append(cfg)
+    return len(_configs) - 1
+
+
+@torch.library.custom_op("xdna::linear", mutates_args=())
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+           transposed: bool, cfg_id: int) -> torch.Tensor:
+    return runtime.linear(_configs[cfg_id], x, weight, bias, transposed)
+
+
+@linear.register_fake
+def _(x, weight, bias, transposed, cfg_id):
+    n = weight.shape[1] if transposed else weight.shape[0]
+    return x.new_empty(*x.shape[:-1], n)
+
+
+@torch.library.custom_op("xdna::linear_cat", mutates_args=())
+def linear_cat(x: torch.Tensor, weights: list[torch.Tensor], biases: list[Optional[torch.Tensor]],
+               cfg_id: int) -> torch.Tensor:
+    """Linears that read the same input as one GEMM; outputs concatenated on the last dim."""
+    return runtime.linear_cat(_configs[cfg_id], x, weights, biases)
+
+
+@linear_cat.register_fake
+def _(x, weights, biases, cfg_id):
+    return x.new_empty(*x.shape[:-1], sum(w.shape[0] for w in weights))
+
+
+@torch.library.custom_op("xdna::linear_i8", mutates_args=())
+def linear_i8(xq: torch.Tensor, weights: list[torch.Tensor], transposed: bool,
+              cfg_id: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """int8 xq [R, K] -> (acc [R, N] int32, sw [N] float32), x @ W^T ~= acc * sx[:, None] * sw."""
+    return runtime.linear_i8(_configs[cfg_id], xq, weights, transposed)
+
+
+@linear_i8.register_fake
+def _(xq, weights, transposed, cfg_id):
+    n = sum(w.shape[1] if transposed else w.shape[0] for w in weights)
+    return xq.new_empty((xq.shape[0], n), dtype=torch.int32), xq.new_empty((n,), dtype=torch.float32)
+
+
+@torch.library.custom_op("xdna::conv3x3", mutates_args=())
+def conv3x3(xq: torch.Tensor, weight: torch.Tensor, relu: bool, cfg_id: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """int8 xq [N, Ci, H, W] -> (q [N, Co, H, W] int8 (uint8 with relu), scale [Co] float32),
+    relu?(conv2d(x, weight, padding=1)) ~= q * scale[co] * sx."""
+    return conv.conv3x3(_configs[cfg_id], xq, weight, relu)
+
+
+@conv3x3.register_fake
+def _(xq, weight, relu, cfg_id):
+    q = xq.new_empty((xq.shape[0], weight.shape[0], xq.shape[2], xq.shape[3]),
+                     dtype=torch.uint8 if relu else torch.int8)
+    return q, weight.new_empty((weight.shape[0],), dtype=torch.float32)
+
+
+@torch.library.custom_op("xdna::conv3x3_fused", mutates_args=())
+def conv3x3_fused(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], relu: bool,
+                  cfg_id: int) -> torch.Tensor:
+    """relu?(conv2d(x, weight, bias, padding=1)) through int8, as conv3x3_int8 defines it."""
+    return conv.conv3x3_fused(_configs[cfg_id], x, weight, bias, relu)
+
+
+@conv3x3_fused.register_fake
+def _(x, weight, bias, relu, cfg_id):
+    return x.new_empty((x.shape[0], weight.shape[0], x.shape[2], x.shape[3]))
+
+
+@torch.library.custom_op("xdna::qwen3_stack", mutates_args=())
+def qwen3_stack(x: torch.Tensor, mask: torch.Tensor, stack_id: int, cfg_id: int) -> torch.Tensor:
+    """A whole Qwen3-0.6B-sized stack with its final norm and linear head: hidden states x [B, L, 1024]
+    under a 4-D attention mask -> the head's output [B, L, N]."""
+    return stack.run(_configs[cfg_id], stack_id, x, mask)
+
+
+@qwen3_stack.register_fake
+def _(x, mask, stack_id, cfg_id):
+    return x.new_empty(*x.shape[:-1], stack.out_features(stack_id))
