@@ -12,6 +12,13 @@ from oracle import xdna_oracle as orc
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _inference():
+    """The xdna ops are inference-only (no autograd formula, as in the reference): run under no_grad."""
+    with torch.no_grad():
+        yield
+
+
 def t(a, dev, dtype=None):
     x = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     return x.to(dtype) if dtype is not None else x

@@ -11,6 +11,13 @@ from oracle import xdna_oracle as orc
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _inference():
+    """The xdna ops are inference-only (no autograd formula, as in the reference): run under no_grad."""
+    with torch.no_grad():
+        yield
+
 TORCH_DT = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
 
 

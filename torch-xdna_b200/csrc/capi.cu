@@ -86,7 +86,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 int encode_tma(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
-               const uint64_t* strides_bytes, const uint32_t* box, const char* what) {
+               const uint64_t* strides_bytes, const uint32_t* box, const char* what, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(XDNA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   if (!aligned16(base)) return fail(XDNA_ERR_INVALID, "%s: base address is not 16-byte aligned", what);
@@ -104,7 +104,7 @@ int encode_tma(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void
     s[i] = strides_bytes[i];
   }
   CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(XDNA_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
   return XDNA_OK;

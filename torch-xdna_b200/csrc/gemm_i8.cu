@@ -6,11 +6,11 @@
 
 namespace xdna {
 
-template <int BN, int LOAD, int EPI>
-static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int sms,
-                       cudaStream_t stream) {
+template <int BN, int LOAD, int EPI, bool TSTORE>
+static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
+                       int sms, cudaStream_t stream) {
   constexpr int smem = smem_bytes_for<BN>();
-  auto kern = umma_gemm_kernel<BN, LOAD, EPI, false>;
+  auto kern = umma_gemm_kernel<BN, LOAD, EPI, false, TSTORE>;
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
@@ -20,20 +20,20 @@ static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   }
   const int tiles = args.m_tiles * args.n_tiles;
   const int grid = std::max(1, std::min(tiles, sms));
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, args);
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, args);
   return check_launch("umma_gemm_kernel");
 }
 
-template <int LOAD, int EPI>
-static int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int sms,
-                       cudaStream_t stream) {
+template <int LOAD, int EPI, bool TSTORE>
+static int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                       const GemmArgs& args, int sms, cudaStream_t stream) {
   switch (bn) {
     case 256:
-      return launch_umma<256, LOAD, EPI>(ta, tb, args, sms, stream);
+      return launch_umma<256, LOAD, EPI, TSTORE>(ta, tb, tc, args, sms, stream);
     case 128:
-      return launch_umma<128, LOAD, EPI>(ta, tb, args, sms, stream);
+      return launch_umma<128, LOAD, EPI, TSTORE>(ta, tb, tc, args, sms, stream);
     default:
-      return launch_umma<64, LOAD, EPI>(ta, tb, args, sms, stream);
+      return launch_umma<64, LOAD, EPI, TSTORE>(ta, tb, tc, args, sms, stream);
   }
 }
 
@@ -96,7 +96,7 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
   a.bias_dtype = bias_dtype;
   a.err = device_error_word();
 
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldx)};
@@ -111,8 +111,26 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
     rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, wq, dims, strides, box, "gemm_i8 weights");
     if (rc != XDNA_OK) return rc;
   }
-  if (y_dtype == XDNA_I32) return dispatch_bn<LOAD_GEMM, EPI_I32>(bn, ta, tb, a, sms, s);
-  return dispatch_bn<LOAD_GEMM, EPI_DEQ>(bn, ta, tb, a, sms, s);
+  // Output through TMA stores when the rows are 16-byte addressable (box: 32 columns x 32 rows).
+  const bool tstore = a.vec_ok != 0;
+  if (tstore) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldy * es)};
+    const uint32_t box[2] = {32, 32};
+    const CUtensorMapDataType dt = es == 4 ? CU_TENSOR_MAP_DATA_TYPE_INT32
+                                   : y_dtype == XDNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    rc = encode_tma(&tc, dt, 2, y, dims, strides, box, "gemm_i8 output",
+                    es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != XDNA_OK) return rc;
+  } else {
+    tc = ta;  // unused
+  }
+  if (y_dtype == XDNA_I32)
+    return tstore ? dispatch_bn<LOAD_GEMM, EPI_I32, true>(bn, ta, tb, tc, a, sms, s)
+                  : dispatch_bn<LOAD_GEMM, EPI_I32, false>(bn, ta, tb, tc, a, sms, s);
+  return tstore ? dispatch_bn<LOAD_GEMM, EPI_DEQ, true>(bn, ta, tb, tc, a, sms, s)
+                : dispatch_bn<LOAD_GEMM, EPI_DEQ, false>(bn, ta, tb, tc, a, sms, s);
 }
 
 int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, int64_t Cp, int64_t Co, int64_t H,
@@ -187,11 +205,11 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   }
   switch (mode) {
     case XDNA_CONV_Q:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_Q>(bn, ta, tb, a, sms, s);
+      return dispatch_bn<LOAD_CONV, EPI_CONV_Q, false>(bn, ta, tb, ta, a, sms, s);
     case XDNA_CONV_DEQUANT:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_DEQ>(bn, ta, tb, a, sms, s);
+      return dispatch_bn<LOAD_CONV, EPI_CONV_DEQ, false>(bn, ta, tb, ta, a, sms, s);
     default:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_CALIB>(bn, ta, tb, a, sms, s);
+      return dispatch_bn<LOAD_CONV, EPI_CONV_CALIB, false>(bn, ta, tb, ta, a, sms, s);
   }
 }
 

@@ -36,10 +36,11 @@ int* device_error_word();
 // Kernel launch error check (after <<<>>>).
 int check_launch(const char* what);
 
-// Encodes a tiled TMA map with 128-byte swizzle and zero fill.
+// Encodes a tiled TMA map (128-byte swizzle unless given) with zero fill for out-of-range loads.
 // dims/strides innermost first; strides_bytes has rank-1 entries (dims 1..rank-1).
 int encode_tma(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
-               const uint64_t* strides_bytes, const uint32_t* box, const char* what);
+               const uint64_t* strides_bytes, const uint32_t* box, const char* what,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 

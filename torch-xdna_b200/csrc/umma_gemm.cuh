@@ -3,14 +3,18 @@
 //
 //   C[m, n] = sum_k A[m, k] * B[n, k]        (A and B K-major; int8 -> int32 or bf16 -> f32)
 //
-// One CTA per SM walks output tiles of 128 x BN. Roles (192 threads):
+// One CTA per SM walks output tiles of 128 x BN. Roles (320 threads):
 //   warp 0        TMA producer: a ring of STAGES shared-memory stages, each one 128-byte-wide
 //                 K block of A (128 rows) and B (BN rows), written with 128-byte swizzle;
 //   warp 1        TMEM allocator and MMA issuer: 4 tcgen05.mma (K = 32 bytes each) per stage into
 //                 one of two TMEM accumulators (2 x BN columns), so the epilogue of tile i
 //                 overlaps the MMAs of tile i+1;
-//   warps 2..5    epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31,
-//                 i.e. output rows), the fused per-mode arithmetic, and global stores.
+//   warps 2..9    epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (its 32 output rows) and one half
+//                 of the tile's columns, 32 columns per tcgen05.ld, issued one chunk ahead of the
+//                 arithmetic. Per-column factors arrive once per tile as one coalesced load per lane
+//                 and are broadcast with warp shuffles. GEMM outputs are staged in swizzled shared
+//                 memory (4 KB per warp) and written by TMA bulk-tensor stores (full lines, tails
+//                 clipped by the tensor map); conv outputs (NCHW scatter) use direct stores.
 //
 // The A operand is either a plain row-major matrix (LOAD_GEMM) or, for the conv, the
 // zero-bordered NHWC activations viewed as a [pixels, Cp] matrix: the K loop runs over 9 taps x
@@ -44,7 +48,7 @@ struct GemmArgs {
   void* out;
   int64_t ldo;         // leading dimension of `out` in elements (GEMM modes)
   int out_dtype;
-  int vec_ok;          // `out` rows allow 16-byte vector stores
+  int vec_ok;          // `out` rows allow 16-byte vector stores (direct-store path)
   const float* sx;
   const float* sw;     // per-column weight scale (GEMM) / requantise scale (conv)
   const void* bias;
@@ -56,8 +60,11 @@ struct GemmArgs {
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;  // one 128-byte swizzle row per operand row per stage
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageOutBytes = 4096;  // per epilogue warp: 32 rows x 32 columns x <= 4 bytes
 constexpr int kGroupM = 8;     // tile raster: GROUP_M m-tiles share a column of n-tiles (L2 reuse)
+constexpr unsigned kFull = 0xffffffffu;
 
 __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
@@ -70,7 +77,8 @@ __host__ __device__ constexpr int stages_for() {
 
 template <int BN>
 __host__ __device__ constexpr int smem_bytes_for() {
-  return stages_for<BN>() * (kBM + BN) * kBKBytes + 1024 /*align*/ + 256 /*barriers*/;
+  return stages_for<BN>() * (kBM + BN) * kBKBytes + kEpiWarps * kStageOutBytes + 1024 /*align*/ +
+         256 /*barriers*/;
 }
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
@@ -89,56 +97,13 @@ __device__ __forceinline__ float load_as_float(const void* p, int dtype, int i) 
   return __half2float(static_cast<const __half*>(p)[i]);
 }
 
-// Store 32 floats (columns c0..c0+31 of one row) in the output dtype, rounding to nearest even.
-__device__ __forceinline__ void store_row32(void* out, int dtype, int64_t off, const float (&v)[32], int valid,
-                                            bool vec) {
-  if (dtype == XDNA_F32) {
-    float* o = static_cast<float*>(out) + off;
-    if (vec && valid == 32) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-      for (int j = 0; j < valid; ++j) o[j] = v[j];
-    }
-  } else if (dtype == XDNA_BF16) {
-    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + off;
-    if (vec && valid == 32) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 u;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
-        u.x = *reinterpret_cast<uint32_t*>(&h0);
-        u.y = *reinterpret_cast<uint32_t*>(&h1);
-        u.z = *reinterpret_cast<uint32_t*>(&h2);
-        u.w = *reinterpret_cast<uint32_t*>(&h3);
-        *reinterpret_cast<uint4*>(o + j) = u;
-      }
-    } else {
-      for (int j = 0; j < valid; ++j) o[j] = __float2bfloat16_rn(v[j]);
-    }
-  } else {
-    __half* o = static_cast<__half*>(out) + off;
-    if (vec && valid == 32) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 u;
-        __half2 h0 = __floats2half2_rn(v[j], v[j + 1]);
-        __half2 h1 = __floats2half2_rn(v[j + 2], v[j + 3]);
-        __half2 h2 = __floats2half2_rn(v[j + 4], v[j + 5]);
-        __half2 h3 = __floats2half2_rn(v[j + 6], v[j + 7]);
-        u.x = *reinterpret_cast<uint32_t*>(&h0);
-        u.y = *reinterpret_cast<uint32_t*>(&h1);
-        u.z = *reinterpret_cast<uint32_t*>(&h2);
-        u.w = *reinterpret_cast<uint32_t*>(&h3);
-        *reinterpret_cast<uint4*>(o + j) = u;
-      }
-    } else {
-      for (int j = 0; j < valid; ++j) o[j] = __float2half_rn(v[j]);
-    }
+__device__ __forceinline__ uint32_t pack2(float a, float b, int dtype) {
+  if (dtype == XDNA_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
   }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
 __device__ __forceinline__ void store_one(void* out, int dtype, int64_t off, float v) {
@@ -156,88 +121,113 @@ __device__ __forceinline__ int requant(int acc, int shift, int relu) {
   return relu ? min(max(q, 0), 255) : min(max(q, -128), 127);
 }
 
-// --------------------------------------------------------------------------- epilogues
-// One thread, one output row `row`, accumulator columns n0..n0+31 in r[].
+// 32 accumulators of one row -> 32 dequantised floats. Column factors: lane j holds column j's.
+__device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float srow, float sw_lane, float b_lane,
+                                          bool has_bias, float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float w = __shfl_sync(kFull, sw_lane, j);
+    float y = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), srow), w);
+    const float b = __shfl_sync(kFull, b_lane, j);
+    if (has_bias) y = __fadd_rn(y, b);
+    v[j] = y;
+  }
+}
+
+// Writes one 32 x 32 output block (this warp's rows, 32 columns) through swizzled shared memory and
+// a TMA store. `words` holds this lane's row: 16 words (2-byte outputs) or 32 words (4-byte outputs).
+template <int NWORDS>
+__device__ __forceinline__ void stage_and_store(uint8_t* buf, const uint32_t (&words)[NWORDS], const CUtensorMap* tmC,
+                                                int x, int y) {
+  const int lane = lane_id();
+  if (lane == 0) bulk_wait_read_all();  // the previous store from this buffer has read it
+  __syncwarp();
+  constexpr int CHUNKS = NWORDS / 4;    // 16-byte chunks per row: 4 (64 B rows) or 8 (128 B rows)
+  uint8_t* row = buf + lane * (CHUNKS * 16);
+  const int sw = CHUNKS == 8 ? (lane & 7) : ((lane >> 1) & 3);  // TMA 128B / 64B swizzle pattern
+#pragma unroll
+  for (int k = 0; k < CHUNKS; ++k)
+    *reinterpret_cast<uint4*>(row + ((k ^ sw) * 16)) =
+        make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmC, buf, x, y);
+    bulk_commit();
+  }
+}
+
+// Direct (non-TMA) stores of one row's 32 values, for outputs TMA cannot address.
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int n0, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void store_direct(const GemmArgs& a, int row, int n0, const uint32_t (&r)[32],
+                                             const float (&v)[32]) {
+  if (row >= a.M) return;
+  const int valid = min(32, a.N - n0);
+  const int64_t off = static_cast<int64_t>(row) * a.ldo + n0;
   if constexpr (EPI == EPI_I32) {
-    if (row >= a.M) return;
-    int32_t* o = static_cast<int32_t*>(a.out) + static_cast<int64_t>(row) * a.ldo + n0;
-    const int valid = min(32, a.N - n0);
-    if (a.vec_ok && valid == 32) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<int4*>(o + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
-    } else {
-      for (int j = 0; j < valid; ++j) o[j] = static_cast<int>(r[j]);
-    }
-  } else if constexpr (EPI == EPI_DEQ) {
-    if (row >= a.M) return;
-    const int valid = min(32, a.N - n0);
-    const float s = a.sx[row];
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = n0 + j;
-      const float w = n < a.N ? __ldg(a.sw + n) : 0.f;
-      float y = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), s), w);
-      if (a.bias != nullptr && n < a.N) y = __fadd_rn(y, load_as_float(a.bias, a.bias_dtype, n));
-      v[j] = y;
-    }
-    store_row32(a.out, a.out_dtype, static_cast<int64_t>(row) * a.ldo + n0, v, valid, a.vec_ok != 0);
+    int32_t* o = static_cast<int32_t*>(a.out) + off;
+    for (int j = 0; j < valid; ++j) o[j] = static_cast<int>(r[j]);
   } else {
-    // conv: row is a bordered pixel index
-    const int p = row;
-    const int img = p / a.HWp;
-    const int rem = p - img * a.HWp;
-    const int yp = rem / a.Wp;
-    const int xp = rem - yp * a.Wp;
-    const bool valid = p < a.M && yp >= 1 && yp <= a.H && xp >= 1 && xp <= a.W;
-    if constexpr (EPI == EPI_CONV_CALIB) {
-      int best = 0;
-      if (valid) {
+    for (int j = 0; j < valid; ++j) store_one(a.out, a.out_dtype, off + j, v[j]);
+  }
+}
+
+// Conv epilogues: one thread, one bordered pixel `p`, channels n0..n0+31 in r[].
+template <int EPI>
+__device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, const uint32_t (&r)[32],
+                                           float scale_lane) {
+  const int img = p / a.HWp;
+  const int rem = p - img * a.HWp;
+  const int yp = rem / a.Wp;
+  const int xp = rem - yp * a.Wp;
+  const bool valid = p < a.M && yp >= 1 && yp <= a.H && xp >= 1 && xp <= a.W;
+  const int nvalid = min(32, a.N - n0);
+  if constexpr (EPI == EPI_CONV_CALIB) {
+    int best = 0;
+    if (valid) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (n0 + j < a.N) {
-            const int acc = static_cast<int>(r[j]);
-            best = max(best, a.relu ? acc : abs(acc));
-          }
+      for (int j = 0; j < 32; ++j) {
+        if (j < nvalid) {
+          const int acc = static_cast<int>(r[j]);
+          best = max(best, a.relu ? acc : abs(acc));
         }
       }
-      best = __reduce_max_sync(0xffffffffu, best);
-      if (lane_id() == 0 && best > 0) atomicMax(a.acc_max, best);
+    }
+    best = __reduce_max_sync(kFull, best);
+    if (lane_id() == 0 && best > 0) atomicMax(a.acc_max, best);
+  } else if constexpr (EPI == EPI_CONV_Q) {
+    if (!valid) return;
+    const int64_t HW = static_cast<int64_t>(a.H) * a.W;
+    const int64_t base = (static_cast<int64_t>(img) * a.N + n0) * HW + static_cast<int64_t>(yp - 1) * a.W + (xp - 1);
+    if (a.relu) {
+      uint8_t* o = static_cast<uint8_t*>(a.out) + base;
+      for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<uint8_t>(requant(static_cast<int>(r[j]), a.shift, 1));
     } else {
-      if (!valid) return;
-      const int64_t HW = static_cast<int64_t>(a.H) * a.W;
-      const int64_t base = (static_cast<int64_t>(img) * a.N + n0) * HW + static_cast<int64_t>(yp - 1) * a.W + (xp - 1);
-      const int nvalid = min(32, a.N - n0);
-      if constexpr (EPI == EPI_CONV_Q) {
-        if (a.relu) {
-          uint8_t* o = static_cast<uint8_t*>(a.out) + base;
-          for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<uint8_t>(requant(static_cast<int>(r[j]), a.shift, 1));
-        } else {
-          int8_t* o = static_cast<int8_t*>(a.out) + base;
-          for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<int8_t>(requant(static_cast<int>(r[j]), a.shift, 0));
-        }
-      } else {  // EPI_CONV_DEQ
-        const float s = a.sx[img];
-        for (int j = 0; j < nvalid; ++j) {
-          const int co = n0 + j;
-          const int q = requant(static_cast<int>(r[j]), a.shift, a.relu);
-          float y = __fmul_rn(static_cast<float>(q), __fmul_rn(__ldg(a.sw + co), s));
-          if (a.bias != nullptr) y = __fadd_rn(y, load_as_float(a.bias, a.bias_dtype, co));
-          store_one(a.out, a.out_dtype, base + j * HW, y);
-        }
-      }
+      int8_t* o = static_cast<int8_t*>(a.out) + base;
+      for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<int8_t>(requant(static_cast<int>(r[j]), a.shift, 0));
+    }
+  } else {  // EPI_CONV_DEQ: q.float() * (scale[co] * sx[img]) (+ bias[co])
+    const float s = valid ? a.sx[img] : 0.f;
+    float f[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __shfl_sync(kFull, scale_lane, j);
+    if (!valid) return;
+    const int64_t HW = static_cast<int64_t>(a.H) * a.W;
+    const int64_t base = (static_cast<int64_t>(img) * a.N + n0) * HW + static_cast<int64_t>(yp - 1) * a.W + (xp - 1);
+    for (int j = 0; j < nvalid; ++j) {
+      const int q = requant(static_cast<int>(r[j]), a.shift, a.relu);
+      float y = __fmul_rn(static_cast<float>(q), __fmul_rn(f[j], s));
+      if (a.bias != nullptr) y = __fadd_rn(y, load_as_float(a.bias, a.bias_dtype, n0 + j));
+      store_one(a.out, a.out_dtype, base + j * HW, y);
     }
   }
 }
 
 // --------------------------------------------------------------------------- the kernel
-template <int BN, int LOAD, int EPI, bool BF16>
+template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   constexpr int STAGES = stages_for<BN>();
   constexpr int A_BYTES = kBM * kBKBytes;
   constexpr int B_BYTES = BN * kBKBytes;
@@ -246,12 +236,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t IDESC = BF16 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN);
   constexpr int KSTEPS = kBKBytes / 32;  // one MMA consumes 32 bytes of K (32 int8 or 16 bf16)
   constexpr int K_ELEMS = BF16 ? kBKBytes / 2 : kBKBytes;
+  constexpr int WCOLS = BN / 2;          // columns per epilogue warp
+  constexpr int NCH = WCOLS / 32;        // 32-column chunks per epilogue warp
+  static_assert(NCH >= 1 && NCH <= 4, "BN must be 64, 128 or 256");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smB + STAGES * B_BYTES);
+  uint8_t* smOut = smB + STAGES * B_BYTES;  // kEpiWarps x kStageOutBytes, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(smOut + kEpiWarps * kStageOutBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -269,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull + b, 1);
-      mbar_init(tempty + b, 4);
+      mbar_init(tempty + b, kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -282,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (TSTORE) tma_prefetch_desc(&tmC);
   }
   tc_fence_before();
   __syncthreads();
@@ -384,33 +379,98 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;  // the TMEM lane quadrant this warp may read
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
+    const int ew = warp - 2;
+    const int q = warp & 3;          // the TMEM lane quadrant this warp may read
+    const int half = ew >> 2;        // which half of the tile's columns
+    uint8_t* obuf = smOut + ew * kStageOutBytes;
+    const bool has_bias = args.bias != nullptr;
     int buf = 0;
     uint32_t bphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
+      const int row0 = mb * kBM + q * 32;
+      const int row = row0 + lane;
+      const int col0 = nb * BN + half * WCOLS;
+      // per-row and per-column factors, loaded before waiting for the accumulator
+      float srow = 0.f;
+      float fcol[NCH], bcol[NCH];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int n = col0 + c * 32 + lane;
+        fcol[c] = 0.f;
+        bcol[c] = 0.f;
+        if constexpr (EPI == EPI_DEQ || EPI == EPI_CONV_DEQ) {
+          if (n < args.N) {
+            fcol[c] = __ldg(args.sw + n);
+            if (has_bias) bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
+          }
+        }
+      }
+      if constexpr (EPI == EPI_DEQ) srow = row < args.M ? __ldg(args.sx + row) : 0.f;
+
       if (!mbar_wait(tfull + buf, bphase, abort_flag, args.err, 6)) break;
       tc_fence_after();
-      const int row = mb * kBM + q * 32 + lane;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n0 = nb * BN + c * 32;
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_ld_wait();
-        if (n0 < args.N) epilogue_chunk<EPI>(args, row, n0, r);
-      }
-      tc_fence_before();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + half * WCOLS);
+      uint32_t r[2][32];
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty + buf);
+      tmem_ld_32x32b_x32(taddr, r[0]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        if (c + 1 < NCH) {
+          __syncwarp();
+          tmem_ld_32x32b_x32(taddr + (c + 1) * 32, r[(c + 1) & 1]);
+        } else {
+          // every column of this tile is in registers: hand the accumulator back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty + buf);
+        }
+        const int n0 = col0 + c * 32;
+        // warp-uniform: this chunk has columns in range (and, for GEMM outputs, rows in range)
+        if (n0 < args.N && (LOAD == LOAD_CONV || row0 < args.M)) {
+          const uint32_t(&rc)[32] = r[c & 1];
+          if constexpr (EPI == EPI_I32 || EPI == EPI_DEQ) {
+            if constexpr (TSTORE) {
+              if constexpr (EPI == EPI_I32) {
+                stage_and_store<32>(obuf, rc, &tmC, n0, row0);
+              } else {
+                float v[32];
+                dequant32(rc, srow, fcol[c], bcol[c], has_bias, v);
+                if (args.out_dtype == XDNA_F32) {
+                  uint32_t w[32];
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
+                  stage_and_store<32>(obuf, w, &tmC, n0, row0);
+                } else {
+                  uint32_t w[16];
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], args.out_dtype);
+                  stage_and_store<16>(obuf, w, &tmC, n0, row0);
+                }
+              }
+            } else {
+              float v[32];
+              if constexpr (EPI == EPI_DEQ) dequant32(rc, srow, fcol[c], bcol[c], has_bias, v);
+              store_direct<EPI>(args, row, n0, rc, v);
+            }
+          } else {
+            conv_chunk<EPI>(args, row, n0, rc, fcol[c]);
+          }
+        }
+        if (c + 1 < NCH) tmem_ld_wait();
+      }
       if (++buf == 2) {
         buf = 0;
         bphase ^= 1;
       }
+    }
+    if constexpr (TSTORE) {
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
     }
   }
 
