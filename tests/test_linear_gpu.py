@@ -52,6 +52,30 @@ def test_quant_rows_bitexact(cuda, dtype, rows, k):
     assert np.array_equal(xq[:, :k].cpu().numpy(), q_ref)
 
 
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_quant_rows_half_integer_boundaries(cuda, dtype):
+    """Values at, and one ulp either side of, (k + 0.5) * scale: where round-half-even of the IEEE
+    quotient decides, and where a quotient computed any other way would round differently."""
+    g = mg.rng(4242)
+    rows, k = 256, 1024
+    amax = (g.uniform(0.1, 50.0, rows)).astype(np.float32)
+    x = np.zeros((rows, k), np.float32)
+    x[:, 0] = amax                                   # fixes each row's scale
+    s = (np.maximum(amax, np.float32(1e-8)) / np.float32(127)).astype(np.float32)
+    kk = g.integers(-126, 126, (rows, k - 1)).astype(np.float32) + np.float32(0.5)
+    base = (kk * s[:, None]).astype(np.float32)
+    which = g.integers(0, 3, (rows, k - 1))
+    x[:, 1:] = np.where(which == 0, np.nextafter(base, np.float32(-np.inf)),
+                        np.where(which == 1, base, np.nextafter(base, np.float32(np.inf))))
+    x = np.clip(x, -amax[:, None], amax[:, None])
+    xv = orc.cast(x, dtype)
+    xq, sx = quant_gpu(t(xv, cuda, TORCH_DT[dtype]))
+    q_ref, s_ref = orc.quant_rows(xv)
+    assert np.array_equal(sx.cpu().numpy(), s_ref)
+    bad = int((xq[:, :k].cpu().numpy() != q_ref).sum())
+    assert bad == 0, f"{bad} boundary values rounded differently"
+
+
 def test_quant_rows_strided_rows(cuda):
     x = torch.randn(64, 2048, device=cuda)[:, :1000]     # ldx 2048, K 1000
     xq, sx = quant_gpu(x)

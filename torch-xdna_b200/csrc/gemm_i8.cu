@@ -6,11 +6,11 @@
 
 namespace xdna {
 
-template <int BN, int LOAD, int EPI, bool TSTORE>
+template <int BN, int LOAD, int EPI, bool TSTORE, int ODT>
 static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
                        int sms, cudaStream_t stream) {
   constexpr int smem = smem_bytes_for<BN>();
-  auto kern = umma_gemm_kernel<BN, LOAD, EPI, false, TSTORE>;
+  auto kern = umma_gemm_kernel<BN, LOAD, EPI, false, TSTORE, ODT>;
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
@@ -24,16 +24,16 @@ static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   return check_launch("umma_gemm_kernel");
 }
 
-template <int LOAD, int EPI, bool TSTORE>
+template <int LOAD, int EPI, bool TSTORE, int ODT>
 static int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                        const GemmArgs& args, int sms, cudaStream_t stream) {
   switch (bn) {
     case 256:
-      return launch_umma<256, LOAD, EPI, TSTORE>(ta, tb, tc, args, sms, stream);
+      return launch_umma<256, LOAD, EPI, TSTORE, ODT>(ta, tb, tc, args, sms, stream);
     case 128:
-      return launch_umma<128, LOAD, EPI, TSTORE>(ta, tb, tc, args, sms, stream);
+      return launch_umma<128, LOAD, EPI, TSTORE, ODT>(ta, tb, tc, args, sms, stream);
     default:
-      return launch_umma<64, LOAD, EPI, TSTORE>(ta, tb, tc, args, sms, stream);
+      return launch_umma<64, LOAD, EPI, TSTORE, ODT>(ta, tb, tc, args, sms, stream);
   }
 }
 
@@ -126,11 +126,20 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
   } else {
     tc = ta;  // unused
   }
-  if (y_dtype == XDNA_I32)
-    return tstore ? dispatch_bn<LOAD_GEMM, EPI_I32, true>(bn, ta, tb, tc, a, sms, s)
-                  : dispatch_bn<LOAD_GEMM, EPI_I32, false>(bn, ta, tb, tc, a, sms, s);
-  return tstore ? dispatch_bn<LOAD_GEMM, EPI_DEQ, true>(bn, ta, tb, tc, a, sms, s)
-                : dispatch_bn<LOAD_GEMM, EPI_DEQ, false>(bn, ta, tb, tc, a, sms, s);
+  if (!tstore) {  // rows TMA cannot address: direct stores (any output type)
+    if (y_dtype == XDNA_I32) return dispatch_bn<LOAD_GEMM, EPI_I32, false, XDNA_I32>(bn, ta, tb, tc, a, sms, s);
+    return dispatch_bn<LOAD_GEMM, EPI_DEQ, false, XDNA_F32>(bn, ta, tb, tc, a, sms, s);
+  }
+  switch (y_dtype) {
+    case XDNA_I32:
+      return dispatch_bn<LOAD_GEMM, EPI_I32, true, XDNA_I32>(bn, ta, tb, tc, a, sms, s);
+    case XDNA_F32:
+      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_F32>(bn, ta, tb, tc, a, sms, s);
+    case XDNA_BF16:
+      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_BF16>(bn, ta, tb, tc, a, sms, s);
+    default:
+      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_F16>(bn, ta, tb, tc, a, sms, s);
+  }
 }
 
 int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, int64_t Cp, int64_t Co, int64_t H,
@@ -205,11 +214,11 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   }
   switch (mode) {
     case XDNA_CONV_Q:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_Q, false>(bn, ta, tb, ta, a, sms, s);
+      return dispatch_bn<LOAD_CONV, EPI_CONV_Q, false, XDNA_I8>(bn, ta, tb, ta, a, sms, s);
     case XDNA_CONV_DEQUANT:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_DEQ, false>(bn, ta, tb, ta, a, sms, s);
+      return dispatch_bn<LOAD_CONV, EPI_CONV_DEQ, false, XDNA_F32>(bn, ta, tb, ta, a, sms, s);
     default:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_CALIB, false>(bn, ta, tb, ta, a, sms, s);
+      return dispatch_bn<LOAD_CONV, EPI_CONV_CALIB, false, XDNA_I32>(bn, ta, tb, ta, a, sms, s);
   }
 }
 

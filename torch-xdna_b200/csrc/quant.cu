@@ -3,9 +3,15 @@
 //   - per image, fused with the NCHW -> zero-bordered NHWC layout the implicit-GEMM conv reads;
 //   - int8 NCHW -> bordered NHWC (the xdna::conv3x3 op's own input), and the conv weight packing.
 //
-// Arithmetic follows the reference exactly: the max of |x| is taken in x's dtype (exact), widened
-// to f32, clamped below by 1e-8 and divided by 127 (IEEE division); each value is x / scale with
-// IEEE division, rounded half to even, clamped to [-127, 127]. No FMA contraction is involved.
+// Results equal the reference's bit for bit: the max of |x| is taken in x's dtype (exact), widened
+// to f32, clamped below by 1e-8 and divided by 127 (IEEE division); each value becomes
+// clamp(round_half_even(fl(x / scale)), -127, 127).
+//
+// The per-value division is done as a product with the correctly rounded reciprocal, which differs
+// from the IEEE quotient fl(x / scale) by at most 1.9e-5 when |x / scale| <= 127 (two roundings of
+// relative 2^-24 on top of the quotient's own half ulp). Rounding to an integer can only come out
+// differently when a half-integer lies within that distance, so whenever the product is within 1e-3
+// of a half-integer the IEEE quotient is computed instead. Every other value rounds identically.
 #include <algorithm>
 
 #include "host_util.h"
@@ -14,7 +20,7 @@
 namespace xdna {
 
 template <typename T>
-struct Vec16;  // 16 bytes of T
+struct Vec16;  // elements of T in 16 bytes
 template <>
 struct Vec16<float> {
   static constexpr int N = 4;
@@ -33,8 +39,77 @@ __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162flo
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
 __device__ __forceinline__ float to_f32(int8_t v) { return static_cast<float>(v); }
 
-__device__ __forceinline__ int8_t quant1(float v, float s) {
-  const float q = rintf(__fdiv_rn(v, s));
+// 1.5 * 2^23: adding it to |y| < 2^22 rounds y to an integer (ties to even) held in the low
+// mantissa bits, two's complement in the low byte for -128 <= y <= 127.
+constexpr float kRoundMagic = 12582912.0f;
+
+// The int8 of one value as the low byte of a 32-bit word: round_half_even(fl(v / s)), r = 1 / s.
+// |v| <= amax makes |v / s| <= 127 (scale = amax / 127), so no clamp is needed.
+__device__ __forceinline__ uint32_t quant_byte(float v, float s, float r) {
+  const float y = __fmul_rn(v, r);
+  float t = __fadd_rn(y, kRoundMagic);
+  const float d = __fsub_rn(y, __fsub_rn(t, kRoundMagic));  // y - round(y), in [-0.5, 0.5]
+  if (fabsf(d) > 0.499f) t = __fadd_rn(__fdiv_rn(v, s), kRoundMagic);  // near a rounding boundary
+  return __float_as_uint(t);
+}
+
+// Four values -> four int8 in one word (byte i = value i).
+__device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s, float r) {
+  const uint32_t lo = __byte_perm(quant_byte(a, s, r), quant_byte(b, s, r), 0x0040);
+  const uint32_t hi = __byte_perm(quant_byte(c, s, r), quant_byte(d, s, r), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
+
+// max |x| over the 16 bytes of `u`, in x's own encoding: non-negative IEEE values order like their
+// bit patterns, so the max is taken on integers with the sign bits cleared.
+template <typename T>
+__device__ __forceinline__ float amax16(const uint4& u);
+template <>
+__device__ __forceinline__ float amax16<float>(const uint4& u) {
+  const uint32_t m = max(max(u.x & 0x7FFFFFFFu, u.y & 0x7FFFFFFFu), max(u.z & 0x7FFFFFFFu, u.w & 0x7FFFFFFFu));
+  return __uint_as_float(m);
+}
+template <>
+__device__ __forceinline__ float amax16<__nv_bfloat16>(const uint4& u) {
+  uint32_t m = __vmaxu2(__vmaxu2(u.x & 0x7FFF7FFFu, u.y & 0x7FFF7FFFu), __vmaxu2(u.z & 0x7FFF7FFFu, u.w & 0x7FFF7FFFu));
+  m = max(m & 0xFFFFu, m >> 16);
+  return __uint_as_float(m << 16);  // bf16 bits are the top half of the f32 bits
+}
+template <>
+__device__ __forceinline__ float amax16<__half>(const uint4& u) {
+  uint32_t m = __vmaxu2(__vmaxu2(u.x & 0x7FFF7FFFu, u.y & 0x7FFF7FFFu), __vmaxu2(u.z & 0x7FFF7FFFu, u.w & 0x7FFF7FFFu));
+  m = max(m & 0xFFFFu, m >> 16);
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(m)));
+}
+
+// 16 bytes of T -> their int8 (4 or 8 bytes, as 1 or 2 words).
+template <typename T>
+__device__ __forceinline__ void quant16(const uint4& u, float s, float r, uint32_t (&out)[2]);
+template <>
+__device__ __forceinline__ void quant16<float>(const uint4& u, float s, float r, uint32_t (&out)[2]) {
+  out[0] = quant4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w), s, r);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+template <>
+__device__ __forceinline__ void quant16<__nv_bfloat16>(const uint4& u, float s, float r, uint32_t (&out)[2]) {
+  out[0] = quant4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y), s, r);
+  out[1] = quant4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w), s, r);
+}
+__device__ __forceinline__ float f16_lo(uint32_t w) { return __half2float(__ushort_as_half(static_cast<unsigned short>(w))); }
+__device__ __forceinline__ float f16_hi(uint32_t w) { return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))); }
+template <>
+__device__ __forceinline__ void quant16<__half>(const uint4& u, float s, float r, uint32_t (&out)[2]) {
+  out[0] = quant4(f16_lo(u.x), f16_hi(u.x), f16_lo(u.y), f16_hi(u.y), s, r);
+  out[1] = quant4(f16_lo(u.z), f16_hi(u.z), f16_lo(u.w), f16_hi(u.w), s, r);
+}
+
+// clamp(round_half_even(fl(v / s)), -127, 127) for one value (scalar paths); r = 1 / s.
+__device__ __forceinline__ int8_t quant1(float v, float s, float r) {
+  float y = __fmul_rn(v, r);
+  const float frac = y - floorf(y);
+  if (fabsf(frac - 0.5f) < 1e-3f) y = __fdiv_rn(v, s);  // near a rounding boundary: the exact quotient
+  const float q = rintf(y);
   return static_cast<int8_t>(static_cast<int>(fminf(fmaxf(q, -127.f), 127.f)));
 }
 
@@ -46,7 +121,46 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// One warp per row. VEC: 16-byte loads when the row allows them.
+// One warp per row, the row held in registers: NV 16-byte vectors per lane, lane-interleaved so
+// every load and store instruction of the warp is contiguous. One read of x, one write of xq.
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                                             int64_t ldx, int8_t* __restrict__ xq, int64_t ldq,
+                                                             float* __restrict__ scale) {
+  constexpr int V = Vec16<T>::N;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const T* xr = x + row * ldx;
+  uint4 buf[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int64_t c = (static_cast<int64_t>(i) * 32 + lane) * V;
+    buf[i] = c < cols ? __ldg(reinterpret_cast<const uint4*>(xr + c)) : make_uint4(0, 0, 0, 0);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) amax = fmaxf(amax, amax16<T>(buf[i]));  // padding vectors are zeros
+  amax = warp_max(amax);
+  const float s = scale_from_amax(amax);
+  const float r = __frcp_rn(s);
+  if (lane == 0) scale[row] = s;
+  int8_t* qr = xq + row * ldq;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int64_t c = (static_cast<int64_t>(i) * 32 + lane) * V;
+    if (c < cols) {
+      uint32_t w[2];
+      quant16<T>(buf[i], s, r, w);
+      if constexpr (V == 4)
+        *reinterpret_cast<uint32_t*>(qr + c) = w[0];
+      else
+        *reinterpret_cast<uint2*>(qr + c) = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
+// Rows too long for registers, or not 16-byte addressable: two passes over the row.
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
                                                          int64_t ldx, int8_t* __restrict__ xq, int64_t ldq,
@@ -70,6 +184,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
   }
   amax = warp_max(amax);
   const float s = scale_from_amax(amax);
+  const float r = __frcp_rn(s);
   if (lane == 0) scale[row] = s;
   if constexpr (VEC) {
     constexpr int V = Vec16<T>::N;
@@ -78,14 +193,14 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
       const T* e = reinterpret_cast<const T*>(&u);
       int8_t q[V];
 #pragma unroll
-      for (int j = 0; j < V; ++j) q[j] = quant1(to_f32(e[j]), s);
+      for (int j = 0; j < V; ++j) q[j] = quant1(to_f32(e[j]), s, r);
       if constexpr (V == 4)
         *reinterpret_cast<uint32_t*>(qr + c) = *reinterpret_cast<uint32_t*>(q);
       else
         *reinterpret_cast<uint2*>(qr + c) = *reinterpret_cast<uint2*>(q);
     }
   } else {
-    for (int64_t c = lane; c < cols; c += 32) qr[c] = quant1(to_f32(xr[c]), s);
+    for (int64_t c = lane; c < cols; c += 32) qr[c] = quant1(to_f32(xr[c]), s, r);
   }
 }
 
@@ -98,12 +213,27 @@ static int launch_quant_rows(const void* x, int64_t rows, int64_t cols, int64_t 
   const int rows_per_block = 8;
   const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   if (blocks > 0x7fffffff) return fail(XDNA_ERR_INVALID, "quant_rows: too many rows");
-  if (vec)
-    quant_rows_kernel<T, true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const T*>(x), rows, cols, ldx, xq, ldq, scale);
-  else
-    quant_rows_kernel<T, false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const T*>(x), rows, cols, ldx, xq, ldq, scale);
+  const unsigned g = static_cast<unsigned>(blocks);
+  const T* xt = static_cast<const T*>(x);
+  const int64_t nv = (cols + 32 * V - 1) / (32 * V);  // 16-byte vectors per lane
+  if (vec && nv <= 16) {
+    if (nv <= 1)
+      quant_rows_reg_kernel<T, 1><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+    else if (nv <= 2)
+      quant_rows_reg_kernel<T, 2><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+    else if (nv <= 4)
+      quant_rows_reg_kernel<T, 4><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+    else if (nv <= 8)
+      quant_rows_reg_kernel<T, 8><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+    else if (nv <= 12)
+      quant_rows_reg_kernel<T, 12><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+    else
+      quant_rows_reg_kernel<T, 16><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+  } else if (vec) {
+    quant_rows_kernel<T, true><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+  } else {
+    quant_rows_kernel<T, false><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+  }
   return check_launch("quant_rows_kernel");
 }
 
@@ -145,9 +275,10 @@ __global__ void __launch_bounds__(256) to_bordered_nhwc_kernel(const T* __restri
   const int n = blockIdx.z / cgroups;
   const int c0 = (blockIdx.z - n * cgroups) * 64;
   const int Wp = W + 2;
-  float s = 1.f;
+  float s = 1.f, r = 1.f;
   if constexpr (QUANT) {
     s = scale_from_amax(__uint_as_float(amax[n]));
+    r = __frcp_rn(s);
     if (blockIdx.x == 0 && blockIdx.y == 0 && c0 == 0 && threadIdx.x == 0) sx[n] = s;
   }
   const int y = yb - 1;
@@ -162,7 +293,7 @@ __global__ void __launch_bounds__(256) to_bordered_nhwc_kernel(const T* __restri
     if (in_row && c < C) {
       const T v = x[((static_cast<int64_t>(n) * C + c) * H + y) * W + xin];
       if constexpr (QUANT)
-        q = quant1(to_f32(v), s);
+        q = quant1(to_f32(v), s, r);
       else
         q = static_cast<int8_t>(v);
     }

@@ -127,10 +127,11 @@ __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float srow, f
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float w = __shfl_sync(kFull, sw_lane, j);
-    float y = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), srow), w);
-    const float b = __shfl_sync(kFull, b_lane, j);
-    if (has_bias) y = __fadd_rn(y, b);
-    v[j] = y;
+    v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), srow), w);
+  }
+  if (has_bias) {  // warp-uniform
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __shfl_sync(kFull, b_lane, j));
   }
 }
 
@@ -224,7 +225,8 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, con
 }
 
 // --------------------------------------------------------------------------- the kernel
-template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE>
+// ODT: the output element type of the GEMM epilogues, fixed at compile time (XDNA_I32 for EPI_I32).
+template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
@@ -440,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               } else {
                 float v[32];
                 dequant32(rc, srow, fcol[c], bcol[c], has_bias, v);
-                if (args.out_dtype == XDNA_F32) {
+                if constexpr (ODT == XDNA_F32) {
                   uint32_t w[32];
 #pragma unroll
                   for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
@@ -448,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                   uint32_t w[16];
 #pragma unroll
-                  for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], args.out_dtype);
+                  for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], ODT);
                   stage_and_store<16>(obuf, w, &tmC, n0, row0);
                 }
               }
