@@ -95,6 +95,22 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
 int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,
                          int64_t Cp, float* sx, uint32_t* amax_scratch, void* stream);
 
+/* xdna_conv_quant_nhwc without caller-provided scratch: the same inputs, outputs and results, but the
+ * per-image max lives in a 16 KB array inside the library, so the call allocates nothing and takes no
+ * scratch pointer. It has no counterpart in the reference (whose quantise runs on the CPU).
+ * It is for callers that must not allocate device memory: plugins whose host framework hands them all
+ * of their memory up front and forbids allocation while serving, and latency-bound serving loops that
+ * cannot afford cudaMalloc's device-wide synchronisation.
+ * Limits and behaviour:
+ *   - at most 4096 images per call; more returns XDNA_ERR_INVALID with a message;
+ *   - the first call on each device looks up the array's device address (cudaGetSymbolAddress, with
+ *     that device current) and caches it; make that first call before any stream capture;
+ *   - every call on a device shares the one array and clears the words it uses first; calls that
+ *     overlap on the GPU (other streams, or other threads) race on it and must be serialised;
+ *   - the array stays allocated on every GPU that loaded the library until the process exits. */
+int xdna_conv_quant_nhwc_static(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,
+                                int64_t Cp, float* sx, void* stream);
+
 /* NCHW int8 xq [N, C, H, W] (the xdna::conv3x3 op's input) -> bordered NHWC xp as above. */
 int xdna_conv_pack_input(const int8_t* xq, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp, int64_t Cp,
                          void* stream);

@@ -13,6 +13,7 @@
 // differently when a half-integer lies within that distance, so whenever the product is within 1e-3
 // of a half-integer the IEEE quotient is computed instead. Every other value rounds identically.
 #include <algorithm>
+#include <mutex>
 
 #include "host_util.h"
 #include "sm100.cuh"
@@ -430,3 +431,56 @@ int xdna_conv_pack_weight(const int8_t* wq, int64_t Co, int64_t Ci, int8_t* wp, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------- no-allocation variant
+// xdna_conv_quant_nhwc needs N words of scratch (the per-image max) that its caller allocates. Some
+// callers cannot allocate: a host framework that hands a plugin all of its device memory when the
+// plugin is loaded and forbids allocation while requests are served, or a serving loop that must not
+// call cudaMalloc because it may synchronise the whole device and stall every other stream. For them
+// this variant keeps its scratch in the file-scope array below, which every GPU that loads the library
+// holds until the process exits.
+namespace xdna {
+
+constexpr int64_t kStaticScratchImages = 4096;  // 16 KB per device
+static __device__ __align__(256) uint32_t g_conv_amax_scratch[kStaticScratchImages];
+
+constexpr int kMaxStaticDevices = 64;
+static uint32_t* g_conv_amax_scratch_ptr[kMaxStaticDevices];  // its device address, per device
+static std::mutex g_conv_amax_scratch_mutex;
+
+// The device address of g_conv_amax_scratch on the current device. In host code the array's name is
+// only a host-side stand-in, never a device address, so it is looked up once per device (with that
+// device current) and cached.
+static int conv_amax_scratch(uint32_t** out) {
+  int dev = 0;
+  XDNA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxStaticDevices) return fail(XDNA_ERR_DEVICE, "device ordinal %d out of range", dev);
+  if (g_conv_amax_scratch_ptr[dev] == nullptr) {
+    std::lock_guard<std::mutex> lock(g_conv_amax_scratch_mutex);
+    if (g_conv_amax_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_conv_amax_scratch);
+      if (e != cudaSuccess)
+        return fail(XDNA_ERR_CUDA, "conv_quant_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      g_conv_amax_scratch_ptr[dev] = static_cast<uint32_t*>(p);
+    }
+  }
+  *out = g_conv_amax_scratch_ptr[dev];
+  return XDNA_OK;
+}
+
+}  // namespace xdna
+
+extern "C" int xdna_conv_quant_nhwc_static(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,
+                                           int8_t* xp, int64_t Cp, float* sx, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  if (N > kStaticScratchImages)
+    return fail(XDNA_ERR_INVALID, "conv_quant_static: %lld images; the static scratch holds at most %lld",
+                static_cast<long long>(N), static_cast<long long>(kStaticScratchImages));
+  uint32_t* scratch = nullptr;
+  rc = conv_amax_scratch(&scratch);
+  if (rc != XDNA_OK) return rc;
+  // the allocating entry point clears the N words it uses before the max kernel runs
+  return xdna_conv_quant_nhwc(x, x_dtype, N, C, H, W, xp, Cp, sx, scratch, stream);
+}
