@@ -132,6 +132,71 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
                     int64_t W, int mode, int shift, int relu, const float* scale, const float* sx, const void* bias,
                     int bias_dtype, void* out, int out_dtype, int32_t* acc_max, void* stream);
 
+/* ------------------------------------------------------------------ the Qwen3 stack (bf16)
+ * Replaces tl.extra.npu.qwen3_stack.Qwen3Stack(...)(x0, x1), the one-launch NPU program called by
+ * stack.run R:torch_xdna/stack.py:360-389, for Qwen3-0.6B's shapes (hidden 1024, 16 query / 8 kv heads
+ * of 128, MLP 3072), any depth, and extends it to causal and general masks and any length. */
+
+/* epilogues of xdna_gemm_bf16 */
+#define XDNA_GEMM_F32ACC 0 /* out = acc (+ bias[n]) in out_dtype */
+#define XDNA_GEMM_RESID 1  /* resid[m, n] += acc (f32, in place) */
+#define XDNA_GEMM_SWIGLU 2 /* B rows interleave 32 gate / 32 up rows: out[m, j] = bf16(silu(gate) * up), N/2 columns */
+#define XDNA_GEMM_QKV 3    /* N = 4096 = q 2048 | k 1024 | v 1024 columns: out [M, 3072] bf16 gets q and k after the
+                              per-head RMSNorm (q_norm / k_norm) and RoPE at position m % seq_len; vt [1024, ldvt]
+                              bf16 gets v transposed */
+
+/* attention masks */
+#define XDNA_MASK_CAUSAL 0 /* key <= query */
+#define XDNA_MASK_PREFIX 1 /* lens[b]: the first n positions see each other, later ones only themselves */
+#define XDNA_MASK_BOOL 2   /* mask [B, 1|16, L, L] bytes, nonzero = may attend */
+#define XDNA_MASK_NONE 3
+
+/* One decoder layer's weights, bf16 matrices (row-major [out, in]) and f32 norm weights. */
+typedef struct {
+  const void* w_qkv;        /* [4096, 1024]: q_proj (2048 rows), k_proj (1024), v_proj (1024) */
+  const void* w_o;          /* [1024, 2048] */
+  const void* w_gu;         /* [6144, 1024]: gate_proj / up_proj interleaved in blocks of 32 rows */
+  const void* w_down;       /* [1024, 3072] */
+  const float* input_norm;  /* [1024] */
+  const float* post_norm;   /* [1024] */
+  const float* q_norm;      /* [128] */
+  const float* k_norm;      /* [128] */
+} xdna_qwen3_layer;
+
+/* y [rows, D] bf16 = x * rsqrt(mean(x^2) + eps) * w, x f32 (D = 128, 512 or 1024). */
+int xdna_rmsnorm_bf16(const float* x, int64_t rows, int64_t D, const float* w, float eps, void* y, void* stream);
+
+/* x [tokens, D] f32 = table[ids] (bf16 or f32 table [vocab, D]); ids outside [0, vocab) give zeros and
+ * record XDNA_ERR_INVALID in the device error word. Replaces the embed_tokens lookup of the model. */
+int xdna_embed(const int64_t* ids, int64_t tokens, const void* table, int table_dtype, int64_t vocab, int64_t D,
+               float* x, void* stream);
+
+/* C [M, N] = A [M, K] . B [N, K]^T, bf16 operands (row pitches lda / ldb in elements, multiples of 8),
+ * f32 accumulation on the tcgen05 tensor cores, with one of the XDNA_GEMM_* epilogues. */
+int xdna_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K, int mode,
+                   void* out, int out_dtype, int64_t ldo, const void* bias, int bias_dtype, float* resid, int64_t ldr,
+                   void* vt, int64_t ldvt, const float* rope_cos, const float* rope_sin, const float* q_norm,
+                   const float* k_norm, int64_t seq_len, float eps, void* stream);
+
+/* out [B*L, 2048] bf16 = softmax(q k^T / sqrt(128) + mask) v for 16 query heads over 8 kv heads (GQA),
+ * q and k read from qk [B*L, 3072] (the XDNA_GEMM_QKV output), v from vt [1024, ldvt]. */
+int xdna_attention(const void* qk, const void* vt, int64_t ldvt, void* out, int64_t B, int64_t L, int mask_kind,
+                   const int32_t* lens, const uint8_t* mask, int mask_heads, void* stream);
+
+/* Bytes of workspace xdna_qwen3_stack needs for B sequences of L tokens. */
+size_t xdna_qwen3_stack_workspace(int64_t B, int64_t L);
+
+/* The whole stack: x [B*L, 1024] f32 (the hidden states, updated in place as the residual stream)
+ * through n_layers decoder layers, the final RMSNorm and the head: out [B*L, head_n] (row pitch ldo)
+ * = h Whead^T (+ bias) in out_dtype. rope_cos / rope_sin: [L, 64] f32 tables of the model's inverse
+ * frequencies at positions 0..L-1. With out == NULL the head is skipped and the final-normed hidden
+ * states [B*L, 1024] bf16 are left at the start of the workspace. */
+int xdna_qwen3_stack(const xdna_qwen3_layer* layers, int n_layers, const float* final_norm, const void* head_w,
+                     int64_t head_n, const void* head_bias, int head_bias_dtype, const float* rope_cos,
+                     const float* rope_sin, float eps, float* x, int64_t B, int64_t L, int mask_kind,
+                     const int32_t* lens, const uint8_t* mask, int mask_heads, void* out, int out_dtype, int64_t ldo,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

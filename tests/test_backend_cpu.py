@@ -160,6 +160,63 @@ def test_no_gpu_fails_loudly():
         kernels.require()
 
 
+def test_stack_found_in_qwen3_graph():
+    """The FX search finds transformers' Qwen3Model + head (2 layers), its mask input and its head bias."""
+    from transformers import Qwen3Config, Qwen3Model
+
+    from torch_xdna import stack
+
+    class Stack(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            cfg = Qwen3Config(hidden_size=1024, intermediate_size=3072, num_hidden_layers=2, num_attention_heads=16,
+                              num_key_value_heads=8, head_dim=128, vocab_size=16, rms_norm_eps=1e-6,
+                              rope_parameters={"rope_type": "default", "rope_theta": 1e6}, attn_implementation="sdpa")
+            self.llm = Qwen3Model(cfg)
+            self.head = torch.nn.Linear(1024, 1000)
+
+        def forward(self, x, mask):
+            return self.head(self.llm(inputs_embeds=x, attention_mask=mask)[0])
+
+    plans = []
+
+    def backend(gm, example_inputs):
+        plans.append(stack.find(gm, example_inputs))
+        return gm.forward
+
+    torch._dynamo.reset()
+    mask = torch.ones(24, 24, dtype=torch.bool).tril().expand(2, 1, 24, 24).contiguous()
+    with torch.no_grad():
+        torch.compile(Stack().eval(), backend=backend)(torch.randn(2, 24, 1024), mask)
+    plan = plans[0]
+    assert plan is not None and plan.layers == 2 and plan.out_features == 1000 and plan.bias is not None
+    assert len(plan.tensors()) == 2 * 11 + 3
+
+
+def test_stack_mask_classification():
+    from torch_xdna import kernels, stack
+
+    import make_golden as mg
+
+    L = 40
+    causal = torch.ones(L, L, dtype=torch.bool).tril().expand(3, 1, L, L)
+    assert stack.classify(causal, 3, L)[0] == kernels.MASK_CAUSAL
+    prefix = torch.from_numpy(mg.prefix_mask([40, 29, 17], L))
+    kind, lens, _ = stack.classify(prefix, 3, L)
+    assert kind == kernels.MASK_PREFIX and lens.tolist() == [40, 29, 17]
+    assert stack.lengths(prefix) == [40, 29, 17]
+    full = torch.zeros(3, 1, L, L)                       # float mask, all 0: attend everywhere
+    assert stack.classify(full, 3, L)[0] == kernels.MASK_NONE
+    other = causal.clone()
+    other[0, 0, 5, 2] = False
+    kind, _, m = stack.classify(other, 3, L)
+    assert kind == kernels.MASK_BOOL and m.dtype == torch.uint8 and m.shape == (3, 1, L, L)
+    bad = torch.zeros(3, 1, L, L)
+    bad[0, 0, 0, 1] = -0.5                               # an additive bias, not a mask
+    assert stack.classify(bad, 3, L) is None
+    assert stack.classify(causal[:, :, :, :L - 1], 3, L) is None
+
+
 def test_report_formats():
     torch_xdna.stats.reset()
     s = torch_xdna.report()

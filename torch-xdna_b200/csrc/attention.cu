@@ -1,0 +1,416 @@
+// GQA flash attention for the Qwen3 stack on tcgen05 (sm_100a): softmax(Q K^T / sqrt(128) + mask) V
+// for 16 query heads sharing 8 key/value heads of dimension 128 (R:torch_xdna/stack.py:43-57).
+//
+// One CTA = 128 queries of one query head of one sequence; 192 threads:
+//   warp 0      TMA: the Q tile once, then K and V^T blocks of 128 keys into a 2-stage ring
+//               (Q and K read from the q/k projection output [T, 3072] bf16, V^T from [1024, T] bf16,
+//               which the projection epilogue wrote transposed so that P.V has a K-major B operand);
+//   warp 1      TMEM (512 columns: two S buffers, two O buffers) and the MMAs:
+//               S_j = Q K_j^T (8 x tcgen05.mma 128x128x16), O_j = P_j V_j (8 more), issued as
+//               S_0, S_1, O_0, S_2, O_1, ... so each S overlaps the previous block's softmax;
+//   warps 2..5  softmax: thread i owns query row i. Two passes over S_j in TMEM (row max, then
+//               exp2 and the row sum), P_j written as bf16 into a 128-byte-swizzled K-major tile,
+//               and O accumulated in registers: O = O * exp2(m_old - m_new) + O_j, l likewise.
+//               The output row is O / l in bf16, written to [T, 2048].
+// Masks: causal, per-sequence prefix blocks (the reference's OmniVoice layout: the first n
+// positions see each other, later ones only themselves), a general bool mask [B, 1|H, L, L], or none.
+// Keys past the sequence end are always masked. Every mbarrier wait is bounded (sm100.cuh).
+#include <algorithm>
+
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace xdna {
+
+enum MaskKind { MASK_CAUSAL = 0, MASK_PREFIX = 1, MASK_BOOL = 2, MASK_NONE = 3 };
+
+struct AttnArgs {
+  __nv_bfloat16* out;     // [T, 2048]
+  int T, L;               // tokens in all, tokens per sequence
+  int L8;                 // round_up(L, 8): V^T column pitch of a sequence
+  int q_blocks;           // ceil(L / 128)
+  int heads_per_kv;       // 2
+  float scale_log2;       // log2(e) / sqrt(128)
+  const int32_t* lens;    // MASK_PREFIX: per-sequence length
+  const uint8_t* mask;    // MASK_BOOL: [B, Hm, L, L]
+  int mask_heads;         // Hm: 1 or 16
+  int* err;
+};
+
+constexpr int kAttnThreads = 192;
+constexpr int kTileBytes = 128 * 128;  // one 128-row x 128-byte operand k-block
+constexpr int kKvStages = 2;
+constexpr int kAttnSmem = (2 /*Q*/ + 2 * kKvStages /*K*/ + 2 * kKvStages /*V*/ + 2 /*P*/) * kTileBytes + 1024 + 256;
+
+__device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ bool key_allowed(int kind, const AttnArgs& a, int seq, int head, int q, int k) {
+  if (k >= a.L) return false;
+  switch (kind) {
+    case MASK_CAUSAL:
+      return k <= q;
+    case MASK_PREFIX: {
+      const int n = a.lens[seq];
+      return q < n ? k < n : k == q;
+    }
+    case MASK_BOOL:
+      return a.mask[((static_cast<int64_t>(seq) * a.mask_heads + (a.mask_heads > 1 ? head : 0)) * a.L + q) * a.L + k] != 0;
+    default:
+      return true;
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmVt,
+                     const AttnArgs args) {
+  constexpr uint32_t IDESC = idesc_bf16(128, 128);
+  constexpr uint32_t TX = 2 * kTileBytes;  // one Q tile, or one K block, or one V^T block
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smQ = smem;
+  uint8_t* smK = smQ + 2 * kTileBytes;
+  uint8_t* smV = smK + 2 * kKvStages * kTileBytes;
+  uint8_t* smP = smV + 2 * kKvStages * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smP + 2 * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;                 // [kKvStages]
+  uint64_t* kv_empty = kv_full + kKvStages;     // [kKvStages]
+  uint64_t* s_full = kv_empty + kKvStages;      // [2]
+  uint64_t* s_empty = s_full + 2;               // [2]
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* p_empty = p_full + 1;
+  uint64_t* o_full = p_empty + 1;               // [2]
+  uint64_t* o_empty = o_full + 2;               // [2]
+  uint64_t* drain = o_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  // heaviest causal blocks first
+  const int qb = KIND == MASK_CAUSAL ? args.q_blocks - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
+  const int head = blockIdx.y;
+  const int seq = blockIdx.z;
+  const int kvh = head / args.heads_per_kv;
+  const int q0 = qb * 128;                 // first query position in the sequence
+  const int tok0 = seq * args.L;           // first token of the sequence
+  const int kv_blocks = KIND == MASK_CAUSAL ? qb + 1 : (args.L + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kKvStages; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full + b, 1);
+      mbar_init(s_empty + b, 4);
+      mbar_init(o_full + b, 1);
+      mbar_init(o_empty + b, 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQK);
+    tma_prefetch_desc(&tmVt);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO[2] = {tmem + 256, tmem + 384};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ TMA
+      mbar_arrive_expect_tx(q_full, TX);
+      for (int kk = 0; kk < 2; ++kk)
+        tma_load_2d(smQ + kk * kTileBytes, &tmQK, q_full, head * 128 + kk * 64, tok0 + q0);
+      int last_parity[kKvStages] = {-1, -1};
+      for (int j = 0; j < kv_blocks; ++j) {
+        const int st = j % kKvStages;
+        const uint32_t ph = (j / kKvStages) & 1;
+        if (!mbar_wait(kv_empty + st, ph ^ 1, abort_flag, args.err, 21)) break;
+        mbar_arrive_expect_tx(kv_full + st, 2 * TX);
+        for (int kk = 0; kk < 2; ++kk) {
+          tma_load_2d(smK + (st * 2 + kk) * kTileBytes, &tmQK, kv_full + st, 16 * 128 + kvh * 128 + kk * 64,
+                      tok0 + j * 128);
+          // V^T column = seq * L8 + key: a multiple of 8 elements, the 16-byte TMA alignment
+          tma_load_2d(smV + (st * 2 + kk) * kTileBytes, &tmVt, kv_full + st, seq * args.L8 + j * 128 + kk * 64,
+                      kvh * 128);
+        }
+        last_parity[st] = static_cast<int>(ph);
+      }
+      volatile int never = 0;
+      mbar_wait(q_full, 0, &never, args.err, 22);
+      for (int s = 0; s < kKvStages; ++s)
+        if (last_parity[s] >= 0) mbar_wait(kv_full + s, static_cast<uint32_t>(last_parity[s]), &never, args.err, 22);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ MMA
+      bool ok = mbar_wait(q_full, 0, abort_flag, args.err, 23);
+      bool issued = false;
+      const uint64_t dQ[2] = {smem_desc_k_sw128(smem_u32(smQ)), smem_desc_k_sw128(smem_u32(smQ + kTileBytes))};
+      const uint64_t dP[2] = {smem_desc_k_sw128(smem_u32(smP)), smem_desc_k_sw128(smem_u32(smP + kTileBytes))};
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i % kKvStages;
+        if (!mbar_wait(p_full, i & 1, abort_flag, args.err, 24)) return false;
+        if (!mbar_wait(o_empty + (i & 1), ((i >> 1) & 1) ^ 1, abort_flag, args.err, 25)) return false;
+        tc_fence_after();
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t dV = smem_desc_k_sw128(smem_u32(smV + (st * 2 + kk) * kTileBytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_f16(tO[i & 1], dP[kk] + 2 * k, dV + 2 * k, IDESC, (kk | k) != 0);
+        }
+        umma_commit(o_full + (i & 1));
+        umma_commit(p_empty);
+        umma_commit(kv_empty + st);
+        issued = true;
+        return true;
+      };
+      for (int j = 0; ok && j < kv_blocks; ++j) {
+        const int st = j % kKvStages;
+        if (!mbar_wait(kv_full + st, (j / kKvStages) & 1, abort_flag, args.err, 26)) break;
+        if (!mbar_wait(s_empty + (j & 1), ((j >> 1) & 1) ^ 1, abort_flag, args.err, 27)) break;
+        tc_fence_after();
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t dK = smem_desc_k_sw128(smem_u32(smK + (st * 2 + kk) * kTileBytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_f16(tS[j & 1], dQ[kk] + 2 * k, dK + 2 * k, IDESC, (kk | k) != 0);
+        }
+        umma_commit(s_full + (j & 1));
+        issued = true;
+        if (j >= 1 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && kv_blocks > 0) issue_pv(kv_blocks - 1);
+      if (issued) {
+        umma_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never, args.err, 28);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------------- softmax (warps 2..5)
+    const int qd = warp & 3;                 // TMEM lane quadrant = row block
+    const int r = qd * 32 + lane;            // query row within the tile
+    const int qpos = q0 + r;                 // query position in the sequence
+    const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+    float o[128];
+#pragma unroll
+    for (int d = 0; d < 128; ++d) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    bool ok = true;
+    uint32_t v[32];
+    for (int j = 0; j < kv_blocks && ok; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(s_full + b, (j >> 1) & 1, abort_flag, args.err, 31)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int k0 = j * 128;
+      // pass 1: the row max of the scaled, masked scores
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        __syncwarp();
+        tmem_ld_32x32b_x32(tS[b] + lane_off + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kpos = k0 + c * 32 + e;
+          const float s = key_allowed(KIND, args, seq, head, qpos, kpos) ? __uint_as_float(v[e]) * args.scale_log2
+                                                                          : -INFINITY;
+          mx = fmaxf(mx, s);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = m_new == -INFINITY ? 1.f : exp2f(m - m_new);
+      // P_j may be written once P_{j-1} has been consumed by its MMA
+      if (j >= 1 && !mbar_wait(p_empty, (j - 1) & 1, abort_flag, args.err, 32)) {
+        ok = false;
+        break;
+      }
+      // pass 2: p = exp2(s - m_new) as bf16 into the swizzled K-major P tile, and the row sum
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        __syncwarp();
+        tmem_ld_32x32b_x32(tS[b] + lane_off + c * 32, v);
+        tmem_ld_wait();
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p2[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int kpos = k0 + c * 32 + e + t;
+            const bool okk = key_allowed(KIND, args, seq, head, qpos, kpos) && m_new != -INFINITY;
+            p2[t] = okk ? exp2f(__uint_as_float(v[e + t]) * args.scale_log2 - m_new) : 0.f;
+          }
+          const __nv_bfloat162 h = __floats2bfloat162_rn(p2[0], p2[1]);
+          // the row sum takes the bf16-rounded probabilities the MMA will use
+          const float2 hf = __bfloat1622float2(h);
+          rs += hf.x + hf.y;
+          w[e / 2] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        // 32 keys = 64 bytes = 4 chunks of 16 bytes in k-block c / 2, chunk offset (c % 2) * 4
+        uint8_t* rowp = smP + (c >> 1) * kTileBytes + r * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (c & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) * 16)) =
+              make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        }
+      }
+      // S_j is no longer needed in TMEM; P_j is ready for the MMA
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_empty + b);
+        mbar_arrive(p_full);
+      }
+      l = l * alpha + rs;
+      m = m_new;
+      // fold in O_{j-1} (scaled by its own alpha) while the MMA computes O_j
+      if (j >= 1) {
+        const int ob = (j - 1) & 1;
+        if (!mbar_wait(o_full + ob, ((j - 1) >> 1) & 1, abort_flag, args.err, 33)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          __syncwarp();
+          tmem_ld_32x32b_x32(tO[ob] + lane_off + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_empty + ob);
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && kv_blocks > 0) {
+      const int last = kv_blocks - 1;
+      const int ob = last & 1;
+      if (mbar_wait(o_full + ob, (last >> 1) & 1, abort_flag, args.err, 34)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          __syncwarp();
+          tmem_ld_32x32b_x32(tO[ob] + lane_off + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
+        }
+        tc_fence_before();
+        // the output row: O / l in bf16, 256 contiguous bytes
+        if (qpos < args.L) {
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<int64_t>(tok0 + qpos) * (16 * 128) + head * 128);
+#pragma unroll
+          for (int d = 0; d < 128; d += 8) {
+            uint4 u;
+            u.x = pack2_bf16(o[d] * inv, o[d + 1] * inv);
+            u.y = pack2_bf16(o[d + 2] * inv, o[d + 3] * inv);
+            u.z = pack2_bf16(o[d + 4] * inv, o[d + 5] * inv);
+            u.w = pack2_bf16(o[d + 6] * inv, o[d + 7] * inv);
+            dst[d / 8] = u;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace xdna
+
+namespace xdna {
+
+int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt, __nv_bfloat16* out, int64_t B,
+                  int64_t L, int mask_kind, const int32_t* lens, const uint8_t* mask, int mask_heads,
+                  cudaStream_t stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(B >= 1 && L >= 1 && B <= 65535, "attention: bad batch / length");
+  XDNA_CHECK_ARG(qk && vt && out, "attention: null pointer");
+  const int64_t T = B * L;
+  const int64_t L8 = (L + 7) / 8 * 8;
+  XDNA_CHECK_ARG(ldvt >= B * L8 && ldvt % 8 == 0,
+                 "attention: V^T row pitch must cover B x round_up(L, 8) columns and be a multiple of 8");
+  XDNA_CHECK_ARG(mask_kind >= MASK_CAUSAL && mask_kind <= MASK_NONE, "attention: unknown mask kind %d", mask_kind);
+  XDNA_CHECK_ARG(mask_kind != MASK_PREFIX || lens != nullptr, "attention: prefix masks need lengths");
+  XDNA_CHECK_ARG(mask_kind != MASK_BOOL || (mask != nullptr && (mask_heads == 1 || mask_heads == 16)),
+                 "attention: bool masks need a [B, 1|16, L, L] mask");
+  CUtensorMap tq, tv;
+  {
+    const uint64_t dims[2] = {3072, static_cast<uint64_t>(T)};
+    const uint64_t strides[1] = {3072 * 2};
+    const uint32_t box[2] = {64, 128};
+    if ((rc = encode_tma(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qk, dims, strides, box, "attention q/k")) != XDNA_OK)
+      return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(B * L8), 1024};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldvt * 2)};
+    const uint32_t box[2] = {64, 128};
+    if ((rc = encode_tma(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, vt, dims, strides, box, "attention v^T")) != XDNA_OK)
+      return rc;
+  }
+  AttnArgs a{};
+  a.out = out;
+  a.T = static_cast<int>(T);
+  a.L = static_cast<int>(L);
+  a.L8 = static_cast<int>(L8);
+  a.q_blocks = static_cast<int>((L + 127) / 128);
+  a.heads_per_kv = 2;
+  a.scale_log2 = 1.4426950408889634f / sqrtf(128.f);
+  a.lens = lens;
+  a.mask = mask;
+  a.mask_heads = mask_heads;
+  a.err = device_error_word();
+  dim3 grid(static_cast<unsigned>(a.q_blocks), 16, static_cast<unsigned>(B));
+  static bool configured[4][64] = {};
+  int dev = 0;
+  XDNA_CUDA(cudaGetDevice(&dev));
+  void (*kern)(const CUtensorMap, const CUtensorMap, const AttnArgs) =
+      mask_kind == MASK_CAUSAL   ? attention_kernel<MASK_CAUSAL>
+      : mask_kind == MASK_PREFIX ? attention_kernel<MASK_PREFIX>
+      : mask_kind == MASK_BOOL   ? attention_kernel<MASK_BOOL>
+                                 : attention_kernel<MASK_NONE>;
+  if (dev < 0 || dev >= 64 || !configured[mask_kind][dev]) {
+    XDNA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+    if (dev >= 0 && dev < 64) configured[mask_kind][dev] = true;
+  }
+  kern<<<grid, kAttnThreads, kAttnSmem, stream>>>(tq, tv, a);
+  return check_launch("attention_kernel");
+}
+
+}  // namespace xdna

@@ -34,7 +34,17 @@ enum EpiMode {
   EPI_CONV_Q = 2,      // requantised int8 / uint8, NCHW
   EPI_CONV_DEQ = 3,    // requantised then dequantised, NCHW
   EPI_CONV_CALIB = 4,  // max of the sums (of image 0) into one int32
+  // bf16 GEMMs of the Qwen3 stack (f32 accumulators)
+  EPI_F32ACC = 5,      // acc (+ bias[n]) -> f32 / bf16 / f16 (the head; precision="bf16" linears)
+  EPI_RESID = 6,       // resid_f32[m, n] += acc (o-proj and down-proj into the residual stream)
+  EPI_SWIGLU = 7,      // columns come as 32 gate / 32 up pairs: act = silu(gate) * up -> bf16
+  EPI_QKV = 8,         // q / k heads: RMSNorm over the head + weight + RoPE -> bf16; v heads -> bf16 V^T
 };
+
+// Geometry of the fused q/k/v projection (Qwen3-0.6B): 16 q heads, 8 k heads, 8 v heads of 128.
+constexpr int kHeadDim = 128;
+constexpr int kQCols = 16 * kHeadDim;
+constexpr int kKCols = 8 * kHeadDim;
 
 struct GemmArgs {
   int M, N;            // output rows (GEMM rows, or bordered pixels for the conv) and columns
@@ -56,6 +66,18 @@ struct GemmArgs {
   int shift, relu;
   int* acc_max;
   int* err;
+  // stack epilogues
+  float* resid;        // EPI_RESID: [M, ldr] f32, updated in place
+  int64_t ldr;
+  __nv_bfloat16* vt;   // EPI_QKV: V^T [8 * 128, ldvt] bf16 (row = v head * 128 + d; column = sequence *
+                       // round_up(seq_len, 8) + position)
+  int64_t ldvt;
+  const float* rope_cos;  // EPI_QKV: [seq_len, 64] f32 tables for positions 0..seq_len-1
+  const float* rope_sin;
+  const float* q_norm;    // EPI_QKV: [128] f32 per-head RMSNorm weights
+  const float* k_norm;
+  int seq_len;         // token m sits at position m % seq_len of its sequence
+  float eps;
 };
 
 constexpr int kBM = 128;
@@ -221,6 +243,105 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, con
       if (a.bias != nullptr) y = __fadd_rn(y, load_as_float(a.bias, a.bias_dtype, n0 + j));
       store_one(a.out, a.out_dtype, base + j * HW, y);
     }
+  }
+}
+
+// --------------------------------------------------------------------------- stack epilogues (bf16)
+__device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u); }
+
+// One warp's half-tile of the fused q/k/v projection: exactly one head (128 columns) of its 32 rows.
+// q and k heads (R:torch_xdna/stack.py:43-57; transformers' Qwen3 attention): per-head RMSNorm in f32
+// (x * rsqrt(mean(x^2) + eps)) times the norm weight, then RoPE with the half rotation
+// (out[d] = x[d] cos - x[d+64] sin, out[d+64] = x[d+64] cos + x[d] sin), stored bf16 through TMA.
+// v heads are written transposed, V^T[head * 128 + d][token], the K-major operand of P.V.
+__device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, uint8_t* obuf,
+                                         const CUtensorMap* tmC) {
+  const int lane = lane_id();
+  const int row = row0 + lane;
+  uint32_t x1[32], x2[32];
+  if (col0 >= kQCols + kKCols) {  // a v head (warp-uniform)
+    const int vh = (col0 - kQCols - kKCols) / kHeadDim;
+    // V^T columns: each sequence starts at a multiple of 8 tokens (TMA reads them as 16-byte aligned boxes)
+    const int l8 = (a.seq_len + 7) / 8 * 8;
+    const int64_t vcol = static_cast<int64_t>(row / a.seq_len) * l8 + row % a.seq_len;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      __syncwarp();
+      tmem_ld_32x32b_x32(taddr + c * 32, x1);
+      tmem_ld_wait();
+      if (row < a.M) {
+        __nv_bfloat16* dst = a.vt + static_cast<int64_t>(vh * kHeadDim + c * 32) * a.ldvt + vcol;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dst[static_cast<int64_t>(j) * a.ldvt] = __float2bfloat16_rn(f32_of(x1[j]));
+      }
+    }
+    return;
+  }
+  // pass 1: sum of squares over the head's 128 values
+  float ss = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    __syncwarp();
+    tmem_ld_32x32b_x32(taddr + c * 32, x1);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) ss = fmaf(f32_of(x1[j]), f32_of(x1[j]), ss);
+  }
+  const float rstd = rsqrtf(ss * (1.0f / kHeadDim) + a.eps);
+  const float* nw = col0 < kQCols ? a.q_norm : a.k_norm;
+  const float w_lane[4] = {nw[lane], nw[32 + lane], nw[64 + lane], nw[96 + lane]};
+  const int pos = (row < a.M ? row : 0) % a.seq_len;
+  const float* cs = a.rope_cos + static_cast<int64_t>(pos) * (kHeadDim / 2);
+  const float* sn = a.rope_sin + static_cast<int64_t>(pos) * (kHeadDim / 2);
+  // pass 2: columns d and d + 64 together (the RoPE pairs), 32 at a time
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    __syncwarp();
+    tmem_ld_32x32b_x32(taddr + c * 32, x1);
+    tmem_ld_32x32b_x32(taddr + 64 + c * 32, x2);
+    tmem_ld_wait();
+    uint32_t lo[16], hi[16];
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float u = f32_of(x1[j + e]) * rstd * __shfl_sync(kFull, w_lane[c], j + e);
+        const float v = f32_of(x2[j + e]) * rstd * __shfl_sync(kFull, w_lane[c + 2], j + e);
+        const float co = cs[c * 32 + j + e], si = sn[c * 32 + j + e];
+        o[e] = u * co - v * si;
+        o[2 + e] = v * co + u * si;
+      }
+      lo[j / 2] = pack2(o[0], o[1], XDNA_BF16);
+      hi[j / 2] = pack2(o[2], o[3], XDNA_BF16);
+    }
+    stage_and_store<16>(obuf, lo, tmC, col0 + c * 32, row0);
+    stage_and_store<16>(obuf, hi, tmC, col0 + 64 + c * 32, row0);
+  }
+}
+
+// One warp's half-tile of the fused gate/up projection. The packed weight interleaves 32 gate rows
+// and the matching 32 up rows, so accumulator chunks 2p and 2p+1 are gate and up of the same 32
+// output columns: act = silu(gate) * up (f32), stored bf16 at act column col0 / 2 + 32 p.
+template <int NCH>
+__device__ __forceinline__ void swiglu_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, uint8_t* obuf,
+                                            const CUtensorMap* tmC) {
+  uint32_t g[32], u[32];
+#pragma unroll 1
+  for (int p = 0; p < NCH / 2; ++p) {
+    __syncwarp();
+    tmem_ld_32x32b_x32(taddr + p * 64, g);
+    tmem_ld_32x32b_x32(taddr + p * 64 + 32, u);
+    tmem_ld_wait();
+    uint32_t w[16];
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      const float g0 = f32_of(g[j]), g1 = f32_of(g[j + 1]);
+      const float a0 = g0 / (1.0f + expf(-g0)) * f32_of(u[j]);
+      const float a1 = g1 / (1.0f + expf(-g1)) * f32_of(u[j + 1]);
+      w[j / 2] = pack2(a0, a1, XDNA_BF16);
+    }
+    if (col0 / 2 + p * 32 < a.N / 2) stage_and_store<16>(obuf, w, tmC, col0 / 2 + p * 32, row0);
   }
 }
 
@@ -409,6 +530,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (has_bias) bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
           }
         }
+        if constexpr (EPI == EPI_F32ACC) {
+          if (n < args.N && has_bias) bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
+        }
       }
       if constexpr (EPI == EPI_DEQ) srow = row < args.M ? __ldg(args.sx + row) : 0.f;
 
@@ -416,6 +540,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + half * WCOLS);
+      if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
+        if (col0 < args.N) {  // warp-uniform
+          if constexpr (EPI == EPI_QKV)
+            qkv_tile(args, taddr, row0, col0, obuf, &tmC);
+          else
+            swiglu_tile<NCH>(args, taddr, row0, col0, obuf, &tmC);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty + buf);
+      } else {
       uint32_t r[2][32];
       __syncwarp();
       tmem_ld_32x32b_x32(taddr, r[0]);
@@ -459,12 +594,57 @@ __global__ void __launch_bounds__(kThreads, 1)
               if constexpr (EPI == EPI_DEQ) dequant32(rc, srow, fcol[c], bcol[c], has_bias, v);
               store_direct<EPI>(args, row, n0, rc, v);
             }
+          } else if constexpr (EPI == EPI_F32ACC) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = f32_of(rc[j]);
+            if (has_bias) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __shfl_sync(kFull, bcol[c], j));
+            }
+            if constexpr (TSTORE) {
+              if constexpr (ODT == XDNA_F32) {
+                uint32_t w[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
+                stage_and_store<32>(obuf, w, &tmC, n0, row0);
+              } else {
+                uint32_t w[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], ODT);
+                stage_and_store<16>(obuf, w, &tmC, n0, row0);
+              }
+            } else {
+              store_direct<EPI>(args, row, n0, rc, v);
+            }
+          } else if constexpr (EPI == EPI_RESID) {
+            // resid[row, n0..n0+31] += acc: 128 contiguous bytes per thread
+            if (row < args.M) {
+              float* res = args.resid + static_cast<int64_t>(row) * args.ldr + n0;
+              if (n0 + 32 <= args.N) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                  float4 o = *reinterpret_cast<float4*>(res + j);
+                  o.x += f32_of(rc[j]);
+                  o.y += f32_of(rc[j + 1]);
+                  o.z += f32_of(rc[j + 2]);
+                  o.w += f32_of(rc[j + 3]);
+                  *reinterpret_cast<float4*>(res + j) = o;
+                }
+              } else {
+                const int nv = args.N - n0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nv) res[j] += f32_of(rc[j]);
+              }
+            }
           } else {
             conv_chunk<EPI>(args, row, n0, rc, fcol[c]);
           }
         }
         if (c + 1 < NCH) tmem_ld_wait();
       }
+      }  // generic chunk loop
       if (++buf == 2) {
         buf = 0;
         bphase ^= 1;

@@ -60,6 +60,14 @@ def _load():
         "xdna_conv_pack_input": ([P, I64, I64, I64, I64, P, I64, P], I),
         "xdna_conv_pack_weight": ([P, I64, I64, P, I64, P], I),
         "xdna_conv3x3_i8": ([P, P, I64, I64, I64, I64, I64, I64, I, I, I, P, P, P, I, P, I, P, P], I),
+        "xdna_rmsnorm_bf16": ([P, I64, I64, P, ctypes.c_float, P, P], I),
+        "xdna_embed": ([P, I64, P, I, I64, I64, P, P], I),
+        "xdna_gemm_bf16": ([P, I64, P, I64, I64, I64, I64, I, P, I, I64, P, I, P, I64, P, I64, P, P, P, P, I64,
+                            ctypes.c_float, P], I),
+        "xdna_attention": ([P, P, I64, P, I64, I64, I, P, P, I, P], I),
+        "xdna_qwen3_stack_workspace": ([I64, I64], ctypes.c_size_t),
+        "xdna_qwen3_stack": ([P, I, P, P, I64, P, I, P, P, ctypes.c_float, P, I64, I64, I, P, P, I, P, I, I64, P,
+                              ctypes.c_size_t, P], I),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -206,3 +214,70 @@ def conv3x3(xp, wp, N, Ci, Co, H, W, mode, shift=1, relu=False, scale=None, sx=N
         _p(xp), _p(wp), N, Ci, Cp, Co, H, W, mode, shift, int(bool(relu)), _p(scale), _p(sx), _p(bias),
         DTYPE_CODES[bias.dtype] if bias is not None else F32, _p(out),
         DTYPE_CODES[out.dtype] if out is not None else I8, _p(acc_max), _stream()))
+
+
+# ---------------------------------------------------------------- the Qwen3 stack (bf16)
+GEMM_F32ACC, GEMM_RESID, GEMM_SWIGLU, GEMM_QKV = 0, 1, 2, 3
+MASK_CAUSAL, MASK_PREFIX, MASK_BOOL, MASK_NONE = 0, 1, 2, 3
+
+
+class Qwen3Layer(ctypes.Structure):
+    """xdna_qwen3_layer: one decoder layer's device pointers."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("w_qkv", "w_o", "w_gu", "w_down", "input_norm", "post_norm", "q_norm",
+                                                 "k_norm")]
+
+
+def rmsnorm_bf16(x, w, eps, y):
+    L = require()
+    _cuda(x, w, y)
+    rows, D = x.shape
+    _check("xdna_rmsnorm_bf16", L.xdna_rmsnorm_bf16(_p(x), rows, D, _p(w), eps, _p(y), _stream()))
+
+
+def embed(ids, table, x):
+    L = require()
+    _cuda(ids, table, x)
+    _check("xdna_embed", L.xdna_embed(_p(ids), ids.numel(), _p(table), DTYPE_CODES[table.dtype], table.shape[0],
+                                      table.shape[1], _p(x), _stream()))
+
+
+def gemm_bf16(a, b, mode, out=None, bias=None, resid=None, vt=None, rope_cos=None, rope_sin=None, q_norm=None,
+              k_norm=None, seq_len=0, eps=1e-6, M=None):
+    """C = a[:, :K] . b[:, :K]^T (bf16) with the epilogue `mode` (GEMM_*); see include/xdna_b200.h."""
+    L = require()
+    _cuda(a, b, out, bias, resid, vt, rope_cos, rope_sin, q_norm, k_norm)
+    M = a.shape[0] if M is None else M
+    N, K = b.shape[0], a.shape[1]
+    _check("xdna_gemm_bf16", L.xdna_gemm_bf16(
+        _p(a), a.stride(0), _p(b), b.stride(0), M, N, K, mode, _p(out),
+        DTYPE_CODES[out.dtype] if out is not None else BF16, out.stride(0) if out is not None else 0,
+        _p(bias), DTYPE_CODES[bias.dtype] if bias is not None else F32, _p(resid),
+        resid.stride(0) if resid is not None else 0, _p(vt), vt.stride(0) if vt is not None else 0,
+        _p(rope_cos), _p(rope_sin), _p(q_norm), _p(k_norm), seq_len, eps, _stream()))
+
+
+def attention(qk, vt, out, B, L_, mask_kind, lens=None, mask=None):
+    L = require()
+    _cuda(qk, vt, out, lens, mask)
+    mh = mask.shape[1] if mask is not None else 1
+    _check("xdna_attention", L.xdna_attention(_p(qk), _p(vt), vt.stride(0), _p(out), B, L_, mask_kind, _p(lens),
+                                              _p(mask), mh, _stream()))
+
+
+def qwen3_stack_workspace(B, L_):
+    return int(require().xdna_qwen3_stack_workspace(B, L_))
+
+
+def qwen3_stack(layers, final_norm, head_w, head_bias, rope_cos, rope_sin, eps, x, B, L_, mask_kind, lens, mask,
+                out, workspace):
+    """The whole stack through xdna_qwen3_stack. layers: a ctypes array of Qwen3Layer."""
+    L = require()
+    _cuda(final_norm, head_w, head_bias, rope_cos, rope_sin, x, lens, mask, out, workspace)
+    mh = mask.shape[1] if mask is not None else 1
+    _check("xdna_qwen3_stack", L.xdna_qwen3_stack(
+        ctypes.cast(layers, ctypes.c_void_p), len(layers), _p(final_norm), _p(head_w), head_w.shape[0],
+        _p(head_bias), DTYPE_CODES[head_bias.dtype] if head_bias is not None else F32, _p(rope_cos), _p(rope_sin),
+        eps, _p(x), B, L_, mask_kind, _p(lens), _p(mask), mh, _p(out),
+        DTYPE_CODES[out.dtype] if out is not None else F32, out.stride(0) if out is not None else 0,
+        _p(workspace), workspace.numel() * workspace.element_size(), _stream()))
