@@ -13,9 +13,16 @@ TOL = 2e-2   # logits: max-abs relative to the fp32 model
 
 
 @pytest.fixture(autouse=True)
-def _inference():
+def _inference(request):
+    """Inference only; each test starts with a clear device error word and must leave it clear."""
+    from torch_xdna import kernels
+
+    if "cuda" in request.fixturenames:
+        kernels.take_device_error()
     with torch.no_grad():
         yield
+    if "cuda" in request.fixturenames:
+        assert kernels.take_device_error() == (0, 0), "a kernel recorded a device-side timeout"
 
 
 def rel_max(got, want):

@@ -153,13 +153,12 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
   a.N = static_cast<int>(g.N);
   a.num_kb = static_cast<int>((g.K + 63) / 64);
   a.m_tiles = static_cast<int>((g.M + kBM - 1) / kBM);
+  // 256-column tiles, or 128 when 256 would leave SMs idle (F32ACC / RESID; the fused q/k/v and SwiGLU
+  // epilogues need the 256-column tile)
   int bn = 256;
-  if (g.mode == XDNA_GEMM_F32ACC || g.mode == XDNA_GEMM_RESID) {
-    if (g.N <= 64)
-      bn = 64;
-    else if (g.N <= 128 || a.m_tiles * ((g.N + 255) / 256) < sms)
-      bn = 128;
-  }
+  if ((g.mode == XDNA_GEMM_F32ACC || g.mode == XDNA_GEMM_RESID) &&
+      (g.N <= 128 || a.m_tiles * ((g.N + 255) / 256) < sms))
+    bn = 128;
   a.n_tiles = static_cast<int>((g.N + bn - 1) / bn);
   a.out = g.out;
   a.ldo = g.ldo;
