@@ -49,10 +49,19 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="xdna", choices=["xdna", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "square"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "square", "stack", "conv"],
+                    help="cfg2: W8A8 projection set (default); square: 4096^3 int8 GEMM; stack: BASELINE config 5; "
+                         "conv: BASELINE config 4")
     ap.add_argument("--rows", type=int, default=8192)
     ap.add_argument("--cpu-rows", type=int, default=1024, help="row sample of the CPU baseline")
-    return ap.parse_args()
+    ap.add_argument("--seqs", type=int, default=16, help="stack: sequences in the global batch")
+    ap.add_argument("--seq-len", type=int, default=1024, help="stack: tokens per sequence")
+    ap.add_argument("--layers", type=int, default=28, help="stack: decoder layers")
+    ap.add_argument("--images", type=int, default=32, help="conv: images in the global batch")
+    args = ap.parse_args()
+    if args.workload in ("stack", "conv") and args.steps == 2000:
+        args.steps = 10          # a step of these workloads is milliseconds, not microseconds
+    return args
 
 
 # ---------------------------------------------------------------- distributed plumbing
@@ -403,12 +412,345 @@ def e2e_measure(args, model, dev, world, work):
             "d2h_bytes_per_step": d2h, "api": "torch.compile(backend='xdna', fallback='eager')"}
 
 
+# ---------------------------------------------------------------- the Qwen3 stack
+V_HEAD = 151936
+
+
+def stack_flops(B, L, layers, vocab):
+    """Algorithmic FLOPs of one step: the projections and head per token, causal attention (QK^T and PV over
+    the keys each query sees)."""
+    per_token = 2 * (layers * (D * 4096 + 2048 * D + D * 6144 + INTER * D) + D * vocab)
+    attn = layers * B * 2 * 2 * 16 * 128 * (L * (L + 1) // 2)
+    return B * L * per_token + attn
+
+
+def run_stack(args, rank, world):
+    """One step = embed the token ids of this rank's sequences and run xdna_qwen3_stack (28 layers, final
+    norm, head over 151936) under a causal mask. Sequences are data-parallel over ranks (no collective:
+    sequences are independent); the global batch is fixed (strong scaling)."""
+    import torch_xdna
+    from torch_xdna import kernels
+
+    if not torch_xdna.gpu_available():
+        raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B_all, L, NL = args.seqs, args.seq_len, args.layers
+    assert B_all % world == 0, "sequences must divide over the ranks"
+    B = B_all // world
+    g = torch.Generator(device=dev).manual_seed(1234)
+
+    def w(*shape):
+        return (torch.randn(*shape, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+
+    table = (kernels.Qwen3Layer * NL)()
+    keep = []
+    for i in range(NL):
+        qkv, o, gu, down = w(4096, D), w(D, 2048), w(2 * INTER, D), w(D, INTER)
+        norms = [torch.ones(D, device=dev), torch.ones(D, device=dev), torch.ones(128, device=dev),
+                 torch.ones(128, device=dev)]
+        keep += [qkv, o, gu, down] + norms
+        table[i] = kernels.Qwen3Layer(qkv.data_ptr(), o.data_ptr(), gu.data_ptr(), down.data_ptr(),
+                                      *[t.data_ptr() for t in norms])
+    final = torch.ones(D, device=dev)
+    head, embed = w(V_HEAD, D), w(V_HEAD, D)
+    inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device=dev) / 128))
+    f = torch.arange(L, dtype=torch.float32, device=dev)[:, None] * inv[None, :]
+    cos, sin = f.cos().contiguous(), f.sin().contiguous()
+    ids = torch.randint(0, V_HEAD, (B * L,), device=dev, generator=g)
+    x = torch.empty(B * L, D, device=dev)
+    out = torch.empty(B * L, V_HEAD, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(kernels.qwen3_stack_workspace(B, L), dtype=torch.uint8, device=dev)
+    launches_per_step = 1 + 7 * NL + 2
+
+    def step(ids_dev):
+        kernels.embed(ids_dev, embed, x)
+        kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
+                            out, ws)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(max(args.warmup, 3)):
+        step(ids)
+    barrier(world)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clocks:
+        barrier(world)
+        for i in range(args.steps):          # weights (1.2 GB) and activations far exceed L2
+            starts[i].record(stream)
+            step(ids)
+            ends[i].record(stream)
+        barrier(world)
+    total_s = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3, world)
+    tokens = B_all * L * args.steps
+    value = tokens / total_s
+    flops = stack_flops(B, L, NL, V_HEAD)
+
+    # roofline: the head GEMM (the largest single launch), timed alone per launch
+    hn = torch.randn(B * L, D, device=dev).to(torch.bfloat16)
+    for _ in range(2):
+        kernels.gemm_bf16(hn, head, kernels.GEMM_F32ACC, out=out)
+    ms = []
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        kernels.gemm_bf16(hn, head, kernels.GEMM_F32ACC, out=out)
+        e.record(stream)
+        e.synchronize()
+        ms.append(s.elapsed_time(e))
+    head_ms = statistics.median(ms)
+    head_flops = 2 * B * L * V_HEAD * D
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    roof = {"bound": "tensor", "kernel": "umma_gemm_kernel bf16 (the head GEMM, EPI_F32ACC)",
+            "achieved": round(head_flops / head_ms / 1e9, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(head_flops / head_ms / 1e9 / peak, 4),
+            "peak_source": "measured dense bf16 cuBLAS burst (MEASURED_PEAKS.json)" if peaks else "fallback",
+            "traffic": None, "per_launch_ms": round(head_ms, 4),
+            "step_tflops": round(flops * args.steps * world / total_s / 1e12, 1)}
+
+    # e2e: token ids from pinned host memory in, every logit back to pinned host memory
+    h_ids = ids.cpu().pin_memory()
+    h_out = torch.empty(B * L, V_HEAD, dtype=torch.bfloat16, pin_memory=True)
+    d_ids = torch.empty_like(ids)
+    e_steps = max(2, min(5, args.steps))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    s.record(stream)
+    for _ in range(e_steps):
+        d_ids.copy_(h_ids, non_blocking=True)
+        step(d_ids)
+        h_out.copy_(out, non_blocking=True)
+    e.record(stream)
+    barrier(world)
+    e2e_s = max_over_ranks(s.elapsed_time(e) / 1e3, world)
+    e2e = {"value": round(B_all * L * e_steps / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h_ids.numel() * 8,
+           "d2h_bytes_per_step": h_out.numel() * 2, "api": "xdna_qwen3_stack C ABI (torch_xdna.kernels)"}
+    cb = cpu_stack_baseline(NL, 1, 128) if (rank == 0 and world == 1) else None
+    if kernels.take_device_error() != (0, 0):
+        raise SystemExit("a kernel recorded a device-side timeout")
+    if rank == 0:
+        line = {"metric": "Qwen3-0.6B stack tokens/s (BASELINE config 5)", "value": round(value, 1),
+                "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+                "ms_per_step": round(total_s * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (uniform token ids, N(0,0.02) weights, unit norms)",
+                "config": {"workload": f"cfg5 Qwen3-0.6B stack: {NL} layers, {B_all} sequences x {L} tokens, causal "
+                                       f"mask, head {V_HEAD}, bf16 with f32 accumulation", "global_batch": B_all,
+                           "seq_len": L, "parallelism": f"dp{world} (sequences)", "l2": "inputs exceed L2"},
+                "gpu_launches": launches_per_step * args.steps, "roofline": roof, "e2e": e2e,
+                "clocks": clocks.summary()}
+        if cb is not None:
+            line["cpu_baseline"] = cb
+        print(json.dumps(line), flush=True)
+
+
+def cpu_stack_baseline(layers, seqs, seq_len):
+    """The reference's parity route for the stack (the fp32 eager model) restated in torch CPU ops
+    (oracle/reference_cpu.py) on a bounded sample, all host threads."""
+    from oracle import reference_cpu as rc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(5)
+
+    def w(*s):
+        return torch.randn(*s, generator=g) * 0.02
+
+    ls = [dict(q=w(2048, D), k=w(1024, D), v=w(1024, D), o=w(D, 2048), gate=w(INTER, D), up=w(INTER, D),
+               down=w(D, INTER), input_norm=torch.ones(D), post_norm=torch.ones(D), q_norm=torch.ones(128),
+               k_norm=torch.ones(128)) for _ in range(layers)]
+    head = w(V_HEAD, D)
+    x = torch.randn(seqs, seq_len, D, generator=g)
+    mask = torch.ones(seq_len, seq_len, dtype=torch.bool).tril()[None, None].expand(seqs, 1, seq_len, seq_len)
+    with torch.no_grad():
+        rc.qwen3_stack(ls, torch.ones(D), head, None, x, mask)
+        t0 = time.perf_counter()
+        rc.qwen3_stack(ls, torch.ones(D), head, None, x, mask)
+        dt = time.perf_counter() - t0
+    return {"value": round(seqs * seq_len / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{seqs} sequence x {seq_len} tokens through {layers} layers + head {V_HEAD}, fp32 eager "
+                      f"torch CPU (the reference's parity model)"}
+
+
+# ---------------------------------------------------------------- BASELINE config 4: VGG16 int8 convs
+VGG16 = [64, 64, "M", 128, 128, "M", 256, 256, 256, "M", 512, 512, 512, "M", 512, 512, 512]
+
+
+def vgg_layers(dev, seed=7):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    layers, ci = [], 3
+    for v in VGG16:
+        if v == "M":
+            layers.append("M")
+            continue
+        w = torch.randn(v, ci, 3, 3, device=dev, generator=g) * (2.0 / (ci * 9)) ** 0.5   # Kaiming normal (ReLU)
+        b = torch.randn(v, device=dev, generator=g) * 0.01
+        layers.append((w, b))
+        ci = v
+    return layers
+
+
+def vgg_macs(batch, hw=224):
+    macs, ci, h = 0, 3, hw
+    for v in VGG16:
+        if v == "M":
+            h //= 2
+            continue
+        macs += batch * h * h * ci * v * 9
+        ci = v
+    return macs
+
+
+def run_conv(args, rank, world):
+    """One step = the 13 int8 conv3x3 layers of VGG16 (bias + ReLU, 2x2 max-pool between blocks) on this
+    rank's share of a batch of 32 images 3x224x224 (batch sharded over ranks, strong scaling). Each conv is
+    xdna::conv3x3_fused: per-image quantise into the bordered NHWC layout, then the implicit-GEMM conv with
+    the dequantise and bias in its epilogue; the ReLU and pool are torch ops. The requantise shift of every
+    layer comes from global image 0 (rank 0), broadcast to the other ranks."""
+    import torch_xdna
+    from torch_xdna import kernels, parallel
+
+    if not torch_xdna.gpu_available():
+        raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if world > 1:
+        parallel.enable_data_parallel()
+    N_all = args.images
+    assert N_all % world == 0
+    N = N_all // world
+    layers = vgg_layers(dev)
+    params = [("M" if l == "M" else (torch.nn.Parameter(l[0]), l[1])) for l in layers]
+    cid = torch_xdna.ops.config_id(torch_xdna.Config(verify="first"))
+    g = torch.Generator(device=dev).manual_seed(99)
+    x_all = torch.randn(N_all, 3, 224, 224, device=dev, generator=g)
+    x = x_all[rank * N:(rank + 1) * N].contiguous()
+    del x_all
+
+    def step(inp):
+        h = inp
+        for p in params:
+            if p == "M":
+                h = torch.nn.functional.max_pool2d(h, 2)
+            else:
+                h = torch.relu(torch.ops.xdna.conv3x3_fused(h, p[0], p[1], False, cid))
+        return h
+
+    stream = torch.cuda.current_stream()
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            step(x)
+        barrier(world)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        torch_xdna.stats.reset()
+        with ClockSampler(dev.index) as clocks:
+            barrier(world)
+            for i in range(args.steps):      # 32 x 64 x 224 x 224 activations (400 MB) exceed L2
+                starts[i].record(stream)
+                y = step(x)
+                ends[i].record(stream)
+            barrier(world)
+        launches = torch_xdna.stats.launches
+    total_s = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3, world)
+    value = 2 * vgg_macs(N_all) * args.steps / total_s / 1e12
+    # roofline: the conv kernel of the largest-work layer (conv 64->64 at 224x224), timed alone
+    from torch_xdna import conv as xconv
+
+    lay = xconv._layer(params[1][0], 224, 224, False)
+    xp = torch.zeros(N, 226, 226, lay.cp, dtype=torch.int8, device=dev)
+    sx = torch.rand(N, device=dev)
+    yo = torch.empty(N, 64, 224, 224, device=dev)
+    ms = []
+    for i in range(6):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, kernels.CONV_DEQUANT, shift=lay.shift, scale=lay.scale,
+                        sx=sx, bias=params[1][1], out=yo)
+        e.record(stream)
+        e.synchronize()
+        if i:
+            ms.append(s.elapsed_time(e))
+    conv_ops = 2 * N * 224 * 224 * 64 * 64 * 9
+    peak, src = int8_peak()
+    achieved = conv_ops / statistics.median(ms) / 1e9
+    roof = {"bound": "tensor", "kernel": "umma_gemm_kernel LOAD_CONV (conv 64->64 224x224, dequantise epilogue)",
+            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS", "frac": round(achieved / peak, 4),
+            "peak_source": src, "traffic": None, "per_launch_ms": round(statistics.median(ms), 4)}
+    cb = cpu_conv_baseline() if (rank == 0 and world == 1) else None
+    if kernels.take_device_error() != (0, 0):
+        raise SystemExit("a kernel recorded a device-side timeout")
+    if rank == 0:
+        line = {"metric": "int8 TOPS/GPU, conv3x3 (BASELINE config 4: VGG16 int8, batch 32)", "value": round(value, 2),
+                "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+                "ms_per_step": round(total_s * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int8", "data": "synthetic (N(0,1) images, Kaiming weights, N(0,0.01) bias)",
+                "config": {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224, bias + ReLU, 2x2 max-pool",
+                           "global_batch": N_all, "parallelism": f"dp{world} (images)", "l2": "activations exceed L2"},
+                "gpu_launches": launches, "roofline": roof, "clocks": clocks.summary()}
+        if cb is not None:
+            line["cpu_baseline"] = cb
+        print(json.dumps(line), flush=True)
+
+
+def cpu_conv_baseline(images=1):
+    """The reference's CPU-integer conv route (oracle/reference_cpu.py: exact fp conv of the integers) through
+    the VGG16 conv stack on a bounded sample, all host threads."""
+    from oracle import reference_cpu as rc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    layers = [("M" if l == "M" else (rc.conv_layer(l[0].cpu(), False), l[1].cpu())) for l in vgg_layers("cpu")]
+    x = torch.randn(images, 3, 224, 224, generator=torch.Generator().manual_seed(3))
+
+    def run():
+        h = x
+        for l in layers:
+            h = torch.nn.functional.max_pool2d(h, 2) if l == "M" else torch.relu(rc.conv3x3_int8(h, l[0], l[1]))
+        return h
+
+    with torch.no_grad():
+        run()
+        t0 = time.perf_counter()
+        run()
+        dt = time.perf_counter() - t0
+    return {"value": round(2 * vgg_macs(images) / dt / 1e12, 4), "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{images} image 3x224x224 through the 13 VGG16 convs (CPU integers: quantise, fp conv of "
+                      f"the integers, requantise, dequantise)"}
+
+
+def run_reference_workload(args, rank, world):
+    """--impl reference for the stack and conv workloads: rank 0 times the CPU route on a bounded sample."""
+    if rank != 0:
+        return
+    if args.workload == "stack":
+        cb = cpu_stack_baseline(args.layers, 1, 128)
+        metric, unit, dtype = "Qwen3-0.6B stack tokens/s (BASELINE config 5)", "tokens/s", "fp32"
+        config = {"workload": f"cfg5 Qwen3-0.6B stack: {args.layers} layers, {args.seqs} sequences x {args.seq_len} "
+                              f"tokens, causal, head {V_HEAD}", "global_batch": args.seqs, "seq_len": args.seq_len}
+    else:
+        cb = cpu_conv_baseline()
+        metric, unit, dtype = "int8 TOPS/GPU, conv3x3 (BASELINE config 4: VGG16 int8, batch 32)", "TOPS", "int8"
+        config = {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224", "global_batch": args.images}
+    line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config, "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank, world = dist_init(args.gpus)
     try:
         if args.impl == "reference":
-            run_reference(args, rank, world)
+            if args.workload in ("stack", "conv"):
+                run_reference_workload(args, rank, world)
+            else:
+                run_reference(args, rank, world)
+        elif args.workload == "stack":
+            run_stack(args, rank, world)
+        elif args.workload == "conv":
+            run_conv(args, rank, world)
         else:
             run_xdna(args, rank, world)
     finally:

@@ -38,6 +38,38 @@ def linear_int8(x, w_kn, sw, bias=None):
     return y.to(x.dtype).reshape(*x.shape[:-1], y.shape[-1])
 
 
+def qwen3_stack(layers, final_norm, head, head_bias, x, allowed, theta=1e6, eps=1e-6):
+    """The fp32 eager model the reference checks its fused stack against (R:torch_xdna/stack.py:444-460),
+    restated with torch CPU ops: transformers' Qwen3 decoder layers on x [B, L, 1024] under a bool mask
+    [B, 1, L, L], the final norm and the head. layers: list of dicts of float32 tensors (LAYER_KEYS)."""
+    B, L, D = x.shape
+    NH, NKV, DH = 16, 8, 128
+    inv_freq = 1.0 / (theta ** (torch.arange(0, DH, 2, dtype=torch.float32) / DH))
+    freqs = torch.arange(L, dtype=torch.float32)[:, None] * inv_freq[None, :]
+    cos, sin = torch.cat([freqs, freqs], -1).cos(), torch.cat([freqs, freqs], -1).sin()
+
+    def rms(t, w):
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps) * w
+
+    def rope(t):
+        return t * cos + torch.cat([-t[..., DH // 2:], t[..., :DH // 2]], -1) * sin
+
+    h = x.float()
+    for w in layers:
+        a = rms(h, w["input_norm"])
+        q = rms((a @ w["q"].t()).view(B, L, NH, DH), w["q_norm"]).transpose(1, 2)
+        k = rms((a @ w["k"].t()).view(B, L, NKV, DH), w["k_norm"]).transpose(1, 2)
+        v = (a @ w["v"].t()).view(B, L, NKV, DH).transpose(1, 2)
+        q, k = rope(q), rope(k)
+        o = torch.nn.functional.scaled_dot_product_attention(q, k.repeat_interleave(NH // NKV, 1),
+                                                             v.repeat_interleave(NH // NKV, 1), attn_mask=allowed)
+        h = h + o.transpose(1, 2).reshape(B, L, NH * DH) @ w["o"].t()
+        a = rms(h, w["post_norm"])
+        h = h + (torch.nn.functional.silu(a @ w["gate"].t()) * (a @ w["up"].t())) @ w["down"].t()
+    out = rms(h, final_norm) @ head.t()
+    return out + head_bias if head_bias is not None else out
+
+
 def conv_layer(weight, relu):
     """ConvLayer weights, R:torch_xdna/conv.py:314-319."""
     wf = weight.detach().float()

@@ -129,6 +129,24 @@ def test_reference_cpu_port_linear(golden, name):
     assert mg.sha(y.float().numpy()) == ent["y_sha"]
 
 
+@pytest.mark.parametrize("name", [c[0] for c in mg.STACK_CASES])
+def test_reference_cpu_port_stack(golden, name):
+    import torch
+
+    from oracle import reference_cpu as rc
+
+    manifest, arrays = golden
+    ent = manifest["stack"][name]
+    ls, final, head, head_b, x = mg.stack_inputs(ent["seed"], ent["layers"], ent["head_n"], ent["batch"], ent["seq"])
+    mask = mg.causal_mask(ent["batch"], ent["seq"]) if ent["mask"] == "causal" else mg.prefix_mask(ent["lens"], ent["seq"])
+    layers = [{k: torch.from_numpy(v) for k, v in L.items()} for L in ls]
+    with torch.no_grad():
+        got = rc.qwen3_stack(layers, torch.from_numpy(final), torch.from_numpy(head), torch.from_numpy(head_b),
+                             torch.from_numpy(x), torch.from_numpy(mask))
+    want = torch.from_numpy(arrays[f"stack/{name}/logits"])
+    assert float((got - want).abs().max() / want.abs().max()) < 1e-4
+
+
 @pytest.mark.parametrize("name", ["odd_3_64_13x37", "odd_64_48_relu"])
 def test_reference_cpu_port_conv(golden, name):
     import torch

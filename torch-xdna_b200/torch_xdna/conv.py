@@ -25,7 +25,7 @@ import weakref
 
 import torch
 
-from . import kernels
+from . import kernels, parallel
 from .runtime import DEVICE, XdnaResultMismatch, stats
 
 log = logging.getLogger("torch_xdna")
@@ -79,7 +79,9 @@ class ConvLayer:
                         acc_max=acc_max)
         stats.launches += 1
         top = float(int(acc_max.item()))
-        self.shift = min(31, max(1, math.ceil(math.log2(max(top * 1.25, 1.0) / (255 if self.relu else 127)))))
+        shift = min(31, max(1, math.ceil(math.log2(max(top * 1.25, 1.0) / (255 if self.relu else 127)))))
+        # data parallel: every rank adopts the shift of rank 0, which holds global image 0
+        self.shift = parallel.broadcast_shift(shift, xp.device)
         self.scale = self.sw * 2.0 ** self.shift
 
     def q(self, xp, n):
