@@ -3,17 +3,19 @@
 //
 // One CTA = 128 queries of one query head of one sequence; 192 threads:
 //   warp 0      TMA: the Q tile once, then K and V^T blocks of 128 keys into a 2-stage ring
-//               (Q and K read from the q/k projection output [T, 3072] bf16, V^T from [1024, T] bf16,
+//               (Q and K read from the q/k projection output [T, 3072] bf16, V^T from [1024, T'] bf16,
 //               which the projection epilogue wrote transposed so that P.V has a K-major B operand);
-//   warp 1      TMEM (512 columns: two S buffers, two O buffers) and the MMAs:
-//               S_j = Q K_j^T (8 x tcgen05.mma 128x128x16), O_j = P_j V_j (8 more), issued as
+//   warp 1      TMEM (two S buffers of 128 columns, one O accumulator of 128) and the MMAs:
+//               S_j = Q K_j^T (8 x tcgen05.mma 128x128x16) and O += P_j V_j (8 more), issued as
 //               S_0, S_1, O_0, S_2, O_1, ... so each S overlaps the previous block's softmax;
-//   warps 2..5  softmax: thread i owns query row i. Two passes over S_j in TMEM (row max, then
-//               exp2 and the row sum), P_j written as bf16 into a 128-byte-swizzled K-major tile,
-//               and O accumulated in registers: O = O * exp2(m_old - m_new) + O_j, l likewise.
-//               The output row is O / l in bf16, written to [T, 2048].
-// Masks: causal, per-sequence prefix blocks (the reference's OmniVoice layout: the first n
-// positions see each other, later ones only themselves), a general bool mask [B, 1|H, L, L], or none.
+//   warps 2..5  softmax: thread i owns query row i. Pass 1 over S_j in TMEM finds the row max; pass 2
+//               writes p = 2^(s * scale * log2 e - m) as bf16 into a 128-byte-swizzled K-major P tile
+//               and sums it. O stays in TMEM and the MMA accumulates into it; the running max m is only
+//               raised (and O, l rescaled in place) when a block's max exceeds it by more than 2^8, so
+//               p <= 256 and most blocks touch O not at all. The output row is O / l in bf16 [T, 2048].
+// Masks: causal, per-sequence prefix blocks (the reference's OmniVoice layout: the first n positions
+// see each other, later ones only themselves), a general bool mask [B, 1|H, L, L], or none; blocks that
+// no mask entry can touch (for causal: every block left of the diagonal) skip the masking entirely.
 // Keys past the sequence end are always masked. Every mbarrier wait is bounded (sm100.cuh).
 #include <algorithm>
 
@@ -40,7 +42,8 @@ struct AttnArgs {
 constexpr int kAttnThreads = 192;
 constexpr int kTileBytes = 128 * 128;  // one 128-row x 128-byte operand k-block
 constexpr int kKvStages = 2;
-constexpr int kAttnSmem = (2 /*Q*/ + 2 * kKvStages /*K*/ + 2 * kKvStages /*V*/ + 2 /*P*/) * kTileBytes + 1024 + 256;
+constexpr int kAttnSmem = (2 /*Q*/ + 2 * kKvStages /*K*/ + 2 * kKvStages /*V*/ + 4 /*P x 2*/) * kTileBytes + 1024 + 256;
+constexpr float kRescaleLog2 = 8.0f;   // lazy rescale threshold: p stays <= 2^8
 
 __device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -75,17 +78,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smK = smQ + 2 * kTileBytes;
   uint8_t* smV = smK + 2 * kKvStages * kTileBytes;
   uint8_t* smP = smV + 2 * kKvStages * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smP + 2 * kTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smP + 4 * kTileBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                 // [kKvStages]
   uint64_t* kv_empty = kv_full + kKvStages;     // [kKvStages]
   uint64_t* s_full = kv_empty + kKvStages;      // [2]
   uint64_t* s_empty = s_full + 2;               // [2]
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* p_empty = p_full + 1;
-  uint64_t* o_full = p_empty + 1;               // [2]
-  uint64_t* o_empty = o_full + 2;               // [2]
-  uint64_t* drain = o_empty + 2;
+  uint64_t* p_full = s_empty + 2;               // [2] P_j written (buffer j & 1) and O rescaled: O += P_j V_j may run
+  uint64_t* p_empty = p_full + 2;               // [2] O += P_j V_j done: buffer j & 1 may be rewritten, O read
+  uint64_t* drain = p_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -108,11 +109,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(s_full + b, 1);
       mbar_init(s_empty + b, 4);
-      mbar_init(o_full + b, 1);
-      mbar_init(o_empty + b, 4);
+      mbar_init(p_full + b, 4);
+      mbar_init(p_empty + b, 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(p_empty, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -130,7 +129,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO[2] = {tmem + 256, tmem + 384};
+  const uint32_t tO = tmem + 256;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -164,19 +163,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = mbar_wait(q_full, 0, abort_flag, args.err, 23);
       bool issued = false;
       const uint64_t dQ[2] = {smem_desc_k_sw128(smem_u32(smQ)), smem_desc_k_sw128(smem_u32(smQ + kTileBytes))};
-      const uint64_t dP[2] = {smem_desc_k_sw128(smem_u32(smP)), smem_desc_k_sw128(smem_u32(smP + kTileBytes))};
       auto issue_pv = [&](int i) -> bool {
         const int st = i % kKvStages;
-        if (!mbar_wait(p_full, i & 1, abort_flag, args.err, 24)) return false;
-        if (!mbar_wait(o_empty + (i & 1), ((i >> 1) & 1) ^ 1, abort_flag, args.err, 25)) return false;
+        const int pb = i & 1;
+        if (!mbar_wait(p_full + pb, (i >> 1) & 1, abort_flag, args.err, 24)) return false;
         tc_fence_after();
         for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t dP = smem_desc_k_sw128(smem_u32(smP + (pb * 2 + kk) * kTileBytes));
           const uint64_t dV = smem_desc_k_sw128(smem_u32(smV + (st * 2 + kk) * kTileBytes));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) umma_f16(tO[i & 1], dP[kk] + 2 * k, dV + 2 * k, IDESC, (kk | k) != 0);
+          for (int k = 0; k < 4; ++k) umma_f16(tO, dP + 2 * k, dV + 2 * k, IDESC, (i | kk | k) != 0);
         }
-        umma_commit(o_full + (i & 1));
-        umma_commit(p_empty);
+        umma_commit(p_empty + pb);
         umma_commit(kv_empty + st);
         issued = true;
         return true;
@@ -211,67 +209,90 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = qd * 32 + lane;            // query row within the tile
     const int qpos = q0 + r;                 // query position in the sequence
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    float o[128];
-#pragma unroll
-    for (int d = 0; d < 128; ++d) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    const float sc = args.scale_log2;
+    float m_use = -INFINITY;                 // the max the probabilities and O are relative to (log2 units)
+    float l = 0.f;
     bool ok = true;
-    uint32_t v[32];
+    uint32_t v[128];                         // this row of S_j, loaded from TMEM once
     for (int j = 0; j < kv_blocks && ok; ++j) {
       const int b = j & 1;
+      const int k0 = j * 128;
+      // warp-uniform: does any entry of this block need the mask?
+      const bool masked = KIND == MASK_PREFIX || KIND == MASK_BOOL || k0 + 128 > args.L ||
+                          (KIND == MASK_CAUSAL && k0 + 127 > q0);
       if (!mbar_wait(s_full + b, (j >> 1) & 1, abort_flag, args.err, 31)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int k0 = j * 128;
-      // pass 1: the row max of the scaled, masked scores
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        __syncwarp();
-        tmem_ld_32x32b_x32(tS[b] + lane_off + c * 32, v);
-        tmem_ld_wait();
+      __syncwarp();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kpos = k0 + c * 32 + e;
-          const float s = key_allowed(KIND, args, seq, head, qpos, kpos) ? __uint_as_float(v[e]) * args.scale_log2
-                                                                          : -INFINITY;
-          mx = fmaxf(mx, s);
-        }
+      for (int c = 0; c < 4; ++c)
+        tmem_ld_32x32b_x32(tS[b] + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
+      tmem_ld_wait();
+      // S_j is in registers: the MMA may compute S_{j+2} into this buffer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_empty + b);
+      if (masked) {
+#pragma unroll
+        for (int e = 0; e < 128; ++e)
+          if (!key_allowed(KIND, args, seq, head, qpos, k0 + e)) v[e] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = m_new == -INFINITY ? 1.f : exp2f(m - m_new);
-      // P_j may be written once P_{j-1} has been consumed by its MMA
-      if (j >= 1 && !mbar_wait(p_empty, (j - 1) & 1, abort_flag, args.err, 32)) {
+      // the row max of the raw scores (scale > 0 commutes with max)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 128; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+      const float m_blk = mx * sc;
+      // raise the running max only when this block would push p above 2^8
+      float alpha = 1.f;
+      const bool raise = m_blk > m_use + kRescaleLog2;
+      if (raise) {
+        alpha = fast_exp2(m_use - m_blk);    // 0 while m_use is -inf
+        m_use = m_blk;
+      }
+      if (j >= 1 && __any_sync(0xffffffffu, raise && l > 0.f)) {
+        // O must hold O_{j-1} before it is rescaled in place (rows that did not raise multiply by 1)
+        if (!mbar_wait(p_empty + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, args.err, 32)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t o[32];
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          __syncwarp();
+          tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + lane_off + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      l *= alpha;
+      // P buffer j & 1 was last read by O += P_{j-2} V_{j-2}
+      if (j >= 2 && !mbar_wait(p_empty + b, ((j - 2) >> 1) & 1, abort_flag, args.err, 33)) {
         ok = false;
         break;
       }
-      // pass 2: p = exp2(s - m_new) as bf16 into the swizzled K-major P tile, and the row sum
+      // p = 2^(s * scale - m) as bf16 into the swizzled K-major P tile, and the row sum
+      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+      const bool none = m_use == -INFINITY;  // every key so far masked
       float rs = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        __syncwarp();
-        tmem_ld_32x32b_x32(tS[b] + lane_off + c * 32, v);
-        tmem_ld_wait();
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p2[2];
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int kpos = k0 + c * 32 + e + t;
-            const bool okk = key_allowed(KIND, args, seq, head, qpos, kpos) && m_new != -INFINITY;
-            p2[t] = okk ? exp2f(__uint_as_float(v[e + t]) * args.scale_log2 - m_new) : 0.f;
-          }
-          const __nv_bfloat162 h = __floats2bfloat162_rn(p2[0], p2[1]);
-          // the row sum takes the bf16-rounded probabilities the MMA will use
-          const float2 hf = __bfloat1622float2(h);
-          rs += hf.x + hf.y;
-          w[e / 2] = *reinterpret_cast<const uint32_t*>(&h);
+          float p0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), sc, neg_m));
+          float p1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), sc, neg_m));
+          if (none) p0 = p1 = 0.f;
+          rs += p0 + p1;
+          w[e / 2] = pack2_bf16(p0, p1);
         }
         // 32 keys = 64 bytes = 4 chunks of 16 bytes in k-block c / 2, chunk offset (c % 2) * 4
-        uint8_t* rowp = smP + (c >> 1) * kTileBytes + r * 128;
+        uint8_t* rowp = smP + (b * 2 + (c >> 1)) * kTileBytes + r * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int chunk = (c & 1) * 4 + q;
@@ -279,66 +300,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
       }
-      // S_j is no longer needed in TMEM; P_j is ready for the MMA
+      l += rs;
+      // P_j (and the rescaled O) are ready for the MMA
       tc_fence_before();
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_empty + b);
-        mbar_arrive(p_full);
-      }
-      l = l * alpha + rs;
-      m = m_new;
-      // fold in O_{j-1} (scaled by its own alpha) while the MMA computes O_j
-      if (j >= 1) {
-        const int ob = (j - 1) & 1;
-        if (!mbar_wait(o_full + ob, ((j - 1) >> 1) & 1, abort_flag, args.err, 33)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          __syncwarp();
-          tmem_ld_32x32b_x32(tO[ob] + lane_off + c * 32, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(o_empty + ob);
-      }
-      alpha_prev = alpha;
+      if (lane == 0) mbar_arrive(p_full + b);
     }
     if (ok && kv_blocks > 0) {
+      // the last O += P V, then O / l
       const int last = kv_blocks - 1;
-      const int ob = last & 1;
-      if (mbar_wait(o_full + ob, (last >> 1) & 1, abort_flag, args.err, 34)) {
+      if (mbar_wait(p_empty + (last & 1), (last >> 1) & 1, abort_flag, args.err, 34)) {
         tc_fence_after();
-#pragma unroll
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<int64_t>(tok0 + qpos) * (16 * 128) + head * 128);
+        uint32_t o[32];
+#pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           __syncwarp();
-          tmem_ld_32x32b_x32(tO[ob] + lane_off + c * 32, v);
+          tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
           tmem_ld_wait();
+          if (qpos < args.L) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
-        }
-        tc_fence_before();
-        // the output row: O / l in bf16, 256 contiguous bytes
-        if (qpos < args.L) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<int64_t>(tok0 + qpos) * (16 * 128) + head * 128);
-#pragma unroll
-          for (int d = 0; d < 128; d += 8) {
-            uint4 u;
-            u.x = pack2_bf16(o[d] * inv, o[d + 1] * inv);
-            u.y = pack2_bf16(o[d + 2] * inv, o[d + 3] * inv);
-            u.z = pack2_bf16(o[d + 4] * inv, o[d + 5] * inv);
-            u.w = pack2_bf16(o[d + 6] * inv, o[d + 7] * inv);
-            dst[d / 8] = u;
+            for (int e = 0; e < 32; e += 8) {
+              uint4 u;
+              u.x = pack2_bf16(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+              u.y = pack2_bf16(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+              u.z = pack2_bf16(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+              u.w = pack2_bf16(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+              dst[(c * 32 + e) / 8] = u;
+            }
           }
         }
+        tc_fence_before();
       }
     }
   }
@@ -349,10 +343,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_dealloc(tmem, 512);
   }
 }
-
-}  // namespace xdna
-
-namespace xdna {
 
 int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt, __nv_bfloat16* out, int64_t B,
                   int64_t L, int mask_kind, const int32_t* lens, const uint8_t* mask, int mask_heads,

@@ -20,7 +20,7 @@ static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   }
   const int tiles = args.m_tiles * args.n_tiles;
   const int grid = std::max(1, std::min(tiles, sms));
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, args);
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, ta, args);
   return check_launch("umma_gemm_kernel");
 }
 

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(256) embed_kernel(const int64_t* __restrict__ 
 // ---------------------------------------------------------------------------- bf16 GEMM launch
 template <int BN, int EPI, int ODT>
 static int launch_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
-                       int sms, cudaStream_t stream) {
+                       int sms, cudaStream_t stream, const CUtensorMap* td = nullptr) {
   constexpr bool TSTORE = (EPI == EPI_F32ACC || EPI == EPI_QKV || EPI == EPI_SWIGLU);
   constexpr int smem = smem_bytes_for<BN>();
   auto kern = umma_gemm_kernel<BN, LOAD_GEMM, EPI, true, TSTORE, ODT>;
@@ -93,7 +93,7 @@ static int launch_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   const int tiles = a.m_tiles * a.n_tiles;
-  kern<<<std::max(1, std::min(tiles, sms)), kThreads, smem, stream>>>(ta, tb, tc, a);
+  kern<<<std::max(1, std::min(tiles, sms)), kThreads, smem, stream>>>(ta, tb, tc, td ? *td : ta, a);
   return check_launch("umma_gemm_kernel (bf16)");
 }
 
@@ -211,7 +211,20 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
                      "gemm_bf16: qkv needs N = 4096, q/k output, V^T (pitch >= sequences x round_up(L, 8)), "
                      "rope tables and norms");
       if ((rc = out_map(&tc, g.out, g.M, kQCols + kKCols, g.ldo, XDNA_BF16, "gemm_bf16 qk out")) != XDNA_OK) return rc;
-      return launch_bf16<256, EPI_QKV, XDNA_BF16>(ta, tb, tc, a, sms, s);
+      {
+        // V^T written by TMA (32 tokens x 32 dims per store) when every 32-row block lies in one sequence
+        CUtensorMap td = ta;
+        a.vt_tma = g.seq_len % 32 == 0 && aligned16(g.vt);
+        if (a.vt_tma) {
+          const uint64_t dims[2] = {static_cast<uint64_t>(g.ldvt), 1024};
+          const uint64_t strides[1] = {static_cast<uint64_t>(g.ldvt * 2)};
+          const uint32_t box[2] = {32, 32};
+          if ((rc = encode_tma(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.vt, dims, strides, box, "gemm_bf16 v^T",
+                               CU_TENSOR_MAP_SWIZZLE_NONE)) != XDNA_OK)
+            return rc;
+        }
+        return launch_bf16<256, EPI_QKV, XDNA_BF16>(ta, tb, tc, a, sms, s, &td);
+      }
     default:
       return fail(XDNA_ERR_INVALID, "gemm_bf16: unknown mode %d", g.mode);
   }

@@ -78,6 +78,7 @@ struct GemmArgs {
   const float* k_norm;
   int seq_len;         // token m sits at position m % seq_len of its sequence
   float eps;
+  int vt_tma;          // EPI_QKV: V^T through TMA stores (seq_len % 32 == 0)
 };
 
 constexpr int kBM = 128;
@@ -255,21 +256,36 @@ __device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u);
 // (out[d] = x[d] cos - x[d+64] sin, out[d+64] = x[d+64] cos + x[d] sin), stored bf16 through TMA.
 // v heads are written transposed, V^T[head * 128 + d][token], the K-major operand of P.V.
 __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, uint8_t* obuf,
-                                         const CUtensorMap* tmC) {
+                                         const CUtensorMap* tmC, const CUtensorMap* tmD) {
   const int lane = lane_id();
   const int row = row0 + lane;
+  if (row0 >= a.M) return;  // warp-uniform: no rows of this warp exist
   uint32_t x1[32], x2[32];
   if (col0 >= kQCols + kKCols) {  // a v head (warp-uniform)
     const int vh = (col0 - kQCols - kKCols) / kHeadDim;
     // V^T columns: each sequence starts at a multiple of 8 tokens (TMA reads them as 16-byte aligned boxes)
     const int l8 = (a.seq_len + 7) / 8 * 8;
-    const int64_t vcol = static_cast<int64_t>(row / a.seq_len) * l8 + row % a.seq_len;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       __syncwarp();
       tmem_ld_32x32b_x32(taddr + c * 32, x1);
       tmem_ld_wait();
-      if (row < a.M) {
+      if (a.vt_tma) {
+        // 32 dims x 32 tokens, transposed through shared memory, one TMA store; the warp's 32 rows are
+        // consecutive positions of one sequence, so their V^T columns are row0 .. row0 + 31
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        __nv_bfloat16* t = reinterpret_cast<__nv_bfloat16*>(obuf);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j * 32 + lane] = __float2bfloat16_rn(f32_of(x1[j]));
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmD, obuf, row0, vh * kHeadDim + c * 32);
+          bulk_commit();
+        }
+      } else if (row < a.M) {
+        const int64_t vcol = static_cast<int64_t>(row / a.seq_len) * l8 + row % a.seq_len;
         __nv_bfloat16* dst = a.vt + static_cast<int64_t>(vh * kHeadDim + c * 32) * a.ldvt + vcol;
 #pragma unroll
         for (int j = 0; j < 32; ++j) dst[static_cast<int64_t>(j) * a.ldvt] = __float2bfloat16_rn(f32_of(x1[j]));
@@ -291,8 +307,9 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
   const float* nw = col0 < kQCols ? a.q_norm : a.k_norm;
   const float w_lane[4] = {nw[lane], nw[32 + lane], nw[64 + lane], nw[96 + lane]};
   const int pos = (row < a.M ? row : 0) % a.seq_len;
-  const float* cs = a.rope_cos + static_cast<int64_t>(pos) * (kHeadDim / 2);
-  const float* sn = a.rope_sin + static_cast<int64_t>(pos) * (kHeadDim / 2);
+  // this row's RoPE table entries, 16 bytes at a time (rows are 256-byte aligned)
+  const float4* cs4 = reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * (kHeadDim / 2));
+  const float4* sn4 = reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * (kHeadDim / 2));
   // pass 2: columns d and d + 64 together (the RoPE pairs), 32 at a time
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
@@ -302,18 +319,24 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
     tmem_ld_wait();
     uint32_t lo[16], hi[16];
 #pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-      float o[4];
+    for (int q = 0; q < 8; ++q) {
+      const float4 cv = __ldg(cs4 + c * 8 + q);
+      const float4 sv = __ldg(sn4 + c * 8 + q);
+      const float co[4] = {cv.x, cv.y, cv.z, cv.w};
+      const float si[4] = {sv.x, sv.y, sv.z, sv.w};
+      float o[4][2];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float u = f32_of(x1[j + e]) * rstd * __shfl_sync(kFull, w_lane[c], j + e);
-        const float v = f32_of(x2[j + e]) * rstd * __shfl_sync(kFull, w_lane[c + 2], j + e);
-        const float co = cs[c * 32 + j + e], si = sn[c * 32 + j + e];
-        o[e] = u * co - v * si;
-        o[2 + e] = v * co + u * si;
+      for (int e = 0; e < 4; ++e) {
+        const int j = q * 4 + e;
+        const float u = f32_of(x1[j]) * rstd * __shfl_sync(kFull, w_lane[c], j);
+        const float v = f32_of(x2[j]) * rstd * __shfl_sync(kFull, w_lane[c + 2], j);
+        o[e][0] = u * co[e] - v * si[e];
+        o[e][1] = v * co[e] + u * si[e];
       }
-      lo[j / 2] = pack2(o[0], o[1], XDNA_BF16);
-      hi[j / 2] = pack2(o[2], o[3], XDNA_BF16);
+      lo[q * 2] = pack2(o[0][0], o[1][0], XDNA_BF16);
+      lo[q * 2 + 1] = pack2(o[2][0], o[3][0], XDNA_BF16);
+      hi[q * 2] = pack2(o[0][1], o[1][1], XDNA_BF16);
+      hi[q * 2 + 1] = pack2(o[2][1], o[3][1], XDNA_BF16);
     }
     stage_and_store<16>(obuf, lo, tmC, col0 + c * 32, row0);
     stage_and_store<16>(obuf, hi, tmC, col0 + 64 + c * 32, row0);
@@ -350,7 +373,8 @@ __device__ __forceinline__ void swiglu_tile(const GemmArgs& a, uint32_t taddr, i
 template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                     const GemmArgs args) {
   constexpr int STAGES = stages_for<BN>();
   constexpr int A_BYTES = kBM * kBKBytes;
   constexpr int B_BYTES = BN * kBKBytes;
@@ -543,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
         if (col0 < args.N) {  // warp-uniform
           if constexpr (EPI == EPI_QKV)
-            qkv_tile(args, taddr, row0, col0, obuf, &tmC);
+            qkv_tile(args, taddr, row0, col0, obuf, &tmC, &tmD);
           else
             swiglu_tile<NCH>(args, taddr, row0, col0, obuf, &tmC);
         }
