@@ -217,7 +217,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     rows = args.cpu_rows if args.workload == "cfg2" else 4096
-    cb = cpu_baseline(args.workload, rows, budget_s=max(5.0, 0.5 * (args.steps + args.warmup)))
+    cb = cpu_baseline(args.workload, rows, budget_s=12.0)   # a bounded sample: ~12 s of CPU work
     line = {"impl": "reference", "metric": metric_name(args.workload), "value": cb["value"], "unit": "TOPS",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
