@@ -43,7 +43,8 @@ extern "C" {
 
 /* ------------------------------------------------------------------ conv3x3 modes */
 #define XDNA_CONV_Q 0         /* q = sat((acc + 2^(shift-1)) >> shift) as int8, or uint8 [0,255] with relu, NCHW */
-#define XDNA_CONV_DEQUANT 1   /* y = float(q) * (scale[co] * sx[n]) (+ bias[co]) in out_dtype, NCHW */
+#define XDNA_CONV_DEQUANT 1   /* y = float(q) * (scale[co] * sx[n]) (+ bias[co]) in out_dtype, channels-last
+                                 memory [N, H, W, Co] (torch's channels_last layout of an [N, Co, H, W] tensor) */
 #define XDNA_CONV_CALIBRATE 2 /* *acc_max = max over the sums of image 0 of (relu ? max(acc,0) : |acc|) */
 
 /* Last error of this thread, as text. */
@@ -95,6 +96,12 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
 int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,
                          int64_t Cp, float* sx, uint32_t* amax_scratch, void* stream);
 
+/* The same quantisation for x in channels-last memory ([N, H, W, C], torch's channels_last layout of
+ * an [N, C, H, W] tensor; 16-byte aligned): a streaming copy with no transpose. This is the layout the
+ * XDNA_CONV_DEQUANT epilogue writes, so one conv's output feeds the next conv's quantise directly. */
+int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,
+                                  int8_t* xp, int64_t Cp, float* sx, uint32_t* amax_scratch, void* stream);
+
 /* xdna_conv_quant_nhwc without caller-provided scratch: the same inputs, outputs and results, but the
  * per-image max lives in a 16 KB array inside the library, so the call allocates nothing and takes no
  * scratch pointer. It has no counterpart in the reference (whose quantise runs on the CPU).
@@ -121,8 +128,8 @@ int xdna_conv_pack_weight(const int8_t* wq, int64_t Co, int64_t Ci, int8_t* wp, 
 /* 3x3 / stride 1 / padding 1 conv of xp by wp on the int8 tensor cores, int32 sums, and one of the
  * epilogues XDNA_CONV_Q / XDNA_CONV_DEQUANT / XDNA_CONV_CALIBRATE (see above). Rounding of the
  * requantise is round half up via an arithmetic shift, then saturation: [-128,127] int8, or
- * [0,255] uint8 when relu != 0. Output `out` is NCHW [N, Co, H, W] in out_dtype (XDNA_I8 / XDNA_U8
- * for XDNA_CONV_Q; XDNA_F32 / XDNA_BF16 / XDNA_F16 for XDNA_CONV_DEQUANT). For XDNA_CONV_CALIBRATE
+ * [0,255] uint8 when relu != 0. Output `out`: NCHW [N, Co, H, W] XDNA_I8 / XDNA_U8 for XDNA_CONV_Q;
+ * channels-last [N, H, W, Co] XDNA_F32 / XDNA_BF16 / XDNA_F16 for XDNA_CONV_DEQUANT. For XDNA_CONV_CALIBRATE
  * only image 0 is computed and acc_max (one int32, cleared by this call) receives the maximum.
  * Replaces tl.extra.npu.conv3x3.Conv3x3(...)(xq) as used by ConvLayer.npu
  * R:torch_xdna/conv.py:334-340,350-359, the CPU integers ConvLayer.cpu R:torch_xdna/conv.py:345-348,

@@ -188,6 +188,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   a.W = static_cast<int>(W);
   a.out = out;
   a.out_dtype = out_dtype;
+  // XDNA_CONV_DEQUANT writes channels-last: 32 channels of a pixel as 16-byte vectors when aligned
+  a.vec_ok = mode == XDNA_CONV_DEQUANT && aligned16(out) && (Co * dtype_size(out_dtype)) % 16 == 0;
   a.sx = sx;
   a.sw = scale;
   a.bias = bias;

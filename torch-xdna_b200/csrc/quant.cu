@@ -320,6 +320,51 @@ __global__ void __launch_bounds__(256) to_bordered_nhwc_kernel(const T* __restri
   }
 }
 
+// ---------------------------------------------------------------------------- channels-last -> bordered NHWC
+// x is [N, H, W, C] in memory (torch's channels_last): no transpose, each bordered row is a stream of
+// 4-channel words. grid (H + 2, N); border rows, border pixels and channels >= C are zeros.
+template <typename T>
+__global__ void __launch_bounds__(256) cl_to_bordered_kernel(const T* __restrict__ x, int C, int H, int W, int Cp,
+                                                             const uint32_t* __restrict__ amax,
+                                                             int8_t* __restrict__ xp, float* __restrict__ sx) {
+  const int yb = blockIdx.x;
+  const int n = blockIdx.y;
+  const int Wp = W + 2;
+  const float s = scale_from_amax(__uint_as_float(amax[n]));
+  const float r = __frcp_rn(s);
+  if (yb == 0 && threadIdx.x == 0) sx[n] = s;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(xp + (static_cast<int64_t>(n) * (H + 2) + yb) * Wp * Cp);
+  const int words = Wp * Cp / 4;
+  const bool border_row = yb == 0 || yb == H + 1;
+  const int y = yb - 1;
+  for (int e = threadIdx.x; e < words; e += blockDim.x) {
+    const int xb = (e * 4) / Cp;
+    const int c = e * 4 - xb * Cp;
+    uint32_t word = 0;
+    if (!border_row && xb >= 1 && xb <= W && c < C) {
+      const T* src = x + ((static_cast<int64_t>(n) * H + y) * W + (xb - 1)) * C + c;
+      float f[4];
+      if (c + 4 <= C && (C & 3) == 0) {
+        if constexpr (sizeof(T) == 4) {
+          const float4 u = __ldg(reinterpret_cast<const float4*>(src));
+          f[0] = u.x, f[1] = u.y, f[2] = u.z, f[3] = u.w;
+        } else {
+          const uint2 u = __ldg(reinterpret_cast<const uint2*>(src));
+          const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) f[k] = to_f32(h[k]);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f[k] = c + k < C ? to_f32(src[k]) : 0.f;
+      }
+      word = quant4(f[0], f[1], f[2], f[3], s, r);
+      if (c + 4 > C) word &= 0xFFFFFFFFu >> (8 * (c + 4 - C));  // channels >= C stay zero
+    }
+    dst[e] = word;
+  }
+}
+
 // wq [Co, Ci, 3, 3] -> wp [Co, 9, Cp], pad channels zero.
 __global__ void pack_weight_kernel(const int8_t* __restrict__ wq, int64_t Co, int64_t Ci, int8_t* __restrict__ wp,
                                    int64_t Cp) {
@@ -398,6 +443,45 @@ int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64
       return fail(XDNA_ERR_INVALID, "conv_quant: x_dtype %d is not f32/bf16/f16", x_dtype);
   }
   return check_launch("conv quantise");
+}
+
+int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,
+                                  int8_t* xp, int64_t Cp, float* sx, uint32_t* amax_scratch, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && C >= 1 && H >= 1 && W >= 1, "conv_quant_cl: bad shape");
+  XDNA_CHECK_ARG(Cp >= C && Cp % 16 == 0, "conv_quant_cl: Cp must be >= C and a multiple of 16");
+  XDNA_CHECK_ARG(H + 2 <= 2147483647 && N <= 65535, "conv_quant_cl: too many images");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(x && xp && sx && amax_scratch, "conv_quant_cl: null pointer");
+  XDNA_CHECK_ARG(aligned16(x) && aligned16(xp), "conv_quant_cl: x and xp must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  XDNA_CUDA(cudaMemsetAsync(amax_scratch, 0, N * sizeof(uint32_t), s));
+  const int64_t per_image = C * H * W;
+  const int chunks = static_cast<int>(std::min<int64_t>((per_image + 256 * 16 - 1) / (256 * 16), 1024));
+  dim3 g_amax(chunks, static_cast<unsigned>(N));
+  dim3 g(static_cast<unsigned>(H + 2), static_cast<unsigned>(N));
+  switch (x_dtype) {
+    case XDNA_F32:
+      image_amax_kernel<float><<<g_amax, 256, 0, s>>>(static_cast<const float*>(x), per_image, amax_scratch);
+      cl_to_bordered_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), (int)C, (int)H, (int)W, (int)Cp,
+                                                     amax_scratch, xp, sx);
+      break;
+    case XDNA_BF16:
+      image_amax_kernel<__nv_bfloat16>
+          <<<g_amax, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), per_image, amax_scratch);
+      cl_to_bordered_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), (int)C, (int)H,
+                                                             (int)W, (int)Cp, amax_scratch, xp, sx);
+      break;
+    case XDNA_F16:
+      image_amax_kernel<__half><<<g_amax, 256, 0, s>>>(static_cast<const __half*>(x), per_image, amax_scratch);
+      cl_to_bordered_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(x), (int)C, (int)H, (int)W, (int)Cp,
+                                                      amax_scratch, xp, sx);
+      break;
+    default:
+      return fail(XDNA_ERR_INVALID, "conv_quant_cl: x_dtype %d is not f32/bf16/f16", x_dtype);
+  }
+  return check_launch("conv quantise (channels-last)");
 }
 
 int xdna_conv_pack_input(const int8_t* xq, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp, int64_t Cp,

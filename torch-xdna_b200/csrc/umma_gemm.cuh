@@ -190,16 +190,20 @@ __device__ __forceinline__ void store_direct(const GemmArgs& a, int row, int n0,
   const int64_t off = static_cast<int64_t>(row) * a.ldo + n0;
   if constexpr (EPI == EPI_I32) {
     int32_t* o = static_cast<int32_t*>(a.out) + off;
-    for (int j = 0; j < valid; ++j) o[j] = static_cast<int>(r[j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) o[j] = static_cast<int>(r[j]);
   } else {
-    for (int j = 0; j < valid; ++j) store_one(a.out, a.out_dtype, off + j, v[j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) store_one(a.out, a.out_dtype, off + j, v[j]);
   }
 }
 
 // Conv epilogues: one thread, one bordered pixel `p`, channels n0..n0+31 in r[].
 template <int EPI>
 __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, const uint32_t (&r)[32],
-                                           float scale_lane) {
+                                           float scale_lane, float bias_lane) {
   const int img = p / a.HWp;
   const int rem = p - img * a.HWp;
   const int yp = rem / a.Wp;
@@ -225,24 +229,46 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, con
     const int64_t base = (static_cast<int64_t>(img) * a.N + n0) * HW + static_cast<int64_t>(yp - 1) * a.W + (xp - 1);
     if (a.relu) {
       uint8_t* o = static_cast<uint8_t*>(a.out) + base;
-      for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<uint8_t>(requant(static_cast<int>(r[j]), a.shift, 1));
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) o[j * HW] = static_cast<uint8_t>(requant(static_cast<int>(r[j]), a.shift, 1));
     } else {
       int8_t* o = static_cast<int8_t*>(a.out) + base;
-      for (int j = 0; j < nvalid; ++j) o[j * HW] = static_cast<int8_t>(requant(static_cast<int>(r[j]), a.shift, 0));
-    }
-  } else {  // EPI_CONV_DEQ: q.float() * (scale[co] * sx[img]) (+ bias[co])
-    const float s = valid ? a.sx[img] : 0.f;
-    float f[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = __shfl_sync(kFull, scale_lane, j);
-    if (!valid) return;
-    const int64_t HW = static_cast<int64_t>(a.H) * a.W;
-    const int64_t base = (static_cast<int64_t>(img) * a.N + n0) * HW + static_cast<int64_t>(yp - 1) * a.W + (xp - 1);
-    for (int j = 0; j < nvalid; ++j) {
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) o[j * HW] = static_cast<int8_t>(requant(static_cast<int>(r[j]), a.shift, 0));
+    }
+  } else {  // EPI_CONV_DEQ: q.float() * (scale[co] * sx[img]) (+ bias[co]), channels-last output
+    const float s = valid ? a.sx[img] : 0.f;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
       const int q = requant(static_cast<int>(r[j]), a.shift, a.relu);
-      float y = __fmul_rn(static_cast<float>(q), __fmul_rn(f[j], s));
-      if (a.bias != nullptr) y = __fadd_rn(y, load_as_float(a.bias, a.bias_dtype, n0 + j));
-      store_one(a.out, a.out_dtype, base + j * HW, y);
+      v[j] = __fmul_rn(static_cast<float>(q), __fmul_rn(__shfl_sync(kFull, scale_lane, j), s));
+    }
+    if (a.bias != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __shfl_sync(kFull, bias_lane, j));
+    }
+    if (!valid) return;
+    // out[img, yp-1, xp-1, co]: the 32 channels of this pixel are contiguous
+    const int64_t base = ((static_cast<int64_t>(img) * a.H + (yp - 1)) * a.W + (xp - 1)) * a.N + n0;
+    if (nvalid == 32 && a.vec_ok) {
+      if (a.out_dtype == XDNA_F32) {
+        float4* o = reinterpret_cast<float4*>(static_cast<float*>(a.out) + base);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      } else {
+        uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + base);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = make_uint4(pack2(v[8 * j], v[8 * j + 1], a.out_dtype), pack2(v[8 * j + 2], v[8 * j + 3], a.out_dtype),
+                            pack2(v[8 * j + 4], v[8 * j + 5], a.out_dtype), pack2(v[8 * j + 6], v[8 * j + 7], a.out_dtype));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) store_one(a.out, a.out_dtype, base + j, v[j]);
     }
   }
 }
@@ -663,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           } else {
-            conv_chunk<EPI>(args, row, n0, rc, fcol[c]);
+            conv_chunk<EPI>(args, row, n0, rc, fcol[c], bcol[c]);
           }
         }
         if (c + 1 < NCH) tmem_ld_wait();

@@ -93,7 +93,10 @@ class ConvLayer:
         return out
 
     def dequant(self, xp, n, sx, bias, dtype):
-        out = torch.empty((n, self.co, self.h, self.w), dtype=dtype, device=xp.device)
+        # channels-last: the epilogue writes each pixel's channels contiguously (same values and shape as
+        # the reference's NCHW tensor; torch ops downstream keep the layout)
+        out = torch.empty((n, self.co, self.h, self.w), dtype=dtype, device=xp.device,
+                          memory_format=torch.channels_last)
         kernels.conv3x3(xp, self.wp, n, self.ci, self.co, self.h, self.w, kernels.CONV_DEQUANT, shift=self.shift,
                         relu=self.relu, scale=self.scale, sx=sx, bias=bias, out=out)
         stats.launches += 1
@@ -116,6 +119,12 @@ def _layer(weight, h, w, relu):
     layer = ConvLayer(weight, h, w, relu)
     _layers[key] = (weakref.ref(weight), layer)
     return layer
+
+
+def _channels_last(t):
+    """True when t [N, C, H, W] is stored channels-last and not also plain contiguous."""
+    return (t.is_contiguous(memory_format=torch.channels_last) and not t.is_contiguous()
+            and t.data_ptr() % 16 == 0)
 
 
 def _bordered(n, h, w, cp, device):
@@ -167,11 +176,14 @@ def conv3x3_fused(cfg, x, weight, bias, relu):
     with _lock:
         layer = _layer(weight, h, w, relu)
         xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
-        xc = xc.contiguous()
         xp = _bordered(n, h, w, layer.cp, x.device)
         sx = torch.empty((n,), dtype=torch.float32, device=x.device)
         scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
-        kernels.conv_quant(xc, xp, sx, scratch)
+        if _channels_last(xc):      # e.g. the previous conv's output: a streaming quantise, no transpose
+            kernels.conv_quant_channels_last(xc, xp, sx, scratch)
+        else:
+            xc = xc.contiguous()
+            kernels.conv_quant(xc, xp, sx, scratch)
         stats.launches += 2
         if layer.shift is None:
             layer.calibrate(xp)

@@ -57,6 +57,7 @@ def _load():
         "xdna_quant_rows_i8": ([P, I, I64, I64, I64, P, I64, P, P], I),
         "xdna_gemm_i8": ([P, I64, P, I64, I64, I64, I64, P, P, P, I, P, I, I64, P], I),
         "xdna_conv_quant_nhwc": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
+        "xdna_conv_quant_channels_last": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_pack_input": ([P, I64, I64, I64, I64, P, I64, P], I),
         "xdna_conv_pack_weight": ([P, I64, I64, P, I64, P], I),
         "xdna_conv3x3_i8": ([P, P, I64, I64, I64, I64, I64, I64, I, I, I, P, P, P, I, P, I, P, P], I),
@@ -189,6 +190,15 @@ def conv_quant(x, xp, sx, scratch):
     N, C, H, W = x.shape
     _check("xdna_conv_quant_nhwc", L.xdna_conv_quant_nhwc(_p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp),
                                                           xp.shape[-1], _p(sx), _p(scratch), _stream()))
+
+
+def conv_quant_channels_last(x, xp, sx, scratch):
+    """conv_quant for x [N, C, H, W] stored channels-last (x.is_contiguous(memory_format=channels_last))."""
+    L = require()
+    _cuda(x, xp, sx, scratch)
+    N, C, H, W = x.shape
+    _check("xdna_conv_quant_channels_last", L.xdna_conv_quant_channels_last(
+        _p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp), xp.shape[-1], _p(sx), _p(scratch), _stream()))
 
 
 def conv_pack_input(xq, xp):

@@ -85,7 +85,9 @@ def conv3x3_fused(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Te
 
 @conv3x3_fused.register_fake
 def _(x, weight, bias, relu, cfg_id):
-    return x.new_empty((x.shape[0], weight.shape[0], x.shape[2], x.shape[3]))
+    # the kernel writes channels-last memory (see conv.ConvLayer.dequant)
+    return torch.empty((x.shape[0], weight.shape[0], x.shape[2], x.shape[3]), dtype=x.dtype, device=x.device,
+                       memory_format=torch.channels_last)
 
 
 @torch.library.custom_op("xdna::qwen3_stack", mutates_args=())
