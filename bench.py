@@ -58,6 +58,10 @@ def parse():
     ap.add_argument("--seq-len", type=int, default=1024, help="stack: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="stack: decoder layers")
     ap.add_argument("--images", type=int, default=32, help="conv: images in the global batch")
+    ap.add_argument("--kernel", default=None,
+                    choices=["gemm_i8", "quant_rows", "conv3x3", "attention", "gemm_bf16"],
+                    help="time one kernel on --shape instead of a workload (profiling)")
+    ap.add_argument("--shape", default="8192,6144,1024", help="--kernel shape, comma-separated")
     args = ap.parse_args()
     if args.workload in ("stack", "conv") and args.steps == 2000:
         args.steps = 10          # a step of these workloads is milliseconds, not microseconds
@@ -738,8 +742,74 @@ def run_reference_workload(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel(args):
+    """--kernel NAME --shape a,b,c: one kernel of libxdna_b200 on one shape, warm-up then 20 launches timed
+    with CUDA events (the command the profiles/ summaries are captured with). Prints one JSON line."""
+    from torch_xdna import conv as xconv
+    from torch_xdna import kernels
+
+    dev = torch.device("cuda", 0)
+    shp = [int(v) for v in args.shape.split(",")]
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel == "gemm_i8":                      # M, N, K: bf16 out through the dequantising epilogue
+        M, N, K = shp
+        xq = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+        wq = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g)
+        sx, sw = torch.rand(M, device=dev) * 0.01, torch.rand(N, device=dev) * 0.01
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        fn, work, unit = (lambda: kernels.gemm_i8(xq, wq, K, y, sx, sw)), 2 * M * N * K, "TOPS"
+    elif args.kernel == "quant_rows":                 # R, K: bf16 rows
+        R, K = shp
+        x = torch.randn(R, K, device=dev, generator=g).to(torch.bfloat16)
+        xq, sx = torch.empty(R, K, dtype=torch.int8, device=dev), torch.empty(R, device=dev)
+        fn, work, unit = (lambda: kernels.quant_rows(x, xq, sx)), 3 * R * K, "GB/s"
+    elif args.kernel == "conv3x3":                    # N, C, H: C -> C channels on H x H, dequantise epilogue
+        N, C, H = shp
+        w = torch.nn.Parameter(torch.randn(C, C, 3, 3, device=dev, generator=g) * (2 / (C * 9)) ** 0.5)
+        lay = xconv.ConvLayer(w, H, H, False)
+        lay.shift, lay.scale = 10, lay.sw * 1024.0
+        xp = torch.randint(-127, 128, (N, H + 2, H + 2, lay.cp), dtype=torch.int8, device=dev, generator=g)
+        sx, b = torch.rand(N, device=dev), torch.randn(C, device=dev) * 0.01
+        y = torch.empty(N, C, H, H, device=dev, memory_format=torch.channels_last)
+        fn = lambda: kernels.conv3x3(xp, lay.wp, N, C, C, H, H, kernels.CONV_DEQUANT, shift=10, scale=lay.scale,  # noqa
+                                     sx=sx, bias=b, out=y)
+        work, unit = 2 * N * C * C * H * H * 9, "TOPS"
+    elif args.kernel == "attention":                  # B, L: causal, 16 q heads / 8 kv heads of 128
+        B, L = shp
+        qk = torch.randn(B * L, 3072, device=dev, generator=g).to(torch.bfloat16)
+        vt = torch.randn(1024, B * ((L + 7) // 8 * 8), device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty(B * L, 2048, dtype=torch.bfloat16, device=dev)
+        fn = lambda: kernels.attention(qk, vt, out, B, L, kernels.MASK_CAUSAL)  # noqa
+        work, unit = B * 2 * 2 * 16 * 128 * (L * (L + 1) // 2), "TFLOP/s"
+    elif args.kernel == "gemm_bf16":                  # M, N, K: bf16 out (the head's epilogue)
+        M, N, K = shp
+        a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        b = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        fn, work, unit = (lambda: kernels.gemm_bf16(a, b, kernels.GEMM_F32ACC, out=y)), 2 * M * N * K, "TFLOP/s"
+    else:
+        raise SystemExit(f"unknown kernel {args.kernel}")
+    for _ in range(5):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(20):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) / 20 * 1e3
+    if kernels.take_device_error() != (0, 0):
+        raise SystemExit("a kernel recorded a device-side timeout")
+    print(json.dumps({"kernel": args.kernel, "shape": shp, "us_per_launch": round(us, 2),
+                      "rate": round(work / us / 1e6 if unit != "GB/s" else work / us / 1e3, 1), "unit": unit}))
+
+
 def main():
     args = parse()
+    if args.kernel:
+        run_kernel(args)
+        return
     rank, world = dist_init(args.gpus)
     try:
         if args.impl == "reference":

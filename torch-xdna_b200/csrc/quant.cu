@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(256) to_bordered_nhwc_kernel(const T* __restri
     if (in_row && c < C) {
       const T v = x[((static_cast<int64_t>(n) * C + c) * H + y) * W + xin];
       if constexpr (QUANT)
-        q = quant1(to_f32(v), s, r);
+        q = static_cast<int8_t>(quant_byte(to_f32(v), s, r) & 0xFFu);
       else
         q = static_cast<int8_t>(v);
     }

@@ -203,7 +203,7 @@ __device__ __forceinline__ void store_direct(const GemmArgs& a, int row, int n0,
 // Conv epilogues: one thread, one bordered pixel `p`, channels n0..n0+31 in r[].
 template <int EPI>
 __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, const uint32_t (&r)[32],
-                                           float scale_lane, float bias_lane) {
+                                           float scale_lane, float bias_lane, uint8_t* stage) {
   const int img = p / a.HWp;
   const int rem = p - img * a.HWp;
   const int yp = rem / a.Wp;
@@ -250,9 +250,43 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, con
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __shfl_sync(kFull, bias_lane, j));
     }
-    if (!valid) return;
     // out[img, yp-1, xp-1, co]: the 32 channels of this pixel are contiguous
     const int64_t base = ((static_cast<int64_t>(img) * a.H + (yp - 1)) * a.W + (xp - 1)) * a.N + n0;
+    if (nvalid == 32 && a.vec_ok && stage != nullptr) {
+      // through shared memory, so that each store instruction writes whole 128-byte lines: lane i first
+      // parks its pixel's 32 values (row i, 16-byte chunks swizzled by i), then the warp writes 4 (f32)
+      // or 8 (2-byte) pixels per instruction, one 16-byte chunk per lane
+      const int lane = lane_id();
+      const bool f32 = a.out_dtype == XDNA_F32;
+      const int chunks = f32 ? 8 : 4;               // 16-byte chunks per pixel
+      uint4* row = reinterpret_cast<uint4*>(stage) + lane * 8;
+      if (f32) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          row[j ^ (lane & 7)] = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                           __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          row[j ^ (lane & 7)] = make_uint4(pack2(v[8 * j], v[8 * j + 1], a.out_dtype), pack2(v[8 * j + 2], v[8 * j + 3], a.out_dtype),
+                                           pack2(v[8 * j + 4], v[8 * j + 5], a.out_dtype), pack2(v[8 * j + 6], v[8 * j + 7], a.out_dtype));
+      }
+      __syncwarp();
+      const int per = 32 / chunks;                  // pixels per store instruction
+      const int es = f32 ? 4 : 2;
+#pragma unroll 1
+      for (int it = 0; it < chunks; ++it) {
+        const int px = it * per + lane / chunks;    // which of the warp's 32 pixels this lane writes
+        const int ch = lane % chunks;
+        const int64_t pbase = __shfl_sync(kFull, static_cast<long long>(base), px);
+        const bool pvalid = __shfl_sync(kFull, valid ? 1 : 0, px) != 0;
+        const uint4 val = reinterpret_cast<const uint4*>(stage)[px * 8 + (ch ^ (px & 7))];
+        if (pvalid) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + pbase * es + ch * 16) = val;
+      }
+      __syncwarp();
+      return;
+    }
+    if (!valid) return;
     if (nvalid == 32 && a.vec_ok) {
       if (a.out_dtype == XDNA_F32) {
         float4* o = reinterpret_cast<float4*>(static_cast<float*>(a.out) + base);
@@ -689,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           } else {
-            conv_chunk<EPI>(args, row, n0, rc, fcol[c], bcol[c]);
+            conv_chunk<EPI>(args, row, n0, rc, fcol[c], bcol[c], obuf);
           }
         }
         if (c + 1 < NCH) tmem_ld_wait();
