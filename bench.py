@@ -743,8 +743,10 @@ def run_reference_workload(args, rank, world):
 
 
 def run_kernel(args):
-    """--kernel NAME --shape a,b,c: one kernel of libxdna_b200 on one shape, warm-up then 20 launches timed
-    with CUDA events (the command the profiles/ summaries are captured with). Prints one JSON line."""
+    """--kernel NAME --shape a,b,c: one kernel of libxdna_b200 on one shape, warm-up then 20 launches replayed
+    from a CUDA graph and timed with CUDA events (the command the profiles/ summaries are captured with;
+    back-to-back launches on the same inputs, so operands may stay in L2 between them). Prints one JSON
+    line."""
     from torch_xdna import conv as xconv
     from torch_xdna import kernels
 
@@ -792,10 +794,16 @@ def run_kernel(args):
     for _ in range(5):
         fn()
     torch.cuda.synchronize()
+    # 20 launches captured in a CUDA graph: the replay times the kernels, not the host's launch path
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(20):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(20):
-        fn()
+    graph.replay()
     e.record()
     torch.cuda.synchronize()
     us = s.elapsed_time(e) / 20 * 1e3

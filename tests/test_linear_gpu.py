@@ -94,6 +94,8 @@ def gemm_gpu(xq, wq, K, out_dtype, sx=None, sw=None, bias=None):
 GEMM_SHAPES = [
     (1, 4096, 1024), (37, 300, 200), (128, 64, 128), (129, 200, 1040), (512, 3072, 1024), (300, 520, 1024),
     (1000, 1000, 1000), (2048, 6144, 1024), (512, 1024, 3072), (4096, 4096, 4096),
+    # 256 x 256 tiles on CTA pairs, with a ragged last pair (odd CTA partly / wholly past M)
+    (2300, 6144, 1024), (1100, 8192, 512),
 ]
 
 
@@ -127,7 +129,7 @@ def test_gemm_int32_extremes(cuda):
 
 @pytest.mark.parametrize("out", ["float32", "bfloat16", "float16"])
 @pytest.mark.parametrize("bias", [False, True])
-@pytest.mark.parametrize("M,N,K", [(37, 300, 200), (512, 3072, 1024), (257, 136, 64)])
+@pytest.mark.parametrize("M,N,K", [(37, 300, 200), (512, 3072, 1024), (257, 136, 64), (1100, 8192, 512)])
 def test_gemm_dequant_bitexact(cuda, out, bias, M, N, K):
     x, w, b = mg.linear_inputs(M * 3 + N, M, K, N, bias=True)
     xq, sx = orc.quant_rows(x)
@@ -287,6 +289,45 @@ def test_bf16_linear_cat_projection_set(cuda):
                                   [None, None, None], cid)
     want, *_ = orc.linear(xb, wb, None, x_dtype="bfloat16")
     assert np.array_equal(y.float().cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("rows,n,k,bias", [(512, 4096, 1024, False), (300, 1000, 333, True), (1, 6, 7, True),
+                                           (129, 3072, 1024, True)])
+def test_precision_bf16_linear(cuda, dtype, rows, n, k, bias):
+    """precision="bf16": bf16 operands, f32 accumulate, bias in f32, one rounding to x.dtype — against the
+    f32 product of the same bf16-rounded operands (bf16 out: within its half-ulp; f32/f16: 1e-5 / 1e-3)."""
+    import torch_xdna
+
+    cid = torch_xdna.ops.config_id(torch_xdna.Config(precision="bf16", verify="first"))
+    g = torch.Generator(device=cuda).manual_seed(rows * n + k)
+    dt = TORCH_DT[dtype]
+    x = torch.randn(rows, k, device=cuda, generator=g).to(dt)
+    w = (torch.randn(n, k, device=cuda, generator=g) * 0.05).to(dt)
+    b = torch.randn(n, device=cuda, generator=g).to(dt) if bias else None
+    y = torch.ops.xdna.linear(x, w, b, False, cid)
+    assert y.dtype == dt and y.shape == (rows, n) and y.is_contiguous()
+    want = x.bfloat16().double() @ w.bfloat16().double().t()
+    if b is not None:
+        want = want + b.double()
+    err = ((y.double() - want).abs().max() / want.abs().max()).item()
+    assert err < {"bfloat16": 8e-3, "float16": 1e-3, "float32": 1e-5}[dtype], err
+    yt = torch.ops.xdna.linear(x, w.t().contiguous(), b, True, cid)       # x @ W with W [K, N]
+    assert torch.equal(yt, y)
+
+
+def test_precision_bf16_linear_cat_and_compile(cuda):
+    """precision="bf16" through torch.compile: the fused q/k/v GEMM equals three separate bf16 GEMMs."""
+    import torch_xdna
+
+    torch.manual_seed(1)
+    net = Attn().eval().to(cuda)
+    x = torch.randn(200, 256, device=cuda)
+    with torch.no_grad():
+        ref = net(x)
+    y = _run(net, x, precision="bf16")
+    assert torch_xdna.stats.as_dict()["calls"] == {"gpu": 2}
+    assert ((y - ref).norm() / ref.norm()).item() < 1e-2
 
 
 def test_verify_first_passes_and_records(cuda):

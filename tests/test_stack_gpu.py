@@ -45,7 +45,8 @@ def test_rmsnorm(cuda):
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("M,N,K", [(333, 520, 1000), (128, 64, 64), (1, 4096, 1024), (1030, 1024, 3072)])
+@pytest.mark.parametrize("M,N,K", [(333, 520, 1000), (128, 64, 64), (1, 4096, 1024), (1030, 1024, 3072),
+                                   (2300, 8192, 1024)])  # the last: 256 x 256 tiles on CTA pairs
 def test_gemm_bf16_f32acc(cuda, out_dtype, M, N, K):
     from torch_xdna import kernels
 
@@ -58,21 +59,22 @@ def test_gemm_bf16_f32acc(cuda, out_dtype, M, N, K):
     assert rel_max(out, want) < (1e-4 if out_dtype == torch.float32 else 8e-3)
 
 
-def test_gemm_bf16_residual(cuda):
+@pytest.mark.parametrize("M", [700, 8300])  # 8300: CTA pairs
+def test_gemm_bf16_residual(cuda, M):
     from torch_xdna import kernels
 
-    a = bf(torch.randn(700, 2048, device=cuda))
+    a = bf(torch.randn(M, 2048, device=cuda))
     b = bf(torch.randn(1024, 2048, device=cuda) * 0.02)
-    resid = torch.randn(700, 1024, device=cuda)
+    resid = torch.randn(M, 1024, device=cuda)
     want = resid + a.float() @ b.float().t()
     kernels.gemm_bf16(a, b, kernels.GEMM_RESID, resid=resid)
     assert rel_max(resid, want) < 1e-5
 
 
-def test_gemm_bf16_swiglu(cuda):
+@pytest.mark.parametrize("M", [500, 1000])  # 1000: CTA pairs
+def test_gemm_bf16_swiglu(cuda, M):
     from torch_xdna import kernels
 
-    M = 500
     h = bf(torch.randn(M, 1024, device=cuda))
     gate = bf(torch.randn(3072, 1024, device=cuda) * 0.03)
     up = bf(torch.randn(3072, 1024, device=cuda) * 0.03)
@@ -117,11 +119,11 @@ def _project(h, L, dev, g):
     return wq, wk, wv, qn, kn
 
 
-def test_gemm_bf16_qkv_norm_rope(cuda):
+@pytest.mark.parametrize("B,L", [(3, 100), (5, 256), (13, 100)])  # the last two: CTA pairs (V^T by TMA / direct)
+def test_gemm_bf16_qkv_norm_rope(cuda, B, L):
     from torch_xdna import kernels
 
     g = torch.Generator(device=cuda).manual_seed(3)
-    B, L = 3, 100
     T = B * L
     h = bf(torch.randn(T, 1024, device=cuda, generator=g))
     wq, wk, wv, qn, kn = _project(h, L, cuda, g)

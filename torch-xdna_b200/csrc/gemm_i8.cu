@@ -6,35 +6,35 @@
 
 namespace xdna {
 
-template <int BN, int LOAD, int EPI, bool TSTORE, int ODT>
+template <int BN, int LOAD, int EPI, bool TSTORE, int ODT, int KB>
 static int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
                        int sms, cudaStream_t stream) {
-  constexpr int smem = smem_bytes_for<BN>();
-  auto kern = umma_gemm_kernel<BN, LOAD, EPI, false, TSTORE, ODT>;
-  static bool configured[64] = {};  // per instantiation and device
-  int dev = 0;
-  XDNA_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    XDNA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
-  const int tiles = args.m_tiles * args.n_tiles;
-  const int grid = std::max(1, std::min(tiles, sms));
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, ta, args);
-  return check_launch("umma_gemm_kernel");
+  return launch_gemm_kernel<BN, LOAD, EPI, false, TSTORE, ODT, KB, false>(ta, tb, tc, ta, args, sms, stream);
 }
 
-template <int LOAD, int EPI, bool TSTORE, int ODT>
-static int dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+template <int LOAD, int EPI, bool TSTORE, int ODT, int KB = kBKBytes>
+static int dispatch_bn(int bn, bool pair, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                        const GemmArgs& args, int sms, cudaStream_t stream) {
   switch (bn) {
     case 256:
-      return launch_umma<256, LOAD, EPI, TSTORE, ODT>(ta, tb, tc, args, sms, stream);
+      if constexpr (LOAD == LOAD_GEMM && KB == 128) {
+        if (pair) return launch_gemm_kernel<256, LOAD, EPI, false, TSTORE, ODT, KB, true>(ta, tb, tc, ta, args, sms, stream);
+      }
+      return launch_umma<256, LOAD, EPI, TSTORE, ODT, KB>(ta, tb, tc, args, sms, stream);
     case 128:
-      return launch_umma<128, LOAD, EPI, TSTORE, ODT>(ta, tb, tc, args, sms, stream);
+      return launch_umma<128, LOAD, EPI, TSTORE, ODT, KB>(ta, tb, tc, args, sms, stream);
     default:
-      return launch_umma<64, LOAD, EPI, TSTORE, ODT>(ta, tb, tc, args, sms, stream);
+      return launch_umma<64, LOAD, EPI, TSTORE, ODT, KB>(ta, tb, tc, args, sms, stream);
   }
+}
+
+// The conv's kernel for one mode, with 64-byte K blocks when the input has at most 64 channels (a
+// 128-byte block would be half zero fill).
+template <int EPI, int ODT>
+static int dispatch_conv(int kb, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int sms,
+                         cudaStream_t stream) {
+  if (kb == 64) return dispatch_bn<LOAD_CONV, EPI, false, ODT, 64>(bn, false, ta, tb, ta, args, sms, stream);
+  return dispatch_bn<LOAD_CONV, EPI, false, ODT, 128>(bn, false, ta, tb, ta, args, sms, stream);
 }
 
 // Widest tile that still gives every SM work; 64 for narrow outputs.
@@ -85,6 +85,8 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
   a.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
   const int bn = choose_bn(a.m_tiles, N, sms);
   a.n_tiles = static_cast<int>((N + bn - 1) / bn);
+  const bool pair = use_pairs(bn, a.m_tiles, a.n_tiles, sms);
+  if (pair) a.m_tiles = static_cast<int>((M + 2 * kBM - 1) / (2 * kBM));
   a.out = y;
   a.ldo = ldy;
   a.out_dtype = y_dtype;
@@ -107,38 +109,38 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldw)};
-    const uint32_t box[2] = {kBKBytes, static_cast<uint32_t>(bn)};
+    const uint32_t box[2] = {kBKBytes, static_cast<uint32_t>(pair ? bn / 2 : bn)};  // a pair: each CTA half of B
     rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, wq, dims, strides, box, "gemm_i8 weights");
     if (rc != XDNA_OK) return rc;
   }
-  // Output through TMA stores when the rows are 16-byte addressable (box: 32 columns x 32 rows).
+  // Output through TMA stores when the rows are 16-byte addressable (box: 32 rows x 64 bytes, i.e. 32
+  // columns of a 2-byte type or 16 of a 4-byte type, 64-byte swizzle).
   const bool tstore = a.vec_ok != 0;
   if (tstore) {
     const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldy * es)};
-    const uint32_t box[2] = {32, 32};
+    const uint32_t box[2] = {static_cast<uint32_t>(64 / es), 32};
     const CUtensorMapDataType dt = es == 4 ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                    : y_dtype == XDNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    rc = encode_tma(&tc, dt, 2, y, dims, strides, box, "gemm_i8 output",
-                    es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    rc = encode_tma(&tc, dt, 2, y, dims, strides, box, "gemm_i8 output", CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc != XDNA_OK) return rc;
   } else {
     tc = ta;  // unused
   }
   if (!tstore) {  // rows TMA cannot address: direct stores (any output type)
-    if (y_dtype == XDNA_I32) return dispatch_bn<LOAD_GEMM, EPI_I32, false, XDNA_I32>(bn, ta, tb, tc, a, sms, s);
-    return dispatch_bn<LOAD_GEMM, EPI_DEQ, false, XDNA_F32>(bn, ta, tb, tc, a, sms, s);
+    if (y_dtype == XDNA_I32) return dispatch_bn<LOAD_GEMM, EPI_I32, false, XDNA_I32>(bn, pair, ta, tb, tc, a, sms, s);
+    return dispatch_bn<LOAD_GEMM, EPI_DEQ, false, XDNA_F32>(bn, pair, ta, tb, tc, a, sms, s);
   }
   switch (y_dtype) {
     case XDNA_I32:
-      return dispatch_bn<LOAD_GEMM, EPI_I32, true, XDNA_I32>(bn, ta, tb, tc, a, sms, s);
+      return dispatch_bn<LOAD_GEMM, EPI_I32, true, XDNA_I32>(bn, pair, ta, tb, tc, a, sms, s);
     case XDNA_F32:
-      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_F32>(bn, ta, tb, tc, a, sms, s);
+      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_F32>(bn, pair, ta, tb, tc, a, sms, s);
     case XDNA_BF16:
-      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_BF16>(bn, ta, tb, tc, a, sms, s);
+      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_BF16>(bn, pair, ta, tb, tc, a, sms, s);
     default:
-      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_F16>(bn, ta, tb, tc, a, sms, s);
+      return dispatch_bn<LOAD_GEMM, EPI_DEQ, true, XDNA_F16>(bn, pair, ta, tb, tc, a, sms, s);
   }
 }
 
@@ -177,7 +179,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   GemmArgs a{};
   a.M = static_cast<int>(NP);
   a.N = static_cast<int>(Co);
-  a.cblocks = static_cast<int>((Cp + kBKBytes - 1) / kBKBytes);
+  const int kb = Cp <= 64 ? 64 : kBKBytes;  // K block bytes (= channels) per tap
+  a.cblocks = static_cast<int>((Cp + kb - 1) / kb);
   a.num_kb = 9 * a.cblocks;
   a.m_tiles = static_cast<int>((NP + kBM - 1) / kBM);
   const int bn = choose_bn(a.m_tiles, Co, sms);
@@ -186,6 +189,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   a.HWp = static_cast<int>(HWp);
   a.H = static_cast<int>(H);
   a.W = static_cast<int>(W);
+  a.div_wp = make_fastdiv(static_cast<uint32_t>(Wp));
+  a.div_hwp = make_fastdiv(static_cast<uint32_t>(HWp));
   a.out = out;
   a.out_dtype = out_dtype;
   // XDNA_CONV_DEQUANT writes channels-last: 32 channels of a pixel as 16-byte vectors when aligned
@@ -203,24 +208,26 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(NP)};
     const uint64_t strides[1] = {static_cast<uint64_t>(Cp)};
-    const uint32_t box[2] = {kBKBytes, kBM};
-    rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations");
+    const uint32_t box[2] = {static_cast<uint32_t>(kb), kBM};
+    rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations",
+                    kb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != XDNA_OK) return rc;
   }
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(Cp), 9, static_cast<uint64_t>(Co)};
     const uint64_t strides[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(9 * Cp)};
-    const uint32_t box[3] = {kBKBytes, 1, static_cast<uint32_t>(bn)};
-    rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wp, dims, strides, box, "conv3x3 weights");
+    const uint32_t box[3] = {static_cast<uint32_t>(kb), 1, static_cast<uint32_t>(bn)};
+    rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wp, dims, strides, box, "conv3x3 weights",
+                    kb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != XDNA_OK) return rc;
   }
   switch (mode) {
     case XDNA_CONV_Q:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_Q, false, XDNA_I8>(bn, ta, tb, ta, a, sms, s);
+      return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, ta, tb, a, sms, s);
     case XDNA_CONV_DEQUANT:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_DEQ, false, XDNA_F32>(bn, ta, tb, ta, a, sms, s);
+      return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, ta, tb, a, sms, s);
     default:
-      return dispatch_bn<LOAD_CONV, EPI_CONV_CALIB, false, XDNA_I32>(bn, ta, tb, ta, a, sms, s);
+      return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, ta, tb, a, sms, s);
   }
 }
 

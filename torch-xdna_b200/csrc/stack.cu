@@ -81,20 +81,15 @@ __global__ void __launch_bounds__(256) embed_kernel(const int64_t* __restrict__ 
 // ---------------------------------------------------------------------------- bf16 GEMM launch
 template <int BN, int EPI, int ODT>
 static int launch_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
-                       int sms, cudaStream_t stream, const CUtensorMap* td = nullptr) {
+                       int sms, bool pair, cudaStream_t stream, const CUtensorMap* td = nullptr) {
   constexpr bool TSTORE = (EPI == EPI_F32ACC || EPI == EPI_QKV || EPI == EPI_SWIGLU);
-  constexpr int smem = smem_bytes_for<BN>();
-  auto kern = umma_gemm_kernel<BN, LOAD_GEMM, EPI, true, TSTORE, ODT>;
-  static bool configured[64] = {};
-  int dev = 0;
-  XDNA_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    XDNA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+  if constexpr (BN == 256) {
+    if (pair)
+      return launch_gemm_kernel<BN, LOAD_GEMM, EPI, true, TSTORE, ODT, kBKBytes, true>(ta, tb, tc, td ? *td : ta, a, sms,
+                                                                                       stream);
   }
-  const int tiles = a.m_tiles * a.n_tiles;
-  kern<<<std::max(1, std::min(tiles, sms)), kThreads, smem, stream>>>(ta, tb, tc, td ? *td : ta, a);
-  return check_launch("umma_gemm_kernel (bf16)");
+  return launch_gemm_kernel<BN, LOAD_GEMM, EPI, true, TSTORE, ODT, kBKBytes, false>(ta, tb, tc, td ? *td : ta, a, sms,
+                                                                                    stream);
 }
 
 static int bf16_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols, int64_t ld, uint32_t box_rows,
@@ -110,11 +105,11 @@ static int out_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols, in
   const int es = dtype_size(dtype);
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
   const uint64_t strides[1] = {static_cast<uint64_t>(ld * es)};
-  const uint32_t box[2] = {32, 32};
+  const uint32_t box[2] = {static_cast<uint32_t>(64 / es), 32};  // 32 rows x 64 bytes (the epilogue's staging)
   const CUtensorMapDataType dt = dtype == XDNA_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : dtype == XDNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return encode_tma(m, dt, 2, p, dims, strides, box, what, es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  return encode_tma(m, dt, 2, p, dims, strides, box, what, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 // C[M, N] = A[M, K] . B[N, K]^T (bf16, f32 accumulate) with one of the stack epilogues.
@@ -160,6 +155,8 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
       (g.N <= 128 || a.m_tiles * ((g.N + 255) / 256) < sms))
     bn = 128;
   a.n_tiles = static_cast<int>((g.N + bn - 1) / bn);
+  const bool pair = use_pairs(bn, a.m_tiles, a.n_tiles, sms);
+  if (pair) a.m_tiles = static_cast<int>((g.M + 2 * kBM - 1) / (2 * kBM));
   a.out = g.out;
   a.ldo = g.ldo;
   a.out_dtype = g.out_dtype;
@@ -178,7 +175,8 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
   a.err = device_error_word();
   CUtensorMap ta, tb, tc;
   if ((rc = bf16_map(&ta, g.a, g.M, g.K, g.lda, kBM, "gemm_bf16 A")) != XDNA_OK) return rc;
-  if ((rc = bf16_map(&tb, g.b, g.N, g.K, g.ldb, static_cast<uint32_t>(bn), "gemm_bf16 B")) != XDNA_OK) return rc;
+  if ((rc = bf16_map(&tb, g.b, g.N, g.K, g.ldb, static_cast<uint32_t>(pair ? bn / 2 : bn), "gemm_bf16 B")) != XDNA_OK)
+    return rc;
   switch (g.mode) {
     case XDNA_GEMM_F32ACC: {
       XDNA_CHECK_ARG(g.out && is_float_dtype(g.out_dtype) && g.ldo >= g.N, "gemm_bf16: bad output");
@@ -187,23 +185,23 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
       XDNA_CHECK_ARG(a.vec_ok, "gemm_bf16: output rows must be 16-byte aligned (base and row pitch)");
       if ((rc = out_map(&tc, g.out, g.M, g.N, g.ldo, g.out_dtype, "gemm_bf16 out")) != XDNA_OK) return rc;
       if (g.out_dtype == XDNA_F32)
-        return bn == 256 ? launch_bf16<256, EPI_F32ACC, XDNA_F32>(ta, tb, tc, a, sms, s)
-                         : launch_bf16<128, EPI_F32ACC, XDNA_F32>(ta, tb, tc, a, sms, s);
+        return bn == 256 ? launch_bf16<256, EPI_F32ACC, XDNA_F32>(ta, tb, tc, a, sms, pair, s)
+                         : launch_bf16<128, EPI_F32ACC, XDNA_F32>(ta, tb, tc, a, sms, pair, s);
       if (g.out_dtype == XDNA_BF16)
-        return bn == 256 ? launch_bf16<256, EPI_F32ACC, XDNA_BF16>(ta, tb, tc, a, sms, s)
-                         : launch_bf16<128, EPI_F32ACC, XDNA_BF16>(ta, tb, tc, a, sms, s);
-      return bn == 256 ? launch_bf16<256, EPI_F32ACC, XDNA_F16>(ta, tb, tc, a, sms, s)
-                       : launch_bf16<128, EPI_F32ACC, XDNA_F16>(ta, tb, tc, a, sms, s);
+        return bn == 256 ? launch_bf16<256, EPI_F32ACC, XDNA_BF16>(ta, tb, tc, a, sms, pair, s)
+                         : launch_bf16<128, EPI_F32ACC, XDNA_BF16>(ta, tb, tc, a, sms, pair, s);
+      return bn == 256 ? launch_bf16<256, EPI_F32ACC, XDNA_F16>(ta, tb, tc, a, sms, pair, s)
+                       : launch_bf16<128, EPI_F32ACC, XDNA_F16>(ta, tb, tc, a, sms, pair, s);
     }
     case XDNA_GEMM_RESID:
       XDNA_CHECK_ARG(g.resid && g.ldr >= g.N && g.ldr % 4 == 0 && aligned16(g.resid), "gemm_bf16: bad residual");
       tc = ta;
-      return bn == 256 ? launch_bf16<256, EPI_RESID, XDNA_F32>(ta, tb, tc, a, sms, s)
-                       : launch_bf16<128, EPI_RESID, XDNA_F32>(ta, tb, tc, a, sms, s);
+      return bn == 256 ? launch_bf16<256, EPI_RESID, XDNA_F32>(ta, tb, tc, a, sms, pair, s)
+                       : launch_bf16<128, EPI_RESID, XDNA_F32>(ta, tb, tc, a, sms, pair, s);
     case XDNA_GEMM_SWIGLU:
       XDNA_CHECK_ARG(g.N % 64 == 0 && g.out && g.ldo >= g.N / 2, "gemm_bf16: swiglu needs N % 64 == 0 and an output");
       if ((rc = out_map(&tc, g.out, g.M, g.N / 2, g.ldo, XDNA_BF16, "gemm_bf16 swiglu out")) != XDNA_OK) return rc;
-      return launch_bf16<256, EPI_SWIGLU, XDNA_BF16>(ta, tb, tc, a, sms, s);
+      return launch_bf16<256, EPI_SWIGLU, XDNA_BF16>(ta, tb, tc, a, sms, pair, s);
     case XDNA_GEMM_QKV:
       XDNA_CHECK_ARG(g.N == kQCols + 2 * kKCols && g.out && g.vt && g.rope_cos && g.rope_sin && g.q_norm && g.k_norm &&
                          g.seq_len > 0 && g.ldvt % 8 == 0 &&
@@ -223,7 +221,7 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
                                CU_TENSOR_MAP_SWIZZLE_NONE)) != XDNA_OK)
             return rc;
         }
-        return launch_bf16<256, EPI_QKV, XDNA_BF16>(ta, tb, tc, a, sms, s, &td);
+        return launch_bf16<256, EPI_QKV, XDNA_BF16>(ta, tb, tc, a, sms, pair, s, &td);
       }
     default:
       return fail(XDNA_ERR_INVALID, "gemm_bf16: unknown mode %d", g.mode);

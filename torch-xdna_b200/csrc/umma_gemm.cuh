@@ -13,7 +13,7 @@
 //                 of the tile's columns, 32 columns per tcgen05.ld, issued one chunk ahead of the
 //                 arithmetic. Per-column factors arrive once per tile as one coalesced load per lane
 //                 and are broadcast with warp shuffles. GEMM outputs are staged in swizzled shared
-//                 memory (4 KB per warp) and written by TMA bulk-tensor stores (full lines, tails
+//                 memory (two 2 KB slots per warp, used in turn) and written by TMA bulk-tensor stores (full lines, tails
 //                 clipped by the tensor map); conv outputs (NCHW scatter) use direct stores.
 //
 // The A operand is either a plain row-major matrix (LOAD_GEMM) or, for the conv, the
@@ -22,6 +22,7 @@
 // TMA's zero fill covers rows before the first / past the last pixel and channels past Cp.
 #pragma once
 
+#include "host_util.h"
 #include "sm100.cuh"
 
 namespace xdna {
@@ -46,6 +47,23 @@ constexpr int kHeadDim = 128;
 constexpr int kQCols = 16 * kHeadDim;
 constexpr int kKCols = 8 * kHeadDim;
 
+// n / d for 32-bit n and a divisor d >= 2 fixed at launch: t = umulhi(n, m), n / d = (t + ((n - t) >> 1))
+// >> (l - 1), with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1 (Granlund and Montgomery,
+// "Division by invariant integers using multiplication", 1994, section 4).
+struct FastDiv {
+  uint32_t d, m, l;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((uint64_t(1) << l) < d) ++l;
+  const uint64_t m = ((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1;
+  return FastDiv{d, static_cast<uint32_t>(m), l};
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  const uint32_t t = __umulhi(n, f.m);
+  return (t + ((n - t) >> 1)) >> (f.l - 1);
+}
+
 struct GemmArgs {
   int M, N;            // output rows (GEMM rows, or bordered pixels for the conv) and columns
   int num_kb;          // 128-byte K blocks per tile
@@ -54,6 +72,7 @@ struct GemmArgs {
   int cblocks;         // 128-channel blocks per tap
   int Wp, HWp;         // W + 2, (H + 2) * (W + 2)
   int H, W;
+  FastDiv div_wp, div_hwp;
   // epilogue
   void* out;
   int64_t ldo;         // leading dimension of `out` in elements (GEMM modes)
@@ -82,10 +101,12 @@ struct GemmArgs {
 };
 
 constexpr int kBM = 128;
-constexpr int kBKBytes = 128;  // one 128-byte swizzle row per operand row per stage
+constexpr int kBKBytes = 128;  // one 128-byte swizzle row per operand row per stage (64 for convs of <= 64
+                               // input channels, whose rows are 64 bytes)
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kStageOutBytes = 4096;  // per epilogue warp: 32 rows x 32 columns x <= 4 bytes
+constexpr int kStageOutBytes = 4096;  // per epilogue warp: two 2 KB TMA-store slots (or one 4 KB scratch)
+constexpr int kStageSlotBytes = 2048; // 32 rows x 64 bytes
 constexpr int kGroupM = 8;     // tile raster: GROUP_M m-tiles share a column of n-tiles (L2 reuse)
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -93,15 +114,22 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
-template <int BN>
+// Operand stages in 192 KB (4 / 6 / 8 for BN = 256 / 128 / 64 with 128-byte K blocks), at most 12.
+template <int BN, int KB = kBKBytes>
 __host__ __device__ constexpr int stages_for() {
-  return BN >= 256 ? 4 : BN >= 128 ? 6 : 8;
+  return (192 * 1024) / ((kBM + BN) * KB) < 12 ? (192 * 1024) / ((kBM + BN) * KB) : 12;
 }
 
-template <int BN>
+template <int BN, int KB = kBKBytes>
 __host__ __device__ constexpr int smem_bytes_for() {
-  return stages_for<BN>() * (kBM + BN) * kBKBytes + kEpiWarps * kStageOutBytes + 1024 /*align*/ +
-         256 /*barriers*/;
+  return stages_for<BN, KB>() * (kBM + BN) * KB + kEpiWarps * kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;
+}
+
+// Tiles of M rows per CTA (pair) and whether a GEMM of m_tiles128 128-row tiles x n_tiles 256-column
+// tiles runs on CTA pairs: 256 x 256 tiles halve each CTA's share of B and cut its operand traffic by a
+// third, worth it once the pairs still cover every SM.
+inline bool use_pairs(int bn, int64_t m_tiles128, int64_t n_tiles, int sms) {
+  return bn == 256 && ((m_tiles128 + 1) / 2) * n_tiles >= sms / 2;
 }
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
@@ -158,26 +186,45 @@ __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float srow, f
   }
 }
 
-// Writes one 32 x 32 output block (this warp's rows, 32 columns) through swizzled shared memory and
-// a TMA store. `words` holds this lane's row: 16 words (2-byte outputs) or 32 words (4-byte outputs).
+// Per-warp staging for TMA stores: two 2 KB slots used in turn, so that the shared-memory writes of
+// one block overlap the TMA store still reading the previous one. Lane 0 issues and commits every
+// store of the warp (one bulk group each), so "at most one group still reading" frees the older slot.
+struct StageRing {
+  uint8_t* base;
+  int slot;
+  __device__ __forceinline__ uint8_t* acquire() {
+    if (lane_id() == 0) bulk_wait_read_one();
+    __syncwarp();
+    uint8_t* b = base + slot * kStageSlotBytes;
+    slot ^= 1;
+    return b;
+  }
+};
+
+// Writes this warp's 32 rows x 32 columns through 64-byte-swizzled staging and TMA stores. `words`
+// holds this lane's row: 16 words (2-byte outputs: one 32-column block) or 32 words (4-byte outputs:
+// two 16-column blocks). Every block is 32 rows x 64 bytes; the tensor map's box matches.
 template <int NWORDS>
-__device__ __forceinline__ void stage_and_store(uint8_t* buf, const uint32_t (&words)[NWORDS], const CUtensorMap* tmC,
-                                                int x, int y) {
+__device__ __forceinline__ void stage_and_store(StageRing& ring, const uint32_t (&words)[NWORDS],
+                                                const CUtensorMap* tmC, int x, int y) {
+  static_assert(NWORDS == 16 || NWORDS == 32, "2-byte or 4-byte outputs");
   const int lane = lane_id();
-  if (lane == 0) bulk_wait_read_all();  // the previous store from this buffer has read it
-  __syncwarp();
-  constexpr int CHUNKS = NWORDS / 4;    // 16-byte chunks per row: 4 (64 B rows) or 8 (128 B rows)
-  uint8_t* row = buf + lane * (CHUNKS * 16);
-  const int sw = CHUNKS == 8 ? (lane & 7) : ((lane >> 1) & 3);  // TMA 128B / 64B swizzle pattern
+  const int sw = (lane >> 1) & 3;  // TMA 64-byte swizzle: 16-byte chunk ^ address bits 7..8
 #pragma unroll
-  for (int k = 0; k < CHUNKS; ++k)
-    *reinterpret_cast<uint4*>(row + ((k ^ sw) * 16)) =
-        make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
-  fence_async_smem();
-  __syncwarp();
-  if (lane == 0) {
-    tma_store_2d(tmC, buf, x, y);
-    bulk_commit();
+  for (int h = 0; h < NWORDS / 16; ++h) {
+    uint8_t* buf = ring.acquire();
+    uint8_t* row = buf + lane * 64;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      *reinterpret_cast<uint4*>(row + ((k ^ sw) * 16)) =
+          make_uint4(words[16 * h + 4 * k], words[16 * h + 4 * k + 1], words[16 * h + 4 * k + 2],
+                     words[16 * h + 4 * k + 3]);
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, buf, x + h * 16, y);
+      bulk_commit();
+    }
   }
 }
 
@@ -200,15 +247,40 @@ __device__ __forceinline__ void store_direct(const GemmArgs& a, int row, int n0,
   }
 }
 
-// Conv epilogues: one thread, one bordered pixel `p`, channels n0..n0+31 in r[].
+// Where an epilogue thread's bordered pixel sits: image, bordered row and column, whether it is an
+// output pixel (not on the border), and the image's activation scale (dequantise only). Computed
+// before the thread waits for the accumulator, so the division and the scale load are off the
+// critical path.
+struct ConvPixel {
+  int img, yp, xp;
+  bool valid;
+  float s;
+};
+
 template <int EPI>
-__device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, const uint32_t (&r)[32],
+__device__ __forceinline__ ConvPixel conv_pixel(const GemmArgs& a, int p) {
+  ConvPixel px;
+  const uint32_t up = static_cast<uint32_t>(p);
+  px.img = static_cast<int>(fast_div(up, a.div_hwp));
+  const uint32_t rem = up - static_cast<uint32_t>(px.img) * static_cast<uint32_t>(a.HWp);
+  px.yp = static_cast<int>(fast_div(rem, a.div_wp));
+  px.xp = static_cast<int>(rem) - px.yp * a.Wp;
+  px.valid = p < a.M && px.yp >= 1 && px.yp <= a.H && px.xp >= 1 && px.xp <= a.W;
+  px.s = 0.f;
+  if constexpr (EPI == EPI_CONV_DEQ) {
+    if (px.valid) px.s = __ldg(a.sx + px.img);
+  }
+  return px;
+}
+
+// Conv epilogues: one thread, one bordered pixel, channels n0..n0+31 in r[].
+template <int EPI>
+__device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& px, int n0, const uint32_t (&r)[32],
                                            float scale_lane, float bias_lane, uint8_t* stage) {
-  const int img = p / a.HWp;
-  const int rem = p - img * a.HWp;
-  const int yp = rem / a.Wp;
-  const int xp = rem - yp * a.Wp;
-  const bool valid = p < a.M && yp >= 1 && yp <= a.H && xp >= 1 && xp <= a.W;
+  const int img = px.img;
+  const int yp = px.yp;
+  const int xp = px.xp;
+  const bool valid = px.valid;
   const int nvalid = min(32, a.N - n0);
   if constexpr (EPI == EPI_CONV_CALIB) {
     int best = 0;
@@ -239,7 +311,7 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, con
         if (j < nvalid) o[j * HW] = static_cast<int8_t>(requant(static_cast<int>(r[j]), a.shift, 0));
     }
   } else {  // EPI_CONV_DEQ: q.float() * (scale[co] * sx[img]) (+ bias[co]), channels-last output
-    const float s = valid ? a.sx[img] : 0.f;
+    const float s = px.s;
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -274,14 +346,16 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, int p, int n0, con
       __syncwarp();
       const int per = 32 / chunks;                  // pixels per store instruction
       const int es = f32 ? 4 : 2;
-#pragma unroll 1
-      for (int it = 0; it < chunks; ++it) {
-        const int px = it * per + lane / chunks;    // which of the warp's 32 pixels this lane writes
-        const int ch = lane % chunks;
-        const int64_t pbase = __shfl_sync(kFull, static_cast<long long>(base), px);
-        const bool pvalid = __shfl_sync(kFull, valid ? 1 : 0, px) != 0;
-        const uint4 val = reinterpret_cast<const uint4*>(stage)[px * 8 + (ch ^ (px & 7))];
-        if (pvalid) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + pbase * es + ch * 16) = val;
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        if (it < chunks) {                          // warp-uniform
+          const int pi = it * per + lane / chunks;  // which of the warp's 32 pixels this lane writes
+          const int ch = lane % chunks;
+          const int64_t pbase = __shfl_sync(kFull, static_cast<long long>(base), pi);
+          const bool pvalid = __shfl_sync(kFull, valid ? 1 : 0, pi) != 0;
+          const uint4 val = reinterpret_cast<const uint4*>(stage)[pi * 8 + (ch ^ (pi & 7))];
+          if (pvalid) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + pbase * es + ch * 16) = val;
+        }
       }
       __syncwarp();
       return;
@@ -315,7 +389,7 @@ __device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u);
 // (x * rsqrt(mean(x^2) + eps)) times the norm weight, then RoPE with the half rotation
 // (out[d] = x[d] cos - x[d+64] sin, out[d+64] = x[d+64] cos + x[d] sin), stored bf16 through TMA.
 // v heads are written transposed, V^T[head * 128 + d][token], the K-major operand of P.V.
-__device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, uint8_t* obuf,
+__device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, StageRing& ring,
                                          const CUtensorMap* tmC, const CUtensorMap* tmD) {
   const int lane = lane_id();
   const int row = row0 + lane;
@@ -333,15 +407,14 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
       if (a.vt_tma) {
         // 32 dims x 32 tokens, transposed through shared memory, one TMA store; the warp's 32 rows are
         // consecutive positions of one sequence, so their V^T columns are row0 .. row0 + 31
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-        __nv_bfloat16* t = reinterpret_cast<__nv_bfloat16*>(obuf);
+        uint8_t* buf = ring.acquire();
+        __nv_bfloat16* t = reinterpret_cast<__nv_bfloat16*>(buf);
 #pragma unroll
         for (int j = 0; j < 32; ++j) t[j * 32 + lane] = __float2bfloat16_rn(f32_of(x1[j]));
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(tmD, obuf, row0, vh * kHeadDim + c * 32);
+          tma_store_2d(tmD, buf, row0, vh * kHeadDim + c * 32);
           bulk_commit();
         }
       } else if (row < a.M) {
@@ -398,8 +471,8 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
       hi[q * 2] = pack2(o[0][1], o[1][1], XDNA_BF16);
       hi[q * 2 + 1] = pack2(o[2][1], o[3][1], XDNA_BF16);
     }
-    stage_and_store<16>(obuf, lo, tmC, col0 + c * 32, row0);
-    stage_and_store<16>(obuf, hi, tmC, col0 + 64 + c * 32, row0);
+    stage_and_store<16>(ring, lo, tmC, col0 + c * 32, row0);
+    stage_and_store<16>(ring, hi, tmC, col0 + 64 + c * 32, row0);
   }
 }
 
@@ -407,7 +480,7 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
 // and the matching 32 up rows, so accumulator chunks 2p and 2p+1 are gate and up of the same 32
 // output columns: act = silu(gate) * up (f32), stored bf16 at act column col0 / 2 + 32 p.
 template <int NCH>
-__device__ __forceinline__ void swiglu_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, uint8_t* obuf,
+__device__ __forceinline__ void swiglu_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, StageRing& ring,
                                             const CUtensorMap* tmC) {
   uint32_t g[32], u[32];
 #pragma unroll 1
@@ -424,25 +497,29 @@ __device__ __forceinline__ void swiglu_tile(const GemmArgs& a, uint32_t taddr, i
       const float a1 = g1 / (1.0f + expf(-g1)) * f32_of(u[j + 1]);
       w[j / 2] = pack2(a0, a1, XDNA_BF16);
     }
-    if (col0 / 2 + p * 32 < a.N / 2) stage_and_store<16>(obuf, w, tmC, col0 / 2 + p * 32, row0);
+    if (col0 / 2 + p * 32 < a.N / 2) stage_and_store<16>(ring, w, tmC, col0 / 2 + p * 32, row0);
   }
 }
 
 // --------------------------------------------------------------------------- the kernel
 // ODT: the output element type of the GEMM epilogues, fixed at compile time (XDNA_I32 for EPI_I32).
-template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT>
+template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB = kBKBytes, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                      const GemmArgs args) {
-  constexpr int STAGES = stages_for<BN>();
-  constexpr int A_BYTES = kBM * kBKBytes;
-  constexpr int B_BYTES = BN * kBKBytes;
-  constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
+  static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
+  static_assert(!PAIR || (LOAD == LOAD_GEMM && BN == 256 && KB == 128), "CTA pairs: GEMM operands, 256 x 256 tiles");
+  constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (tile columns) this CTA loads
+  constexpr int STAGES = stages_for<BROWS, KB>();
+  constexpr int A_BYTES = kBM * KB;
+  constexpr int B_BYTES = BROWS * KB;
+  constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (A_BYTES + B_BYTES);  // a pair's stage: both CTAs' bytes
   constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
-  constexpr uint32_t IDESC = BF16 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN);
-  constexpr int KSTEPS = kBKBytes / 32;  // one MMA consumes 32 bytes of K (32 int8 or 16 bf16)
-  constexpr int K_ELEMS = BF16 ? kBKBytes / 2 : kBKBytes;
+  constexpr int MMA_M = PAIR ? 2 * kBM : kBM;
+  constexpr uint32_t IDESC = BF16 ? idesc_bf16(MMA_M, BN) : idesc_i8(MMA_M, BN);
+  constexpr int KSTEPS = KB / 32;  // one MMA consumes 32 bytes of K (32 int8 or 16 bf16)
+  constexpr int K_ELEMS = BF16 ? KB / 2 : KB;
   constexpr int WCOLS = BN / 2;          // columns per epilogue warp
   constexpr int NCH = WCOLS / 32;        // 32-column chunks per epilogue warp
   static_assert(NCH >= 1 && NCH <= 4, "BN must be 64, 128 or 256");
@@ -462,6 +539,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
+  // CTA pairs: the even CTA (rank 0) issues the MMAs of a 256 x 256 tile whose rows 0..127 are its own
+  // and rows 128..255 the odd CTA's; each CTA loads its own A rows and half of the B rows.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int t_first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int t_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  auto tile_row0 = [&](int mb) { return PAIR ? (2 * mb + static_cast<int>(rank)) * kBM : mb * kBM; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -470,15 +554,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull + b, 1);
-      mbar_init(tempty + b, kEpiWarps);
+      mbar_init(tempty + b, PAIR ? 2 * kEpiWarps : kEpiWarps);  // a pair: both CTAs' epilogue warps
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -486,7 +575,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (TSTORE) tma_prefetch_desc(&tmC);
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA arrival
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total = args.m_tiles * args.n_tiles;
@@ -500,19 +592,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      for (int t = t_first; t < total && ok; t += t_step) {
         int mb, nb;
         tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
         for (int kb = 0; kb < args.num_kb; ++kb) {
-          if (!mbar_wait(empty + stage, phase ^ 1, abort_flag, args.err, 1)) {
+          if (!mbar_wait<PAIR>(empty + stage, phase ^ 1, abort_flag, args.err, 1)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full + stage, STAGE_TX);
-          if constexpr (LOAD == LOAD_GEMM) {
+          if constexpr (PAIR) {
+            // both CTAs' bytes complete on the even CTA's barrier, which only it arms
+            if (leader) mbar_arrive_expect_tx(full + stage, STAGE_TX);
+            const uint32_t fb = cluster_addr(full + stage, 0);
+            tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, kb * K_ELEMS, tile_row0(mb));
+            tma_load_2d_pair(smB + stage * B_BYTES, &tmB, fb, kb * K_ELEMS, nb * BN + static_cast<int>(rank) * BROWS);
+          } else if constexpr (LOAD == LOAD_GEMM) {
+            mbar_arrive_expect_tx(full + stage, STAGE_TX);
             tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, kb * K_ELEMS, mb * kBM);
             tma_load_2d(smB + stage * B_BYTES, &tmB, full + stage, kb * K_ELEMS, nb * BN);
           } else {
+            mbar_arrive_expect_tx(full + stage, STAGE_TX);
             const int tap = kb / args.cblocks;
             const int cb = kb - tap * args.cblocks;
             const int dy = tap / 3 - 1;
@@ -528,15 +627,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: the last load of every stage has landed before the CTA may exit (a no-op on the
-      // normal path, where the MMA warp consumed them all).
+      // normal path, where the MMA warp consumed them all). A pair's loads complete on the even CTA's
+      // barriers, so the even CTA drains for both.
       for (int s = 0; s < STAGES; ++s)
-        if (last_parity[s] >= 0) {
+        if (last_parity[s] >= 0 && leader) {
           volatile int never = 0;
           mbar_wait(full + s, static_cast<uint32_t>(last_parity[s]), &never, args.err, 2);
         }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       // ---------------------------------------------------------------- MMA issuer
       int stage = 0;
       uint32_t phase = 0;
@@ -544,27 +644,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t bphase = 0;
       bool issued = false;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        if (!mbar_wait(tempty + buf, bphase ^ 1, abort_flag, args.err, 3)) break;
+      for (int t = t_first; t < total && ok; t += t_step) {
+        if (!mbar_wait<PAIR>(tempty + buf, bphase ^ 1, abort_flag, args.err, 3)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
         for (int kb = 0; kb < args.num_kb; ++kb) {
-          if (!mbar_wait(full + stage, phase, abort_flag, args.err, 4)) {
+          if (!mbar_wait<PAIR>(full + stage, phase, abort_flag, args.err, 4)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t da = smem_desc_k_sw128(smem_u32(smA + stage * A_BYTES));
-          const uint64_t db = smem_desc_k_sw128(smem_u32(smB + stage * B_BYTES));
+          const uint64_t da = KB == 128 ? smem_desc_k_sw128(smem_u32(smA + stage * A_BYTES))
+                                        : smem_desc_k_sw64(smem_u32(smA + stage * A_BYTES));
+          const uint64_t db = KB == 128 ? smem_desc_k_sw128(smem_u32(smB + stage * B_BYTES))
+                                        : smem_desc_k_sw64(smem_u32(smB + stage * B_BYTES));
 #pragma unroll
           for (int k = 0; k < KSTEPS; ++k) {
             const uint32_t acc = (kb | k) != 0;
-            if constexpr (BF16)
+            if constexpr (PAIR && BF16)
+              umma_f16_pair(d, da + 2 * k, db + 2 * k, IDESC, acc);
+            else if constexpr (PAIR)
+              umma_i8_pair(d, da + 2 * k, db + 2 * k, IDESC, acc);
+            else if constexpr (BF16)
               umma_f16(d, da + 2 * k, db + 2 * k, IDESC, acc);
             else
               umma_i8(d, da + 2 * k, db + 2 * k, IDESC, acc);
           }
-          umma_commit(empty + stage);
+          if constexpr (PAIR)
+            umma_commit_pair(empty + stage, 0x3);  // frees the stage in both CTAs
+          else
+            umma_commit(empty + stage);
           issued = true;
           if (++stage == STAGES) {
             stage = 0;
@@ -572,7 +681,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        umma_commit(tfull + buf);
+        if constexpr (PAIR)
+          umma_commit_pair(tfull + buf, 0x3);
+        else
+          umma_commit(tfull + buf);
         if (++buf == 2) {
           buf = 0;
           bphase ^= 1;
@@ -580,7 +692,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: every MMA this thread issued has completed before TMEM is freed.
       if (issued) {
-        umma_commit(drain);
+        if constexpr (PAIR)
+          umma_commit_pair(drain, 0x1);
+        else
+          umma_commit(drain);
         volatile int never = 0;
         mbar_wait(drain, 0, &never, args.err, 5);
       }
@@ -591,49 +706,82 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;          // the TMEM lane quadrant this warp may read
     const int half = ew >> 2;        // which half of the tile's columns
     uint8_t* obuf = smOut + ew * kStageOutBytes;
+    StageRing ring{obuf, 0};
+    // hand an accumulator back to the MMA issuer (in a pair: the even CTA's, for both CTAs' warps)
+    auto release_accumulator = [](uint64_t* bar) {
+      if constexpr (PAIR)
+        mbar_arrive_remote(cluster_addr(bar, 0));
+      else
+        mbar_arrive(bar);
+    };
     const bool has_bias = args.bias != nullptr;
     int buf = 0;
     uint32_t bphase = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    // Per-row and per-column factors of a tile (and, for the conv, where its pixel sits). Loaded one
+    // tile ahead: right after this warp's accumulator for tile t is ready, the loads for the next
+    // tile are issued, and their latency passes while tile t is drained.
+    struct Factors {
+      float srow;
+      float fcol[NCH], bcol[NCH];
+      ConvPixel px;
+    };
+    auto load_factors = [&](int t) {
+      Factors f{};
       int mb, nb;
       tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
-      const int row0 = mb * kBM + q * 32;
-      const int row = row0 + lane;
+      const int row = tile_row0(mb) + q * 32 + lane;
       const int col0 = nb * BN + half * WCOLS;
-      // per-row and per-column factors, loaded before waiting for the accumulator
-      float srow = 0.f;
-      float fcol[NCH], bcol[NCH];
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         const int n = col0 + c * 32 + lane;
-        fcol[c] = 0.f;
-        bcol[c] = 0.f;
+        f.fcol[c] = 0.f;
+        f.bcol[c] = 0.f;
         if constexpr (EPI == EPI_DEQ || EPI == EPI_CONV_DEQ) {
           if (n < args.N) {
-            fcol[c] = __ldg(args.sw + n);
-            if (has_bias) bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
+            f.fcol[c] = __ldg(args.sw + n);
+            if (has_bias) f.bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
           }
         }
         if constexpr (EPI == EPI_F32ACC) {
-          if (n < args.N && has_bias) bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
+          if (n < args.N && has_bias) f.bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
         }
       }
-      if constexpr (EPI == EPI_DEQ) srow = row < args.M ? __ldg(args.sx + row) : 0.f;
+      if constexpr (EPI == EPI_DEQ) f.srow = row < args.M ? __ldg(args.sx + row) : 0.f;
+      if constexpr (LOAD == LOAD_CONV) f.px = conv_pixel<EPI>(args, row);
+      return f;
+    };
+    Factors fac{};
+    if (t_first < total) fac = load_factors(t_first);
+    for (int t = t_first; t < total; t += t_step) {
+      int mb, nb;
+      tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
+      const int row0 = tile_row0(mb) + q * 32;
+      const int row = row0 + lane;
+      const int col0 = nb * BN + half * WCOLS;
+      const float srow = fac.srow;
+      float fcol[NCH], bcol[NCH];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        fcol[c] = fac.fcol[c];
+        bcol[c] = fac.bcol[c];
+      }
+      const ConvPixel px = fac.px;
 
-      if (!mbar_wait(tfull + buf, bphase, abort_flag, args.err, 6)) break;
+      if (!mbar_wait<PAIR>(tfull + buf, bphase, abort_flag, args.err, 6)) break;
       tc_fence_after();
+      if (t + t_step < total) fac = load_factors(t + t_step);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + half * WCOLS);
       if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
         if (col0 < args.N) {  // warp-uniform
           if constexpr (EPI == EPI_QKV)
-            qkv_tile(args, taddr, row0, col0, obuf, &tmC, &tmD);
+            qkv_tile(args, taddr, row0, col0, ring, &tmC, &tmD);
           else
-            swiglu_tile<NCH>(args, taddr, row0, col0, obuf, &tmC);
+            swiglu_tile<NCH>(args, taddr, row0, col0, ring, &tmC);
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(tempty + buf);
+        if (lane == 0) release_accumulator(tempty + buf);
       } else {
       uint32_t r[2][32];
       __syncwarp();
@@ -648,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // every column of this tile is in registers: hand the accumulator back to the MMA warp
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(tempty + buf);
+          if (lane == 0) release_accumulator(tempty + buf);
         }
         const int n0 = col0 + c * 32;
         // warp-uniform: this chunk has columns in range (and, for GEMM outputs, rows in range)
@@ -657,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (EPI == EPI_I32 || EPI == EPI_DEQ) {
             if constexpr (TSTORE) {
               if constexpr (EPI == EPI_I32) {
-                stage_and_store<32>(obuf, rc, &tmC, n0, row0);
+                stage_and_store<32>(ring, rc, &tmC, n0, row0);
               } else {
                 float v[32];
                 dequant32(rc, srow, fcol[c], bcol[c], has_bias, v);
@@ -665,12 +813,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                   uint32_t w[32];
 #pragma unroll
                   for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
-                  stage_and_store<32>(obuf, w, &tmC, n0, row0);
+                  stage_and_store<32>(ring, w, &tmC, n0, row0);
                 } else {
                   uint32_t w[16];
 #pragma unroll
                   for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], ODT);
-                  stage_and_store<16>(obuf, w, &tmC, n0, row0);
+                  stage_and_store<16>(ring, w, &tmC, n0, row0);
                 }
               }
             } else {
@@ -691,12 +839,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t w[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
-                stage_and_store<32>(obuf, w, &tmC, n0, row0);
+                stage_and_store<32>(ring, w, &tmC, n0, row0);
               } else {
                 uint32_t w[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], ODT);
-                stage_and_store<16>(obuf, w, &tmC, n0, row0);
+                stage_and_store<16>(ring, w, &tmC, n0, row0);
               }
             } else {
               store_direct<EPI>(args, row, n0, rc, v);
@@ -723,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           } else {
-            conv_chunk<EPI>(args, row, n0, rc, fcol[c], bcol[c], obuf);
+            conv_chunk<EPI>(args, px, n0, rc, fcol[c], bcol[c], obuf);
           }
         }
         if (c + 1 < NCH) tmem_ld_wait();
@@ -741,11 +889,79 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
+  // A pair: the even CTA's MMAs read this CTA's shared memory and write its TMEM, and this CTA's
+  // warps arrive on the even CTA's barriers; neither may free or exit before both are done.
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
+}
+
+// ----------------------------------------------------------------------------- host launcher
+// Persistent grid: one CTA per SM, or (PAIR) as many 2-CTA clusters as can be resident at once, and
+// never more CTAs (pairs) than tiles. args.m_tiles counts 256-row tiles for pairs.
+// (static: its per-instantiation caches stay private to each translation unit and to this library)
+template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB, bool PAIR>
+static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                              const CUtensorMap& td, const GemmArgs& args, int sms, cudaStream_t stream) {
+  constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB>();
+  auto kern = umma_gemm_kernel<BN, LOAD, EPI, BF16, TSTORE, ODT, KB, PAIR>;
+  static bool configured[64] = {};  // per instantiation and device
+  static int max_pairs[64] = {};
+  int dev = 0;
+  XDNA_CUDA(cudaGetDevice(&dev));
+  const bool cached = dev >= 0 && dev < 64 && configured[dev];
+  int pairs_resident = sms / 2;
+  if (!cached) {
+    XDNA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if constexpr (PAIR) {
+      cudaLaunchConfig_t cfg{};
+      cudaLaunchAttribute attr{};
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      XDNA_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      pairs_resident = n > 0 ? n : 1;
+    }
+    if (dev >= 0 && dev < 64) {
+      max_pairs[dev] = pairs_resident;
+      configured[dev] = true;
+    }
+  } else {
+    pairs_resident = max_pairs[dev];
+  }
+  const int tiles = args.m_tiles * args.n_tiles;
+  if constexpr (PAIR) {
+    const int pairs = std::max(1, std::min(tiles, pairs_resident));
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    XDNA_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, td, args));
+  } else {
+    kern<<<std::max(1, std::min(tiles, sms)), kThreads, smem, stream>>>(ta, tb, tc, td, args);
+  }
+  return check_launch("umma_gemm_kernel");
 }
 
 }  // namespace xdna

@@ -158,7 +158,9 @@ _verified = set()
 
 
 def _bn_for(rows, n):
-    """The tile width libxdna_b200 picks (mirrors choose_bn in csrc/gemm_i8.cu), for verify keys."""
+    """The kernel configuration libxdna_b200 picks for a GEMM (mirrors choose_bn and use_pairs in
+    csrc/gemm_i8.cu / csrc/umma_gemm.cuh), for verify keys: the tile width, and "pair" when 256 x 256
+    tiles run on CTA pairs."""
     m_tiles = -(-rows // 128)
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     if n <= 64:
@@ -166,7 +168,7 @@ def _bn_for(rows, n):
     if n <= 128:
         return 128
     if m_tiles * -(-n // 256) >= sms:
-        return 256
+        return "256 pair" if -(-m_tiles // 2) * -(-n // 256) >= sms // 2 else 256
     if m_tiles * -(-n // 128) >= sms:
         return 128
     return 64 if n >= 1024 else 128
@@ -228,7 +230,43 @@ def _w8a8(cfg, x2d, qw, bias, out_dtype):
 
 
 def _bf16(cfg, x2d, qw, bias, out_dtype):
-    raise kernels.XdnaUnavailable("precision='bf16' linears are not built yet in this version of torch_xdna")
+    """y [R, N] = x @ W^T (+ bias) with bf16 operands and f32 accumulation on the bf16 tensor cores: one
+    gemm_bf16 whose epilogue adds the bias in f32 and rounds once to out_dtype. The reference runs the
+    same product on the NPU (bfp16 MACs) and adds bias.float() on the host (R:torch_xdna/runtime.py:218-237,
+    :299-313, :340-345)."""
+    R, K = x2d.shape
+    w = qw.bf16()                                       # [N, K8] bf16, K zero-padded to 8
+    K8 = w.shape[1]
+    if (x2d.dtype == torch.bfloat16 and K == K8 and x2d.stride(1) == 1 and x2d.stride(0) % 8 == 0
+            and x2d.data_ptr() % 16 == 0):
+        a = x2d
+    else:                                               # TMA wants 16-byte rows: stage a padded bf16 copy
+        a = torch.zeros((R, K8), dtype=torch.bfloat16, device=x2d.device)
+        a[:, :K].copy_(x2d)
+    per16 = 16 // torch.empty((), dtype=out_dtype).element_size()
+    Np = kernels.round_up(qw.N, per16)
+    y = torch.empty((R, Np), dtype=out_dtype, device=x2d.device)
+    kernels.gemm_bf16(a, w, kernels.GEMM_F32ACC, out=y, bias=bias)
+    if Np != qw.N:
+        y = y[:, :qw.N].contiguous()
+    key = ("bf16", qw.N, qw.K, str(out_dtype), bias is not None, R % 128 != 0)
+    if _want_check(cfg, key):
+        _check_bf16(key, a, w, bias, y)
+    return y
+
+
+def _check_bf16(key, a, w, bias, y):
+    """The launch vs the f32 product of the same bf16 operands, with the reference's tolerance for its
+    bf16 route (norm-relative error below 5e-2, all finite; R:torch_xdna/runtime.py:174-188)."""
+    want = a.float().cpu() @ w.float().cpu().t()
+    if bias is not None:
+        want = want + bias.float().cpu()
+    got = y.float().cpu()
+    err = float((got - want).norm() / want.norm().clamp(min=1e-30))
+    if not bool(torch.isfinite(got).all()) or err >= 5e-2:
+        raise XdnaResultMismatch(f"gemm_bf16 {key} disagrees with the f32 product: rel err {err:.3g}")
+    _verified.add(key)
+    stats.checks.append((f"gemm_bf16 {key}", f"rel err {err:.2e} vs the f32 product of the bf16 operands"))
 
 
 def linear(cfg, x, weight, bias, transposed):
