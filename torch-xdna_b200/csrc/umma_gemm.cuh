@@ -192,14 +192,47 @@ __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float srow, f
 struct StageRing {
   uint8_t* base;
   int slot;
+  int nslots;  // 2, or 1 where the second 2 KB holds the warp's column factors (EPI_DEQ)
   __device__ __forceinline__ uint8_t* acquire() {
-    if (lane_id() == 0) bulk_wait_read_one();
+    if (lane_id() == 0) {
+      if (nslots == 2)
+        bulk_wait_read_one();
+      else
+        bulk_wait_read_all();
+    }
     __syncwarp();
     uint8_t* b = base + slot * kStageSlotBytes;
-    slot ^= 1;
+    if (nslots == 2) slot ^= 1;
     return b;
   }
 };
+
+// The same with the column factors in this warp's shared memory (sw, and bias as f32, for the 32
+// columns of the chunk; every lane reads the same 16 bytes, a broadcast) and packed f32x2 products:
+// per value one conversion, one packed multiply by sx and one by sw, each rounded as __fmul_rn, then
+// the bias added as __fadd_rn. Cheaper than 32 shuffles per chunk.
+__device__ __forceinline__ void dequant32_smem(const uint32_t (&r)[32], float srow, const float* sw, const float* bias,
+                                               bool has_bias, float (&v)[32]) {
+  const float4* sw4 = reinterpret_cast<const float4*>(sw);
+  const float2 sx2 = make_float2(srow, srow);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 f = sw4[q];
+    float2 a0 = make_float2(__int2float_rn(static_cast<int>(r[4 * q])), __int2float_rn(static_cast<int>(r[4 * q + 1])));
+    float2 a1 = make_float2(__int2float_rn(static_cast<int>(r[4 * q + 2])), __int2float_rn(static_cast<int>(r[4 * q + 3])));
+    a0 = __fmul2_rn(__fmul2_rn(a0, sx2), make_float2(f.x, f.y));
+    a1 = __fmul2_rn(__fmul2_rn(a1, sx2), make_float2(f.z, f.w));
+    if (has_bias) {  // warp-uniform
+      const float4 b = reinterpret_cast<const float4*>(bias)[q];
+      a0 = __fadd2_rn(a0, make_float2(b.x, b.y));
+      a1 = __fadd2_rn(a1, make_float2(b.z, b.w));
+    }
+    v[4 * q] = a0.x;
+    v[4 * q + 1] = a0.y;
+    v[4 * q + 2] = a1.x;
+    v[4 * q + 3] = a1.y;
+  }
+}
 
 // Writes this warp's 32 rows x 32 columns through 64-byte-swizzled staging and TMA stores. `words`
 // holds this lane's row: 16 words (2-byte outputs: one 32-column block) or 32 words (4-byte outputs:
@@ -706,7 +739,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;          // the TMEM lane quadrant this warp may read
     const int half = ew >> 2;        // which half of the tile's columns
     uint8_t* obuf = smOut + ew * kStageOutBytes;
-    StageRing ring{obuf, 0};
+    // EPI_DEQ through TMA: one staging slot, and the second 2 KB holds the tile's column factors
+    constexpr bool kSmemFactors = EPI == EPI_DEQ && TSTORE;
+    StageRing ring{obuf, 0, kSmemFactors ? 1 : 2};
+    float* col_sw = reinterpret_cast<float*>(obuf + kStageSlotBytes);  // [WCOLS]
+    float* col_bias = col_sw + WCOLS;                                    // [WCOLS]
+    static_assert(!kSmemFactors || 2 * WCOLS * 4 <= kStageOutBytes - kStageSlotBytes, "factor area");
     // hand an accumulator back to the MMA issuer (in a pair: the even CTA's, for both CTAs' warps)
     auto release_accumulator = [](uint64_t* bar) {
       if constexpr (PAIR)
@@ -766,6 +804,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         bcol[c] = fac.bcol[c];
       }
       const ConvPixel px = fac.px;
+      if constexpr (kSmemFactors) {
+        __syncwarp();  // this warp is done reading the previous tile's factors
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          col_sw[c * 32 + lane] = fcol[c];
+          col_bias[c * 32 + lane] = bcol[c];
+        }
+        __syncwarp();
+      }
 
       if (!mbar_wait<PAIR>(tfull + buf, bphase, abort_flag, args.err, 6)) break;
       tc_fence_after();
@@ -808,7 +855,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 stage_and_store<32>(ring, rc, &tmC, n0, row0);
               } else {
                 float v[32];
-                dequant32(rc, srow, fcol[c], bcol[c], has_bias, v);
+                if constexpr (kSmemFactors)
+                  dequant32_smem(rc, srow, col_sw + c * 32, col_bias + c * 32, has_bias, v);
+                else
+                  dequant32(rc, srow, fcol[c], bcol[c], has_bias, v);
                 if constexpr (ODT == XDNA_F32) {
                   uint32_t w[32];
 #pragma unroll
