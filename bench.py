@@ -609,7 +609,7 @@ def run_conv(args, rank, world):
     """One step = the 13 int8 conv3x3 layers of VGG16 (bias + ReLU, 2x2 max-pool between blocks) on this
     rank's share of a batch of 32 images 3x224x224 (batch sharded over ranks, strong scaling). Each conv is
     xdna::conv3x3_fused: per-image quantise into the bordered NHWC layout, then the implicit-GEMM conv with
-    the dequantise and bias in its epilogue; the ReLU and pool are torch ops. The requantise shift of every
+    the dequantise, bias and ReLU in its epilogue; the pool is a torch op. The requantise shift of every
     layer comes from global image 0 (rank 0), broadcast to the other ranks."""
     import torch_xdna
     from torch_xdna import kernels, parallel
@@ -636,7 +636,7 @@ def run_conv(args, rank, world):
             if p == "M":
                 h = torch.nn.functional.max_pool2d(h, 2)
             else:
-                h = torch.relu(torch.ops.xdna.conv3x3_fused(h, p[0], p[1], False, cid))
+                h = torch.ops.xdna.conv3x3_fused(h, p[0], p[1], False, cid, True)  # ReLU after the bias
         return h
 
     stream = torch.cuda.current_stream()
@@ -783,12 +783,17 @@ def run_kernel(args):
         out = torch.empty(B * L, 2048, dtype=torch.bfloat16, device=dev)
         fn = lambda: kernels.attention(qk, vt, out, B, L, kernels.MASK_CAUSAL)  # noqa
         work, unit = B * 2 * 2 * 16 * 128 * (L * (L + 1) // 2), "TFLOP/s"
-    elif args.kernel == "gemm_bf16":                  # M, N, K: bf16 out (the head's epilogue)
-        M, N, K = shp
+    elif args.kernel == "gemm_bf16":                  # M, N, K[, 1]: bf16 out (the head's epilogue); 1: residual add
+        M, N, K = shp[:3]
         a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
         b = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-        fn, work, unit = (lambda: kernels.gemm_bf16(a, b, kernels.GEMM_F32ACC, out=y)), 2 * M * N * K, "TFLOP/s"
+        if len(shp) > 3 and shp[3] == 1:
+            resid = torch.zeros(M, N, device=dev)
+            fn = lambda: kernels.gemm_bf16(a, b, kernels.GEMM_RESID, resid=resid)  # noqa
+        else:
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            fn = lambda: kernels.gemm_bf16(a, b, kernels.GEMM_F32ACC, out=y)  # noqa
+        work, unit = 2 * M * N * K, "TFLOP/s"
     else:
         raise SystemExit(f"unknown kernel {args.kernel}")
     for _ in range(5):

@@ -46,6 +46,10 @@ extern "C" {
 #define XDNA_CONV_DEQUANT 1   /* y = float(q) * (scale[co] * sx[n]) (+ bias[co]) in out_dtype, channels-last
                                  memory [N, H, W, Co] (torch's channels_last layout of an [N, Co, H, W] tensor) */
 #define XDNA_CONV_CALIBRATE 2 /* *acc_max = max over the sums of image 0 of (relu ? max(acc,0) : |acc|) */
+/* `relu` of xdna_conv3x3_i8: 0 none; 1 fused into the requantise ([0,255] uint8, the reference's ReLU of
+ * a bias-free conv); XDNA_RELU_AFTER_BIAS (DEQUANT only) applied to the dequantised output after the
+ * bias, the requantise saturating to int8 — the same values as torch.relu on the DEQUANT output. */
+#define XDNA_RELU_AFTER_BIAS 2
 
 /* Last error of this thread, as text. */
 const char* xdna_last_error(void);

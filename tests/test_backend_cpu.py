@@ -117,14 +117,18 @@ def test_shared_input_fusion():
 
 
 def test_conv_pass_which_convs_and_relu():
-    """3 of 4 convs rewritten; only the bias-free conv's ReLU fused; stride 2 left alone
-    (R:tests/test_backend.py:220-240)."""
+    """3 of 4 convs rewritten, stride 2 left alone (R:tests/test_backend.py:220-240); the bias-free conv's
+    ReLU fused into the requantise as in the reference, the biased conv's ReLU after its bias."""
     (gm,) = capture_graphs(CNN().eval(), torch.randn(1, 64, 16, 64), torch_xdna.Config(policy="npu"))
     nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
     convs = [n for n in nodes if n.target is conv3x3_int8]
     assert [n.args[3] for n in convs] == [False, True, False], [n.args for n in convs]
-    assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes) == 1
+    assert [n.args[5] for n in convs] == [True, False, False], [n.args for n in convs]
+    assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes) == 0
     assert sum(n.target is torch.conv2d for n in nodes) == 1
+    (gm2,) = capture_graphs(CNN().eval(), torch.randn(1, 64, 16, 64), torch_xdna.Config(policy="npu", fuse=False))
+    nodes2 = [n for n in gm2.graph.nodes if n.op == "call_function"]
+    assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes2) == 2
 
 
 def test_policy_cpu_rewrites_nothing_and_runs():

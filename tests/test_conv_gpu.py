@@ -68,14 +68,17 @@ def test_conv_q_bitexact_vs_oracle(cuda, relu, n, ci, co, h, w):
     assert np.array_equal(scale.cpu().numpy(), want["scale"])
 
 
+@pytest.mark.parametrize("post_relu", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_conv_fused_dequant_bitexact(cuda, dtype):
+def test_conv_fused_dequant_bitexact(cuda, dtype, post_relu):
+    """The dequantise (+ bias) to x.dtype, bit for bit; post_relu equals torch.relu of it."""
     x, wt, b = mg.conv_inputs(5, 2, 96, 80, 30, 50, bias=True)
     xd = orc.cast(x, "bfloat16") if dtype == torch.bfloat16 else x
     want = orc.conv3x3_int8(xd, wt, b, relu=False, x_dtype="bfloat16" if dtype == torch.bfloat16 else "float32")
     weight = torch.nn.Parameter(t(wt, cuda))
-    y = torch.ops.xdna.conv3x3_fused(t(xd, cuda, dtype), weight, t(b, cuda), False, _cid(verify="off"))
-    assert np.array_equal(y.float().cpu().numpy(), want["y"])
+    y = torch.ops.xdna.conv3x3_fused(t(xd, cuda, dtype), weight, t(b, cuda), False, _cid(verify="off"), post_relu)
+    w = np.maximum(want["y"], 0) if post_relu else want["y"]
+    assert np.array_equal(y.float().cpu().numpy(), w)
 
 
 def test_cfg3_chain_matches_reference(cuda, golden):

@@ -154,6 +154,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   XDNA_CHECK_ARG(Cp >= Ci && Cp % 16 == 0, "conv3x3: Cp must be >= Ci and a multiple of 16");
   XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE,
                  "conv3x3: unknown mode %d", mode);
+  XDNA_CHECK_ARG(relu == 0 || relu == 1 || (relu == XDNA_RELU_AFTER_BIAS && mode == XDNA_CONV_DEQUANT),
+                 "conv3x3: relu %d (0, 1, or XDNA_RELU_AFTER_BIAS with XDNA_CONV_DEQUANT)", relu);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (mode == XDNA_CONV_CALIBRATE) {
     XDNA_CHECK_ARG(acc_max != nullptr, "conv3x3: calibration needs acc_max");
@@ -200,7 +202,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   a.bias = bias;
   a.bias_dtype = bias_dtype;
   a.shift = shift;
-  a.relu = relu ? 1 : 0;
+  a.relu = relu == 1 ? 1 : 0;
+  a.post_relu = relu == XDNA_RELU_AFTER_BIAS ? 1 : 0;
   a.acc_max = acc_max;
   a.err = device_error_word();
 

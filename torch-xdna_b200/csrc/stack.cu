@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(256) embed_kernel(const int64_t* __restrict__ 
 template <int BN, int EPI, int ODT>
 static int launch_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
                        int sms, bool pair, cudaStream_t stream, const CUtensorMap* td = nullptr) {
-  constexpr bool TSTORE = (EPI == EPI_F32ACC || EPI == EPI_QKV || EPI == EPI_SWIGLU);
+  constexpr bool TSTORE = (EPI == EPI_F32ACC || EPI == EPI_QKV || EPI == EPI_SWIGLU || EPI == EPI_RESID);
   if constexpr (BN == 256) {
     if (pair)
       return launch_gemm_kernel<BN, LOAD_GEMM, EPI, true, TSTORE, ODT, kBKBytes, true>(ta, tb, tc, td ? *td : ta, a, sms,
@@ -195,7 +195,7 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
     }
     case XDNA_GEMM_RESID:
       XDNA_CHECK_ARG(g.resid && g.ldr >= g.N && g.ldr % 4 == 0 && aligned16(g.resid), "gemm_bf16: bad residual");
-      tc = ta;
+      if ((rc = out_map(&tc, g.resid, g.M, g.N, g.ldr, XDNA_F32, "gemm_bf16 residual")) != XDNA_OK) return rc;
       return bn == 256 ? launch_bf16<256, EPI_RESID, XDNA_F32>(ta, tb, tc, a, sms, pair, s)
                        : launch_bf16<128, EPI_RESID, XDNA_F32>(ta, tb, tc, a, sms, pair, s);
     case XDNA_GEMM_SWIGLU:

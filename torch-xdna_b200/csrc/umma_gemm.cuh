@@ -37,7 +37,8 @@ enum EpiMode {
   EPI_CONV_CALIB = 4,  // max of the sums (of image 0) into one int32
   // bf16 GEMMs of the Qwen3 stack (f32 accumulators)
   EPI_F32ACC = 5,      // acc (+ bias[n]) -> f32 / bf16 / f16 (the head; precision="bf16" linears)
-  EPI_RESID = 6,       // resid_f32[m, n] += acc (o-proj and down-proj into the residual stream)
+  EPI_RESID = 6,       // resid_f32[m, n] += acc (o-proj and down-proj into the residual stream; with TSTORE
+                       // a TMA reduce-add over tmC, which then maps the residual)
   EPI_SWIGLU = 7,      // columns come as 32 gate / 32 up pairs: act = silu(gate) * up -> bf16
   EPI_QKV = 8,         // q / k heads: RMSNorm over the head + weight + RoPE -> bf16; v heads -> bf16 V^T
 };
@@ -82,7 +83,8 @@ struct GemmArgs {
   const float* sw;     // per-column weight scale (GEMM) / requantise scale (conv)
   const void* bias;
   int bias_dtype;
-  int shift, relu;
+  int shift, relu;     // relu: ReLU in the requantise (uint8 saturation)
+  int post_relu;       // EPI_CONV_DEQ: max(y, 0) after the bias
   int* acc_max;
   int* err;
   // stack epilogues
@@ -237,7 +239,8 @@ __device__ __forceinline__ void dequant32_smem(const uint32_t (&r)[32], float sr
 // Writes this warp's 32 rows x 32 columns through 64-byte-swizzled staging and TMA stores. `words`
 // holds this lane's row: 16 words (2-byte outputs: one 32-column block) or 32 words (4-byte outputs:
 // two 16-column blocks). Every block is 32 rows x 64 bytes; the tensor map's box matches.
-template <int NWORDS>
+// REDUCE: the block is added to the destination (TMA reduce-add, f32) instead of stored.
+template <int NWORDS, bool REDUCE = false>
 __device__ __forceinline__ void stage_and_store(StageRing& ring, const uint32_t (&words)[NWORDS],
                                                 const CUtensorMap* tmC, int x, int y) {
   static_assert(NWORDS == 16 || NWORDS == 32, "2-byte or 4-byte outputs");
@@ -255,7 +258,10 @@ __device__ __forceinline__ void stage_and_store(StageRing& ring, const uint32_t 
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(tmC, buf, x + h * 16, y);
+      if constexpr (REDUCE)
+        tma_reduce_add_2d(tmC, buf, x + h * 16, y);
+      else
+        tma_store_2d(tmC, buf, x + h * 16, y);
       bulk_commit();
     }
   }
@@ -354,6 +360,10 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     if (a.bias != nullptr) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __shfl_sync(kFull, bias_lane, j));
+    }
+    if (a.post_relu) {  // after the bias; rounding to the output dtype keeps the order (monotone, 0 -> 0)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = v[j] > 0.f ? v[j] : 0.f;
     }
     // out[img, yp-1, xp-1, co]: the 32 channels of this pixel are contiguous
     const int64_t base = ((static_cast<int64_t>(img) * a.H + (yp - 1)) * a.W + (xp - 1)) * a.N + n0;
@@ -899,6 +909,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               store_direct<EPI>(args, row, n0, rc, v);
             }
+          } else if constexpr (EPI == EPI_RESID && TSTORE) {
+            // resid[rows, n0..n0+31] += acc by a TMA reduce-add of the staged block (one f32 add per
+            // element, in L2; rows and columns past the residual's extent are clipped)
+            stage_and_store<32, true>(ring, rc, &tmC, n0, row0);
           } else if constexpr (EPI == EPI_RESID) {
             // resid[row, n0..n0+31] += acc: 128 contiguous bytes per thread
             if (row < args.M) {

@@ -135,7 +135,8 @@ def _is_relu(n):
 
 def _offload_convs(gm, params, cid, attr, cfg):
     """3x3 / stride-1 / padding-1 / groups-1 convs of a parameter weight -> conv3x3_int8
-    (R:torch_xdna/backend.py:130-174). The sole-user ReLU of a bias-free conv is fused."""
+    (R:torch_xdna/backend.py:130-174). A sole-user ReLU is fused: into the requantise for a bias-free conv
+    (as the reference does), into the epilogue after the bias for a biased one."""
     from .conv import conv3x3_int8, supported
 
     if not cfg.offload:
@@ -158,10 +159,13 @@ def _offload_convs(gm, params, cid, attr, cfg):
         if not supported(int(wt.shape[1]), int(wt.shape[0]), int(xt.shape[2]), int(xt.shape[3])):
             continue
         users = list(node.users)
-        relu = users[0] if (cfg.fuse and b is None and len(users) == 1 and _is_relu(users[0])) else None
+        relu = users[0] if (cfg.fuse and len(users) == 1 and _is_relu(users[0])) else None
         last = relu or node
         with gm.graph.inserting_after(last):
-            new = gm.graph.call_function(conv3x3_int8, (x, w, b, relu is not None, cid))
+            # bias-free: the ReLU goes into the requantise (the reference's fusion); biased: it is applied
+            # in the epilogue after the bias (the reference leaves it in the graph; the values are the same)
+            args = (x, w, b, relu is not None and b is None, cid, relu is not None and b is not None)
+            new = gm.graph.call_function(conv3x3_int8, args)
         new.meta.update(last.meta)
         last.replace_all_uses_with(new)
         if relu is not None:

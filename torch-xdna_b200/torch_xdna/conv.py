@@ -39,10 +39,12 @@ def supported(ci, co, h, w):
     return 1 <= ci <= 512 and co >= 1 and h >= 1 and w >= 1
 
 
-def conv3x3_int8(x, weight, bias, relu: bool, cfg_id: int):
+def conv3x3_int8(x, weight, bias, relu: bool, cfg_id: int, post_relu: bool = False):
     """relu?(conv2d(x, weight, bias, padding=1)) through int8: what the backend puts in the graph
-    (R:torch_xdna/conv.py:43-51). One custom op: quantise, conv and dequantise run as B200 kernels."""
-    return torch.ops.xdna.conv3x3_fused(x, weight, bias, relu, cfg_id)
+    (R:torch_xdna/conv.py:43-51). One custom op: quantise, conv and dequantise run as B200 kernels.
+    post_relu: torch.relu of the result, applied in the epilogue after the bias (for biased convs, whose
+    ReLU the reference leaves in the graph; same values)."""
+    return torch.ops.xdna.conv3x3_fused(x, weight, bias, relu, cfg_id, post_relu)
 
 
 def channels_padded(c):
@@ -92,13 +94,14 @@ class ConvLayer:
         stats.launches += 1
         return out
 
-    def dequant(self, xp, n, sx, bias, dtype):
+    def dequant(self, xp, n, sx, bias, dtype, post_relu=False):
         # channels-last: the epilogue writes each pixel's channels contiguously (same values and shape as
         # the reference's NCHW tensor; torch ops downstream keep the layout)
         out = torch.empty((n, self.co, self.h, self.w), dtype=dtype, device=xp.device,
                           memory_format=torch.channels_last)
+        relu = kernels.RELU_AFTER_BIAS if post_relu else self.relu
         kernels.conv3x3(xp, self.wp, n, self.ci, self.co, self.h, self.w, kernels.CONV_DEQUANT, shift=self.shift,
-                        relu=self.relu, scale=self.scale, sx=sx, bias=bias, out=out)
+                        relu=relu, scale=self.scale, sx=sx, bias=bias, out=out)
         stats.launches += 1
         return out
 
@@ -166,9 +169,11 @@ def conv3x3(cfg, xq, weight, relu):
     return q, layer.scale.clone()
 
 
-def conv3x3_fused(cfg, x, weight, bias, relu):
+def conv3x3_fused(cfg, x, weight, bias, relu, post_relu=False):
     """conv3x3_int8 in three kernels: per-image max, quantise into the bordered NHWC layout, and the
-    conv whose epilogue requantises and dequantises (q * (scale * sx) + bias) straight to x.dtype."""
+    conv whose epilogue requantises and dequantises (q * (scale * sx) + bias, then max(., 0) when
+    post_relu) straight to x.dtype."""
+    assert not (relu and post_relu), "relu fuses into the requantise, post_relu after the bias: one of them"
     kernels._cuda(x, weight, bias)
     n, ci, h, w = x.shape
     co = weight.shape[0]
@@ -194,7 +199,7 @@ def conv3x3_fused(cfg, x, weight, bias, relu):
             return torch.round(xf / s).clamp(-127, 127).to(torch.int8)
 
         _verify(cfg, layer, xp, xq_cpu)
-        y = layer.dequant(xp, n, sx, bias, x.dtype)
+        y = layer.dequant(xp, n, sx, bias, x.dtype, post_relu)
     stats.calls[DEVICE] += 1
     stats.seconds[DEVICE] += time.perf_counter() - t0
     stats.macs[DEVICE] += n * co * ci * h * w * 9

@@ -215,13 +215,16 @@ def conv_pack_weight(wq, wp):
     _check("xdna_conv_pack_weight", L.xdna_conv_pack_weight(_p(wq), Co, Ci, _p(wp), wp.shape[-1], _stream()))
 
 
+RELU_AFTER_BIAS = 2  # conv3x3 relu mode: max(y, 0) after the dequantise and the bias (XDNA_RELU_AFTER_BIAS)
+
+
 def conv3x3(xp, wp, N, Ci, Co, H, W, mode, shift=1, relu=False, scale=None, sx=None, bias=None, out=None,
             acc_max=None):
     L = require()
     _cuda(xp, wp, scale, sx, bias, out, acc_max)
     Cp = wp.shape[-1]
     _check("xdna_conv3x3_i8", L.xdna_conv3x3_i8(
-        _p(xp), _p(wp), N, Ci, Cp, Co, H, W, mode, shift, int(bool(relu)), _p(scale), _p(sx), _p(bias),
+        _p(xp), _p(wp), N, Ci, Cp, Co, H, W, mode, shift, int(relu), _p(scale), _p(sx), _p(bias),
         DTYPE_CODES[bias.dtype] if bias is not None else F32, _p(out),
         DTYPE_CODES[out.dtype] if out is not None else I8, _p(acc_max), _stream()))
 

@@ -78,13 +78,14 @@ def _(xq, weight, relu, cfg_id):
 
 @torch.library.custom_op("xdna::conv3x3_fused", mutates_args=())
 def conv3x3_fused(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], relu: bool,
-                  cfg_id: int) -> torch.Tensor:
-    """relu?(conv2d(x, weight, bias, padding=1)) through int8, as conv3x3_int8 defines it."""
-    return conv.conv3x3_fused(_configs[cfg_id], x, weight, bias, relu)
+                  cfg_id: int, post_relu: bool = False) -> torch.Tensor:
+    """relu?(conv2d(x, weight, bias, padding=1)) through int8, as conv3x3_int8 defines it; post_relu:
+    torch.relu of that result, applied in the epilogue after the bias."""
+    return conv.conv3x3_fused(_configs[cfg_id], x, weight, bias, relu, post_relu)
 
 
 @conv3x3_fused.register_fake
-def _(x, weight, bias, relu, cfg_id):
+def _(x, weight, bias, relu, cfg_id, post_relu=False):
     # the kernel writes channels-last memory (see conv.ConvLayer.dequant)
     return torch.empty((x.shape[0], weight.shape[0], x.shape[2], x.shape[3]), dtype=x.dtype, device=x.device,
                        memory_format=torch.channels_last)
