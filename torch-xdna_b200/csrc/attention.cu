@@ -1,18 +1,22 @@
 // GQA flash attention for the Qwen3 stack on tcgen05 (sm_100a): softmax(Q K^T / sqrt(128) + mask) V
 // for 16 query heads sharing 8 key/value heads of dimension 128 (R:torch_xdna/stack.py:43-57).
 //
-// One CTA = 128 queries of one query head of one sequence; 192 threads:
-//   warp 0      TMA: the Q tile once, then K and V^T blocks of 128 keys into a 2-stage ring
-//               (Q and K read from the q/k projection output [T, 3072] bf16, V^T from [1024, T'] bf16,
-//               which the projection epilogue wrote transposed so that P.V has a K-major B operand);
-//   warp 1      TMEM (two S buffers of 128 columns, one O accumulator of 128) and the MMAs:
-//               S_j = Q K_j^T (8 x tcgen05.mma 128x128x16) and O += P_j V_j (8 more), issued as
-//               S_0, S_1, O_0, S_2, O_1, ... so each S overlaps the previous block's softmax;
-//   warps 2..5  softmax: thread i owns query row i. Pass 1 over S_j in TMEM finds the row max; pass 2
-//               writes p = 2^(s * scale * log2 e - m) as bf16 into a 128-byte-swizzled K-major P tile
-//               and sums it. O stays in TMEM and the MMA accumulates into it; the running max m is only
-//               raised (and O, l rescaled in place) when a block's max exceeds it by more than 2^8, so
-//               p <= 256 and most blocks touch O not at all. The output row is O / l in bf16 [T, 2048].
+// One CTA = 128 queries of the two query heads that share one key/value head (2g and 2g+1), so each
+// K and V^T block is loaded once for both; 320 threads:
+//   warp 0      TMA: both heads' Q tiles once, then K blocks of 128 keys into a 2-stage ring and V^T
+//               blocks into a 1-stage slot (Q and K read from the q/k projection output [T, 3072] bf16,
+//               V^T from [1024, T'] bf16, which the projection epilogue wrote transposed so that P.V
+//               has a K-major B operand);
+//   warp 1      TMEM (per head: S, 128 columns; O, 128 columns) and the MMAs, issued as
+//               S_A(j), S_B(j), O_A += P_A(j-1) V(j-1), O_B += P_B(j-1) V(j-1), ... so that while one
+//               head's softmax works on block j the tensor core computes the other head's S and the
+//               previous block's P.V;
+//   warps 2..5  softmax of head A, warps 6..9 of head B: thread i of a group owns query row i. S_j is
+//               loaded from TMEM once into registers; p = 2^(s * scale * log2 e - m) is written as bf16
+//               into the head's 128-byte-swizzled K-major P tile and summed. O stays in TMEM and the
+//               MMA accumulates into it; the running max m is only raised (and O, l rescaled in place)
+//               when a block's max exceeds it by more than 2^8, so p <= 256 and most blocks touch O not
+//               at all. The output row is O / l in bf16 [T, 2048].
 // Masks: causal, per-sequence prefix blocks (the reference's OmniVoice layout: the first n positions
 // see each other, later ones only themselves), a general bool mask [B, 1|H, L, L], or none; blocks that
 // no mask entry can touch (for causal: every block left of the diagonal) skip the masking entirely.
@@ -31,7 +35,6 @@ struct AttnArgs {
   int T, L;               // tokens in all, tokens per sequence
   int L8;                 // round_up(L, 8): V^T column pitch of a sequence
   int q_blocks;           // ceil(L / 128)
-  int heads_per_kv;       // 2
   float scale_log2;       // log2(e) / sqrt(128)
   const int32_t* lens;    // MASK_PREFIX: per-sequence length
   const uint8_t* mask;    // MASK_BOOL: [B, Hm, L, L]
@@ -39,10 +42,11 @@ struct AttnArgs {
   int* err;
 };
 
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 320;
 constexpr int kTileBytes = 128 * 128;  // one 128-row x 128-byte operand k-block
-constexpr int kKvStages = 2;
-constexpr int kAttnSmem = (2 /*Q*/ + 2 * kKvStages /*K*/ + 2 * kKvStages /*V*/ + 4 /*P x 2*/) * kTileBytes + 1024 + 256;
+constexpr int kKStages = 2;
+constexpr int kAttnSmem = (2 * 2 /*Q, 2 heads*/ + 2 * kKStages /*K*/ + 2 /*V*/ + 2 * 2 /*P, 2 heads*/) * kTileBytes +
+                          1024 + 256;
 constexpr float kRescaleLog2 = 8.0f;   // lazy rescale threshold: p stays <= 2^8
 
 __device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
@@ -71,21 +75,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmVt,
                      const AttnArgs args) {
   constexpr uint32_t IDESC = idesc_bf16(128, 128);
-  constexpr uint32_t TX = 2 * kTileBytes;  // one Q tile, or one K block, or one V^T block
+  constexpr uint32_t TX = 2 * kTileBytes;  // one head's Q tile, or one K block, or one V^T block
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smQ = smem;
-  uint8_t* smK = smQ + 2 * kTileBytes;
-  uint8_t* smV = smK + 2 * kKvStages * kTileBytes;
-  uint8_t* smP = smV + 2 * kKvStages * kTileBytes;
+  uint8_t* smQ = smem;                              // [head][k-block]
+  uint8_t* smK = smQ + 4 * kTileBytes;              // [stage][k-block]
+  uint8_t* smV = smK + 2 * kKStages * kTileBytes;   // [k-block]
+  uint8_t* smP = smV + 2 * kTileBytes;              // [head][k-block]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smP + 4 * kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;                 // [kKvStages]
-  uint64_t* kv_empty = kv_full + kKvStages;     // [kKvStages]
-  uint64_t* s_full = kv_empty + kKvStages;      // [2]
-  uint64_t* s_empty = s_full + 2;               // [2]
-  uint64_t* p_full = s_empty + 2;               // [2] P_j written (buffer j & 1) and O rescaled: O += P_j V_j may run
-  uint64_t* p_empty = p_full + 2;               // [2] O += P_j V_j done: buffer j & 1 may be rewritten, O read
+  uint64_t* k_full = bars + 1;               // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;     // [kKStages]
+  uint64_t* v_full = k_empty + kKStages;
+  uint64_t* v_empty = v_full + 1;
+  uint64_t* s_full = v_empty + 1;            // [head] S_j ready in TMEM
+  uint64_t* s_empty = s_full + 2;            // [head] S_j loaded by the softmax: S_{j+1} may be computed
+  uint64_t* p_full = s_empty + 2;            // [head] P_j written (and O rescaled): O += P_j V_j may run
+  uint64_t* p_empty = p_full + 2;            // [head] O += P_j V_j done: P may be rewritten, O read
   uint64_t* drain = p_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -93,24 +99,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = warp_id(), lane = lane_id();
   // heaviest causal blocks first
   const int qb = KIND == MASK_CAUSAL ? args.q_blocks - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
-  const int head = blockIdx.y;
+  const int kvh = blockIdx.y;                // key/value head; query heads 2 kvh and 2 kvh + 1
   const int seq = blockIdx.z;
-  const int kvh = head / args.heads_per_kv;
   const int q0 = qb * 128;                 // first query position in the sequence
   const int tok0 = seq * args.L;           // first token of the sequence
   const int kv_blocks = KIND == MASK_CAUSAL ? qb + 1 : (args.L + 127) / 128;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kKvStages; ++s) {
-      mbar_init(kv_full + s, 1);
-      mbar_init(kv_empty + s, 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(s_full + b, 1);
-      mbar_init(s_empty + b, 4);
-      mbar_init(p_full + b, 4);
-      mbar_init(p_empty + b, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(s_full + h, 1);
+      mbar_init(s_empty + h, 4);
+      mbar_init(p_full + h, 4);
+      mbar_init(p_empty + h, 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -128,69 +135,94 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
+  // per head: S at columns [256 h, 256 h + 128), O at [256 h + 128, 256 h + 256)
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------------ TMA
-      mbar_arrive_expect_tx(q_full, TX);
-      for (int kk = 0; kk < 2; ++kk)
-        tma_load_2d(smQ + kk * kTileBytes, &tmQK, q_full, head * 128 + kk * 64, tok0 + q0);
-      int last_parity[kKvStages] = {-1, -1};
-      for (int j = 0; j < kv_blocks; ++j) {
-        const int st = j % kKvStages;
-        const uint32_t ph = (j / kKvStages) & 1;
-        if (!mbar_wait(kv_empty + st, ph ^ 1, abort_flag, args.err, 21)) break;
-        mbar_arrive_expect_tx(kv_full + st, 2 * TX);
-        for (int kk = 0; kk < 2; ++kk) {
-          tma_load_2d(smK + (st * 2 + kk) * kTileBytes, &tmQK, kv_full + st, 16 * 128 + kvh * 128 + kk * 64,
+      mbar_arrive_expect_tx(q_full, 2 * TX);
+      for (int h = 0; h < 2; ++h)
+        for (int kk = 0; kk < 2; ++kk)
+          tma_load_2d(smQ + (h * 2 + kk) * kTileBytes, &tmQK, q_full, (2 * kvh + h) * 128 + kk * 64, tok0 + q0);
+      int k_last[kKStages] = {-1, -1};
+      int v_last = -1;
+      auto load_k = [&](int j) -> bool {
+        const int st = j % kKStages;
+        const uint32_t ph = (j / kKStages) & 1;
+        if (!mbar_wait(k_empty + st, ph ^ 1, abort_flag, args.err, 21)) return false;
+        mbar_arrive_expect_tx(k_full + st, TX);
+        for (int kk = 0; kk < 2; ++kk)
+          tma_load_2d(smK + (st * 2 + kk) * kTileBytes, &tmQK, k_full + st, 16 * 128 + kvh * 128 + kk * 64,
                       tok0 + j * 128);
-          // V^T column = seq * L8 + key: a multiple of 8 elements, the 16-byte TMA alignment
-          tma_load_2d(smV + (st * 2 + kk) * kTileBytes, &tmVt, kv_full + st, seq * args.L8 + j * 128 + kk * 64,
-                      kvh * 128);
-        }
-        last_parity[st] = static_cast<int>(ph);
+        k_last[st] = static_cast<int>(ph);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const uint32_t ph = j & 1;
+        if (!mbar_wait(v_empty, ph ^ 1, abort_flag, args.err, 22)) return false;
+        mbar_arrive_expect_tx(v_full, TX);
+        // V^T column = seq * L8 + key: a multiple of 8 elements, the 16-byte TMA alignment
+        for (int kk = 0; kk < 2; ++kk)
+          tma_load_2d(smV + kk * kTileBytes, &tmVt, v_full, seq * args.L8 + j * 128 + kk * 64, kvh * 128);
+        v_last = static_cast<int>(ph);
+        return true;
+      };
+      // K runs one block ahead of V: K_{j+1} is issued before waiting for V_j's slot
+      bool ok = load_k(0);
+      for (int j = 0; ok && j < kv_blocks; ++j) {
+        if (j + 1 < kv_blocks && !load_k(j + 1)) break;
+        ok = load_v(j);
       }
       volatile int never = 0;
-      mbar_wait(q_full, 0, &never, args.err, 22);
-      for (int s = 0; s < kKvStages; ++s)
-        if (last_parity[s] >= 0) mbar_wait(kv_full + s, static_cast<uint32_t>(last_parity[s]), &never, args.err, 22);
+      mbar_wait(q_full, 0, &never, args.err, 23);
+      for (int s = 0; s < kKStages; ++s)
+        if (k_last[s] >= 0) mbar_wait(k_full + s, static_cast<uint32_t>(k_last[s]), &never, args.err, 23);
+      if (v_last >= 0) mbar_wait(v_full, static_cast<uint32_t>(v_last), &never, args.err, 23);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------------ MMA
-      bool ok = mbar_wait(q_full, 0, abort_flag, args.err, 23);
+      bool ok = mbar_wait(q_full, 0, abort_flag, args.err, 24);
       bool issued = false;
-      const uint64_t dQ[2] = {smem_desc_k_sw128(smem_u32(smQ)), smem_desc_k_sw128(smem_u32(smQ + kTileBytes))};
       auto issue_pv = [&](int i) -> bool {
-        const int st = i % kKvStages;
-        const int pb = i & 1;
-        if (!mbar_wait(p_full + pb, (i >> 1) & 1, abort_flag, args.err, 24)) return false;
-        tc_fence_after();
-        for (int kk = 0; kk < 2; ++kk) {
-          const uint64_t dP = smem_desc_k_sw128(smem_u32(smP + (pb * 2 + kk) * kTileBytes));
-          const uint64_t dV = smem_desc_k_sw128(smem_u32(smV + (st * 2 + kk) * kTileBytes));
+        if (!mbar_wait(v_full, i & 1, abort_flag, args.err, 25)) return false;
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(p_full + h, i & 1, abort_flag, args.err, 26)) return false;
+          tc_fence_after();
+          const uint32_t tO = tmem + 256 * h + 128;
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint64_t dP = smem_desc_k_sw128(smem_u32(smP + (h * 2 + kk) * kTileBytes));
+            const uint64_t dV = smem_desc_k_sw128(smem_u32(smV + kk * kTileBytes));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) umma_f16(tO, dP + 2 * k, dV + 2 * k, IDESC, (i | kk | k) != 0);
+            for (int k = 0; k < 4; ++k) umma_f16(tO, dP + 2 * k, dV + 2 * k, IDESC, (i | kk | k) != 0);
+          }
+          umma_commit(p_empty + h);
+          issued = true;
         }
-        umma_commit(p_empty + pb);
-        umma_commit(kv_empty + st);
-        issued = true;
+        umma_commit(v_empty);
         return true;
       };
       for (int j = 0; ok && j < kv_blocks; ++j) {
-        const int st = j % kKvStages;
-        if (!mbar_wait(kv_full + st, (j / kKvStages) & 1, abort_flag, args.err, 26)) break;
-        if (!mbar_wait(s_empty + (j & 1), ((j >> 1) & 1) ^ 1, abort_flag, args.err, 27)) break;
-        tc_fence_after();
-        for (int kk = 0; kk < 2; ++kk) {
-          const uint64_t dK = smem_desc_k_sw128(smem_u32(smK + (st * 2 + kk) * kTileBytes));
+        const int st = j % kKStages;
+        if (!mbar_wait(k_full + st, (j / kKStages) & 1, abort_flag, args.err, 27)) break;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!mbar_wait(s_empty + h, (j & 1) ^ 1, abort_flag, args.err, 28)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tS = tmem + 256 * h;
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint64_t dQ = smem_desc_k_sw128(smem_u32(smQ + (h * 2 + kk) * kTileBytes));
+            const uint64_t dK = smem_desc_k_sw128(smem_u32(smK + (st * 2 + kk) * kTileBytes));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) umma_f16(tS[j & 1], dQ[kk] + 2 * k, dK + 2 * k, IDESC, (kk | k) != 0);
+            for (int k = 0; k < 4; ++k) umma_f16(tS, dQ + 2 * k, dK + 2 * k, IDESC, (kk | k) != 0);
+          }
+          umma_commit(s_full + h);
+          issued = true;
         }
-        umma_commit(s_full + (j & 1));
-        issued = true;
+        if (!ok) break;
+        umma_commit(k_empty + st);
         if (j >= 1 && !issue_pv(j - 1)) {
           ok = false;
           break;
@@ -200,27 +232,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (issued) {
         umma_commit(drain);
         volatile int never = 0;
-        mbar_wait(drain, 0, &never, args.err, 28);
+        mbar_wait(drain, 0, &never, args.err, 29);
       }
     }
   } else {
-    // -------------------------------------------------------------------- softmax (warps 2..5)
+    // -------------------------------------------------------------------- softmax (warps 2..9)
+    const int hg = (warp - 2) >> 2;          // 0: query head 2 kvh, 1: 2 kvh + 1
+    const int head = 2 * kvh + hg;
     const int qd = warp & 3;                 // TMEM lane quadrant = row block
     const int r = qd * 32 + lane;            // query row within the tile
     const int qpos = q0 + r;                 // query position in the sequence
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+    const uint32_t tS = tmem + 256 * hg;
+    const uint32_t tO = tS + 128;
+    uint8_t* myP = smP + hg * 2 * kTileBytes;
     const float sc = args.scale_log2;
     float m_use = -INFINITY;                 // the max the probabilities and O are relative to (log2 units)
     float l = 0.f;
     bool ok = true;
     uint32_t v[128];                         // this row of S_j, loaded from TMEM once
     for (int j = 0; j < kv_blocks && ok; ++j) {
-      const int b = j & 1;
       const int k0 = j * 128;
       // warp-uniform: does any entry of this block need the mask?
       const bool masked = KIND == MASK_PREFIX || KIND == MASK_BOOL || k0 + 128 > args.L ||
                           (KIND == MASK_CAUSAL && k0 + 127 > q0);
-      if (!mbar_wait(s_full + b, (j >> 1) & 1, abort_flag, args.err, 31)) {
+      if (!mbar_wait(s_full + hg, j & 1, abort_flag, args.err, 31)) {
         ok = false;
         break;
       }
@@ -228,12 +264,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        tmem_ld_32x32b_x32(tS[b] + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
+        tmem_ld_32x32b_x32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
       tmem_ld_wait();
-      // S_j is in registers: the MMA may compute S_{j+2} into this buffer
+      // S_j is in registers: the MMA may compute S_{j+1} into these columns
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty + b);
+      if (lane == 0) mbar_arrive(s_empty + hg);
       if (masked) {
 #pragma unroll
         for (int e = 0; e < 128; ++e)
@@ -251,12 +287,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         alpha = fast_exp2(m_use - m_blk);    // 0 while m_use is -inf
         m_use = m_blk;
       }
+      // O += P_{j-1} V_{j-1} has finished: O may be rescaled and the P tile rewritten
+      if (j >= 1 && !mbar_wait(p_empty + hg, (j - 1) & 1, abort_flag, args.err, 32)) {
+        ok = false;
+        break;
+      }
       if (j >= 1 && __any_sync(0xffffffffu, raise && l > 0.f)) {
-        // O must hold O_{j-1} before it is rescaled in place (rows that did not raise multiply by 1)
-        if (!mbar_wait(p_empty + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, args.err, 32)) {
-          ok = false;
-          break;
-        }
+        // rows that did not raise multiply by 1
         tc_fence_after();
         uint32_t o[32];
 #pragma unroll 1
@@ -271,11 +308,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_st_wait();
       }
       l *= alpha;
-      // P buffer j & 1 was last read by O += P_{j-2} V_{j-2}
-      if (j >= 2 && !mbar_wait(p_empty + b, ((j - 2) >> 1) & 1, abort_flag, args.err, 33)) {
-        ok = false;
-        break;
-      }
       // p = 2^(s * scale - m) as bf16 into the swizzled K-major P tile, and the row sum
       const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
       const bool none = m_use == -INFINITY;  // every key so far masked
@@ -292,7 +324,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           w[e / 2] = pack2_bf16(p0, p1);
         }
         // 32 keys = 64 bytes = 4 chunks of 16 bytes in k-block c / 2, chunk offset (c % 2) * 4
-        uint8_t* rowp = smP + (b * 2 + (c >> 1)) * kTileBytes + r * 128;
+        uint8_t* rowp = myP + (c >> 1) * kTileBytes + r * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int chunk = (c & 1) * 4 + q;
@@ -305,12 +337,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before();
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + b);
+      if (lane == 0) mbar_arrive(p_full + hg);
     }
     if (ok && kv_blocks > 0) {
       // the last O += P V, then O / l
       const int last = kv_blocks - 1;
-      if (mbar_wait(p_empty + (last & 1), (last >> 1) & 1, abort_flag, args.err, 34)) {
+      if (mbar_wait(p_empty + hg, last & 1, abort_flag, args.err, 34)) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<int64_t>(tok0 + qpos) * (16 * 128) + head * 128);
@@ -380,13 +412,12 @@ int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt
   a.L = static_cast<int>(L);
   a.L8 = static_cast<int>(L8);
   a.q_blocks = static_cast<int>((L + 127) / 128);
-  a.heads_per_kv = 2;
   a.scale_log2 = 1.4426950408889634f / sqrtf(128.f);
   a.lens = lens;
   a.mask = mask;
   a.mask_heads = mask_heads;
   a.err = device_error_word();
-  dim3 grid(static_cast<unsigned>(a.q_blocks), 16, static_cast<unsigned>(B));
+  dim3 grid(static_cast<unsigned>(a.q_blocks), 8, static_cast<unsigned>(B));  // (query block, kv head, sequence)
   static bool configured[4][64] = {};
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
