@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--seq-len", type=int, default=1024, help="stack: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="stack: decoder layers")
     ap.add_argument("--images", type=int, default=32, help="conv: images in the global batch")
+    ap.add_argument("--head", default="column", choices=["column", "dp"],
+                    help="stack on N > 1 GPUs: head column-parallel after an all-gather (default), or with the sequences")
     ap.add_argument("--kernel", default=None,
                     choices=["gemm_i8", "quant_rows", "conv3x3", "attention", "gemm_bf16"],
                     help="time one kernel on --shape instead of a workload (profiling)")
@@ -308,6 +310,8 @@ def run_xdna(args, rank, world):
 
     # ---- roofline: the GEMM kernel alone (same shapes, same stream), event-timed per launch
     roof = gemm_roofline(shapes, dev, args.steps, flush)
+    # config 2's square M = N = K = 4096 GEMM, the case the >= 70 %-of-peak target is stated on
+    roof_sq = gemm_roofline([(4096, 4096, 4096)], dev, args.steps, flush) if args.workload == "cfg2" else None
     # ---- e2e through torch.compile(backend="xdna") with host buffers
     e2e = e2e_measure(args, model, dev, world, work)
     # ---- CPU baseline (rank 0, one GPU only)
@@ -321,6 +325,8 @@ def run_xdna(args, rank, world):
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
                 "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)", "config": config_of(args),
                 "gpu_launches": launches, "roofline": roof, "e2e": e2e, "clocks": clocks.summary()}
+        if roof_sq is not None:
+            line["roofline_square_4096"] = roof_sq
         if cb is not None:
             line["cpu_baseline"] = cb
         print(json.dumps(line), flush=True)
@@ -458,10 +464,13 @@ def stack_flops(B, L, layers, vocab):
 
 def run_stack(args, rank, world):
     """One step = embed the token ids of this rank's sequences and run xdna_qwen3_stack (28 layers, final
-    norm, head over 151936) under a causal mask. Sequences are data-parallel over ranks (no collective:
-    sequences are independent); the global batch is fixed (strong scaling)."""
+    norm, head over 151936) under a causal mask; the global batch is fixed (strong scaling). The layers
+    are data-parallel over sequences (independent: no collective). The head, on more than one GPU, is
+    column-parallel by default: an NCCL all-gather of every rank's final hidden states
+    over NVLink, then each rank computes its 151936 / N vocabulary columns for all tokens; --head dp keeps
+    it with the sequences instead."""
     import torch_xdna
-    from torch_xdna import kernels
+    from torch_xdna import kernels, parallel
 
     if not torch_xdna.gpu_available():
         raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
@@ -485,23 +494,40 @@ def run_stack(args, rank, world):
                                       *[t.data_ptr() for t in norms])
     final = torch.ones(D, device=dev)
     head, embed = w(V_HEAD, D), w(V_HEAD, D)
+    column = world > 1 and args.head == "column"
+    n_cols = V_HEAD // world if column else V_HEAD       # 151936 = 2^7 x 1187: divides by 2, 4 and 8
+    if column:
+        head = head[rank * n_cols:(rank + 1) * n_cols].contiguous()
     inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device=dev) / 128))
     f = torch.arange(L, dtype=torch.float32, device=dev)[:, None] * inv[None, :]
     cos, sin = f.cos().contiguous(), f.sin().contiguous()
     ids = torch.randint(0, V_HEAD, (B * L,), device=dev, generator=g)
     x = torch.empty(B * L, D, device=dev)
-    out = torch.empty(B * L, V_HEAD, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(B_all * L if column else B * L, n_cols, dtype=torch.bfloat16, device=dev)
     ws = torch.empty(kernels.qwen3_stack_workspace(B, L), dtype=torch.uint8, device=dev)
+    hidden = ws[:B * L * D * 2].view(torch.bfloat16).view(B * L, D)   # the final-normed states (workspace head)
+    h_all = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev) if column else None
     launches_per_step = 1 + 7 * NL + 2
 
     def step(ids_dev):
         kernels.embed(ids_dev, embed, x)
-        kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
-                            out, ws)
+        if column:
+            kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
+                                None, ws)
+            parallel.gather_rows(hidden, h_all)
+            kernels.gemm_bf16(h_all, head, kernels.GEMM_F32ACC, out=out)
+        else:
+            kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
+                                out, ws)
 
     stream = torch.cuda.current_stream()
     for _ in range(max(args.warmup, 3)):
         step(ids)
+    if column:   # once, untimed: this rank's vocabulary slice of 256 gathered rows vs an f32 product
+        ref = h_all[:256].float() @ head.float().t()
+        err = float((out[:256].float() - ref).abs().max() / ref.abs().max())
+        if not err < 2e-2:
+            raise SystemExit(f"rank {rank}: column-parallel head disagrees with the f32 product (rel {err:.3g})")
     barrier(world)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -518,7 +544,7 @@ def run_stack(args, rank, world):
     flops = stack_flops(B, L, NL, V_HEAD)
 
     # roofline: the head GEMM (the largest single launch), timed alone per launch
-    hn = torch.randn(B * L, D, device=dev).to(torch.bfloat16)
+    hn = torch.randn(out.shape[0], D, device=dev).to(torch.bfloat16)
     for _ in range(2):
         kernels.gemm_bf16(hn, head, kernels.GEMM_F32ACC, out=out)
     ms = []
@@ -530,7 +556,7 @@ def run_stack(args, rank, world):
         e.synchronize()
         ms.append(s.elapsed_time(e))
     head_ms = statistics.median(ms)
-    head_flops = 2 * B * L * V_HEAD * D
+    head_flops = 2 * out.shape[0] * n_cols * D
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("bf16_tflops", 1590.0))
     roof = {"bound": "tensor", "kernel": "umma_gemm_kernel bf16 (the head GEMM, EPI_F32ACC)",
@@ -542,7 +568,7 @@ def run_stack(args, rank, world):
 
     # e2e: token ids from pinned host memory in, every logit back to pinned host memory
     h_ids = ids.cpu().pin_memory()
-    h_out = torch.empty(B * L, V_HEAD, dtype=torch.bfloat16, pin_memory=True)
+    h_out = torch.empty(out.shape, dtype=torch.bfloat16, pin_memory=True)
     d_ids = torch.empty_like(ids)
     e_steps = max(2, min(5, args.steps))
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -568,7 +594,9 @@ def run_stack(args, rank, world):
                 "data": "synthetic (uniform token ids, N(0,0.02) weights, unit norms)",
                 "config": {"workload": f"cfg5 Qwen3-0.6B stack: {NL} layers, {B_all} sequences x {L} tokens, causal "
                                        f"mask, head {V_HEAD}, bf16 with f32 accumulation", "global_batch": B_all,
-                           "seq_len": L, "parallelism": f"dp{world} (sequences)", "l2": "inputs exceed L2"},
+                           "seq_len": L, "l2": "inputs exceed L2",
+                           "parallelism": (f"dp{world} sequences; head column-parallel over {world} (NCCL all-gather "
+                                           "of hidden states)") if column else f"dp{world} (sequences)"},
                 "gpu_launches": launches_per_step * args.steps, "roofline": roof, "e2e": e2e,
                 "clocks": clocks.summary()}
         if cb is not None:
@@ -631,6 +659,40 @@ def vgg_macs(batch, hw=224):
         macs += batch * h * h * ci * v * 9
         ci = v
     return macs
+
+
+def single_conv_roofline(dev, stream, peak, src):
+    """The conv kernel on BASELINE config 4's single Ci = Co = 256 conv of one 1536 x 64 image (dequantise
+    epilogue with bias and ReLU), event-timed per launch with L2 flushed before each."""
+    from torch_xdna import conv as xconv
+    from torch_xdna import kernels
+
+    g = torch.Generator(device=dev).manual_seed(7)
+    w = torch.nn.Parameter(torch.randn(256, 256, 3, 3, device=dev, generator=g) * (2.0 / (256 * 9)) ** 0.5)
+    b = torch.randn(256, device=dev, generator=g) * 0.01
+    lay = xconv.ConvLayer(w, 1536, 64, False)
+    xp = torch.randint(-127, 128, (1, 1538, 66, lay.cp), dtype=torch.int8, device=dev, generator=g)
+    xp[:, 0].zero_(), xp[:, -1].zero_(), xp[:, :, 0].zero_(), xp[:, :, -1].zero_()
+    lay.calibrate(xp)
+    sx = torch.rand(1, device=dev)
+    yo = torch.empty(1, 256, 1536, 64, device=dev, memory_format=torch.channels_last)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    ms = []
+    for i in range(8):
+        flush.fill_(1)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        kernels.conv3x3(xp, lay.wp, 1, 256, 256, 1536, 64, kernels.CONV_DEQUANT, shift=lay.shift, scale=lay.scale,
+                        sx=sx, bias=b, relu=kernels.RELU_AFTER_BIAS, out=yo)
+        e.record(stream)
+        e.synchronize()
+        if i >= 2:
+            ms.append(s.elapsed_time(e))
+    ops = 2 * 1536 * 64 * 256 * 256 * 9
+    achieved = ops / statistics.median(ms) / 1e9
+    return {"bound": "tensor", "kernel": "umma_gemm_kernel LOAD_CONV (conv 256->256, 1 x 1536 x 64, bias + ReLU)",
+            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS", "frac": round(achieved / peak, 4),
+            "peak_source": src, "per_launch_ms": round(statistics.median(ms), 4)}
 
 
 def run_conv(args, rank, world):
@@ -708,6 +770,8 @@ def run_conv(args, rank, world):
     roof = {"bound": "tensor", "kernel": "umma_gemm_kernel LOAD_CONV (conv 64->64 224x224, dequantise epilogue)",
             "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS", "frac": round(achieved / peak, 4),
             "peak_source": src, "traffic": None, "per_launch_ms": round(statistics.median(ms), 4)}
+    # config 4's single Ci = Co = 256 conv on one 1536 x 64 image (bias, ReLU after it), timed alone
+    single = single_conv_roofline(dev, stream, peak, src)
     cb = cpu_conv_baseline() if (rank == 0 and world == 1) else None
     if kernels.take_device_error() != (0, 0):
         raise SystemExit("a kernel recorded a device-side timeout")
@@ -718,7 +782,8 @@ def run_conv(args, rank, world):
                 "vs_baseline": None, "dtype": "int8", "data": "synthetic (N(0,1) images, Kaiming weights, N(0,0.01) bias)",
                 "config": {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224, bias + ReLU, 2x2 max-pool",
                            "global_batch": N_all, "parallelism": f"dp{world} (images)", "l2": "activations exceed L2"},
-                "gpu_launches": launches, "roofline": roof, "clocks": clocks.summary()}
+                "gpu_launches": launches, "roofline": roof, "single_conv_256x1536x64": single,
+                "clocks": clocks.summary()}
         if cb is not None:
             line["cpu_baseline"] = cb
         print(json.dumps(line), flush=True)

@@ -1,5 +1,7 @@
 """Data-parallel host logic on CPU with two gloo ranks: every rank adopts rank 0's conv shift (rank 0 holds
-global image 0, whose sums fix the shift in the reference), and batches shard contiguously."""
+global image 0, whose sums fix the shift in the reference), batches shard contiguously, and the stack's
+column-parallel head (all-gather of hidden rows, then a vocabulary slice per rank) reassembles the full
+logits."""
 
 import os
 import socket
@@ -37,7 +39,14 @@ def _worker(rank, world, port, q):
         parallel.disable_data_parallel()
         x = torch.arange(8 * 3).view(8, 3)
         part = parallel.shard(x, rank, world)
-        q.put((rank, own, s1, s2, part[:, 0].tolist()))
+        # column-parallel head: rows of this rank's sequences -> all rows -> this rank's vocabulary slice
+        h_local = torch.arange(2 * 4, dtype=torch.float32).view(2, 4) + 100 * rank
+        h_all = torch.empty(2 * world, 4)
+        parallel.gather_rows(h_local, h_all)
+        w = torch.arange(6 * 4, dtype=torch.float32).view(6, 4)
+        n_cols = 6 // world
+        logits = h_all @ w[rank * n_cols:(rank + 1) * n_cols].t()
+        q.put((rank, own, s1, s2, part[:, 0].tolist(), h_all.tolist(), logits.tolist()))
     finally:
         dist.destroy_process_group()
 
@@ -53,8 +62,14 @@ def test_shift_broadcast_and_shards_two_ranks():
         p.join(120)
         assert p.exitcode == 0
     res = sorted(q.get(timeout=10) for _ in range(2))
-    assert res[0] == (0, 10, 10, 20, [0, 3, 6, 9])
-    assert res[1] == (1, 11, 10, 20, [12, 15, 18, 21])
+    assert res[0][:5] == (0, 10, 10, 20, [0, 3, 6, 9])
+    assert res[1][:5] == (1, 11, 10, 20, [12, 15, 18, 21])
+    h_all = torch.tensor(res[0][5])
+    want_h = torch.cat([torch.arange(8, dtype=torch.float32).view(2, 4) + 100 * r for r in range(2)])
+    assert torch.equal(h_all, want_h) and res[1][5] == res[0][5]
+    w = torch.arange(6 * 4, dtype=torch.float32).view(6, 4)
+    logits = torch.cat([torch.tensor(res[r][6]) for r in range(2)], dim=1)
+    assert torch.equal(logits, want_h @ w.t())
 
 
 def test_shard_rejects_uneven():

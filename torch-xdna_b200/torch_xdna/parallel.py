@@ -6,8 +6,9 @@ What shards (the reference is single-device; the build adds these):
     image of the first call (R:torch_xdna/conv.py:171-172). With enable_data_parallel(), every conv
     layer's first calibration takes the shift computed on rank 0 (which holds global image 0) and
     broadcasts it, so every rank requantises exactly as one GPU running the whole batch would;
-  - stack sequences: sequences are independent under the mask, so they split over ranks with no
-    collective at all;
+  - stack sequences: sequences are independent under the mask, so the layers split over ranks with no
+    collective at all; the linear head can then run column-parallel (each rank 1/world of the
+    vocabulary for every token) after gather_rows of the final hidden states;
   - the W8A8 linears do not shard usefully (their outputs are larger than their work): replicas.
 """
 
@@ -54,3 +55,13 @@ def shard(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
         raise ValueError(f"{n} items do not divide over {world} ranks")
     k = n // world
     return t.narrow(dim, rank * k, k)
+
+
+def gather_rows(local: torch.Tensor, out: torch.Tensor, group=None) -> torch.Tensor:
+    """out [world x rows, ...] = every rank's `local` [rows, ...] in rank order (an NCCL all-gather over
+    NVLink on GPUs): the hidden states of all sequences for a column-parallel head."""
+    import torch.distributed as dist
+
+    assert out.shape[0] == local.shape[0] * dist.get_world_size(group) and out.shape[1:] == local.shape[1:]
+    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    return out
