@@ -340,6 +340,12 @@ def int8_peak():
     return 2 * 1590.0, "2x fallback dense bf16 1.59 PFLOP/s"
 
 
+# DRAM bytes (read + write) of one gemm_i8 launch per shape, from one ncu capture each
+# (profiles/gemm_i8_dram_traffic.md has the command).
+PROFILED_DRAM_BYTES = {(8192, 4096, 1024): 26222336, (8192, 6144, 1024): 61992960, (8192, 1024, 3072): 28405248,
+                       (4096, 4096, 4096): 36336640}
+
+
 def gemm_roofline(shapes, dev, steps, flush):
     """Algorithmic int8 ops per launch of the GEMM kernel / its CUDA-event duration, summed over the
     workload's GEMMs; inputs pre-quantised, L2 flushed before every launch."""
@@ -374,9 +380,13 @@ def gemm_roofline(shapes, dev, steps, flush):
     torch.cuda.synchronize()
     peak, src = int8_peak()
     achieved = total_ops / (total_ms / 1e3) / 1e12
+    traffic = None
+    if all(tuple(sh) in PROFILED_DRAM_BYTES for sh in shapes):
+        traffic = round(sum(PROFILED_DRAM_BYTES[tuple(sh)] for sh in shapes) / len(shapes))
     return {"bound": "tensor", "kernel": "umma_gemm_kernel (gemm_i8, dequantising epilogue, bf16 out)",
             "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
-            "frac": round(achieved / peak, 4), "peak_source": src, "traffic": None,
+            "frac": round(achieved / peak, 4), "peak_source": src, "traffic": traffic,
+            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
             "per_launch_ms": round(total_ms / len(shapes), 4)}
 
 
