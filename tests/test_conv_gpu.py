@@ -53,7 +53,9 @@ def test_conv_op_matches_reference_digests(cuda, golden, name):
 @pytest.mark.parametrize("relu", [False, True])
 @pytest.mark.parametrize("n,ci,co,h,w", [(1, 256, 256, 64, 64), (2, 3, 64, 13, 37), (2, 64, 48, 13, 37),
                                          (1, 16, 16, 1, 1), (3, 130, 20, 7, 129), (1, 512, 512, 14, 14),
-                                         (2, 64, 64, 224, 224)])
+                                         (2, 64, 64, 224, 224),
+                                         # 256 x 256 tiles on CTA pairs (the second: ragged Co and channel block)
+                                         (8, 128, 256, 56, 56), (5, 160, 300, 40, 52)])
 def test_conv_q_bitexact_vs_oracle(cuda, relu, n, ci, co, h, w):
     x, wt, _ = mg.conv_inputs(n * 1000 + ci + co + h, n, ci, co, h, w)
     want = orc.conv3x3_int8(x, wt, None, relu=relu)
@@ -70,9 +72,10 @@ def test_conv_q_bitexact_vs_oracle(cuda, relu, n, ci, co, h, w):
 
 @pytest.mark.parametrize("post_relu", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_conv_fused_dequant_bitexact(cuda, dtype, post_relu):
+@pytest.mark.parametrize("n,ci,co,h,w", [(2, 96, 80, 30, 50), (5, 160, 300, 40, 52)])  # the second: CTA pairs
+def test_conv_fused_dequant_bitexact(cuda, dtype, post_relu, n, ci, co, h, w):
     """The dequantise (+ bias) to x.dtype, bit for bit; post_relu equals torch.relu of it."""
-    x, wt, b = mg.conv_inputs(5, 2, 96, 80, 30, 50, bias=True)
+    x, wt, b = mg.conv_inputs(5, n, ci, co, h, w, bias=True)
     xd = orc.cast(x, "bfloat16") if dtype == torch.bfloat16 else x
     want = orc.conv3x3_int8(xd, wt, b, relu=False, x_dtype="bfloat16" if dtype == torch.bfloat16 else "float32")
     weight = torch.nn.Parameter(t(wt, cuda))

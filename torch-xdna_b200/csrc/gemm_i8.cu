@@ -17,7 +17,7 @@ static int dispatch_bn(int bn, bool pair, const CUtensorMap& ta, const CUtensorM
                        const GemmArgs& args, int sms, cudaStream_t stream) {
   switch (bn) {
     case 256:
-      if constexpr (LOAD == LOAD_GEMM && KB == 128) {
+      if constexpr (KB == 128) {
         if (pair) return launch_gemm_kernel<256, LOAD, EPI, false, TSTORE, ODT, KB, true>(ta, tb, tc, ta, args, sms, stream);
       }
       return launch_umma<256, LOAD, EPI, TSTORE, ODT, KB>(ta, tb, tc, args, sms, stream);
@@ -31,10 +31,10 @@ static int dispatch_bn(int bn, bool pair, const CUtensorMap& ta, const CUtensorM
 // The conv's kernel for one mode, with 64-byte K blocks when the input has at most 64 channels (a
 // 128-byte block would be half zero fill).
 template <int EPI, int ODT>
-static int dispatch_conv(int kb, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int sms,
-                         cudaStream_t stream) {
+static int dispatch_conv(int kb, int bn, bool pair, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
+                         int sms, cudaStream_t stream) {
   if (kb == 64) return dispatch_bn<LOAD_CONV, EPI, false, ODT, 64>(bn, false, ta, tb, ta, args, sms, stream);
-  return dispatch_bn<LOAD_CONV, EPI, false, ODT, 128>(bn, false, ta, tb, ta, args, sms, stream);
+  return dispatch_bn<LOAD_CONV, EPI, false, ODT, 128>(bn, pair, ta, tb, ta, args, sms, stream);
 }
 
 // Widest tile that still gives every SM work; 64 for narrow outputs.
@@ -187,6 +187,9 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   a.m_tiles = static_cast<int>((NP + kBM - 1) / kBM);
   const int bn = choose_bn(a.m_tiles, Co, sms);
   a.n_tiles = static_cast<int>((Co + bn - 1) / bn);
+  // 256 x 256 tiles on CTA pairs for wide convs (not the calibration, which runs one image)
+  const bool pair = kb == 128 && mode != XDNA_CONV_CALIBRATE && use_pairs(bn, a.m_tiles, a.n_tiles, sms);
+  if (pair) a.m_tiles = static_cast<int>((NP + 2 * kBM - 1) / (2 * kBM));
   a.Wp = static_cast<int>(Wp);
   a.HWp = static_cast<int>(HWp);
   a.H = static_cast<int>(H);
@@ -219,18 +222,18 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(Cp), 9, static_cast<uint64_t>(Co)};
     const uint64_t strides[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(9 * Cp)};
-    const uint32_t box[3] = {static_cast<uint32_t>(kb), 1, static_cast<uint32_t>(bn)};
+    const uint32_t box[3] = {static_cast<uint32_t>(kb), 1, static_cast<uint32_t>(pair ? bn / 2 : bn)};
     rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wp, dims, strides, box, "conv3x3 weights",
                     kb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != XDNA_OK) return rc;
   }
   switch (mode) {
     case XDNA_CONV_Q:
-      return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, pair, ta, tb, a, sms, s);
     case XDNA_CONV_DEQUANT:
-      return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, pair, ta, tb, a, sms, s);
     default:
-      return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, false, ta, tb, a, sms, s);
   }
 }
 

@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                      const GemmArgs args) {
   static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
-  static_assert(!PAIR || (LOAD == LOAD_GEMM && BN == 256 && KB == 128), "CTA pairs: GEMM operands, 256 x 256 tiles");
+  static_assert(!PAIR || (BN == 256 && KB == 128), "CTA pairs: 256 x 256 tiles of 128-byte K blocks");
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (tile columns) this CTA loads
   constexpr int STAGES = stages_for<BROWS, KB>();
   constexpr int A_BYTES = kBM * KB;
@@ -647,8 +647,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             // both CTAs' bytes complete on the even CTA's barrier, which only it arms
             if (leader) mbar_arrive_expect_tx(full + stage, STAGE_TX);
             const uint32_t fb = cluster_addr(full + stage, 0);
-            tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, kb * K_ELEMS, tile_row0(mb));
-            tma_load_2d_pair(smB + stage * B_BYTES, &tmB, fb, kb * K_ELEMS, nb * BN + static_cast<int>(rank) * BROWS);
+            const int b_row = nb * BN + static_cast<int>(rank) * BROWS;  // this CTA's half of the B rows
+            if constexpr (LOAD == LOAD_GEMM) {
+              tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, kb * K_ELEMS, tile_row0(mb));
+              tma_load_2d_pair(smB + stage * B_BYTES, &tmB, fb, kb * K_ELEMS, b_row);
+            } else {
+              const int tap = kb / args.cblocks;
+              const int cb = kb - tap * args.cblocks;
+              tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, cb * K_ELEMS,
+                               tile_row0(mb) + (tap / 3 - 1) * args.Wp + (tap % 3 - 1));
+              tma_load_3d_pair(smB + stage * B_BYTES, &tmB, fb, cb * K_ELEMS, tap, b_row);
+            }
           } else if constexpr (LOAD == LOAD_GEMM) {
             mbar_arrive_expect_tx(full + stage, STAGE_TX);
             tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, kb * K_ELEMS, mb * kBM);
