@@ -58,8 +58,10 @@ def parse():
     ap.add_argument("--seq-len", type=int, default=1024, help="stack: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="stack: decoder layers")
     ap.add_argument("--images", type=int, default=32, help="conv: images in the global batch")
-    ap.add_argument("--head", default="column", choices=["column", "dp"],
-                    help="stack on N > 1 GPUs: head column-parallel after an all-gather (default), or with the sequences")
+    ap.add_argument("--head", default="column", choices=["column", "column-direct", "column-nccl", "dp"],
+                    help="stack on N > 1 GPUs: head column-parallel with the all-gather pipelined into its GEMMs "
+                         "(default: peer blocks copied over NVLink once, overlapping the GEMM), read by the GEMM's "
+                         "TMA straight from peer memory, after an NCCL all-gather; or data-parallel with the sequences")
     ap.add_argument("--kernel", default=None,
                     choices=["gemm_i8", "quant_rows", "conv3x3", "attention", "gemm_bf16"],
                     help="time one kernel on --shape instead of a workload (profiling)")
@@ -504,7 +506,8 @@ def run_stack(args, rank, world):
                                       *[t.data_ptr() for t in norms])
     final = torch.ones(D, device=dev)
     head, embed = w(V_HEAD, D), w(V_HEAD, D)
-    column = world > 1 and args.head == "column"
+    column = world > 1 and args.head in ("column", "column-direct", "column-nccl")
+    fused = column and args.head != "column-nccl"  # the all-gather inside the head's GEMM pipeline
     n_cols = V_HEAD // world if column else V_HEAD       # 151936 = 2^7 x 1187: divides by 2, 4 and 8
     if column:
         head = head[rank * n_cols:(rank + 1) * n_cols].contiguous()
@@ -516,7 +519,9 @@ def run_stack(args, rank, world):
     out = torch.empty(B_all * L if column else B * L, n_cols, dtype=torch.bfloat16, device=dev)
     ws = torch.empty(kernels.qwen3_stack_workspace(B, L), dtype=torch.uint8, device=dev)
     hidden = ws[:B * L * D * 2].view(torch.bfloat16).view(B * L, D)   # the final-normed states (workspace head)
-    h_all = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev) if column else None
+    h_all = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev) if column and not fused else None
+    rg = parallel.RowGather(B * L, D, dev, mode="direct" if args.head == "column-direct" else "pipelined") \
+        if fused else None
     launches_per_step = 1 + 7 * NL + 2
 
     def step(ids_dev):
@@ -524,8 +529,12 @@ def run_stack(args, rank, world):
         if column:
             kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
                                 None, ws)
-            parallel.gather_rows(hidden, h_all)
-            kernels.gemm_bf16(h_all, head, kernels.GEMM_F32ACC, out=out)
+            if fused:
+                rg.local.copy_(hidden)
+                rg.gemm(head, out)
+            else:
+                parallel.gather_rows(hidden, h_all)
+                kernels.gemm_bf16(h_all, head, kernels.GEMM_F32ACC, out=out)
         else:
             kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
                                 out, ws)
@@ -533,11 +542,17 @@ def run_stack(args, rank, world):
     stream = torch.cuda.current_stream()
     for _ in range(max(args.warmup, 3)):
         step(ids)
-    if column:   # once, untimed: this rank's vocabulary slice of 256 gathered rows vs an f32 product
-        ref = h_all[:256].float() @ head.float().t()
-        err = float((out[:256].float() - ref).abs().max() / ref.abs().max())
-        if not err < 2e-2:
-            raise SystemExit(f"rank {rank}: column-parallel head disagrees with the f32 product (rel {err:.3g})")
+    if column:   # once, untimed: this rank's vocabulary slice of 256 rows of every rank vs an f32 product
+        gathered = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev)
+        parallel.gather_rows(hidden, gathered)
+        for r in range(world):
+            rows = slice(r * B * L, r * B * L + 256)
+            ref = gathered[rows].float() @ head.float().t()
+            err = float((out[rows].float() - ref).abs().max() / ref.abs().max())
+            if not err < 2e-2:
+                raise SystemExit(f"rank {rank}: column-parallel head rows of rank {r} disagree with the f32 "
+                                 f"product (rel {err:.3g})")
+        del gathered
     barrier(world)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -593,6 +608,8 @@ def run_stack(args, rank, world):
     e2e_s = max_over_ranks(s.elapsed_time(e) / 1e3, world)
     e2e = {"value": round(B_all * L * e_steps / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h_ids.numel() * 8,
            "d2h_bytes_per_step": h_out.numel() * 2, "api": "xdna_qwen3_stack C ABI (torch_xdna.kernels)"}
+    if rg is not None:
+        rg.close()
     cb = cpu_stack_baseline(NL, 1, 128) if (rank == 0 and world == 1) else None
     if kernels.take_device_error() != (0, 0):
         raise SystemExit("a kernel recorded a device-side timeout")
@@ -605,8 +622,11 @@ def run_stack(args, rank, world):
                 "config": {"workload": f"cfg5 Qwen3-0.6B stack: {NL} layers, {B_all} sequences x {L} tokens, causal "
                                        f"mask, head {V_HEAD}, bf16 with f32 accumulation", "global_batch": B_all,
                            "seq_len": L, "l2": "inputs exceed L2",
-                           "parallelism": (f"dp{world} sequences; head column-parallel over {world} (NCCL all-gather "
-                                           "of hidden states)") if column else f"dp{world} (sequences)"},
+                           "parallelism": (f"dp{world} sequences; head column-parallel over {world}, " + (
+                               ("peer blocks copied over NVLink once, overlapping the GEMM over this rank's rows"
+                                if args.head == "column" else "the GEMM's TMA reading every rank's rows from its memory")
+                               if fused else "NCCL all-gather of hidden states before the head GEMM"))
+                           if column else f"dp{world} (sequences)"},
                 "gpu_launches": launches_per_step * args.steps, "roofline": roof, "e2e": e2e,
                 "clocks": clocks.summary()}
         if cb is not None:

@@ -189,6 +189,29 @@ int xdna_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64
                    void* vt, int64_t ldvt, const float* rope_cos, const float* rope_sin, const float* q_norm,
                    const float* k_norm, int64_t seq_len, float eps, void* stream);
 
+/* The head GEMM of a column-parallel stack, fused with the all-gather of its input: out [n_parts *
+ * rows_per_part, N] = A . b^T (+ bias) with the XDNA_GEMM_F32ACC epilogue, where rows [i * rows_per_part,
+ * (i + 1) * rows_per_part) of A are a_parts[i] ([rows_per_part, K] bf16, pitch lda) — device pointers
+ * that may belong to other GPUs of the box (peer memory opened with xdna_ipc_open), read by the GEMM's
+ * TMA producer over NVLink while the tensor cores run, instead of a separate all-gather. rows_per_part
+ * must be a multiple of 256. maps: device memory for n_parts tensor maps (128 bytes each, 64-byte
+ * aligned), written by this call (stream-ordered). The caller orders the parts' writes before this call
+ * on every GPU (e.g. a barrier collective). Replaces the all-gather + head of SURVEY §8e's column-parallel
+ * head, which the reference (single device) does not have. */
+int xdna_gemm_bf16_gather(const void* const* a_parts, int n_parts, int64_t rows_per_part, int64_t lda, const void* b,
+                          int64_t ldb, int64_t N, int64_t K, void* out, int out_dtype, int64_t ldo, const void* bias,
+                          int bias_dtype, void* maps, void* stream);
+
+/* CUDA IPC for xdna_gemm_bf16_gather's peer parts (no reference counterpart; the only entry points
+ * that allocate): a dedicated device allocation that can be shared, its release; the 64-byte handle of
+ * such an allocation; the device pointer of another process's allocation on this box (NVLink peer
+ * access enabled) and its release. */
+int xdna_ipc_alloc(size_t bytes, void** dev_ptr);
+int xdna_ipc_free(void* dev_ptr);
+int xdna_ipc_handle(const void* dev_ptr, void* handle64);
+int xdna_ipc_open(const void* handle64, void** dev_ptr);
+int xdna_ipc_close(void* dev_ptr);
+
 /* out [B*L, 2048] bf16 = softmax(q k^T / sqrt(128) + mask) v for 16 query heads over 8 kv heads (GQA),
  * q and k read from qk [B*L, 3072] (the XDNA_GEMM_QKV output), v from vt [1024, ldvt]. */
 int xdna_attention(const void* qk, const void* vt, int64_t ldvt, void* out, int64_t B, int64_t L, int mask_kind,

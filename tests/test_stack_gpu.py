@@ -59,6 +59,37 @@ def test_gemm_bf16_f32acc(cuda, out_dtype, M, N, K):
     assert rel_max(out, want) < (1e-4 if out_dtype == torch.float32 else 8e-3)
 
 
+@pytest.mark.parametrize("parts,rows,N", [(1, 256, 1024), (2, 1024, 2048), (3, 2048, 4096), (2, 128, 520)])
+def test_gemm_bf16_gather(cuda, parts, rows, N):
+    """The head GEMM over A split by rows into several buffers (the fused all-gather of the column-parallel
+    head; here every part is on this GPU): equals one GEMM over the concatenated rows."""
+    from torch_xdna import kernels
+
+    g = torch.Generator(device=cuda).manual_seed(parts * rows + N)
+    bufs = [bf(torch.randn(rows, 1024, device=cuda, generator=g)) for _ in range(parts)]
+    w = bf(torch.randn(N, 1024, device=cuda, generator=g) * 0.03)
+    out = torch.empty(parts * rows, N, dtype=torch.bfloat16, device=cuda)
+    maps = torch.empty(parts * 128, dtype=torch.uint8, device=cuda)
+    kernels.gemm_bf16_gather(bufs, rows, 1024, w, out, maps)
+    want = torch.empty_like(out)
+    kernels.gemm_bf16(torch.cat(bufs), w, kernels.GEMM_F32ACC, out=want)
+    assert torch.equal(out, want)
+    assert rel_max(out, torch.cat(bufs).float() @ w.float().t()) < 8e-3
+
+
+def test_ipc_allocation_and_handle(cuda):
+    """The shareable allocation of the fused head's parts: usable as a tensor, a 64-byte handle, freed."""
+    from torch_xdna import kernels
+
+    t, ptr = kernels.ipc_alloc((256, 1024), cuda)
+    t.copy_(torch.ones(256, 1024, dtype=torch.bfloat16, device=cuda))
+    assert t.data_ptr() == ptr and float(t.float().sum()) == 256 * 1024
+    h = kernels.ipc_handle(ptr)
+    assert len(h) == 64 and any(h)
+    del t
+    kernels.ipc_free(ptr)
+
+
 @pytest.mark.parametrize("M", [700, 8300])  # 8300: CTA pairs
 def test_gemm_bf16_residual(cuda, M):
     from torch_xdna import kernels

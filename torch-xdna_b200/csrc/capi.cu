@@ -118,6 +118,39 @@ const char* xdna_last_error(void) { return xdna::t_last_error.c_str(); }
 
 int xdna_abi_version(void) { return 1; }
 
+int xdna_ipc_alloc(size_t bytes, void** dev_ptr) {
+  XDNA_CHECK_ARG(dev_ptr != nullptr && bytes > 0, "ipc_alloc: bad arguments");
+  XDNA_CUDA(cudaMalloc(dev_ptr, bytes));
+  return XDNA_OK;
+}
+
+int xdna_ipc_free(void* dev_ptr) {
+  if (dev_ptr != nullptr) XDNA_CUDA(cudaFree(dev_ptr));
+  return XDNA_OK;
+}
+
+int xdna_ipc_handle(const void* dev_ptr, void* handle64) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  XDNA_CHECK_ARG(dev_ptr != nullptr && handle64 != nullptr, "ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  XDNA_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+  std::memcpy(handle64, &h, sizeof(h));
+  return XDNA_OK;
+}
+
+int xdna_ipc_open(const void* handle64, void** dev_ptr) {
+  XDNA_CHECK_ARG(dev_ptr != nullptr && handle64 != nullptr, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  XDNA_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return XDNA_OK;
+}
+
+int xdna_ipc_close(void* dev_ptr) {
+  if (dev_ptr != nullptr) XDNA_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+  return XDNA_OK;
+}
+
 int xdna_device_check(int device) {
   int cur = 0;
   XDNA_CUDA(cudaGetDevice(&cur));

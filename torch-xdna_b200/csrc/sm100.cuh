@@ -135,6 +135,13 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
 }
 
 // ------------------------------------------------------------------ TMA
+// A tensor map written to global memory (by a copy before this kernel) is read by TMA through the
+// tensormap proxy: acquire it before first use.
+__device__ __forceinline__ void tensormap_acquire(const CUtensorMap* map) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(reinterpret_cast<uint64_t>(map))
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

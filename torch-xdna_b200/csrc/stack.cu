@@ -15,6 +15,7 @@
 // then h = bf16(rmsnorm(x) * final_norm) and out = h Whead^T (+ bias) (GEMM, EPI_F32ACC).
 // The residual stream x stays f32 for the whole stack.
 #include <algorithm>
+#include <vector>
 
 #include "host_util.h"
 #include "umma_gemm.cuh"
@@ -114,7 +115,7 @@ static int out_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols, in
 
 // C[M, N] = A[M, K] . B[N, K]^T (bf16, f32 accumulate) with one of the stack epilogues.
 struct Bf16Gemm {
-  const void* a;
+  const void* a;  // (with a_maps: the first row block, used only to type the unused tmA)
   int64_t lda;
   const void* b;
   int64_t ldb;
@@ -132,6 +133,8 @@ struct Bf16Gemm {
   const float *rope_cos, *rope_sin, *q_norm, *k_norm;
   int seq_len;
   float eps;
+  const CUtensorMap* a_maps = nullptr;  // A split by rows over several buffers (xdna_gemm_bf16_gather)
+  int a_rows = 0;
 };
 
 static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
@@ -173,8 +176,10 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
   a.seq_len = g.seq_len;
   a.eps = g.eps;
   a.err = device_error_word();
+  a.a_maps = g.a_maps;
+  a.a_rows = g.a_rows;
   CUtensorMap ta, tb, tc;
-  if ((rc = bf16_map(&ta, g.a, g.M, g.K, g.lda, kBM, "gemm_bf16 A")) != XDNA_OK) return rc;
+  if ((rc = bf16_map(&ta, g.a, g.a_maps ? g.a_rows : g.M, g.K, g.lda, kBM, "gemm_bf16 A")) != XDNA_OK) return rc;
   if ((rc = bf16_map(&tb, g.b, g.N, g.K, g.ldb, static_cast<uint32_t>(pair ? bn / 2 : bn), "gemm_bf16 B")) != XDNA_OK)
     return rc;
   switch (g.mode) {
@@ -286,6 +291,32 @@ int xdna_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64
   Bf16Gemm g{a, lda, b, ldb, M, N, K, mode, out, out_dtype, ldo, bias, bias_dtype, resid, ldr,
              static_cast<__nv_bfloat16*>(vt), ldvt, rope_cos, rope_sin, q_norm, k_norm, static_cast<int>(seq_len), eps};
   return run_bf16_gemm(g, static_cast<cudaStream_t>(stream));
+}
+
+int xdna_gemm_bf16_gather(const void* const* a_parts, int n_parts, int64_t rows_per_part, int64_t lda, const void* b,
+                          int64_t ldb, int64_t N, int64_t K, void* out, int out_dtype, int64_t ldo, const void* bias,
+                          int bias_dtype, void* maps, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(a_parts != nullptr && n_parts >= 1 && n_parts <= 64, "gemm_bf16_gather: 1..64 parts");
+  XDNA_CHECK_ARG(rows_per_part >= kBM && rows_per_part % kBM == 0 && rows_per_part < (1ll << 31) / n_parts,
+                 "gemm_bf16_gather: rows per part must be a positive multiple of %d", kBM);
+  XDNA_CHECK_ARG(maps != nullptr && reinterpret_cast<uintptr_t>(maps) % 64 == 0,
+                 "gemm_bf16_gather: the tensor-map buffer must be 64-byte aligned device memory");
+  std::vector<CUtensorMap> host(static_cast<size_t>(n_parts));
+  for (int i = 0; i < n_parts; ++i) {
+    XDNA_CHECK_ARG(a_parts[i] != nullptr, "gemm_bf16_gather: part %d is null", i);
+    if ((rc = bf16_map(&host[i], a_parts[i], rows_per_part, K, lda, kBM, "gemm_bf16_gather part")) != XDNA_OK)
+      return rc;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // pageable source: staged before the call returns, ordered on the stream before the GEMM reads it
+  XDNA_CUDA(cudaMemcpyAsync(maps, host.data(), host.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s));
+  Bf16Gemm g{a_parts[0], lda, b, ldb, n_parts * rows_per_part, N, K, XDNA_GEMM_F32ACC, out, out_dtype, ldo, bias,
+             bias_dtype, nullptr, 0, nullptr, 0, nullptr, nullptr, nullptr, nullptr, 0, 0.f};
+  g.a_maps = static_cast<const CUtensorMap*>(maps);
+  g.a_rows = static_cast<int>(rows_per_part);
+  return run_bf16_gemm(g, s);
 }
 
 int xdna_attention(const void* qk, const void* vt, int64_t ldvt, void* out, int64_t B, int64_t L, int mask_kind,

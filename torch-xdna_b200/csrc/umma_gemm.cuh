@@ -100,6 +100,11 @@ struct GemmArgs {
   int seq_len;         // token m sits at position m % seq_len of its sequence
   float eps;
   int vt_tma;          // EPI_QKV: V^T through TMA stores (seq_len % 32 == 0)
+  // LOAD_GEMM with the A rows split over several buffers (e.g. every rank's hidden states, read over
+  // NVLink from the GPU that holds them): tensor maps in global memory, rows [i * a_rows, (i + 1) *
+  // a_rows) of A from a_maps[i]; nullptr: A is tmA
+  const CUtensorMap* a_maps;
+  int a_rows;
 };
 
 constexpr int kBM = 128;
@@ -615,6 +620,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (LOAD == LOAD_GEMM) {
+      if (args.a_maps != nullptr)
+        for (int i = 0; i * args.a_rows < args.M; ++i) tensormap_acquire(args.a_maps + i);
+    }
     if constexpr (TSTORE) tma_prefetch_desc(&tmC);
   }
   tc_fence_before();
@@ -649,7 +658,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t fb = cluster_addr(full + stage, 0);
             const int b_row = nb * BN + static_cast<int>(rank) * BROWS;  // this CTA's half of the B rows
             if constexpr (LOAD == LOAD_GEMM) {
-              tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, kb * K_ELEMS, tile_row0(mb));
+              const int ar = tile_row0(mb);
+              if (args.a_maps != nullptr)
+                tma_load_2d_pair(smA + stage * A_BYTES, args.a_maps + ar / args.a_rows, fb, kb * K_ELEMS, ar % args.a_rows);
+              else
+                tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, kb * K_ELEMS, ar);
               tma_load_2d_pair(smB + stage * B_BYTES, &tmB, fb, kb * K_ELEMS, b_row);
             } else {
               const int tap = kb / args.cblocks;
@@ -660,7 +673,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else if constexpr (LOAD == LOAD_GEMM) {
             mbar_arrive_expect_tx(full + stage, STAGE_TX);
-            tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, kb * K_ELEMS, mb * kBM);
+            if (args.a_maps != nullptr)
+              tma_load_2d(smA + stage * A_BYTES, args.a_maps + (mb * kBM) / args.a_rows, full + stage, kb * K_ELEMS,
+                          (mb * kBM) % args.a_rows);
+            else
+              tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, kb * K_ELEMS, mb * kBM);
             tma_load_2d(smB + stage * B_BYTES, &tmB, full + stage, kb * K_ELEMS, nb * BN);
           } else {
             mbar_arrive_expect_tx(full + stage, STAGE_TX);

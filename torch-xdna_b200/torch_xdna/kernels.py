@@ -65,6 +65,12 @@ def _load():
         "xdna_embed": ([P, I64, P, I, I64, I64, P, P], I),
         "xdna_gemm_bf16": ([P, I64, P, I64, I64, I64, I64, I, P, I, I64, P, I, P, I64, P, I64, P, P, P, P, I64,
                             ctypes.c_float, P], I),
+        "xdna_gemm_bf16_gather": ([P, I, I64, I64, P, I64, I64, I64, P, I, I64, P, I, P, P], I),
+        "xdna_ipc_alloc": ([ctypes.c_size_t, P], I),
+        "xdna_ipc_free": ([P], I),
+        "xdna_ipc_handle": ([P, P], I),
+        "xdna_ipc_open": ([P, P], I),
+        "xdna_ipc_close": ([P], I),
         "xdna_attention": ([P, P, I64, P, I64, I64, I, P, P, I, P], I),
         "xdna_qwen3_stack_workspace": ([I64, I64], ctypes.c_size_t),
         "xdna_qwen3_stack": ([P, I, P, P, I64, P, I, P, P, ctypes.c_float, P, I64, I64, I, P, P, I, P, I, I64, P,
@@ -268,6 +274,66 @@ def gemm_bf16(a, b, mode, out=None, bias=None, resid=None, vt=None, rope_cos=Non
         _p(bias), DTYPE_CODES[bias.dtype] if bias is not None else F32, _p(resid),
         resid.stride(0) if resid is not None else 0, _p(vt), vt.stride(0) if vt is not None else 0,
         _p(rope_cos), _p(rope_sin), _p(q_norm), _p(k_norm), seq_len, eps, _stream()))
+
+
+def gemm_bf16_gather(parts, rows_per_part, lda, b, out, maps, bias=None):
+    """out = A . b^T with the head epilogue, A the row-concatenation of `parts` (device pointers, possibly
+    on peer GPUs, each [rows_per_part, K] bf16 with row pitch lda); maps: a device buffer of at least
+    128 * len(parts) bytes, 64-byte aligned (xdna_gemm_bf16_gather)."""
+    L = require()
+    _cuda(b, out, maps, bias)
+    arr = (ctypes.c_void_p * len(parts))(*[p if isinstance(p, int) else p.data_ptr() for p in parts])
+    N, K = b.shape
+    _check("xdna_gemm_bf16_gather", L.xdna_gemm_bf16_gather(
+        ctypes.cast(arr, ctypes.c_void_p), len(parts), rows_per_part, lda, _p(b), b.stride(0), N, K, _p(out),
+        DTYPE_CODES[out.dtype], out.stride(0), _p(bias), DTYPE_CODES[bias.dtype] if bias is not None else F32,
+        _p(maps), _stream()))
+
+
+class _CudaArray:
+    """A zero-copy view of raw device memory for torch.as_tensor (__cuda_array_interface__)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3}
+
+
+def ipc_alloc(shape, device):
+    """A bf16 tensor on `device` in its own shareable allocation (xdna_ipc_alloc); free with ipc_free."""
+    L = require()
+    ptr = ctypes.c_void_p()
+    numel = 1
+    for d in shape:
+        numel *= d
+    with torch.cuda.device(device):
+        _check("xdna_ipc_alloc", L.xdna_ipc_alloc(numel * 2, ctypes.byref(ptr)))
+    return device_view(ptr.value, shape, device), ptr.value
+
+
+def device_view(ptr, shape, device):
+    """A bf16 tensor over existing device memory at `ptr` (e.g. a peer GPU's buffer opened with ipc_open)."""
+    with torch.cuda.device(device):
+        return torch.as_tensor(_CudaArray(ptr, shape, "<i2"), device=device).view(torch.bfloat16)
+
+
+def ipc_free(ptr):
+    _check("xdna_ipc_free", require().xdna_ipc_free(ctypes.c_void_p(ptr)))
+
+
+def ipc_handle(ptr) -> bytes:
+    buf = ctypes.create_string_buffer(64)
+    _check("xdna_ipc_handle", require().xdna_ipc_handle(ctypes.c_void_p(ptr), buf))
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    _check("xdna_ipc_open", require().xdna_ipc_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(ptr)))
+    return ptr.value
+
+
+def ipc_close(ptr):
+    _check("xdna_ipc_close", require().xdna_ipc_close(ctypes.c_void_p(ptr)))
 
 
 def attention(qk, vt, out, B, L_, mask_kind, lens=None, mask=None):

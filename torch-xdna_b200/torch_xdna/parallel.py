@@ -65,3 +65,88 @@ def gather_rows(local: torch.Tensor, out: torch.Tensor, group=None) -> torch.Ten
     assert out.shape[0] == local.shape[0] * dist.get_world_size(group) and out.shape[1:] == local.shape[1:]
     dist.all_gather_into_tensor(out, local.contiguous(), group=group)
     return out
+
+
+class RowGather:
+    """Every rank's [rows, cols] bf16 buffer as the row-concatenated A operand of the column-parallel head
+    GEMM, gathered and multiplied in one pipeline instead of an all-gather followed by a GEMM.
+
+    Each rank's buffer is a shareable allocation whose peers map it through CUDA IPC (NVLink). gemm():
+      - "pipelined" (default): the GEMM over this rank's own rows starts at once; meanwhile a copy engine
+        brings every peer's block across NVLink exactly once, in ring order, into local staging, and the
+        GEMM over each peer's rows starts as soon as its block has landed (copies overlap the math);
+      - "direct": one GEMM whose TMA producer reads the peers' rows straight from their memory
+        (xdna_gemm_bf16_gather). Every column tile re-reads its A rows, and remote rows do not stay in
+        this GPU's L2, so each remote row crosses NVLink once per column tile: correct, but slower.
+    `local` is this rank's buffer; write it, then call gemm() on every rank in the same order (it brackets
+    the work with two one-element all-reduces, the device-side barriers that order every rank's writes of
+    `local` before the peers read it, and the reads before the next writes)."""
+
+    def __init__(self, rows: int, cols: int, device, group=None, mode: str = "pipelined"):
+        import torch.distributed as dist
+
+        from . import kernels
+
+        assert mode in ("pipelined", "direct")
+        self.group, self.mode = group, mode
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.rows, self.cols = rows, cols
+        self.local, self._ptr = kernels.ipc_alloc((rows, cols), device)
+        mine = torch.frombuffer(bytearray(kernels.ipc_handle(self._ptr)), dtype=torch.uint8).to(device)
+        everyone = torch.empty(self.world * 64, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(everyone, mine, group=group)
+        handles = everyone.cpu().numpy().tobytes()
+        self.ptrs = [self._ptr if r == self.rank else kernels.ipc_open(handles[64 * r:64 * (r + 1)])
+                     for r in range(self.world)]
+        self.peers = [kernels.device_view(p, (rows, cols), device) if r != self.rank else self.local
+                      for r, p in enumerate(self.ptrs)]
+        self.staged = {r: torch.empty(rows, cols, dtype=torch.bfloat16, device=device)
+                       for r in range(self.world) if r != self.rank} if mode == "pipelined" else {}
+        self.maps = torch.empty(self.world * 128, dtype=torch.uint8, device=device)   # allocator blocks: 512-aligned
+        self._copy = torch.cuda.Stream(device)
+        self._landed = {r: torch.cuda.Event() for r in self.staged}
+        self._flag = torch.zeros(1, device=device)
+
+    def gemm(self, w: torch.Tensor, out: torch.Tensor, bias=None) -> torch.Tensor:
+        """out [world * rows, N] = (all ranks' `local`, in rank order) . w^T, w [N, cols]."""
+        import torch.distributed as dist
+
+        from . import kernels
+
+        dist.all_reduce(self._flag, group=self.group)        # every rank's `local` is written
+        if self.mode == "direct":
+            kernels.gemm_bf16_gather(self.ptrs, self.rows, self.cols, w, out, self.maps, bias)
+        else:
+            cur = torch.cuda.current_stream()
+            self._copy.wait_stream(cur)
+            with torch.cuda.stream(self._copy):              # every peer block crosses NVLink once
+                for k in range(1, self.world):
+                    r = (self.rank + k) % self.world
+                    self.staged[r].copy_(self.peers[r], non_blocking=True)
+                    self._landed[r].record(self._copy)
+            rows = self.rows
+            kernels.gemm_bf16(self.local, w, kernels.GEMM_F32ACC, out=out[self.rank * rows:(self.rank + 1) * rows],
+                              bias=bias)
+            for k in range(1, self.world):
+                r = (self.rank + k) % self.world
+                cur.wait_event(self._landed[r])
+                kernels.gemm_bf16(self.staged[r], w, kernels.GEMM_F32ACC, out=out[r * rows:(r + 1) * rows],
+                                  bias=bias)
+        dist.all_reduce(self._flag, group=self.group)        # every rank has read them
+        return out
+
+    def close(self):
+        import torch.distributed as dist
+
+        from . import kernels
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.peers = None
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                kernels.ipc_close(p)
+        dist.barrier(group=self.group)                       # no peer still maps `local`
+        self.local = None
+        kernels.ipc_free(self._ptr)
