@@ -11,10 +11,11 @@
 //                 overlaps the MMAs of tile i+1;
 //   warps 2..9    epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (its 32 output rows) and one half
 //                 of the tile's columns, 32 columns per tcgen05.ld, issued one chunk ahead of the
-//                 arithmetic. Per-column factors arrive once per tile as one coalesced load per lane
-//                 and are broadcast with warp shuffles. GEMM outputs are staged in swizzled shared
-//                 memory (two 2 KB slots per warp, used in turn) and written by TMA bulk-tensor stores (full lines, tails
-//                 clipped by the tensor map); conv outputs (NCHW scatter) use direct stores.
+//                 arithmetic. Per-column factors arrive once per tile as one coalesced load per lane,
+//                 then sit in the warp's shared memory (dequantising epilogues) or are broadcast with
+//                 warp shuffles. GEMM outputs are staged in swizzled shared memory (2 KB slots) and
+//                 written by TMA bulk-tensor stores (full lines, tails clipped by the tensor map); conv
+//                 outputs are staged per pixel and written as whole lines with direct stores.
 //
 // The A operand is either a plain row-major matrix (LOAD_GEMM) or, for the conv, the
 // zero-bordered NHWC activations viewed as a [pixels, Cp] matrix: the K loop runs over 9 taps x
@@ -121,15 +122,27 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
-// Operand stages in 192 KB (4 / 6 / 8 for BN = 256 / 128 / 64 with 128-byte K blocks), at most 12.
-template <int BN, int KB = kBKBytes>
+// Operand stages in 224 KB less the epilogue's staging (8 x OUTB), at most 12: with 4 KB per epilogue
+// warp 4 / 6 / 8 stages for BN = 256 / 128 / 64 and 128-byte K blocks.
+template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes>
 __host__ __device__ constexpr int stages_for() {
-  return (192 * 1024) / ((kBM + BN) * KB) < 12 ? (192 * 1024) / ((kBM + BN) * KB) : 12;
+  return (224 * 1024 - kEpiWarps * OUTB) / ((kBM + BN) * KB) < 12 ? (224 * 1024 - kEpiWarps * OUTB) / ((kBM + BN) * KB)
+                                                                   : 12;
 }
 
-template <int BN, int KB = kBKBytes>
+template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes>
 __host__ __device__ constexpr int smem_bytes_for() {
-  return stages_for<BN, KB>() * (kBM + BN) * KB + kEpiWarps * kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;
+  return stages_for<BN, KB, OUTB>() * (kBM + BN) * KB + kEpiWarps * OUTB + 1024 /*align*/ + 256 /*barriers*/;
+}
+
+// Shared memory per epilogue warp: 8 KB where the epilogue keeps the tile's column factors (and, for
+// the conv, its pixels' output offsets) beside the staging, as long as the operand ring keeps at least
+// 5 stages; 4 KB otherwise (factors then come by warp shuffles).
+template <int BROWS, int KB, int EPI, bool PAIR>
+__host__ __device__ constexpr int stage_out_bytes() {
+  return ((EPI == EPI_CONV_DEQ || (PAIR && EPI == EPI_DEQ)) && stages_for<BROWS, KB, 8192>() >= 5)
+             ? 8192
+             : kStageOutBytes;
 }
 
 // Tiles of M rows per CTA (pair) and whether a GEMM of m_tiles128 128-row tiles x n_tiles 256-column
@@ -429,6 +442,84 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
   }
 }
 
+// EPI_CONV_DEQ for a full chunk of 32 channels (one pixel per lane), with the tile's channel scales
+// and biases in this warp's shared memory (every lane reads the same 16 bytes, a broadcast). The
+// requantise runs in integers; the int -> float conversion of q (|q| <= 255) is exact through the
+// 1.5 * 2^23 bias: the bit pattern 0x4B400000 + q is the float 12582912 + q, from which 12582912 is
+// subtracted exactly. Products and sums are packed f32x2 with the rounding of __fmul_rn / __fadd_rn:
+// y = q * (scale[co] * s) (+ bias[co]) (then y > 0 ? y : 0), as conv_chunk computes.
+// The 32 values are staged per pixel in swizzled rows, then the warp writes whole 128-byte lines with
+// 16-byte stores, each pixel's output offset (-1: a border pixel) read from the tile's table.
+__device__ __forceinline__ void conv_deq_smem(const GemmArgs& a, float s, int n0, const uint32_t (&r)[32],
+                                              const float* scale, const float* bias, const long long* pix_off,
+                                              uint8_t* stage) {
+  const int lane = lane_id();
+  const int shift = a.shift;
+  const int rnd = 1 << (shift - 1);
+  const int lo = a.relu ? 0 : -128;
+  const int hi = a.relu ? 255 : 127;
+  const float2 s2 = make_float2(s, s);
+  const float2 unbias = make_float2(-12582912.f, -12582912.f);
+  const bool has_bias = a.bias != nullptr;
+  const bool relu_after = a.post_relu != 0;
+  // four values (channels 4g .. 4g+3) at a time, staged as soon as they are done
+  auto dq4 = [&](int g) {
+    const float4 f = reinterpret_cast<const float4*>(scale)[g];
+    int t[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      t[i] = min(max((static_cast<int>(r[4 * g + i]) + rnd) >> shift, lo), hi) + 0x4B400000;
+    float2 a0 = __fadd2_rn(make_float2(__int_as_float(t[0]), __int_as_float(t[1])), unbias);
+    float2 a1 = __fadd2_rn(make_float2(__int_as_float(t[2]), __int_as_float(t[3])), unbias);
+    a0 = __fmul2_rn(a0, __fmul2_rn(make_float2(f.x, f.y), s2));
+    a1 = __fmul2_rn(a1, __fmul2_rn(make_float2(f.z, f.w), s2));
+    if (has_bias) {  // warp-uniform
+      const float4 b = reinterpret_cast<const float4*>(bias)[g];
+      a0 = __fadd2_rn(a0, make_float2(b.x, b.y));
+      a1 = __fadd2_rn(a1, make_float2(b.z, b.w));
+    }
+    float4 o = make_float4(a0.x, a0.y, a1.x, a1.y);
+    if (relu_after) {  // y > 0 ? y : 0 on the bits: positive floats are positive integers
+      o.x = __int_as_float(max(__float_as_int(o.x), 0));
+      o.y = __int_as_float(max(__float_as_int(o.y), 0));
+      o.z = __int_as_float(max(__float_as_int(o.z), 0));
+      o.w = __int_as_float(max(__float_as_int(o.w), 0));
+    }
+    return o;
+  };
+  const bool f32 = a.out_dtype == XDNA_F32;
+  uint4* row = reinterpret_cast<uint4*>(stage) + lane * 8;
+  if (f32) {
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const float4 o = dq4(g);
+      row[g ^ (lane & 7)] = make_uint4(__float_as_uint(o.x), __float_as_uint(o.y), __float_as_uint(o.z), __float_as_uint(o.w));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 o0 = dq4(2 * j);
+      const float4 o1 = dq4(2 * j + 1);
+      row[j ^ (lane & 7)] = make_uint4(pack2(o0.x, o0.y, a.out_dtype), pack2(o0.z, o0.w, a.out_dtype),
+                                       pack2(o1.x, o1.y, a.out_dtype), pack2(o1.z, o1.w, a.out_dtype));
+    }
+  }
+  __syncwarp();
+  const int lg = f32 ? 3 : 2;  // log2 of the 16-byte chunks per pixel
+  const int es = f32 ? 4 : 2;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    if (it < (1 << lg)) {  // warp-uniform
+      const int pi = (it << (5 - lg)) + (lane >> lg);  // the pixel whose chunk this lane writes
+      const int ch = lane & ((1 << lg) - 1);
+      const long long off = pix_off[pi];
+      const uint4 val = reinterpret_cast<const uint4*>(stage)[pi * 8 + (ch ^ (pi & 7))];
+      if (off >= 0) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.out) + (off + n0) * es + ch * 16) = val;
+    }
+  }
+  __syncwarp();
+}
+
 // --------------------------------------------------------------------------- stack epilogues (bf16)
 __device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u); }
 
@@ -559,7 +650,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
   static_assert(!PAIR || (BN == 256 && KB == 128), "CTA pairs: 256 x 256 tiles of 128-byte K blocks");
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (tile columns) this CTA loads
-  constexpr int STAGES = stages_for<BROWS, KB>();
+  constexpr int OUTB = stage_out_bytes<BROWS, KB, EPI, PAIR>();
+  constexpr int STAGES = stages_for<BROWS, KB, OUTB>();
   constexpr int A_BYTES = kBM * KB;
   constexpr int B_BYTES = BROWS * KB;
   constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (A_BYTES + B_BYTES);  // a pair's stage: both CTAs' bytes
@@ -576,8 +668,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * A_BYTES;
-  uint8_t* smOut = smB + STAGES * B_BYTES;  // kEpiWarps x kStageOutBytes, 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(smOut + kEpiWarps * kStageOutBytes);
+  uint8_t* smOut = smB + STAGES * B_BYTES;  // kEpiWarps x OUTB, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(smOut + kEpiWarps * OUTB);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -774,13 +866,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;
     const int q = warp & 3;          // the TMEM lane quadrant this warp may read
     const int half = ew >> 2;        // which half of the tile's columns
-    uint8_t* obuf = smOut + ew * kStageOutBytes;
-    // EPI_DEQ through TMA: one staging slot, and the second 2 KB holds the tile's column factors
-    constexpr bool kSmemFactors = EPI == EPI_DEQ && TSTORE;
-    StageRing ring{obuf, 0, kSmemFactors ? 1 : 2};
-    float* col_sw = reinterpret_cast<float*>(obuf + kStageSlotBytes);  // [WCOLS]
-    float* col_bias = col_sw + WCOLS;                                    // [WCOLS]
-    static_assert(!kSmemFactors || 2 * WCOLS * 4 <= kStageOutBytes - kStageSlotBytes, "factor area");
+    uint8_t* obuf = smOut + ew * OUTB;
+    // The tile's column factors in shared memory: EPI_DEQ through TMA (with 4 KB per warp one staging
+    // slot and the factors in the second 2 KB; with 8 KB two slots and the factors behind them) and
+    // EPI_CONV_DEQ with 8 KB (4 KB of staging, the factors, then the 32 pixels' output offsets).
+    constexpr bool kConvRows = EPI == EPI_CONV_DEQ && OUTB == 8192;
+    constexpr bool kSmemFactors = (EPI == EPI_DEQ && TSTORE) || kConvRows;
+    constexpr int kFactorOff = OUTB == 8192 ? 4096 : kStageSlotBytes;
+    StageRing ring{obuf, 0, (EPI == EPI_DEQ && TSTORE && OUTB == kStageOutBytes) ? 1 : 2};
+    float* col_sw = reinterpret_cast<float*>(obuf + kFactorOff);          // [WCOLS]
+    float* col_bias = col_sw + WCOLS;                                      // [WCOLS]
+    long long* pix_off = reinterpret_cast<long long*>(col_bias + WCOLS);  // kConvRows: [32]
+    static_assert(!kSmemFactors || kFactorOff + 2 * WCOLS * 4 + 32 * 8 <= OUTB, "factor area");
     // hand an accumulator back to the MMA issuer (in a pair: the even CTA's, for both CTAs' warps)
     auto release_accumulator = [](uint64_t* bar) {
       if constexpr (PAIR)
@@ -847,6 +944,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           col_sw[c * 32 + lane] = fcol[c];
           col_bias[c * 32 + lane] = bcol[c];
         }
+        if constexpr (kConvRows)  // out[img, yp-1, xp-1, 0] of this lane's pixel (channels-last), -1: border
+          pix_off[lane] = px.valid ? ((static_cast<long long>(px.img) * args.H + (px.yp - 1)) * args.W + (px.xp - 1)) *
+                                         args.N
+                                   : -1ll;
         __syncwarp();
       }
 
@@ -960,6 +1061,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                   if (j < nv) res[j] += f32_of(rc[j]);
               }
             }
+          } else if constexpr (kConvRows) {
+            if (n0 + 32 <= args.N && args.vec_ok)  // warp-uniform
+              conv_deq_smem(args, px.s, n0, rc, col_sw + c * 32, col_bias + c * 32, pix_off, obuf);
+            else
+              conv_chunk<EPI>(args, px, n0, rc, col_sw[c * 32 + lane], col_bias[c * 32 + lane], nullptr);
           } else {
             conv_chunk<EPI>(args, px, n0, rc, fcol[c], bcol[c], obuf);
           }
@@ -999,7 +1105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB, bool PAIR>
 static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                               const CUtensorMap& td, const GemmArgs& args, int sms, cudaStream_t stream) {
-  constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB>();
+  constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB, stage_out_bytes<PAIR ? BN / 2 : BN, KB, EPI, PAIR>()>();
   auto kern = umma_gemm_kernel<BN, LOAD, EPI, BF16, TSTORE, ODT, KB, PAIR>;
   static bool configured[64] = {};  // per instantiation and device
   static int max_pairs[64] = {};
