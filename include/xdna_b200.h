@@ -196,8 +196,8 @@ int xdna_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64
  * TMA producer over NVLink while the tensor cores run, instead of a separate all-gather. rows_per_part
  * must be a multiple of 256. maps: device memory for n_parts tensor maps (128 bytes each, 64-byte
  * aligned), written by this call (stream-ordered). The caller orders the parts' writes before this call
- * on every GPU (e.g. a barrier collective). Replaces the all-gather + head of SURVEY §8e's column-parallel
- * head, which the reference (single device) does not have. */
+ * on every GPU (e.g. a barrier collective). Replaces the all-gather followed by the head GEMM of the
+ * column-parallel head on several GPUs, which the reference (one device) does not have. */
 int xdna_gemm_bf16_gather(const void* const* a_parts, int n_parts, int64_t rows_per_part, int64_t lda, const void* b,
                           int64_t ldb, int64_t N, int64_t K, void* out, int out_dtype, int64_t ldo, const void* bias,
                           int bias_dtype, void* maps, void* stream);

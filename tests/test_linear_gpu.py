@@ -96,6 +96,8 @@ GEMM_SHAPES = [
     (1000, 1000, 1000), (2048, 6144, 1024), (512, 1024, 3072), (4096, 4096, 4096),
     # 256 x 256 tiles on CTA pairs, with a ragged last pair (odd CTA partly / wholly past M)
     (2300, 6144, 1024), (1100, 8192, 512),
+    # CTA pairs with a ragged last column tile (columns 3840..3999 of its 256)
+    (4096, 4000, 384),
 ]
 
 
@@ -129,7 +131,8 @@ def test_gemm_int32_extremes(cuda):
 
 @pytest.mark.parametrize("out", ["float32", "bfloat16", "float16"])
 @pytest.mark.parametrize("bias", [False, True])
-@pytest.mark.parametrize("M,N,K", [(37, 300, 200), (512, 3072, 1024), (257, 136, 64), (1100, 8192, 512)])
+@pytest.mark.parametrize("M,N,K", [(37, 300, 200), (512, 3072, 1024), (257, 136, 64), (1100, 8192, 512),
+                                   (4096, 4000, 384)])
 def test_gemm_dequant_bitexact(cuda, out, bias, M, N, K):
     x, w, b = mg.linear_inputs(M * 3 + N, M, K, N, bias=True)
     xq, sx = orc.quant_rows(x)
