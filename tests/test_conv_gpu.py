@@ -53,7 +53,7 @@ def test_conv_op_matches_reference_digests(cuda, golden, name):
 @pytest.mark.parametrize("relu", [False, True])
 @pytest.mark.parametrize("n,ci,co,h,w", [(1, 256, 256, 64, 64), (2, 3, 64, 13, 37), (2, 64, 48, 13, 37),
                                          (1, 16, 16, 1, 1), (3, 130, 20, 7, 129), (1, 512, 512, 14, 14),
-                                         (2, 64, 64, 224, 224),
+                                         (2, 64, 64, 224, 224), (2, 40, 128, 17, 23), (1, 64, 200, 16, 16),
                                          # 256 x 256 tiles on CTA pairs (the second: ragged Co and channel block)
                                          (8, 128, 256, 56, 56), (5, 160, 300, 40, 52)])
 def test_conv_q_bitexact_vs_oracle(cuda, relu, n, ci, co, h, w):
@@ -72,7 +72,9 @@ def test_conv_q_bitexact_vs_oracle(cuda, relu, n, ci, co, h, w):
 
 @pytest.mark.parametrize("post_relu", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("n,ci,co,h,w", [(2, 96, 80, 30, 50), (5, 160, 300, 40, 52)])  # the second: CTA pairs
+# (2, 64, 64, ...) and (3, 40, 128, ...): weights resident in shared memory; (5, 160, 300, ...): CTA pairs
+@pytest.mark.parametrize("n,ci,co,h,w", [(2, 96, 80, 30, 50), (5, 160, 300, 40, 52), (2, 64, 64, 30, 50),
+                                         (3, 40, 128, 21, 19)])
 def test_conv_fused_dequant_bitexact(cuda, dtype, post_relu, n, ci, co, h, w):
     """The dequantise (+ bias) to x.dtype, bit for bit; post_relu equals torch.relu of it."""
     x, wt, b = mg.conv_inputs(5, n, ci, co, h, w, bias=True)

@@ -33,7 +33,14 @@ static int dispatch_bn(int bn, bool pair, const CUtensorMap& ta, const CUtensorM
 template <int EPI, int ODT>
 static int dispatch_conv(int kb, int bn, bool pair, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
                          int sms, cudaStream_t stream) {
-  if (kb == 64) return dispatch_bn<LOAD_CONV, EPI, false, ODT, 64>(bn, false, ta, tb, ta, args, sms, stream);
+  if (kb == 64) {
+    // one column tile of <= 128 output channels: the 9 taps' weights stay in shared memory
+    if (args.n_tiles == 1 && args.cblocks == 1 && bn <= 128) {
+      if (bn == 128) return launch_umma<128, LOAD_CONV_RB, EPI, false, ODT, 64>(ta, tb, ta, args, sms, stream);
+      return launch_umma<64, LOAD_CONV_RB, EPI, false, ODT, 64>(ta, tb, ta, args, sms, stream);
+    }
+    return dispatch_bn<LOAD_CONV, EPI, false, ODT, 64>(bn, false, ta, tb, ta, args, sms, stream);
+  }
   return dispatch_bn<LOAD_CONV, EPI, false, ODT, 128>(bn, pair, ta, tb, ta, args, sms, stream);
 }
 

@@ -28,7 +28,10 @@
 
 namespace xdna {
 
-enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1 };
+// LOAD_CONV_RB: the conv with its weights resident in shared memory for the whole kernel (one channel
+// block of <= 64 channels, one column tile of <= 128 output channels): each stage then holds only the
+// activation rows, which halves the TMA row requests per stage when rows are 64 bytes.
+enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1, LOAD_CONV_RB = 2 };
 
 enum EpiMode {
   EPI_I32 = 0,         // int32 accumulators
@@ -122,25 +125,37 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
-// Operand stages in 224 KB less the epilogue's staging (8 x OUTB), at most 12: with 4 KB per epilogue
-// warp 4 / 6 / 8 stages for BN = 256 / 128 / 64 and 128-byte K blocks.
-template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes>
-__host__ __device__ constexpr int stages_for() {
-  return (224 * 1024 - kEpiWarps * OUTB) / ((kBM + BN) * KB) < 12 ? (224 * 1024 - kEpiWarps * OUTB) / ((kBM + BN) * KB)
-                                                                   : 12;
+// Operand bytes per stage (RB: A only, the weights are resident) and of the resident weights (9 taps).
+template <int BN, int KB, bool RB>
+__host__ __device__ constexpr int stage_bytes() {
+  return (kBM + (RB ? 0 : BN)) * KB;
+}
+template <int BN, int KB, bool RB>
+__host__ __device__ constexpr int resident_bytes() {
+  return RB ? 9 * BN * KB : 0;
 }
 
-template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes>
+// Operand stages in 224 KB less the epilogue's staging (8 x OUTB) and any resident weights, at most 12:
+// with 4 KB per epilogue warp 4 / 6 / 8 stages for BN = 256 / 128 / 64 and 128-byte K blocks.
+template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes, bool RB = false>
+__host__ __device__ constexpr int stages_for() {
+  return (224 * 1024 - kEpiWarps * OUTB - resident_bytes<BN, KB, RB>()) / stage_bytes<BN, KB, RB>() < 12
+             ? (224 * 1024 - kEpiWarps * OUTB - resident_bytes<BN, KB, RB>()) / stage_bytes<BN, KB, RB>()
+             : 12;
+}
+
+template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes, bool RB = false>
 __host__ __device__ constexpr int smem_bytes_for() {
-  return stages_for<BN, KB, OUTB>() * (kBM + BN) * KB + kEpiWarps * OUTB + 1024 /*align*/ + 256 /*barriers*/;
+  return stages_for<BN, KB, OUTB, RB>() * stage_bytes<BN, KB, RB>() + resident_bytes<BN, KB, RB>() + kEpiWarps * OUTB +
+         1024 /*align*/ + 256 /*barriers*/;
 }
 
 // Shared memory per epilogue warp: 8 KB where the epilogue keeps the tile's column factors (and, for
 // the conv, its pixels' output offsets) beside the staging, as long as the operand ring keeps at least
 // 5 stages; 4 KB otherwise (factors then come by warp shuffles).
-template <int BROWS, int KB, int EPI, bool PAIR>
+template <int BROWS, int KB, int EPI, bool PAIR, bool RB = false>
 __host__ __device__ constexpr int stage_out_bytes() {
-  return ((EPI == EPI_CONV_DEQ || (PAIR && EPI == EPI_DEQ)) && stages_for<BROWS, KB, 8192>() >= 5)
+  return ((EPI == EPI_CONV_DEQ || (PAIR && EPI == EPI_DEQ)) && stages_for<BROWS, KB, 8192, RB>() >= 5)
              ? 8192
              : kStageOutBytes;
 }
@@ -649,12 +664,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const GemmArgs args) {
   static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
   static_assert(!PAIR || (BN == 256 && KB == 128), "CTA pairs: 256 x 256 tiles of 128-byte K blocks");
+  constexpr bool RB = LOAD == LOAD_CONV_RB;   // conv weights resident in shared memory
+  constexpr bool kConv = LOAD != LOAD_GEMM;
+  static_assert(!RB || (!PAIR && KB == 64 && BN <= 128), "resident conv weights: one 64-byte channel block, BN <= 128");
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (tile columns) this CTA loads
-  constexpr int OUTB = stage_out_bytes<BROWS, KB, EPI, PAIR>();
-  constexpr int STAGES = stages_for<BROWS, KB, OUTB>();
+  constexpr int OUTB = stage_out_bytes<BROWS, KB, EPI, PAIR, RB>();
+  constexpr int STAGES = stages_for<BROWS, KB, OUTB, RB>();
   constexpr int A_BYTES = kBM * KB;
-  constexpr int B_BYTES = BROWS * KB;
-  constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (A_BYTES + B_BYTES);  // a pair's stage: both CTAs' bytes
+  constexpr int B_BYTES = BROWS * KB;        // one K block of B (one tap, for the conv)
+  constexpr int B_STAGE = RB ? 0 : B_BYTES;  // B bytes in each ring stage
+  constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (A_BYTES + B_STAGE);  // a pair's stage: both CTAs' bytes
   constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
   constexpr int MMA_M = PAIR ? 2 * kBM : kBM;
   constexpr uint32_t IDESC = BF16 ? idesc_bf16(MMA_M, BN) : idesc_i8(MMA_M, BN);
@@ -668,13 +687,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * A_BYTES;
-  uint8_t* smOut = smB + STAGES * B_BYTES;  // kEpiWarps x OUTB, 1024-aligned
+  uint8_t* smRes = smB + STAGES * B_STAGE;  // RB: the 9 taps' weights, B_BYTES each
+  uint8_t* smOut = smRes + resident_bytes<BROWS, KB, RB>();  // kEpiWarps x OUTB, 1024-aligned
   uint64_t* full = reinterpret_cast<uint64_t*>(smOut + kEpiWarps * OUTB);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* bres = drain + 1;  // RB: the resident weights have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres + 1);
+  static_assert((2 * STAGES + 6) * 8 + 8 <= 256, "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -697,6 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(tempty + b, PAIR ? 2 * kEpiWarps : kEpiWarps);  // a pair: both CTAs' epilogue warps
     }
     mbar_init(drain, 1);
+    mbar_init(bres, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -736,6 +759,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
       bool ok = true;
+      if constexpr (RB) {  // the weights of all 9 taps, once
+        if (t_first < total) {
+          mbar_arrive_expect_tx(bres, 9 * B_BYTES);
+          for (int tap = 0; tap < 9; ++tap) tma_load_3d(smRes + tap * B_BYTES, &tmB, bres, 0, tap, 0);
+        }
+      }
       for (int t = t_first; t < total && ok; t += t_step) {
         int mb, nb;
         tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
@@ -778,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int dy = tap / 3 - 1;
             const int dx = tap % 3 - 1;
             tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, cb * K_ELEMS, mb * kBM + dy * args.Wp + dx);
-            tma_load_3d(smB + stage * B_BYTES, &tmB, full + stage, cb * K_ELEMS, tap, nb * BN);
+            if constexpr (!RB) tma_load_3d(smB + stage * B_BYTES, &tmB, full + stage, cb * K_ELEMS, tap, nb * BN);
           }
           last_parity[stage] = static_cast<int>(phase);
           if (++stage == STAGES) {
@@ -795,6 +824,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           volatile int never = 0;
           mbar_wait(full + s, static_cast<uint32_t>(last_parity[s]), &never, args.err, 2);
         }
+      if constexpr (RB) {
+        if (t_first < total) {
+          volatile int never = 0;
+          mbar_wait(bres, 0, &never, args.err, 2);
+        }
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
@@ -805,6 +840,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t bphase = 0;
       bool issued = false;
       bool ok = true;
+      if constexpr (RB) {
+        if (t_first < total && !mbar_wait(bres, 0, abort_flag, args.err, 4)) ok = false;
+      }
       for (int t = t_first; t < total && ok; t += t_step) {
         if (!mbar_wait<PAIR>(tempty + buf, bphase ^ 1, abort_flag, args.err, 3)) break;
         tc_fence_after();
@@ -817,8 +855,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint64_t da = KB == 128 ? smem_desc_k_sw128(smem_u32(smA + stage * A_BYTES))
                                         : smem_desc_k_sw64(smem_u32(smA + stage * A_BYTES));
-          const uint64_t db = KB == 128 ? smem_desc_k_sw128(smem_u32(smB + stage * B_BYTES))
-                                        : smem_desc_k_sw64(smem_u32(smB + stage * B_BYTES));
+          // RB: one channel block, so K block kb is tap kb
+          uint8_t* const b_src = RB ? smRes + kb * B_BYTES : smB + stage * B_BYTES;
+          const uint64_t db = KB == 128 ? smem_desc_k_sw128(smem_u32(b_src)) : smem_desc_k_sw64(smem_u32(b_src));
 #pragma unroll
           for (int k = 0; k < KSTEPS; ++k) {
             const uint32_t acc = (kb | k) != 0;
@@ -918,7 +957,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if constexpr (EPI == EPI_DEQ) f.srow = row < args.M ? __ldg(args.sx + row) : 0.f;
-      if constexpr (LOAD == LOAD_CONV) f.px = conv_pixel<EPI>(args, row);
+      if constexpr (kConv) f.px = conv_pixel<EPI>(args, row);
       return f;
     };
     Factors fac{};
@@ -984,7 +1023,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int n0 = col0 + c * 32;
         // warp-uniform: this chunk has columns in range (and, for GEMM outputs, rows in range)
-        if (n0 < args.N && (LOAD == LOAD_CONV || row0 < args.M)) {
+        if (n0 < args.N && (kConv || row0 < args.M)) {
           const uint32_t(&rc)[32] = r[c & 1];
           if constexpr (EPI == EPI_I32 || EPI == EPI_DEQ) {
             if constexpr (TSTORE) {
@@ -1105,7 +1144,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB, bool PAIR>
 static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                               const CUtensorMap& td, const GemmArgs& args, int sms, cudaStream_t stream) {
-  constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB, stage_out_bytes<PAIR ? BN / 2 : BN, KB, EPI, PAIR>()>();
+  constexpr bool RB = LOAD == LOAD_CONV_RB;
+  constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB, stage_out_bytes<PAIR ? BN / 2 : BN, KB, EPI, PAIR, RB>(), RB>();
   auto kern = umma_gemm_kernel<BN, LOAD, EPI, BF16, TSTORE, ODT, KB, PAIR>;
   static bool configured[64] = {};  // per instantiation and device
   static int max_pairs[64] = {};
