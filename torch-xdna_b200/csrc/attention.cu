@@ -97,10 +97,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
-  // heaviest causal blocks first
-  const int qb = KIND == MASK_CAUSAL ? args.q_blocks - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
-  const int kvh = blockIdx.y;                // key/value head; query heads 2 kvh and 2 kvh + 1
-  const int seq = blockIdx.z;
+  // CTAs start in launch order (x fastest, z slowest): the query block is z, so for causal masks every
+  // (head, sequence) of the last query block (the most key blocks) goes first, the lightest last
+  const int qb = KIND == MASK_CAUSAL ? args.q_blocks - 1 - static_cast<int>(blockIdx.z) : static_cast<int>(blockIdx.z);
+  const int kvh = blockIdx.x;                // key/value head; query heads 2 kvh and 2 kvh + 1
+  const int seq = blockIdx.y;
   const int q0 = qb * 128;                 // first query position in the sequence
   const int tok0 = seq * args.L;           // first token of the sequence
   const int kv_blocks = KIND == MASK_CAUSAL ? qb + 1 : (args.L + 127) / 128;
@@ -381,7 +382,7 @@ int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt
                   cudaStream_t stream) {
   int rc = check_device(nullptr);
   if (rc != XDNA_OK) return rc;
-  XDNA_CHECK_ARG(B >= 1 && L >= 1 && B <= 65535, "attention: bad batch / length");
+  XDNA_CHECK_ARG(B >= 1 && L >= 1 && B <= 65535 && L <= 65535ll * 128, "attention: bad batch / length");
   XDNA_CHECK_ARG(qk && vt && out, "attention: null pointer");
   const int64_t T = B * L;
   const int64_t L8 = (L + 7) / 8 * 8;
@@ -417,7 +418,7 @@ int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt
   a.mask = mask;
   a.mask_heads = mask_heads;
   a.err = device_error_word();
-  dim3 grid(static_cast<unsigned>(a.q_blocks), 8, static_cast<unsigned>(B));  // (query block, kv head, sequence)
+  dim3 grid(8, static_cast<unsigned>(B), static_cast<unsigned>(a.q_blocks));  // (kv head, sequence, query block)
   static bool configured[4][64] = {};
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
