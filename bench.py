@@ -63,7 +63,7 @@ def parse():
                          "(default: peer blocks copied over NVLink once, overlapping the GEMM), read by the GEMM's "
                          "TMA straight from peer memory, after an NCCL all-gather; or data-parallel with the sequences")
     ap.add_argument("--kernel", default=None,
-                    choices=["gemm_i8", "quant_rows", "conv3x3", "attention", "gemm_bf16"],
+                    choices=["gemm_i8", "quant_rows", "conv3x3", "attention", "gemm_bf16", "gemm_bf16_qkv"],
                     help="time one kernel on --shape instead of a workload (profiling)")
     ap.add_argument("--shape", default="8192,6144,1024", help="--kernel shape, comma-separated")
     args = ap.parse_args()
@@ -917,6 +917,20 @@ def run_kernel(args):
             y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             fn = lambda: kernels.gemm_bf16(a, b, kernels.GEMM_F32ACC, out=y)  # noqa
         work, unit = 2 * M * N * K, "TFLOP/s"
+    elif args.kernel == "gemm_bf16_qkv":             # B, L: the stack's fused q/k/v projection over B x L tokens
+        B, L = shp
+        T, L8 = B * L, (L + 7) // 8 * 8
+        h = torch.randn(T, 1024, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(4096, 1024, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=dev, dtype=torch.float32) / 128))
+        ang = torch.arange(L, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+        cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+        qn, kn = torch.ones(128, device=dev), torch.ones(128, device=dev)
+        qk = torch.empty(T, 3072, dtype=torch.bfloat16, device=dev)
+        vt = torch.zeros(1024, B * L8, dtype=torch.bfloat16, device=dev)
+        fn = lambda: kernels.gemm_bf16(h, w, kernels.GEMM_QKV, out=qk, vt=vt, rope_cos=cos, rope_sin=sin,  # noqa
+                                       q_norm=qn, k_norm=kn, seq_len=L)
+        work, unit = 2 * T * 4096 * 1024, "TFLOP/s"
     else:
         raise SystemExit(f"unknown kernel {args.kernel}")
     for _ in range(5):

@@ -150,12 +150,13 @@ __host__ __device__ constexpr int smem_bytes_for() {
          1024 /*align*/ + 256 /*barriers*/;
 }
 
-// Shared memory per epilogue warp: 8 KB where the epilogue keeps the tile's column factors (and, for
-// the conv, its pixels' output offsets) beside the staging, as long as the operand ring keeps at least
-// 5 stages; 4 KB otherwise (factors then come by warp shuffles).
+// Shared memory per epilogue warp: 8 KB where the epilogue keeps the tile's column factors (for the conv
+// also its pixels' output offsets; for the q/k/v projection the head's RMSNorm weights) beside two
+// staging slots, as long as the operand ring keeps at least 5 stages; 4 KB otherwise (one slot, or
+// factors by warp shuffles).
 template <int BROWS, int KB, int EPI, bool PAIR, bool RB = false>
 __host__ __device__ constexpr int stage_out_bytes() {
-  return ((EPI == EPI_CONV_DEQ || (PAIR && EPI == EPI_DEQ)) && stages_for<BROWS, KB, 8192, RB>() >= 5)
+  return ((EPI == EPI_CONV_DEQ || (PAIR && (EPI == EPI_DEQ || EPI == EPI_QKV))) && stages_for<BROWS, KB, 8192, RB>() >= 5)
              ? 8192
              : kStageOutBytes;
 }
@@ -544,7 +545,7 @@ __device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u);
 // (out[d] = x[d] cos - x[d+64] sin, out[d+64] = x[d+64] cos + x[d] sin), stored bf16 through TMA.
 // v heads are written transposed, V^T[head * 128 + d][token], the K-major operand of P.V.
 __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int row0, int col0, StageRing& ring,
-                                         const CUtensorMap* tmC, const CUtensorMap* tmD) {
+                                         const CUtensorMap* tmC, const CUtensorMap* tmD, float* wsm) {
   const int lane = lane_id();
   const int row = row0 + lane;
   if (row0 >= a.M) return;  // warp-uniform: no rows of this warp exist
@@ -580,24 +581,35 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
     }
     return;
   }
-  // pass 1: sum of squares over the head's 128 values
-  float ss = 0.f;
+  // pass 1: sum of squares over the head's 128 values (two packed partial sums)
+  float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll 1
   for (int c = 0; c < 4; ++c) {
     __syncwarp();
     tmem_ld_32x32b_x32(taddr + c * 32, x1);
     tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 32; ++j) ss = fmaf(f32_of(x1[j]), f32_of(x1[j]), ss);
+    for (int j = 0; j < 32; j += 2) {
+      const float2 xv = make_float2(f32_of(x1[j]), f32_of(x1[j + 1]));
+      ss2 = __ffma2_rn(xv, xv, ss2);
+    }
   }
-  const float rstd = rsqrtf(ss * (1.0f / kHeadDim) + a.eps);
+  const float rstd = rsqrtf((ss2.x + ss2.y) * (1.0f / kHeadDim) + a.eps);
+  // the head's norm weights into this warp's shared memory: read back 4 at a time as a broadcast
   const float* nw = col0 < kQCols ? a.q_norm : a.k_norm;
-  const float w_lane[4] = {nw[lane], nw[32 + lane], nw[64 + lane], nw[96 + lane]};
+  __syncwarp();  // this warp's reads of the previous head's weights are done
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wsm[i * 32 + lane] = __ldg(nw + i * 32 + lane);
+  __syncwarp();
+  const float4* w4 = reinterpret_cast<const float4*>(wsm);
   const int pos = (row < a.M ? row : 0) % a.seq_len;
   // this row's RoPE table entries, 16 bytes at a time (rows are 256-byte aligned)
   const float4* cs4 = reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * (kHeadDim / 2));
   const float4* sn4 = reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * (kHeadDim / 2));
-  // pass 2: columns d and d + 64 together (the RoPE pairs), 32 at a time
+  const float2 r2 = make_float2(rstd, rstd);
+  // pass 2: columns d and d + 64 together (the RoPE pairs), 32 at a time, two neighbouring d per packed
+  // f32x2 operation: u = x_d w_d rstd, v = x_{d+64} w_{d+64} rstd, out_d = u cos - v sin,
+  // out_{d+64} = v cos + u sin
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     __syncwarp();
@@ -609,21 +621,24 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
     for (int q = 0; q < 8; ++q) {
       const float4 cv = __ldg(cs4 + c * 8 + q);
       const float4 sv = __ldg(sn4 + c * 8 + q);
-      const float co[4] = {cv.x, cv.y, cv.z, cv.w};
-      const float si[4] = {sv.x, sv.y, sv.z, sv.w};
-      float o[4][2];
+      const float4 wa = w4[c * 8 + q];       // w[d .. d+3], d = 32 c + 4 q
+      const float4 wb = w4[16 + c * 8 + q];  // w[d+64 .. d+67]
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = q * 4 + e;
-        const float u = f32_of(x1[j]) * rstd * __shfl_sync(kFull, w_lane[c], j);
-        const float v = f32_of(x2[j]) * rstd * __shfl_sync(kFull, w_lane[c + 2], j);
-        o[e][0] = u * co[e] - v * si[e];
-        o[e][1] = v * co[e] + u * si[e];
+      for (int h = 0; h < 2; ++h) {
+        const int j = 4 * q + 2 * h;
+        const float2 c2 = h ? make_float2(cv.z, cv.w) : make_float2(cv.x, cv.y);
+        const float2 s2 = h ? make_float2(sv.z, sv.w) : make_float2(sv.x, sv.y);
+        const float2 u = __fmul2_rn(__fmul2_rn(make_float2(f32_of(x1[j]), f32_of(x1[j + 1])),
+                                               h ? make_float2(wa.z, wa.w) : make_float2(wa.x, wa.y)),
+                                    r2);
+        const float2 v = __fmul2_rn(__fmul2_rn(make_float2(f32_of(x2[j]), f32_of(x2[j + 1])),
+                                               h ? make_float2(wb.z, wb.w) : make_float2(wb.x, wb.y)),
+                                    r2);
+        const float2 o_lo = __ffma2_rn(v, make_float2(-s2.x, -s2.y), __fmul2_rn(u, c2));
+        const float2 o_hi = __ffma2_rn(u, s2, __fmul2_rn(v, c2));
+        lo[q * 2 + h] = pack2(o_lo.x, o_lo.y, XDNA_BF16);
+        hi[q * 2 + h] = pack2(o_hi.x, o_hi.y, XDNA_BF16);
       }
-      lo[q * 2] = pack2(o[0][0], o[1][0], XDNA_BF16);
-      lo[q * 2 + 1] = pack2(o[2][0], o[3][0], XDNA_BF16);
-      hi[q * 2] = pack2(o[0][1], o[1][1], XDNA_BF16);
-      hi[q * 2 + 1] = pack2(o[2][1], o[3][1], XDNA_BF16);
     }
     stage_and_store<16>(ring, lo, tmC, col0 + c * 32, row0);
     stage_and_store<16>(ring, hi, tmC, col0 + 64 + c * 32, row0);
@@ -912,7 +927,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr bool kConvRows = EPI == EPI_CONV_DEQ && OUTB == 8192;
     constexpr bool kSmemFactors = (EPI == EPI_DEQ && TSTORE) || kConvRows;
     constexpr int kFactorOff = OUTB == 8192 ? 4096 : kStageSlotBytes;
-    StageRing ring{obuf, 0, (EPI == EPI_DEQ && TSTORE && OUTB == kStageOutBytes) ? 1 : 2};
+    // (EPI_QKV: the head's norm weights where the factors would be; with 4 KB, one staging slot)
+    StageRing ring{obuf, 0, ((EPI == EPI_DEQ && TSTORE) || EPI == EPI_QKV) && OUTB == kStageOutBytes ? 1 : 2};
     float* col_sw = reinterpret_cast<float*>(obuf + kFactorOff);          // [WCOLS]
     float* col_bias = col_sw + WCOLS;                                      // [WCOLS]
     long long* pix_off = reinterpret_cast<long long*>(col_bias + WCOLS);  // kConvRows: [32]
@@ -998,7 +1014,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
         if (col0 < args.N) {  // warp-uniform
           if constexpr (EPI == EPI_QKV)
-            qkv_tile(args, taddr, row0, col0, ring, &tmC, &tmD);
+            qkv_tile(args, taddr, row0, col0, ring, &tmC, &tmD, col_sw);
           else
             swiglu_tile<NCH>(args, taddr, row0, col0, ring, &tmC);
         }
