@@ -924,7 +924,7 @@ def run_kernel(args):
         w = (torch.randn(4096, 1024, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=dev, dtype=torch.float32) / 128))
         ang = torch.arange(L, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
-        cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+        cos, sin = kernels.rope_layout(ang.cos()), kernels.rope_layout(ang.sin())
         qn, kn = torch.ones(128, device=dev), torch.ones(128, device=dev)
         qk = torch.empty(T, 3072, dtype=torch.bfloat16, device=dev)
         vt = torch.zeros(1024, B * L8, dtype=torch.bfloat16, device=dev)

@@ -183,7 +183,9 @@ int xdna_embed(const int64_t* ids, int64_t tokens, const void* table, int table_
                float* x, void* stream);
 
 /* C [M, N] = A [M, K] . B [N, K]^T, bf16 operands (row pitches lda / ldb in elements, multiples of 8),
- * f32 accumulation on the tcgen05 tensor cores, with one of the XDNA_GEMM_* epilogues. */
+ * f32 accumulation on the tcgen05 tensor cores, with one of the XDNA_GEMM_* epilogues. XDNA_GEMM_QKV's
+ * rope_cos / rope_sin: f32 tables of the model's inverse frequencies at positions 0..seq_len-1 in the layout
+ * [16, seq_len, 4]: frequency d of position p at index (d / 4) * seq_len * 4 + p * 4 + d % 4. */
 int xdna_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N, int64_t K, int mode,
                    void* out, int out_dtype, int64_t ldo, const void* bias, int bias_dtype, float* resid, int64_t ldr,
                    void* vt, int64_t ldvt, const float* rope_cos, const float* rope_sin, const float* q_norm,
@@ -222,8 +224,8 @@ size_t xdna_qwen3_stack_workspace(int64_t B, int64_t L);
 
 /* The whole stack: x [B*L, 1024] f32 (the hidden states, updated in place as the residual stream)
  * through n_layers decoder layers, the final RMSNorm and the head: out [B*L, head_n] (row pitch ldo)
- * = h Whead^T (+ bias) in out_dtype. rope_cos / rope_sin: [L, 64] f32 tables of the model's inverse
- * frequencies at positions 0..L-1. With out == NULL the head is skipped and the final-normed hidden
+ * = h Whead^T (+ bias) in out_dtype. rope_cos / rope_sin: f32 tables of the model's inverse frequencies
+ * at positions 0..L-1, laid out [16, L, 4] as for xdna_gemm_bf16. With out == NULL the head is skipped and the final-normed hidden
  * states [B*L, 1024] bf16 are left at the start of the workspace. */
 int xdna_qwen3_stack(const xdna_qwen3_layer* layers, int n_layers, const float* final_norm, const void* head_w,
                      int64_t head_n, const void* head_bias, int head_bias_dtype, const float* rope_cos,

@@ -162,8 +162,9 @@ def test_gemm_bf16_qkv_norm_rope(cuda, B, L):
     qk = torch.empty(T, 3072, dtype=torch.bfloat16, device=cuda)
     L8 = -(-L // 8) * 8           # V^T: every sequence starts at a multiple of 8 columns
     vt = torch.zeros(1024, B * L8, dtype=torch.bfloat16, device=cuda)
-    kernels.gemm_bf16(h, torch.cat([wq, wk, wv]).contiguous(), kernels.GEMM_QKV, out=qk, vt=vt, rope_cos=cos,
-                      rope_sin=sin, q_norm=qn, k_norm=kn, seq_len=L)
+    kernels.gemm_bf16(h, torch.cat([wq, wk, wv]).contiguous(), kernels.GEMM_QKV, out=qk, vt=vt,
+                      rope_cos=kernels.rope_layout(cos), rope_sin=kernels.rope_layout(sin), q_norm=qn, k_norm=kn,
+                      seq_len=L)
     q, k, v = _qkv_ref(h, wq, wk, wv, qn, kn, cos, sin, L)
     assert rel_max(qk[:, :2048].view(T, 16, 128), q) < 1e-2
     assert rel_max(qk[:, 2048:].view(T, 8, 128), k) < 1e-2

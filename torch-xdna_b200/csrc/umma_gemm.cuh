@@ -603,9 +603,11 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
   __syncwarp();
   const float4* w4 = reinterpret_cast<const float4*>(wsm);
   const int pos = (row < a.M ? row : 0) % a.seq_len;
-  // this row's RoPE table entries, 16 bytes at a time (rows are 256-byte aligned)
-  const float4* cs4 = reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * (kHeadDim / 2));
-  const float4* sn4 = reinterpret_cast<const float4*>(a.rope_sin + static_cast<int64_t>(pos) * (kHeadDim / 2));
+  // this row's RoPE table entries: the tables are [16][seq_len] float4 (four frequencies per vector,
+  // positions fastest), so the warp's consecutive positions read consecutive 16-byte vectors
+  const float4* cs4 = reinterpret_cast<const float4*>(a.rope_cos) + pos;
+  const float4* sn4 = reinterpret_cast<const float4*>(a.rope_sin) + pos;
+  const int64_t qstride = a.seq_len;  // float4s between one group of four frequencies and the next
   const float2 r2 = make_float2(rstd, rstd);
   // pass 2: columns d and d + 64 together (the RoPE pairs), 32 at a time, two neighbouring d per packed
   // f32x2 operation: u = x_d w_d rstd, v = x_{d+64} w_{d+64} rstd, out_d = u cos - v sin,
@@ -619,8 +621,8 @@ __device__ __forceinline__ void qkv_tile(const GemmArgs& a, uint32_t taddr, int 
     uint32_t lo[16], hi[16];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const float4 cv = __ldg(cs4 + c * 8 + q);
-      const float4 sv = __ldg(sn4 + c * 8 + q);
+      const float4 cv = __ldg(cs4 + (c * 8 + q) * qstride);
+      const float4 sv = __ldg(sn4 + (c * 8 + q) * qstride);
       const float4 wa = w4[c * 8 + q];       // w[d .. d+3], d = 32 c + 4 q
       const float4 wb = w4[16 + c * 8 + q];  // w[d+64 .. d+67]
 #pragma unroll

@@ -261,6 +261,14 @@ def embed(ids, table, x):
                                       table.shape[1], _p(x), _stream()))
 
 
+def rope_layout(table):
+    """A RoPE table [L, 64] (position, frequency) f32 in the layout the q/k/v epilogue reads, [16, L, 4]:
+    four frequencies per 16-byte vector, positions fastest, so that the 32 consecutive positions of a warp's
+    rows are one coalesced 512-byte load."""
+    L = table.shape[0]
+    return table.reshape(L, 16, 4).transpose(0, 1).contiguous()
+
+
 def gemm_bf16(a, b, mode, out=None, bias=None, resid=None, vt=None, rope_cos=None, rope_sin=None, q_norm=None,
               k_norm=None, seq_len=0, eps=1e-6, M=None):
     """C = a[:, :K] . b[:, :K]^T (bf16) with the epilogue `mode` (GEMM_*); see include/xdna_b200.h."""

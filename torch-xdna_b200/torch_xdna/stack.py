@@ -271,11 +271,12 @@ class Packed:
         self._rope = {}
 
     def rope(self, L):
-        """cos / sin [L, 64] f32 at positions 0..L-1, as transformers computes them (f32 outer product)."""
+        """cos / sin at positions 0..L-1, as transformers computes them (f32 outer product), in the kernel's
+        [16, L, 4] layout (kernels.rope_layout)."""
         if L not in self._rope:
             pos = torch.arange(L, device=self.inv_freq.device, dtype=torch.float32)
             freqs = pos[:, None] * self.inv_freq[None, :]
-            self._rope[L] = (freqs.cos().contiguous(), freqs.sin().contiguous())
+            self._rope[L] = (kernels.rope_layout(freqs.cos()), kernels.rope_layout(freqs.sin()))
         return self._rope[L]
 
 
