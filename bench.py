@@ -513,7 +513,7 @@ def run_stack(args, rank, world):
         head = head[rank * n_cols:(rank + 1) * n_cols].contiguous()
     inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device=dev) / 128))
     f = torch.arange(L, dtype=torch.float32, device=dev)[:, None] * inv[None, :]
-    cos, sin = f.cos().contiguous(), f.sin().contiguous()
+    cos, sin = kernels.rope_layout(f.cos()), kernels.rope_layout(f.sin())
     ids = torch.randint(0, V_HEAD, (B * L,), device=dev, generator=g)
     x = torch.empty(B * L, D, device=dev)
     out = torch.empty(B_all * L if column else B * L, n_cols, dtype=torch.bfloat16, device=dev)
