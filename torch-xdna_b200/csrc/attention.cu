@@ -1,9 +1,11 @@
 // GQA flash attention for the Qwen3 stack on tcgen05 (sm_100a): softmax(Q K^T / sqrt(128) + mask) V
 // for 16 query heads sharing 8 key/value heads of dimension 128 (R:torch_xdna/stack.py:43-57).
 //
-// One CTA = 128 queries of the two query heads that share one key/value head (2g and 2g+1), so each
-// K and V^T block is loaded once for both; 320 threads:
-//   warp 0      TMA: both heads' Q tiles once, then K blocks of 128 keys into a 2-stage ring and V^T
+// A work item = 128 queries of the two query heads that share one key/value head (2g and 2g+1), so each
+// K and V^T block is loaded once for both. The kernel is persistent: one CTA per SM walks its share of
+// the items (heaviest causal items first, snake order), and its roles run across item boundaries, so
+// the next item's Q, K and first S overlap the current item's last P.V and output. 320 threads:
+//   warp 0      TMA: both heads' Q tiles per item, then K blocks of 128 keys into a 2-stage ring and V^T
 //               blocks into a 1-stage slot (Q and K read from the q/k projection output [T, 3072] bf16,
 //               V^T from [1024, T'] bf16, which the projection epilogue wrote transposed so that P.V
 //               has a K-major B operand);
@@ -35,6 +37,8 @@ struct AttnArgs {
   int T, L;               // tokens in all, tokens per sequence
   int L8;                 // round_up(L, 8): V^T column pitch of a sequence
   int q_blocks;           // ceil(L / 128)
+  int B;                  // sequences
+  int n_items;            // q_blocks x B x 8 work items (query block, sequence, key/value head)
   float scale_log2;       // log2(e) / sqrt(128)
   const int32_t* lens;    // MASK_PREFIX: per-sequence length
   const uint8_t* mask;    // MASK_BOOL: [B, Hm, L, L]
@@ -84,30 +88,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smP = smV + 2 * kTileBytes;              // [head][k-block]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smP + 4 * kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;               // [kKStages]
+  uint64_t* q_empty = bars + 1;              // an item's S MMAs done: Q may be reloaded
+  uint64_t* k_full = bars + 2;               // [kKStages]
   uint64_t* k_empty = k_full + kKStages;     // [kKStages]
   uint64_t* v_full = k_empty + kKStages;
   uint64_t* v_empty = v_full + 1;
-  uint64_t* s_full = v_empty + 1;            // [head] S_j ready in TMEM
-  uint64_t* s_empty = s_full + 2;            // [head] S_j loaded by the softmax: S_{j+1} may be computed
-  uint64_t* p_full = s_empty + 2;            // [head] P_j written (and O rescaled): O += P_j V_j may run
-  uint64_t* p_empty = p_full + 2;            // [head] O += P_j V_j done: P may be rewritten, O read
+  uint64_t* s_full = v_empty + 1;            // [head] S ready in TMEM
+  uint64_t* s_empty = s_full + 2;            // [head] S loaded by the softmax: the next S may be computed
+  uint64_t* p_full = s_empty + 2;            // [head] P written (and O rescaled): O += P V may run
+  uint64_t* p_empty = p_full + 2;            // [head] O += P V done: P may be rewritten, O read
   uint64_t* drain = p_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
-  // CTAs start in launch order (x fastest, z slowest): the query block is z, so for causal masks every
-  // (head, sequence) of the last query block (the most key blocks) goes first, the lightest last
-  const int qb = KIND == MASK_CAUSAL ? args.q_blocks - 1 - static_cast<int>(blockIdx.z) : static_cast<int>(blockIdx.z);
-  const int kvh = blockIdx.x;                // key/value head; query heads 2 kvh and 2 kvh + 1
-  const int seq = blockIdx.y;
-  const int q0 = qb * 128;                 // first query position in the sequence
-  const int tok0 = seq * args.L;           // first token of the sequence
-  const int kv_blocks = KIND == MASK_CAUSAL ? qb + 1 : (args.L + 127) / 128;
+  // Work items (query block, sequence, key/value head) with the query block slowest, so that for causal
+  // masks the items with the most key blocks come first. Round k of the G = gridDim.x CTAs takes items
+  // kG .. kG+G-1, in snake order (CTA c takes kG + c in even rounds, kG + G-1-c in odd ones): with the
+  // heaviest items first this balances the CTAs' total key blocks like a longest-first greedy schedule.
+  // Every role walks the same items and counts key blocks across them (g), which gives each barrier's
+  // phase: one K stage / V slot / S / P round per key block, one Q load per item.
+  const int cta = static_cast<int>(blockIdx.x), G = static_cast<int>(gridDim.x);
+  auto item_index = [&](int k) { return k * G + ((k & 1) ? G - 1 - cta : cta); };
+  auto item_of = [&](int idx, int& qb, int& seq, int& kvh) {
+    const int per = args.B * 8;
+    const int lev = idx / per;
+    const int rem = idx - lev * per;
+    qb = KIND == MASK_CAUSAL ? args.q_blocks - 1 - lev : lev;
+    seq = rem >> 3;
+    kvh = rem & 7;
+  };
+  auto blocks_of = [&](int qb) { return KIND == MASK_CAUSAL ? qb + 1 : (args.L + 127) / 128; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(k_empty + s, 1);
@@ -141,25 +156,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------------ TMA
-      mbar_arrive_expect_tx(q_full, 2 * TX);
-      for (int h = 0; h < 2; ++h)
-        for (int kk = 0; kk < 2; ++kk)
-          tma_load_2d(smQ + (h * 2 + kk) * kTileBytes, &tmQK, q_full, (2 * kvh + h) * 128 + kk * 64, tok0 + q0);
       int k_last[kKStages] = {-1, -1};
       int v_last = -1;
-      auto load_k = [&](int j) -> bool {
-        const int st = j % kKStages;
-        const uint32_t ph = (j / kKStages) & 1;
+      int q_loads = 0;
+      // item number n's Q tiles (both heads), once the previous item's S MMAs have read the old ones
+      auto load_q = [&](int n, int seq, int kvh, int q0) -> bool {
+        if (!mbar_wait(q_empty, (n & 1) ^ 1, abort_flag, args.err, 20)) return false;
+        mbar_arrive_expect_tx(q_full, 2 * TX);
+        for (int h = 0; h < 2; ++h)
+          for (int kk = 0; kk < 2; ++kk)
+            tma_load_2d(smQ + (h * 2 + kk) * kTileBytes, &tmQK, q_full, (2 * kvh + h) * 128 + kk * 64,
+                        seq * args.L + q0);
+        ++q_loads;
+        return true;
+      };
+      // key block j of (seq, kvh) as global block gb
+      auto load_k = [&](int gb, int seq, int kvh, int j) -> bool {
+        const int st = gb % kKStages;
+        const uint32_t ph = (gb / kKStages) & 1;
         if (!mbar_wait(k_empty + st, ph ^ 1, abort_flag, args.err, 21)) return false;
         mbar_arrive_expect_tx(k_full + st, TX);
         for (int kk = 0; kk < 2; ++kk)
           tma_load_2d(smK + (st * 2 + kk) * kTileBytes, &tmQK, k_full + st, 16 * 128 + kvh * 128 + kk * 64,
-                      tok0 + j * 128);
+                      seq * args.L + j * 128);
         k_last[st] = static_cast<int>(ph);
         return true;
       };
-      auto load_v = [&](int j) -> bool {
-        const uint32_t ph = j & 1;
+      auto load_v = [&](int gb, int seq, int kvh, int j) -> bool {
+        const uint32_t ph = gb & 1;
         if (!mbar_wait(v_empty, ph ^ 1, abort_flag, args.err, 22)) return false;
         mbar_arrive_expect_tx(v_full, TX);
         // V^T column = seq * L8 + key: a multiple of 8 elements, the 16-byte TMA alignment
@@ -168,14 +192,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         v_last = static_cast<int>(ph);
         return true;
       };
-      // K runs one block ahead of V: K_{j+1} is issued before waiting for V_j's slot
-      bool ok = load_k(0);
-      for (int j = 0; ok && j < kv_blocks; ++j) {
-        if (j + 1 < kv_blocks && !load_k(j + 1)) break;
-        ok = load_v(j);
+      // K runs one block ahead of V (K_{g+1} is issued before V_g), across items too: after an item's
+      // last V come the next item's Q and first K.
+      bool ok = true;
+      int g = 0;
+      for (int n = 0; ok && item_index(n) < args.n_items; ++n) {
+        int qb, seq, kvh;
+        item_of(item_index(n), qb, seq, kvh);
+        const int nb = blocks_of(qb);
+        if (n == 0) ok = load_q(0, seq, kvh, qb * 128) && load_k(0, seq, kvh, 0);
+        for (int j = 0; ok && j < nb; ++j, ++g) {
+          if (j + 1 < nb) {
+            ok = load_k(g + 1, seq, kvh, j + 1) && load_v(g, seq, kvh, j);
+          } else {
+            ok = load_v(g, seq, kvh, j);
+            if (ok && item_index(n + 1) < args.n_items) {
+              int qb2, seq2, kvh2;
+              item_of(item_index(n + 1), qb2, seq2, kvh2);
+              ok = load_q(n + 1, seq2, kvh2, qb2 * 128) && load_k(g + 1, seq2, kvh2, 0);
+            }
+          }
+        }
       }
+      // every load has landed before the CTA may exit
       volatile int never = 0;
-      mbar_wait(q_full, 0, &never, args.err, 23);
+      if (q_loads > 0) mbar_wait(q_full, static_cast<uint32_t>((q_loads - 1) & 1), &never, args.err, 23);
       for (int s = 0; s < kKStages; ++s)
         if (k_last[s] >= 0) mbar_wait(k_full + s, static_cast<uint32_t>(k_last[s]), &never, args.err, 23);
       if (v_last >= 0) mbar_wait(v_full, static_cast<uint32_t>(v_last), &never, args.err, 23);
@@ -183,19 +224,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------------ MMA
-      bool ok = mbar_wait(q_full, 0, abort_flag, args.err, 24);
+      bool ok = true;
       bool issued = false;
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(v_full, i & 1, abort_flag, args.err, 25)) return false;
+      // O_h += P_h V for global block gb; the first block of an item overwrites O (acc = 0)
+      auto issue_pv = [&](int gb, bool item_start) -> bool {
+        if (!mbar_wait(v_full, gb & 1, abort_flag, args.err, 25)) return false;
         for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(p_full + h, i & 1, abort_flag, args.err, 26)) return false;
+          if (!mbar_wait(p_full + h, gb & 1, abort_flag, args.err, 26)) return false;
           tc_fence_after();
           const uint32_t tO = tmem + 256 * h + 128;
           for (int kk = 0; kk < 2; ++kk) {
             const uint64_t dP = smem_desc_k_sw128(smem_u32(smP + (h * 2 + kk) * kTileBytes));
             const uint64_t dV = smem_desc_k_sw128(smem_u32(smV + kk * kTileBytes));
 #pragma unroll
-            for (int k = 0; k < 4; ++k) umma_f16(tO, dP + 2 * k, dV + 2 * k, IDESC, (i | kk | k) != 0);
+            for (int k = 0; k < 4; ++k) umma_f16(tO, dP + 2 * k, dV + 2 * k, IDESC, (!item_start || kk | k) != 0);
           }
           umma_commit(p_empty + h);
           issued = true;
@@ -203,33 +245,46 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         umma_commit(v_empty);
         return true;
       };
-      for (int j = 0; ok && j < kv_blocks; ++j) {
-        const int st = j % kKStages;
-        if (!mbar_wait(k_full + st, (j / kKStages) & 1, abort_flag, args.err, 27)) break;
-        for (int h = 0; h < 2 && ok; ++h) {
-          if (!mbar_wait(s_empty + h, (j & 1) ^ 1, abort_flag, args.err, 28)) {
+      int g = 0;
+      bool prev_start = false;  // block g - 1 is the first of its item
+      for (int n = 0; ok && item_index(n) < args.n_items; ++n) {
+        int qb, seq, kvh;
+        item_of(item_index(n), qb, seq, kvh);
+        const int nb = blocks_of(qb);
+        if (!mbar_wait(q_full, n & 1, abort_flag, args.err, 24)) break;
+        for (int j = 0; j < nb; ++j, ++g) {
+          const int st = g % kKStages;
+          if (!mbar_wait(k_full + st, (g / kKStages) & 1, abort_flag, args.err, 27)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t tS = tmem + 256 * h;
-          for (int kk = 0; kk < 2; ++kk) {
-            const uint64_t dQ = smem_desc_k_sw128(smem_u32(smQ + (h * 2 + kk) * kTileBytes));
-            const uint64_t dK = smem_desc_k_sw128(smem_u32(smK + (st * 2 + kk) * kTileBytes));
+          for (int h = 0; h < 2 && ok; ++h) {
+            if (!mbar_wait(s_empty + h, (g & 1) ^ 1, abort_flag, args.err, 28)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t tS = tmem + 256 * h;
+            for (int kk = 0; kk < 2; ++kk) {
+              const uint64_t dQ = smem_desc_k_sw128(smem_u32(smQ + (h * 2 + kk) * kTileBytes));
+              const uint64_t dK = smem_desc_k_sw128(smem_u32(smK + (st * 2 + kk) * kTileBytes));
 #pragma unroll
-            for (int k = 0; k < 4; ++k) umma_f16(tS, dQ + 2 * k, dK + 2 * k, IDESC, (kk | k) != 0);
+              for (int k = 0; k < 4; ++k) umma_f16(tS, dQ + 2 * k, dK + 2 * k, IDESC, (kk | k) != 0);
+            }
+            umma_commit(s_full + h);
+            issued = true;
           }
-          umma_commit(s_full + h);
-          issued = true;
-        }
-        if (!ok) break;
-        umma_commit(k_empty + st);
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
+          if (!ok) break;
+          if (j == nb - 1) umma_commit(q_empty);  // this item's Q has been read once these complete
+          umma_commit(k_empty + st);
+          if (g >= 1 && !issue_pv(g - 1, prev_start)) {
+            ok = false;
+            break;
+          }
+          prev_start = j == 0;
         }
       }
-      if (ok && kv_blocks > 0) issue_pv(kv_blocks - 1);
+      if (ok && g > 0) issue_pv(g - 1, prev_start);
       if (issued) {
         umma_commit(drain);
         volatile int never = 0;
@@ -239,134 +294,140 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else {
     // -------------------------------------------------------------------- softmax (warps 2..9)
     const int hg = (warp - 2) >> 2;          // 0: query head 2 kvh, 1: 2 kvh + 1
-    const int head = 2 * kvh + hg;
     const int qd = warp & 3;                 // TMEM lane quadrant = row block
     const int r = qd * 32 + lane;            // query row within the tile
-    const int qpos = q0 + r;                 // query position in the sequence
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
     const uint32_t tS = tmem + 256 * hg;
     const uint32_t tO = tS + 128;
     uint8_t* myP = smP + hg * 2 * kTileBytes;
     const float sc = args.scale_log2;
-    float m_use = -INFINITY;                 // the max the probabilities and O are relative to (log2 units)
-    float l = 0.f;
     bool ok = true;
-    uint32_t v[128];                         // this row of S_j, loaded from TMEM once
-    for (int j = 0; j < kv_blocks && ok; ++j) {
-      const int k0 = j * 128;
-      // warp-uniform: does any entry of this block need the mask?
-      const bool masked = KIND == MASK_PREFIX || KIND == MASK_BOOL || k0 + 128 > args.L ||
-                          (KIND == MASK_CAUSAL && k0 + 127 > q0);
-      if (!mbar_wait(s_full + hg, j & 1, abort_flag, args.err, 31)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      __syncwarp();
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
-      tmem_ld_wait();
-      // S_j is in registers: the MMA may compute S_{j+1} into these columns
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty + hg);
-      if (masked) {
-#pragma unroll
-        for (int e = 0; e < 128; ++e)
-          if (!key_allowed(KIND, args, seq, head, qpos, k0 + e)) v[e] = __float_as_uint(-INFINITY);
-      }
-      // the row max of the raw scores (scale > 0 commutes with max)
-      float mx = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < 128; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
-      const float m_blk = mx * sc;
-      // raise the running max only when this block would push p above 2^8
-      float alpha = 1.f;
-      const bool raise = m_blk > m_use + kRescaleLog2;
-      if (raise) {
-        alpha = fast_exp2(m_use - m_blk);    // 0 while m_use is -inf
-        m_use = m_blk;
-      }
-      // O += P_{j-1} V_{j-1} has finished: O may be rescaled and the P tile rewritten
-      if (j >= 1 && !mbar_wait(p_empty + hg, (j - 1) & 1, abort_flag, args.err, 32)) {
-        ok = false;
-        break;
-      }
-      if (j >= 1 && __any_sync(0xffffffffu, raise && l > 0.f)) {
-        // rows that did not raise multiply by 1
+    uint32_t v[128];                         // this row of S, loaded from TMEM once
+    int g = 0;
+    for (int n = 0; ok && item_index(n) < args.n_items; ++n) {
+      int qb, seq, kvh;
+      item_of(item_index(n), qb, seq, kvh);
+      const int nb = blocks_of(qb);
+      const int head = 2 * kvh + hg;
+      const int q0 = qb * 128;               // first query position in the sequence
+      const int qpos = q0 + r;               // this row's query position
+      float m_use = -INFINITY;               // the max the probabilities and O are relative to (log2 units)
+      float l = 0.f;
+      for (int j = 0; j < nb; ++j, ++g) {
+        const int k0 = j * 128;
+        // warp-uniform: does any entry of this block need the mask?
+        const bool masked = KIND == MASK_PREFIX || KIND == MASK_BOOL || k0 + 128 > args.L ||
+                            (KIND == MASK_CAUSAL && k0 + 127 > q0);
+        if (!mbar_wait(s_full + hg, g & 1, abort_flag, args.err, 31)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        uint32_t o[32];
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tmem_ld_32x32b_x32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
+        tmem_ld_wait();
+        // S is in registers: the MMA may compute the next S into these columns
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty + hg);
+        if (masked) {
+#pragma unroll
+          for (int e = 0; e < 128; ++e)
+            if (!key_allowed(KIND, args, seq, head, qpos, k0 + e)) v[e] = __float_as_uint(-INFINITY);
+        }
+        // the row max of the raw scores (scale > 0 commutes with max)
+        float mx = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 128; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+        const float m_blk = mx * sc;
+        // raise the running max only when this block would push p above 2^8
+        float alpha = 1.f;
+        const bool raise = m_blk > m_use + kRescaleLog2;
+        if (raise) {
+          alpha = fast_exp2(m_use - m_blk);  // 0 while m_use is -inf
+          m_use = m_blk;
+        }
+        // O += P V of the previous block has finished: O may be rescaled and the P tile rewritten (for an
+        // item's first block the previous item's output pass already waited for it)
+        if (j >= 1 && !mbar_wait(p_empty + hg, (g - 1) & 1, abort_flag, args.err, 32)) {
+          ok = false;
+          break;
+        }
+        if (j >= 1 && __any_sync(0xffffffffu, raise && l > 0.f)) {
+          // rows that did not raise multiply by 1
+          tc_fence_after();
+          uint32_t o[32];
 #pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            __syncwarp();
+            tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_32x32b_x32(tO + lane_off + c * 32, o);
+          }
+          tmem_st_wait();
+        }
+        l *= alpha;
+        // p = 2^(s * scale - m) as bf16 into the swizzled K-major P tile, and the row sum
+        const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+        const bool none = m_use == -INFINITY;  // every key so far masked
+        float rs = 0.f;
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          __syncwarp();
-          tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
-          tmem_ld_wait();
+          uint32_t w[16];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st_32x32b_x32(tO + lane_off + c * 32, o);
-        }
-        tmem_st_wait();
-      }
-      l *= alpha;
-      // p = 2^(s * scale - m) as bf16 into the swizzled K-major P tile, and the row sum
-      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
-      const bool none = m_use == -INFINITY;  // every key so far masked
-      float rs = 0.f;
+          for (int e = 0; e < 32; e += 2) {
+            float p0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), sc, neg_m));
+            float p1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), sc, neg_m));
+            if (none) p0 = p1 = 0.f;
+            rs += p0 + p1;
+            w[e / 2] = pack2_bf16(p0, p1);
+          }
+          // 32 keys = 64 bytes = 4 chunks of 16 bytes in k-block c / 2, chunk offset (c % 2) * 4
+          uint8_t* rowp = myP + (c >> 1) * kTileBytes + r * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t w[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), sc, neg_m));
-          float p1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), sc, neg_m));
-          if (none) p0 = p1 = 0.f;
-          rs += p0 + p1;
-          w[e / 2] = pack2_bf16(p0, p1);
-        }
-        // 32 keys = 64 bytes = 4 chunks of 16 bytes in k-block c / 2, chunk offset (c % 2) * 4
-        uint8_t* rowp = myP + (c >> 1) * kTileBytes + r * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = (c & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) * 16)) =
-              make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-        }
-      }
-      l += rs;
-      // P_j (and the rescaled O) are ready for the MMA
-      tc_fence_before();
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + hg);
-    }
-    if (ok && kv_blocks > 0) {
-      // the last O += P V, then O / l
-      const int last = kv_blocks - 1;
-      if (mbar_wait(p_empty + hg, last & 1, abort_flag, args.err, 34)) {
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<int64_t>(tok0 + qpos) * (16 * 128) + head * 128);
-        uint32_t o[32];
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          __syncwarp();
-          tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
-          tmem_ld_wait();
-          if (qpos < args.L) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 8) {
-              uint4 u;
-              u.x = pack2_bf16(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
-              u.y = pack2_bf16(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
-              u.z = pack2_bf16(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
-              u.w = pack2_bf16(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
-              dst[(c * 32 + e) / 8] = u;
-            }
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = (c & 1) * 4 + q;
+            *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) * 16)) =
+                make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
           }
         }
+        l += rs;
+        // P (and the rescaled O) are ready for the MMA
         tc_fence_before();
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + hg);
       }
+      if (!ok || nb == 0) break;
+      // the item's last O += P V, then O / l
+      if (!mbar_wait(p_empty + hg, (g - 1) & 1, abort_flag, args.err, 34)) break;
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<int64_t>(seq * args.L + qpos) * (16 * 128) + head * 128);
+      uint32_t o[32];
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        __syncwarp();
+        tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
+        tmem_ld_wait();
+        if (qpos < args.L) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 u;
+            u.x = pack2_bf16(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+            u.y = pack2_bf16(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+            u.z = pack2_bf16(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+            u.w = pack2_bf16(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+            dst[(c * 32 + e) / 8] = u;
+          }
+        }
+      }
+      // O has been read: the next item's first O = P V (issued after this warp's next P) may overwrite it
+      tc_fence_before();
     }
   }
   __syncthreads();
@@ -380,9 +441,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt, __nv_bfloat16* out, int64_t B,
                   int64_t L, int mask_kind, const int32_t* lens, const uint8_t* mask, int mask_heads,
                   cudaStream_t stream) {
-  int rc = check_device(nullptr);
+  int sms = 0;
+  int rc = check_device(&sms);
   if (rc != XDNA_OK) return rc;
-  XDNA_CHECK_ARG(B >= 1 && L >= 1 && B <= 65535 && L <= 65535ll * 128, "attention: bad batch / length");
+  XDNA_CHECK_ARG(B >= 1 && L >= 1 && (L + 127) / 128 * B * 8 < (1ll << 31), "attention: bad batch / length");
   XDNA_CHECK_ARG(qk && vt && out, "attention: null pointer");
   const int64_t T = B * L;
   const int64_t L8 = (L + 7) / 8 * 8;
@@ -413,12 +475,15 @@ int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt
   a.L = static_cast<int>(L);
   a.L8 = static_cast<int>(L8);
   a.q_blocks = static_cast<int>((L + 127) / 128);
+  a.B = static_cast<int>(B);
+  a.n_items = a.q_blocks * a.B * 8;
   a.scale_log2 = 1.4426950408889634f / sqrtf(128.f);
   a.lens = lens;
   a.mask = mask;
   a.mask_heads = mask_heads;
   a.err = device_error_word();
-  dim3 grid(8, static_cast<unsigned>(B), static_cast<unsigned>(a.q_blocks));  // (kv head, sequence, query block)
+  // persistent: one CTA per SM (its shared memory allows no second), each walking its share of the items
+  const int grid = std::min(a.n_items, sms);
   static bool configured[4][64] = {};
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
