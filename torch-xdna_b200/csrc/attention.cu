@@ -337,10 +337,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int e = 0; e < 128; ++e)
             if (!key_allowed(KIND, args, seq, head, qpos, k0 + e)) v[e] = __float_as_uint(-INFINITY);
         }
-        // the row max of the raw scores (scale > 0 commutes with max)
-        float mx = -INFINITY;
+        // the row max of the raw scores (scale > 0 commutes with max), as 8 independent partial maxima so
+        // that the reduction is not one 128-long dependent chain
+        float m8[8];
 #pragma unroll
-        for (int e = 0; e < 128; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+        for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(v[i]);
+#pragma unroll
+        for (int e = 8; e < 128; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(v[e]));
+        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         const float m_blk = mx * sc;
         // raise the running max only when this block would push p above 2^8
         float alpha = 1.f;
@@ -374,7 +378,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // p = 2^(s * scale - m) as bf16 into the swizzled K-major P tile, and the row sum
         const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
         const bool none = m_use == -INFINITY;  // every key so far masked
-        float rs = 0.f;
+        float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial row sums
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t w[16];
@@ -383,7 +387,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             float p0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), sc, neg_m));
             float p1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), sc, neg_m));
             if (none) p0 = p1 = 0.f;
-            rs += p0 + p1;
+            rs8[(e >> 1) & 7] += p0 + p1;
             w[e / 2] = pack2_bf16(p0, p1);
           }
           // 32 keys = 64 bytes = 4 chunks of 16 bytes in k-block c / 2, chunk offset (c % 2) * 4
@@ -395,7 +399,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
           }
         }
-        l += rs;
+        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         // P (and the rescaled O) are ready for the MMA
         tc_fence_before();
         fence_async_smem();
