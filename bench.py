@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--seq-len", type=int, default=1024, help="stack: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="stack: decoder layers")
     ap.add_argument("--images", type=int, default=32, help="conv: images in the global batch")
+    ap.add_argument("--conv-unchained", action="store_true",
+                    help="conv: float tensors between convs (conv3x3_fused + torch max-pool) instead of int8 codes")
     ap.add_argument("--head", default="column", choices=["column", "column-direct", "column-nccl", "dp"],
                     help="stack on N > 1 GPUs: head column-parallel with the all-gather pipelined into its GEMMs "
                          "(default: peer blocks copied over NVLink once, overlapping the GEMM), read by the GEMM's "
@@ -727,9 +729,11 @@ def single_conv_roofline(dev, stream, peak, src):
 
 def run_conv(args, rank, world):
     """One step = the 13 int8 conv3x3 layers of VGG16 (bias + ReLU, 2x2 max-pool between blocks) on this
-    rank's share of a batch of 32 images 3x224x224 (batch sharded over ranks, strong scaling). Each conv is
-    xdna::conv3x3_fused: per-image quantise into the bordered NHWC layout, then the implicit-GEMM conv with
-    the dequantise, bias and ReLU in its epilogue; the pool is a torch op. The requantise shift of every
+    rank's share of a batch of 32 images 3x224x224 (batch sharded over ranks, strong scaling), as the
+    backend compiles it: xdna::conv3x3_chain, the activations between convs kept as int8 codes (the next
+    conv's quantise rebuilds the float values and takes the 2x2 max-pool on the codes), the last conv's
+    output dequantised with bias and ReLU in its epilogue and max-pooled by torch. --conv-unchained runs
+    xdna::conv3x3_fused per conv with torch's max-pool between (same values). The requantise shift of every
     layer comes from global image 0 (rank 0), broadcast to the other ranks."""
     import torch_xdna
     from torch_xdna import kernels, parallel
@@ -750,7 +754,11 @@ def run_conv(args, rank, world):
     x = x_all[rank * N:(rank + 1) * N].contiguous()
     del x_all
 
-    def step(inp):
+    from torch_xdna.conv import IN_CODES, IN_CODES_POOL, IN_FLOAT
+
+    n_convs = sum(p != "M" for p in params)
+
+    def step_unchained(inp):
         h = inp
         for p in params:
             if p == "M":
@@ -758,6 +766,23 @@ def run_conv(args, rank, world):
             else:
                 h = torch.ops.xdna.conv3x3_fused(h, p[0], p[1], False, cid, True)  # ReLU after the bias
         return h
+
+    def step_chained(inp):
+        h, meta, k, pool = inp, None, 0, False
+        for p in params:
+            if p == "M":
+                if k == n_convs:   # after the last conv: a float tensor
+                    h = torch.nn.functional.max_pool2d(h, 2)
+                else:
+                    pool = True    # taken into the next conv's quantise
+                continue
+            mode = IN_FLOAT if k == 0 else (IN_CODES_POOL if pool else IN_CODES)
+            k += 1
+            h, meta = torch.ops.xdna.conv3x3_chain(h, meta, p[0], p[1], False, cid, True, mode, k > 1, k < n_convs)
+            pool = False
+        return h
+
+    step = step_unchained if args.conv_unchained else step_chained
 
     stream = torch.cuda.current_stream()
     with torch.no_grad():
@@ -811,6 +836,8 @@ def run_conv(args, rank, world):
                 "ms_per_step": round(total_s * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "int8", "data": "synthetic (N(0,1) images, Kaiming weights, N(0,0.01) bias)",
                 "config": {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224, bias + ReLU, 2x2 max-pool",
+                           "between_convs": "fp32 tensors, torch max-pool" if args.conv_unchained
+                           else "int8 codes (pool on the codes)",
                            "global_batch": N_all, "parallelism": f"dp{world} (images)", "l2": "activations exceed L2"},
                 "gpu_launches": launches, "roofline": roof, "single_conv_256x1536x64": single,
                 "clocks": clocks.summary()}

@@ -46,6 +46,8 @@ extern "C" {
 #define XDNA_CONV_DEQUANT 1   /* y = float(q) * (scale[co] * sx[n]) (+ bias[co]) in out_dtype, channels-last
                                  memory [N, H, W, Co] (torch's channels_last layout of an [N, Co, H, W] tensor) */
 #define XDNA_CONV_CALIBRATE 2 /* *acc_max = max over the sums of image 0 of (relu ? max(acc,0) : |acc|) */
+#define XDNA_CONV_Q_NHWC 3    /* q as XDNA_CONV_Q, written channels-last [N, H, W, Co]: the int8 form in which
+                                 one conv's output feeds the next (xdna_conv_quant_codes) */
 /* `relu` of xdna_conv3x3_i8: 0 none; 1 fused into the requantise ([0,255] uint8, the reference's ReLU of
  * a bias-free conv); XDNA_RELU_AFTER_BIAS (DEQUANT only) applied to the dequantised output after the
  * bias, the requantise saturating to int8 — the same values as torch.relu on the DEQUANT output. */
@@ -106,6 +108,21 @@ int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64
 int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,
                                   int8_t* xp, int64_t Cp, float* sx, uint32_t* amax_scratch, void* stream);
 
+/* The next conv's input straight from a conv's int8 output, with no float tensor in between: q [N, H, W, C]
+ * (XDNA_CONV_Q_NHWC; uint8 when q_unsigned, else int8; C a multiple of 4) stands for the dequantised
+ * y = float(q) * (scale[c] * sx_in[n]) (+ bias[c]) (then max(y, 0) when relu_after), computed with the
+ * same f32 roundings as XDNA_CONV_DEQUANT. With pool, y is max-pooled 2x2 / stride 2 first (output
+ * H / 2 x W / 2, rounded down: torch's max_pool2d(2)); pooling the codes is exact because y grows with q.
+ * Then y is quantised per image exactly as xdna_conv_quant_nhwc does (sx_out[n] = max(amax, 1e-8) / 127,
+ * round half even, saturate to +-127) into the bordered xp [N, H'+2, W'+2, Cp]. amax_scratch: N words.
+ * Replaces the dequantise at the end of conv3x3_int8 R:torch_xdna/conv.py:47-50, the graph's relu and
+ * max_pool2d, and the next conv3x3_int8's quantise R:torch_xdna/conv.py:45-46, for a chain of convs whose
+ * intermediate activations have no other use (the int8 NHWC chaining the reference names as its largest
+ * remaining cost). */
+int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
+                          const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,
+                          int8_t* xp, int64_t Cp, float* sx_out, uint32_t* amax_scratch, void* stream);
+
 /* xdna_conv_quant_nhwc without caller-provided scratch: the same inputs, outputs and results, but the
  * per-image max lives in a 16 KB array inside the library, so the call allocates nothing and takes no
  * scratch pointer. It has no counterpart in the reference (whose quantise runs on the CPU).
@@ -135,6 +152,7 @@ int xdna_conv_pack_weight(const int8_t* wq, int64_t Co, int64_t Ci, int8_t* wp, 
  * [0,255] uint8 when relu != 0. Output `out`: NCHW [N, Co, H, W] XDNA_I8 / XDNA_U8 for XDNA_CONV_Q;
  * channels-last [N, H, W, Co] XDNA_F32 / XDNA_BF16 / XDNA_F16 for XDNA_CONV_DEQUANT. For XDNA_CONV_CALIBRATE
  * only image 0 is computed and acc_max (one int32, cleared by this call) receives the maximum.
+ * XDNA_CONV_Q_NHWC writes the same q as XDNA_CONV_Q, channels-last [N, H, W, Co] (XDNA_I8 / XDNA_U8).
  * Replaces tl.extra.npu.conv3x3.Conv3x3(...)(xq) as used by ConvLayer.npu
  * R:torch_xdna/conv.py:334-340,350-359, the CPU integers ConvLayer.cpu R:torch_xdna/conv.py:345-348,
  * the calibration sums of ConvLayer.calibrate R:torch_xdna/conv.py:327-332, and (DEQUANT) the

@@ -9,7 +9,7 @@ import torch
 
 import torch_xdna
 from torch_xdna import kernels
-from torch_xdna.conv import conv3x3_int8
+from torch_xdna.conv import IN_CODES, IN_CODES_POOL, IN_FLOAT, conv3x3_chain_int8, conv3x3_int8
 
 
 def capture_graphs(model, x, cfg):
@@ -118,17 +118,75 @@ def test_shared_input_fusion():
 
 def test_conv_pass_which_convs_and_relu():
     """3 of 4 convs rewritten, stride 2 left alone (R:tests/test_backend.py:220-240); the bias-free conv's
-    ReLU fused into the requantise as in the reference, the biased conv's ReLU after its bias."""
-    (gm,) = capture_graphs(CNN().eval(), torch.randn(1, 64, 16, 64), torch_xdna.Config(policy="npu"))
-    nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
-    convs = [n for n in nodes if n.target is conv3x3_int8]
-    assert [n.args[3] for n in convs] == [False, True, False], [n.args for n in convs]
-    assert [n.args[5] for n in convs] == [True, False, False], [n.args for n in convs]
-    assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes) == 0
-    assert sum(n.target is torch.conv2d for n in nodes) == 1
+    ReLU fused into the requantise as in the reference, the biased conv's ReLU after its bias. Without
+    fusion the three stay separate conv3x3_int8 nodes with the ReLUs in the graph."""
     (gm2,) = capture_graphs(CNN().eval(), torch.randn(1, 64, 16, 64), torch_xdna.Config(policy="npu", fuse=False))
     nodes2 = [n for n in gm2.graph.nodes if n.op == "call_function"]
+    assert sum(n.target is conv3x3_int8 for n in nodes2) == 3
     assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes2) == 2
+    assert sum(n.target is torch.conv2d for n in nodes2) == 1
+    # with fusion the three consecutive convs also pass int8 codes between them (conv3x3_chain)
+    (gm,) = capture_graphs(CNN().eval(), torch.randn(1, 64, 16, 64), torch_xdna.Config(policy="npu"))
+    nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
+    chain = [n for n in nodes if n.target is conv3x3_chain_int8]
+    # args: (x, xmeta, w, b, relu, cfg_id, post_relu, in_mode, in_relu_after, out_q)
+    assert [n.args[4] for n in chain] == [False, True, False], [n.args for n in chain]
+    assert [n.args[6] for n in chain] == [True, False, False]
+    assert [n.args[7] for n in chain] == [IN_FLOAT, IN_CODES, IN_CODES]
+    assert [n.args[8] for n in chain] == [False, True, False]   # the previous conv's ReLU after its bias
+    assert [n.args[9] for n in chain] == [True, True, False]    # the last one feeds the stride-2 conv: float
+    assert sum(n.target is conv3x3_int8 for n in nodes) == 0
+    assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes) == 0
+    assert sum(n.target is torch.conv2d for n in nodes) == 1
+
+
+class VGGish(torch.nn.Module):
+    """VGG-style blocks: conv, ReLU, conv, ReLU, 2x2 max-pool, ...; `tap` also returns an intermediate
+    activation, which then must stay a float tensor."""
+
+    def __init__(self, tap=False):
+        super().__init__()
+        self.c1 = torch.nn.Conv2d(3, 64, 3, padding=1)
+        self.c2 = torch.nn.Conv2d(64, 64, 3, padding=1)
+        self.c3 = torch.nn.Conv2d(64, 128, 3, padding=1)
+        self.c4 = torch.nn.Conv2d(128, 128, 3, padding=1, bias=False)
+        self.pool = torch.nn.MaxPool2d(2)
+        self.tap = tap
+
+    def forward(self, x):
+        h = torch.relu(self.c1(x))
+        a = torch.relu(self.c2(h))
+        h = torch.relu(self.c3(self.pool(a)))
+        h = self.pool(torch.relu(self.c4(h)))
+        return (h, a) if self.tap else h
+
+
+def test_conv_chain_through_max_pool():
+    """The 2x2 max-pool between two convs is taken into the chain (pooled on the codes); the last pool,
+    whose input is the graph's output, stays."""
+    (gm,) = capture_graphs(VGGish().eval(), torch.randn(1, 3, 16, 16), torch_xdna.Config(policy="npu"))
+    nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
+    chain = [n for n in nodes if n.target is conv3x3_chain_int8]
+    assert [n.args[7] for n in chain] == [IN_FLOAT, IN_CODES, IN_CODES_POOL, IN_CODES]
+    assert [n.args[9] for n in chain] == [True, True, True, False]
+    assert [n.args[8] for n in chain] == [False, True, True, True]
+    assert sum(n.target in (torch.nn.functional.max_pool2d, torch.max_pool2d) for n in nodes) == 1
+
+
+def test_conv_chain_stops_at_other_uses_and_non_f32():
+    """An activation with another user (here a graph output) is not chained across; bf16 activations are
+    not chained at all."""
+    (gm,) = capture_graphs(VGGish(tap=True).eval(), torch.randn(1, 3, 16, 16), torch_xdna.Config(policy="npu"))
+    nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
+    chain = [n for n in nodes if n.target is conv3x3_chain_int8]
+    # c1 -> c2 chained; c2's output is also returned, so c2 -> pool -> c3 is not; c3 -> c4 chained
+    assert [(n.args[7], n.args[9]) for n in chain] == [(IN_FLOAT, True), (IN_CODES, False), (IN_FLOAT, True),
+                                                       (IN_CODES, False)]
+    (gmb,) = capture_graphs(VGGish().eval().to(torch.bfloat16), torch.randn(1, 3, 16, 16, dtype=torch.bfloat16),
+                            torch_xdna.Config(policy="npu"))
+    nodes = [n for n in gmb.graph.nodes if n.op == "call_function"]
+    assert sum(n.target is conv3x3_chain_int8 for n in nodes) == 0
+    assert sum(n.target is conv3x3_int8 for n in nodes) == 4
 
 
 def test_policy_cpu_rewrites_nothing_and_runs():

@@ -159,7 +159,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   if (rc != XDNA_OK) return rc;
   XDNA_CHECK_ARG(N >= 0 && Ci >= 1 && Co >= 1 && H >= 1 && W >= 1, "conv3x3: bad shape");
   XDNA_CHECK_ARG(Cp >= Ci && Cp % 16 == 0, "conv3x3: Cp must be >= Ci and a multiple of 16");
-  XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE,
+  XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE ||
+                     mode == XDNA_CONV_Q_NHWC,
                  "conv3x3: unknown mode %d", mode);
   XDNA_CHECK_ARG(relu == 0 || relu == 1 || (relu == XDNA_RELU_AFTER_BIAS && mode == XDNA_CONV_DEQUANT),
                  "conv3x3: relu %d (0, 1, or XDNA_RELU_AFTER_BIAS with XDNA_CONV_DEQUANT)", relu);
@@ -171,8 +172,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
     N = 1;  // the shift is fixed from the first image's sums
   } else {
     XDNA_CHECK_ARG(shift >= 1 && shift <= 31, "conv3x3: shift %d outside [1, 31]", shift);
-    XDNA_CHECK_ARG(scale != nullptr || mode == XDNA_CONV_Q, "conv3x3: dequantise needs scale");
-    if (mode == XDNA_CONV_Q)
+    XDNA_CHECK_ARG(scale != nullptr || mode == XDNA_CONV_Q || mode == XDNA_CONV_Q_NHWC, "conv3x3: dequantise needs scale");
+    if (mode == XDNA_CONV_Q || mode == XDNA_CONV_Q_NHWC)
       XDNA_CHECK_ARG(out_dtype == (relu ? XDNA_U8 : XDNA_I8), "conv3x3: requantised output is %s",
                      relu ? "uint8 with relu" : "int8 without relu");
     else
@@ -206,7 +207,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   a.out = out;
   a.out_dtype = out_dtype;
   // XDNA_CONV_DEQUANT writes channels-last: 32 channels of a pixel as 16-byte vectors when aligned
-  a.vec_ok = mode == XDNA_CONV_DEQUANT && aligned16(out) && (Co * dtype_size(out_dtype)) % 16 == 0;
+  a.vec_ok = mode == XDNA_CONV_DEQUANT ? (aligned16(out) && (Co * dtype_size(out_dtype)) % 16 == 0)
+            : mode == XDNA_CONV_Q_NHWC ? (aligned16(out) && Co % 16 == 0) : 0;
   a.sx = sx;
   a.sw = scale;
   a.bias = bias;
@@ -239,6 +241,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
       return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, pair, ta, tb, a, sms, s);
     case XDNA_CONV_DEQUANT:
       return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, pair, ta, tb, a, sms, s);
+    case XDNA_CONV_Q_NHWC:
+      return dispatch_conv<EPI_CONV_QNHWC, XDNA_I8>(kb, bn, pair, ta, tb, a, sms, s);
     default:
       return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, false, ta, tb, a, sms, s);
   }

@@ -399,6 +399,113 @@ __global__ void __launch_bounds__(256) cl_to_bordered_kernel(const T* __restrict
   }
 }
 
+// ---------------------------------------------------------------------------- int8 codes -> bordered NHWC
+// The next conv's input from a conv's channels-last codes q [N, H, W, C] (C % 4 == 0), read as words of 4
+// channels. A code stands for y = float(q) * (scale[c] * sx[n]) (+ bias[c]) (then max(y, 0)), the same
+// f32 operations as the conv's dequantising epilogue; y grows with q (scale, sx > 0), so a 2x2 max-pool
+// of y is y of the bytewise max of the codes. amax pass: grid (chunks, N), one word per thread; quantise
+// pass: grid (H' + 2, N) as cl_to_bordered_kernel.
+template <bool POOL, bool USGN>
+__device__ __forceinline__ uint32_t codes_word(const uint32_t* __restrict__ q, int n, int yo, int xo, int c4, int H, int W,
+                                               int C4) {
+  if constexpr (!POOL) {
+    return __ldg(q + ((static_cast<int64_t>(n) * H + yo) * W + xo) * C4 + c4);
+  } else {
+    const uint32_t* p = q + ((static_cast<int64_t>(n) * H + 2 * yo) * W + 2 * xo) * C4 + c4;
+    const uint32_t a = __ldg(p), b = __ldg(p + C4), c = __ldg(p + static_cast<int64_t>(W) * C4),
+                   d = __ldg(p + static_cast<int64_t>(W) * C4 + C4);
+    return USGN ? __vmaxu4(__vmaxu4(a, b), __vmaxu4(c, d)) : __vmaxs4(__vmaxs4(a, b), __vmaxs4(c, d));
+  }
+}
+
+template <bool USGN>
+__device__ __forceinline__ void codes_values(uint32_t word, int c, float t, const float* __restrict__ scale,
+                                             const float* __restrict__ bias, bool relu_after, float (&v)[4]) {
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t byte = (word >> (8 * b)) & 0xFFu;
+    const int qv = USGN ? static_cast<int>(byte) : static_cast<int>(static_cast<int8_t>(byte));
+    float y = __fmul_rn(static_cast<float>(qv), __fmul_rn(__ldg(scale + c + b), t));
+    if (bias != nullptr) y = __fadd_rn(y, __ldg(bias + c + b));
+    if (relu_after) y = y > 0.f ? y : 0.f;
+    v[b] = y;
+  }
+}
+
+template <bool POOL, bool USGN>
+__global__ void __launch_bounds__(256) codes_amax_kernel(const uint32_t* __restrict__ q, int H, int W, int C4,
+                                                         const float* __restrict__ scale, const float* __restrict__ sx,
+                                                         const float* __restrict__ bias, int relu_after,
+                                                         uint32_t* __restrict__ amax) {
+  const int n = blockIdx.y;
+  const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
+  const int64_t per = static_cast<int64_t>(Ho) * Wo * C4;
+  const float t = __ldg(sx + n);
+  float m = 0.f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < per; i += stride) {
+    const int c4 = static_cast<int>(i % C4);
+    const int64_t pix = i / C4;
+    const int xo = static_cast<int>(pix % Wo), yo = static_cast<int>(pix / Wo);
+    float v[4];
+    codes_values<USGN>(codes_word<POOL, USGN>(q, n, yo, xo, c4, H, W, C4), 4 * c4, t, scale, bias, relu_after != 0, v);
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+  }
+  m = warp_max(m);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float u = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    u = warp_max(u);
+    if (threadIdx.x == 0) atomicMax(amax + n, __float_as_uint(u));
+  }
+}
+
+template <bool POOL, bool USGN>
+__global__ void __launch_bounds__(256) codes_to_bordered_kernel(const uint32_t* __restrict__ q, int H, int W, int C4,
+                                                                const float* __restrict__ scale,
+                                                                const float* __restrict__ sx_in,
+                                                                const float* __restrict__ bias, int relu_after, int Cp,
+                                                                const uint32_t* __restrict__ amax,
+                                                                int8_t* __restrict__ xp, float* __restrict__ sx_out) {
+  const int yb = blockIdx.x;
+  const int n = blockIdx.y;
+  const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
+  const int Wp = Wo + 2;
+  const float s = scale_from_amax(__uint_as_float(amax[n]));
+  const float r = __frcp_rn(s);
+  const float t = __ldg(sx_in + n);
+  if (yb == 0 && threadIdx.x == 0) sx_out[n] = s;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(xp + (static_cast<int64_t>(n) * (Ho + 2) + yb) * Wp * Cp);
+  const int words = Wp * Cp / 4;
+  const bool border_row = yb == 0 || yb == Ho + 1;
+  for (int e = threadIdx.x; e < words; e += blockDim.x) {
+    const int xb = (e * 4) / Cp;
+    const int c = e * 4 - xb * Cp;
+    uint32_t word = 0;
+    if (!border_row && xb >= 1 && xb <= Wo && c < 4 * C4) {
+      float v[4];
+      codes_values<USGN>(codes_word<POOL, USGN>(q, n, yb - 1, xb - 1, c / 4, H, W, C4), c, t, scale, bias,
+                         relu_after != 0, v);
+      word = quant4(v[0], v[1], v[2], v[3], s, r);
+    }
+    dst[e] = word;
+  }
+}
+
+template <bool POOL, bool USGN>
+static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const float* scale, const float* sx_in,
+                         const float* bias, int relu_after, int Cp, uint32_t* amax, int8_t* xp, float* sx_out,
+                         cudaStream_t s) {
+  const int Ho = POOL ? H / 2 : H;
+  const int64_t per = static_cast<int64_t>(Ho) * (POOL ? W / 2 : W) * C4;
+  const int chunks = static_cast<int>(std::min<int64_t>((per + 256 * 8 - 1) / (256 * 8), 1024));
+  codes_amax_kernel<POOL, USGN><<<dim3(chunks, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, amax);
+  codes_to_bordered_kernel<POOL, USGN>
+      <<<dim3(Ho + 2, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, Cp, amax, xp, sx_out);
+}
+
 // wq [Co, Ci, 3, 3] -> wp [Co, 9, Cp], pad channels zero.
 __global__ void pack_weight_kernel(const int8_t* __restrict__ wq, int64_t Co, int64_t Ci, int8_t* __restrict__ wp,
                                    int64_t Cp) {
@@ -477,6 +584,39 @@ int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64
       return fail(XDNA_ERR_INVALID, "conv_quant: x_dtype %d is not f32/bf16/f16", x_dtype);
   }
   return check_launch("conv quantise");
+}
+
+int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
+                          const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,
+                          int8_t* xp, int64_t Cp, float* sx_out, uint32_t* amax_scratch, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && C >= 4 && C % 4 == 0 && H >= 1 && W >= 1,
+                 "conv_quant_codes: bad shape (C must be a positive multiple of 4)");
+  XDNA_CHECK_ARG(!pool || (H >= 2 && W >= 2), "conv_quant_codes: a 2x2 pool needs H, W >= 2");
+  XDNA_CHECK_ARG(Cp >= C && Cp % 16 == 0, "conv_quant_codes: Cp must be >= C and a multiple of 16");
+  XDNA_CHECK_ARG(N <= 65535 && H + 2 <= 65535 && N * H * W * C < (1ll << 40), "conv_quant_codes: too large");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(q && scale && sx_in && xp && sx_out && amax_scratch, "conv_quant_codes: null pointer");
+  XDNA_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 4 == 0 && aligned16(xp), "conv_quant_codes: q must be 4-byte and "
+                 "xp 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  XDNA_CUDA(cudaMemsetAsync(amax_scratch, 0, N * sizeof(uint32_t), s));
+  const uint32_t* qw = static_cast<const uint32_t*>(q);
+  const int n = static_cast<int>(N), h = static_cast<int>(H), w = static_cast<int>(W), c4 = static_cast<int>(C / 4);
+  const int cp = static_cast<int>(Cp), ra = relu_after ? 1 : 0;
+  if (pool) {
+    if (q_unsigned)
+      launch_codes<true, true>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, amax_scratch, xp, sx_out, s);
+    else
+      launch_codes<true, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, amax_scratch, xp, sx_out, s);
+  } else {
+    if (q_unsigned)
+      launch_codes<false, true>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, amax_scratch, xp, sx_out, s);
+    else
+      launch_codes<false, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, amax_scratch, xp, sx_out, s);
+  }
+  return check_launch("conv quantise (int8 codes)");
 }
 
 int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,

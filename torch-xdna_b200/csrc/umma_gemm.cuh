@@ -45,6 +45,7 @@ enum EpiMode {
                        // a TMA reduce-add over tmC, which then maps the residual)
   EPI_SWIGLU = 7,      // columns come as 32 gate / 32 up pairs: act = silu(gate) * up -> bf16
   EPI_QKV = 8,         // q / k heads: RMSNorm over the head + weight + RoPE -> bf16; v heads -> bf16 V^T
+  EPI_CONV_QNHWC = 9,  // requantised int8 / uint8, channels-last [N, H, W, Co]
 };
 
 // Geometry of the fused q/k/v projection (Qwen3-0.6B): 16 q heads, 8 k heads, 8 v heads of 128.
@@ -368,6 +369,27 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     }
     best = __reduce_max_sync(kFull, best);
     if (lane_id() == 0 && best > 0) atomicMax(a.acc_max, best);
+  } else if constexpr (EPI == EPI_CONV_QNHWC) {
+    if (!valid) return;
+    // out[img, yp-1, xp-1, n0 ..]: this pixel's 32 codes are 32 contiguous bytes
+    uint8_t* o = static_cast<uint8_t*>(a.out) + ((static_cast<int64_t>(img) * a.H + (yp - 1)) * a.W + (xp - 1)) * a.N + n0;
+    if (nvalid == 32 && a.vec_ok) {
+      uint32_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          word |= (static_cast<uint32_t>(requant(static_cast<int>(r[4 * k + b]), a.shift, a.relu)) & 0xFFu) << (8 * b);
+        w[k] = word;
+      }
+      reinterpret_cast<uint4*>(o)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      reinterpret_cast<uint4*>(o)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) o[j] = static_cast<uint8_t>(requant(static_cast<int>(r[j]), a.shift, a.relu) & 0xFF);
+    }
   } else if constexpr (EPI == EPI_CONV_Q) {
     if (!valid) return;
     const int64_t HW = static_cast<int64_t>(a.H) * a.W;

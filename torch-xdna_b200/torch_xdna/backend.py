@@ -112,6 +112,8 @@ def offload_gemms(gm: torch.fx.GraphModule, example_inputs, cfg) -> int:
     if cfg.fuse:
         _fuse_shared_input(gm, cid)
     count += _offload_convs(gm, params, cid, attr, cfg)
+    if cfg.fuse:
+        _chain_convs(gm)
     gm.graph.lint()
     gm.recompile()
     return count
@@ -173,6 +175,84 @@ def _offload_convs(gm, params, cid, attr, cfg):
         gm.graph.erase_node(node)
         count += 1
     return count
+
+
+MAXPOOL2D = {F.max_pool2d, torch.max_pool2d}
+
+
+def _is_maxpool_2x2(n):
+    """max_pool2d(x, 2) / (x, 2, 2): a 2x2 window, stride 2, no padding, dilation 1, floor, no indices."""
+    if n.op != "call_function" or n.target not in MAXPOOL2D:
+        return False
+    names = ("input", "kernel_size", "stride", "padding", "dilation", "ceil_mode", "return_indices")
+    a = dict(zip(names, n.args), **n.kwargs)
+    stride = a.get("stride")
+    return (_pair(a.get("kernel_size")) == (2, 2) and (stride in (None, []) or _pair(stride) == (2, 2))
+            and _pair(a.get("padding", 0)) == (0, 0) and _pair(a.get("dilation", 1)) == (1, 1)
+            and not a.get("ceil_mode", False) and not a.get("return_indices", False))
+
+
+def _chain_convs(gm):
+    """Offloaded convs feeding the next offloaded conv directly or through a 2x2 max-pool, with the
+    activation in between used by nothing else, become xdna::conv3x3_chain nodes that pass int8 codes
+    [N, H, W, C] (and their float factors) instead of a float tensor: the int8 NHWC chaining the reference
+    names as its largest remaining conv cost (R:results/conv3x3_cascade.md:214-219). Same values: the next
+    conv's quantise rebuilds the float activation with the epilogue's f32 operations. Only float32
+    activations with a channel count divisible by 4 are chained."""
+    from .conv import IN_CODES, IN_CODES_POOL, IN_FLOAT, conv3x3_chain_int8, conv3x3_int8
+
+    def is_conv(n):
+        return isinstance(n, torch.fx.Node) and n.op == "call_function" and n.target is conv3x3_int8
+
+    def chainable(n):  # the activation n produces: f32, channels divisible by 4
+        t = n.meta.get("example_value")
+        return isinstance(t, torch.Tensor) and t.dtype == torch.float32 and t.dim() == 4 and t.shape[1] % 4 == 0
+
+    link = {}  # producer conv -> (consumer conv, pool node or None)
+    for c2 in gm.graph.nodes:
+        if not is_conv(c2):
+            continue
+        src, pool = c2.args[0], None
+        if isinstance(src, torch.fx.Node) and _is_maxpool_2x2(src) and len(src.users) == 1:
+            pool, src = src, src.args[0]
+        if is_conv(src) and len(src.users) == 1 and chainable(src) and src not in link:
+            link[src] = (c2, pool)
+    if not link:
+        return 0
+    fed = {c2: (c1, pool) for c1, (c2, pool) in link.items()}
+    codes = {}  # producer -> (codes node, meta node, its ReLU applies after the bias)
+    erase = []
+    for n in list(gm.graph.nodes):
+        if n not in link and n not in fed:
+            continue
+        x, w, b, relu, cid = n.args[:5]
+        post_relu = n.args[5] if len(n.args) > 5 else False
+        if n in fed:
+            c1, pool = fed[n]
+            xin, xmeta, in_ra = codes[c1]
+            in_mode = IN_CODES_POOL if pool is not None else IN_CODES
+            if pool is not None:
+                erase.append(pool)
+        else:
+            xin, xmeta, in_mode, in_ra = x, None, IN_FLOAT, False
+        out_q = n in link
+        with gm.graph.inserting_after(n):
+            call = gm.graph.call_function(conv3x3_chain_int8, (xin, xmeta, w, b, relu, cid, post_relu, in_mode, in_ra,
+                                                               out_q))
+        with gm.graph.inserting_after(call):
+            first = gm.graph.call_function(operator.getitem, (call, 0))
+        with gm.graph.inserting_after(first):
+            second = gm.graph.call_function(operator.getitem, (call, 1))
+        if out_q:
+            codes[n] = (first, second, post_relu)
+        else:
+            first.meta.update(n.meta)
+            n.replace_all_uses_with(first)
+        erase.append(n)
+    for n in reversed(list(gm.graph.nodes)):  # consumers before producers
+        if n in erase:
+            gm.graph.erase_node(n)
+    return len(link)
 
 
 def _out_features(w):

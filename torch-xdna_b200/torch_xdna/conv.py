@@ -47,6 +47,12 @@ def conv3x3_int8(x, weight, bias, relu: bool, cfg_id: int, post_relu: bool = Fal
     return torch.ops.xdna.conv3x3_fused(x, weight, bias, relu, cfg_id, post_relu)
 
 
+def conv3x3_chain_int8(x, xmeta, weight, bias, relu: bool, cfg_id: int, post_relu: bool, in_mode: int,
+                       in_relu_after: bool, out_q: bool):
+    """One conv of a chain whose activations between convs stay int8 (xdna::conv3x3_chain)."""
+    return torch.ops.xdna.conv3x3_chain(x, xmeta, weight, bias, relu, cfg_id, post_relu, in_mode, in_relu_after, out_q)
+
+
 def channels_padded(c):
     return kernels.round_up(c, 16)
 
@@ -204,3 +210,87 @@ def conv3x3_fused(cfg, x, weight, bias, relu, post_relu=False):
     stats.seconds[DEVICE] += time.perf_counter() - t0
     stats.macs[DEVICE] += n * co * ci * h * w * 9
     return y
+
+
+# int8 chaining: IN_FLOAT takes a float input; IN_CODES / IN_CODES_POOL take the previous conv's codes
+IN_FLOAT, IN_CODES, IN_CODES_POOL = 0, 1, 2
+
+
+def codes_meta(sx, scale, bias, co):
+    """The float data that turns a conv's codes back into its output: sx [N], scale [Co], bias [Co]."""
+    b = bias.float() if bias is not None else torch.zeros((co,), dtype=torch.float32, device=scale.device)
+    return torch.cat([sx, scale, b])
+
+
+def codes_to_float(q, meta, relu_after, pool):
+    """The float activation a chain's codes stand for, on the CPU with torch's f32 ops in the epilogue's
+    order (float(q) * (scale * sx) + bias, max(., 0), 2x2 max-pool), NCHW: the reference's own tensor."""
+    n, h, w, c = q.shape
+    m = meta.cpu()
+    sx, scale, bias = m[:n], m[n:n + c], m[n + c:n + 2 * c]
+    t = scale[None, :] * sx[:, None]                                  # [N, C], rounded as scale * sx
+    y = q.cpu().to(torch.int32).float() * t[:, None, None, :] + bias  # NHWC
+    if relu_after:
+        y = torch.relu(y)
+    y = y.permute(0, 3, 1, 2)
+    return torch.nn.functional.max_pool2d(y, 2) if pool else y
+
+
+def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu_after, out_q):
+    """A conv of a chain (R:torch_xdna/conv.py:43-51 applied layer after layer, with the graph's ReLU and
+    2x2 max-pool between): the activations between convs stay int8 codes [N, H, W, C] with their float
+    factors, and the next conv's quantise rebuilds the float values the reference would have (same f32
+    operations), pools them on the codes (exact: the value grows with the code) and quantises per image.
+    x: the float input [N, Ci, H, W] (IN_FLOAT), or the previous conv's codes [N, H, W, Ci] with
+    xmeta = codes_meta(...) (IN_CODES; IN_CODES_POOL: 2x2 max-pooled first). in_relu_after: the previous
+    conv's ReLU applies after its bias. Returns (codes [N, H, W, Co], their meta) when out_q, else (the
+    float output [N, Co, H, W] channels-last, an empty tensor)."""
+    assert not (relu and post_relu), "relu fuses into the requantise, post_relu after the bias: one of them"
+    kernels._cuda(x, xmeta, weight, bias)
+    if in_mode == IN_FLOAT:
+        n, ci, h, w = x.shape
+    else:
+        n, hq, wq, ci = x.shape
+        h, w = (hq // 2, wq // 2) if in_mode == IN_CODES_POOL else (hq, wq)
+    co = weight.shape[0]
+    t0 = time.perf_counter()
+    with _lock:
+        layer = _layer(weight, h, w, relu)
+        xp = _bordered(n, h, w, layer.cp, x.device)
+        sx = torch.empty((n,), dtype=torch.float32, device=x.device)
+        scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
+        if in_mode == IN_FLOAT:
+            xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
+            if _channels_last(xc):
+                kernels.conv_quant_channels_last(xc, xp, sx, scratch)
+            else:
+                xc = xc.contiguous()
+                kernels.conv_quant(xc, xp, sx, scratch)
+            float_in = lambda: xc.float().cpu()  # noqa: E731
+        else:
+            xq = x.contiguous()
+            kernels.conv_quant_codes(xq, xmeta[n:n + ci], xmeta[:n], xmeta[n + ci:n + 2 * ci], in_relu_after,
+                                     in_mode == IN_CODES_POOL, xp, sx, scratch)
+            float_in = lambda: codes_to_float(xq, xmeta, in_relu_after, in_mode == IN_CODES_POOL)  # noqa: E731
+        stats.launches += 2
+        if layer.shift is None:
+            layer.calibrate(xp)
+
+        def xq_cpu():
+            xf = float_in()
+            s = xf.abs().amax(dim=(1, 2, 3), keepdim=True).clamp(min=1e-8) / 127
+            return torch.round(xf / s).clamp(-127, 127).to(torch.int8)
+
+        _verify(cfg, layer, xp, xq_cpu)
+        if out_q:
+            q = torch.empty((n, h, w, co), dtype=torch.uint8 if relu else torch.int8, device=x.device)
+            kernels.conv3x3(xp, layer.wp, n, ci, co, h, w, kernels.CONV_Q_NHWC, shift=layer.shift, relu=relu, out=q)
+            stats.launches += 1
+            out = (q, codes_meta(sx, layer.scale, bias, co))
+        else:
+            dtype = x.dtype if in_mode == IN_FLOAT else torch.float32
+            out = (layer.dequant(xp, n, sx, bias, dtype, post_relu), sx.new_empty((0,)))
+    stats.calls[DEVICE] += 1
+    stats.seconds[DEVICE] += time.perf_counter() - t0
+    stats.macs[DEVICE] += n * co * ci * h * w * 9
+    return out

@@ -24,7 +24,7 @@ F32, BF16, F16, I32, I8, U8 = 0, 1, 2, 3, 4, 5
 DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16, torch.int32: I32, torch.int8: I8,
                torch.uint8: U8}
 # conv3x3 modes
-CONV_Q, CONV_DEQUANT, CONV_CALIBRATE = 0, 1, 2
+CONV_Q, CONV_DEQUANT, CONV_CALIBRATE, CONV_Q_NHWC = 0, 1, 2, 3
 # status codes
 ERR_TIMEOUT = -4
 
@@ -58,6 +58,7 @@ def _load():
         "xdna_gemm_i8": ([P, I64, P, I64, I64, I64, I64, P, P, P, I, P, I, I64, P], I),
         "xdna_conv_quant_nhwc": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_channels_last": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
+        "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
         "xdna_conv_pack_input": ([P, I64, I64, I64, I64, P, I64, P], I),
         "xdna_conv_pack_weight": ([P, I64, I64, P, I64, P], I),
         "xdna_conv3x3_i8": ([P, P, I64, I64, I64, I64, I64, I64, I, I, I, P, P, P, I, P, I, P, P], I),
@@ -205,6 +206,18 @@ def conv_quant_channels_last(x, xp, sx, scratch):
     N, C, H, W = x.shape
     _check("xdna_conv_quant_channels_last", L.xdna_conv_quant_channels_last(
         _p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp), xp.shape[-1], _p(sx), _p(scratch), _stream()))
+
+
+def conv_quant_codes(q, scale, sx_in, bias, relu_after, pool, xp, sx, scratch):
+    """The next conv's bordered input xp from a conv's channels-last codes q [N, H, W, C] (uint8 / int8):
+    y = float(q) * (scale * sx_in) (+ bias) (then max(y, 0)), 2x2 max-pooled when `pool`, quantised per
+    image (xdna_conv_quant_codes)."""
+    L = require()
+    _cuda(q, scale, sx_in, bias, xp, sx, scratch)
+    N, H, W, C = q.shape
+    _check("xdna_conv_quant_codes", L.xdna_conv_quant_codes(
+        _p(q), int(q.dtype == torch.uint8), N, C, H, W, _p(scale), _p(sx_in), _p(bias), int(relu_after), int(pool),
+        _p(xp), xp.shape[-1], _p(sx), _p(scratch), _stream()))
 
 
 def conv_pack_input(xq, xp):
