@@ -3,9 +3,10 @@
 Schemas are the reference's, unchanged (R:torch_xdna/ops.py:25-89), so graphs and code that call
 torch.ops.xdna.* keep working; the implementations call the B200 kernels. To the rest of
 torch.compile each op is opaque with a shape function (the fake impl), and Inductor calls it as an
-extern kernel. One op is new: xdna::conv3x3_fused, the whole quantise -> conv -> dequantise of
+extern kernel. Two ops are new: xdna::conv3x3_fused, the whole quantise -> conv -> dequantise of
 conv3x3_int8 as one op, because on the B200 those three steps are kernels of ours rather than
-graph ops for the CPU compiler to fuse.
+graph ops for the CPU compiler to fuse; and xdna::conv3x3_chain, the same for a conv inside a chain of
+convs whose activations between them stay int8 codes.
 """
 
 from typing import Optional
