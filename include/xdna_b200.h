@@ -48,6 +48,11 @@ extern "C" {
 #define XDNA_CONV_CALIBRATE 2 /* *acc_max = max over the sums of image 0 of (relu ? max(acc,0) : |acc|) */
 #define XDNA_CONV_Q_NHWC 3    /* q as XDNA_CONV_Q, written channels-last [N, H, W, Co]: the int8 form in which
                                  one conv's output feeds the next (xdna_conv_quant_codes) */
+/* Or'ed into a mode: one tap at offset 0 instead of the 3x3 stencil's nine, i.e. a 1x1 conv over the
+ * bordered input with weights wp [Co, 1, Cp]. With the input from xdna_conv_quant_taps (the nine taps of
+ * a few channels packed into each pixel's row) and the weights packed the same way, it is the 3x3 conv
+ * of a layer with <= 7 input channels in one K block instead of nine. */
+#define XDNA_CONV_SINGLE_TAP 16
 /* `relu` of xdna_conv3x3_i8: 0 none; 1 fused into the requantise ([0,255] uint8, the reference's ReLU of
  * a bias-free conv); XDNA_RELU_AFTER_BIAS (DEQUANT only) applied to the dequantised output after the
  * bias, the requantise saturating to int8 — the same values as torch.relu on the DEQUANT output. */
@@ -119,6 +124,14 @@ int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t
  * max_pool2d, and the next conv3x3_int8's quantise R:torch_xdna/conv.py:45-46, for a chain of convs whose
  * intermediate activations have no other use (the int8 NHWC chaining the reference names as its largest
  * remaining cost). */
+/* xdna_conv_quant_nhwc for a layer of C <= 7 input channels with the 3x3 stencil's taps packed into each
+ * pixel's row: xp [N, H+2, W+2, Kp] (Kp = round_up(9 C, 16)), byte t * C + c of bordered pixel (yb, xb) is
+ * the quantised x[n, c, yb - 2 + t / 3, xb - 2 + t % 3] (0 outside the image), the rest zeros. The same
+ * per-image scale and quantised values as xdna_conv_quant_nhwc; the conv then runs with
+ * XDNA_CONV_SINGLE_TAP and weights wp [Co, 1, Kp], byte t * C + c of row co = wq[co, c, t / 3, t % 3]. */
+int xdna_conv_quant_taps(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,
+                         int64_t Kp, float* sx, uint32_t* amax_scratch, void* stream);
+
 int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
                           const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,
                           int8_t* xp, int64_t Cp, float* sx_out, uint32_t* amax_scratch, void* stream);

@@ -72,9 +72,10 @@ def test_conv_q_bitexact_vs_oracle(cuda, relu, n, ci, co, h, w):
 
 @pytest.mark.parametrize("post_relu", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-# (2, 64, 64, ...) and (3, 40, 128, ...): weights resident in shared memory; (5, 160, 300, ...): CTA pairs
+# (2, 64, 64, ...) and (3, 40, 128, ...): weights resident in shared memory; (5, 160, 300, ...): CTA pairs;
+# (2, 3, 64, ...) and (1, 7, 20, ...): <= 7 input channels, the stencil's taps packed into the channels
 @pytest.mark.parametrize("n,ci,co,h,w", [(2, 96, 80, 30, 50), (5, 160, 300, 40, 52), (2, 64, 64, 30, 50),
-                                         (3, 40, 128, 21, 19)])
+                                         (3, 40, 128, 21, 19), (2, 3, 64, 33, 47), (1, 7, 20, 9, 5)])
 def test_conv_fused_dequant_bitexact(cuda, dtype, post_relu, n, ci, co, h, w):
     """The dequantise (+ bias) to x.dtype, bit for bit; post_relu equals torch.relu of it."""
     x, wt, b = mg.conv_inputs(5, n, ci, co, h, w, bias=True)

@@ -159,6 +159,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   if (rc != XDNA_OK) return rc;
   XDNA_CHECK_ARG(N >= 0 && Ci >= 1 && Co >= 1 && H >= 1 && W >= 1, "conv3x3: bad shape");
   XDNA_CHECK_ARG(Cp >= Ci && Cp % 16 == 0, "conv3x3: Cp must be >= Ci and a multiple of 16");
+  const bool single_tap = (mode & XDNA_CONV_SINGLE_TAP) != 0;
+  mode &= ~XDNA_CONV_SINGLE_TAP;
   XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE ||
                      mode == XDNA_CONV_Q_NHWC,
                  "conv3x3: unknown mode %d", mode);
@@ -191,7 +193,8 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   a.N = static_cast<int>(Co);
   const int kb = Cp <= 64 ? 64 : kBKBytes;  // K block bytes (= channels) per tap
   a.cblocks = static_cast<int>((Cp + kb - 1) / kb);
-  a.num_kb = 9 * a.cblocks;
+  a.single_tap = single_tap ? 1 : 0;
+  a.num_kb = (single_tap ? 1 : 9) * a.cblocks;
   a.m_tiles = static_cast<int>((NP + kBM - 1) / kBM);
   const int bn = choose_bn(a.m_tiles, Co, sms);
   a.n_tiles = static_cast<int>((Co + bn - 1) / bn);
@@ -229,8 +232,9 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
     if (rc != XDNA_OK) return rc;
   }
   {
-    const uint64_t dims[3] = {static_cast<uint64_t>(Cp), 9, static_cast<uint64_t>(Co)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(9 * Cp)};
+    const uint64_t taps = single_tap ? 1 : 9;
+    const uint64_t dims[3] = {static_cast<uint64_t>(Cp), taps, static_cast<uint64_t>(Co)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(taps * Cp)};
     const uint32_t box[3] = {static_cast<uint32_t>(kb), 1, static_cast<uint32_t>(pair ? bn / 2 : bn)};
     rc = encode_tma(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wp, dims, strides, box, "conv3x3 weights",
                     kb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);

@@ -399,6 +399,38 @@ __global__ void __launch_bounds__(256) cl_to_bordered_kernel(const T* __restrict
   }
 }
 
+// ---------------------------------------------------------------------------- NCHW -> tap-packed bordered
+// One thread per bordered pixel (yb, xb), i.e. output pixel (yb - 1, xb - 1): the 3x3 stencil's taps of
+// C <= 7 channels as 9 C quantised bytes of its Kp-byte row, tap t = 3 dy + dx reading input pixel
+// (yb - 2 + dy, xb - 2 + dx); zeros outside the image and past byte 9 C. grid (ceil((H+2)(W+2) / 256), N).
+template <typename T>
+__global__ void __launch_bounds__(256) to_taps_kernel(const T* __restrict__ x, int C, int H, int W, int Kp,
+                                                      const uint32_t* __restrict__ amax, int8_t* __restrict__ xp,
+                                                      float* __restrict__ sx) {
+  const int n = blockIdx.y;
+  const int Wp = W + 2, HWp = (H + 2) * Wp;
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  const float s = scale_from_amax(__uint_as_float(amax[n]));
+  const float r = __frcp_rn(s);
+  if (blockIdx.x == 0 && threadIdx.x == 0) sx[n] = s;
+  if (p >= HWp) return;
+  const int yb = p / Wp, xb = p - yb * Wp;
+  uint32_t words[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) words[i] = 0;
+  for (int t = 0; t < 9; ++t) {
+    const int y = yb - 2 + t / 3, xx = xb - 2 + t % 3;
+    if (y < 0 || y >= H || xx < 0 || xx >= W) continue;
+    for (int c = 0; c < C; ++c) {
+      const uint32_t q = quant_byte(to_f32(x[((static_cast<int64_t>(n) * C + c) * H + y) * W + xx]), s, r) & 0xFFu;
+      const int k = t * C + c;
+      words[k >> 2] |= q << (8 * (k & 3));
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(xp + (static_cast<int64_t>(n) * HWp + p) * Kp);
+  for (int i = 0; i < Kp / 16; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+}
+
 // ---------------------------------------------------------------------------- int8 codes -> bordered NHWC
 // The next conv's input from a conv's channels-last codes q [N, H, W, C] (C % 4 == 0), read as words of 4
 // channels. A code stands for y = float(q) * (scale[c] * sx[n]) (+ bias[c]) (then max(y, 0)), the same
@@ -584,6 +616,44 @@ int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64
       return fail(XDNA_ERR_INVALID, "conv_quant: x_dtype %d is not f32/bf16/f16", x_dtype);
   }
   return check_launch("conv quantise");
+}
+
+int xdna_conv_quant_taps(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,
+                         int64_t Kp, float* sx, uint32_t* amax_scratch, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && C >= 1 && C <= 7 && H >= 1 && W >= 1, "conv_quant_taps: bad shape (1 <= C <= 7)");
+  XDNA_CHECK_ARG(Kp >= 9 * C && Kp % 16 == 0 && Kp <= 64, "conv_quant_taps: Kp must cover 9 C, a multiple of 16");
+  XDNA_CHECK_ARG(N <= 65535 && (H + 2) * (W + 2) < (1ll << 31), "conv_quant_taps: too large");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(x && xp && sx && amax_scratch, "conv_quant_taps: null pointer");
+  XDNA_CHECK_ARG(aligned16(xp), "conv_quant_taps: xp must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  XDNA_CUDA(cudaMemsetAsync(amax_scratch, 0, N * sizeof(uint32_t), s));
+  const int64_t per_image = C * H * W;
+  const int chunks = static_cast<int>(std::min<int64_t>((per_image + 256 * 16 - 1) / (256 * 16), 1024));
+  dim3 g_amax(chunks, static_cast<unsigned>(N));
+  dim3 g(static_cast<unsigned>(((H + 2) * (W + 2) + 255) / 256), static_cast<unsigned>(N));
+  const int c = static_cast<int>(C), h = static_cast<int>(H), w = static_cast<int>(W), kp = static_cast<int>(Kp);
+  switch (x_dtype) {
+    case XDNA_F32:
+      image_amax_kernel<float><<<g_amax, 256, 0, s>>>(static_cast<const float*>(x), per_image, amax_scratch);
+      to_taps_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), c, h, w, kp, amax_scratch, xp, sx);
+      break;
+    case XDNA_BF16:
+      image_amax_kernel<__nv_bfloat16>
+          <<<g_amax, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), per_image, amax_scratch);
+      to_taps_kernel<__nv_bfloat16>
+          <<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), c, h, w, kp, amax_scratch, xp, sx);
+      break;
+    case XDNA_F16:
+      image_amax_kernel<__half><<<g_amax, 256, 0, s>>>(static_cast<const __half*>(x), per_image, amax_scratch);
+      to_taps_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(x), c, h, w, kp, amax_scratch, xp, sx);
+      break;
+    default:
+      return fail(XDNA_ERR_INVALID, "conv_quant_taps: x_dtype %d is not f32/bf16/f16", x_dtype);
+  }
+  return check_launch("conv quantise (taps packed)");
 }
 
 int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,

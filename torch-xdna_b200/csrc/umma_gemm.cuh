@@ -76,6 +76,8 @@ struct GemmArgs {
   int m_tiles, n_tiles;
   // conv geometry
   int cblocks;         // 128-channel blocks per tap
+  int single_tap;      // 1: one tap at offset 0 (a 1x1 conv over the bordered layout, e.g. taps packed into
+                       // channels); 0: the 3x3 stencil's 9 taps
   int Wp, HWp;         // W + 2, (H + 2) * (W + 2)
   int H, W;
   FastDiv div_wp, div_hwp;
@@ -798,10 +800,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
       bool ok = true;
-      if constexpr (RB) {  // the weights of all 9 taps, once
+      if constexpr (RB) {  // the weights of all taps, once
         if (t_first < total) {
-          mbar_arrive_expect_tx(bres, 9 * B_BYTES);
-          for (int tap = 0; tap < 9; ++tap) tma_load_3d(smRes + tap * B_BYTES, &tmB, bres, 0, tap, 0);
+          const int ntaps = args.single_tap ? 1 : 9;
+          mbar_arrive_expect_tx(bres, ntaps * B_BYTES);
+          for (int tap = 0; tap < ntaps; ++tap) tma_load_3d(smRes + tap * B_BYTES, &tmB, bres, 0, tap, 0);
         }
       }
       for (int t = t_first; t < total && ok; t += t_step) {
@@ -827,8 +830,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               const int tap = kb / args.cblocks;
               const int cb = kb - tap * args.cblocks;
-              tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, cb * K_ELEMS,
-                               tile_row0(mb) + (tap / 3 - 1) * args.Wp + (tap % 3 - 1));
+              const int off = args.single_tap ? 0 : (tap / 3 - 1) * args.Wp + (tap % 3 - 1);
+              tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, cb * K_ELEMS, tile_row0(mb) + off);
               tma_load_3d_pair(smB + stage * B_BYTES, &tmB, fb, cb * K_ELEMS, tap, b_row);
             }
           } else if constexpr (LOAD == LOAD_GEMM) {
@@ -843,8 +846,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(full + stage, STAGE_TX);
             const int tap = kb / args.cblocks;
             const int cb = kb - tap * args.cblocks;
-            const int dy = tap / 3 - 1;
-            const int dx = tap % 3 - 1;
+            const int dy = args.single_tap ? 0 : tap / 3 - 1;
+            const int dx = args.single_tap ? 0 : tap % 3 - 1;
             tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, cb * K_ELEMS, mb * kBM + dy * args.Wp + dx);
             if constexpr (!RB) tma_load_3d(smB + stage * B_BYTES, &tmB, full + stage, cb * K_ELEMS, tap, nb * BN);
           }

@@ -58,9 +58,11 @@ def channels_padded(c):
 
 
 class ConvLayer:
-    """One conv weight at one input size: int8 weights packed for the implicit GEMM, the shift."""
+    """One conv weight at one input size: int8 weights packed for the implicit GEMM, the shift.
+    taps: a layer of <= 7 input channels whose float input is quantised with the stencil's 9 taps packed
+    into each pixel's row (conv_quant_taps): its conv is one K block of a single tap instead of nine."""
 
-    def __init__(self, weight, h, w, relu):
+    def __init__(self, weight, h, w, relu, taps=False):
         kernels._cuda(weight)
         co, ci = weight.shape[:2]
         wf = weight.detach()
@@ -73,8 +75,17 @@ class ConvLayer:
         self.ci, self.co, self.cp = ci, co, channels_padded(ci)
         wq4 = self.wq[:, :ci * 9].contiguous().view(co, ci, 3, 3)
         self.wq4 = wq4
-        self.wp = torch.empty((co, 9, self.cp), dtype=torch.int8, device=weight.device)
-        kernels.conv_pack_weight(wq4, self.wp)
+        self.taps = bool(taps) and ci <= 7
+        if self.taps:
+            # byte (3 ky + kx) C + c of row co = wq[co, c, ky, kx]: the order conv_quant_taps packs the input in
+            self.cp = channels_padded(9 * ci)
+            self.wp = torch.zeros((co, 1, self.cp), dtype=torch.int8, device=weight.device)
+            self.wp[:, 0, :9 * ci] = wq4.permute(0, 2, 3, 1).reshape(co, 9 * ci)
+            self.mode_flag, self.ci_k = kernels.CONV_SINGLE_TAP, 9 * ci
+        else:
+            self.wp = torch.empty((co, 9, self.cp), dtype=torch.int8, device=weight.device)
+            kernels.conv_pack_weight(wq4, self.wp)
+            self.mode_flag, self.ci_k = 0, ci
         self.h, self.w, self.relu = h, w, relu
         self.shift = self.scale = None
         self.checked = False
@@ -83,8 +94,8 @@ class ConvLayer:
     def calibrate(self, xp):
         """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:327-332)."""
         acc_max = torch.empty((1,), dtype=torch.int32, device=xp.device)
-        kernels.conv3x3(xp, self.wp, 1, self.ci, self.co, self.h, self.w, kernels.CONV_CALIBRATE, relu=self.relu,
-                        acc_max=acc_max)
+        kernels.conv3x3(xp, self.wp, 1, self.ci_k, self.co, self.h, self.w, kernels.CONV_CALIBRATE | self.mode_flag,
+                        relu=self.relu, acc_max=acc_max)
         stats.launches += 1
         top = float(int(acc_max.item()))
         shift = min(31, max(1, math.ceil(math.log2(max(top * 1.25, 1.0) / (255 if self.relu else 127)))))
@@ -95,8 +106,8 @@ class ConvLayer:
     def q(self, xp, n):
         out = torch.empty((n, self.co, self.h, self.w), dtype=torch.uint8 if self.relu else torch.int8,
                           device=xp.device)
-        kernels.conv3x3(xp, self.wp, n, self.ci, self.co, self.h, self.w, kernels.CONV_Q, shift=self.shift,
-                        relu=self.relu, out=out)
+        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_Q | self.mode_flag,
+                        shift=self.shift, relu=self.relu, out=out)
         stats.launches += 1
         return out
 
@@ -106,8 +117,8 @@ class ConvLayer:
         out = torch.empty((n, self.co, self.h, self.w), dtype=dtype, device=xp.device,
                           memory_format=torch.channels_last)
         relu = kernels.RELU_AFTER_BIAS if post_relu else self.relu
-        kernels.conv3x3(xp, self.wp, n, self.ci, self.co, self.h, self.w, kernels.CONV_DEQUANT, shift=self.shift,
-                        relu=relu, scale=self.scale, sx=sx, bias=bias, out=out)
+        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_DEQUANT | self.mode_flag,
+                        shift=self.shift, relu=relu, scale=self.scale, sx=sx, bias=bias, out=out)
         stats.launches += 1
         return out
 
@@ -120,12 +131,12 @@ class ConvLayer:
         return q.clamp_(0, 255).to(torch.uint8) if self.relu else q.clamp_(-128, 127).to(torch.int8)
 
 
-def _layer(weight, h, w, relu):
-    key = (id(weight), h, w, relu)
+def _layer(weight, h, w, relu, taps=False):
+    key = (id(weight), h, w, relu, bool(taps))
     hit = _layers.get(key)
     if hit is not None and hit[0]() is weight:
         return hit[1]
-    layer = ConvLayer(weight, h, w, relu)
+    layer = ConvLayer(weight, h, w, relu, taps)
     _layers[key] = (weakref.ref(weight), layer)
     return layer
 
@@ -134,6 +145,18 @@ def _channels_last(t):
     """True when t [N, C, H, W] is stored channels-last and not also plain contiguous."""
     return (t.is_contiguous(memory_format=torch.channels_last) and not t.is_contiguous()
             and t.data_ptr() % 16 == 0)
+
+
+def _quantise_float(layer, xc, xp, sx, scratch):
+    """The per-image quantise of a float input into layer's bordered layout: taps packed for a layer of
+    few channels, a streaming pass for a channels-last input (e.g. the previous conv's output), else the
+    NCHW transpose."""
+    if layer.taps:
+        kernels.conv_quant_taps(xc.contiguous(), xp, sx, scratch)
+    elif _channels_last(xc):
+        kernels.conv_quant_channels_last(xc, xp, sx, scratch)
+    else:
+        kernels.conv_quant(xc.contiguous(), xp, sx, scratch)
 
 
 def _bordered(n, h, w, cp, device):
@@ -185,16 +208,12 @@ def conv3x3_fused(cfg, x, weight, bias, relu, post_relu=False):
     co = weight.shape[0]
     t0 = time.perf_counter()
     with _lock:
-        layer = _layer(weight, h, w, relu)
+        layer = _layer(weight, h, w, relu, taps=ci <= 7)
         xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
         xp = _bordered(n, h, w, layer.cp, x.device)
         sx = torch.empty((n,), dtype=torch.float32, device=x.device)
         scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
-        if _channels_last(xc):      # e.g. the previous conv's output: a streaming quantise, no transpose
-            kernels.conv_quant_channels_last(xc, xp, sx, scratch)
-        else:
-            xc = xc.contiguous()
-            kernels.conv_quant(xc, xp, sx, scratch)
+        _quantise_float(layer, xc, xp, sx, scratch)
         stats.launches += 2
         if layer.shift is None:
             layer.calibrate(xp)
@@ -255,17 +274,13 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
     co = weight.shape[0]
     t0 = time.perf_counter()
     with _lock:
-        layer = _layer(weight, h, w, relu)
+        layer = _layer(weight, h, w, relu, taps=in_mode == IN_FLOAT and ci <= 7)
         xp = _bordered(n, h, w, layer.cp, x.device)
         sx = torch.empty((n,), dtype=torch.float32, device=x.device)
         scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
         if in_mode == IN_FLOAT:
             xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
-            if _channels_last(xc):
-                kernels.conv_quant_channels_last(xc, xp, sx, scratch)
-            else:
-                xc = xc.contiguous()
-                kernels.conv_quant(xc, xp, sx, scratch)
+            _quantise_float(layer, xc, xp, sx, scratch)
             float_in = lambda: xc.float().cpu()  # noqa: E731
         else:
             xq = x.contiguous()
@@ -284,7 +299,8 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
         _verify(cfg, layer, xp, xq_cpu)
         if out_q:
             q = torch.empty((n, h, w, co), dtype=torch.uint8 if relu else torch.int8, device=x.device)
-            kernels.conv3x3(xp, layer.wp, n, ci, co, h, w, kernels.CONV_Q_NHWC, shift=layer.shift, relu=relu, out=q)
+            kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, kernels.CONV_Q_NHWC | layer.mode_flag,
+                            shift=layer.shift, relu=relu, out=q)
             stats.launches += 1
             out = (q, codes_meta(sx, layer.scale, bias, co))
         else:

@@ -25,6 +25,7 @@ DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16, tor
                torch.uint8: U8}
 # conv3x3 modes
 CONV_Q, CONV_DEQUANT, CONV_CALIBRATE, CONV_Q_NHWC = 0, 1, 2, 3
+CONV_SINGLE_TAP = 16  # or'ed into a conv mode: one tap at offset 0 (taps packed into channels)
 # status codes
 ERR_TIMEOUT = -4
 
@@ -59,6 +60,7 @@ def _load():
         "xdna_conv_quant_nhwc": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_channels_last": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
+        "xdna_conv_quant_taps": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_pack_input": ([P, I64, I64, I64, I64, P, I64, P], I),
         "xdna_conv_pack_weight": ([P, I64, I64, P, I64, P], I),
         "xdna_conv3x3_i8": ([P, P, I64, I64, I64, I64, I64, I64, I, I, I, P, P, P, I, P, I, P, P], I),
@@ -206,6 +208,16 @@ def conv_quant_channels_last(x, xp, sx, scratch):
     N, C, H, W = x.shape
     _check("xdna_conv_quant_channels_last", L.xdna_conv_quant_channels_last(
         _p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp), xp.shape[-1], _p(sx), _p(scratch), _stream()))
+
+
+def conv_quant_taps(x, xp, sx, scratch):
+    """conv_quant for x [N, C <= 7, H, W] (NCHW contiguous) with the 3x3 stencil's taps packed into each
+    pixel's row of xp [N, H+2, W+2, Kp] (xdna_conv_quant_taps)."""
+    L = require()
+    _cuda(x, xp, sx, scratch)
+    N, C, H, W = x.shape
+    _check("xdna_conv_quant_taps", L.xdna_conv_quant_taps(_p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp),
+                                                          xp.shape[-1], _p(sx), _p(scratch), _stream()))
 
 
 def conv_quant_codes(q, scale, sx_in, bias, relu_after, pool, xp, sx, scratch):
