@@ -786,21 +786,31 @@ def run_conv(args, rank, world):
 
     stream = torch.cuda.current_stream()
     with torch.no_grad():
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(max(args.warmup, 3)):   # includes each layer's calibration and first-call verify
             step(x)
+        torch.cuda.synchronize()
+        # One step captured as a CUDA graph (the same kernels, launched without Python in between): with a
+        # half or quarter batch per GPU the per-op host work would otherwise pace the step
+        torch_xdna.stats.reset()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(x)
+        per_step = torch_xdna.stats.launches
+        graph.replay()
         barrier(world)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        torch_xdna.stats.reset()
         with ClockSampler(dev.index) as clocks:
             barrier(world)
             for i in range(args.steps):      # 32 x 64 x 224 x 224 activations (400 MB) exceed L2
                 starts[i].record(stream)
-                y = step(x)
+                graph.replay()
                 ends[i].record(stream)
             barrier(world)
-        launches = torch_xdna.stats.launches
-    total_s = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3, world)
+        launches = per_step * args.steps
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        del graph
+    total_s = max_over_ranks(sum(step_ms) / 1e3, world)
     value = 2 * vgg_macs(N_all) * args.steps / total_s / 1e12
     # roofline: the conv kernel of the largest-work layer (conv 64->64 at 224x224), timed alone
     from torch_xdna import conv as xconv
