@@ -1,0 +1,74 @@
+"""Host-side layouts and rebuilds that the kernels rely on, checked on the CPU: the RoPE table layout the
+q/k/v epilogue reads, the float activation a chain of convs' int8 codes stands for (the verify path's
+CPU rebuild, against a numpy restatement of the conv epilogue's arithmetic), and which max-pools the
+conv chaining pass takes into a chain."""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from torch_xdna import backend, conv, kernels
+
+
+def test_rope_layout_index():
+    """Frequency d of position p sits at (d / 4) * L * 4 + p * 4 + d % 4 (the header's layout)."""
+    L = 37
+    t = torch.arange(L * 64, dtype=torch.float32).reshape(L, 64)
+    flat = kernels.rope_layout(t).reshape(-1)
+    assert flat.shape[0] == L * 64
+    for p in (0, 1, 17, L - 1):
+        for d in (0, 3, 4, 31, 63):
+            assert flat[(d // 4) * L * 4 + p * 4 + d % 4] == t[p, d]
+
+
+def _epilogue_f32(q, scale, sx, bias, relu_after):
+    """numpy f32 restatement of the dequantising epilogue: float(q) * (scale[c] * sx[n]) + bias[c], each
+    operation rounded to f32, then max(y, 0)."""
+    n, h, w, c = q.shape
+    t = (scale[None, :].astype(np.float32) * sx[:, None].astype(np.float32)).astype(np.float32)
+    y = (q.astype(np.float32) * t[:, None, None, :]).astype(np.float32)
+    y = (y + bias[None, None, None, :].astype(np.float32)).astype(np.float32)
+    if relu_after:
+        y = np.maximum(y, np.float32(0))
+    return y
+
+
+@pytest.mark.parametrize("unsigned,relu_after,pool", [(False, True, False), (False, True, True),
+                                                      (False, False, True), (True, False, True)])
+def test_codes_to_float_matches_epilogue_arithmetic(unsigned, relu_after, pool):
+    g = np.random.default_rng(3)
+    n, h, w, c = 2, 7, 9, 12
+    q = (g.integers(0, 256, (n, h, w, c)) if unsigned else g.integers(-128, 128, (n, h, w, c)))
+    q = q.astype(np.uint8 if unsigned else np.int8)
+    sx = g.random(n, dtype=np.float32) * np.float32(0.1) + np.float32(1e-3)
+    scale = g.random(c, dtype=np.float32) * np.float32(0.05) + np.float32(1e-4)
+    bias = np.zeros(c, np.float32) if unsigned else (g.standard_normal(c).astype(np.float32) * np.float32(0.1))
+    meta = torch.from_numpy(np.concatenate([sx, scale, bias]))
+    got = conv.codes_to_float(torch.from_numpy(q), meta, relu_after, pool).numpy()
+    y = _epilogue_f32(q, scale, sx, bias, relu_after)            # NHWC
+    if pool:  # 2x2, stride 2, rounding the size down
+        hh, ww = h // 2, w // 2
+        y = y[:, :2 * hh, :2 * ww].reshape(n, hh, 2, ww, 2, c).max(axis=(2, 4))
+    want = y.transpose(0, 3, 1, 2)
+    assert got.shape == want.shape
+    assert np.array_equal(got, want)
+    # pooling the codes first gives the same values: the value grows with the code
+    if pool:
+        qp = q[:, :2 * (h // 2), :2 * (w // 2)].reshape(n, h // 2, 2, w // 2, 2, c).max(axis=(2, 4))
+        assert np.array_equal(_epilogue_f32(qp, scale, sx, bias, relu_after).transpose(0, 3, 1, 2), want)
+
+
+def _pool_node(*args, **kwargs):
+    g = torch.fx.Graph()
+    x = g.placeholder("x")
+    return g.call_function(F.max_pool2d, (x, *args), kwargs)
+
+
+@pytest.mark.parametrize("args,kwargs,ok", [
+    ((2,), {}, True), ((2, 2), {}, True), (((2, 2), (2, 2), 0, 1), {}, True), ((2,), {"stride": None}, True),
+    ((3,), {}, False), ((2, 1), {}, False), ((2, 2, 1), {}, False), ((2,), {"ceil_mode": True}, False),
+    ((2,), {"dilation": 2}, False), ((2,), {"return_indices": True}, False),
+])
+def test_maxpool_pattern(args, kwargs, ok):
+    assert backend._is_maxpool_2x2(_pool_node(*args, **kwargs)) is ok
