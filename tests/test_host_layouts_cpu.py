@@ -1,7 +1,7 @@
 """Host-side layouts and rebuilds that the kernels rely on, checked on the CPU: the RoPE table layout the
 q/k/v epilogue reads, the float activation a chain of convs' int8 codes stands for (the verify path's
-CPU rebuild, against a numpy restatement of the conv epilogue's arithmetic), and which max-pools the
-conv chaining pass takes into a chain."""
+CPU rebuild, against a numpy restatement of the conv epilogue's arithmetic and against the oracle's conv
+outputs), and which max-pools the conv chaining pass takes into a chain."""
 
 import numpy as np
 import pytest
@@ -72,3 +72,26 @@ def _pool_node(*args, **kwargs):
 ])
 def test_maxpool_pattern(args, kwargs, ok):
     assert backend._is_maxpool_2x2(_pool_node(*args, **kwargs)) is ok
+
+
+@pytest.mark.parametrize("bias,relu,pool", [(True, False, False), (True, False, True), (False, True, True)])
+def test_codes_rebuild_the_oracle_conv_output(bias, relu, pool):
+    """A conv's codes and factors, as the chain passes them, rebuild exactly the float output the oracle
+    (the reference's CPU route, pinned to its goldens) computes, after the graph's ReLU and max-pool."""
+    from oracle import xdna_oracle as orc
+
+    g = np.random.default_rng(5)
+    x = g.standard_normal((2, 12, 10, 14)).astype(np.float32)
+    w = (g.standard_normal((16, 12, 3, 3)) * 0.15).astype(np.float32)
+    b = (g.standard_normal(16) * 0.1).astype(np.float32) if bias else None
+    r = orc.conv3x3_int8(x, w, b, relu=relu)
+    y = torch.from_numpy(np.asarray(r["y"], np.float32))
+    if bias:                       # a biased conv's ReLU stays in the graph after it
+        y = torch.relu(y)
+    if pool:
+        y = F.max_pool2d(y, 2)
+    q = torch.from_numpy(np.ascontiguousarray(np.asarray(r["q"]).transpose(0, 2, 3, 1)))   # NHWC codes
+    meta = conv.codes_meta(torch.from_numpy(r["sx"].astype(np.float32)), torch.from_numpy(r["scale"]),
+                           torch.from_numpy(b) if bias else None, 16)
+    got = conv.codes_to_float(q, meta, relu_after=bias, pool=pool)
+    assert got.dtype == torch.float32 and torch.equal(got, y)
