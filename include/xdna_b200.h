@@ -167,8 +167,8 @@ int xdna_conv_pack_weight(const int8_t* wq, int64_t Co, int64_t Ci, int8_t* wp, 
  * only image 0 is computed and acc_max (one int32, cleared by this call) receives the maximum.
  * XDNA_CONV_Q_NHWC writes the same q as XDNA_CONV_Q, channels-last [N, H, W, Co] (XDNA_I8 / XDNA_U8).
  * Replaces tl.extra.npu.conv3x3.Conv3x3(...)(xq) as used by ConvLayer.npu
- * R:torch_xdna/conv.py:334-340,350-359, the CPU integers ConvLayer.cpu R:torch_xdna/conv.py:345-348,
- * the calibration sums of ConvLayer.calibrate R:torch_xdna/conv.py:327-332, and (DEQUANT) the
+ * R:torch_xdna/conv.py:78-84,94-103, the CPU integers ConvLayer.cpu R:torch_xdna/conv.py:86-92,
+ * the calibration sums of ConvLayer.calibrate R:torch_xdna/conv.py:71-76, and (DEQUANT) the
  * dequantise ops of conv3x3_int8 R:torch_xdna/conv.py:47-50. */
 int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, int64_t Cp, int64_t Co, int64_t H,
                     int64_t W, int mode, int shift, int relu, const float* scale, const float* sx, const void* bias,

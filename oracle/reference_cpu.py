@@ -71,7 +71,7 @@ def qwen3_stack(layers, final_norm, head, head_bias, x, allowed, theta=1e6, eps=
 
 
 def conv_layer(weight, relu):
-    """ConvLayer weights, R:torch_xdna/conv.py:314-319."""
+    """ConvLayer weights, R:torch_xdna/conv.py:58-63."""
     wf = weight.detach().float()
     sw = wf.abs().amax(dim=(1, 2, 3)).clamp(min=1e-8) / 127
     wq = torch.round(wf / sw[:, None, None, None]).clamp(-127, 127).to(torch.int8)
@@ -80,7 +80,7 @@ def conv_layer(weight, relu):
 
 
 def conv3x3_int8(x, layer, bias=None):
-    """conv3x3_int8 on the CPU route, R:torch_xdna/conv.py:43-51,327-348."""
+    """conv3x3_int8 on the CPU route, R:torch_xdna/conv.py:43-51,71-76,86-92."""
     sx = x.abs().amax(dim=(1, 2, 3), keepdim=True).float().clamp(min=1e-8) / 127
     xq = torch.round(x.float() / sx).clamp(-127, 127).to(torch.int8)
     acc = torch.nn.functional.conv2d(xq.to(layer["dt"]), layer["wq"].to(layer["dt"]), padding=1).to(torch.int32)

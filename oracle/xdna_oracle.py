@@ -114,7 +114,7 @@ def conv_quant(x):
 
 
 def conv_weight(w):
-    """ConvLayer int8 weights, R:torch_xdna/conv.py:314-316. w [Co, Ci, 3, 3] -> (wq, sw [Co])."""
+    """ConvLayer int8 weights, R:torch_xdna/conv.py:58-60. w [Co, Ci, 3, 3] -> (wq, sw [Co])."""
     w = np.asarray(w, dtype=F32)
     sw = (np.maximum(np.abs(w).reshape(w.shape[0], -1).max(axis=1), F32(1e-8)) / F32(127)).astype(F32)
     wq = np.clip(np.rint(w / sw[:, None, None, None]), -127, 127).astype(np.int8)
@@ -122,7 +122,7 @@ def conv_weight(w):
 
 
 def conv_acc(xq, wq):
-    """Exact int32 sums of the 3x3 / padding-1 conv of the integers, R:torch_xdna/conv.py:342-343."""
+    """Exact int32 sums of the 3x3 / padding-1 conv of the integers, R:torch_xdna/conv.py:86-87."""
     xq = np.asarray(xq, dtype=np.float64)
     wq = np.asarray(wq, dtype=np.float64)
     n, ci, h, w = xq.shape
@@ -138,7 +138,7 @@ def conv_acc(xq, wq):
 
 
 def calibrate_shift(acc0, relu):
-    """ConvLayer.calibrate, R:torch_xdna/conv.py:327-332 (acc0: the sums of the first image)."""
+    """ConvLayer.calibrate, R:torch_xdna/conv.py:71-76 (acc0: the sums of the first image)."""
     import math
 
     acc0 = np.asarray(acc0, dtype=np.int64)
@@ -147,7 +147,7 @@ def calibrate_shift(acc0, relu):
 
 
 def requant(acc, shift, relu):
-    """ConvLayer.cpu, R:torch_xdna/conv.py:345-348: round half up by an arithmetic shift, saturate."""
+    """ConvLayer.cpu, R:torch_xdna/conv.py:89-92: round half up by an arithmetic shift, saturate."""
     q = (np.asarray(acc, dtype=np.int32) + np.int32(1 << (shift - 1))) >> np.int32(shift)
     return np.clip(q, 0, 255).astype(np.uint8) if relu else np.clip(q, -128, 127).astype(np.int8)
 

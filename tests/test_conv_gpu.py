@@ -87,6 +87,31 @@ def test_conv_fused_dequant_bitexact(cuda, dtype, post_relu, n, ci, co, h, w):
     assert np.array_equal(y.float().cpu().numpy(), w)
 
 
+@pytest.mark.parametrize("layout", ["nchw", "channels_last"])
+def test_conv_quant_nan_image_scale(cuda, layout):
+    """An image holding a NaN gets a NaN scale, as the reference's x.abs().amax(...).clamp(min=1e-8)
+    (R:torch_xdna/conv.py:45) does; the other images' scales and codes stay bit-exact. The codes of the NaN
+    image are outside the parity claim (the reference's int8 cast of NaN is platform-defined)."""
+    from torch_xdna import kernels
+
+    n, c, h, w = 4, 32, 9, 11
+    x, _, _ = mg.conv_inputs(71, n, c, 8, h, w)
+    x[2, 5, 3, 4] = np.nan
+    xt = t(x, cuda)
+    if layout == "channels_last":
+        xt = xt.contiguous(memory_format=torch.channels_last)
+    xp = torch.empty((n, h + 2, w + 2, 32), dtype=torch.int8, device=cuda)
+    sx = torch.empty((n,), dtype=torch.float32, device=cuda)
+    scratch = torch.empty((n,), dtype=torch.int32, device=cuda)
+    (kernels.conv_quant_channels_last if layout == "channels_last" else kernels.conv_quant)(xt, xp, sx, scratch)
+    got = sx.cpu().numpy()
+    assert np.isnan(got[2]) and not np.isnan(got[[0, 1, 3]]).any()
+    q_ref, s_ref = orc.conv_quant(x[[0, 1, 3]])
+    assert np.array_equal(got[[0, 1, 3]], s_ref)
+    inner = xp[[0, 1, 3], 1:h + 1, 1:w + 1, :c].permute(0, 3, 1, 2).cpu().numpy()
+    assert np.array_equal(inner, q_ref)
+
+
 def test_cfg3_chain_matches_reference(cuda, golden):
     """4 x (conv3x3 256->256 + fused ReLU) on 1x256x64x64; shifts and every layer's
     integers equal the reference's."""

@@ -76,6 +76,46 @@ def test_quant_rows_half_integer_boundaries(cuda, dtype):
     assert bad == 0, f"{bad} boundary values rounded differently"
 
 
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+def test_quant_rows_edge_scales(cuda, dtype):
+    """The division-free quotient against numpy's IEEE division at the scales where a reciprocal product
+    is most fragile: rows whose max is below the 1e-8 clamp (scale 1e-8 / 127, so quotients of tiny values),
+    subnormal values, values near the type's largest, and rows of one repeated value."""
+    g = mg.rng(777)
+    rows, k = 64, 512
+    x = g.standard_normal((rows, k)).astype(np.float32)
+    mag = {"float32": [1e-12, 1e-9, 3e-39, 1e-30, 1e30, 3e38], "bfloat16": [1e-12, 1e-9, 1e-30, 1e30, 3e38],
+           "float16": [1e-7, 6e-8, 1e-4, 6e4]}[dtype]
+    for i in range(rows):
+        x[i] *= np.float32(mag[i % len(mag)])
+    x[-1] = np.float32(mag[0])          # every value equal: each quotient is exactly 127
+    xv = orc.cast(x, dtype)
+    xq, sx = quant_gpu(t(xv, cuda, TORCH_DT[dtype]))
+    q_ref, s_ref = orc.quant_rows(xv)
+    assert np.array_equal(sx.cpu().numpy(), s_ref)
+    assert np.array_equal(xq[:, :k].cpu().numpy(), q_ref)
+
+
+def test_quant_rows_nan_scale(cuda):
+    """A NaN in a row makes that row's scale NaN, as the reference's abs().amax().clamp(min=1e-8) does
+    (R:torch_xdna/runtime.py:146); the other rows are unaffected and bit-exact. The int8 codes of a NaN row
+    are outside the parity claim (the reference's cast of NaN to int8 is platform-defined)."""
+    g = mg.rng(31)
+    x = g.standard_normal((48, 1024)).astype(np.float32)
+    nan_rows = [3, 17, 40]
+    for r in nan_rows:
+        x[r, (r * 37) % 1024] = np.nan
+    for dtype in ("float32", "bfloat16"):
+        xv = orc.cast(x, dtype)
+        xq, sx = quant_gpu(t(xv, cuda, TORCH_DT[dtype]))
+        got = sx.cpu().numpy()
+        assert np.isnan(got[nan_rows]).all()
+        keep = [r for r in range(48) if r not in nan_rows]
+        q_ref, s_ref = orc.quant_rows(xv[keep])
+        assert np.array_equal(got[keep], s_ref)
+        assert np.array_equal(xq[keep, :1024].cpu().numpy(), q_ref)
+
+
 def test_quant_rows_strided_rows(cuda):
     x = torch.randn(64, 2048, device=cuda)[:, :1000]     # ldx 2048, K 1000
     xq, sx = quant_gpu(x)

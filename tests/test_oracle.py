@@ -105,6 +105,28 @@ def test_bf16_round_half_even():
     assert r[0] == 1.0 and r[1] == 1.0 and r[2] == np.float32(1.0 + 2 ** -6) and r[3] == -2.5
 
 
+def test_oracle_nan_scale_follows_torch():
+    """Non-finite inputs: the reference's scale is torch's x.abs().amax().float().clamp(min=1e-8) / 127
+    (R:torch_xdna/runtime.py:146, R:torch_xdna/conv.py:45), which propagates NaN, and so do the oracle's
+    per-row and per-image scales (the GPU kernels are checked against them by the -m gpu NaN tests); finite
+    rows keep their scales."""
+    import torch
+
+    g = mg.rng(5)
+    x = g.standard_normal((6, 40)).astype(np.float32)
+    x[1, 7] = np.nan
+    x[4, 0] = np.inf
+    with np.errstate(invalid="ignore"):
+        _, s = orc.quant_rows(x)
+        _, si = orc.conv_quant(x.reshape(3, 2, 4, 10))
+    xt = torch.from_numpy(x)
+    want = (xt.abs().amax(dim=1).float().clamp(min=1e-8) / 127).numpy()
+    want_img = (xt.view(3, 80).abs().amax(dim=1).float().clamp(min=1e-8) / 127).numpy()
+    assert np.isnan(s[1]) and np.isinf(s[4])
+    assert np.array_equal(s, want, equal_nan=True)
+    assert np.array_equal(si, want_img, equal_nan=True)
+
+
 def test_requant_rounds_half_up_and_saturates():
     acc = np.array([[-5, -4, -3, 3, 4, 5, 10 ** 6, -10 ** 6]], np.int32)
     assert orc.requant(acc, 1, False).tolist() == [[-2, -2, -1, 2, 2, 3, 127, -128]]

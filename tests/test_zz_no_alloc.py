@@ -7,7 +7,10 @@ a fixed array inside the library instead. Its results must be exactly those of t
 point, xdna_conv_quant_nhwc; the second call in a row checks that the shared array is cleared between
 calls (it is given fewer images with smaller values than the first).
 
-This file is collected last on purpose, and runs alone in a fresh process as well as after the others.
+This file is collected last on purpose, so that a run stopping at the first failure has run every other
+test first. It passes both after the others and alone in a fresh process
+(`python -m pytest tests/test_zz_no_alloc.py -m gpu`), where its first call on the device is the one that
+looks up the array's address.
 """
 
 import ctypes

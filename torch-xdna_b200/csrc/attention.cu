@@ -488,7 +488,7 @@ int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt
   a.err = device_error_word();
   // persistent: one CTA per SM (its shared memory allows no second), each walking its share of the items
   const int grid = std::min(a.n_items, sms);
-  static bool configured[4][64] = {};
+  static std::atomic<bool> configured[4][64];  // setting the attribute twice from two threads is harmless
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
   void (*kern)(const CUtensorMap, const CUtensorMap, const AttnArgs) =
@@ -496,9 +496,9 @@ int run_attention(const __nv_bfloat16* qk, const __nv_bfloat16* vt, int64_t ldvt
       : mask_kind == MASK_PREFIX ? attention_kernel<MASK_PREFIX>
       : mask_kind == MASK_BOOL   ? attention_kernel<MASK_BOOL>
                                  : attention_kernel<MASK_NONE>;
-  if (dev < 0 || dev >= 64 || !configured[mask_kind][dev]) {
+  if (dev < 0 || dev >= 64 || !configured[mask_kind][dev].load(std::memory_order_acquire)) {
     XDNA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
-    if (dev >= 0 && dev < 64) configured[mask_kind][dev] = true;
+    if (dev >= 0 && dev < 64) configured[mask_kind][dev].store(true, std::memory_order_release);
   }
   kern<<<grid, kAttnThreads, kAttnSmem, stream>>>(tq, tv, a);
   return check_launch("attention_kernel");

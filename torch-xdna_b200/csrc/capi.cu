@@ -1,5 +1,6 @@
 // Library-wide entry points and host helpers: last error, device checks, the device error word
 // that bounded waits write, and TMA tensor-map encoding.
+#include <atomic>
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
@@ -28,28 +29,36 @@ int fail(int code, const char* fmt, ...) {
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
-int g_sm_count[kMaxDevices];    // 0 = unchecked, -1 = not an sm_100 device
-int* g_err_ptr[kMaxDevices];
+// Per device: the SM count (0 = unchecked, -1 = not an sm_100 device) and the device address of
+// g_device_error. The address is stored first and the count published after it with release order, so
+// a thread that reads a positive count (acquire) also sees the address. The cached address belongs to
+// the device's primary context: the library must not be used across a cudaDeviceReset of that device.
+std::atomic<int> g_sm_count[kMaxDevices];
+std::atomic<int*> g_err_ptr[kMaxDevices];
 }  // namespace
 
 int check_device(int* sm_count) {
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(XDNA_ERR_DEVICE, "device ordinal %d out of range", dev);
-  int sms = g_sm_count[dev];
+  int sms = g_sm_count[dev].load(std::memory_order_acquire);
   if (sms == 0) {
     std::lock_guard<std::mutex> lock(g_mutex);
-    cudaDeviceProp prop;
-    XDNA_CUDA(cudaGetDeviceProperties(&prop, dev));
-    if (prop.major != 10) {
-      g_sm_count[dev] = -1;
-      return fail(XDNA_ERR_DEVICE, "device %d (%s) is sm_%d%d; these kernels need sm_100a (B200)", dev, prop.name,
-                  prop.major, prop.minor);
+    sms = g_sm_count[dev].load(std::memory_order_relaxed);  // another thread may have finished meanwhile
+    if (sms == 0) {
+      cudaDeviceProp prop;
+      XDNA_CUDA(cudaGetDeviceProperties(&prop, dev));
+      if (prop.major != 10) {
+        g_sm_count[dev].store(-1, std::memory_order_release);
+        return fail(XDNA_ERR_DEVICE, "device %d (%s) is sm_%d%d; these kernels need sm_100a (B200)", dev, prop.name,
+                    prop.major, prop.minor);
+      }
+      void* p = nullptr;
+      XDNA_CUDA(cudaGetSymbolAddress(&p, g_device_error));
+      g_err_ptr[dev].store(static_cast<int*>(p), std::memory_order_relaxed);
+      sms = prop.multiProcessorCount;
+      g_sm_count[dev].store(sms, std::memory_order_release);
     }
-    void* p = nullptr;
-    XDNA_CUDA(cudaGetSymbolAddress(&p, g_device_error));
-    g_err_ptr[dev] = static_cast<int*>(p);
-    g_sm_count[dev] = sms = prop.multiProcessorCount;
   }
   if (sms < 0) return fail(XDNA_ERR_DEVICE, "device %d is not an sm_100 GPU", dev);
   if (sm_count) *sm_count = sms;
@@ -59,7 +68,8 @@ int check_device(int* sm_count) {
 int* device_error_word() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  return g_err_ptr[dev];
+  if (g_sm_count[dev].load(std::memory_order_acquire) <= 0) return nullptr;
+  return g_err_ptr[dev].load(std::memory_order_relaxed);
 }
 
 int check_launch(const char* what) {

@@ -9,11 +9,17 @@
 //
 // The per-value division needs no divide instruction: with r = RN(1/scale), y = RN(x * r) is within
 // an ulp of x / scale, and one FMA correction step, q = RN(y + r * RN(x - y * scale)), is the
-// correctly rounded quotient fl(x / scale) (Markstein's theorem; where the residual underflows,
-// |x / scale| is far below 0.5 and both round to 0). The construction was checked against IEEE
-// division on the final int8, exhaustively for every bf16 and every f16 (x, amax) pair with
-// |x| <= amax and on 8.8e8 random f32 pairs: no difference.
+// correctly rounded quotient fl(x / scale). This is the correction theorem of P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1),
+// 1990 (Theorem 1: if y is within an ulp of a/b and r = RN(1/b), then RN(y + r * (a - b y)) = RN(a/b),
+// the residual a - b y being exact in one FMA), as restated for FMA hardware by M. Cornea, J. Harrison
+// and P. T. P. Tang, "Scientific Computing on Itanium-based Systems", Intel Press, 2002, ch. 8. Where the
+// residual underflows, |x / scale| is far below 0.5 and both round to 0. The construction was checked
+// against IEEE division on the final int8, exhaustively for every bf16 and every f16 (x, amax) pair with
+// |x| <= amax and on 8.8e8 random f32 pairs: no difference; tests/test_linear_gpu.py compares it with
+// numpy's IEEE division at edge scales (amax below the 1e-8 clamp, subnormal and huge values).
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "host_util.h"
@@ -138,12 +144,20 @@ __device__ __forceinline__ int8_t quant1(float v, float s, float r) {
   return static_cast<int8_t>(quant_byte(v, s, r) & 0xFFu);
 }
 
-__device__ __forceinline__ float scale_from_amax(float amax) { return __fdiv_rn(fmaxf(amax, 1e-8f), 127.f); }
+// max(amax, 1e-8) / 127 as torch's clamp(min=1e-8) then / 127: a NaN amax stays NaN.
+__device__ __forceinline__ float scale_from_amax(float amax) {
+  return __fdiv_rn(amax < 1e-8f ? 1e-8f : amax, 127.f);
+}
+
+// The max of two absolute values (non-negative floats or NaN) by their bit patterns: non-negative floats
+// order like their bits and every NaN pattern with the sign cleared sorts above +inf, so a NaN anywhere
+// makes the max NaN, as torch's amax does (fmaxf would drop it).
+__device__ __forceinline__ float amax_max(float a, float b) {
+  return __uint_as_float(max(__float_as_uint(a), __float_as_uint(b)));
+}
 
 __device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
 }
 
 
@@ -155,7 +169,7 @@ __device__ __forceinline__ void quant_row_share(const uint4 (&buf)[NV], int64_t 
   constexpr int V = Vec16<T>::N;
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) amax = fmaxf(amax, amax16<T>(buf[i]));
+  for (int i = 0; i < NV; ++i) amax = amax_max(amax, amax16<T>(buf[i]));
   amax = warp_max(amax);
   const float s = scale_from_amax(amax);
   const float r = __frcp_rn(s);
@@ -211,10 +225,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x
       const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + c));
       const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-      for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(to_f32(e[j])));
+      for (int j = 0; j < V; ++j) amax = amax_max(amax, fabsf(to_f32(e[j])));
     }
   } else {
-    for (int64_t c = lane; c < cols; c += 32) amax = fmaxf(amax, fabsf(to_f32(xr[c])));
+    for (int64_t c = lane; c < cols; c += 32) amax = amax_max(amax, fabsf(to_f32(xr[c])));
   }
   amax = warp_max(amax);
   const float s = scale_from_amax(amax);
@@ -283,7 +297,7 @@ __global__ void __launch_bounds__(256) image_amax_kernel(const T* __restrict__ x
   float m = 0.f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < per_image; i += stride)
-    m = fmaxf(m, fabsf(to_f32(xi[i])));
+    m = amax_max(m, fabsf(to_f32(xi[i])));
   m = warp_max(m);
   __shared__ float red[8];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
@@ -773,27 +787,32 @@ constexpr int64_t kStaticScratchImages = 4096;  // 16 KB per device
 static __device__ __align__(256) uint32_t g_conv_amax_scratch[kStaticScratchImages];
 
 constexpr int kMaxStaticDevices = 64;
-static uint32_t* g_conv_amax_scratch_ptr[kMaxStaticDevices];  // its device address, per device
+// its device address, per device (published with release order once looked up)
+static std::atomic<uint32_t*> g_conv_amax_scratch_ptr[kMaxStaticDevices];
 static std::mutex g_conv_amax_scratch_mutex;
 
 // The device address of g_conv_amax_scratch on the current device. In host code the array's name is
 // only a host-side stand-in, never a device address, so it is looked up once per device (with that
-// device current) and cached.
+// device current) and cached. The cached address belongs to the device's primary context: the library
+// must not be used across a cudaDeviceReset of that device.
 static int conv_amax_scratch(uint32_t** out) {
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxStaticDevices) return fail(XDNA_ERR_DEVICE, "device ordinal %d out of range", dev);
-  if (g_conv_amax_scratch_ptr[dev] == nullptr) {
+  uint32_t* ptr = g_conv_amax_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
     std::lock_guard<std::mutex> lock(g_conv_amax_scratch_mutex);
-    if (g_conv_amax_scratch_ptr[dev] == nullptr) {
+    ptr = g_conv_amax_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (ptr == nullptr) {
       void* p = nullptr;
       const cudaError_t e = cudaGetSymbolAddress(&p, g_conv_amax_scratch);
       if (e != cudaSuccess)
         return fail(XDNA_ERR_CUDA, "conv_quant_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-      g_conv_amax_scratch_ptr[dev] = static_cast<uint32_t*>(p);
+      ptr = static_cast<uint32_t*>(p);
+      g_conv_amax_scratch_ptr[dev].store(ptr, std::memory_order_release);
     }
   }
-  *out = g_conv_amax_scratch_ptr[dev];
+  *out = ptr;
   return XDNA_OK;
 }
 

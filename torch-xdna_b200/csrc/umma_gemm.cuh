@@ -1190,13 +1190,14 @@ static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, cons
   constexpr bool RB = LOAD == LOAD_CONV_RB;
   constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB, stage_out_bytes<PAIR ? BN / 2 : BN, KB, EPI, PAIR, RB>(), RB>();
   auto kern = umma_gemm_kernel<BN, LOAD, EPI, BF16, TSTORE, ODT, KB, PAIR>;
-  static bool configured[64] = {};  // per instantiation and device
-  static int max_pairs[64] = {};
+  // per instantiation and device: resident pairs once the kernel is configured (0 = not yet). Two threads
+  // configuring at once both set the same attribute and store the same count.
+  static std::atomic<int> max_pairs[64];
   int dev = 0;
   XDNA_CUDA(cudaGetDevice(&dev));
-  const bool cached = dev >= 0 && dev < 64 && configured[dev];
+  const int cached_pairs = dev >= 0 && dev < 64 ? max_pairs[dev].load(std::memory_order_acquire) : 0;
   int pairs_resident = sms / 2;
-  if (!cached) {
+  if (cached_pairs == 0) {
     XDNA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     if constexpr (PAIR) {
       cudaLaunchConfig_t cfg{};
@@ -1214,12 +1215,9 @@ static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, cons
       XDNA_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
       pairs_resident = n > 0 ? n : 1;
     }
-    if (dev >= 0 && dev < 64) {
-      max_pairs[dev] = pairs_resident;
-      configured[dev] = true;
-    }
+    if (dev >= 0 && dev < 64) max_pairs[dev].store(pairs_resident, std::memory_order_release);
   } else {
-    pairs_resident = max_pairs[dev];
+    pairs_resident = cached_pairs;
   }
   const int tiles = args.m_tiles * args.n_tiles;
   if constexpr (PAIR) {

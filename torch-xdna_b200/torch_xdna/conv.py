@@ -7,7 +7,7 @@ The math is the reference's (R:torch_xdna/conv.py:1-19):
   sums        int32 on the int8 tensor cores (implicit GEMM: K = 9 taps x input channels),
               requantised in the epilogue by one shift: round half up, saturate to int8, or to
               [0, 255] with a fused ReLU. The shift is fixed on the layer's first call from the
-              first image's sums with 25% headroom (R:torch_xdna/conv.py:327-332).
+              first image's sums with 25% headroom (R:torch_xdna/conv.py:71-76).
   output      q * sw[co] * 2^shift * sx (+ bias)
 
 Data layout on the device: activations are quantised straight into a zero-bordered NHWC int8
@@ -71,7 +71,7 @@ class ConvLayer:
         rows = wf.reshape(co, ci * 9).contiguous()
         self.wq = torch.empty((co, kernels.round_up(ci * 9, 16)), dtype=torch.int8, device=weight.device)
         self.sw = torch.empty((co,), dtype=torch.float32, device=weight.device)
-        kernels.quant_rows(rows, self.wq, self.sw)           # R:torch_xdna/conv.py:315-316
+        kernels.quant_rows(rows, self.wq, self.sw)           # R:torch_xdna/conv.py:58-60
         self.ci, self.co, self.cp = ci, co, channels_padded(ci)
         wq4 = self.wq[:, :ci * 9].contiguous().view(co, ci, 3, 3)
         self.wq4 = wq4
@@ -92,7 +92,7 @@ class ConvLayer:
         self.name = f"conv3x3 {ci}->{co} {h}x{w}" + (" relu" if relu else "")
 
     def calibrate(self, xp):
-        """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:327-332)."""
+        """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:71-76)."""
         acc_max = torch.empty((1,), dtype=torch.int32, device=xp.device)
         kernels.conv3x3(xp, self.wp, 1, self.ci_k, self.co, self.h, self.w, kernels.CONV_CALIBRATE | self.mode_flag,
                         relu=self.relu, acc_max=acc_max)
@@ -124,7 +124,7 @@ class ConvLayer:
 
     def cpu_integers(self, xq_nchw_cpu):
         """The reference's CPU integers for the same layer and shift (ConvLayer.cpu,
-        R:torch_xdna/conv.py:342-348), used only to verify launches."""
+        R:torch_xdna/conv.py:86-92), used only to verify launches."""
         dt = torch.float32 if 127 * float(self.wq4.abs().sum(dim=(1, 2, 3)).max()) < 2 ** 24 else torch.float64
         acc = torch.nn.functional.conv2d(xq_nchw_cpu.to(dt), self.wq4.cpu().to(dt), padding=1)
         q = (acc.to(torch.int32) + (1 << (self.shift - 1))) >> self.shift
