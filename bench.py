@@ -1,26 +1,32 @@
-"""Benchmark: int8 TOPS of the W8A8 linear path on B200.
+"""Benchmark of the three offloaded ops on B200: W8A8 linear, int8 conv3x3 and the Qwen3 stack.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl xdna|reference] [--workload cfg2|square]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl xdna|reference] [--workload all|cfg2|...]
 
-One step = one pass of the hot path over one batch: BASELINE config 2's Qwen3-0.6B projection set at
-M = 8192 rows, bf16 activations, W8A8 -- xdna::linear_cat q/k/v (N = 2048+1024+1024, K = 1024),
-xdna::linear_cat gate/up (N = 2x3072, K = 1024) and xdna::linear down (N = 1024, K = 3072). Each op is
-our quantise kernel followed by our tcgen05 int8 GEMM with the dequantising epilogue. Metric: int8
-TOPS = 2*M*sum(N*K) per step / step time, whole job (all ranks).
+The default run (--workload all) prints ONE JSON line whose top level is BASELINE config 2 and whose
+sub-records carry the other headline metrics, so that every driver run measures all of them:
 
-  value      device time of the K steps (CUDA events on the launching stream), inputs resident in HBM,
-             L2 flushed (a 256 MiB write) between steps, outside the events;
-  e2e        the same steps through the public API (torch.compile(backend="xdna")) with the inputs
-             copied from pinned host memory and every output copied back, inside the timed region;
-  roofline   the GEMM kernel alone: its algorithmic int8 ops per launch / its event-timed duration,
-             against the int8 peak (2x the measured dense bf16 cuBLAS rate in MEASURED_PEAKS.json --
-             B200's dense int8 rate is twice its bf16 rate);
-  cpu_baseline  the reference's CPU route (torch._int_mm + its eager quantise / dequantise ops),
-             restated in oracle/reference_cpu.py, on a bounded row sample, all host threads.
+  top level  config 2: the Qwen3-0.6B projection set at M = 8192 bf16 rows, W8A8 -- xdna::linear_cat
+             q/k/v (N = 2048+1024+1024, K = 1024), xdna::linear_cat gate/up (N = 2x3072, K = 1024),
+             xdna::linear down (N = 1024, K = 3072), each our quantise kernel + tcgen05 int8 GEMM with the
+             dequantising epilogue. Metric int8 TOPS = 2*M*sum(N*K) per step / step time, whole job;
+  m_sweep    config 2 at M = 1, 128, 512, 2048 (N = 1 only): TOPS and, for M <= 128, where streaming the
+             weights from HBM bounds the step, an HBM roofline;
+  conv       config 4: the 13 VGG16 conv3x3 layers (bias + ReLU, 2x2 max-pools, int8 chained) on a batch of
+             32 images 3x224x224, batch sharded over ranks; the single Ci = Co = 256 conv on a 1536x64 image;
+             config 3: four 256-channel convs + ReLU on 1x256x64x64, in ms (device and end to end);
+  stack      config 5: 28 layers + final norm + head 151936 on 16 x 1024 token ids under a causal mask;
+             sequences sharded over ranks, the head column-parallel on N > 1 GPUs (every rank's hidden
+             states exchanged over NVLink inside the head GEMM's pipeline), with a per-N breakdown.
 
---impl reference times only that CPU route, on rank 0, and prints its own line.
-Multi-GPU (torchrun): the linear does not shard (replicas only): every rank runs the whole workload,
-value = ranks x units / max-over-ranks time.
+Every record: value (device time, CUDA events on the launching stream, max over ranks), roofline of its
+dominant kernel against MEASURED_PEAKS.json, clocks sampled during its timed region, and (rank 0, N = 1)
+cpu_baseline = the reference's CPU route (oracle/reference_cpu.py, the same torch CPU calls the reference
+makes with policy="cpu") on the host cores. e2e: the same work through the public API with host buffers.
+
+--impl reference times the reference's CPU route for the same records on rank 0 (other ranks exit) and
+prints one line with "impl": "reference".
+Other workloads print their own line: cfg2, square (4096^3), msweep, conv, cfg3, stack.
+--kernel NAME --shape a,b,c times one kernel (the commands the ncu summaries are captured with).
 """
 
 import argparse
@@ -40,20 +46,23 @@ sys.path.insert(0, str(ROOT))
 import torch  # noqa: E402
 
 D, NQ, NKV, INTER = 1024, 2048, 1024, 3072
+V_HEAD = 151936
 L2_FLUSH_BYTES = 256 << 20
+M_SWEEP = (1, 128, 512, 2048)
+CFG2_METRIC = "int8 TOPS/GPU, W8A8 linear (BASELINE config 2 Qwen3-0.6B projection set)"
+CONV_METRIC = "int8 TOPS/GPU, conv3x3 (BASELINE config 4: VGG16 int8, batch 32)"
+STACK_METRIC = "Qwen3-0.6B stack tokens/s (BASELINE config 5)"
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="xdna", choices=["xdna", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "square", "stack", "conv"],
-                    help="cfg2: W8A8 projection set (default); square: 4096^3 int8 GEMM; stack: BASELINE config 5; "
-                         "conv: BASELINE config 4")
+    ap.add_argument("--workload", default="all", choices=["all", "cfg2", "square", "msweep", "conv", "cfg3", "stack"],
+                    help="all: config 2 with the m_sweep, conv and stack records (default)")
     ap.add_argument("--rows", type=int, default=8192)
-    ap.add_argument("--cpu-rows", type=int, default=1024, help="row sample of the CPU baseline")
     ap.add_argument("--seqs", type=int, default=16, help="stack: sequences in the global batch")
     ap.add_argument("--seq-len", type=int, default=1024, help="stack: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="stack: decoder layers")
@@ -68,10 +77,7 @@ def parse():
                     choices=["gemm_i8", "quant_rows", "conv3x3", "attention", "gemm_bf16", "gemm_bf16_qkv"],
                     help="time one kernel on --shape instead of a workload (profiling)")
     ap.add_argument("--shape", default="8192,6144,1024", help="--kernel shape, comma-separated")
-    args = ap.parse_args()
-    if args.workload in ("stack", "conv") and args.steps == 2000:
-        args.steps = 10          # a step of these workloads is milliseconds, not microseconds
-    return args
+    return ap.parse_args()
 
 
 # ---------------------------------------------------------------- distributed plumbing
@@ -107,41 +113,29 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-# ---------------------------------------------------------------- workload
-class ProjectionSet(torch.nn.Module):
-    """The projections of one Qwen3-0.6B layer: q/k/v and gate/up share an input, down reads the MLP act."""
-
-    def __init__(self):
-        super().__init__()
-        self.q = torch.nn.Linear(D, NQ, bias=False)
-        self.k = torch.nn.Linear(D, NKV, bias=False)
-        self.v = torch.nn.Linear(D, NKV, bias=False)
-        self.gate = torch.nn.Linear(D, INTER, bias=False)
-        self.up = torch.nn.Linear(D, INTER, bias=False)
-        self.down = torch.nn.Linear(INTER, D, bias=False)
-
-    def forward(self, x_attn, x_mlp, act):
-        return (self.q(x_attn), self.k(x_attn), self.v(x_attn), self.gate(x_mlp), self.up(x_mlp),
-                self.down(act))
+def peaks():
+    """(int8 TOPS, HBM GB/s, bf16 burst TFLOP/s, bf16 sustained TFLOP/s, source)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return (2 * float(d["bf16_tflops"]), float(d["hbm_gbs"]), float(d["bf16_tflops"]),
+                float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured (MEASURED_PEAKS.json)")
+    return 2 * 1590.0, 6650.0, 1590.0, 1400.0, "fallback (6.65 TB/s, 1.59 PFLOP/s burst, 1.4 sustained)"
 
 
-def gemm_shapes(workload, rows):
-    if workload == "square":
-        return [(4096, 4096, 4096)]
-    return [(rows, NQ + 2 * NKV, D), (rows, 2 * INTER, D), (rows, D, INTER)]
+INT8_PEAK_NOTE = "int8 peak = 2 x the measured dense bf16 cuBLAS burst (B200's dense int8 rate is twice its bf16 rate)"
 
 
-def make_model(dev):
-    g = torch.Generator().manual_seed(0)
-    m = ProjectionSet()
-    for p in m.parameters():
-        p.data = (torch.randn(p.shape, generator=g) * 0.02)
-    return m.to(dev, torch.bfloat16).eval()
+def roof(bound, kernel, achieved, peak, unit, per_launch_ms, **extra):
+    r = {"bound": bound, "kernel": kernel, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": unit,
+         "frac": round(achieved / peak, 4), "per_launch_ms": round(per_launch_ms, 4)}
+    r.update(extra)
+    return r
 
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) of this GPU's clocks and throttle reasons while running."""
+    """nvidia-smi samples (every 20 ms) of this GPU's clocks and throttle reasons while running."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -191,210 +185,167 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-# ---------------------------------------------------------------- the CPU baseline (reference route)
-def cpu_baseline(workload, rows_sample, budget_s=12.0):
-    """The reference's CPU route on a bounded row sample (oracle/reference_cpu.py), all host threads."""
-    from oracle import reference_cpu as rc
+def time_graph(step, steps, world, dev, flush=None):
+    """Capture one call of step() in a CUDA graph, replay it `steps` times between CUDA events on the current
+    stream (a write of `flush` outside the events before each replay when given), with clocks sampled
+    meanwhile. Returns (total seconds, max over ranks; per-step ms list; clocks summary)."""
+    stream = torch.cuda.current_stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    barrier(world)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    with ClockSampler(dev.index) as clocks:
+        barrier(world)
+        for i in range(steps):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            graph.replay()
+            ends[i].record(stream)
+        barrier(world)
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    del graph
+    return max_over_ranks(sum(ms) / 1e3, world), ms, clocks.summary()
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(1)
-    shapes = gemm_shapes(workload, rows_sample)
-    ops = []
+
+def event_ms(fn, reps, flush=None, warm=2):
+    """Median CUDA-event duration of fn() on the current stream (L2 flushed before each call when given)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warm):
+        fn()
+    ms = []
+    for _ in range(reps):
+        if flush is not None:
+            flush.fill_(1)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        e.synchronize()
+        ms.append(s.elapsed_time(e))
+    return statistics.median(ms)
+
+
+# ================================================================ BASELINE config 2: the W8A8 projection set
+class ProjectionSet(torch.nn.Module):
+    """The projections of one Qwen3-0.6B layer: q/k/v and gate/up share an input, down reads the MLP act."""
+
+    def __init__(self):
+        super().__init__()
+        self.q = torch.nn.Linear(D, NQ, bias=False)
+        self.k = torch.nn.Linear(D, NKV, bias=False)
+        self.v = torch.nn.Linear(D, NKV, bias=False)
+        self.gate = torch.nn.Linear(D, INTER, bias=False)
+        self.up = torch.nn.Linear(D, INTER, bias=False)
+        self.down = torch.nn.Linear(INTER, D, bias=False)
+
+    def forward(self, x_attn, x_mlp, act):
+        return (self.q(x_attn), self.k(x_attn), self.v(x_attn), self.gate(x_mlp), self.up(x_mlp),
+                self.down(act))
+
+
+def gemm_shapes(workload, rows):
+    if workload == "square":
+        return [(4096, 4096, 4096)]
+    return [(rows, NQ + 2 * NKV, D), (rows, 2 * INTER, D), (rows, D, INTER)]
+
+
+def make_model(dev):
+    g = torch.Generator().manual_seed(0)
+    m = ProjectionSet()
+    for p in m.parameters():
+        p.data = (torch.randn(p.shape, generator=g) * 0.02)
+    return m.to(dev, torch.bfloat16).eval()
+
+
+def cfg2_config(rows):
+    return {"workload": f"cfg2 Qwen3-0.6B projection set, W8A8, M={rows} rows bf16: linear_cat qkv (N=4096,K=1024) "
+                        f"+ linear_cat gate/up (N=6144,K=1024) + linear down (N=1024,K=3072)",
+            "global_batch": rows, "parallelism": "replicas", "l2": "flushed between steps (256 MiB write)"}
+
+
+# The DRAM and L2 -> SM bytes of one gemm_i8 launch per shape (bf16 out), from an earlier ncu capture of
+# `bench.py --kernel gemm_i8 --shape M,N,K` (dram__bytes_read.sum + dram__bytes_write.sum;
+# lts__t_sectors_srcunit_tex_op_read.sum x 32). Not measured by this run: DRAM writes still in L2 when the
+# kernel ends are not counted in its DRAM bytes, so the L2 -> SM bytes show the on-chip re-reads instead.
+PAST_CAPTURE = {(8192, 4096, 1024): (26222336, None), (8192, 6144, 1024): (61992960, 407.6e6),
+                (8192, 1024, 3072): (28405248, None), (4096, 4096, 4096): (36336640, None)}
+
+
+def gemm_roofline(shapes, dev, reps, flush):
+    """The GEMM kernel alone: algorithmic int8 ops per launch / its CUDA-event duration, summed over the
+    shapes (inputs pre-quantised, L2 flushed before every launch)."""
+    from torch_xdna import kernels
+
+    total_ms, total_ops = 0.0, 0
     for (m, n, k) in shapes:
-        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
-        w_kn, sw = rc.quant_weight(w)
-        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
-        ops.append((x, w_kn, sw))
-    with torch.no_grad():
-        for x, w_kn, sw in ops:           # warm-up
-            rc.linear_int8(x, w_kn, sw)
-        times = []
-        t_end = time.perf_counter() + budget_s
-        while time.perf_counter() < t_end or len(times) < 3:
-            t0 = time.perf_counter()
-            for x, w_kn, sw in ops:
-                rc.linear_int8(x, w_kn, sw)
-            times.append(time.perf_counter() - t0)
-    step = statistics.median(times)
-    work = sum(2 * m * n * k for m, n, k in shapes)
-    return {"value": round(work / step / 1e12, 4), "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"{workload} projection set at {rows_sample} rows (of the workload's rows), "
-                      f"median of {len(times)} passes; torch._int_mm + eager quantise/dequantise (reference route)"}
+        xq = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev)
+        wq = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev)
+        sx, sw = torch.rand(m, device=dev) * 0.01, torch.rand(n, device=dev) * 0.01
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        total_ms += event_ms(lambda: kernels.gemm_i8(xq, wq, k, y, sx, sw), max(5, reps), flush, warm=3)
+        total_ops += 2 * m * n * k
+    peak = peaks()[0]
+    caps = [PAST_CAPTURE.get(tuple(s)) for s in shapes]
+    traffic = round(sum(c[0] for c in caps) / len(caps)) if all(caps) else None
+    return roof("tensor", "umma_gemm_kernel (gemm_i8, dequantising epilogue, bf16 out)",
+                total_ops / (total_ms / 1e3) / 1e12, peak, "TOPS", total_ms / len(shapes),
+                peak_source=INT8_PEAK_NOTE, traffic=traffic,
+                traffic_source="earlier ncu capture of the same shapes (dram__bytes_read.sum + dram__bytes_write."
+                               "sum per launch, averaged over the shapes), not measured by this run",
+                l2_to_sm_bytes={f"{m}x{n}x{k}": c[1] for (m, n, k), c in zip(shapes, caps) if c and c[1]} or None)
 
 
-def run_reference(args, rank, world):
-    if rank != 0:
-        return
-    rows = args.cpu_rows if args.workload == "cfg2" else 4096
-    cb = cpu_baseline(args.workload, rows, budget_s=12.0)   # a bounded sample: ~12 s of CPU work
-    line = {"impl": "reference", "metric": metric_name(args.workload), "value": cb["value"], "unit": "TOPS",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": config_of(args), "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
-
-
-def metric_name(workload):
-    return "int8 TOPS/GPU, W8A8 linear (BASELINE config 2" + (" square 4096^3)" if workload == "square" else
-                                                               " Qwen3-0.6B projection set)")
-
-
-def config_of(args):
-    if args.workload == "square":
-        return {"workload": "cfg2 square int8 GEMM M=N=K=4096 (quantise + GEMM + dequantise to bf16)",
-                "l2": "flushed between steps"}
-    return {"workload": f"cfg2 Qwen3-0.6B projection set, W8A8, M={args.rows} rows bf16: linear_cat qkv "
-                        f"(N=4096,K=1024) + linear_cat gate/up (N=6144,K=1024) + linear down (N=1024,K=3072)",
-            "global_batch": args.rows, "parallelism": "replicas", "l2": "flushed between steps (256 MiB write)"}
-
-
-# ---------------------------------------------------------------- the B200 arm
-def run_xdna(args, rank, world):
+def cfg2_records(args, rank, world, dev, flush):
+    """Config 2 at args.rows (the top level) and its square 4096^3 case."""
     import torch_xdna
     from torch_xdna import kernels
 
-    dev = torch.device("cuda", torch.cuda.current_device())
-    if not torch_xdna.gpu_available():
-        raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
-    torch.manual_seed(0)
-    cfg = torch_xdna.Config(verify="first", fallback="eager")
-    cid = torch_xdna.ops.config_id(cfg)
+    cid = torch_xdna.ops.config_id(torch_xdna.Config(verify="first", fallback="eager"))
     model = make_model(dev)
     R = args.rows
-    x = torch.randn(R, D, device=dev).to(torch.bfloat16)          # attention-norm output
-    x2 = torch.randn(R, D, device=dev).to(torch.bfloat16)         # MLP-norm output
-    act = torch.randn(R, INTER, device=dev).to(torch.bfloat16)    # silu(gate) * up
-    if args.workload == "square":
-        w_sq = (torch.randn(4096, 4096, device=dev) * 0.02).to(torch.bfloat16)
-        x = torch.randn(4096, 4096, device=dev).to(torch.bfloat16)
+    square = args.workload == "square"
+    g = torch.Generator(device=dev).manual_seed(0)
+    if square:
+        x = torch.randn(4096, 4096, device=dev, generator=g).to(torch.bfloat16)
+        w_sq = (torch.randn(4096, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    else:
+        x = torch.randn(R, D, device=dev, generator=g).to(torch.bfloat16)        # attention-norm output
+    x2 = torch.randn(R, D, device=dev, generator=g).to(torch.bfloat16)           # MLP-norm output
+    act = torch.randn(R, INTER, device=dev, generator=g).to(torch.bfloat16)      # silu(gate) * up
     shapes = gemm_shapes(args.workload, R)
     work = sum(2 * m * n * k for m, n, k in shapes)
-
     qkv = [model.q.weight, model.k.weight, model.v.weight]
     gu = [model.gate.weight, model.up.weight]
 
     def step():
-        if args.workload == "square":
+        if square:
             return [torch.ops.xdna.linear(x, w_sq, None, False, cid)]
         return [torch.ops.xdna.linear_cat(x, qkv, [None] * 3, cid), torch.ops.xdna.linear_cat(x2, gu, [None] * 2, cid),
                 torch.ops.xdna.linear(act, model.down.weight, None, False, cid)]
 
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream()
     with torch.no_grad():
         for _ in range(max(args.warmup, 3)):   # includes each kernel configuration's first-call verify
             step()
         torch.cuda.synchronize()
-        # One step captured as a CUDA graph (the same kernels, launched without Python in between):
-        # the timed region measures device work, not host launch overhead.
         torch_xdna.stats.reset()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
+        total_s, _, clocks = time_graph(step, args.steps, world, dev, flush)
         per_step = torch_xdna.stats.launches
-        graph.replay()
-        barrier(world)
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        with ClockSampler(dev.index) as clocks:
-            barrier(world)
-            for i in range(args.steps):
-                flush.fill_(i & 0xFF)
-                starts[i].record(stream)
-                graph.replay()
-                ends[i].record(stream)
-            barrier(world)
-        launches = per_step * args.steps
-        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-        del graph
-    total_s = max_over_ranks(sum(step_ms) / 1e3, world)
-    value = world * work * args.steps / total_s / 1e12
-
-    # ---- roofline: the GEMM kernel alone (same shapes, same stream), event-timed per launch
-    roof = gemm_roofline(shapes, dev, args.steps, flush)
-    # config 2's square M = N = K = 4096 GEMM, the case the >= 70 %-of-peak target is stated on
-    roof_sq = gemm_roofline([(4096, 4096, 4096)], dev, args.steps, flush) if args.workload == "cfg2" else None
-    # ---- e2e through torch.compile(backend="xdna") with host buffers
-    e2e = e2e_measure(args, model, dev, world, work)
-    # ---- CPU baseline (rank 0, one GPU only)
-    cb = cpu_baseline(args.workload, args.cpu_rows if args.workload == "cfg2" else 1024) \
-        if (rank == 0 and world == 1) else None
+    rec = {"value": round(world * work * args.steps / total_s / 1e12, 2), "unit": "TOPS",
+           "ms_per_step": round(total_s * 1e3 / args.steps, 4), "gpu_launches": per_step * args.steps,
+           "roofline": gemm_roofline(shapes, dev, args.steps, flush), "clocks": clocks}
+    if not square:
+        rec["roofline_square_4096"] = gemm_roofline([(4096, 4096, 4096)], dev, args.steps, flush)
+        rec["e2e"] = cfg2_e2e(args, model, dev, world, work)
     if kernels.take_device_error() != (0, 0):
         raise SystemExit("a kernel recorded a device-side timeout")
-    if rank == 0:
-        line = {"metric": metric_name(args.workload), "value": round(value, 2), "unit": "TOPS", "n_gpus": world,
-                "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(total_s * 1e3 / args.steps, 4),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-                "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)", "config": config_of(args),
-                "gpu_launches": launches, "roofline": roof, "e2e": e2e, "clocks": clocks.summary()}
-        if roof_sq is not None:
-            line["roofline_square_4096"] = roof_sq
-        if cb is not None:
-            line["cpu_baseline"] = cb
-        print(json.dumps(line), flush=True)
+    return rec
 
 
-def int8_peak():
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        d = json.loads(p.read_text())
-        return 2 * float(d["bf16_tflops"]), "2x measured dense bf16 cuBLAS burst (MEASURED_PEAKS.json)"
-    return 2 * 1590.0, "2x fallback dense bf16 1.59 PFLOP/s"
-
-
-# DRAM bytes (read + write) of one gemm_i8 launch per shape, from one ncu capture each
-# (profiles/gemm_i8_dram_traffic.md has the command).
-PROFILED_DRAM_BYTES = {(8192, 4096, 1024): 26222336, (8192, 6144, 1024): 61992960, (8192, 1024, 3072): 28405248,
-                       (4096, 4096, 4096): 36336640}
-
-
-def gemm_roofline(shapes, dev, steps, flush):
-    """Algorithmic int8 ops per launch of the GEMM kernel / its CUDA-event duration, summed over the
-    workload's GEMMs; inputs pre-quantised, L2 flushed before every launch."""
-    from torch_xdna import kernels
-
-    cases = []
-    for (m, n, k) in shapes:
-        xq = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev)
-        wq = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev)
-        sx = torch.rand(m, device=dev) * 0.01
-        sw = torch.rand(n, device=dev) * 0.01
-        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-        cases.append((xq, wq, k, y, sx, sw))
-    stream = torch.cuda.current_stream()
-    for c in cases:
-        for _ in range(3):
-            kernels.gemm_i8(c[0], c[1], c[2], c[3], c[4], c[5])
-    total_ms, total_ops = 0.0, 0
-    reps = max(5, steps)
-    for (m, n, k), c in zip(shapes, cases):
-        ms = []
-        for _ in range(reps):
-            flush.fill_(1)
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            kernels.gemm_i8(c[0], c[1], c[2], c[3], c[4], c[5])
-            e.record(stream)
-            e.synchronize()
-            ms.append(s.elapsed_time(e))
-        total_ms += statistics.median(ms)
-        total_ops += 2 * m * n * k
-    torch.cuda.synchronize()
-    peak, src = int8_peak()
-    achieved = total_ops / (total_ms / 1e3) / 1e12
-    traffic = None
-    if all(tuple(sh) in PROFILED_DRAM_BYTES for sh in shapes):
-        traffic = round(sum(PROFILED_DRAM_BYTES[tuple(sh)] for sh in shapes) / len(shapes))
-    return {"bound": "tensor", "kernel": "umma_gemm_kernel (gemm_i8, dequantising epilogue, bf16 out)",
-            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
-            "frac": round(achieved / peak, 4), "peak_source": src, "traffic": traffic,
-            "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
-            "per_launch_ms": round(total_ms / len(shapes), 4)}
-
-
-def e2e_measure(args, model, dev, world, work):
+def cfg2_e2e(args, model, dev, world, work):
     """The step through torch.compile(backend="xdna"), fed from and drained to pinned host memory as a
     serving loop would: every step copies its three inputs host -> device and its six outputs device ->
     host, on their own streams (the copy engines work in both directions at once), double-buffered so
@@ -402,8 +353,6 @@ def e2e_measure(args, model, dev, world, work):
     copy-in, compute and copy-out. The timed region covers every step's copies."""
     import torch_xdna  # noqa: F401  (registers the backend)
 
-    if args.workload == "square":
-        return None
     torch._dynamo.reset()
     comp = torch.compile(model, backend="xdna", options={"fallback": "eager", "verify": "off"})
     R = args.rows
@@ -457,214 +406,79 @@ def e2e_measure(args, model, dev, world, work):
         e.synchronize()
         barrier(world)
     sec = max_over_ranks(s.elapsed_time(e) / 1e3, world)
-    h2d = sum(t.numel() for t in hin[0]) * 2
-    d2h = sum(t.numel() for t in hout[0]) * 2
-    return {"value": round(world * work * steps / sec / 1e12, 2), "unit": "TOPS", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "api": "torch.compile(backend='xdna', fallback='eager')",
+    torch._dynamo.reset()
+    return {"value": round(world * work * steps / sec / 1e12, 2), "unit": "TOPS",
+            "h2d_bytes_per_step": sum(t.numel() for t in hin[0]) * 2,
+            "d2h_bytes_per_step": sum(t.numel() for t in hout[0]) * 2,
+            "api": "torch.compile(backend='xdna', fallback='eager')",
             "pipeline": "copy-in / compute / copy-out streams, double-buffered pinned host and device buffers"}
 
 
-# ---------------------------------------------------------------- the Qwen3 stack
-V_HEAD = 151936
+def gemm_hbm_bytes(m, n, k):
+    """Algorithmic HBM bytes of one dequantising int8 GEMM launch: int8 weights and activations read once,
+    bf16 output written once, the row and column scales."""
+    return n * k + m * k + 2 * m * n + 4 * (m + n)
 
 
-def stack_flops(B, L, layers, vocab):
-    """Algorithmic FLOPs of one step: the projections and head per token, causal attention (QK^T and PV over
-    the keys each query sees)."""
-    per_token = 2 * (layers * (D * 4096 + 2048 * D + D * 6144 + INTER * D) + D * vocab)
-    attn = layers * B * 2 * 2 * 16 * 128 * (L * (L + 1) // 2)
-    return B * L * per_token + attn
-
-
-def run_stack(args, rank, world):
-    """One step = embed the token ids of this rank's sequences and run xdna_qwen3_stack (28 layers, final
-    norm, head over 151936) under a causal mask; the global batch is fixed (strong scaling). The layers
-    are data-parallel over sequences (independent: no collective). The head, on more than one GPU, is
-    column-parallel by default: an NCCL all-gather of every rank's final hidden states
-    over NVLink, then each rank computes its 151936 / N vocabulary columns for all tokens; --head dp keeps
-    it with the sequences instead."""
+def msweep_record(args, dev, flush):
+    """Config 2's row sweep: the projection set (quantise + GEMM per op, as the top level) at M = 1, 128,
+    512, 2048. M <= 128: the step streams 13.6 MB of int8 weights and little else, so its roofline is HBM
+    (algorithmic GEMM bytes / GEMM time against the measured copy bandwidth); larger M: the int8 peak."""
     import torch_xdna
-    from torch_xdna import kernels, parallel
+    from torch_xdna import kernels
 
-    if not torch_xdna.gpu_available():
-        raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
-    dev = torch.device("cuda", torch.cuda.current_device())
-    B_all, L, NL = args.seqs, args.seq_len, args.layers
-    assert B_all % world == 0, "sequences must divide over the ranks"
-    B = B_all // world
-    g = torch.Generator(device=dev).manual_seed(1234)
+    cid = torch_xdna.ops.config_id(torch_xdna.Config(verify="first", fallback="eager"))
+    model = make_model(dev)
+    qkv = [model.q.weight, model.k.weight, model.v.weight]
+    gu = [model.gate.weight, model.up.weight]
+    int8_peak, hbm, _, _, src = peaks()
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(2)
+    for M in M_SWEEP:
+        x = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+        x2 = torch.randn(M, D, device=dev, generator=g).to(torch.bfloat16)
+        act = torch.randn(M, INTER, device=dev, generator=g).to(torch.bfloat16)
 
-    def w(*shape):
-        return (torch.randn(*shape, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        def step():
+            return [torch.ops.xdna.linear_cat(x, qkv, [None] * 3, cid),
+                    torch.ops.xdna.linear_cat(x2, gu, [None] * 2, cid),
+                    torch.ops.xdna.linear(act, model.down.weight, None, False, cid)]
 
-    table = (kernels.Qwen3Layer * NL)()
-    keep = []
-    for i in range(NL):
-        qkv, o, gu, down = w(4096, D), w(D, 2048), w(2 * INTER, D), w(D, INTER)
-        norms = [torch.ones(D, device=dev), torch.ones(D, device=dev), torch.ones(128, device=dev),
-                 torch.ones(128, device=dev)]
-        keep += [qkv, o, gu, down] + norms
-        table[i] = kernels.Qwen3Layer(qkv.data_ptr(), o.data_ptr(), gu.data_ptr(), down.data_ptr(),
-                                      *[t.data_ptr() for t in norms])
-    final = torch.ones(D, device=dev)
-    head, embed = w(V_HEAD, D), w(V_HEAD, D)
-    column = world > 1 and args.head in ("column", "column-direct", "column-nccl")
-    fused = column and args.head != "column-nccl"  # the all-gather inside the head's GEMM pipeline
-    n_cols = V_HEAD // world if column else V_HEAD       # 151936 = 2^7 x 1187: divides by 2, 4 and 8
-    if column:
-        head = head[rank * n_cols:(rank + 1) * n_cols].contiguous()
-    inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device=dev) / 128))
-    f = torch.arange(L, dtype=torch.float32, device=dev)[:, None] * inv[None, :]
-    cos, sin = kernels.rope_layout(f.cos()), kernels.rope_layout(f.sin())
-    ids = torch.randint(0, V_HEAD, (B * L,), device=dev, generator=g)
-    x = torch.empty(B * L, D, device=dev)
-    out = torch.empty(B_all * L if column else B * L, n_cols, dtype=torch.bfloat16, device=dev)
-    ws = torch.empty(kernels.qwen3_stack_workspace(B, L), dtype=torch.uint8, device=dev)
-    hidden = ws[:B * L * D * 2].view(torch.bfloat16).view(B * L, D)   # the final-normed states (workspace head)
-    h_all = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev) if column and not fused else None
-    rg = parallel.RowGather(B * L, D, dev, mode="direct" if args.head == "column-direct" else "pipelined") \
-        if fused else None
-    launches_per_step = 1 + 7 * NL + 2
-
-    def step(ids_dev):
-        kernels.embed(ids_dev, embed, x)
-        if column:
-            kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
-                                None, ws)
-            if fused:
-                rg.local.copy_(hidden)
-                rg.gemm(head, out)
-            else:
-                parallel.gather_rows(hidden, h_all)
-                kernels.gemm_bf16(h_all, head, kernels.GEMM_F32ACC, out=out)
+        shapes = gemm_shapes("cfg2", M)
+        work = sum(2 * m * n * k for m, n, k in shapes)
+        with torch.no_grad():
+            for _ in range(3):
+                step()
+            torch_xdna.stats.reset()
+            total_s, _, clocks = time_graph(step, args.steps, 1, dev, flush)
+            launches = torch_xdna.stats.launches
+        # the GEMM kernels alone, L2 flushed before each (weights from HBM)
+        gem_ms, gem_bytes = 0.0, 0
+        for (m, n, k) in shapes:
+            xq = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev)
+            wq = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev)
+            sx, sw = torch.rand(m, device=dev) * 0.01, torch.rand(n, device=dev) * 0.01
+            y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            gem_ms += event_ms(lambda: kernels.gemm_i8(xq, wq, k, y, sx, sw), max(5, args.steps), flush, warm=3)
+            gem_bytes += gemm_hbm_bytes(m, n, k)
+        step_ms = total_s * 1e3 / args.steps
+        rec = {"value": round(work * args.steps / total_s / 1e12, 3), "unit": "TOPS", "ms_per_step": round(step_ms, 4),
+               "gpu_launches": launches * args.steps, "clocks": clocks}
+        if M <= 128:
+            rec["roofline"] = roof("hbm", "umma_gemm_kernel (gemm_i8, the three GEMMs of the set)",
+                                   gem_bytes / (gem_ms / 1e3) / 1e9, hbm, "GB/s", gem_ms / 3,
+                                   peak_source=src, bytes_per_step=gem_bytes,
+                                   step_gbs=round(gem_bytes / (step_ms / 1e3) / 1e9, 1))
         else:
-            kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
-                                out, ws)
-
-    stream = torch.cuda.current_stream()
-    for _ in range(max(args.warmup, 3)):
-        step(ids)
-    if column:   # once, untimed: this rank's vocabulary slice of 256 rows of every rank vs an f32 product
-        gathered = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev)
-        parallel.gather_rows(hidden, gathered)
-        for r in range(world):
-            rows = slice(r * B * L, r * B * L + 256)
-            ref = gathered[rows].float() @ head.float().t()
-            err = float((out[rows].float() - ref).abs().max() / ref.abs().max())
-            if not err < 2e-2:
-                raise SystemExit(f"rank {rank}: column-parallel head rows of rank {r} disagree with the f32 "
-                                 f"product (rel {err:.3g})")
-        del gathered
-    barrier(world)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(dev.index) as clocks:
-        barrier(world)
-        for i in range(args.steps):          # weights (1.2 GB) and activations far exceed L2
-            starts[i].record(stream)
-            step(ids)
-            ends[i].record(stream)
-        barrier(world)
-    total_s = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3, world)
-    tokens = B_all * L * args.steps
-    value = tokens / total_s
-    flops = stack_flops(B, L, NL, V_HEAD)
-
-    # roofline: the head GEMM (the largest single launch), timed alone per launch
-    hn = torch.randn(out.shape[0], D, device=dev).to(torch.bfloat16)
-    for _ in range(2):
-        kernels.gemm_bf16(hn, head, kernels.GEMM_F32ACC, out=out)
-    ms = []
-    for _ in range(5):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        kernels.gemm_bf16(hn, head, kernels.GEMM_F32ACC, out=out)
-        e.record(stream)
-        e.synchronize()
-        ms.append(s.elapsed_time(e))
-    head_ms = statistics.median(ms)
-    head_flops = 2 * out.shape[0] * n_cols * D
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    peak = float(peaks.get("bf16_tflops", 1590.0))
-    roof = {"bound": "tensor", "kernel": "umma_gemm_kernel bf16 (the head GEMM, EPI_F32ACC)",
-            "achieved": round(head_flops / head_ms / 1e9, 1), "peak": peak, "unit": "TFLOP/s",
-            "frac": round(head_flops / head_ms / 1e9 / peak, 4),
-            "peak_source": "measured dense bf16 cuBLAS burst (MEASURED_PEAKS.json)" if peaks else "fallback",
-            "traffic": None, "per_launch_ms": round(head_ms, 4),
-            "step_tflops": round(flops * args.steps * world / total_s / 1e12, 1)}
-
-    # e2e: token ids from pinned host memory in, every logit back to pinned host memory
-    h_ids = ids.cpu().pin_memory()
-    h_out = torch.empty(out.shape, dtype=torch.bfloat16, pin_memory=True)
-    d_ids = torch.empty_like(ids)
-    e_steps = max(2, min(5, args.steps))
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    s.record(stream)
-    for _ in range(e_steps):
-        d_ids.copy_(h_ids, non_blocking=True)
-        step(d_ids)
-        h_out.copy_(out, non_blocking=True)
-    e.record(stream)
-    barrier(world)
-    e2e_s = max_over_ranks(s.elapsed_time(e) / 1e3, world)
-    e2e = {"value": round(B_all * L * e_steps / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": h_ids.numel() * 8,
-           "d2h_bytes_per_step": h_out.numel() * 2, "api": "xdna_qwen3_stack C ABI (torch_xdna.kernels)"}
-    if rg is not None:
-        rg.close()
-    cb = cpu_stack_baseline(NL, 1, 128) if (rank == 0 and world == 1) else None
+            rec["roofline"] = roof("tensor", "umma_gemm_kernel (gemm_i8, the three GEMMs of the set)",
+                                   work / (gem_ms / 1e3) / 1e12, int8_peak, "TOPS", gem_ms / 3, peak_source=INT8_PEAK_NOTE)
+        out[str(M)] = rec
     if kernels.take_device_error() != (0, 0):
         raise SystemExit("a kernel recorded a device-side timeout")
-    if rank == 0:
-        line = {"metric": "Qwen3-0.6B stack tokens/s (BASELINE config 5)", "value": round(value, 1),
-                "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-                "ms_per_step": round(total_s * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (uniform token ids, N(0,0.02) weights, unit norms)",
-                "config": {"workload": f"cfg5 Qwen3-0.6B stack: {NL} layers, {B_all} sequences x {L} tokens, causal "
-                                       f"mask, head {V_HEAD}, bf16 with f32 accumulation", "global_batch": B_all,
-                           "seq_len": L, "l2": "inputs exceed L2",
-                           "parallelism": (f"dp{world} sequences; head column-parallel over {world}, " + (
-                               ("peer blocks copied over NVLink once, overlapping the GEMM over this rank's rows"
-                                if args.head == "column" else "the GEMM's TMA reading every rank's rows from its memory")
-                               if fused else "NCCL all-gather of hidden states before the head GEMM"))
-                           if column else f"dp{world} (sequences)"},
-                "gpu_launches": launches_per_step * args.steps, "roofline": roof, "e2e": e2e,
-                "clocks": clocks.summary()}
-        if cb is not None:
-            line["cpu_baseline"] = cb
-        print(json.dumps(line), flush=True)
+    return out
 
 
-def cpu_stack_baseline(layers, seqs, seq_len):
-    """The reference's parity route for the stack (the fp32 eager model) restated in torch CPU ops
-    (oracle/reference_cpu.py) on a bounded sample, all host threads."""
-    from oracle import reference_cpu as rc
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(5)
-
-    def w(*s):
-        return torch.randn(*s, generator=g) * 0.02
-
-    ls = [dict(q=w(2048, D), k=w(1024, D), v=w(1024, D), o=w(D, 2048), gate=w(INTER, D), up=w(INTER, D),
-               down=w(D, INTER), input_norm=torch.ones(D), post_norm=torch.ones(D), q_norm=torch.ones(128),
-               k_norm=torch.ones(128)) for _ in range(layers)]
-    head = w(V_HEAD, D)
-    x = torch.randn(seqs, seq_len, D, generator=g)
-    mask = torch.ones(seq_len, seq_len, dtype=torch.bool).tril()[None, None].expand(seqs, 1, seq_len, seq_len)
-    with torch.no_grad():
-        rc.qwen3_stack(ls, torch.ones(D), head, None, x, mask)
-        t0 = time.perf_counter()
-        rc.qwen3_stack(ls, torch.ones(D), head, None, x, mask)
-        dt = time.perf_counter() - t0
-    return {"value": round(seqs * seq_len / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{seqs} sequence x {seq_len} tokens through {layers} layers + head {V_HEAD}, fp32 eager "
-                      f"torch CPU (the reference's parity model)"}
-
-
-# ---------------------------------------------------------------- BASELINE config 4: VGG16 int8 convs
+# ================================================================ BASELINE configs 3 and 4: int8 convs
 VGG16 = [64, 64, "M", 128, 128, "M", 256, 256, 256, "M", 512, 512, 512, "M", 512, 512, 512]
 
 
@@ -693,7 +507,31 @@ def vgg_macs(batch, hw=224):
     return macs
 
 
-def single_conv_roofline(dev, stream, peak, src):
+def cfg3_weights(dev, seed=3):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return [torch.randn(256, 256, 3, 3, device=dev, generator=g) * (2.0 / (256 * 9)) ** 0.5 for _ in range(4)]
+
+
+CFG3_OPS = 4 * 2 * 64 * 64 * 256 * 256 * 9       # 19.3 G int8 ops
+
+
+class Cfg3Net(torch.nn.Module):
+    """BASELINE config 3 (R:examples/conv_xdna.py:20-82 shapes): four bias-free 3x3 convs 256 -> 256, each
+    followed by ReLU."""
+
+    def __init__(self, ws):
+        super().__init__()
+        self.convs = torch.nn.ModuleList(torch.nn.Conv2d(256, 256, 3, padding=1, bias=False) for _ in ws)
+        for c, w in zip(self.convs, ws):
+            c.weight.data = w
+
+    def forward(self, x):
+        for c in self.convs:
+            x = torch.relu(c(x))
+        return x
+
+
+def single_conv_roofline(dev, peak, flush):
     """The conv kernel on BASELINE config 4's single Ci = Co = 256 conv of one 1536 x 64 image (dequantise
     epilogue with bias and ReLU), event-timed per launch with L2 flushed before each."""
     from torch_xdna import conv as xconv
@@ -708,43 +546,31 @@ def single_conv_roofline(dev, stream, peak, src):
     lay.calibrate(xp)
     sx = torch.rand(1, device=dev)
     yo = torch.empty(1, 256, 1536, 64, device=dev, memory_format=torch.channels_last)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    ms = []
-    for i in range(8):
-        flush.fill_(1)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        kernels.conv3x3(xp, lay.wp, 1, 256, 256, 1536, 64, kernels.CONV_DEQUANT, shift=lay.shift, scale=lay.scale,
-                        sx=sx, bias=b, relu=kernels.RELU_AFTER_BIAS, out=yo)
-        e.record(stream)
-        e.synchronize()
-        if i >= 2:
-            ms.append(s.elapsed_time(e))
+    ms = event_ms(lambda: kernels.conv3x3(xp, lay.wp, 1, 256, 256, 1536, 64, kernels.CONV_DEQUANT, shift=lay.shift,
+                                          scale=lay.scale, sx=sx, bias=b, relu=kernels.RELU_AFTER_BIAS, out=yo),
+                  6, flush)
     ops = 2 * 1536 * 64 * 256 * 256 * 9
-    achieved = ops / statistics.median(ms) / 1e9
-    return {"bound": "tensor", "kernel": "umma_gemm_kernel LOAD_CONV (conv 256->256, 1 x 1536 x 64, bias + ReLU)",
-            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS", "frac": round(achieved / peak, 4),
-            "peak_source": src, "per_launch_ms": round(statistics.median(ms), 4)}
+    return roof("tensor", "umma_gemm_kernel LOAD_CONV (conv 256->256, 1 x 1536 x 64, bias + ReLU)",
+                ops / ms / 1e9, peak, "TOPS", ms, peak_source=INT8_PEAK_NOTE)
 
 
-def run_conv(args, rank, world):
-    """One step = the 13 int8 conv3x3 layers of VGG16 (bias + ReLU, 2x2 max-pool between blocks) on this
-    rank's share of a batch of 32 images 3x224x224 (batch sharded over ranks, strong scaling), as the
+def conv_record(args, rank, world, dev, flush):
+    """Config 4: one step = the 13 int8 conv3x3 layers of VGG16 (bias + ReLU, 2x2 max-pool between blocks) on
+    this rank's share of a batch of 32 images 3x224x224 (batch sharded over ranks, strong scaling), as the
     backend compiles it: xdna::conv3x3_chain, the activations between convs kept as int8 codes (the next
     conv's quantise rebuilds the float values and takes the 2x2 max-pool on the codes), the last conv's
     output dequantised with bias and ReLU in its epilogue and max-pooled by torch. --conv-unchained runs
     xdna::conv3x3_fused per conv with torch's max-pool between (same values). The requantise shift of every
     layer comes from global image 0 (rank 0), broadcast to the other ranks."""
     import torch_xdna
+    from torch_xdna import conv as xconv
     from torch_xdna import kernels, parallel
+    from torch_xdna.conv import IN_CODES, IN_CODES_POOL, IN_FLOAT
 
-    if not torch_xdna.gpu_available():
-        raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
-    dev = torch.device("cuda", torch.cuda.current_device())
     if world > 1:
         parallel.enable_data_parallel()
     N_all = args.images
-    assert N_all % world == 0
+    assert N_all % world == 0, "images must divide over the ranks"
     N = N_all // world
     layers = vgg_layers(dev)
     params = [("M" if l == "M" else (torch.nn.Parameter(l[0]), l[1])) for l in layers]
@@ -753,13 +579,10 @@ def run_conv(args, rank, world):
     x_all = torch.randn(N_all, 3, 224, 224, device=dev, generator=g)
     x = x_all[rank * N:(rank + 1) * N].contiguous()
     del x_all
-
-    from torch_xdna.conv import IN_CODES, IN_CODES_POOL, IN_FLOAT
-
     n_convs = sum(p != "M" for p in params)
 
-    def step_unchained(inp):
-        h = inp
+    def step_unchained():
+        h = x
         for p in params:
             if p == "M":
                 h = torch.nn.functional.max_pool2d(h, 2)
@@ -767,8 +590,8 @@ def run_conv(args, rank, world):
                 h = torch.ops.xdna.conv3x3_fused(h, p[0], p[1], False, cid, True)  # ReLU after the bias
         return h
 
-    def step_chained(inp):
-        h, meta, k, pool = inp, None, 0, False
+    def step_chained():
+        h, meta, k, pool = x, None, 0, False
         for p in params:
             if p == "M":
                 if k == n_convs:   # after the last conv: a float tensor
@@ -783,86 +606,329 @@ def run_conv(args, rank, world):
         return h
 
     step = step_unchained if args.conv_unchained else step_chained
-
-    stream = torch.cuda.current_stream()
     with torch.no_grad():
         for _ in range(max(args.warmup, 3)):   # includes each layer's calibration and first-call verify
-            step(x)
+            step()
         torch.cuda.synchronize()
-        # One step captured as a CUDA graph (the same kernels, launched without Python in between): with a
-        # half or quarter batch per GPU the per-op host work would otherwise pace the step
         torch_xdna.stats.reset()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step(x)
+        # replayed from a CUDA graph: with a half or quarter batch per GPU, per-op host work would pace the step
+        total_s, _, clocks = time_graph(step, args.steps, world, dev)   # 400 MB of activations exceed L2
         per_step = torch_xdna.stats.launches
-        graph.replay()
-        barrier(world)
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        with ClockSampler(dev.index) as clocks:
-            barrier(world)
-            for i in range(args.steps):      # 32 x 64 x 224 x 224 activations (400 MB) exceed L2
-                starts[i].record(stream)
-                graph.replay()
-                ends[i].record(stream)
-            barrier(world)
-        launches = per_step * args.steps
-        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-        del graph
-    total_s = max_over_ranks(sum(step_ms) / 1e3, world)
-    value = 2 * vgg_macs(N_all) * args.steps / total_s / 1e12
-    # roofline: the conv kernel of the largest-work layer (conv 64->64 at 224x224), timed alone
-    from torch_xdna import conv as xconv
-
+    if world > 1:
+        parallel.disable_data_parallel()
+    int8_peak = peaks()[0]
+    # roofline: the conv kernel of the largest-work layer (conv 64->64 at 224x224, this rank's images)
     lay = xconv._layer(params[1][0], 224, 224, False)
     xp = torch.zeros(N, 226, 226, lay.cp, dtype=torch.int8, device=dev)
     sx = torch.rand(N, device=dev)
-    yo = torch.empty(N, 64, 224, 224, device=dev)
-    ms = []
-    for i in range(6):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, kernels.CONV_DEQUANT, shift=lay.shift, scale=lay.scale,
-                        sx=sx, bias=params[1][1], out=yo)
-        e.record(stream)
-        e.synchronize()
-        if i:
-            ms.append(s.elapsed_time(e))
+    yo = torch.empty(N, 64, 224, 224, device=dev, memory_format=torch.channels_last)
+    ms = event_ms(lambda: kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, kernels.CONV_DEQUANT, shift=lay.shift,
+                                          scale=lay.scale, sx=sx, bias=params[1][1], relu=kernels.RELU_AFTER_BIAS,
+                                          out=yo), 5)
+    del xp, yo
     conv_ops = 2 * N * 224 * 224 * 64 * 64 * 9
-    peak, src = int8_peak()
-    achieved = conv_ops / statistics.median(ms) / 1e9
-    roof = {"bound": "tensor", "kernel": "umma_gemm_kernel LOAD_CONV (conv 64->64 224x224, dequantise epilogue)",
-            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS", "frac": round(achieved / peak, 4),
-            "peak_source": src, "traffic": None, "per_launch_ms": round(statistics.median(ms), 4)}
-    # config 4's single Ci = Co = 256 conv on one 1536 x 64 image (bias, ReLU after it), timed alone
-    single = single_conv_roofline(dev, stream, peak, src)
-    cb = cpu_conv_baseline() if (rank == 0 and world == 1) else None
+    rec = {"metric": CONV_METRIC, "value": round(2 * vgg_macs(N_all) * args.steps / total_s / 1e12, 2), "unit": "TOPS",
+           "ms_per_step": round(total_s * 1e3 / args.steps, 3), "scaling": "strong", "dtype": "int8",
+           "config": {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224, bias + ReLU, 2x2 max-pool",
+                      "between_convs": "fp32 tensors, torch max-pool" if args.conv_unchained
+                      else "int8 codes (pool on the codes)", "global_batch": N_all,
+                      "parallelism": f"dp{world} (images)", "l2": "activations exceed L2"},
+           "gpu_launches": per_step * args.steps,
+           "roofline": roof("tensor", "umma_gemm_kernel LOAD_CONV_RB (conv 64->64 224x224, dequantise epilogue, bias "
+                            "+ ReLU)", conv_ops / ms / 1e9, int8_peak, "TOPS", ms, peak_source=INT8_PEAK_NOTE,
+                            traffic=None),
+           "step_frac": round(2 * vgg_macs(N_all) * args.steps / total_s / 1e12 / world / int8_peak, 4),
+           "clocks": clocks}
+    rec["single_conv_256x1536x64"] = single_conv_roofline(dev, int8_peak, flush)
+    rec["cfg3"] = cfg3_record(args, rank, world, dev)
     if kernels.take_device_error() != (0, 0):
         raise SystemExit("a kernel recorded a device-side timeout")
-    if rank == 0:
-        line = {"metric": "int8 TOPS/GPU, conv3x3 (BASELINE config 4: VGG16 int8, batch 32)", "value": round(value, 2),
-                "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-                "ms_per_step": round(total_s * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "int8", "data": "synthetic (N(0,1) images, Kaiming weights, N(0,0.01) bias)",
-                "config": {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224, bias + ReLU, 2x2 max-pool",
-                           "between_convs": "fp32 tensors, torch max-pool" if args.conv_unchained
-                           else "int8 codes (pool on the codes)",
-                           "global_batch": N_all, "parallelism": f"dp{world} (images)", "l2": "activations exceed L2"},
-                "gpu_launches": launches, "roofline": roof, "single_conv_256x1536x64": single,
-                "clocks": clocks.summary()}
-        if cb is not None:
-            line["cpu_baseline"] = cb
-        print(json.dumps(line), flush=True)
+    return rec
 
 
-def cpu_conv_baseline(images=1):
-    """The reference's CPU-integer conv route (oracle/reference_cpu.py: exact fp conv of the integers) through
-    the VGG16 conv stack on a bounded sample, all host threads."""
+def cfg3_record(args, rank, world, dev):
+    """Config 3: four bias-free 256-channel convs + ReLU on one 1x256x64x64 image, compiled by the backend
+    (which chains them on int8 codes). ms_per_step: device time of the compiled call replayed from a CUDA
+    graph; e2e_ms: the compiled call with the input copied from pinned host memory and the output copied
+    back, per call. On N > 1 GPUs every rank runs the same image (replicas; a batch of one does not shard)."""
+    import torch_xdna
+
+    ws = cfg3_weights(dev)
+    net = Cfg3Net(ws).to(dev).eval()
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(1, 256, 64, 64, device=dev, generator=g)
+    torch._dynamo.reset()
+    comp = torch.compile(net, backend="xdna", options={"fallback": "eager", "verify": "first"})
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            comp(x)
+        torch.cuda.synchronize()
+        torch_xdna.stats.reset()
+        total_s, _, clocks = time_graph(lambda: comp(x), args.steps, world, dev)
+        per_call = torch_xdna.stats.launches
+        hx = x.cpu().pin_memory()
+        hy = torch.empty(1, 256, 64, 64, pin_memory=True)
+        dx = torch.empty_like(x)
+        stream = torch.cuda.current_stream()
+        reps = max(5, args.steps)
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(reps):
+            dx.copy_(hx, non_blocking=True)
+            hy.copy_(comp(dx), non_blocking=True)
+        e.record(stream)
+        e.synchronize()
+        e2e_ms = max_over_ranks(s.elapsed_time(e) / reps, world)
+    torch._dynamo.reset()
+    ms = total_s * 1e3 / args.steps
+    return {"ms_per_step": round(ms, 4), "tops": round(CFG3_OPS / ms / 1e9, 1), "gpu_launches": per_call * args.steps,
+            "e2e_ms": round(e2e_ms, 4), "e2e_h2d_bytes": hx.numel() * 4, "e2e_d2h_bytes": hy.numel() * 4,
+            "api": "torch.compile(backend='xdna') of 4 x (conv3x3 256->256 + ReLU)", "clocks": clocks,
+            "parallelism": "replicas" if world > 1 else "one GPU",
+            "reference_published_ms": {"inductor_fp32_cpu": 5.72, "xdna_npu_end_to_end": 1.68, "npu_launches": 0.80}}
+
+
+# ================================================================ BASELINE config 5: the Qwen3 stack
+def stack_flops(B, L, layers, vocab):
+    """Algorithmic FLOPs of one step: the projections and head per token, causal attention (QK^T and PV over
+    the keys each query sees)."""
+    per_token = 2 * (layers * (D * 4096 + 2048 * D + D * 6144 + INTER * D) + D * vocab)
+    attn = layers * B * 2 * 2 * 16 * 128 * (L * (L + 1) // 2)
+    return B * L * per_token + attn
+
+
+def stack_record(args, rank, world, dev):
+    """Config 5: one step = embed the token ids of this rank's sequences and run xdna_qwen3_stack (28 layers,
+    final norm, head over 151936) under a causal mask; the global batch is fixed (strong scaling). The layers
+    are data-parallel over sequences (independent: no collective). The head, on more than one GPU, is
+    column-parallel by default: each rank computes its 151936 / N vocabulary columns for every token of every
+    rank, reading the other ranks' final hidden states over NVLink inside the head GEMM's pipeline."""
+    from torch_xdna import kernels, parallel
+
+    B_all, L, NL = args.seqs, args.seq_len, args.layers
+    assert B_all % world == 0, "sequences must divide over the ranks"
+    B = B_all // world
+    g = torch.Generator(device=dev).manual_seed(1234)
+
+    def w(*shape):
+        return (torch.randn(*shape, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+
+    table = (kernels.Qwen3Layer * NL)()
+    keep = []
+    for i in range(NL):
+        qkv, o, gu, down = w(4096, D), w(D, 2048), w(2 * INTER, D), w(D, INTER)
+        norms = [torch.ones(D, device=dev), torch.ones(D, device=dev), torch.ones(128, device=dev),
+                 torch.ones(128, device=dev)]
+        keep += [qkv, o, gu, down] + norms
+        table[i] = kernels.Qwen3Layer(qkv.data_ptr(), o.data_ptr(), gu.data_ptr(), down.data_ptr(),
+                                      *[t.data_ptr() for t in norms])
+    final = torch.ones(D, device=dev)
+    head, embed = w(V_HEAD, D), w(V_HEAD, D)
+    column = world > 1 and args.head in ("column", "column-direct", "column-nccl")
+    fused = column and args.head != "column-nccl"  # the all-gather inside the head's GEMM pipeline
+    n_cols = V_HEAD // world if column else V_HEAD       # 151936 = 2^7 x 1187: divides by 2, 4 and 8
+    if column:
+        head = head[rank * n_cols:(rank + 1) * n_cols].contiguous()
+    inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device=dev) / 128))
+    f = torch.arange(L, dtype=torch.float32, device=dev)[:, None] * inv[None, :]
+    cos, sin = kernels.rope_layout(f.cos()), kernels.rope_layout(f.sin())
+    ids_all = torch.randint(0, V_HEAD, (B_all * L,), device=dev, generator=g)
+    ids = ids_all[rank * B * L:(rank + 1) * B * L].contiguous()
+    x = torch.empty(B * L, D, device=dev)
+    out = torch.empty(B_all * L if column else B * L, n_cols, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(kernels.qwen3_stack_workspace(B, L), dtype=torch.uint8, device=dev)
+    hidden = ws[:B * L * D * 2].view(torch.bfloat16).view(B * L, D)   # the final-normed states (workspace head)
+    h_all = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev) if column and not fused else None
+    rg = parallel.RowGather(B * L, D, dev, mode="direct" if args.head == "column-direct" else "pipelined") \
+        if fused else None
+    launches_per_step = 1 + 7 * NL + 2 + ((world - 1 if args.head == "column" else 0) if column else 0)
+
+    def layers_only(ids_dev):
+        kernels.embed(ids_dev, embed, x)
+        kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
+                            None, ws)
+
+    def head_part():
+        if fused:
+            rg.local.copy_(hidden)
+            rg.gemm(head, out)
+        else:
+            parallel.gather_rows(hidden, h_all)
+            kernels.gemm_bf16(h_all, head, kernels.GEMM_F32ACC, out=out)
+
+    def step(ids_dev):
+        if column:
+            layers_only(ids_dev)
+            head_part()
+        else:
+            kernels.embed(ids_dev, embed, x)
+            kernels.qwen3_stack(table, final, head, None, cos, sin, 1e-6, x, B, L, kernels.MASK_CAUSAL, None, None,
+                                out, ws)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(max(args.warmup, 3)):
+        step(ids)
+    head_check = None
+    if column:   # once, untimed: the pipelined head's logits against the 1-GPU head's for this rank's columns
+        gathered = torch.empty(B_all * L, D, dtype=torch.bfloat16, device=dev)
+        parallel.gather_rows(hidden, gathered)
+        one_gpu = torch.empty_like(out)
+        kernels.gemm_bf16(gathered, head, kernels.GEMM_F32ACC, out=one_gpu)   # one GEMM over all rows
+        exact = bool(torch.equal(out, one_gpu))
+        rows = torch.arange(0, B_all * L, 61, device=dev)
+        ref = gathered[rows].float() @ head.float().t()
+        err = float((out[rows].float() - ref).abs().max() / ref.abs().max())
+        head_check = {"bit_exact_vs_one_gemm": exact, "max_rel_vs_f32_sampled_rows": round(err, 5),
+                      "rows_checked": B_all * L}
+        if not exact and not err < 2e-2:
+            raise SystemExit(f"rank {rank}: column-parallel head disagrees with the one-GEMM head (rel {err:.3g})")
+        del gathered, one_gpu
+    barrier(world)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clocks:
+        barrier(world)
+        for i in range(args.steps):          # weights (1.2 GB) and activations far exceed L2
+            starts[i].record(stream)
+            step(ids)
+            ends[i].record(stream)
+        barrier(world)
+    total_s = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3, world)
+    tokens = B_all * L * args.steps
+    flops = stack_flops(B_all, L, NL, V_HEAD)
+    _, _, bf16_burst, bf16_sust, src = peaks()
+    step_tflops = flops * args.steps / total_s / 1e12
+
+    # breakdown: the layers alone, the head GEMM alone (all rows x this rank's columns, local operands), and
+    # on N > 1 the exchange alone (every peer block copied over NVLink) and the overlapped head
+    reps = max(3, min(args.steps, 10))
+    layers_ms = max_over_ranks(event_ms(lambda: layers_only(ids), reps, warm=1), world)
+    hn = torch.randn(out.shape[0], D, device=dev).to(torch.bfloat16)
+    head_gemm_ms = event_ms(lambda: kernels.gemm_bf16(hn, head, kernels.GEMM_F32ACC, out=out), 5)
+    head_flops = 2 * out.shape[0] * n_cols * D
+    breakdown = {"layers_ms": round(layers_ms, 3), "head_gemm_ms": round(max_over_ranks(head_gemm_ms, world), 3)}
+    if column:
+        breakdown["head_total_ms"] = round(max_over_ranks(event_ms(head_part, reps, warm=1), world), 3)
+        if fused and rg.mode == "pipelined":
+            breakdown["exchange_ms"] = round(max_over_ranks(event_ms(rg.exchange, reps, warm=1), world), 3)
+            breakdown["exchange_bytes_per_rank"] = (world - 1) * B * L * D * 2
+        breakdown["exchange"] = ("peer blocks copied over NVLink by a copy engine while the GEMM runs"
+                                 if args.head == "column" else "the GEMM's TMA reads peer rows" if fused
+                                 else "NCCL all-gather, then the GEMM")
+    rec = {"metric": STACK_METRIC, "value": round(tokens / total_s, 1), "unit": "tokens/s",
+           "ms_per_step": round(total_s * 1e3 / args.steps, 3), "scaling": "strong", "dtype": "bf16",
+           "config": {"workload": f"cfg5 Qwen3-0.6B stack: {NL} layers, {B_all} sequences x {L} tokens, causal "
+                                  f"mask, head {V_HEAD}, bf16 with f32 accumulation", "global_batch": B_all,
+                      "seq_len": L, "l2": "inputs exceed L2",
+                      "parallelism": (f"dp{world} sequences; head column-parallel over {world}") if column
+                      else f"dp{world} (sequences)"},
+           "gpu_launches": launches_per_step * args.steps,
+           "roofline": roof("tensor", "the whole step (bf16 tcgen05 GEMMs + attention), algorithmic FLOPs",
+                            step_tflops / world, bf16_sust, "TFLOP/s", total_s * 1e3 / args.steps,
+                            peak_source=f"dense bf16 cuBLAS sustained, {src}", traffic=None,
+                            flops_per_step=flops),
+           "head_roofline": roof("tensor", "umma_gemm_kernel bf16 (the head GEMM, EPI_F32ACC)",
+                                 head_flops / head_gemm_ms / 1e9, bf16_burst, "TFLOP/s", head_gemm_ms,
+                                 peak_source=f"dense bf16 cuBLAS burst, {src}"),
+           "breakdown": breakdown, "clocks": clocks.summary()}
+    if head_check is not None:
+        rec["head_check"] = head_check
+
+    # e2e: token ids from pinned host memory in, every logit back to pinned host memory
+    h_ids = ids.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=torch.bfloat16, pin_memory=True)
+    d_ids = torch.empty_like(ids)
+    e_steps = max(2, min(5, args.steps))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    s.record(stream)
+    for _ in range(e_steps):
+        d_ids.copy_(h_ids, non_blocking=True)
+        step(d_ids)
+        h_out.copy_(out, non_blocking=True)
+    e.record(stream)
+    barrier(world)
+    e2e_s = max_over_ranks(s.elapsed_time(e) / 1e3, world)
+    rec["e2e"] = {"value": round(B_all * L * e_steps / e2e_s, 1), "unit": "tokens/s",
+                  "h2d_bytes_per_step": h_ids.numel() * 8, "d2h_bytes_per_step": h_out.numel() * 2,
+                  "api": "xdna_embed + xdna_qwen3_stack C ABI (torch_xdna.kernels)"}
+    if rg is not None:
+        rg.close()
+    if kernels.take_device_error() != (0, 0):
+        raise SystemExit("a kernel recorded a device-side timeout")
+    return rec
+
+
+# ================================================================ CPU baselines (the reference's CPU route)
+def _threads():
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_cfg2(rows, budget_s=8.0, min_passes=3):
+    """The reference's CPU route for config 2 (torch._int_mm + its eager quantise / dequantise,
+    oracle/reference_cpu.py) at `rows` rows, all host threads; (TOPS, passes, median seconds)."""
     from oracle import reference_cpu as rc
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+    threads = _threads()
+    g = torch.Generator().manual_seed(1)
+    ops = []
+    for (m, n, k) in gemm_shapes("cfg2", rows):
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        w_kn, sw = rc.quant_weight(w)
+        ops.append((torch.randn(m, k, generator=g).to(torch.bfloat16), w_kn, sw))
+    with torch.no_grad():
+        for x, w_kn, sw in ops:           # warm-up
+            rc.linear_int8(x, w_kn, sw)
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < min_passes:
+            t0 = time.perf_counter()
+            for x, w_kn, sw in ops:
+                rc.linear_int8(x, w_kn, sw)
+            times.append(time.perf_counter() - t0)
+    step = statistics.median(times)
+    work = sum(2 * m * n * k for m, n, k in gemm_shapes("cfg2", rows))
+    return {"value": round(work / step / 1e12, 4), "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"the whole cfg2 projection set at {rows} rows, median of {len(times)} passes; torch._int_mm + "
+                      f"eager quantise/dequantise (the reference's policy='cpu' route)"}
+
+
+def cpu_stack(layers, seqs=1, seq_len=1024):
+    """The reference's parity route for the stack (the fp32 eager model) restated in torch CPU ops
+    (oracle/reference_cpu.py) on a bounded sample: one sequence of the config's length, all host threads."""
+    from oracle import reference_cpu as rc
+
+    threads = _threads()
+    g = torch.Generator().manual_seed(5)
+
+    def w(*s):
+        return torch.randn(*s, generator=g) * 0.02
+
+    ls = [dict(q=w(2048, D), k=w(1024, D), v=w(1024, D), o=w(D, 2048), gate=w(INTER, D), up=w(INTER, D),
+               down=w(D, INTER), input_norm=torch.ones(D), post_norm=torch.ones(D), q_norm=torch.ones(128),
+               k_norm=torch.ones(128)) for _ in range(layers)]
+    head = w(V_HEAD, D)
+    x = torch.randn(seqs, seq_len, D, generator=g)
+    mask = torch.ones(seq_len, seq_len, dtype=torch.bool).tril()[None, None].expand(seqs, 1, seq_len, seq_len)
+    with torch.no_grad():
+        rc.qwen3_stack(ls[:1], torch.ones(D), head[:1024], None, x[:, :64], mask[:, :, :64, :64])   # warm-up
+        t0 = time.perf_counter()
+        rc.qwen3_stack(ls, torch.ones(D), head, None, x, mask)
+        dt = time.perf_counter() - t0
+    return {"value": round(seqs * seq_len / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{seqs} sequence x {seq_len} tokens (causal) through {layers} layers + head {V_HEAD}, fp32 "
+                      f"eager torch CPU (the reference's parity model), one pass of {dt:.1f} s"}
+
+
+def cpu_vgg(images=2, budget_s=6.0):
+    """The reference's CPU-integer conv route (oracle/reference_cpu.py: exact fp conv of the integers) through
+    the VGG16 conv stack on a bounded sample of images, all host threads."""
+    from oracle import reference_cpu as rc
+
+    threads = _threads()
     layers = [("M" if l == "M" else (rc.conv_layer(l[0].cpu(), False), l[1].cpu())) for l in vgg_layers("cpu")]
     x = torch.randn(images, 3, 224, 224, generator=torch.Generator().manual_seed(3))
 
@@ -874,37 +940,197 @@ def cpu_conv_baseline(images=1):
 
     with torch.no_grad():
         run()
-        t0 = time.perf_counter()
-        run()
-        dt = time.perf_counter() - t0
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < 2:
+            t0 = time.perf_counter()
+            run()
+            times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
     return {"value": round(2 * vgg_macs(images) / dt / 1e12, 4), "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"{images} image 3x224x224 through the 13 VGG16 convs (CPU integers: quantise, fp conv of "
-                      f"the integers, requantise, dequantise)"}
+            "sample": f"{images} images 3x224x224 through the 13 VGG16 convs (CPU integers: quantise, fp conv of the "
+                      f"integers, requantise, dequantise), median of {len(times)} passes"}
 
 
-def run_reference_workload(args, rank, world):
-    """--impl reference for the stack and conv workloads: rank 0 times the CPU route on a bounded sample."""
+def cpu_cfg3(budget_s=3.0):
+    """Config 3 on the reference's CPU-integer route (the whole config: one image, four convs + ReLU)."""
+    from oracle import reference_cpu as rc
+
+    threads = _threads()
+    layers = [rc.conv_layer(w.cpu(), True) for w in cfg3_weights("cpu")]
+    x = torch.randn(1, 256, 64, 64, generator=torch.Generator().manual_seed(11))
+
+    def run():
+        h = x
+        for l in layers:
+            h = rc.conv3x3_int8(h, l)
+        return h
+
+    with torch.no_grad():
+        run()
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            run()
+            times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
+    return {"value": round(dt * 1e3, 3), "unit": "ms", "cores": threads, "kind": "port",
+            "sample": f"the whole config (1x256x64x64, 4 convs + ReLU) on the CPU-integer route, median of "
+                      f"{len(times)} passes"}
+
+
+def cpu_msweep():
+    return {str(M): cpu_cfg2(M, budget_s=1.5, min_passes=3) for M in M_SWEEP}
+
+
+# ================================================================ the two arms
+def base_line(args, world, metric, value, unit, dtype, config, scaling="weak"):
+    return {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": dtype, "data": "synthetic (seeded: N(0,1) activations and images, N(0,0.02) or Kaiming weights, "
+                                    "uniform token ids)", "config": config}
+
+
+def run_xdna(args, rank, world):
+    import torch_xdna
+    from torch_xdna import kernels
+
+    if not torch_xdna.gpu_available():
+        raise SystemExit(f"no usable B200: {kernels.unavailable_reason()}")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    wl = args.workload
+    line = None
+    if wl in ("all", "cfg2", "square"):
+        rec = cfg2_records(args, rank, world, dev, flush)
+        metric = CFG2_METRIC if wl != "square" else "int8 TOPS/GPU, W8A8 linear (BASELINE config 2 square 4096^3)"
+        config = cfg2_config(args.rows) if wl != "square" else {
+            "workload": "cfg2 square int8 GEMM M=N=K=4096 (quantise + GEMM + dequantise to bf16)", "l2": "flushed between steps"}
+        line = base_line(args, world, metric, rec.pop("value"), "TOPS", "int8", config)
+        line.update(rec)
+    if wl in ("all", "msweep") and world == 1:
+        ms = msweep_record(args, dev, flush)
+        if line is None:
+            line = base_line(args, world, "int8 TOPS/GPU, W8A8 linear (BASELINE config 2 row sweep)", None, "TOPS",
+                             "int8", {"workload": f"cfg2 projection set at M = {list(M_SWEEP)}"})
+        line["m_sweep"] = ms
+    torch.cuda.empty_cache()
+    if wl in ("all", "conv"):
+        rec = conv_record(args, rank, world, dev, flush)
+        if line is None:
+            line = base_line(args, world, rec.pop("metric"), rec.pop("value"), "TOPS", "int8", rec.pop("config"),
+                             "strong")
+            line.update(rec)
+        else:
+            line["conv"] = rec
+    elif wl == "cfg3":
+        rec = cfg3_record(args, rank, world, dev)
+        line = base_line(args, world, "ms per call, conv3x3 (BASELINE config 3: 4 x 256ch 64x64 + ReLU)",
+                         rec.pop("ms_per_step"), "ms", "int8", {"workload": "cfg3 1x256x64x64, 4 convs + ReLU"})
+        line["higher_is_better"] = False
+        line.update(rec)
+    torch.cuda.empty_cache()
+    if wl in ("all", "stack"):
+        rec = stack_record(args, rank, world, dev)
+        if line is None:
+            line = base_line(args, world, rec.pop("metric"), rec.pop("value"), "tokens/s", "bf16", rec.pop("config"),
+                             "strong")
+            line.update(rec)
+        else:
+            line["stack"] = rec
+    del flush
+    torch.cuda.synchronize()
+    # CPU baselines last (rank 0, one GPU): host work after every GPU measurement
+    if rank == 0 and world == 1:
+        if wl in ("all", "cfg2"):
+            line["cpu_baseline"] = cpu_cfg2(args.rows)
+        if wl in ("all", "msweep"):
+            for k, cb in cpu_msweep().items():
+                line["m_sweep"][k]["cpu_baseline"] = cb
+        conv = line.get("conv", line if wl == "conv" else None)
+        if conv is not None:
+            conv["cpu_baseline"] = cpu_vgg()
+            conv["cfg3"]["cpu_baseline"] = cpu_cfg3()
+        if wl == "cfg3":
+            line["cpu_baseline"] = cpu_cfg3()
+        stack = line.get("stack", line if wl == "stack" else None)
+        if stack is not None:
+            stack["cpu_baseline"] = cpu_stack(args.layers)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU route for the same records on the host cores, rank 0 only. The
+    top level is config 2 at the full row count, one pass of the whole projection set per step."""
     if rank != 0:
         return
-    if args.workload == "stack":
-        cb = cpu_stack_baseline(args.layers, 1, 128)
-        metric, unit, dtype = "Qwen3-0.6B stack tokens/s (BASELINE config 5)", "tokens/s", "fp32"
-        config = {"workload": f"cfg5 Qwen3-0.6B stack: {args.layers} layers, {args.seqs} sequences x {args.seq_len} "
-                              f"tokens, causal, head {V_HEAD}", "global_batch": args.seqs, "seq_len": args.seq_len}
-    else:
-        cb = cpu_conv_baseline()
-        metric, unit, dtype = "int8 TOPS/GPU, conv3x3 (BASELINE config 4: VGG16 int8, batch 32)", "TOPS", "int8"
-        config = {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224", "global_batch": args.images}
-    line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config, "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    wl = args.workload
+    if wl in ("all", "cfg2", "square"):
+        rows = args.rows if wl != "square" else 4096
+        cb = cpu_cfg2(rows, budget_s=0.0, min_passes=max(1, args.steps)) if wl != "square" else None
+        if wl == "square":
+            cb = cpu_square(max(1, args.steps))
+        line = base_line(args, world, CFG2_METRIC if wl != "square" else
+                         "int8 TOPS/GPU, W8A8 linear (BASELINE config 2 square 4096^3)", cb["value"], "TOPS", "int8",
+                         cfg2_config(args.rows) if wl != "square" else {"workload": "cfg2 square int8 GEMM M=N=K=4096"})
+    elif wl == "conv":
+        cb = cpu_vgg()
+        line = base_line(args, world, CONV_METRIC, cb["value"], "TOPS", "int8",
+                         {"workload": "cfg4 VGG16 conv3x3 stack int8, 32x3x224x224", "global_batch": args.images},
+                         "strong")
+    elif wl == "cfg3":
+        cb = cpu_cfg3()
+        line = base_line(args, world, "ms per call, conv3x3 (BASELINE config 3: 4 x 256ch 64x64 + ReLU)", cb["value"],
+                         "ms", "int8", {"workload": "cfg3 1x256x64x64, 4 convs + ReLU"})
+        line["higher_is_better"] = False
+    elif wl == "stack":
+        cb = cpu_stack(args.layers)
+        line = base_line(args, world, STACK_METRIC, cb["value"], "tokens/s", "fp32",
+                         {"workload": f"cfg5 Qwen3-0.6B stack: {args.layers} layers, {args.seqs} sequences x "
+                                      f"{args.seq_len} tokens, causal, head {V_HEAD}", "global_batch": args.seqs,
+                          "seq_len": args.seq_len}, "strong")
+    else:   # msweep
+        ms = cpu_msweep()
+        cb = ms[str(M_SWEEP[-1])]
+        line = base_line(args, world, "int8 TOPS/GPU, W8A8 linear (BASELINE config 2 row sweep)", cb["value"], "TOPS",
+                         "int8", {"workload": f"cfg2 projection set at M = {list(M_SWEEP)}"})
+        line["m_sweep"] = {k: {"value": v["value"], "unit": "TOPS", "cpu_baseline": v} for k, v in ms.items()}
+    line.update({"impl": "reference", "cpu_baseline": cb,
+                 "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+    if wl == "all":
+        ms = cpu_msweep()
+        line["m_sweep"] = {k: {"value": v["value"], "unit": "TOPS", "cpu_baseline": v} for k, v in ms.items()}
+        vgg, c3, st = cpu_vgg(), cpu_cfg3(), cpu_stack(args.layers)
+        line["conv"] = {"metric": CONV_METRIC, "value": vgg["value"], "unit": "TOPS", "cpu_baseline": vgg,
+                        "cfg3": {"ms_per_step": c3["value"], "cpu_baseline": c3}}
+        line["stack"] = {"metric": STACK_METRIC, "value": st["value"], "unit": "tokens/s", "cpu_baseline": st}
     print(json.dumps(line), flush=True)
 
 
+def cpu_square(passes):
+    from oracle import reference_cpu as rc
+
+    threads = _threads()
+    g = torch.Generator().manual_seed(1)
+    w_kn, sw = rc.quant_weight((torch.randn(4096, 4096, generator=g) * 0.02).to(torch.bfloat16))
+    x = torch.randn(4096, 4096, generator=g).to(torch.bfloat16)
+    with torch.no_grad():
+        rc.linear_int8(x, w_kn, sw)
+        times = []
+        for _ in range(passes):
+            t0 = time.perf_counter()
+            rc.linear_int8(x, w_kn, sw)
+            times.append(time.perf_counter() - t0)
+    return {"value": round(2 * 4096 ** 3 / statistics.median(times) / 1e12, 4), "unit": "TOPS", "cores": threads,
+            "kind": "port", "sample": f"the whole 4096^3 linear, median of {passes} passes"}
+
+
+# ================================================================ one kernel (profiling)
 def run_kernel(args):
     """--kernel NAME --shape a,b,c: one kernel of libxdna_b200 on one shape, warm-up then 20 launches replayed
-    from a CUDA graph and timed with CUDA events (the command the profiles/ summaries are captured with;
+    from a CUDA graph and timed with CUDA events (the command the ncu summaries are captured with;
     back-to-back launches on the same inputs, so operands may stay in L2 between them). Prints one JSON
     line."""
     from torch_xdna import conv as xconv
@@ -1000,14 +1226,7 @@ def main():
     rank, world = dist_init(args.gpus)
     try:
         if args.impl == "reference":
-            if args.workload in ("stack", "conv"):
-                run_reference_workload(args, rank, world)
-            else:
-                run_reference(args, rank, world)
-        elif args.workload == "stack":
-            run_stack(args, rank, world)
-        elif args.workload == "conv":
-            run_conv(args, rank, world)
+            run_reference(args, rank, world)
         else:
             run_xdna(args, rank, world)
     finally:

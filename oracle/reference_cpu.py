@@ -41,11 +41,14 @@ def linear_int8(x, w_kn, sw, bias=None):
 def qwen3_stack(layers, final_norm, head, head_bias, x, allowed, theta=1e6, eps=1e-6):
     """The fp32 eager model the reference checks its fused stack against (R:torch_xdna/stack.py:444-460),
     restated with torch CPU ops: transformers' Qwen3 decoder layers on x [B, L, 1024] under a bool mask
-    [B, 1, L, L], the final norm and the head. layers: list of dicts of float32 tensors (LAYER_KEYS)."""
+    [B, 1, L, L], the final norm and the head. layers: list of dicts of float32 tensors (LAYER_KEYS).
+    The same torch ops run on whatever device x is on (the full-size parity test runs them on the GPU in
+    fp32, TF32 off)."""
     B, L, D = x.shape
     NH, NKV, DH = 16, 8, 128
-    inv_freq = 1.0 / (theta ** (torch.arange(0, DH, 2, dtype=torch.float32) / DH))
-    freqs = torch.arange(L, dtype=torch.float32)[:, None] * inv_freq[None, :]
+    dev = x.device
+    inv_freq = 1.0 / (theta ** (torch.arange(0, DH, 2, dtype=torch.float32, device=dev) / DH))
+    freqs = torch.arange(L, dtype=torch.float32, device=dev)[:, None] * inv_freq[None, :]
     cos, sin = torch.cat([freqs, freqs], -1).cos(), torch.cat([freqs, freqs], -1).sin()
 
     def rms(t, w):

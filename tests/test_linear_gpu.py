@@ -86,8 +86,8 @@ def test_quant_rows_edge_scales(cuda, dtype):
     x = g.standard_normal((rows, k)).astype(np.float32)
     mag = {"float32": [1e-12, 1e-9, 3e-39, 1e-30, 1e30, 3e38], "bfloat16": [1e-12, 1e-9, 1e-30, 1e30, 3e38],
            "float16": [1e-7, 6e-8, 1e-4, 6e4]}[dtype]
-    for i in range(rows):
-        x[i] *= np.float32(mag[i % len(mag)])
+    for i in range(rows):   # each row's max |x| is exactly its magnitude (no overflow to inf)
+        x[i] = (x[i] / np.abs(x[i]).max()).astype(np.float32) * np.float32(mag[i % len(mag)])
     x[-1] = np.float32(mag[0])          # every value equal: each quotient is exactly 127
     xv = orc.cast(x, dtype)
     xq, sx = quant_gpu(t(xv, cuda, TORCH_DT[dtype]))

@@ -136,6 +136,23 @@ class RowGather:
         dist.all_reduce(self._flag, group=self.group)        # every rank has read them
         return out
 
+    def exchange(self):
+        """The exchange of gemm() without the GEMMs ("pipelined" mode): every peer block copied over NVLink
+        into local staging, bracketed by the same two flag all-reduces, the current stream waiting for the
+        copies. Measures the NVLink share of the pipelined head."""
+        import torch.distributed as dist
+
+        assert self.mode == "pipelined"
+        dist.all_reduce(self._flag, group=self.group)
+        cur = torch.cuda.current_stream()
+        self._copy.wait_stream(cur)
+        with torch.cuda.stream(self._copy):
+            for k in range(1, self.world):
+                r = (self.rank + k) % self.world
+                self.staged[r].copy_(self.peers[r], non_blocking=True)
+        cur.wait_stream(self._copy)
+        dist.all_reduce(self._flag, group=self.group)
+
     def close(self):
         import torch.distributed as dist
 
