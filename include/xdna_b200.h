@@ -53,6 +53,16 @@ extern "C" {
  * a few channels packed into each pixel's row) and the weights packed the same way, it is the 3x3 conv
  * of a layer with <= 7 input channels in one K block instead of nine. */
 #define XDNA_CONV_SINGLE_TAP 16
+/* Or'ed into a mode: a stride-2 conv (3x3 with padding 1, or with XDNA_CONV_SINGLE_TAP the 1x1 conv with no
+ * padding). xp is then the input split into its stride phases by xdna_conv_quant_phases,
+ * [planes, N, Ho+2, Wo+2, Cp] with planes = 4 (3x3) or 1 (1x1), and H, W are the OUTPUT's height and width
+ * (Ho = ceil(H_in / 2), Wo = ceil(W_in / 2)). Plane 2 * ry + rx at bordered pixel (Y, X) holds input pixel
+ * (2 (Y - 1) + ry, 2 (X - 1) + rx), zero outside the input; tap (ky, kx) of output pixel (y, x) reads plane
+ * ((ky != 1), (kx != 1)) at bordered row y + (ky != 0), column x + (kx != 0), so every tap is a constant row
+ * offset as in the stride-1 conv. Extends the reference's conv route (which offloads only 3x3 stride-1 convs,
+ * R:torch_xdna/backend.py:130-174) to the ResNet-style layers it lists as missing
+ * (R:results/conv3x3_cascade.md:222-223): same quantise, calibration and requantise. */
+#define XDNA_CONV_STRIDE2 32
 /* `relu` of xdna_conv3x3_i8: 0 none; 1 fused into the requantise ([0,255] uint8, the reference's ReLU of
  * a bias-free conv); XDNA_RELU_AFTER_BIAS (DEQUANT only) applied to the dequantised output after the
  * bias, the requantise saturating to int8 — the same values as torch.relu on the DEQUANT output. */
@@ -131,6 +141,15 @@ int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t
  * XDNA_CONV_SINGLE_TAP and weights wp [Co, 1, Kp], byte t * C + c of row co = wq[co, c, t / 3, t % 3]. */
 int xdna_conv_quant_taps(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,
                          int64_t Kp, float* sx, uint32_t* amax_scratch, void* stream);
+
+/* The per-image quantisation of xdna_conv_quant_nhwc (same sx, same values) written as the stride phases a
+ * stride-2 conv reads (XDNA_CONV_STRIDE2): xp [planes, N, Ho+2, Wo+2, Cp], Ho = ceil(H / 2), Wo = ceil(W / 2),
+ * planes 4 (all phases, for the 3x3 conv) or 1 (the even-even phase, for the 1x1 conv). x [N, C, H, W] in
+ * NCHW memory (x_channels_last 0) or channels-last memory (1). Every byte of xp is written (borders and pixels
+ * past the input are zeros). amax_scratch: N words. */
+int xdna_conv_quant_phases(const void* x, int x_dtype, int x_channels_last, int64_t N, int64_t C, int64_t H,
+                           int64_t W, int planes, int8_t* xp, int64_t Cp, float* sx, uint32_t* amax_scratch,
+                           void* stream);
 
 int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
                           const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,

@@ -121,18 +121,23 @@ def conv_weight(w):
     return wq, sw
 
 
-def conv_acc(xq, wq):
-    """Exact int32 sums of the 3x3 / padding-1 conv of the integers, R:torch_xdna/conv.py:86-87."""
+def conv_acc(xq, wq, stride=1):
+    """Exact int32 sums of the conv of the integers, R:torch_xdna/conv.py:86-87 (F.conv2d(xq, wq, padding=1)
+    for the reference's 3x3 convs). A [Co, Ci, 1, 1] wq is a 1x1 conv with no padding, and stride 2 takes
+    every second output row and column -- F.conv2d(xq, wq, stride, padding=k // 2), the same call applied to
+    the 1x1 / stride-2 convs the reference lists as missing (R:results/conv3x3_cascade.md:222-223)."""
     xq = np.asarray(xq, dtype=np.float64)
     wq = np.asarray(wq, dtype=np.float64)
     n, ci, h, w = xq.shape
-    co = wq.shape[0]
-    xp = np.zeros((n, ci, h + 2, w + 2), np.float64)
-    xp[:, :, 1:-1, 1:-1] = xq
-    acc = np.zeros((n, co, h, w), np.float64)
-    for ky in range(3):
-        for kx in range(3):
-            win = xp[:, :, ky:ky + h, kx:kx + w]                       # [n, ci, h, w]
+    co, k = wq.shape[0], wq.shape[-1]
+    p = k // 2
+    ho, wo = (h + 2 * p - k) // stride + 1, (w + 2 * p - k) // stride + 1
+    xp = np.zeros((n, ci, h + 2 * p, w + 2 * p), np.float64)
+    xp[:, :, p:p + h, p:p + w] = xq
+    acc = np.zeros((n, co, ho, wo), np.float64)
+    for ky in range(k):
+        for kx in range(k):
+            win = xp[:, :, ky:ky + stride * (ho - 1) + 1:stride, kx:kx + stride * (wo - 1) + 1:stride]
             acc += np.einsum("nchw,oc->nohw", win, wq[:, :, ky, kx], optimize=True)
     return acc.astype(np.int64).astype(np.int32)
 
@@ -152,12 +157,12 @@ def requant(acc, shift, relu):
     return np.clip(q, 0, 255).astype(np.uint8) if relu else np.clip(q, -128, 127).astype(np.int8)
 
 
-def conv3x3_int8(x, w, bias=None, relu=False, shift=None, x_dtype="float32"):
-    """conv3x3_int8 + xdna::conv3x3 on the CPU route, R:torch_xdna/conv.py:43-51,164-189.
-    Returns dict(y, q, scale, shift, xq, sx, wq, sw)."""
+def conv3x3_int8(x, w, bias=None, relu=False, shift=None, x_dtype="float32", stride=1):
+    """conv3x3_int8 + xdna::conv3x3 on the CPU route, R:torch_xdna/conv.py:43-51,164-189 (and, for a 1x1 w or
+    stride 2, the same route on that conv's sums, conv_acc). Returns dict(y, q, scale, shift, xq, sx, wq, sw)."""
     xq, sx = conv_quant(x)
     wq, sw = conv_weight(w)
-    acc = conv_acc(xq, wq)
+    acc = conv_acc(xq, wq, stride)
     if shift is None:
         shift = calibrate_shift(acc[0], relu)
     q = requant(acc, shift, relu)

@@ -140,6 +140,47 @@ def test_conv_pass_which_convs_and_relu():
     assert sum(n.target is torch.conv2d for n in nodes) == 1
 
 
+class Bottleneck(torch.nn.Module):
+    """A ResNet-50 bottleneck with a stride-2 downsample and a stride-1 3x3 in the middle block."""
+
+    def __init__(self):
+        super().__init__()
+        self.c1 = torch.nn.Conv2d(256, 64, 1, bias=False)
+        self.c2 = torch.nn.Conv2d(64, 64, 3, stride=2, padding=1)
+        self.c3 = torch.nn.Conv2d(64, 256, 1)
+        self.down = torch.nn.Conv2d(256, 256, 1, stride=2, bias=False)
+        self.c4 = torch.nn.Conv2d(256, 64, 3, padding=1)
+        self.c5 = torch.nn.Conv2d(64, 64, 5, padding=2)    # a 5x5 conv: never offloaded
+
+    def forward(self, x):
+        h = torch.relu(self.c1(x))
+        h = torch.relu(self.c2(h))
+        h = torch.relu(self.c3(h) + self.down(x))
+        return self.c5(torch.relu(self.c4(h)))
+
+
+def test_conv_ext_offloads_resnet_convs_only_when_asked():
+    """By default the pass rewrites exactly the reference's convs (3x3 / stride 1 / padding 1: c4 here); with
+    conv_ext also the 1x1 convs (stride 1 and 2) and the stride-2 3x3, each with its stride and the ReLU
+    fusion rules of the 3x3 convs (bias-free: into the requantise; biased: after the bias)."""
+    from torch_xdna.conv import conv_ext_int8
+
+    x = torch.randn(1, 256, 16, 16)
+    (gm,) = capture_graphs(Bottleneck().eval(), x, torch_xdna.Config(policy="npu"))
+    nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
+    assert sum(n.target is conv_ext_int8 for n in nodes) == 0
+    assert sum(n.target is torch.conv2d for n in nodes) == 5
+    assert sum(n.target in (conv3x3_int8, conv3x3_chain_int8) for n in nodes) == 1
+    (gm,) = capture_graphs(Bottleneck().eval(), x, torch_xdna.Config(policy="npu", conv_ext=True))
+    nodes = [n for n in gm.graph.nodes if n.op == "call_function"]
+    ext = [n for n in nodes if n.target is conv_ext_int8]
+    # args: (x, w, b, stride, relu into the requantise, cfg_id, relu after the bias)
+    assert [(n.args[3], n.args[4], n.args[6]) for n in ext] == [(1, True, False), (2, False, True), (1, False, False),
+                                                                (2, False, False)]
+    assert sum(n.target is torch.conv2d for n in nodes) == 1              # the 5x5 conv
+    assert sum(n.target in (torch.relu, torch.nn.functional.relu) for n in nodes) == 1   # after the residual add
+
+
 class VGGish(torch.nn.Module):
     """VGG-style blocks: conv, ReLU, conv, ReLU, 2x2 max-pool, ...; `tap` also returns an intermediate
     activation, which then must stay a float tensor."""

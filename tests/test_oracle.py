@@ -127,6 +127,20 @@ def test_oracle_nan_scale_follows_torch():
     assert np.array_equal(si, want_img, equal_nan=True)
 
 
+@pytest.mark.parametrize("k,stride,h,w", [(3, 1, 9, 11), (1, 1, 7, 5), (1, 2, 7, 6), (3, 2, 9, 10), (3, 2, 8, 8)])
+def test_conv_acc_is_the_references_conv2d_call(k, stride, h, w):
+    """The oracle's exact sums are the reference's F.conv2d(xq, wq, padding=1) (R:torch_xdna/conv.py:86-87),
+    and for the 1x1 / stride-2 extension the same call with the conv's own stride and padding k // 2."""
+    import torch
+
+    g = mg.rng(k * 10 + stride)
+    xq = g.integers(-127, 128, (2, 5, h, w)).astype(np.int8)
+    wq = g.integers(-127, 128, (4, 5, k, k)).astype(np.int8)
+    want = torch.nn.functional.conv2d(torch.from_numpy(xq).double(), torch.from_numpy(wq).double(), stride=stride,
+                                      padding=k // 2).to(torch.int32).numpy()
+    assert np.array_equal(orc.conv_acc(xq, wq, stride), want)
+
+
 def test_requant_rounds_half_up_and_saturates():
     acc = np.array([[-5, -4, -3, 3, 4, 5, 10 ** 6, -10 ** 6]], np.int32)
     assert orc.requant(acc, 1, False).tolist() == [[-2, -2, -1, 2, 2, 3, 127, -128]]

@@ -160,13 +160,15 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   XDNA_CHECK_ARG(N >= 0 && Ci >= 1 && Co >= 1 && H >= 1 && W >= 1, "conv3x3: bad shape");
   XDNA_CHECK_ARG(Cp >= Ci && Cp % 16 == 0, "conv3x3: Cp must be >= Ci and a multiple of 16");
   const bool single_tap = (mode & XDNA_CONV_SINGLE_TAP) != 0;
-  mode &= ~XDNA_CONV_SINGLE_TAP;
+  const bool stride2 = (mode & XDNA_CONV_STRIDE2) != 0;
+  mode &= ~(XDNA_CONV_SINGLE_TAP | XDNA_CONV_STRIDE2);
   XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE ||
                      mode == XDNA_CONV_Q_NHWC,
                  "conv3x3: unknown mode %d", mode);
   XDNA_CHECK_ARG(relu == 0 || relu == 1 || (relu == XDNA_RELU_AFTER_BIAS && mode == XDNA_CONV_DEQUANT),
                  "conv3x3: relu %d (0, 1, or XDNA_RELU_AFTER_BIAS with XDNA_CONV_DEQUANT)", relu);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n_in = N;  // images in xp (a stride-2 input's phase planes are n_in images apart)
   if (mode == XDNA_CONV_CALIBRATE) {
     XDNA_CHECK_ARG(acc_max != nullptr, "conv3x3: calibration needs acc_max");
     XDNA_CUDA(cudaMemsetAsync(acc_max, 0, sizeof(int32_t), s));
@@ -186,15 +188,30 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   XDNA_CHECK_ARG(xp && wp, "conv3x3: null pointer");
   const int64_t Wp = W + 2, HWp = (H + 2) * (W + 2);
   const int64_t NP = N * HWp;
-  XDNA_CHECK_ARG(NP < (1ll << 31) && Co * Cp * 9 < (1ll << 31), "conv3x3: problem exceeds 2^31 elements");
+  // rows of the activation matrix: one bordered image per image, or for a stride-2 conv the phase planes
+  // (4, or the even-even plane alone for the 1x1 conv), each n_in bordered images of the output's geometry
+  const int planes = stride2 ? (single_tap ? 1 : 4) : 1;
+  const int64_t a_rows = stride2 ? planes * n_in * HWp : NP;
+  XDNA_CHECK_ARG(a_rows < (1ll << 31) && Co * Cp * 9 < (1ll << 31), "conv3x3: problem exceeds 2^31 elements");
 
   GemmArgs a{};
   a.M = static_cast<int>(NP);
   a.N = static_cast<int>(Co);
   const int kb = Cp <= 64 ? 64 : kBKBytes;  // K block bytes (= channels) per tap
   a.cblocks = static_cast<int>((Cp + kb - 1) / kb);
-  a.single_tap = single_tap ? 1 : 0;
-  a.num_kb = (single_tap ? 1 : 9) * a.cblocks;
+  a.ntaps = single_tap ? 1 : 9;
+  for (int t = 0; t < a.ntaps; ++t) {
+    const int ky = single_tap ? 1 : t / 3, kx = single_tap ? 1 : t % 3;
+    if (stride2) {
+      // input row 2y + ky - 1 is row y - 1 (ky = 0) or y (ky = 2) of the odd phase, row y of the even one (ky = 1)
+      const int ry = ky == 1 ? 0 : 1, rx = kx == 1 ? 0 : 1;
+      const int dy = ky == 0 ? -1 : 0, dx = kx == 0 ? -1 : 0;
+      a.tap_off[t] = static_cast<int>((2 * ry + rx) * n_in * HWp + dy * Wp + dx);
+    } else {
+      a.tap_off[t] = static_cast<int>((ky - 1) * Wp + (kx - 1));
+    }
+  }
+  a.num_kb = a.ntaps * a.cblocks;
   a.m_tiles = static_cast<int>((NP + kBM - 1) / kBM);
   const int bn = choose_bn(a.m_tiles, Co, sms);
   a.n_tiles = static_cast<int>((Co + bn - 1) / bn);
@@ -224,7 +241,7 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
 
   CUtensorMap ta, tb;
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(NP)};
+    const uint64_t dims[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(a_rows)};
     const uint64_t strides[1] = {static_cast<uint64_t>(Cp)};
     const uint32_t box[2] = {static_cast<uint32_t>(kb), kBM};
     rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations",

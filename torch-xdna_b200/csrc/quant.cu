@@ -413,6 +413,63 @@ __global__ void __launch_bounds__(256) cl_to_bordered_kernel(const T* __restrict
   }
 }
 
+// ---------------------------------------------------------------------------- stride phases of a stride-2 conv
+// xp [planes, N, Ho+2, Wo+2, Cp]: plane 2 ry + rx at bordered pixel (Y, X) holds the quantised input pixel
+// (2 (Y - 1) + ry, 2 (X - 1) + rx), zeros on the border, past the input and for channels >= C. One block per
+// bordered row of one plane of one image, grid (Ho + 2, planes * N), each thread a stream of 4-channel words as
+// cl_to_bordered_kernel. CL: x is channels-last [N, H, W, C] (VEC: 4-channel vector loads), else NCHW.
+template <typename T, bool CL, bool VEC>
+__global__ void __launch_bounds__(256) to_phases_kernel(const T* __restrict__ x, int N, int C, int H, int W, int Ho,
+                                                        int Wo, int Cp, const uint32_t* __restrict__ amax,
+                                                        int8_t* __restrict__ xp, float* __restrict__ sx) {
+  const int Yb = blockIdx.x;
+  const int plane = blockIdx.y / N;
+  const int n = blockIdx.y - plane * N;
+  const int ry = plane >> 1, rx = plane & 1;
+  const int Wp = Wo + 2;
+  const float s = scale_from_amax(__uint_as_float(amax[n]));
+  const float r = __frcp_rn(s);
+  if (plane == 0 && Yb == 0 && threadIdx.x == 0) sx[n] = s;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(xp + ((static_cast<int64_t>(plane) * N + n) * (Ho + 2) + Yb) * Wp * Cp);
+  const int words = Wp * Cp / 4;
+  const int y = 2 * (Yb - 1) + ry;
+  const bool row_ok = Yb >= 1 && Yb <= Ho && y < H;
+  for (int e = threadIdx.x; e < words; e += blockDim.x) {
+    const int Xb = (e * 4) / Cp;
+    const int c = e * 4 - Xb * Cp;
+    const int xx = 2 * (Xb - 1) + rx;
+    uint32_t word = 0;
+    if (row_ok && Xb >= 1 && Xb <= Wo && xx < W && c < C) {
+      float f[4];
+      if constexpr (CL) {
+        const T* src = x + ((static_cast<int64_t>(n) * H + y) * W + xx) * C + c;
+        if (VEC && c + 4 <= C) {
+          if constexpr (sizeof(T) == 4) {
+            const float4 u = __ldg(reinterpret_cast<const float4*>(src));
+            f[0] = u.x, f[1] = u.y, f[2] = u.z, f[3] = u.w;
+          } else {
+            const uint2 u = __ldg(reinterpret_cast<const uint2*>(src));
+            const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) f[k] = to_f32(h[k]);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) f[k] = c + k < C ? to_f32(src[k]) : 0.f;
+        }
+      } else {
+        const int64_t hw = static_cast<int64_t>(H) * W;
+        const T* src = x + (static_cast<int64_t>(n) * C + c) * hw + static_cast<int64_t>(y) * W + xx;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f[k] = c + k < C ? to_f32(src[k * hw]) : 0.f;
+      }
+      word = quant4(f[0], f[1], f[2], f[3], s, r);
+      if (c + 4 > C) word &= 0xFFFFFFFFu >> (8 * (c + 4 - C));  // channels >= C stay zero
+    }
+    dst[e] = word;
+  }
+}
+
 // ---------------------------------------------------------------------------- NCHW -> tap-packed bordered
 // One thread per bordered pixel (yb, xb), i.e. output pixel (yb - 1, xb - 1): the 3x3 stencil's taps of
 // C <= 7 channels as 9 C quantised bytes of its Kp-byte row, tap t = 3 dy + dx reading input pixel
@@ -565,6 +622,18 @@ __global__ void pack_weight_kernel(const int8_t* __restrict__ wq, int64_t Co, in
   }
 }
 
+template <typename T>
+static void launch_phases(const void* x, bool cl, bool vec, int N, int C, int H, int W, int Ho, int Wo, int Cp,
+                          dim3 grid, const uint32_t* amax, int8_t* xp, float* sx, cudaStream_t s) {
+  const T* xt = static_cast<const T*>(x);
+  if (!cl)
+    to_phases_kernel<T, false, false><<<grid, 256, 0, s>>>(xt, N, C, H, W, Ho, Wo, Cp, amax, xp, sx);
+  else if (vec)
+    to_phases_kernel<T, true, true><<<grid, 256, 0, s>>>(xt, N, C, H, W, Ho, Wo, Cp, amax, xp, sx);
+  else
+    to_phases_kernel<T, true, false><<<grid, 256, 0, s>>>(xt, N, C, H, W, Ho, Wo, Cp, amax, xp, sx);
+}
+
 }  // namespace xdna
 
 using namespace xdna;
@@ -630,6 +699,50 @@ int xdna_conv_quant_nhwc(const void* x, int x_dtype, int64_t N, int64_t C, int64
       return fail(XDNA_ERR_INVALID, "conv_quant: x_dtype %d is not f32/bf16/f16", x_dtype);
   }
   return check_launch("conv quantise");
+}
+
+int xdna_conv_quant_phases(const void* x, int x_dtype, int x_channels_last, int64_t N, int64_t C, int64_t H,
+                           int64_t W, int planes, int8_t* xp, int64_t Cp, float* sx, uint32_t* amax_scratch,
+                           void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && C >= 1 && H >= 1 && W >= 1, "conv_quant_phases: bad shape");
+  XDNA_CHECK_ARG(planes == 1 || planes == 4, "conv_quant_phases: planes must be 1 or 4");
+  XDNA_CHECK_ARG(Cp >= C && Cp % 16 == 0, "conv_quant_phases: Cp must be >= C and a multiple of 16");
+  const int64_t Ho = (H + 1) / 2, Wo = (W + 1) / 2;
+  XDNA_CHECK_ARG(Ho + 2 <= 65535 && N * planes <= 65535, "conv_quant_phases: image or batch too large");
+  XDNA_CHECK_ARG(N * C * H * W < (1ll << 40) && (Wo + 2) * Cp < (1ll << 31), "conv_quant_phases: too large");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(x && xp && sx && amax_scratch, "conv_quant_phases: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  XDNA_CUDA(cudaMemsetAsync(amax_scratch, 0, N * sizeof(uint32_t), s));
+  const int64_t per_image = C * H * W;  // an image is contiguous in either layout
+  const int chunks = static_cast<int>(std::min<int64_t>((per_image + 256 * 16 - 1) / (256 * 16), 1024));
+  const dim3 g_amax(chunks, static_cast<unsigned>(N));
+  const dim3 g_ph(static_cast<unsigned>(Ho + 2), static_cast<unsigned>(N * planes));
+  const bool cl = x_channels_last != 0;
+  const bool vec = cl && C % 4 == 0 && aligned16(x);
+  switch (x_dtype) {
+    case XDNA_F32:
+      image_amax_kernel<float><<<g_amax, 256, 0, s>>>(static_cast<const float*>(x), per_image, amax_scratch);
+      launch_phases<float>(x, cl, vec, (int)N, (int)C, (int)H, (int)W, (int)Ho, (int)Wo, (int)Cp, g_ph, amax_scratch,
+                           xp, sx, s);
+      break;
+    case XDNA_BF16:
+      image_amax_kernel<__nv_bfloat16>
+          <<<g_amax, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), per_image, amax_scratch);
+      launch_phases<__nv_bfloat16>(x, cl, vec, (int)N, (int)C, (int)H, (int)W, (int)Ho, (int)Wo, (int)Cp, g_ph,
+                                   amax_scratch, xp, sx, s);
+      break;
+    case XDNA_F16:
+      image_amax_kernel<__half><<<g_amax, 256, 0, s>>>(static_cast<const __half*>(x), per_image, amax_scratch);
+      launch_phases<__half>(x, cl, vec, (int)N, (int)C, (int)H, (int)W, (int)Ho, (int)Wo, (int)Cp, g_ph, amax_scratch,
+                            xp, sx, s);
+      break;
+    default:
+      return fail(XDNA_ERR_INVALID, "conv_quant_phases: x_dtype %d is not f32/bf16/f16", x_dtype);
+  }
+  return check_launch("conv quantise (stride phases)");
 }
 
 int xdna_conv_quant_taps(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp,

@@ -76,9 +76,12 @@ struct GemmArgs {
   int m_tiles, n_tiles;
   // conv geometry
   int cblocks;         // 128-channel blocks per tap
-  int single_tap;      // 1: one tap at offset 0 (a 1x1 conv over the bordered layout, e.g. taps packed into
-                       // channels); 0: the 3x3 stencil's 9 taps
-  int Wp, HWp;         // W + 2, (H + 2) * (W + 2)
+  int ntaps;           // taps of the stencil: 9 (3x3), or 1 (a 1x1 conv over the bordered layout, or taps
+                       // packed into channels)
+  int tap_off[9];      // per tap, the row offset of its input pixel from the output pixel's row in the [pixels,
+                       // Cp] activation matrix: (ky-1)(W+2) + (kx-1) for a stride-1 3x3 conv; for a stride-2
+                       // conv, whose input is split into phase planes, the plane's first row plus the offset
+  int Wp, HWp;         // W + 2, (H + 2) * (W + 2) of the output's bordered geometry
   int H, W;
   FastDiv div_wp, div_hwp;
   // epilogue
@@ -702,7 +705,7 @@ template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB = k
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
-                     const GemmArgs args) {
+                     const __grid_constant__ GemmArgs args) {
   static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
   static_assert(!PAIR || (BN == 256 && KB == 128), "CTA pairs: 256 x 256 tiles of 128-byte K blocks");
   constexpr bool RB = LOAD == LOAD_CONV_RB;   // conv weights resident in shared memory
@@ -802,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       if constexpr (RB) {  // the weights of all taps, once
         if (t_first < total) {
-          const int ntaps = args.single_tap ? 1 : 9;
+          const int ntaps = args.ntaps;
           mbar_arrive_expect_tx(bres, ntaps * B_BYTES);
           for (int tap = 0; tap < ntaps; ++tap) tma_load_3d(smRes + tap * B_BYTES, &tmB, bres, 0, tap, 0);
         }
@@ -830,7 +833,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               const int tap = kb / args.cblocks;
               const int cb = kb - tap * args.cblocks;
-              const int off = args.single_tap ? 0 : (tap / 3 - 1) * args.Wp + (tap % 3 - 1);
+              const int off = args.tap_off[tap];
               tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, cb * K_ELEMS, tile_row0(mb) + off);
               tma_load_3d_pair(smB + stage * B_BYTES, &tmB, fb, cb * K_ELEMS, tap, b_row);
             }
@@ -846,9 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(full + stage, STAGE_TX);
             const int tap = kb / args.cblocks;
             const int cb = kb - tap * args.cblocks;
-            const int dy = args.single_tap ? 0 : tap / 3 - 1;
-            const int dx = args.single_tap ? 0 : tap % 3 - 1;
-            tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, cb * K_ELEMS, mb * kBM + dy * args.Wp + dx);
+            tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, cb * K_ELEMS, mb * kBM + args.tap_off[tap]);
             if constexpr (!RB) tma_load_3d(smB + stage * B_BYTES, &tmB, full + stage, cb * K_ELEMS, tap, nb * BN);
           }
           last_parity[stage] = static_cast<int>(phase);

@@ -138,8 +138,10 @@ def _is_relu(n):
 def _offload_convs(gm, params, cid, attr, cfg):
     """3x3 / stride-1 / padding-1 / groups-1 convs of a parameter weight -> conv3x3_int8
     (R:torch_xdna/backend.py:130-174). A sole-user ReLU is fused: into the requantise for a bias-free conv
-    (as the reference does), into the epilogue after the bias for a biased one."""
-    from .conv import conv3x3_int8, supported
+    (as the reference does), into the epilogue after the bias for a biased one. With cfg.conv_ext, also 1x1
+    convs (stride 1 or 2, no padding) and 3x3 convs with stride 2 and padding 1 -> conv_ext_int8
+    (xdna::conv_int8), the same arithmetic on the conv's own stride and padding."""
+    from .conv import conv3x3_int8, conv_ext_int8, supported
 
     if not cfg.offload:
         return 0
@@ -148,17 +150,26 @@ def _offload_convs(gm, params, cid, attr, cfg):
         if node.op != "call_function" or node.target not in CONV2D:
             continue
         x, w, b, stride, padding, dilation, groups = _conv_args(node)
-        if (_pair(stride) != (1, 1) or (padding != "same" and _pair(padding) != (1, 1))
-                or _pair(dilation) != (1, 1) or groups != 1):
+        if _pair(dilation) != (1, 1) or groups != 1:
             continue
         if not (isinstance(w, torch.fx.Node) and (w in params or w.op == "get_attr")):
             continue
         wt = _tensor_of(w, attr)
         xt = x.meta.get("example_value") if isinstance(x, torch.fx.Node) else None
-        if not (isinstance(wt, torch.Tensor) and wt.dim() == 4 and tuple(wt.shape[2:]) == (3, 3)
-                and isinstance(xt, torch.Tensor) and xt.dim() == 4 and xt.dtype in FLOATS):
+        if not (isinstance(wt, torch.Tensor) and wt.dim() == 4 and isinstance(xt, torch.Tensor) and xt.dim() == 4
+                and xt.dtype in FLOATS):
             continue
-        if not supported(int(wt.shape[1]), int(wt.shape[0]), int(xt.shape[2]), int(xt.shape[3])):
+        k, s = tuple(wt.shape[2:]), _pair(stride)
+        pad = (0, 0) if padding == "valid" or (padding == "same" and k == (1, 1)) else \
+            (1, 1) if (padding == "same" and k == (3, 3)) else _pair(padding)
+        if k == (3, 3) and s == (1, 1) and pad == (1, 1):
+            if not supported(int(wt.shape[1]), int(wt.shape[0]), int(xt.shape[2]), int(xt.shape[3])):
+                continue
+            ext = False
+        elif cfg.conv_ext and ((k == (1, 1) and s in ((1, 1), (2, 2)) and pad == (0, 0))
+                               or (k == (3, 3) and s == (2, 2) and pad == (1, 1))):
+            ext = True
+        else:
             continue
         users = list(node.users)
         relu = users[0] if (cfg.fuse and len(users) == 1 and _is_relu(users[0])) else None
@@ -166,8 +177,11 @@ def _offload_convs(gm, params, cid, attr, cfg):
         with gm.graph.inserting_after(last):
             # bias-free: the ReLU goes into the requantise (the reference's fusion); biased: it is applied
             # in the epilogue after the bias (the reference leaves it in the graph; the values are the same)
-            args = (x, w, b, relu is not None and b is None, cid, relu is not None and b is not None)
-            new = gm.graph.call_function(conv3x3_int8, args)
+            fused, post = relu is not None and b is None, relu is not None and b is not None
+            if ext:
+                new = gm.graph.call_function(conv_ext_int8, (x, w, b, s[0], fused, cid, post))
+            else:
+                new = gm.graph.call_function(conv3x3_int8, (x, w, b, fused, cid, post))
         new.meta.update(last.meta)
         last.replace_all_uses_with(new)
         if relu is not None:

@@ -19,6 +19,11 @@ so existing option dictionaries keep working. On the B200 build their meaning is
                integers (bit for bit) or the fp32 model (stack); a mismatch raises.
                "always": every launch. "off": never.
   verbose      log rewrites.
+
+One option is new in this build (off by default, so the default rewrites exactly the reference's convs):
+  conv_ext     also offload the ResNet-style convs the reference has no kernel for
+               (R:results/conv3x3_cascade.md:222-223): 1x1 convs (stride 1 or 2, no padding) and 3x3
+               convs with stride 2 and padding 1, through the same int8 arithmetic (xdna::conv_int8).
 """
 
 from dataclasses import dataclass, fields, replace
@@ -44,6 +49,7 @@ class Config:
     tuned_tilings: bool = True
     verify: str = "first"
     verbose: bool = False
+    conv_ext: bool = False
 
     def __post_init__(self):
         assert self.policy in POLICIES, f"policy must be one of {POLICIES}"

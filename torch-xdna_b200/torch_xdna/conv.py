@@ -47,6 +47,12 @@ def conv3x3_int8(x, weight, bias, relu: bool, cfg_id: int, post_relu: bool = Fal
     return torch.ops.xdna.conv3x3_fused(x, weight, bias, relu, cfg_id, post_relu)
 
 
+def conv_ext_int8(x, weight, bias, stride: int, relu: bool, cfg_id: int, post_relu: bool = False):
+    """A 1x1 conv (stride 1 or 2) or a stride-2 3x3 conv through int8 (xdna::conv_int8): what the backend
+    puts in the graph for the convs Config(conv_ext=True) offloads."""
+    return torch.ops.xdna.conv_int8(x, weight, bias, stride, relu, cfg_id, post_relu)
+
+
 def conv3x3_chain_int8(x, xmeta, weight, bias, relu: bool, cfg_id: int, post_relu: bool, in_mode: int,
                        in_relu_after: bool, out_q: bool):
     """One conv of a chain whose activations between convs stay int8 (xdna::conv3x3_chain)."""
@@ -60,20 +66,23 @@ def channels_padded(c):
 class ConvLayer:
     """One conv weight at one input size: int8 weights packed for the implicit GEMM, the shift.
     taps: a layer of <= 7 input channels whose float input is quantised with the stencil's 9 taps packed
-    into each pixel's row (conv_quant_taps): its conv is one K block of a single tap instead of nine."""
+    into each pixel's row (conv_quant_taps): its conv is one K block of a single tap instead of nine.
+    A [Co, Ci, 1, 1] weight is a 1x1 conv (one tap); stride 2 reads the input's stride phases
+    (conv_quant_phases). h, w: the input's size; self.h, self.w: the output's."""
 
-    def __init__(self, weight, h, w, relu, taps=False):
+    def __init__(self, weight, h, w, relu, taps=False, stride=1):
         kernels._cuda(weight)
-        co, ci = weight.shape[:2]
+        co, ci, k = weight.shape[0], weight.shape[1], weight.shape[-1]
+        assert k in (1, 3) and stride in (1, 2) and (k == 3 or not taps) and (stride == 1 or not taps)
         wf = weight.detach()
         if wf.dtype not in (torch.float32, torch.bfloat16, torch.float16):
             wf = wf.float()
-        rows = wf.reshape(co, ci * 9).contiguous()
-        self.wq = torch.empty((co, kernels.round_up(ci * 9, 16)), dtype=torch.int8, device=weight.device)
+        rows = wf.reshape(co, ci * k * k).contiguous()
+        self.wq = torch.empty((co, kernels.round_up(ci * k * k, 16)), dtype=torch.int8, device=weight.device)
         self.sw = torch.empty((co,), dtype=torch.float32, device=weight.device)
         kernels.quant_rows(rows, self.wq, self.sw)           # R:torch_xdna/conv.py:58-60
-        self.ci, self.co, self.cp = ci, co, channels_padded(ci)
-        wq4 = self.wq[:, :ci * 9].contiguous().view(co, ci, 3, 3)
+        self.ci, self.co, self.cp, self.k, self.stride = ci, co, channels_padded(ci), k, stride
+        wq4 = self.wq[:, :ci * k * k].contiguous().view(co, ci, k, k)
         self.wq4 = wq4
         self.taps = bool(taps) and ci <= 7
         if self.taps:
@@ -82,19 +91,45 @@ class ConvLayer:
             self.wp = torch.zeros((co, 1, self.cp), dtype=torch.int8, device=weight.device)
             self.wp[:, 0, :9 * ci] = wq4.permute(0, 2, 3, 1).reshape(co, 9 * ci)
             self.mode_flag, self.ci_k = kernels.CONV_SINGLE_TAP, 9 * ci
+        elif k == 1:
+            self.wp = torch.zeros((co, 1, self.cp), dtype=torch.int8, device=weight.device)
+            self.wp[:, 0, :ci] = wq4[:, :, 0, 0]
+            self.mode_flag, self.ci_k = kernels.CONV_SINGLE_TAP, ci
         else:
             self.wp = torch.empty((co, 9, self.cp), dtype=torch.int8, device=weight.device)
             kernels.conv_pack_weight(wq4, self.wp)
             self.mode_flag, self.ci_k = 0, ci
-        self.h, self.w, self.relu = h, w, relu
+        if stride == 2:
+            self.mode_flag |= kernels.CONV_STRIDE2
+        self.hi, self.wi = h, w
+        self.h, self.w = (h + 1) // 2 if stride == 2 else h, (w + 1) // 2 if stride == 2 else w
+        self.relu = relu
         self.shift = self.scale = None
         self.checked = False
-        self.name = f"conv3x3 {ci}->{co} {h}x{w}" + (" relu" if relu else "")
+        kind = "conv3x3" if k == 3 else "conv1x1"
+        self.name = f"{kind}{' stride 2' if stride == 2 else ''} {ci}->{co} {h}x{w}" + (" relu" if relu else "")
 
-    def calibrate(self, xp):
-        """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:71-76)."""
+    def quantise(self, xc, n):
+        """(xp, sx) of the float input xc [n, Ci, h, w]: the per-image quantise into the layout this layer's
+        conv reads (bordered, tap-packed, or the stride-2 phase planes)."""
+        sx = torch.empty((n,), dtype=torch.float32, device=xc.device)
+        scratch = torch.empty((n,), dtype=torch.int32, device=xc.device)
+        if self.stride == 2:
+            xp = torch.empty((1 if self.k == 1 else 4, n, self.h + 2, self.w + 2, self.cp), dtype=torch.int8,
+                             device=xc.device)
+            cl = _channels_last(xc)
+            kernels.conv_quant_phases(xc if cl else xc.contiguous(), xp, sx, scratch, cl)
+        else:
+            xp = _bordered(n, self.h, self.w, self.cp, xc.device)
+            _quantise_float(self, xc, xp, sx, scratch)
+        stats.launches += 2
+        return xp, sx
+
+    def calibrate(self, xp, n=1):
+        """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:71-76). n: the images in xp
+        (a stride-2 input's phase planes are n images apart)."""
         acc_max = torch.empty((1,), dtype=torch.int32, device=xp.device)
-        kernels.conv3x3(xp, self.wp, 1, self.ci_k, self.co, self.h, self.w, kernels.CONV_CALIBRATE | self.mode_flag,
+        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_CALIBRATE | self.mode_flag,
                         relu=self.relu, acc_max=acc_max)
         stats.launches += 1
         top = float(int(acc_max.item()))
@@ -126,17 +161,18 @@ class ConvLayer:
         """The reference's CPU integers for the same layer and shift (ConvLayer.cpu,
         R:torch_xdna/conv.py:86-92), used only to verify launches."""
         dt = torch.float32 if 127 * float(self.wq4.abs().sum(dim=(1, 2, 3)).max()) < 2 ** 24 else torch.float64
-        acc = torch.nn.functional.conv2d(xq_nchw_cpu.to(dt), self.wq4.cpu().to(dt), padding=1)
+        acc = torch.nn.functional.conv2d(xq_nchw_cpu.to(dt), self.wq4.cpu().to(dt), stride=self.stride,
+                                         padding=self.k // 2)
         q = (acc.to(torch.int32) + (1 << (self.shift - 1))) >> self.shift
         return q.clamp_(0, 255).to(torch.uint8) if self.relu else q.clamp_(-128, 127).to(torch.int8)
 
 
-def _layer(weight, h, w, relu, taps=False):
-    key = (id(weight), h, w, relu, bool(taps))
+def _layer(weight, h, w, relu, taps=False, stride=1):
+    key = (id(weight), h, w, relu, bool(taps), stride)
     hit = _layers.get(key)
     if hit is not None and hit[0]() is weight:
         return hit[1]
-    layer = ConvLayer(weight, h, w, relu, taps)
+    layer = ConvLayer(weight, h, w, relu, taps, stride)
     _layers[key] = (weakref.ref(weight), layer)
     return layer
 
@@ -163,10 +199,10 @@ def _bordered(n, h, w, cp, device):
     return torch.empty((n, h + 2, w + 2, cp), dtype=torch.int8, device=device)
 
 
-def _verify(cfg, layer, xp, xq_cpu_fn):
+def _verify(cfg, layer, xp, xq_cpu_fn, n=None):
     if cfg.verify == "off" or (cfg.verify == "first" and layer.checked):
         return
-    n = xp.shape[0]
+    n = xp.shape[0] if n is None else n
     got = layer.q(xp, n).cpu()
     want = layer.cpu_integers(xq_cpu_fn())
     if not torch.equal(got, want):
@@ -228,6 +264,41 @@ def conv3x3_fused(cfg, x, weight, bias, relu, post_relu=False):
     stats.calls[DEVICE] += 1
     stats.seconds[DEVICE] += time.perf_counter() - t0
     stats.macs[DEVICE] += n * co * ci * h * w * 9
+    return y
+
+
+def conv_int8(cfg, x, weight, bias, stride, relu, post_relu=False):
+    """The reference's conv route (R:torch_xdna/conv.py:43-51: per-image quantise, int8 weights per output
+    channel, exact int32 sums, the 25 %-headroom shift fixed from image 0, requantise, dequantise + bias)
+    applied to the ResNet-style convs the reference lists as missing (R:results/conv3x3_cascade.md:222-223):
+    a 1x1 conv (stride 1 or 2, no padding) or a 3x3 conv with stride 2 and padding 1. The integer sums are
+    those of F.conv2d on the integers with the conv's own stride and padding (ConvLayer.cpu_integers).
+    Output channels-last, x.dtype; post_relu as conv3x3_fused."""
+    assert not (relu and post_relu), "relu fuses into the requantise, post_relu after the bias: one of them"
+    kernels._cuda(x, weight, bias)
+    k = weight.shape[-1]
+    if k == 3 and stride == 1:
+        return conv3x3_fused(cfg, x, weight, bias, relu, post_relu)
+    n, ci, h, w = x.shape
+    co = weight.shape[0]
+    t0 = time.perf_counter()
+    with _lock:
+        layer = _layer(weight, h, w, relu, stride=stride)
+        xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
+        xp, sx = layer.quantise(xc, n)
+        if layer.shift is None:
+            layer.calibrate(xp, n)
+
+        def xq_cpu():
+            xf = xc.float().cpu()
+            s = xf.abs().amax(dim=(1, 2, 3), keepdim=True).clamp(min=1e-8) / 127
+            return torch.round(xf / s).clamp(-127, 127).to(torch.int8)
+
+        _verify(cfg, layer, xp, xq_cpu, n)
+        y = layer.dequant(xp, n, sx, bias, x.dtype, post_relu)
+    stats.calls[DEVICE] += 1
+    stats.seconds[DEVICE] += time.perf_counter() - t0
+    stats.macs[DEVICE] += n * co * ci * layer.h * layer.w * k * k
     return y
 
 

@@ -25,7 +25,8 @@ DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16, tor
                torch.uint8: U8}
 # conv3x3 modes
 CONV_Q, CONV_DEQUANT, CONV_CALIBRATE, CONV_Q_NHWC = 0, 1, 2, 3
-CONV_SINGLE_TAP = 16  # or'ed into a conv mode: one tap at offset 0 (taps packed into channels)
+CONV_SINGLE_TAP = 16  # or'ed into a conv mode: one tap at offset 0 (a 1x1 conv, or taps packed into channels)
+CONV_STRIDE2 = 32     # or'ed into a conv mode: stride 2, the input split into phase planes (conv_quant_phases)
 # status codes
 ERR_TIMEOUT = -4
 
@@ -61,6 +62,7 @@ def _load():
         "xdna_conv_quant_channels_last": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
         "xdna_conv_quant_taps": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
+        "xdna_conv_quant_phases": ([P, I, I, I64, I64, I64, I64, I, P, I64, P, P, P], I),
         "xdna_conv_pack_input": ([P, I64, I64, I64, I64, P, I64, P], I),
         "xdna_conv_pack_weight": ([P, I64, I64, P, I64, P], I),
         "xdna_conv3x3_i8": ([P, P, I64, I64, I64, I64, I64, I64, I, I, I, P, P, P, I, P, I, P, P], I),
@@ -218,6 +220,18 @@ def conv_quant_taps(x, xp, sx, scratch):
     N, C, H, W = x.shape
     _check("xdna_conv_quant_taps", L.xdna_conv_quant_taps(_p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp),
                                                           xp.shape[-1], _p(sx), _p(scratch), _stream()))
+
+
+def conv_quant_phases(x, xp, sx, scratch, channels_last):
+    """The per-image quantise of x [N, C, H, W] (NCHW or, with channels_last, channels-last memory) written as
+    the stride phases of a stride-2 conv: xp [planes, N, ceil(H/2)+2, ceil(W/2)+2, Cp], planes 4 (3x3 conv) or
+    1 (1x1 conv) (xdna_conv_quant_phases)."""
+    L = require()
+    _cuda(x, xp, sx, scratch)
+    N, C, H, W = x.shape
+    _check("xdna_conv_quant_phases", L.xdna_conv_quant_phases(
+        _p(x), DTYPE_CODES[x.dtype], int(channels_last), N, C, H, W, xp.shape[0], _p(xp), xp.shape[-1], _p(sx),
+        _p(scratch), _stream()))
 
 
 def conv_quant_codes(q, scale, sx_in, bias, relu_after, pool, xp, sx, scratch):

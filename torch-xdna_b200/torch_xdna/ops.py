@@ -5,8 +5,9 @@ torch.ops.xdna.* keep working; the implementations call the B200 kernels. To the
 torch.compile each op is opaque with a shape function (the fake impl), and Inductor calls it as an
 extern kernel. Two ops are new: xdna::conv3x3_fused, the whole quantise -> conv -> dequantise of
 conv3x3_int8 as one op, because on the B200 those three steps are kernels of ours rather than
-graph ops for the CPU compiler to fuse; and xdna::conv3x3_chain, the same for a conv inside a chain of
-convs whose activations between them stay int8 codes.
+graph ops for the CPU compiler to fuse; xdna::conv3x3_chain, the same for a conv inside a chain of
+convs whose activations between them stay int8 codes; and xdna::conv_int8, the same arithmetic for the
+1x1 and stride-2 convs the reference has no kernel for (offloaded with Config(conv_ext=True)).
 """
 
 from typing import Optional
@@ -89,6 +90,23 @@ def conv3x3_fused(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Te
 def _(x, weight, bias, relu, cfg_id, post_relu=False):
     # the kernel writes channels-last memory (see conv.ConvLayer.dequant)
     return torch.empty((x.shape[0], weight.shape[0], x.shape[2], x.shape[3]), dtype=x.dtype, device=x.device,
+                       memory_format=torch.channels_last)
+
+
+@torch.library.custom_op("xdna::conv_int8", mutates_args=())
+def conv_int8(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], stride: int, relu: bool,
+              cfg_id: int, post_relu: bool = False) -> torch.Tensor:
+    """A 1x1 conv (stride 1 or 2, padding 0) or a stride-2 3x3 conv (padding 1) through int8 with the
+    arithmetic of conv3x3_int8 (conv.conv_int8); the ReLU options as conv3x3_fused."""
+    return conv.conv_int8(_configs[cfg_id], x, weight, bias, stride, relu, post_relu)
+
+
+@conv_int8.register_fake
+def _(x, weight, bias, stride, relu, cfg_id, post_relu=False):
+    h, w = x.shape[2], x.shape[3]
+    if stride == 2:
+        h, w = (h + 1) // 2, (w + 1) // 2
+    return torch.empty((x.shape[0], weight.shape[0], h, w), dtype=x.dtype, device=x.device,
                        memory_format=torch.channels_last)
 
 
