@@ -151,6 +151,18 @@ int xdna_conv_quant_phases(const void* x, int x_dtype, int x_channels_last, int6
                            int64_t W, int planes, int8_t* xp, int64_t Cp, float* sx, uint32_t* amax_scratch,
                            void* stream);
 
+/* The two halves of xdna_conv_quant_nhwc / xdna_conv_quant_channels_last, for an image split into strips of
+ * rows over several GPUs, whose scale needs the max over every strip (combined between the two calls, e.g.
+ * by an all-reduce of the words): xdna_conv_image_amax writes each image's max |x| as its f32 bit pattern
+ * (amax [N], cleared first; per_image = C * H * W contiguous elements, NaN propagates); xdna_conv_quant_given_amax
+ * quantises x [N, C, H, W] (NCHW, or channels-last memory with x_channels_last) into the bordered xp with
+ * sx[n] = max(amax[n], 1e-8) / 127 from the given words. A strip's border rows are written as zeros: the
+ * halo rows from its neighbours are copied over them afterwards. No reference counterpart (the reference
+ * runs on one device); the arithmetic is that of R:torch_xdna/conv.py:45-46. */
+int xdna_conv_image_amax(const void* x, int x_dtype, int64_t N, int64_t per_image, uint32_t* amax, void* stream);
+int xdna_conv_quant_given_amax(const void* x, int x_dtype, int x_channels_last, int64_t N, int64_t C, int64_t H,
+                               int64_t W, int8_t* xp, int64_t Cp, float* sx, const uint32_t* amax, void* stream);
+
 int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
                           const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,
                           int8_t* xp, int64_t Cp, float* sx_out, uint32_t* amax_scratch, void* stream);

@@ -72,6 +72,74 @@ def test_shift_broadcast_and_shards_two_ranks():
     assert torch.equal(logits, want_h @ w.t())
 
 
+def _strip_worker(rank, world, port, q):
+    """One rank of an image split into strips of rows: the per-image max and the calibration max combined
+    over ranks, the strip quantised with the combined scale into the bordered layout, the halo rows
+    exchanged, and the strip's exact conv sums read off its bordered rows -- compared with the whole image."""
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "torch-xdna_b200"))
+    sys.path.insert(0, root)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import numpy as np
+
+        from oracle import xdna_oracle as orc
+        from torch_xdna import parallel
+
+        g = np.random.default_rng(17)
+        N, C, Co, H, W = 2, 5, 4, 11, 7
+        x = g.standard_normal((N, C, H, W)).astype(np.float32)
+        wq = g.integers(-127, 128, (Co, C, 3, 3)).astype(np.int8)
+        r0, r1 = parallel.strip_rows(H, rank, world)
+        rows = r1 - r0
+        xl = x[:, :, r0:r1]
+        # per-image max |x| as bit patterns, combined over the strips
+        amax = torch.from_numpy(np.abs(xl).reshape(N, -1).max(axis=1).astype(np.float32).view(np.int32).copy())
+        parallel.all_max_(amax)
+        xq_all, s_all = orc.conv_quant(x)
+        ok_amax = np.array_equal(amax.numpy().view(np.float32), np.abs(x).reshape(N, -1).max(axis=1))
+        s = (np.maximum(amax.numpy().view(np.float32), np.float32(1e-8)) / np.float32(127)).astype(np.float32)
+        # this strip quantised into the bordered NHWC layout, border rows zero, then the halo
+        xp = torch.zeros(N, rows + 2, W + 2, C, dtype=torch.int8)
+        xp[:, 1:rows + 1, 1:W + 1] = torch.from_numpy(
+            np.clip(np.rint(xl / s[:, None, None, None]), -127, 127).astype(np.int8)).permute(0, 2, 3, 1)
+        parallel.exchange_halo(xp)
+        # the strip's sums: the 3x3 conv over its bordered rows with no further padding
+        acc = torch.nn.functional.conv2d(xp.permute(0, 3, 1, 2).double(), torch.from_numpy(wq).double()).to(torch.int32)
+        want = orc.conv_acc(xq_all, wq)[:, :, r0:r1]
+        ok_acc = np.array_equal(acc.numpy(), want)
+        # the calibration max of image 0's sums, combined over the strips
+        top = torch.tensor([int(acc[0].abs().max())], dtype=torch.int32)
+        parallel.all_max_(top)
+        ok_top = int(top) == int(np.abs(orc.conv_acc(xq_all, wq)[0]).max())
+        q.put((rank, (r0, r1), ok_amax, bool(np.array_equal(s, s_all)), ok_acc, ok_top))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_image_strips_halo_and_combined_maxima(world):
+    """Image strips for batch-1 convs: 11 rows over 2 or 3 ranks (the middle rank exchanges both halos)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_strip_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    spans = [r[1] for r in res]
+    assert spans[0][0] == 0 and spans[-1][1] == 11 and all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    for r in res:
+        assert r[2:] == (True, True, True, True), r
+
+
 def test_shard_rejects_uneven():
     from torch_xdna import parallel
 

@@ -855,6 +855,79 @@ int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t
   return check_launch("conv quantise (channels-last)");
 }
 
+int xdna_conv_image_amax(const void* x, int x_dtype, int64_t N, int64_t per_image, uint32_t* amax, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && N <= 65535 && per_image >= 1, "conv_image_amax: bad shape");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(x && amax, "conv_image_amax: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  XDNA_CUDA(cudaMemsetAsync(amax, 0, N * sizeof(uint32_t), s));
+  const int chunks = static_cast<int>(std::min<int64_t>((per_image + 256 * 16 - 1) / (256 * 16), 1024));
+  const dim3 g(chunks, static_cast<unsigned>(N));
+  switch (x_dtype) {
+    case XDNA_F32:
+      image_amax_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), per_image, amax);
+      break;
+    case XDNA_BF16:
+      image_amax_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), per_image, amax);
+      break;
+    case XDNA_F16:
+      image_amax_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(x), per_image, amax);
+      break;
+    default:
+      return fail(XDNA_ERR_INVALID, "conv_image_amax: x_dtype %d is not f32/bf16/f16", x_dtype);
+  }
+  return check_launch("image_amax_kernel");
+}
+
+int xdna_conv_quant_given_amax(const void* x, int x_dtype, int x_channels_last, int64_t N, int64_t C, int64_t H,
+                               int64_t W, int8_t* xp, int64_t Cp, float* sx, const uint32_t* amax, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && C >= 1 && H >= 1 && W >= 1, "conv_quant_given_amax: bad shape");
+  XDNA_CHECK_ARG(Cp >= C && Cp % 16 == 0, "conv_quant_given_amax: Cp must be >= C and a multiple of 16");
+  XDNA_CHECK_ARG(H + 2 <= 65535 && N * ((Cp + 63) / 64) <= 65535, "conv_quant_given_amax: too large");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(x && xp && sx && amax, "conv_quant_given_amax: null pointer");
+  const bool cl = x_channels_last != 0;
+  if (cl) XDNA_CHECK_ARG(aligned16(x) && aligned16(xp), "conv_quant_given_amax: x and xp must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int cgroups = static_cast<int>((Cp + 63) / 64);
+  const dim3 g_tr(static_cast<unsigned>((W + 2 + 31) / 32), static_cast<unsigned>(H + 2),
+                  static_cast<unsigned>(N * cgroups));
+  const dim3 g_cl(static_cast<unsigned>(H + 2), static_cast<unsigned>(N));
+  switch (x_dtype) {
+    case XDNA_F32:
+      if (cl)
+        cl_to_bordered_kernel<float><<<g_cl, 256, 0, s>>>(static_cast<const float*>(x), (int)C, (int)H, (int)W,
+                                                          (int)Cp, amax, xp, sx);
+      else
+        to_bordered_nhwc_kernel<float, true><<<g_tr, 256, 0, s>>>(static_cast<const float*>(x), (int)C, (int)H,
+                                                                  (int)W, (int)Cp, cgroups, amax, xp, sx);
+      break;
+    case XDNA_BF16:
+      if (cl)
+        cl_to_bordered_kernel<__nv_bfloat16><<<g_cl, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), (int)C,
+                                                                  (int)H, (int)W, (int)Cp, amax, xp, sx);
+      else
+        to_bordered_nhwc_kernel<__nv_bfloat16, true><<<g_tr, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(x), (int)C, (int)H, (int)W, (int)Cp, cgroups, amax, xp, sx);
+      break;
+    case XDNA_F16:
+      if (cl)
+        cl_to_bordered_kernel<__half><<<g_cl, 256, 0, s>>>(static_cast<const __half*>(x), (int)C, (int)H, (int)W,
+                                                           (int)Cp, amax, xp, sx);
+      else
+        to_bordered_nhwc_kernel<__half, true><<<g_tr, 256, 0, s>>>(static_cast<const __half*>(x), (int)C, (int)H,
+                                                                   (int)W, (int)Cp, cgroups, amax, xp, sx);
+      break;
+    default:
+      return fail(XDNA_ERR_INVALID, "conv_quant_given_amax: x_dtype %d is not f32/bf16/f16", x_dtype);
+  }
+  return check_launch("conv quantise (given maxima)");
+}
+
 int xdna_conv_pack_input(const int8_t* xq, int64_t N, int64_t C, int64_t H, int64_t W, int8_t* xp, int64_t Cp,
                          void* stream) {
   int rc = check_device(nullptr);

@@ -47,6 +47,39 @@ def conv3x3_int8(x, weight, bias, relu: bool, cfg_id: int, post_relu: bool = Fal
     return torch.ops.xdna.conv3x3_fused(x, weight, bias, relu, cfg_id, post_relu)
 
 
+def conv3x3_strip(cfg, x, weight, bias, relu, post_relu=False, group=None):
+    """conv3x3_int8 (R:torch_xdna/conv.py:43-51) of images split into strips of rows over the ranks of
+    `group` (parallel.strip_rows): x [N, Ci, rows, W] holds this rank's rows, the result this rank's rows of
+    the output -- the same values one GPU computes for the whole images. Each image's max |x| and the
+    calibration's max of the sums are combined over the ranks (all-reduce max) and every strip's bordered
+    input gets the neighbouring strips' edge rows (parallel.exchange_halo) before the conv."""
+    assert not (relu and post_relu), "relu fuses into the requantise, post_relu after the bias: one of them"
+    kernels._cuda(x, weight, bias)
+    n, ci, rows, w = x.shape
+    co = weight.shape[0]
+    t0 = time.perf_counter()
+    with _lock:
+        layer = _layer(weight, rows, w, relu, strips=True)
+        xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
+        cl = _channels_last(xc)
+        xc = xc if cl else xc.contiguous()
+        amax = torch.empty((n,), dtype=torch.int32, device=x.device)
+        kernels.conv_image_amax(xc, amax)
+        parallel.all_max_(amax, group)
+        xp = _bordered(n, rows, w, layer.cp, x.device)
+        sx = torch.empty((n,), dtype=torch.float32, device=x.device)
+        kernels.conv_quant_given_amax(xc, xp, sx, amax, cl)
+        parallel.exchange_halo(xp, group)
+        stats.launches += 2
+        if layer.shift is None:
+            layer.calibrate(xp, strips=group if group is not None else True)
+        y = layer.dequant(xp, n, sx, bias, x.dtype, post_relu)
+    stats.calls[DEVICE] += 1
+    stats.seconds[DEVICE] += time.perf_counter() - t0
+    stats.macs[DEVICE] += n * co * ci * rows * w * 9
+    return y
+
+
 def conv_ext_int8(x, weight, bias, stride: int, relu: bool, cfg_id: int, post_relu: bool = False):
     """A 1x1 conv (stride 1 or 2) or a stride-2 3x3 conv through int8 (xdna::conv_int8): what the backend
     puts in the graph for the convs Config(conv_ext=True) offloads."""
@@ -125,17 +158,21 @@ class ConvLayer:
         stats.launches += 2
         return xp, sx
 
-    def calibrate(self, xp, n=1):
+    def calibrate(self, xp, n=1, strips=None):
         """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:71-76). n: the images in xp
-        (a stride-2 input's phase planes are n images apart)."""
+        (a stride-2 input's phase planes are n images apart). strips: the process group over whose ranks the
+        image is split into strips of rows; the max of the sums is then the max over every rank's strip."""
         acc_max = torch.empty((1,), dtype=torch.int32, device=xp.device)
         kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_CALIBRATE | self.mode_flag,
                         relu=self.relu, acc_max=acc_max)
         stats.launches += 1
+        if strips is not None:
+            parallel.all_max_(acc_max, None if strips is True else strips)
         top = float(int(acc_max.item()))
         shift = min(31, max(1, math.ceil(math.log2(max(top * 1.25, 1.0) / (255 if self.relu else 127)))))
-        # data parallel: every rank adopts the shift of rank 0, which holds global image 0
-        self.shift = parallel.broadcast_shift(shift, xp.device)
+        # data parallel: every rank adopts the shift of rank 0, which holds global image 0 (strips: every rank
+        # computed the same shift from the combined max)
+        self.shift = parallel.broadcast_shift(shift, xp.device) if strips is None else shift
         self.scale = self.sw * 2.0 ** self.shift
 
     def q(self, xp, n):
@@ -167,8 +204,9 @@ class ConvLayer:
         return q.clamp_(0, 255).to(torch.uint8) if self.relu else q.clamp_(-128, 127).to(torch.int8)
 
 
-def _layer(weight, h, w, relu, taps=False, stride=1):
-    key = (id(weight), h, w, relu, bool(taps), stride)
+def _layer(weight, h, w, relu, taps=False, stride=1, strips=False):
+    # strips: a layer of a strip-split image keeps its own (combined) shift, apart from a same-size whole image
+    key = (id(weight), h, w, relu, bool(taps), stride, strips)
     hit = _layers.get(key)
     if hit is not None and hit[0]() is weight:
         return hit[1]

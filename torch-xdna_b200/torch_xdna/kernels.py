@@ -63,6 +63,8 @@ def _load():
         "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
         "xdna_conv_quant_taps": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_phases": ([P, I, I, I64, I64, I64, I64, I, P, I64, P, P, P], I),
+        "xdna_conv_image_amax": ([P, I, I64, I64, P, P], I),
+        "xdna_conv_quant_given_amax": ([P, I, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_pack_input": ([P, I64, I64, I64, I64, P, I64, P], I),
         "xdna_conv_pack_weight": ([P, I64, I64, P, I64, P], I),
         "xdna_conv3x3_i8": ([P, P, I64, I64, I64, I64, I64, I64, I, I, I, P, P, P, I, P, I, P, P], I),
@@ -220,6 +222,26 @@ def conv_quant_taps(x, xp, sx, scratch):
     N, C, H, W = x.shape
     _check("xdna_conv_quant_taps", L.xdna_conv_quant_taps(_p(x), DTYPE_CODES[x.dtype], N, C, H, W, _p(xp),
                                                           xp.shape[-1], _p(sx), _p(scratch), _stream()))
+
+
+def conv_image_amax(x, amax):
+    """amax [N] int32 = the bit patterns of each image's max |x| (x [N, ...], each image contiguous)."""
+    L = require()
+    _cuda(x, amax)
+    N = x.shape[0]
+    _check("xdna_conv_image_amax", L.xdna_conv_image_amax(_p(x), DTYPE_CODES[x.dtype], N, x.numel() // max(N, 1),
+                                                          _p(amax), _stream()))
+
+
+def conv_quant_given_amax(x, xp, sx, amax, channels_last):
+    """The bordered quantise of x [N, C, H, W] (NCHW, or channels-last memory) with the per-image maxima given
+    as bit patterns in amax [N] (e.g. combined over an image's strips)."""
+    L = require()
+    _cuda(x, xp, sx, amax)
+    N, C, H, W = x.shape
+    _check("xdna_conv_quant_given_amax", L.xdna_conv_quant_given_amax(
+        _p(x), DTYPE_CODES[x.dtype], int(channels_last), N, C, H, W, _p(xp), xp.shape[-1], _p(sx), _p(amax),
+        _stream()))
 
 
 def conv_quant_phases(x, xp, sx, scratch, channels_last):

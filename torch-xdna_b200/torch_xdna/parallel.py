@@ -48,6 +48,50 @@ def broadcast_shift(shift: int, device) -> int:
     return int(t.item())
 
 
+def strip_rows(H: int, rank: int, world: int):
+    """Rows [r0, r1) of an H-row image that rank `rank` of `world` holds: equal strips, the first H % world
+    ranks one row more."""
+    base, extra = divmod(H, world)
+    r0 = rank * base + min(rank, extra)
+    return r0, r0 + base + (1 if rank < extra else 0)
+
+
+def all_max_(t: torch.Tensor, group=None) -> torch.Tensor:
+    """t = the elementwise max of t over the ranks (in place). Non-negative float bit patterns held as int32
+    (per-image maxima of |x|) order like their values, so their max is the max of the values, bit for bit."""
+    import torch.distributed as dist
+
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return t
+
+
+def exchange_halo(xp: torch.Tensor, group=None) -> torch.Tensor:
+    """The 1-row halo of a strip in the bordered layout xp [N, rows + 2, W + 2, Cp] (rows 1..rows this rank's
+    own): row 0 receives the last own row of the rank above, row rows + 1 the first own row of the rank below;
+    the image's top and bottom ranks keep their zero border. Every rank calls it in the same order."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    if world == 1:
+        return xp
+    peer = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
+    rows = xp.shape[1] - 2
+    send_up, send_dn = xp[:, 1].contiguous(), xp[:, rows].contiguous()
+    recv_up, recv_dn = torch.empty_like(send_up), torch.empty_like(send_dn)
+    ops = []
+    if rank > 0:
+        ops += [dist.P2POp(dist.isend, send_up, peer(rank - 1), group), dist.P2POp(dist.irecv, recv_up, peer(rank - 1), group)]
+    if rank < world - 1:
+        ops += [dist.P2POp(dist.isend, send_dn, peer(rank + 1), group), dist.P2POp(dist.irecv, recv_dn, peer(rank + 1), group)]
+    for req in dist.batch_isend_irecv(ops):
+        req.wait()
+    if rank > 0:
+        xp[:, 0] = recv_up
+    if rank < world - 1:
+        xp[:, rows + 1] = recv_dn
+    return xp
+
+
 def shard(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
     """This rank's contiguous slice of `t` along `dim` (rank 0 holds the first elements)."""
     n = t.shape[dim]
