@@ -126,11 +126,14 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
   if (tstore) {
     const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(ldy * es)};
-    const uint32_t box[2] = {static_cast<uint32_t>(64 / es), 32};
+    // pair tiles with 2-byte outputs store 32 x 128-byte blocks (stage_wide), the rest 32 x 64-byte ones
+    const bool wide = y_dtype != XDNA_I32 && wide_store_map(EPI_DEQ, pair, es);
+    const uint32_t box[2] = {static_cast<uint32_t>((wide ? 128 : 64) / es), 32};
     const CUtensorMapDataType dt = es == 4 ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                    : y_dtype == XDNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    rc = encode_tma(&tc, dt, 2, y, dims, strides, box, "gemm_i8 output", CU_TENSOR_MAP_SWIZZLE_64B);
+    rc = encode_tma(&tc, dt, 2, y, dims, strides, box, "gemm_i8 output",
+                    wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc != XDNA_OK) return rc;
   } else {
     tc = ta;  // unused

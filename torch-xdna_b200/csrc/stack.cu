@@ -102,15 +102,16 @@ static int bf16_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols, i
 }
 
 static int out_map(CUtensorMap* m, const void* p, int64_t rows, int64_t cols, int64_t ld, int dtype,
-                   const char* what) {
+                   const char* what, bool wide = false) {
   const int es = dtype_size(dtype);
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
   const uint64_t strides[1] = {static_cast<uint64_t>(ld * es)};
-  const uint32_t box[2] = {static_cast<uint32_t>(64 / es), 32};  // 32 rows x 64 bytes (the epilogue's staging)
+  // 32 rows x 64 bytes (the epilogue's staging blocks), or 32 x 128 bytes for stage_wide's blocks
+  const uint32_t box[2] = {static_cast<uint32_t>((wide ? 128 : 64) / es), 32};
   const CUtensorMapDataType dt = dtype == XDNA_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : dtype == XDNA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return encode_tma(m, dt, 2, p, dims, strides, box, what, CU_TENSOR_MAP_SWIZZLE_64B);
+  return encode_tma(m, dt, 2, p, dims, strides, box, what, wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 // C[M, N] = A[M, K] . B[N, K]^T (bf16, f32 accumulate) with one of the stack epilogues.
@@ -188,7 +189,9 @@ static int run_bf16_gemm(const Bf16Gemm& g, cudaStream_t s) {
       XDNA_CHECK_ARG(g.bias == nullptr || is_float_dtype(g.bias_dtype), "gemm_bf16: bad bias dtype");
       a.vec_ok = aligned16(g.out) && (g.ldo * dtype_size(g.out_dtype)) % 16 == 0;
       XDNA_CHECK_ARG(a.vec_ok, "gemm_bf16: output rows must be 16-byte aligned (base and row pitch)");
-      if ((rc = out_map(&tc, g.out, g.M, g.N, g.ldo, g.out_dtype, "gemm_bf16 out")) != XDNA_OK) return rc;
+      if ((rc = out_map(&tc, g.out, g.M, g.N, g.ldo, g.out_dtype, "gemm_bf16 out",
+                        wide_store_map(EPI_F32ACC, pair && bn == 256, dtype_size(g.out_dtype)))) != XDNA_OK)
+        return rc;
       if (g.out_dtype == XDNA_F32)
         return bn == 256 ? launch_bf16<256, EPI_F32ACC, XDNA_F32>(ta, tb, tc, a, sms, pair, s)
                          : launch_bf16<128, EPI_F32ACC, XDNA_F32>(ta, tb, tc, a, sms, pair, s);

@@ -307,6 +307,46 @@ __device__ __forceinline__ void stage_and_store(StageRing& ring, const uint32_t 
   }
 }
 
+// 2-byte outputs on CTA-pair tiles: two consecutive 32-column chunks form one 32-row x 128-byte block of the
+// warp's staging (128-byte swizzle: 16-byte chunk j of row r at position j ^ (r & 7), conflict-free), written
+// by one TMA store once both halves are in -- or after the left half alone when the right one lies past the
+// output's last column (the tensor map clips it). Half the store rows of 64-byte blocks: the TMA unit that
+// issues every operand load of the mainloop spends its time per row, and the output's rows were most of it.
+// buf: 4 KB, 1024-byte aligned; the tensor map's box is 32 rows x 128 bytes with SWIZZLE_128B.
+__device__ __forceinline__ void stage_wide(uint8_t* buf, const uint32_t (&w)[16], int half, bool flush,
+                                           const CUtensorMap* tmC, int x0, int y) {
+  const int lane = lane_id();
+  if (half == 0) {  // the previous block's store has finished reading the staging
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *reinterpret_cast<uint4*>(buf + lane * 128 + (((4 * half + k) ^ (lane & 7)) * 16)) =
+        make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  if (flush) {
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, buf, x0, y);
+      bulk_commit();
+    }
+  }
+}
+
+// Whether an epilogue stores through 32 x 128-byte blocks (stage_wide): CTA pairs, 2-byte outputs, and 4 KB of
+// the warp's staging free of column factors. The host encodes the output's tensor map to match
+// (wide_store_map).
+template <int EPI, int ODT, bool PAIR, int OUTB>
+__host__ __device__ constexpr bool wide_store() {
+  return PAIR && ODT != XDNA_F32 && ODT != XDNA_I32 &&
+         ((EPI == EPI_DEQ && OUTB == 8192) || EPI == EPI_F32ACC);
+}
+// The host side of the same choice (pair tiles of 256 columns, 2-byte output elements).
+inline bool wide_store_map(int epi, bool pair, int out_bytes) {
+  return pair && out_bytes == 2 && (epi == EPI_DEQ || epi == EPI_F32ACC);
+}
+
 // Direct (non-TMA) stores of one row's 32 values, for outputs TMA cannot address.
 template <int EPI>
 __device__ __forceinline__ void store_direct(const GemmArgs& a, int row, int n0, const uint32_t (&r)[32],
@@ -955,6 +995,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr bool kConvRows = EPI == EPI_CONV_DEQ && OUTB == 8192;
     constexpr bool kSmemFactors = (EPI == EPI_DEQ && TSTORE) || kConvRows;
     constexpr int kFactorOff = OUTB == 8192 ? 4096 : kStageSlotBytes;
+    // 32 x 128-byte output blocks (stage_wide): the first 4 KB of the warp's area, factors behind them
+    constexpr bool kWide = TSTORE && wide_store<EPI, ODT, PAIR, OUTB>();
+    static_assert(!(TSTORE && PAIR && EPI == EPI_DEQ && ODT != XDNA_F32 && ODT != XDNA_I32) || kWide,
+                  "the host encodes 32 x 128-byte output blocks for every pair tile with 2-byte outputs");
+    static_assert(!kWide || (NCH % 2 == 0 && (!kSmemFactors || kFactorOff >= 4096)), "wide blocks: 4 KB of staging");
     // (EPI_QKV: the head's norm weights where the factors would be; with 4 KB, one staging slot)
     StageRing ring{obuf, 0, ((EPI == EPI_DEQ && TSTORE) || EPI == EPI_QKV) && OUTB == kStageOutBytes ? 1 : 2};
     float* col_sw = reinterpret_cast<float*>(obuf + kFactorOff);          // [WCOLS]
@@ -1088,7 +1133,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                   uint32_t w[16];
 #pragma unroll
                   for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], ODT);
-                  stage_and_store<16>(ring, w, &tmC, n0, row0);
+                  if constexpr (kWide)
+                    stage_wide(obuf, w, c & 1, (c & 1) || c + 1 == NCH || n0 + 32 >= args.N, &tmC,
+                               n0 - 32 * (c & 1), row0);
+                  else
+                    stage_and_store<16>(ring, w, &tmC, n0, row0);
                 }
               }
             } else {
@@ -1114,7 +1163,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t w[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) w[j] = pack2(v[2 * j], v[2 * j + 1], ODT);
-                stage_and_store<16>(ring, w, &tmC, n0, row0);
+                if constexpr (kWide)
+                  stage_wide(obuf, w, c & 1, (c & 1) || c + 1 == NCH || n0 + 32 >= args.N, &tmC,
+                             n0 - 32 * (c & 1), row0);
+                else
+                  stage_and_store<16>(ring, w, &tmC, n0, row0);
               }
             } else {
               store_direct<EPI>(args, row, n0, rc, v);
