@@ -1,5 +1,6 @@
 // xdna_gemm_i8 and xdna_conv3x3_i8: host side of the tcgen05 int8 GEMM (umma_gemm.cuh).
 #include <algorithm>
+#include <cstdlib>
 
 #include "host_util.h"
 #include "umma_gemm.cuh"
@@ -31,8 +32,12 @@ static int dispatch_bn(int bn, bool pair, const CUtensorMap& ta, const CUtensorM
 // The conv's kernel for one mode, with 64-byte K blocks when the input has at most 64 channels (a
 // 128-byte block would be half zero fill).
 template <int EPI, int ODT>
-static int dispatch_conv(int kb, int bn, bool pair, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
-                         int sms, cudaStream_t stream) {
+static int dispatch_conv(int kb, int bn, bool pair, bool win, const CUtensorMap& ta, const CUtensorMap& tb,
+                         const GemmArgs& args, int sms, cudaStream_t stream) {
+  if (win) {  // resident weights, one window of 130 activation rows per ky (conv_window)
+    if (bn == 128) return launch_umma<128, LOAD_CONV_WIN, EPI, false, ODT, 64>(ta, tb, ta, args, sms, stream);
+    return launch_umma<64, LOAD_CONV_WIN, EPI, false, ODT, 64>(ta, tb, ta, args, sms, stream);
+  }
   if (kb == 64) {
     // one column tile of <= 128 output channels: the 9 taps' weights stay in shared memory
     if (args.n_tiles == 1 && args.cblocks == 1 && bn <= 128) {
@@ -42,6 +47,16 @@ static int dispatch_conv(int kb, int bn, bool pair, const CUtensorMap& ta, const
     return dispatch_bn<LOAD_CONV, EPI, false, ODT, 64>(bn, false, ta, tb, ta, args, sms, stream);
   }
   return dispatch_bn<LOAD_CONV, EPI, false, ODT, 128>(bn, pair, ta, tb, ta, args, sms, stream);
+}
+
+// Whether stride-1 3x3 convs of <= 64 input channels use the window load (LOAD_CONV_WIN); XDNA_CONV_WINDOW=0
+// in the environment turns it off (the per-tap loads of LOAD_CONV_RB), e.g. to compare the two.
+static bool conv_window() {
+  static const bool on = [] {
+    const char* e = std::getenv("XDNA_CONV_WINDOW");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
 }
 
 // Widest tile that still gives every SM work; 64 for narrow outputs.
@@ -215,6 +230,10 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
     }
   }
   a.num_kb = a.ntaps * a.cblocks;
+  // a stride-1 3x3 conv on the resident-weight path (<= 64 input channels, one column tile of <= 128 output
+  // channels) loads one window of kBM + 2 rows per ky, which its three kx taps share (LOAD_CONV_WIN)
+  const bool win = conv_window() && kb == 64 && a.cblocks == 1 && a.ntaps == 9 && !stride2 && Co <= 128;
+  if (win) a.num_kb = 3;
   a.m_tiles = static_cast<int>((NP + kBM - 1) / kBM);
   const int bn = choose_bn(a.m_tiles, Co, sms);
   a.n_tiles = static_cast<int>((Co + bn - 1) / bn);
@@ -246,7 +265,7 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(a_rows)};
     const uint64_t strides[1] = {static_cast<uint64_t>(Cp)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kb), kBM};
+    const uint32_t box[2] = {static_cast<uint32_t>(kb), win ? kBM + 2 : kBM};
     rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations",
                     kb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != XDNA_OK) return rc;
@@ -262,13 +281,13 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   }
   switch (mode) {
     case XDNA_CONV_Q:
-      return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, pair, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, pair, win, ta, tb, a, sms, s);
     case XDNA_CONV_DEQUANT:
-      return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, pair, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, pair, win, ta, tb, a, sms, s);
     case XDNA_CONV_Q_NHWC:
-      return dispatch_conv<EPI_CONV_QNHWC, XDNA_I8>(kb, bn, pair, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_QNHWC, XDNA_I8>(kb, bn, pair, win, ta, tb, a, sms, s);
     default:
-      return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, false, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, false, win, ta, tb, a, sms, s);
   }
 }
 

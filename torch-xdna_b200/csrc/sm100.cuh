@@ -365,6 +365,12 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw64(uint32_t smem_addr) {
   return d;
 }
 
+// The same for a matrix that starts some 64-byte rows into a 512-byte swizzle atom (a conv window read from
+// row 1 or 2 on): the tensor core applies the swizzle to the absolute shared-memory address, as TMA wrote it,
+// so the plain descriptor with the shifted start address reads the shifted rows (checked bit for bit against
+// the CPU integers by the conv tests; the descriptor's base-offset field stays 0).
+__device__ __forceinline__ uint64_t smem_desc_k_sw64_at(uint32_t smem_addr) { return smem_desc_k_sw64(smem_addr); }
+
 __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);

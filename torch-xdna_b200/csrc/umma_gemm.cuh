@@ -31,7 +31,10 @@ namespace xdna {
 // LOAD_CONV_RB: the conv with its weights resident in shared memory for the whole kernel (one channel
 // block of <= 64 channels, one column tile of <= 128 output channels): each stage then holds only the
 // activation rows, which halves the TMA row requests per stage when rows are 64 bytes.
-enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1, LOAD_CONV_RB = 2 };
+// LOAD_CONV_WIN: LOAD_CONV_RB for a stride-1 3x3 conv whose stages each hold one window of kBM + 2 activation
+// rows per ky: the ky's three kx taps read it at row offsets 0, 1 and 2 (their MMA descriptors start one or
+// two 64-byte rows into the window), so each row is requested from TMA once per ky instead of once per tap.
+enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1, LOAD_CONV_RB = 2, LOAD_CONV_WIN = 3 };
 
 enum EpiMode {
   EPI_I32 = 0,         // int32 accumulators
@@ -131,26 +134,30 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
+// RB: 0 -- A and B per stage; 1 -- conv weights resident (9 taps), A per stage; 2 -- resident weights and a
+// window of kBM + 2 A rows per stage that serves a ky's three kx taps, stored in whole 8-row swizzle atoms.
+__host__ __device__ constexpr int a_stage_rows(int RB) { return RB == 2 ? kBM + 8 : kBM; }
+
 // Operand bytes per stage (RB: A only, the weights are resident) and of the resident weights (9 taps).
-template <int BN, int KB, bool RB>
+template <int BN, int KB, int RB>
 __host__ __device__ constexpr int stage_bytes() {
-  return (kBM + (RB ? 0 : BN)) * KB;
+  return (a_stage_rows(RB) + (RB ? 0 : BN)) * KB;
 }
-template <int BN, int KB, bool RB>
+template <int BN, int KB, int RB>
 __host__ __device__ constexpr int resident_bytes() {
   return RB ? 9 * BN * KB : 0;
 }
 
 // Operand stages in 224 KB less the epilogue's staging (8 x OUTB) and any resident weights, at most 12:
 // with 4 KB per epilogue warp 4 / 6 / 8 stages for BN = 256 / 128 / 64 and 128-byte K blocks.
-template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes, bool RB = false>
+template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes, int RB = 0>
 __host__ __device__ constexpr int stages_for() {
   return (224 * 1024 - kEpiWarps * OUTB - resident_bytes<BN, KB, RB>()) / stage_bytes<BN, KB, RB>() < 12
              ? (224 * 1024 - kEpiWarps * OUTB - resident_bytes<BN, KB, RB>()) / stage_bytes<BN, KB, RB>()
              : 12;
 }
 
-template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes, bool RB = false>
+template <int BN, int KB = kBKBytes, int OUTB = kStageOutBytes, int RB = 0>
 __host__ __device__ constexpr int smem_bytes_for() {
   return stages_for<BN, KB, OUTB, RB>() * stage_bytes<BN, KB, RB>() + resident_bytes<BN, KB, RB>() + kEpiWarps * OUTB +
          1024 /*align*/ + 256 /*barriers*/;
@@ -160,7 +167,7 @@ __host__ __device__ constexpr int smem_bytes_for() {
 // also its pixels' output offsets; for the q/k/v projection the head's RMSNorm weights) beside two
 // staging slots, as long as the operand ring keeps at least 5 stages; 4 KB otherwise (one slot, or
 // factors by warp shuffles).
-template <int BROWS, int KB, int EPI, bool PAIR, bool RB = false>
+template <int BROWS, int KB, int EPI, bool PAIR, int RB = 0>
 __host__ __device__ constexpr int stage_out_bytes() {
   return ((EPI == EPI_CONV_DEQ || (PAIR && (EPI == EPI_DEQ || EPI == EPI_QKV))) && stages_for<BROWS, KB, 8192, RB>() >= 5)
              ? 8192
@@ -748,16 +755,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ GemmArgs args) {
   static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
   static_assert(!PAIR || (BN == 256 && KB == 128), "CTA pairs: 256 x 256 tiles of 128-byte K blocks");
-  constexpr bool RB = LOAD == LOAD_CONV_RB;   // conv weights resident in shared memory
+  constexpr int RBM = LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
+  constexpr bool RB = RBM != 0;               // conv weights resident in shared memory
+  constexpr bool WIN = RBM == 2;              // one A window per ky serves its three kx taps
   constexpr bool kConv = LOAD != LOAD_GEMM;
   static_assert(!RB || (!PAIR && KB == 64 && BN <= 128), "resident conv weights: one 64-byte channel block, BN <= 128");
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (tile columns) this CTA loads
-  constexpr int OUTB = stage_out_bytes<BROWS, KB, EPI, PAIR, RB>();
-  constexpr int STAGES = stages_for<BROWS, KB, OUTB, RB>();
-  constexpr int A_BYTES = kBM * KB;
+  constexpr int OUTB = stage_out_bytes<BROWS, KB, EPI, PAIR, RBM>();
+  constexpr int STAGES = stages_for<BROWS, KB, OUTB, RBM>();
+  constexpr int A_BYTES = a_stage_rows(RBM) * KB;  // WIN: kBM + 2 rows used, whole swizzle atoms kept
   constexpr int B_BYTES = BROWS * KB;        // one K block of B (one tap, for the conv)
   constexpr int B_STAGE = RB ? 0 : B_BYTES;  // B bytes in each ring stage
-  constexpr uint32_t STAGE_TX = (PAIR ? 2 : 1) * (A_BYTES + B_STAGE);  // a pair's stage: both CTAs' bytes
+  // a pair's stage: both CTAs' bytes; WIN: the window's kBM + 2 rows
+  constexpr uint32_t STAGE_TX = WIN ? (kBM + 2) * KB : (PAIR ? 2 : 1) * (A_BYTES + B_STAGE);
+  static_assert(!WIN || (A_BYTES % (8 * KB) == 0), "window stages in whole swizzle atoms");
   constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
   constexpr int MMA_M = PAIR ? 2 * kBM : kBM;
   constexpr uint32_t IDESC = BF16 ? idesc_bf16(MMA_M, BN) : idesc_i8(MMA_M, BN);
@@ -772,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * A_BYTES;
   uint8_t* smRes = smB + STAGES * B_STAGE;  // RB: the 9 taps' weights, B_BYTES each
-  uint8_t* smOut = smRes + resident_bytes<BROWS, KB, RB>();  // kEpiWarps x OUTB, 1024-aligned
+  uint8_t* smOut = smRes + resident_bytes<BROWS, KB, RBM>();  // kEpiWarps x OUTB (1024-aligned unless WIN)
   uint64_t* full = reinterpret_cast<uint64_t*>(smOut + kEpiWarps * OUTB);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -887,8 +898,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(smB + stage * B_BYTES, &tmB, full + stage, kb * K_ELEMS, nb * BN);
           } else {
             mbar_arrive_expect_tx(full + stage, STAGE_TX);
-            const int tap = kb / args.cblocks;
-            const int cb = kb - tap * args.cblocks;
+            // WIN: K block kb is ky = kb, its window starting at the row of tap (ky, kx = 0)
+            const int tap = WIN ? 3 * kb : kb / args.cblocks;
+            const int cb = WIN ? 0 : kb - tap * args.cblocks;
             tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, cb * K_ELEMS, mb * kBM + args.tap_off[tap]);
             if constexpr (!RB) tma_load_3d(smB + stage * B_BYTES, &tmB, full + stage, cb * K_ELEMS, tap, nb * BN);
           }
@@ -936,6 +948,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if constexpr (WIN) {
+            // K block kb is ky = kb; its three kx taps read the window from row kx on (64-byte rows, so the
+            // descriptor starts kx rows into the stage) and weights of tap 3 ky + kx
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) {
+              const uint64_t da = smem_desc_k_sw64_at(smem_u32(smA + stage * A_BYTES + kx * KB));
+              const uint64_t db = smem_desc_k_sw64(smem_u32(smRes + (3 * kb + kx) * B_BYTES));
+#pragma unroll
+              for (int k = 0; k < KSTEPS; ++k) umma_i8(d, da + 2 * k, db + 2 * k, IDESC, (kb | kx | k) != 0);
+            }
+          } else {
           const uint64_t da = KB == 128 ? smem_desc_k_sw128(smem_u32(smA + stage * A_BYTES))
                                         : smem_desc_k_sw64(smem_u32(smA + stage * A_BYTES));
           // RB: one channel block, so K block kb is tap kb
@@ -952,6 +975,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_f16(d, da + 2 * k, db + 2 * k, IDESC, acc);
             else
               umma_i8(d, da + 2 * k, db + 2 * k, IDESC, acc);
+          }
           }
           if constexpr (PAIR)
             umma_commit_pair(empty + stage, 0x3);  // frees the stage in both CTAs
@@ -1241,7 +1265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB, bool PAIR>
 static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                               const CUtensorMap& td, const GemmArgs& args, int sms, cudaStream_t stream) {
-  constexpr bool RB = LOAD == LOAD_CONV_RB;
+  constexpr int RB = LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
   constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB, stage_out_bytes<PAIR ? BN / 2 : BN, KB, EPI, PAIR, RB>(), RB>();
   auto kern = umma_gemm_kernel<BN, LOAD, EPI, BF16, TSTORE, ODT, KB, PAIR>;
   // per instantiation and device: resident pairs once the kernel is configured (0 = not yet). Two threads
