@@ -81,6 +81,12 @@ int xdna_device_check(int device);
  * `stream`. *code is XDNA_OK when no kernel recorded an error since the last call. */
 int xdna_take_device_error(int* code, int* site, void* stream);
 
+/* Self-test of the bounded device waits (no reference counterpart): launches one block whose wait on an
+ * mbarrier that nothing arrives at gives up after limit_ns (1 us .. 2 s) of device time, exactly as the
+ * waits inside every kernel of the library do, records XDNA_ERR_TIMEOUT at site 99 in the device error word
+ * and returns; xdna_take_device_error then reports it. The GPU context stays usable. */
+int xdna_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
 /* ------------------------------------------------------------------ W8A8 linear
  * Per-row symmetric int8 quantisation: for each row r of x [rows, cols] (leading dim ldx, dtype
  * f32 / bf16 / f16): scale[r] = max(max_c |x[r,c]|, 1e-8) / 127 (the max taken in x's dtype),
@@ -102,6 +108,12 @@ int xdna_quant_rows_i8(const void* x, int x_dtype, int64_t rows, int64_t cols, i
 int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, int64_t M, int64_t N, int64_t K,
                  const float* sx, const float* sw, const void* bias, int bias_dtype, void* y, int y_dtype,
                  int64_t ldy, void* stream);
+
+/* The kernel configuration xdna_gemm_i8 launches for an M x N output on the current device: *tile_n output
+ * columns per tile (64, 128 or 256) and *pair = 1 when 256 x 256 tiles run on CTA pairs. Callers that
+ * verify one launch per configuration (the reference's verify="first", R:torch_xdna/runtime.py:191-209)
+ * key their checks with it. */
+int xdna_gemm_i8_config(int64_t M, int64_t N, int* tile_n, int* pair);
 
 /* ------------------------------------------------------------------ conv3x3
  * The implicit-GEMM conv reads activations as a zero-bordered NHWC int8 tensor

@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "host_util.h"
+#include "sm100.cuh"
 
 namespace xdna {
 
@@ -63,6 +64,23 @@ int check_device(int* sm_count) {
   if (sms < 0) return fail(XDNA_ERR_DEVICE, "device %d is not an sm_100 GPU", dev);
   if (sm_count) *sm_count = sms;
   return XDNA_OK;
+}
+
+// The self-test of the bounded waits: one thread waits, with limit_ns, on a fresh mbarrier that nothing
+// ever arrives at -- the same bounded wait as every role of the library's kernels -- so the wait runs out,
+// records XDNA_ERR_TIMEOUT at site kSelftestSite in the device error word, and the kernel returns.
+constexpr int kSelftestSite = 99;
+__global__ void wait_selftest_kernel(int* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, err, kSelftestSite, limit_ns);
+  __syncthreads();
 }
 
 int* device_error_word() {
@@ -168,6 +186,14 @@ int xdna_device_check(int device) {
   int rc = xdna::check_device(nullptr);
   if (cur != device) cudaSetDevice(cur);
   return rc;
+}
+
+int xdna_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  int rc = xdna::check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(limit_ns >= 1000 && limit_ns <= 2000000000ull, "selftest: limit must be 1 us .. 2 s");
+  xdna::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(xdna::device_error_word(), limit_ns);
+  return xdna::check_launch("wait_selftest_kernel");
 }
 
 int xdna_take_device_error(int* code, int* site, void* stream) {

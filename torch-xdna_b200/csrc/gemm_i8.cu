@@ -169,6 +169,18 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
   }
 }
 
+int xdna_gemm_i8_config(int64_t M, int64_t N, int* tile_n, int* pair) {
+  int sms = 0;
+  int rc = check_device(&sms);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(M >= 0 && N >= 0 && M < (1ll << 31) && N < (1ll << 31) && tile_n && pair, "gemm_i8_config: bad args");
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  const int bn = choose_bn(m_tiles, N, sms);  // the calls xdna_gemm_i8 makes
+  *tile_n = bn;
+  *pair = use_pairs(bn, m_tiles, (N + bn - 1) / bn, sms) ? 1 : 0;
+  return XDNA_OK;
+}
+
 int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, int64_t Cp, int64_t Co, int64_t H,
                     int64_t W, int mode, int shift, int relu, const float* scale, const float* sx, const void* bias,
                     int bias_dtype, void* out, int out_dtype, int32_t* acc_max, void* stream) {

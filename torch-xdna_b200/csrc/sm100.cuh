@@ -92,9 +92,10 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 // XDNA_WAIT_LIMIT_NS, or as soon as another role of this CTA raised `abort`.
 // CLUSTER: the phase may have been completed by arrivals from the other CTA of a pair (acquire at
 // cluster scope).
+// limit_ns: the bound (XDNA_WAIT_LIMIT_NS in every kernel of the library; shorter in the self-test).
 template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
-                                          int site) {
+                                          int site, uint64_t limit_ns = XDNA_WAIT_LIMIT_NS) {
   auto try_once = [&] { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
   if (try_once()) return true;
   const uint64_t t0 = global_timer();
@@ -103,7 +104,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 32; ++i)
       if (try_once()) return true;
     if (*abort) return false;
-    if (global_timer() - t0 > XDNA_WAIT_LIMIT_NS) {
+    if (global_timer() - t0 > limit_ns) {
       record_error(err, XDNA_ERR_TIMEOUT, site);
       *abort = 1;
       return false;

@@ -16,10 +16,11 @@ import json
 from . import kernels, ops  # noqa: F401  (registers the xdna:: ops)
 from .backend import offload_gemms, xdna_backend
 from .config import Config, set_config
-from .runtime import stats
+from .kernels import XdnaError, XdnaUnavailable
+from .runtime import XdnaResultMismatch, stats
 
 __all__ = ["Config", "set_config", "xdna_backend", "offload_gemms", "compile", "stats", "report",
-           "npu_available", "gpu_available"]
+           "npu_available", "gpu_available", "XdnaError", "XdnaUnavailable", "XdnaResultMismatch"]
 __version__ = "0.1.0+b200"
 
 

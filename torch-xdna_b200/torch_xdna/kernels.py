@@ -58,6 +58,8 @@ def _load():
         "xdna_take_device_error": ([P, P, P], I),
         "xdna_quant_rows_i8": ([P, I, I64, I64, I64, P, I64, P, P], I),
         "xdna_gemm_i8": ([P, I64, P, I64, I64, I64, I64, P, P, P, I, P, I, I64, P], I),
+        "xdna_gemm_i8_config": ([I64, I64, P, P], I),
+        "xdna_selftest_wait_timeout": ([ctypes.c_uint64, P], I),
         "xdna_conv_quant_nhwc": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_channels_last": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
@@ -171,6 +173,19 @@ def take_device_error():
     code, site = ctypes.c_int(0), ctypes.c_int(0)
     _check("xdna_take_device_error", L.xdna_take_device_error(ctypes.byref(code), ctypes.byref(site), _stream()))
     return code.value, site.value
+
+
+def selftest_wait_timeout(limit_ns=1_000_000):
+    """Launch the bounded-wait self-test (a wait that nothing completes, limit_ns of device time); read the
+    result with take_device_error(): (ERR_TIMEOUT, 99)."""
+    _check("xdna_selftest_wait_timeout", require().xdna_selftest_wait_timeout(limit_ns, _stream()))
+
+
+def gemm_i8_config(M, N):
+    """(columns per tile, on CTA pairs) of the kernel xdna_gemm_i8 launches for an M x N output here."""
+    tile_n, pair = ctypes.c_int(0), ctypes.c_int(0)
+    _check("xdna_gemm_i8_config", require().xdna_gemm_i8_config(M, N, ctypes.byref(tile_n), ctypes.byref(pair)))
+    return tile_n.value, bool(pair.value)
 
 
 def round_up(x, m):

@@ -158,20 +158,11 @@ _verified = set()
 
 
 def _bn_for(rows, n):
-    """The kernel configuration libxdna_b200 picks for a GEMM (mirrors choose_bn and use_pairs in
-    csrc/gemm_i8.cu / csrc/umma_gemm.cuh), for verify keys: the tile width, and "pair" when 256 x 256
-    tiles run on CTA pairs."""
-    m_tiles = -(-rows // 128)
-    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    if n <= 64:
-        return 64
-    if n <= 128:
-        return 128
-    if m_tiles * -(-n // 256) >= sms:
-        return "256 pair" if -(-m_tiles // 2) * -(-n // 256) >= sms // 2 else 256
-    if m_tiles * -(-n // 128) >= sms:
-        return 128
-    return 64 if n >= 1024 else 128
+    """The kernel configuration libxdna_b200 launches for a GEMM, as the library reports it
+    (xdna_gemm_i8_config), for verify keys: the tile width, and "pair" when 256 x 256 tiles run on CTA
+    pairs. A new configuration is verified on its first launch."""
+    tile_n, pair = kernels.gemm_i8_config(rows, n)
+    return f"{tile_n} pair" if pair else tile_n
 
 
 def _want_check(cfg, key):
