@@ -592,7 +592,7 @@ def conv_record(args, rank, world, dev, flush):
 
     def step_chained():
         h, meta, k, pool = x, None, 0, False
-        for p in params:
+        for i, p in enumerate(params):
             if p == "M":
                 if k == n_convs:   # after the last conv: a float tensor
                     h = torch.nn.functional.max_pool2d(h, 2)
@@ -601,7 +601,9 @@ def conv_record(args, rank, world, dev, flush):
                 continue
             mode = IN_FLOAT if k == 0 else (IN_CODES_POOL if pool else IN_CODES)
             k += 1
-            h, meta = torch.ops.xdna.conv3x3_chain(h, meta, p[0], p[1], False, cid, True, mode, k > 1, k < n_convs)
+            out_pool = k < n_convs and i + 1 < len(params) and params[i + 1] == "M"
+            h, meta = torch.ops.xdna.conv3x3_chain(h, meta, p[0], p[1], False, cid, True, mode, k > 1, k < n_convs,
+                                                   out_pool)
             pool = False
         return h
 
@@ -617,15 +619,22 @@ def conv_record(args, rank, world, dev, flush):
     if world > 1:
         parallel.disable_data_parallel()
     int8_peak = peaks()[0]
-    # roofline: the conv kernel of the largest-work layer (conv 64->64 at 224x224, this rank's images)
+    # roofline: the conv kernel of the largest-work layer (conv 64->64 at 224x224, this rank's images) as the
+    # chain runs it: int8 codes out, the next layer's per-image maxima over the 2x2 pool's region in the epilogue
     lay = xconv._layer(params[1][0], 224, 224, False)
-    xp = torch.zeros(N, 226, 226, lay.cp, dtype=torch.int8, device=dev)
-    sx = torch.rand(N, device=dev)
+    xp = torch.randint(-127, 128, (N, 226, 226, lay.cp), dtype=torch.int8, device=dev)
+    sx = torch.rand(N, device=dev) + 0.5
+    bias = params[1][1].detach().float().contiguous()
+    qo = torch.empty(N, 224, 224, 64, dtype=torch.int8, device=dev)
+    amax = torch.empty(N, dtype=torch.int32, device=dev)
+    chain_mode = kernels.CONV_Q_NHWC | kernels.CONV_NEXT_AMAX | kernels.CONV_NEXT_RELU | kernels.CONV_NEXT_POOL
+    ms = event_ms(lambda: kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, chain_mode | lay.mode_flag,
+                                          shift=lay.shift, scale=lay.scale, sx=sx, bias=bias, out=qo, acc_max=amax), 5)
     yo = torch.empty(N, 64, 224, 224, device=dev, memory_format=torch.channels_last)
-    ms = event_ms(lambda: kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, kernels.CONV_DEQUANT, shift=lay.shift,
-                                          scale=lay.scale, sx=sx, bias=params[1][1], relu=kernels.RELU_AFTER_BIAS,
-                                          out=yo), 5)
-    del xp, yo
+    ms_f32 = event_ms(lambda: kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, kernels.CONV_DEQUANT | lay.mode_flag,
+                                              shift=lay.shift, scale=lay.scale, sx=sx, bias=params[1][1],
+                                              relu=kernels.RELU_AFTER_BIAS, out=yo), 5)
+    del xp, yo, qo
     conv_ops = 2 * N * 224 * 224 * 64 * 64 * 9
     rec = {"metric": CONV_METRIC, "value": round(2 * vgg_macs(N_all) * args.steps / total_s / 1e12, 2), "unit": "TOPS",
            "ms_per_step": round(total_s * 1e3 / args.steps, 3), "scaling": "strong", "dtype": "int8",
@@ -634,9 +643,12 @@ def conv_record(args, rank, world, dev, flush):
                       else "int8 codes (pool on the codes)", "global_batch": N_all,
                       "parallelism": f"dp{world} (images)", "l2": "activations exceed L2"},
            "gpu_launches": per_step * args.steps,
-           "roofline": roof("tensor", "umma_gemm_kernel LOAD_CONV_RB (conv 64->64 224x224, dequantise epilogue, bias "
-                            "+ ReLU)", conv_ops / ms / 1e9, int8_peak, "TOPS", ms, peak_source=INT8_PEAK_NOTE,
-                            traffic=None),
+           "roofline": roof("tensor", "umma_gemm_kernel conv (conv 64->64 224x224 as chained: int8 codes out, next "
+                            "layer's pooled per-image maxima in the epilogue)", conv_ops / ms / 1e9, int8_peak, "TOPS",
+                            ms, peak_source=INT8_PEAK_NOTE, traffic=None),
+           "roofline_dequant_f32": roof("tensor", "umma_gemm_kernel conv (conv 64->64 224x224, f32 out, dequantise "
+                                        "epilogue, bias + ReLU)", conv_ops / ms_f32 / 1e9, int8_peak, "TOPS", ms_f32,
+                                        peak_source=INT8_PEAK_NOTE, traffic=None),
            "step_frac": round(2 * vgg_macs(N_all) * args.steps / total_s / 1e12 / world / int8_peak, 4),
            "clocks": clocks}
     rec["single_conv_256x1536x64"] = single_conv_roofline(dev, int8_peak, flush)

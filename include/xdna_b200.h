@@ -63,6 +63,17 @@ extern "C" {
  * R:torch_xdna/backend.py:130-174) to the ResNet-style layers it lists as missing
  * (R:results/conv3x3_cascade.md:222-223): same quantise, calibration and requantise. */
 #define XDNA_CONV_STRIDE2 32
+/* Or'ed into XDNA_CONV_Q_NHWC: the next layer's per-image maxima, so that its quantise from these codes
+ * (xdna_conv_quant_codes_given_amax) needs no pass of its own over them. acc_max then holds N words, cleared by
+ * this call, that receive per image the f32 bit pattern of max |y| over the output pixels, where
+ * y = float(q) * (scale[c] * sx[n]) (+ bias[c], f32) is computed with the f32 operations of
+ * xdna_conv_quant_codes; with XDNA_CONV_NEXT_RELU y is max(y, 0) first; with XDNA_CONV_NEXT_POOL only the
+ * rows and columns a 2x2 / stride-2 pool keeps (an odd last one is left out) count, which is the pooled
+ * image's max when y >= 0 (so it needs XDNA_CONV_NEXT_RELU, or relu = 1 and no bias). Needs scale, sx
+ * (this conv's input scales) and bias (f32 or NULL). */
+#define XDNA_CONV_NEXT_AMAX 64
+#define XDNA_CONV_NEXT_RELU 128
+#define XDNA_CONV_NEXT_POOL 256
 /* `relu` of xdna_conv3x3_i8: 0 none; 1 fused into the requantise ([0,255] uint8, the reference's ReLU of
  * a bias-free conv); XDNA_RELU_AFTER_BIAS (DEQUANT only) applied to the dequantised output after the
  * bias, the requantise saturating to int8 — the same values as torch.relu on the DEQUANT output. */
@@ -178,6 +189,13 @@ int xdna_conv_quant_given_amax(const void* x, int x_dtype, int x_channels_last, 
 int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
                           const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,
                           int8_t* xp, int64_t Cp, float* sx_out, uint32_t* amax_scratch, void* stream);
+
+/* xdna_conv_quant_codes with the per-image maxima already known (amax [N], the bit patterns the producing
+ * conv wrote with XDNA_CONV_NEXT_AMAX, XDNA_CONV_NEXT_POOL iff pool): one pass over the codes instead of two. */
+int xdna_conv_quant_codes_given_amax(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
+                                     const float* scale, const float* sx_in, const float* bias, int relu_after,
+                                     int pool, int8_t* xp, int64_t Cp, float* sx_out, const uint32_t* amax,
+                                     void* stream);
 
 /* xdna_conv_quant_nhwc without caller-provided scratch: the same inputs, outputs and results, but the
  * per-image max lives in a 16 KB array inside the library, so the call allocates nothing and takes no

@@ -39,7 +39,11 @@ CASES = [
 
 @pytest.mark.parametrize("case", range(len(CASES)))
 @pytest.mark.parametrize("verify", ["off", "always"])
-def test_chain_equals_unchained(cuda, case, verify):
+@pytest.mark.parametrize("hint", [True, False])
+def test_chain_equals_unchained(cuda, case, verify, hint):
+    """hint: each conv is told whether the next one pools its codes, so its epilogue writes the next
+    layer's per-image maxima (over the pool's region); without, a pooling consumer finds maxima of the
+    unpooled image and makes its own two passes."""
     from torch_xdna.conv import IN_CODES, IN_CODES_POOL, IN_FLOAT
 
     shapes, biased, pools, H, W = CASES[case]
@@ -59,13 +63,67 @@ def test_chain_equals_unchained(cuda, case, verify):
     for i, (w, b) in enumerate(layers):
         last = i == len(layers) - 1
         mode = IN_FLOAT if i == 0 else (IN_CODES_POOL if pools[i] else IN_CODES)
-        q, meta = torch.ops.xdna.conv3x3_chain(q, meta, w, b, b is None, cid, b is not None, mode, ra, not last)
+        out_pool = hint and not last and pools[i + 1]
+        q, meta = torch.ops.xdna.conv3x3_chain(q, meta, w, b, b is None, cid, b is not None, mode, ra, not last,
+                                               out_pool)
         if not last:
             assert q.dtype == (torch.uint8 if b is None else torch.int8) and q.shape[-1] == w.shape[0]
         ra = b is not None
     got = q
     assert got.shape == want.shape and got.dtype == want.dtype
     assert torch.equal(got, want), f"{int((got != want).sum())} of {want.numel()} values differ"
+
+
+KINDS = ["relu_after_bias", "fused_relu", "signed"]
+
+
+@pytest.mark.parametrize("shape", [(3, 40, 64, 15, 17), (2, 64, 128, 30, 22), (9, 16, 32, 3, 4)])
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("pool", [False, True])
+def test_next_layer_maxima_from_the_producer(cuda, shape, kind, pool):
+    """A conv with XDNA_CONV_NEXT_AMAX writes, per image, the max |y| of the float values its codes stand for
+    (y = float(q) * (scale * sx) + bias, then the ReLU after the bias; over the 2x2 pool's region when the
+    next conv pools): the same bits the two-pass quantise of those codes finds, so the one-pass quantise
+    from them gives the same input bytes and factors."""
+    from torch_xdna import conv as xconv
+    from torch_xdna import kernels
+
+    if pool and kind == "signed":
+        pytest.skip("pooled maxima need non-negative values")
+    n, ci, co, h, w = shape
+    g = torch.Generator(device=cuda).manual_seed(sum(shape) + KINDS.index(kind) + 10 * pool)
+    wt = torch.randn(co, ci, 3, 3, device=cuda, generator=g) * (2.0 / (ci * 9)) ** 0.5
+    fused = kind == "fused_relu"
+    bias = None if fused else torch.randn(co, device=cuda, generator=g) * 0.05
+    layer = xconv.ConvLayer(wt, h, w, fused)
+    xp, sx = layer.quantise(torch.randn(n, ci, h, w, device=cuda, generator=g), n)
+    layer.calibrate(xp)
+    relu_after = kind == "relu_after_bias"
+    q = torch.empty((n, h, w, co), dtype=torch.uint8 if fused else torch.int8, device=cuda)
+    meta = xconv.codes_meta(sx, layer.scale, bias, co, amax=True, pool=pool)
+    mode = (kernels.CONV_Q_NHWC | kernels.CONV_NEXT_AMAX | (kernels.CONV_NEXT_RELU if relu_after else 0)
+            | (kernels.CONV_NEXT_POOL if pool else 0))
+    amax = meta[n + 2 * co:2 * n + 2 * co].view(torch.int32)
+    kernels.conv3x3(xp, layer.wp, n, ci, co, h, w, mode, shift=layer.shift, relu=fused, scale=meta[n:n + co],
+                    sx=sx, bias=meta[n + co:n + 2 * co] if bias is not None else None, out=q, acc_max=amax)
+    # the codes are those of the plain requantise
+    q0 = torch.empty_like(q)
+    kernels.conv3x3(xp, layer.wp, n, ci, co, h, w, kernels.CONV_Q_NHWC, shift=layer.shift, relu=fused, out=q0)
+    assert torch.equal(q, q0)
+    # the maxima: max |y| over each image (pooled) on the CPU with the epilogue's f32 operations
+    y = xconv.codes_to_float(q, meta, relu_after, pool)
+    want = y.abs().amax(dim=(1, 2, 3))
+    assert torch.equal(amax.cpu().view(torch.float32), want)
+    # the next conv's input from them equals the two-pass one
+    hn, wn = (h // 2, w // 2) if pool else (h, w)
+    cp = xconv.channels_padded(co)
+    xa, xb = (torch.full((n, hn + 2, wn + 2, cp), 77, dtype=torch.int8, device=cuda) for _ in range(2))
+    sa, sb = torch.empty(n, device=cuda), torch.empty(n, device=cuda)
+    scratch = torch.empty(n, dtype=torch.int32, device=cuda)
+    args = (q, meta[n:n + co], meta[:n], meta[n + co:n + 2 * co], relu_after, pool)
+    kernels.conv_quant_codes(*args, xa, sa, scratch)
+    kernels.conv_quant_codes_given_amax(*args, xb, sb, amax)
+    assert torch.equal(sa, sb) and torch.equal(xa, xb)
 
 
 def test_compiled_vgg_block_chained_equals_unchained(cuda):

@@ -191,7 +191,15 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   XDNA_CHECK_ARG(Cp >= Ci && Cp % 16 == 0, "conv3x3: Cp must be >= Ci and a multiple of 16");
   const bool single_tap = (mode & XDNA_CONV_SINGLE_TAP) != 0;
   const bool stride2 = (mode & XDNA_CONV_STRIDE2) != 0;
-  mode &= ~(XDNA_CONV_SINGLE_TAP | XDNA_CONV_STRIDE2);
+  const bool next_amax = (mode & XDNA_CONV_NEXT_AMAX) != 0;
+  const bool next_relu = (mode & XDNA_CONV_NEXT_RELU) != 0;
+  const bool next_pool = (mode & XDNA_CONV_NEXT_POOL) != 0;
+  mode &= ~(XDNA_CONV_SINGLE_TAP | XDNA_CONV_STRIDE2 | XDNA_CONV_NEXT_AMAX | XDNA_CONV_NEXT_RELU | XDNA_CONV_NEXT_POOL);
+  XDNA_CHECK_ARG(!next_amax || (mode == XDNA_CONV_Q_NHWC && scale != nullptr && sx != nullptr && acc_max != nullptr),
+                 "conv3x3: XDNA_CONV_NEXT_AMAX needs XDNA_CONV_Q_NHWC, scale, sx and acc_max (N words)");
+  XDNA_CHECK_ARG(!next_amax || !next_pool || next_relu || (relu == 1 && bias == nullptr),
+                 "conv3x3: pooled maxima need non-negative values (XDNA_CONV_NEXT_RELU, or a fused ReLU and no bias)");
+  XDNA_CHECK_ARG(!next_amax || bias == nullptr || bias_dtype == XDNA_F32, "conv3x3: next maxima need an f32 bias");
   XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE ||
                      mode == XDNA_CONV_Q_NHWC,
                  "conv3x3: unknown mode %d", mode);
@@ -271,6 +279,13 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   a.relu = relu == 1 ? 1 : 0;
   a.post_relu = relu == XDNA_RELU_AFTER_BIAS ? 1 : 0;
   a.acc_max = acc_max;
+  if (next_amax) {
+    XDNA_CUDA(cudaMemsetAsync(acc_max, 0, N * sizeof(uint32_t), s));
+    a.next_amax = reinterpret_cast<uint32_t*>(acc_max);
+    a.next_relu = next_relu ? 1 : 0;
+    a.next_h = static_cast<int>(next_pool ? H & ~1ll : H);
+    a.next_w = static_cast<int>(next_pool ? W & ~1ll : W);
+  }
   a.err = device_error_word();
 
   CUtensorMap ta, tb;

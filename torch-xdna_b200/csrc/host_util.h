@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <climits>
 #include <cstdio>
 #include <string>
 

@@ -600,11 +600,12 @@ __global__ void __launch_bounds__(256) codes_to_bordered_kernel(const uint32_t* 
 template <bool POOL, bool USGN>
 static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const float* scale, const float* sx_in,
                          const float* bias, int relu_after, int Cp, uint32_t* amax, int8_t* xp, float* sx_out,
-                         cudaStream_t s) {
+                         cudaStream_t s, bool amax_given = false) {
   const int Ho = POOL ? H / 2 : H;
   const int64_t per = static_cast<int64_t>(Ho) * (POOL ? W / 2 : W) * C4;
   const int chunks = static_cast<int>(std::min<int64_t>((per + 256 * 8 - 1) / (256 * 8), 1024));
-  codes_amax_kernel<POOL, USGN><<<dim3(chunks, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, amax);
+  if (!amax_given)
+    codes_amax_kernel<POOL, USGN><<<dim3(chunks, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, amax);
   codes_to_bordered_kernel<POOL, USGN>
       <<<dim3(Ho + 2, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, Cp, amax, xp, sx_out);
 }
@@ -814,6 +815,40 @@ int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, i
       launch_codes<false, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, amax_scratch, xp, sx_out, s);
   }
   return check_launch("conv quantise (int8 codes)");
+}
+
+int xdna_conv_quant_codes_given_amax(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
+                                     const float* scale, const float* sx_in, const float* bias, int relu_after,
+                                     int pool, int8_t* xp, int64_t Cp, float* sx_out, const uint32_t* amax,
+                                     void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && C >= 4 && C % 4 == 0 && H >= 1 && W >= 1,
+                 "conv_quant_codes_given_amax: bad shape (C must be a positive multiple of 4)");
+  XDNA_CHECK_ARG(!pool || (H >= 2 && W >= 2), "conv_quant_codes_given_amax: a 2x2 pool needs H, W >= 2");
+  XDNA_CHECK_ARG(Cp >= C && Cp % 16 == 0, "conv_quant_codes_given_amax: Cp must be >= C and a multiple of 16");
+  XDNA_CHECK_ARG(N <= 65535 && H + 2 <= 65535 && N * H * W * C < (1ll << 40), "conv_quant_codes_given_amax: too large");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(q && scale && sx_in && xp && sx_out && amax, "conv_quant_codes_given_amax: null pointer");
+  XDNA_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 4 == 0 && aligned16(xp),
+                 "conv_quant_codes_given_amax: q must be 4-byte and xp 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint32_t* qw = static_cast<const uint32_t*>(q);
+  uint32_t* am = const_cast<uint32_t*>(amax);  // only read: the max pass is skipped
+  const int n = static_cast<int>(N), h = static_cast<int>(H), w = static_cast<int>(W), c4 = static_cast<int>(C / 4);
+  const int cp = static_cast<int>(Cp), ra = relu_after ? 1 : 0;
+  if (pool) {
+    if (q_unsigned)
+      launch_codes<true, true>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, am, xp, sx_out, s, true);
+    else
+      launch_codes<true, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, am, xp, sx_out, s, true);
+  } else {
+    if (q_unsigned)
+      launch_codes<false, true>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, am, xp, sx_out, s, true);
+    else
+      launch_codes<false, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, am, xp, sx_out, s, true);
+  }
+  return check_launch("conv quantise (int8 codes, given maxima)");
 }
 
 int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,

@@ -99,6 +99,11 @@ struct GemmArgs {
   int shift, relu;     // relu: ReLU in the requantise (uint8 saturation)
   int post_relu;       // EPI_CONV_DEQ: max(y, 0) after the bias
   int* acc_max;
+  // EPI_CONV_QNHWC with the next layer's maxima (XDNA_CONV_NEXT_AMAX): per image, the bit pattern of the max
+  // |y| of the values the codes stand for, y = float(q) * (sw[c] * sx[n]) (+ bias[c]) (then max(y, 0) with
+  // next_relu), over output rows < next_h and columns < next_w (a 2x2 pool's region); nullptr: not wanted
+  uint32_t* next_amax;
+  int next_relu, next_h, next_w;
   int* err;
   // stack epilogues
   float* resid;        // EPI_RESID: [M, ldr] f32, updated in place
@@ -399,6 +404,50 @@ __device__ __forceinline__ ConvPixel conv_pixel(const GemmArgs& a, int p) {
   return px;
 }
 
+// The next conv's per-image max from this conv's codes (XDNA_CONV_NEXT_AMAX). The value a code stands for,
+// y(q) = fl(fl(q) * fl(scale[c] * sx[n])) (+ bias[c]) (then max(y, 0)) -- the next layer's quantise rebuilds it
+// with exactly these f32 operations -- never decreases as q grows, so per channel only the largest code of the
+// warp's pixels (and the smallest, for values that may be negative) decides max |y|: one warp max per channel,
+// then lane c evaluates y for channel n0 + c alone, and one atomicMax on the bit pattern per image the warp
+// holds. qv: this pixel's requantised codes. The whole warp calls it.
+__device__ __forceinline__ void conv_next_amax(const GemmArgs& a, const ConvPixel& px, int nvalid, const int (&qv)[32],
+                                               float scale_lane, float bias_lane) {
+  const bool in = px.valid && px.yp - 1 < a.next_h && px.xp - 1 < a.next_w;
+  const bool nonneg = a.next_relu || a.relu;  // y >= 0: the largest code gives the largest |y|
+  const int img = in ? px.img : -1;
+  // the warp's pixels may span several images (a tile crossing an image's end): one pass per image
+  const int lo = __reduce_min_sync(kFull, in ? img : INT_MAX);
+  const int hi = __reduce_max_sync(kFull, img);
+  const int lane = lane_id();
+  for (int i = lo; i <= hi; ++i) {  // warp-uniform; no pass when no pixel counts (hi < 0)
+    const bool mine = img == i;
+    int qmax = INT_MIN, qmin = INT_MAX;  // of channel n0 + lane over this warp's pixels of image i
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int mx = __reduce_max_sync(kFull, mine ? qv[j] : INT_MIN);
+      qmax = lane == j ? mx : qmax;
+      if (!nonneg) {  // warp-uniform
+        const int mn = __reduce_min_sync(kFull, mine ? qv[j] : INT_MAX);
+        qmin = lane == j ? mn : qmin;
+      }
+    }
+    uint32_t m = 0;  // max |y| of channel n0 + lane, as bits (non-negative floats order like their bit patterns)
+    if (lane < nvalid && qmax != INT_MIN) {
+      const float t = __fmul_rn(scale_lane, __ldg(a.sx + i));
+      auto abs_y = [&](int q) {
+        float y = __fmul_rn(static_cast<float>(q), t);
+        if (a.bias != nullptr) y = __fadd_rn(y, bias_lane);
+        if (a.next_relu) y = y > 0.f ? y : 0.f;
+        return __float_as_uint(y) & 0x7FFFFFFFu;
+      };
+      m = abs_y(qmax);
+      if (!nonneg) m = max(m, abs_y(qmin));
+    }
+    const uint32_t mi = __reduce_max_sync(kFull, m);
+    if (lane == 0 && mi != 0u) atomicMax(a.next_amax + i, mi);
+  }
+}
+
 // Conv epilogues: one thread, one bordered pixel, channels n0..n0+31 in r[].
 template <int EPI>
 __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& px, int n0, const uint32_t (&r)[32],
@@ -422,6 +471,10 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     best = __reduce_max_sync(kFull, best);
     if (lane_id() == 0 && best > 0) atomicMax(a.acc_max, best);
   } else if constexpr (EPI == EPI_CONV_QNHWC) {
+    int qv[32];  // this pixel's codes
+#pragma unroll
+    for (int j = 0; j < 32; ++j) qv[j] = requant(static_cast<int>(r[j]), a.shift, a.relu);
+    if (a.next_amax != nullptr) conv_next_amax(a, px, nvalid, qv, scale_lane, bias_lane);  // warp-uniform
     if (!valid) return;
     // out[img, yp-1, xp-1, n0 ..]: this pixel's 32 codes are 32 contiguous bytes
     uint8_t* o = static_cast<uint8_t*>(a.out) + ((static_cast<int64_t>(img) * a.H + (yp - 1)) * a.W + (xp - 1)) * a.N + n0;
@@ -431,8 +484,7 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
       for (int k = 0; k < 8; ++k) {
         uint32_t word = 0;
 #pragma unroll
-        for (int b = 0; b < 4; ++b)
-          word |= (static_cast<uint32_t>(requant(static_cast<int>(r[4 * k + b]), a.shift, a.relu)) & 0xFFu) << (8 * b);
+        for (int b = 0; b < 4; ++b) word |= (static_cast<uint32_t>(qv[4 * k + b]) & 0xFFu) << (8 * b);
         w[k] = word;
       }
       reinterpret_cast<uint4*>(o)[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -440,7 +492,7 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (j < nvalid) o[j] = static_cast<uint8_t>(requant(static_cast<int>(r[j]), a.shift, a.relu) & 0xFF);
+        if (j < nvalid) o[j] = static_cast<uint8_t>(qv[j] & 0xFF);
     }
   } else if constexpr (EPI == EPI_CONV_Q) {
     if (!valid) return;
@@ -1059,8 +1111,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n = col0 + c * 32 + lane;
         f.fcol[c] = 0.f;
         f.bcol[c] = 0.f;
-        if constexpr (EPI == EPI_DEQ || EPI == EPI_CONV_DEQ) {
-          if (n < args.N) {
+        if constexpr (EPI == EPI_DEQ || EPI == EPI_CONV_DEQ || EPI == EPI_CONV_QNHWC) {
+          if (n < args.N && (EPI != EPI_CONV_QNHWC || args.next_amax != nullptr)) {
             f.fcol[c] = __ldg(args.sw + n);
             if (has_bias) f.bcol[c] = load_as_float(args.bias, args.bias_dtype, n);
           }

@@ -250,9 +250,10 @@ def _chain_convs(gm):
         else:
             xin, xmeta, in_mode, in_ra = x, None, IN_FLOAT, False
         out_q = n in link
+        out_pool = out_q and link[n][1] is not None
         with gm.graph.inserting_after(n):
             call = gm.graph.call_function(conv3x3_chain_int8, (xin, xmeta, w, b, relu, cid, post_relu, in_mode, in_ra,
-                                                               out_q))
+                                                               out_q, out_pool))
         with gm.graph.inserting_after(call):
             first = gm.graph.call_function(operator.getitem, (call, 0))
         with gm.graph.inserting_after(first):

@@ -87,9 +87,10 @@ def conv_ext_int8(x, weight, bias, stride: int, relu: bool, cfg_id: int, post_re
 
 
 def conv3x3_chain_int8(x, xmeta, weight, bias, relu: bool, cfg_id: int, post_relu: bool, in_mode: int,
-                       in_relu_after: bool, out_q: bool):
+                       in_relu_after: bool, out_q: bool, out_pool: bool = False):
     """One conv of a chain whose activations between convs stay int8 (xdna::conv3x3_chain)."""
-    return torch.ops.xdna.conv3x3_chain(x, xmeta, weight, bias, relu, cfg_id, post_relu, in_mode, in_relu_after, out_q)
+    return torch.ops.xdna.conv3x3_chain(x, xmeta, weight, bias, relu, cfg_id, post_relu, in_mode, in_relu_after,
+                                        out_q, out_pool)
 
 
 def channels_padded(c):
@@ -344,10 +345,23 @@ def conv_int8(cfg, x, weight, bias, stride, relu, post_relu=False):
 IN_FLOAT, IN_CODES, IN_CODES_POOL = 0, 1, 2
 
 
-def codes_meta(sx, scale, bias, co):
-    """The float data that turns a conv's codes back into its output: sx [N], scale [Co], bias [Co]."""
+def codes_meta(sx, scale, bias, co, amax=False, pool=False):
+    """The float data that turns a conv's codes back into its output: sx [N], scale [Co], bias [Co]; with
+    amax, N more words for the next layer's per-image maxima (bit patterns, written by the producing conv's
+    epilogue), and one word more when they cover a 2x2 pool's region -- the consumer reads which from the
+    length alone, so it needs no device read."""
     b = bias.float() if bias is not None else torch.zeros((co,), dtype=torch.float32, device=scale.device)
-    return torch.cat([sx, scale, b])
+    parts = [sx, scale, b]
+    if amax:
+        parts.append(torch.empty((sx.numel() + (1 if pool else 0),), dtype=torch.float32, device=sx.device))
+    return torch.cat(parts)
+
+
+def next_amax_ok(relu, bias, post_relu, pool):
+    """Whether a chain producer can compute the next layer's per-image maxima in its epilogue: always without
+    a pool; with a 2x2 max-pool only for non-negative values (the pooled image's max is then the max over the
+    pool's region), i.e. a ReLU after the bias, or a ReLU fused into a bias-free conv's requantise."""
+    return (not pool) or bool(post_relu) or (bool(relu) and bias is None)
 
 
 def codes_to_float(q, meta, relu_after, pool):
@@ -364,7 +378,7 @@ def codes_to_float(q, meta, relu_after, pool):
     return torch.nn.functional.max_pool2d(y, 2) if pool else y
 
 
-def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu_after, out_q):
+def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu_after, out_q, out_pool=False):
     """A conv of a chain (R:torch_xdna/conv.py:43-51 applied layer after layer, with the graph's ReLU and
     2x2 max-pool between): the activations between convs stay int8 codes [N, H, W, C] with their float
     factors, and the next conv's quantise rebuilds the float values the reference would have (same f32
@@ -372,7 +386,9 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
     x: the float input [N, Ci, H, W] (IN_FLOAT), or the previous conv's codes [N, H, W, Ci] with
     xmeta = codes_meta(...) (IN_CODES; IN_CODES_POOL: 2x2 max-pooled first). in_relu_after: the previous
     conv's ReLU applies after its bias. Returns (codes [N, H, W, Co], their meta) when out_q, else (the
-    float output [N, Co, H, W] channels-last, an empty tensor)."""
+    float output [N, Co, H, W] channels-last, an empty tensor). out_pool: the next conv pools these codes
+    first; with out_q the epilogue then also writes the next layer's per-image maxima (over the pool's
+    region), so the next quantise makes one pass over the codes instead of two."""
     assert not (relu and post_relu), "relu fuses into the requantise, post_relu after the bias: one of them"
     kernels._cuda(x, xmeta, weight, bias)
     if in_mode == IN_FLOAT:
@@ -393,8 +409,14 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
             float_in = lambda: xc.float().cpu()  # noqa: E731
         else:
             xq = x.contiguous()
-            kernels.conv_quant_codes(xq, xmeta[n:n + ci], xmeta[:n], xmeta[n + ci:n + 2 * ci], in_relu_after,
-                                     in_mode == IN_CODES_POOL, xp, sx, scratch)
+            in_pool = in_mode == IN_CODES_POOL
+            if xmeta.numel() == 2 * n + 2 * ci + (1 if in_pool else 0):   # maxima from the producing conv
+                kernels.conv_quant_codes_given_amax(xq, xmeta[n:n + ci], xmeta[:n], xmeta[n + ci:n + 2 * ci],
+                                                    in_relu_after, in_pool, xp, sx,
+                                                    xmeta[n + 2 * ci:2 * n + 2 * ci].view(torch.int32))
+            else:
+                kernels.conv_quant_codes(xq, xmeta[n:n + ci], xmeta[:n], xmeta[n + ci:n + 2 * ci], in_relu_after,
+                                         in_pool, xp, sx, scratch)
             float_in = lambda: codes_to_float(xq, xmeta, in_relu_after, in_mode == IN_CODES_POOL)  # noqa: E731
         stats.launches += 2
         if layer.shift is None:
@@ -408,10 +430,19 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
         _verify(cfg, layer, xp, xq_cpu)
         if out_q:
             q = torch.empty((n, h, w, co), dtype=torch.uint8 if relu else torch.int8, device=x.device)
-            kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, kernels.CONV_Q_NHWC | layer.mode_flag,
-                            shift=layer.shift, relu=relu, out=q)
+            if next_amax_ok(relu, bias, post_relu, out_pool):
+                meta = codes_meta(sx, layer.scale, bias, co, amax=True, pool=out_pool)
+                mode = (kernels.CONV_Q_NHWC | layer.mode_flag | kernels.CONV_NEXT_AMAX
+                        | (kernels.CONV_NEXT_RELU if post_relu else 0) | (kernels.CONV_NEXT_POOL if out_pool else 0))
+                kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, mode, shift=layer.shift, relu=relu,
+                                scale=meta[n:n + co], sx=sx, bias=meta[n + co:n + 2 * co] if bias is not None else None,
+                                out=q, acc_max=meta[n + 2 * co:2 * n + 2 * co].view(torch.int32))
+                out = (q, meta)
+            else:
+                kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, kernels.CONV_Q_NHWC | layer.mode_flag,
+                                shift=layer.shift, relu=relu, out=q)
+                out = (q, codes_meta(sx, layer.scale, bias, co))
             stats.launches += 1
-            out = (q, codes_meta(sx, layer.scale, bias, co))
         else:
             dtype = x.dtype if in_mode == IN_FLOAT else torch.float32
             out = (layer.dequant(xp, n, sx, bias, dtype, post_relu), sx.new_empty((0,)))

@@ -27,6 +27,8 @@ DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16, tor
 CONV_Q, CONV_DEQUANT, CONV_CALIBRATE, CONV_Q_NHWC = 0, 1, 2, 3
 CONV_SINGLE_TAP = 16  # or'ed into a conv mode: one tap at offset 0 (a 1x1 conv, or taps packed into channels)
 CONV_STRIDE2 = 32     # or'ed into a conv mode: stride 2, the input split into phase planes (conv_quant_phases)
+# or'ed into CONV_Q_NHWC: the next layer's per-image maxima into acc_max (with its ReLU / 2x2 pool region)
+CONV_NEXT_AMAX, CONV_NEXT_RELU, CONV_NEXT_POOL = 64, 128, 256
 # status codes
 ERR_TIMEOUT = -4
 
@@ -63,6 +65,7 @@ def _load():
         "xdna_conv_quant_nhwc": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_channels_last": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
+        "xdna_conv_quant_codes_given_amax": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
         "xdna_conv_quant_taps": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_phases": ([P, I, I, I64, I64, I64, I64, I, P, I64, P, P, P], I),
         "xdna_conv_image_amax": ([P, I, I64, I64, P, P], I),
@@ -281,6 +284,17 @@ def conv_quant_codes(q, scale, sx_in, bias, relu_after, pool, xp, sx, scratch):
     _check("xdna_conv_quant_codes", L.xdna_conv_quant_codes(
         _p(q), int(q.dtype == torch.uint8), N, C, H, W, _p(scale), _p(sx_in), _p(bias), int(relu_after), int(pool),
         _p(xp), xp.shape[-1], _p(sx), _p(scratch), _stream()))
+
+
+def conv_quant_codes_given_amax(q, scale, sx_in, bias, relu_after, pool, xp, sx, amax):
+    """conv_quant_codes with each image's max already known (amax [N] int32 bit patterns written by the
+    producing conv with CONV_NEXT_AMAX): one pass over the codes."""
+    L = require()
+    _cuda(q, scale, sx_in, bias, xp, sx, amax)
+    N, H, W, C = q.shape
+    _check("xdna_conv_quant_codes_given_amax", L.xdna_conv_quant_codes_given_amax(
+        _p(q), int(q.dtype == torch.uint8), N, C, H, W, _p(scale), _p(sx_in), _p(bias), int(relu_after), int(pool),
+        _p(xp), xp.shape[-1], _p(sx), _p(amax), _stream()))
 
 
 def conv_pack_input(xq, xp):

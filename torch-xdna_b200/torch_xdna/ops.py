@@ -113,15 +113,15 @@ def _(x, weight, bias, stride, relu, cfg_id, post_relu=False):
 @torch.library.custom_op("xdna::conv3x3_chain", mutates_args=())
 def conv3x3_chain(x: torch.Tensor, xmeta: Optional[torch.Tensor], weight: torch.Tensor, bias: Optional[torch.Tensor],
                   relu: bool, cfg_id: int, post_relu: bool, in_mode: int, in_relu_after: bool,
-                  out_q: bool) -> tuple[torch.Tensor, torch.Tensor]:
+                  out_q: bool, out_pool: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     """One conv of a chain whose activations between convs stay int8 codes (conv.conv3x3_chain): the
     same values as conv3x3_fused layer after layer with the graph's ReLU and 2x2 max-pool between."""
     return conv.conv3x3_chain(_configs[cfg_id], x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu_after,
-                              out_q)
+                              out_q, out_pool)
 
 
 @conv3x3_chain.register_fake
-def _(x, xmeta, weight, bias, relu, cfg_id, post_relu, in_mode, in_relu_after, out_q):
+def _(x, xmeta, weight, bias, relu, cfg_id, post_relu, in_mode, in_relu_after, out_q, out_pool=False):
     n, co = x.shape[0], weight.shape[0]
     if in_mode == conv.IN_FLOAT:
         h, w = x.shape[2], x.shape[3]
@@ -129,7 +129,8 @@ def _(x, xmeta, weight, bias, relu, cfg_id, post_relu, in_mode, in_relu_after, o
         h, w = (x.shape[1] // 2, x.shape[2] // 2) if in_mode == conv.IN_CODES_POOL else (x.shape[1], x.shape[2])
     if out_q:
         q = x.new_empty((n, h, w, co), dtype=torch.uint8 if relu else torch.int8)
-        return q, x.new_empty((n + 2 * co,), dtype=torch.float32)
+        extra = n + (1 if out_pool else 0) if conv.next_amax_ok(relu, bias, post_relu, out_pool) else 0
+        return q, x.new_empty((n + 2 * co + extra,), dtype=torch.float32)
     dtype = x.dtype if in_mode == conv.IN_FLOAT else torch.float32
     y = torch.empty((n, co, h, w), dtype=dtype, device=x.device, memory_format=torch.channels_last)
     return y, x.new_empty((0,), dtype=torch.float32)
