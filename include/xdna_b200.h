@@ -74,6 +74,12 @@ extern "C" {
 #define XDNA_CONV_NEXT_AMAX 64
 #define XDNA_CONV_NEXT_RELU 128
 #define XDNA_CONV_NEXT_POOL 256
+/* Or'ed into any conv mode: the bias inside the int32 sums, before the requantise (an option the reference
+ * names as future work; its own route adds the bias to the dequantised floats, R:results/conv3x3_cascade.md:224).
+ * `bias` is then int32 [N, Co] (bias_dtype XDNA_I32, one row per image: the units of the sums depend on the
+ * image's sx), from xdna_conv_bias_int32; the sums become acc + bias[n][co] in every mode (the calibration's
+ * max included), and DEQUANT adds no float bias. |acc| must stay below 2^31 - 3 * 2^29 (K * 127^2 < 5.3e8). */
+#define XDNA_CONV_BIAS_INT32 512
 /* `relu` of xdna_conv3x3_i8: 0 none; 1 fused into the requantise ([0,255] uint8, the reference's ReLU of
  * a bias-free conv); XDNA_RELU_AFTER_BIAS (DEQUANT only) applied to the dequantised output after the
  * bias, the requantise saturating to int8 — the same values as torch.relu on the DEQUANT output. */
@@ -192,6 +198,12 @@ int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, i
 
 /* xdna_conv_quant_codes with the per-image maxima already known (amax [N], the bit patterns the producing
  * conv wrote with XDNA_CONV_NEXT_AMAX, XDNA_CONV_NEXT_POOL iff pool): one pass over the codes instead of two. */
+/* The int32 bias of XDNA_CONV_BIAS_INT32: out[n][co] = rint(bias[co] / (sw[co] * sx[n])) in f32 (the product
+ * and the quotient correctly rounded, rint to nearest even), clamped to [-2^29, 2^29], NaN -> 0. bias: Co
+ * values of bias_dtype (f32 / bf16 / f16); sw: the layer's weight scales [Co]; sx: the images' scales [N]. */
+int xdna_conv_bias_int32(const void* bias, int bias_dtype, const float* sw, const float* sx, int64_t N, int64_t Co,
+                         int32_t* out, void* stream);
+
 int xdna_conv_quant_codes_given_amax(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
                                      const float* scale, const float* sx_in, const float* bias, int relu_after,
                                      int pool, int8_t* xp, int64_t Cp, float* sx_out, const uint32_t* amax,

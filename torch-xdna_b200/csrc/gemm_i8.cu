@@ -194,7 +194,13 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   const bool next_amax = (mode & XDNA_CONV_NEXT_AMAX) != 0;
   const bool next_relu = (mode & XDNA_CONV_NEXT_RELU) != 0;
   const bool next_pool = (mode & XDNA_CONV_NEXT_POOL) != 0;
-  mode &= ~(XDNA_CONV_SINGLE_TAP | XDNA_CONV_STRIDE2 | XDNA_CONV_NEXT_AMAX | XDNA_CONV_NEXT_RELU | XDNA_CONV_NEXT_POOL);
+  const bool bias_i32 = (mode & XDNA_CONV_BIAS_INT32) != 0;
+  mode &= ~(XDNA_CONV_SINGLE_TAP | XDNA_CONV_STRIDE2 | XDNA_CONV_NEXT_AMAX | XDNA_CONV_NEXT_RELU | XDNA_CONV_NEXT_POOL |
+            XDNA_CONV_BIAS_INT32);
+  XDNA_CHECK_ARG(!bias_i32 || (bias != nullptr && bias_dtype == XDNA_I32),
+                 "conv3x3: XDNA_CONV_BIAS_INT32 needs an int32 bias [N, Co]");
+  XDNA_CHECK_ARG(bias_i32 || bias == nullptr || is_float_dtype(bias_dtype), "conv3x3: a float bias (or XDNA_CONV_BIAS_INT32)");
+  if (bias_i32) XDNA_CHECK_ARG(aligned16(bias), "conv3x3: int32 bias not 16-byte aligned");
   XDNA_CHECK_ARG(!next_amax || (mode == XDNA_CONV_Q_NHWC && scale != nullptr && sx != nullptr && acc_max != nullptr),
                  "conv3x3: XDNA_CONV_NEXT_AMAX needs XDNA_CONV_Q_NHWC, scale, sx and acc_max (N words)");
   XDNA_CHECK_ARG(!next_amax || !next_pool || next_relu || (relu == 1 && bias == nullptr),
@@ -273,8 +279,9 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
             : mode == XDNA_CONV_Q_NHWC ? (aligned16(out) && Co % 16 == 0) : 0;
   a.sx = sx;
   a.sw = scale;
-  a.bias = bias;
-  a.bias_dtype = bias_dtype;
+  a.bias = bias_i32 ? nullptr : bias;
+  a.bias_dtype = bias_i32 ? XDNA_F32 : bias_dtype;
+  a.bias_i32 = bias_i32 ? static_cast<const int32_t*>(bias) : nullptr;
   a.shift = shift;
   a.relu = relu == 1 ? 1 : 0;
   a.post_relu = relu == XDNA_RELU_AFTER_BIAS ? 1 : 0;

@@ -635,6 +635,21 @@ static void launch_phases(const void* x, bool cl, bool vec, int N, int C, int H,
     to_phases_kernel<T, true, false><<<grid, 256, 0, s>>>(xt, N, C, H, W, Ho, Wo, Cp, amax, xp, sx);
 }
 
+// out[n][co] = rint(bias[co] / (sw[co] * sx[n])), clamped to [-2^29, 2^29], NaN -> 0 (XDNA_CONV_BIAS_INT32).
+template <typename T>
+__global__ void __launch_bounds__(256) bias_int32_kernel(const T* __restrict__ bias, const float* __restrict__ sw,
+                                                         const float* __restrict__ sx, int N, int Co,
+                                                         int32_t* __restrict__ out) {
+  const int64_t total = static_cast<int64_t>(N) * Co;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(i / Co), c = static_cast<int>(i - static_cast<int64_t>(n) * Co);
+    const float v = rintf(__fdiv_rn(to_f32(bias[c]), __fmul_rn(sw[c], sx[n])));
+    const float lim = 536870912.f;  // 2^29
+    out[i] = v != v ? 0 : static_cast<int32_t>(fminf(fmaxf(v, -lim), lim));
+  }
+}
+
 }  // namespace xdna
 
 using namespace xdna;
@@ -849,6 +864,32 @@ int xdna_conv_quant_codes_given_amax(const void* q, int q_unsigned, int64_t N, i
       launch_codes<false, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, cp, am, xp, sx_out, s, true);
   }
   return check_launch("conv quantise (int8 codes, given maxima)");
+}
+
+int xdna_conv_bias_int32(const void* bias, int bias_dtype, const float* sw, const float* sx, int64_t N, int64_t Co,
+                         int32_t* out, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && Co >= 1 && N * Co < (1ll << 31), "conv_bias_int32: bad shape");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(bias && sw && sx && out, "conv_bias_int32: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int n = static_cast<int>(N), co = static_cast<int>(Co);
+  const int blocks = static_cast<int>(std::min<int64_t>((N * Co + 255) / 256, 1024));
+  switch (bias_dtype) {
+    case XDNA_F32:
+      bias_int32_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(bias), sw, sx, n, co, out);
+      break;
+    case XDNA_BF16:
+      bias_int32_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(bias), sw, sx, n, co, out);
+      break;
+    case XDNA_F16:
+      bias_int32_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(bias), sw, sx, n, co, out);
+      break;
+    default:
+      return fail(XDNA_ERR_INVALID, "conv_bias_int32: bias_dtype %d is not f32/bf16/f16", bias_dtype);
+  }
+  return check_launch("conv bias to int32");
 }
 
 int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,

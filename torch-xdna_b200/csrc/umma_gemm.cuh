@@ -104,6 +104,7 @@ struct GemmArgs {
   // next_relu), over output rows < next_h and columns < next_w (a 2x2 pool's region); nullptr: not wanted
   uint32_t* next_amax;
   int next_relu, next_h, next_w;
+  const int32_t* bias_i32;  // XDNA_CONV_BIAS_INT32: [N images, Co], added to the sums before the requantise
   int* err;
   // stack epilogues
   float* resid;        // EPI_RESID: [M, ldr] f32, updated in place
@@ -445,6 +446,27 @@ __device__ __forceinline__ void conv_next_amax(const GemmArgs& a, const ConvPixe
     }
     const uint32_t mi = __reduce_max_sync(kFull, m);
     if (lane == 0 && mi != 0u) atomicMax(a.next_amax + i, mi);
+  }
+}
+
+// XDNA_CONV_BIAS_INT32: the sums of this lane's pixel, channels n0..n0+31, plus the image's int32 bias row.
+__device__ __forceinline__ void add_bias_i32(const GemmArgs& a, const ConvPixel& px, int n0, uint32_t (&r)[32]) {
+  if (!px.valid) return;
+  const int32_t* b = a.bias_i32 + static_cast<int64_t>(px.img) * a.N + n0;
+  if (n0 + 32 <= a.N && (a.N & 3) == 0) {  // 16-byte aligned rows
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const int4 v = __ldg(reinterpret_cast<const int4*>(b + j));
+      r[j] += static_cast<uint32_t>(v.x);
+      r[j + 1] += static_cast<uint32_t>(v.y);
+      r[j + 2] += static_cast<uint32_t>(v.z);
+      r[j + 3] += static_cast<uint32_t>(v.w);
+    }
+  } else {
+    const int nvalid = min(32, a.N - n0);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nvalid) r[j] += static_cast<uint32_t>(__ldg(b + j));
   }
 }
 
@@ -1189,6 +1211,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n0 = col0 + c * 32;
         // warp-uniform: this chunk has columns in range (and, for GEMM outputs, rows in range)
         if (n0 < args.N && (kConv || row0 < args.M)) {
+          if constexpr (kConv) {
+            if (args.bias_i32 != nullptr) add_bias_i32(args, px, n0, r[c & 1]);  // warp-uniform
+          }
           const uint32_t(&rc)[32] = r[c & 1];
           if constexpr (EPI == EPI_I32 || EPI == EPI_DEQ) {
             if constexpr (TSTORE) {
