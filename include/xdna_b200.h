@@ -70,7 +70,8 @@ extern "C" {
  * xdna_conv_quant_codes; with XDNA_CONV_NEXT_RELU y is max(y, 0) first; with XDNA_CONV_NEXT_POOL only the
  * rows and columns a 2x2 / stride-2 pool keeps (an odd last one is left out) count, which is the pooled
  * image's max when y >= 0 (so it needs XDNA_CONV_NEXT_RELU, or relu = 1 and no bias). Needs scale, sx
- * (this conv's input scales) and bias (f32 or NULL). */
+ * (this conv's input scales) and bias (f32 or NULL; with XDNA_CONV_BIAS_INT32 the bias is in the codes and y
+ * has no float bias term). */
 #define XDNA_CONV_NEXT_AMAX 64
 #define XDNA_CONV_NEXT_RELU 128
 #define XDNA_CONV_NEXT_POOL 256

@@ -157,20 +157,41 @@ def requant(acc, shift, relu):
     return np.clip(q, 0, 255).astype(np.uint8) if relu else np.clip(q, -128, 127).astype(np.int8)
 
 
-def conv3x3_int8(x, w, bias=None, relu=False, shift=None, x_dtype="float32", stride=1):
+def conv_bias_int32(bias, sw, sx):
+    """The optional bias inside the int32 sums (R:results/conv3x3_cascade.md:224-225 names it as future work;
+    the reference has no code for it, so this restates the definition the B200 build adopts):
+    b[n, co] = rint(bias[co] / (sw[co] * sx[n])) in f32 -- product and quotient correctly rounded, rint to
+    nearest even -- clamped to [-2^29, 2^29], NaN -> 0."""
+    b = np.asarray(bias, F32)
+    t = (np.asarray(sx, F32)[:, None] * np.asarray(sw, F32)[None, :]).astype(F32)
+    with np.errstate(all="ignore"):
+        v = np.rint((b[None, :] / t).astype(F32))
+    lim = F32(2.0 ** 29)
+    v = np.where(np.isnan(v), F32(0), np.clip(v, -lim, lim))
+    return v.astype(np.int32)
+
+
+def conv3x3_int8(x, w, bias=None, relu=False, shift=None, x_dtype="float32", stride=1, bias_int32=False):
     """conv3x3_int8 + xdna::conv3x3 on the CPU route, R:torch_xdna/conv.py:43-51,164-189 (and, for a 1x1 w or
-    stride 2, the same route on that conv's sums, conv_acc). Returns dict(y, q, scale, shift, xq, sx, wq, sw)."""
+    stride 2, the same route on that conv's sums, conv_acc). Returns dict(y, q, scale, shift, xq, sx, wq, sw).
+    bias_int32 (a biased conv): the bias joins the sums as conv_bias_int32 before the calibration and the
+    requantise, relu is then the ReLU after the bias, and y has no float bias term."""
     xq, sx = conv_quant(x)
     wq, sw = conv_weight(w)
     acc = conv_acc(xq, wq, stride)
+    bint = None
+    if bias_int32 and bias is not None:
+        bint = conv_bias_int32(bias, sw, sx)
+        acc = (acc.astype(np.int64) + bint[:, :, None, None]).astype(np.int32)
     if shift is None:
         shift = calibrate_shift(acc[0], relu)
     q = requant(acc, shift, relu)
     scale = (sw * F32(2.0 ** shift)).astype(F32)
     y = q.astype(F32) * (scale[None, :, None, None] * sx[:, None, None, None])
-    if bias is not None:
+    if bias is not None and bint is None:
         y = y + np.asarray(bias, F32)[None, :, None, None]
-    return dict(y=cast(y.astype(F32), x_dtype), q=q, scale=scale, shift=shift, xq=xq, sx=sx, wq=wq, sw=sw, acc=acc)
+    return dict(y=cast(y.astype(F32), x_dtype), q=q, scale=scale, shift=shift, xq=xq, sx=sx, wq=wq, sw=sw, acc=acc,
+                bint=bint)
 
 
 # ---------------------------------------------------------------- Qwen3 stack (fp64)

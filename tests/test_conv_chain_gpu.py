@@ -40,17 +40,18 @@ CASES = [
 @pytest.mark.parametrize("case", range(len(CASES)))
 @pytest.mark.parametrize("verify", ["off", "always"])
 @pytest.mark.parametrize("hint", [True, False])
-def test_chain_equals_unchained(cuda, case, verify, hint):
+@pytest.mark.parametrize("bint", [False, True])
+def test_chain_equals_unchained(cuda, case, verify, hint, bint):
     """hint: each conv is told whether the next one pools its codes, so its epilogue writes the next
     layer's per-image maxima (over the pool's region); without, a pooling consumer finds maxima of the
-    unpooled image and makes its own two passes."""
+    unpooled image and makes its own two passes. bint: Config(conv_bias_int32=True) on both routes."""
     from torch_xdna.conv import IN_CODES, IN_CODES_POOL, IN_FLOAT
 
     shapes, biased, pools, H, W = CASES[case]
     g = torch.Generator(device=cuda).manual_seed(7 + case)
     layers = _weights(cuda, g, shapes, biased)
     x = torch.randn(3, shapes[0][1], H, W, device=cuda, generator=g)
-    cid = _cid(verify=verify)
+    cid = _cid(verify=verify, conv_bias_int32=bint)
     # one by one: a biased conv's ReLU after its bias, a bias-free conv's ReLU in the requantise
     y = x
     for i, (w, b) in enumerate(layers):
@@ -67,7 +68,7 @@ def test_chain_equals_unchained(cuda, case, verify, hint):
         q, meta = torch.ops.xdna.conv3x3_chain(q, meta, w, b, b is None, cid, b is not None, mode, ra, not last,
                                                out_pool)
         if not last:
-            assert q.dtype == (torch.uint8 if b is None else torch.int8) and q.shape[-1] == w.shape[0]
+            assert q.dtype == (torch.uint8 if b is None or bint else torch.int8) and q.shape[-1] == w.shape[0]
         ra = b is not None
     got = q
     assert got.shape == want.shape and got.dtype == want.dtype

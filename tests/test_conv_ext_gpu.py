@@ -128,26 +128,86 @@ class Bottleneck(torch.nn.Module):
         return torch.relu(self.c3(h) + self.down(x))
 
 
-def test_compiled_bottleneck_vs_oracle(cuda):
+@pytest.mark.parametrize("bint", [False, True])
+def test_compiled_bottleneck_vs_oracle(cuda, bint):
+    """bint: Config(conv_bias_int32=True), every conv's bias inside its int32 sums and the sole-user ReLUs
+    in the requantise."""
     import torch_xdna
 
     g = torch.Generator().manual_seed(3)
     net = Bottleneck(256, 128, 512, g).eval()
     x = torch.randn(2, 256, 28, 28, generator=torch.Generator().manual_seed(4))
 
-    def oc(h, c, stride):
-        return orc.conv3x3_int8(h, c.weight.detach().numpy(), c.bias.detach().numpy(), relu=False, stride=stride)["y"]
+    def oc(h, c, stride, relu_next=False):
+        return orc.conv3x3_int8(h, c.weight.detach().numpy(), c.bias.detach().numpy(), relu=bint and relu_next,
+                                stride=stride, bias_int32=bint)["y"]
 
     relu = lambda a: np.maximum(a, np.float32(0))  # noqa: E731
     xn = x.numpy()
-    h = relu(oc(xn, net.c1, 1))
-    h = relu(oc(h, net.c2, 2))
+    h = relu(oc(xn, net.c1, 1, True))
+    h = relu(oc(h, net.c2, 2, True))
     want = relu((oc(h, net.c3, 1) + oc(xn, net.down, 2)).astype(np.float32))
     torch._dynamo.reset()
     torch_xdna.stats.reset()
-    comp = torch.compile(net.to(cuda), backend="xdna", options={"fallback": "eager", "conv_ext": True})
+    comp = torch.compile(net.to(cuda), backend="xdna",
+                         options={"fallback": "eager", "conv_ext": True, "conv_bias_int32": bint})
     y = comp(x.to(cuda))
     assert torch_xdna.stats.as_dict()["calls"]["gpu"] == 4
     assert len(torch_xdna.stats.checks) == 4      # every conv's first launch verified against the CPU integers
     got = y.cpu().numpy()
     assert np.array_equal(got, want), f"{int((got != want).sum())} of {want.size} values differ"
+
+
+def test_conv_bias_int32_kernel_vs_oracle(cuda):
+    """xdna_conv_bias_int32: rint(bias / (sw * sx)) in f32 per image, ties to even, clamped, NaN -> 0; f32 and
+    bf16 biases."""
+    from torch_xdna import kernels
+
+    g = mg.rng(31)
+    co, n = 300, 5
+    bias = (g.standard_normal(co) * 0.3).astype(np.float32)
+    bias[:6] = [1.25, -0.375, 1e12, -np.inf, np.nan, 2.5]
+    sw = (np.abs(g.standard_normal(co)) * 1e-2 + 1e-6).astype(np.float32)
+    sw[:6] = [0.5, 0.25, 1.0, 2.0, 1.0, 1.0]
+    sx = (np.abs(g.standard_normal(n)) * 0.02 + 1e-4).astype(np.float32)
+    sx[0] = 1.0
+    for dtype in ("float32", "bfloat16"):
+        b = orc.cast(bias, dtype)
+        want = orc.conv_bias_int32(b, sw, sx)
+        out = torch.empty((n, co), dtype=torch.int32, device=cuda)
+        bt = torch.from_numpy(b).to(cuda, torch.float32 if dtype == "float32" else torch.bfloat16)
+        kernels.conv_bias_int32(bt, torch.from_numpy(sw).to(cuda), torch.from_numpy(sx).to(cuda), out)
+        got = out.cpu().numpy()
+        assert np.array_equal(got, want), f"{dtype}: {int((got != want).sum())} of {want.size} differ"
+    assert want[0, :6].tolist()[:3] == [2, -2, 2 ** 29] and want[0, 4] == 0
+
+
+BINT_CASES = [  # (k, stride, n, ci, co, h, w)
+    (3, 1, 2, 64, 64, 30, 22), (3, 1, 3, 3, 30, 17, 19), (3, 1, 2, 256, 300, 14, 14), (1, 1, 2, 64, 256, 14, 14),
+    (1, 2, 2, 40, 24, 13, 11), (3, 2, 2, 64, 64, 28, 28),
+]
+
+
+@pytest.mark.parametrize("relu", [True, False])
+@pytest.mark.parametrize("k,stride,n,ci,co,h,w", BINT_CASES)
+def test_bias_int32_bitexact_vs_oracle(cuda, k, stride, n, ci, co, h, w, relu):
+    """Config(conv_bias_int32=True): the bias inside the int32 sums (calibration included), the ReLU after the
+    bias as the requantise's saturation; f32 y bit for bit against the oracle's route, the shift the same."""
+    from torch_xdna import conv as xconv
+
+    x, _, b = mg.conv_inputs(k * 100 + stride * 10 + ci + co + h + relu, n, ci, co, h, w, bias=True, bias_std=0.5)
+    g = mg.rng(ci * 5 + co + k)
+    wt = (g.standard_normal((co, ci, k, k)) * np.sqrt(2.0 / (ci * k * k))).astype(np.float32)
+    want = orc.conv3x3_int8(x, wt, b, relu=relu, stride=stride, bias_int32=True)
+    weight = torch.nn.Parameter(torch.from_numpy(wt).to(cuda))
+    cid = _cid(verify="first", conv_ext=True, conv_bias_int32=True)
+    y = torch.ops.xdna.conv_int8(torch.from_numpy(x).to(cuda), weight, torch.from_numpy(b).to(cuda), stride, False,
+                                 cid, relu)
+    got = y.cpu().numpy()
+    bad = int((got != want["y"]).sum())
+    assert bad == 0, f"{bad} of {got.size} values differ"
+    if k == 3 and stride == 1:
+        layer = xconv._layer(weight, h, w, relu, taps=ci <= 7, bint=True)
+    else:
+        layer = xconv._layer(weight, h, w, relu, stride=stride, bint=True)
+    assert layer.shift == want["shift"] and layer.checked

@@ -141,6 +141,32 @@ def test_conv_acc_is_the_references_conv2d_call(k, stride, h, w):
     assert np.array_equal(orc.conv_acc(xq, wq, stride), want)
 
 
+def test_conv_bias_int32_definition():
+    """The int32 bias of the optional bias-inside-the-sums route: f32 quotient, ties to even, clamp, NaN -> 0;
+    with a zero bias the route gives the reference's values."""
+    sw = np.array([0.5, 0.25, 1.0, 2.0, 1.0, 1.0], np.float32)
+    sx = np.array([1.0, 0.5], np.float32)
+    bias = np.array([1.25, -0.375, 1e12, -1e12, np.nan, 2.5], np.float32)
+    b = orc.conv_bias_int32(bias, sw, sx)
+    assert b.dtype == np.int32 and b.shape == (2, 6)
+    # 1.25 / 0.5 = 2.5 -> 2 (even); -0.375 / 0.25 = -1.5 -> -2; the clamps; NaN -> 0; 2.5 / 1 -> 2
+    assert b[0].tolist() == [2, -2, 2 ** 29, -2 ** 29, 0, 2]
+    # image 1 (sx 0.5): 1.25 / 0.25 = 5; -0.375 / 0.125 = -3; 2.5 / 0.5 = 5
+    assert b[1].tolist() == [5, -3, 2 ** 29, -2 ** 29, 0, 5]
+    g = mg.rng(5)
+    x = g.standard_normal((2, 6, 7, 5)).astype(np.float32)
+    w = (g.standard_normal((4, 6, 3, 3)) * 0.2).astype(np.float32)
+    plain = orc.conv3x3_int8(x, w, None, relu=True)
+    zero = orc.conv3x3_int8(x, w, np.zeros(4, np.float32), relu=True, bias_int32=True)
+    assert np.array_equal(plain["y"], zero["y"]) and plain["shift"] == zero["shift"]
+    # the int32 route's values approximate relu(conv + bias) within its rounding
+    bias = (g.standard_normal(4) * 0.5).astype(np.float32)
+    bi = orc.conv3x3_int8(x, w, bias, relu=True, bias_int32=True)
+    fl = orc.conv3x3_int8(x, w, bias, relu=False)
+    ref = np.maximum(fl["y"], 0)
+    assert np.abs(bi["y"] - ref).max() <= 2 * float((bi["scale"][:, None] * bi["sx"][None, :]).max())
+
+
 def test_requant_rounds_half_up_and_saturates():
     acc = np.array([[-5, -4, -3, 3, 4, 5, 10 ** 6, -10 ** 6]], np.int32)
     assert orc.requant(acc, 1, False).tolist() == [[-2, -2, -1, 2, 2, 3, 127, -128]]

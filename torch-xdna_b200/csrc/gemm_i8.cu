@@ -203,9 +203,10 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   if (bias_i32) XDNA_CHECK_ARG(aligned16(bias), "conv3x3: int32 bias not 16-byte aligned");
   XDNA_CHECK_ARG(!next_amax || (mode == XDNA_CONV_Q_NHWC && scale != nullptr && sx != nullptr && acc_max != nullptr),
                  "conv3x3: XDNA_CONV_NEXT_AMAX needs XDNA_CONV_Q_NHWC, scale, sx and acc_max (N words)");
-  XDNA_CHECK_ARG(!next_amax || !next_pool || next_relu || (relu == 1 && bias == nullptr),
-                 "conv3x3: pooled maxima need non-negative values (XDNA_CONV_NEXT_RELU, or a fused ReLU and no bias)");
-  XDNA_CHECK_ARG(!next_amax || bias == nullptr || bias_dtype == XDNA_F32, "conv3x3: next maxima need an f32 bias");
+  XDNA_CHECK_ARG(!next_amax || !next_pool || next_relu || (relu == 1 && (bias == nullptr || bias_i32)),
+                 "conv3x3: pooled maxima need non-negative values (XDNA_CONV_NEXT_RELU, or a fused ReLU and no float bias)");
+  XDNA_CHECK_ARG(!next_amax || bias_i32 || bias == nullptr || bias_dtype == XDNA_F32,
+                 "conv3x3: next maxima need an f32 bias");
   XDNA_CHECK_ARG(mode == XDNA_CONV_Q || mode == XDNA_CONV_DEQUANT || mode == XDNA_CONV_CALIBRATE ||
                      mode == XDNA_CONV_Q_NHWC,
                  "conv3x3: unknown mode %d", mode);

@@ -20,10 +20,15 @@ so existing option dictionaries keep working. On the B200 build their meaning is
                "always": every launch. "off": never.
   verbose      log rewrites.
 
-One option is new in this build (off by default, so the default rewrites exactly the reference's convs):
+Two options are new in this build (off by default, so the default computes exactly the reference's values):
   conv_ext     also offload the ResNet-style convs the reference has no kernel for
                (R:results/conv3x3_cascade.md:222-223): 1x1 convs (stride 1 or 2, no padding) and 3x3
                convs with stride 2 and padding 1, through the same int8 arithmetic (xdna::conv_int8).
+  conv_bias_int32
+               a biased conv adds its bias inside the int32 sums, before the requantise, as
+               rint(bias / (sw * sx)) per image (R:results/conv3x3_cascade.md:224-225 names this as future
+               work); a ReLU after the bias becomes the requantise's [0, 255] saturation. Different numerics
+               from the reference's route (the bias is rounded to the sums' units and shares their shift).
 """
 
 from dataclasses import dataclass, fields, replace
@@ -50,6 +55,7 @@ class Config:
     verify: str = "first"
     verbose: bool = False
     conv_ext: bool = False
+    conv_bias_int32: bool = False
 
     def __post_init__(self):
         assert self.policy in POLICIES, f"policy must be one of {POLICIES}"

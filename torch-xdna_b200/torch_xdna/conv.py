@@ -104,7 +104,7 @@ class ConvLayer:
     A [Co, Ci, 1, 1] weight is a 1x1 conv (one tap); stride 2 reads the input's stride phases
     (conv_quant_phases). h, w: the input's size; self.h, self.w: the output's."""
 
-    def __init__(self, weight, h, w, relu, taps=False, stride=1):
+    def __init__(self, weight, h, w, relu, taps=False, stride=1, bint=False):
         kernels._cuda(weight)
         co, ci, k = weight.shape[0], weight.shape[1], weight.shape[-1]
         assert k in (1, 3) and stride in (1, 2) and (k == 3 or not taps) and (stride == 1 or not taps)
@@ -138,10 +138,12 @@ class ConvLayer:
         self.hi, self.wi = h, w
         self.h, self.w = (h + 1) // 2 if stride == 2 else h, (w + 1) // 2 if stride == 2 else w
         self.relu = relu
+        self.bint = bool(bint)  # the bias inside the int32 sums (Config(conv_bias_int32=True))
         self.shift = self.scale = None
         self.checked = False
         kind = "conv3x3" if k == 3 else "conv1x1"
-        self.name = f"{kind}{' stride 2' if stride == 2 else ''} {ci}->{co} {h}x{w}" + (" relu" if relu else "")
+        self.name = (f"{kind}{' stride 2' if stride == 2 else ''} {ci}->{co} {h}x{w}" + (" relu" if relu else "")
+                     + (" int32-bias" if bint else ""))
 
     def quantise(self, xc, n):
         """(xp, sx) of the float input xc [n, Ci, h, w]: the per-image quantise into the layout this layer's
@@ -159,13 +161,14 @@ class ConvLayer:
         stats.launches += 2
         return xp, sx
 
-    def calibrate(self, xp, n=1, strips=None):
+    def calibrate(self, xp, n=1, strips=None, bint=None):
         """Fix the shift from the first image's integer sums (R:torch_xdna/conv.py:71-76). n: the images in xp
         (a stride-2 input's phase planes are n images apart). strips: the process group over whose ranks the
-        image is split into strips of rows; the max of the sums is then the max over every rank's strip."""
+        image is split into strips of rows; the max of the sums is then the max over every rank's strip.
+        bint: the int32 bias [n, Co] (bias_int32), part of the sums the shift must hold."""
         acc_max = torch.empty((1,), dtype=torch.int32, device=xp.device)
-        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_CALIBRATE | self.mode_flag,
-                        relu=self.relu, acc_max=acc_max)
+        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w,
+                        kernels.CONV_CALIBRATE | self.flags(bint), relu=self.relu, bias=bint, acc_max=acc_max)
         stats.launches += 1
         if strips is not None:
             parallel.all_max_(acc_max, None if strips is True else strips)
@@ -176,42 +179,58 @@ class ConvLayer:
         self.shift = parallel.broadcast_shift(shift, xp.device) if strips is None else shift
         self.scale = self.sw * 2.0 ** self.shift
 
-    def q(self, xp, n):
-        out = torch.empty((n, self.co, self.h, self.w), dtype=torch.uint8 if self.relu else torch.int8,
-                          device=xp.device)
-        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_Q | self.mode_flag,
-                        shift=self.shift, relu=self.relu, out=out)
+    def flags(self, bint=None):
+        return self.mode_flag | (kernels.CONV_BIAS_INT32 if bint is not None else 0)
+
+    def bias_int32(self, bias, sx):
+        """The int32 bias [n, Co] of Config(conv_bias_int32=True): rint(bias / (sw * sx)) per image, the units
+        of the integer sums (xdna_conv_bias_int32)."""
+        out = torch.empty((sx.numel(), self.co), dtype=torch.int32, device=sx.device)
+        kernels.conv_bias_int32(bias, self.sw, sx, out)
         stats.launches += 1
         return out
 
-    def dequant(self, xp, n, sx, bias, dtype, post_relu=False):
+    def q(self, xp, n, bint=None):
+        out = torch.empty((n, self.co, self.h, self.w), dtype=torch.uint8 if self.relu else torch.int8,
+                          device=xp.device)
+        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_Q | self.flags(bint),
+                        shift=self.shift, relu=self.relu, bias=bint, out=out)
+        stats.launches += 1
+        return out
+
+    def dequant(self, xp, n, sx, bias, dtype, post_relu=False, bint=None):
         # channels-last: the epilogue writes each pixel's channels contiguously (same values and shape as
         # the reference's NCHW tensor; torch ops downstream keep the layout)
         out = torch.empty((n, self.co, self.h, self.w), dtype=dtype, device=xp.device,
                           memory_format=torch.channels_last)
         relu = kernels.RELU_AFTER_BIAS if post_relu else self.relu
-        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_DEQUANT | self.mode_flag,
-                        shift=self.shift, relu=relu, scale=self.scale, sx=sx, bias=bias, out=out)
+        kernels.conv3x3(xp, self.wp, n, self.ci_k, self.co, self.h, self.w, kernels.CONV_DEQUANT | self.flags(bint),
+                        shift=self.shift, relu=relu, scale=self.scale, sx=sx, bias=bint if bint is not None else bias,
+                        out=out)
         stats.launches += 1
         return out
 
-    def cpu_integers(self, xq_nchw_cpu):
+    def cpu_integers(self, xq_nchw_cpu, bint=None):
         """The reference's CPU integers for the same layer and shift (ConvLayer.cpu,
-        R:torch_xdna/conv.py:86-92), used only to verify launches."""
+        R:torch_xdna/conv.py:86-92), used only to verify launches; with bint [N, Co], added to the sums
+        before the shift."""
         dt = torch.float32 if 127 * float(self.wq4.abs().sum(dim=(1, 2, 3)).max()) < 2 ** 24 else torch.float64
         acc = torch.nn.functional.conv2d(xq_nchw_cpu.to(dt), self.wq4.cpu().to(dt), stride=self.stride,
-                                         padding=self.k // 2)
-        q = (acc.to(torch.int32) + (1 << (self.shift - 1))) >> self.shift
+                                         padding=self.k // 2).to(torch.int32)
+        if bint is not None:
+            acc = acc + bint.cpu()[:, :, None, None]
+        q = (acc + (1 << (self.shift - 1))) >> self.shift
         return q.clamp_(0, 255).to(torch.uint8) if self.relu else q.clamp_(-128, 127).to(torch.int8)
 
 
-def _layer(weight, h, w, relu, taps=False, stride=1, strips=False):
-    # strips: a layer of a strip-split image keeps its own (combined) shift, apart from a same-size whole image
-    key = (id(weight), h, w, relu, bool(taps), stride, strips)
+def _layer(weight, h, w, relu, taps=False, stride=1, strips=False, bint=False):
+    # strips: a layer of a strip-split image keeps its own (combined) shift, apart from a same-size whole image;
+    # bint: the int32-bias route calibrates on the sums with the bias in them
+    key = (id(weight), h, w, relu, bool(taps), stride, strips, bool(bint))
     hit = _layers.get(key)
     if hit is not None and hit[0]() is weight:
         return hit[1]
-    layer = ConvLayer(weight, h, w, relu, taps, stride)
+    layer = ConvLayer(weight, h, w, relu, taps, stride, bint)
     _layers[key] = (weakref.ref(weight), layer)
     return layer
 
@@ -238,12 +257,25 @@ def _bordered(n, h, w, cp, device):
     return torch.empty((n, h + 2, w + 2, cp), dtype=torch.int8, device=device)
 
 
-def _verify(cfg, layer, xp, xq_cpu_fn, n=None):
+def int32_bias(cfg, bias):
+    """Whether this conv adds its bias inside the int32 sums (Config(conv_bias_int32=True), biased convs)."""
+    return bool(getattr(cfg, "conv_bias_int32", False)) and bias is not None
+
+
+def effective_relu(cfg, relu, bias, post_relu):
+    """(ReLU fused into the requantise, ReLU after the float bias) of a conv: with the bias inside the int32
+    sums, a ReLU after the bias is the requantise's [0, 255] saturation."""
+    if int32_bias(cfg, bias):
+        return bool(relu or post_relu), False
+    return relu, post_relu
+
+
+def _verify(cfg, layer, xp, xq_cpu_fn, n=None, bint=None):
     if cfg.verify == "off" or (cfg.verify == "first" and layer.checked):
         return
     n = xp.shape[0] if n is None else n
-    got = layer.q(xp, n).cpu()
-    want = layer.cpu_integers(xq_cpu_fn())
+    got = layer.q(xp, n, bint).cpu()
+    want = layer.cpu_integers(xq_cpu_fn(), bint)
     if not torch.equal(got, want):
         raise XdnaResultMismatch(f"{layer.name} disagrees with the CPU integers: "
                                  f"{int((got != want).sum())} of {want.numel()} values differ")
@@ -281,25 +313,28 @@ def conv3x3_fused(cfg, x, weight, bias, relu, post_relu=False):
     kernels._cuda(x, weight, bias)
     n, ci, h, w = x.shape
     co = weight.shape[0]
+    bint_mode = int32_bias(cfg, bias)
+    relu, post_relu = effective_relu(cfg, relu, bias, post_relu)
     t0 = time.perf_counter()
     with _lock:
-        layer = _layer(weight, h, w, relu, taps=ci <= 7)
+        layer = _layer(weight, h, w, relu, taps=ci <= 7, bint=bint_mode)
         xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
         xp = _bordered(n, h, w, layer.cp, x.device)
         sx = torch.empty((n,), dtype=torch.float32, device=x.device)
         scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
         _quantise_float(layer, xc, xp, sx, scratch)
         stats.launches += 2
+        bint = layer.bias_int32(bias, sx) if bint_mode else None
         if layer.shift is None:
-            layer.calibrate(xp)
+            layer.calibrate(xp, bint=bint)
 
         def xq_cpu():
             xf = xc.float().cpu()
             s = xf.abs().amax(dim=(1, 2, 3), keepdim=True).clamp(min=1e-8) / 127
             return torch.round(xf / s).clamp(-127, 127).to(torch.int8)
 
-        _verify(cfg, layer, xp, xq_cpu)
-        y = layer.dequant(xp, n, sx, bias, x.dtype, post_relu)
+        _verify(cfg, layer, xp, xq_cpu, bint=bint)
+        y = layer.dequant(xp, n, sx, bias, x.dtype, post_relu, bint)
     stats.calls[DEVICE] += 1
     stats.seconds[DEVICE] += time.perf_counter() - t0
     stats.macs[DEVICE] += n * co * ci * h * w * 9
@@ -320,21 +355,24 @@ def conv_int8(cfg, x, weight, bias, stride, relu, post_relu=False):
         return conv3x3_fused(cfg, x, weight, bias, relu, post_relu)
     n, ci, h, w = x.shape
     co = weight.shape[0]
+    bint_mode = int32_bias(cfg, bias)
+    relu, post_relu = effective_relu(cfg, relu, bias, post_relu)
     t0 = time.perf_counter()
     with _lock:
-        layer = _layer(weight, h, w, relu, stride=stride)
+        layer = _layer(weight, h, w, relu, stride=stride, bint=bint_mode)
         xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
         xp, sx = layer.quantise(xc, n)
+        bint = layer.bias_int32(bias, sx) if bint_mode else None
         if layer.shift is None:
-            layer.calibrate(xp, n)
+            layer.calibrate(xp, n, bint=bint)
 
         def xq_cpu():
             xf = xc.float().cpu()
             s = xf.abs().amax(dim=(1, 2, 3), keepdim=True).clamp(min=1e-8) / 127
             return torch.round(xf / s).clamp(-127, 127).to(torch.int8)
 
-        _verify(cfg, layer, xp, xq_cpu, n)
-        y = layer.dequant(xp, n, sx, bias, x.dtype, post_relu)
+        _verify(cfg, layer, xp, xq_cpu, n, bint=bint)
+        y = layer.dequant(xp, n, sx, bias, x.dtype, post_relu, bint)
     stats.calls[DEVICE] += 1
     stats.seconds[DEVICE] += time.perf_counter() - t0
     stats.macs[DEVICE] += n * co * ci * layer.h * layer.w * k * k
@@ -397,9 +435,12 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
         n, hq, wq, ci = x.shape
         h, w = (hq // 2, wq // 2) if in_mode == IN_CODES_POOL else (hq, wq)
     co = weight.shape[0]
+    bint_mode = int32_bias(cfg, bias)
+    relu, post_relu = effective_relu(cfg, relu, bias, post_relu)
+    fbias = None if bint_mode else bias   # the bias added to the floats (none when it is in the sums)
     t0 = time.perf_counter()
     with _lock:
-        layer = _layer(weight, h, w, relu, taps=in_mode == IN_FLOAT and ci <= 7)
+        layer = _layer(weight, h, w, relu, taps=in_mode == IN_FLOAT and ci <= 7, bint=bint_mode)
         xp = _bordered(n, h, w, layer.cp, x.device)
         sx = torch.empty((n,), dtype=torch.float32, device=x.device)
         scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
@@ -419,33 +460,35 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
                                          in_pool, xp, sx, scratch)
             float_in = lambda: codes_to_float(xq, xmeta, in_relu_after, in_mode == IN_CODES_POOL)  # noqa: E731
         stats.launches += 2
+        bint = layer.bias_int32(bias, sx) if bint_mode else None
         if layer.shift is None:
-            layer.calibrate(xp)
+            layer.calibrate(xp, bint=bint)
 
         def xq_cpu():
             xf = float_in()
             s = xf.abs().amax(dim=(1, 2, 3), keepdim=True).clamp(min=1e-8) / 127
             return torch.round(xf / s).clamp(-127, 127).to(torch.int8)
 
-        _verify(cfg, layer, xp, xq_cpu)
+        _verify(cfg, layer, xp, xq_cpu, bint=bint)
         if out_q:
             q = torch.empty((n, h, w, co), dtype=torch.uint8 if relu else torch.int8, device=x.device)
-            if next_amax_ok(relu, bias, post_relu, out_pool):
-                meta = codes_meta(sx, layer.scale, bias, co, amax=True, pool=out_pool)
-                mode = (kernels.CONV_Q_NHWC | layer.mode_flag | kernels.CONV_NEXT_AMAX
+            if next_amax_ok(relu, fbias, post_relu, out_pool):
+                meta = codes_meta(sx, layer.scale, fbias, co, amax=True, pool=out_pool)
+                mode = (kernels.CONV_Q_NHWC | layer.flags(bint) | kernels.CONV_NEXT_AMAX
                         | (kernels.CONV_NEXT_RELU if post_relu else 0) | (kernels.CONV_NEXT_POOL if out_pool else 0))
+                kb = bint if bint is not None else (meta[n + co:n + 2 * co] if bias is not None else None)
                 kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, mode, shift=layer.shift, relu=relu,
-                                scale=meta[n:n + co], sx=sx, bias=meta[n + co:n + 2 * co] if bias is not None else None,
-                                out=q, acc_max=meta[n + 2 * co:2 * n + 2 * co].view(torch.int32))
+                                scale=meta[n:n + co], sx=sx, bias=kb, out=q,
+                                acc_max=meta[n + 2 * co:2 * n + 2 * co].view(torch.int32))
                 out = (q, meta)
             else:
-                kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, kernels.CONV_Q_NHWC | layer.mode_flag,
-                                shift=layer.shift, relu=relu, out=q)
-                out = (q, codes_meta(sx, layer.scale, bias, co))
+                kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, kernels.CONV_Q_NHWC | layer.flags(bint),
+                                shift=layer.shift, relu=relu, bias=bint, out=q)
+                out = (q, codes_meta(sx, layer.scale, fbias, co))
             stats.launches += 1
         else:
             dtype = x.dtype if in_mode == IN_FLOAT else torch.float32
-            out = (layer.dequant(xp, n, sx, bias, dtype, post_relu), sx.new_empty((0,)))
+            out = (layer.dequant(xp, n, sx, bias, dtype, post_relu, bint), sx.new_empty((0,)))
     stats.calls[DEVICE] += 1
     stats.seconds[DEVICE] += time.perf_counter() - t0
     stats.macs[DEVICE] += n * co * ci * h * w * 9

@@ -29,6 +29,7 @@ CONV_SINGLE_TAP = 16  # or'ed into a conv mode: one tap at offset 0 (a 1x1 conv,
 CONV_STRIDE2 = 32     # or'ed into a conv mode: stride 2, the input split into phase planes (conv_quant_phases)
 # or'ed into CONV_Q_NHWC: the next layer's per-image maxima into acc_max (with its ReLU / 2x2 pool region)
 CONV_NEXT_AMAX, CONV_NEXT_RELU, CONV_NEXT_POOL = 64, 128, 256
+CONV_BIAS_INT32 = 512  # or'ed into any conv mode: `bias` is int32 [N, Co] (conv_bias_int32), added to the sums
 # status codes
 ERR_TIMEOUT = -4
 
@@ -66,6 +67,7 @@ def _load():
         "xdna_conv_quant_channels_last": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
         "xdna_conv_quant_codes_given_amax": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
+        "xdna_conv_bias_int32": ([P, I, P, P, I64, I64, P, P], I),
         "xdna_conv_quant_taps": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_phases": ([P, I, I, I64, I64, I64, I64, I, P, I64, P, P, P], I),
         "xdna_conv_image_amax": ([P, I, I64, I64, P, P], I),
@@ -295,6 +297,14 @@ def conv_quant_codes_given_amax(q, scale, sx_in, bias, relu_after, pool, xp, sx,
     _check("xdna_conv_quant_codes_given_amax", L.xdna_conv_quant_codes_given_amax(
         _p(q), int(q.dtype == torch.uint8), N, C, H, W, _p(scale), _p(sx_in), _p(bias), int(relu_after), int(pool),
         _p(xp), xp.shape[-1], _p(sx), _p(amax), _stream()))
+
+
+def conv_bias_int32(bias, sw, sx, out):
+    """out [N, Co] int32 = rint(bias / (sw * sx)) per image (xdna_conv_bias_int32)."""
+    L = require()
+    _cuda(bias, sw, sx, out)
+    _check("xdna_conv_bias_int32", L.xdna_conv_bias_int32(_p(bias), DTYPE_CODES[bias.dtype], _p(sw), _p(sx),
+                                                          sx.numel(), sw.numel(), _p(out), _stream()))
 
 
 def conv_pack_input(xq, xp):

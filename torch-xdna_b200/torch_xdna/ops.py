@@ -128,8 +128,11 @@ def _(x, xmeta, weight, bias, relu, cfg_id, post_relu, in_mode, in_relu_after, o
     else:
         h, w = (x.shape[1] // 2, x.shape[2] // 2) if in_mode == conv.IN_CODES_POOL else (x.shape[1], x.shape[2])
     if out_q:
+        cfg = _configs[cfg_id]
+        fbias = None if conv.int32_bias(cfg, bias) else bias
+        relu, post_relu = conv.effective_relu(cfg, relu, bias, post_relu)
         q = x.new_empty((n, h, w, co), dtype=torch.uint8 if relu else torch.int8)
-        extra = n + (1 if out_pool else 0) if conv.next_amax_ok(relu, bias, post_relu, out_pool) else 0
+        extra = n + (1 if out_pool else 0) if conv.next_amax_ok(relu, fbias, post_relu, out_pool) else 0
         return q, x.new_empty((n + 2 * co + extra,), dtype=torch.float32)
     dtype = x.dtype if in_mode == conv.IN_FLOAT else torch.float32
     y = torch.empty((n, co, h, w), dtype=dtype, device=x.device, memory_format=torch.channels_last)
