@@ -78,7 +78,8 @@ def test_chain_equals_unchained(cuda, case, verify, hint, bint):
 KINDS = ["relu_after_bias", "fused_relu", "signed"]
 
 
-@pytest.mark.parametrize("shape", [(3, 40, 64, 15, 17), (2, 64, 128, 30, 22), (9, 16, 32, 3, 4)])
+@pytest.mark.parametrize("shape", [(3, 40, 64, 15, 17), (2, 64, 128, 30, 22), (9, 16, 32, 3, 4), (2, 32, 320, 9, 11),
+                                   (2, 128, 512, 20, 20)])
 @pytest.mark.parametrize("kind", KINDS)
 @pytest.mark.parametrize("pool", [False, True])
 def test_next_layer_maxima_from_the_producer(cuda, shape, kind, pool):

@@ -405,6 +405,12 @@ __device__ __forceinline__ ConvPixel conv_pixel(const GemmArgs& a, int p) {
   return px;
 }
 
+// Whether every value the codes stand for is >= 0 (a ReLU after the bias, or one in the requantise of a conv
+// without a float bias), so that the largest code of a channel gives its largest |y|.
+__device__ __forceinline__ bool next_nonneg(const GemmArgs& a) {
+  return a.next_relu || (a.relu && a.bias == nullptr);
+}
+
 // The next conv's per-image max from this conv's codes (XDNA_CONV_NEXT_AMAX). The value a code stands for,
 // y(q) = fl(fl(q) * fl(scale[c] * sx[n])) (+ bias[c]) (then max(y, 0)) -- the next layer's quantise rebuilds it
 // with exactly these f32 operations -- never decreases as q grows, so per channel only the largest code of the
@@ -414,7 +420,7 @@ __device__ __forceinline__ ConvPixel conv_pixel(const GemmArgs& a, int p) {
 __device__ __forceinline__ void conv_next_amax(const GemmArgs& a, const ConvPixel& px, int nvalid, const int (&qv)[32],
                                                float scale_lane, float bias_lane) {
   const bool in = px.valid && px.yp - 1 < a.next_h && px.xp - 1 < a.next_w;
-  const bool nonneg = a.next_relu || a.relu;  // y >= 0: the largest code gives the largest |y|
+  const bool nonneg = next_nonneg(a);  // y >= 0: the largest code gives the largest |y|
   const int img = in ? px.img : -1;
   // the warp's pixels may span several images (a tile crossing an image's end): one pass per image
   const int lo = __reduce_min_sync(kFull, in ? img : INT_MAX);
@@ -449,6 +455,55 @@ __device__ __forceinline__ void conv_next_amax(const GemmArgs& a, const ConvPixe
   }
 }
 
+// XDNA_CONV_NEXT_AMAX for values >= 0 (next_nonneg), accumulated across tiles: each epilogue lane keeps, per
+// channel of its chunks, the largest code of its pixels over the tiles it drains of one image and one column
+// tile (four codes per word, in unsigned order: a signed code is stored as code + 128), and the warp combines
+// them and evaluates y once per channel when the image or the column tile changes and after the last tile --
+// instead of a warp reduction per channel per tile. img < 0: nothing held. sc / bi: this lane's channel
+// scale and bias for each chunk; sx: the image's scale.
+template <int NCH>
+struct NextMax {
+  int img, nb;
+  float sx;
+  uint32_t w[NCH][8];
+  float sc[NCH], bi[NCH];
+};
+
+// Combine a NextMax over the warp and raise the image's max (the whole warp calls it). col0: the first
+// column of the warp's chunks in the held column tile.
+template <int NCH>
+__device__ __forceinline__ void next_max_flush(const GemmArgs& a, const NextMax<NCH>& nm, int col0) {
+  const int lane = lane_id();
+  uint32_t best = 0;  // max |y| over this lane's channels, as bits (non-negative floats order like them)
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int n0 = col0 + c * 32;
+    if (n0 < a.N) {  // warp-uniform
+      uint32_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) w[k] = nm.w[c][k];
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = __vmaxu4(w[k], __shfl_xor_sync(kFull, w[k], s));
+      }
+      uint32_t word = w[0];  // every lane holds the 32 channels' largest codes; lane j takes channel n0 + j
+#pragma unroll
+      for (int k = 1; k < 8; ++k) word = (lane >> 2) == k ? w[k] : word;
+      const int u = static_cast<int>((word >> (8 * (lane & 3))) & 0xFFu);
+      const int q = a.relu ? u : u - 128;
+      if (lane < a.N - n0) {
+        float y = __fmul_rn(static_cast<float>(q), __fmul_rn(nm.sc[c], nm.sx));
+        if (a.bias != nullptr) y = __fadd_rn(y, nm.bi[c]);
+        if (a.next_relu) y = y > 0.f ? y : 0.f;
+        best = max(best, __float_as_uint(y) & 0x7FFFFFFFu);
+      }
+    }
+  }
+  best = __reduce_max_sync(kFull, best);
+  if (lane == 0 && best != 0u) atomicMax(a.next_amax + nm.img, best);
+}
+
 // XDNA_CONV_BIAS_INT32: the sums of this lane's pixel, channels n0..n0+31, plus the image's int32 bias row.
 __device__ __forceinline__ void add_bias_i32(const GemmArgs& a, const ConvPixel& px, int n0, uint32_t (&r)[32]) {
   if (!px.valid) return;
@@ -471,9 +526,12 @@ __device__ __forceinline__ void add_bias_i32(const GemmArgs& a, const ConvPixel&
 }
 
 // Conv epilogues: one thread, one bordered pixel, channels n0..n0+31 in r[].
+// nm_mode (EPI_CONV_QNHWC with XDNA_CONV_NEXT_AMAX): 1 fold the codes of the pixels in the next layer's
+// region (nm_in) into nm_acc (NextMax), 2 reduce this chunk's maxima at once (conv_next_amax), 0 neither.
 template <int EPI>
 __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& px, int n0, const uint32_t (&r)[32],
-                                           float scale_lane, float bias_lane, uint8_t* stage) {
+                                           float scale_lane, float bias_lane, uint8_t* stage, int nm_mode,
+                                           bool nm_in, uint32_t (&nm_acc)[8]) {
   const int img = px.img;
   const int yp = px.yp;
   const int xp = px.xp;
@@ -496,19 +554,25 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     int qv[32];  // this pixel's codes
 #pragma unroll
     for (int j = 0; j < 32; ++j) qv[j] = requant(static_cast<int>(r[j]), a.shift, a.relu);
-    if (a.next_amax != nullptr) conv_next_amax(a, px, nvalid, qv, scale_lane, bias_lane);  // warp-uniform
+    uint32_t w[8];  // packed, four codes per word
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) word |= (static_cast<uint32_t>(qv[4 * k + b]) & 0xFFu) << (8 * b);
+      w[k] = word;
+    }
+    if (nm_mode == 1) {  // warp-uniform
+      const uint32_t flip = a.relu ? 0u : 0x80808080u;  // signed codes in unsigned order
+#pragma unroll
+      for (int k = 0; k < 8; ++k) nm_acc[k] = __vmaxu4(nm_acc[k], nm_in ? (w[k] ^ flip) : 0u);
+    } else if (nm_mode == 2) {
+      conv_next_amax(a, px, nvalid, qv, scale_lane, bias_lane);
+    }
     if (!valid) return;
     // out[img, yp-1, xp-1, n0 ..]: this pixel's 32 codes are 32 contiguous bytes
     uint8_t* o = static_cast<uint8_t*>(a.out) + ((static_cast<int64_t>(img) * a.H + (yp - 1)) * a.W + (xp - 1)) * a.N + n0;
     if (nvalid == 32 && a.vec_ok) {
-      uint32_t w[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) word |= (static_cast<uint32_t>(qv[4 * k + b]) & 0xFFu) << (8 * b);
-        w[k] = word;
-      }
       reinterpret_cast<uint4*>(o)[0] = make_uint4(w[0], w[1], w[2], w[3]);
       reinterpret_cast<uint4*>(o)[1] = make_uint4(w[4], w[5], w[6], w[7]);
     } else {
@@ -918,6 +982,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total = args.m_tiles * args.n_tiles;
+  // Convs walk one contiguous range of tiles per CTA (pair), so that an epilogue warp's consecutive tiles lie
+  // in one image (the next layer's maxima are then combined once per image, not per tile); GEMMs interleave
+  // the CTAs' tiles (t_first, t_first + t_step, ...).
+  const int t_begin = kConv ? static_cast<int>(static_cast<int64_t>(t_first) * total / t_step) : t_first;
+  const int t_end = kConv ? static_cast<int>(static_cast<int64_t>(t_first + 1) * total / t_step) : total;
+  const int t_inc = kConv ? 1 : t_step;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -929,13 +999,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
       bool ok = true;
       if constexpr (RB) {  // the weights of all taps, once
-        if (t_first < total) {
+        if (t_begin < t_end) {
           const int ntaps = args.ntaps;
           mbar_arrive_expect_tx(bres, ntaps * B_BYTES);
           for (int tap = 0; tap < ntaps; ++tap) tma_load_3d(smRes + tap * B_BYTES, &tmB, bres, 0, tap, 0);
         }
       }
-      for (int t = t_first; t < total && ok; t += t_step) {
+      for (int t = t_begin; t < t_end && ok; t += t_inc) {
         int mb, nb;
         tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
         for (int kb = 0; kb < args.num_kb; ++kb) {
@@ -994,7 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(full + s, static_cast<uint32_t>(last_parity[s]), &never, args.err, 2);
         }
       if constexpr (RB) {
-        if (t_first < total) {
+        if (t_begin < t_end) {
           volatile int never = 0;
           mbar_wait(bres, 0, &never, args.err, 2);
         }
@@ -1010,9 +1080,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool issued = false;
       bool ok = true;
       if constexpr (RB) {
-        if (t_first < total && !mbar_wait(bres, 0, abort_flag, args.err, 4)) ok = false;
+        if (t_begin < t_end && !mbar_wait(bres, 0, abort_flag, args.err, 4)) ok = false;
       }
-      for (int t = t_first; t < total && ok; t += t_step) {
+      for (int t = t_begin; t < t_end && ok; t += t_inc) {
         if (!mbar_wait<PAIR>(tempty + buf, bphase ^ 1, abort_flag, args.err, 3)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
@@ -1148,8 +1218,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       return f;
     };
     Factors fac{};
-    if (t_first < total) fac = load_factors(t_first);
-    for (int t = t_first; t < total; t += t_step) {
+    if (t_begin < t_end) fac = load_factors(t_begin);
+    NextMax<NCH> nm;  // EPI_CONV_QNHWC with XDNA_CONV_NEXT_AMAX
+    nm.img = -1;
+    nm.nb = 0;
+    for (int t = t_begin; t < t_end; t += t_inc) {
       int mb, nb;
       tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
       const int row0 = tile_row0(mb) + q * 32;
@@ -1163,6 +1236,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         bcol[c] = fac.bcol[c];
       }
       const ConvPixel px = fac.px;
+      int nm_mode = 0;
+      bool nm_in = false;
+      if constexpr (EPI == EPI_CONV_QNHWC) {
+        if (args.next_amax != nullptr) {  // warp-uniform from here on
+          nm_in = px.valid && px.yp - 1 < args.next_h && px.xp - 1 < args.next_w;
+          if (next_nonneg(args)) {
+            const int img = nm_in ? px.img : -1;
+            const int lo = __reduce_min_sync(kFull, nm_in ? img : INT_MAX);
+            const int hi = __reduce_max_sync(kFull, img);
+            if (hi >= 0) {  // some pixel of this warp counts
+              if (nm.img >= 0 && (lo != nm.img || hi != nm.img || nb != nm.nb)) {
+                next_max_flush(args, nm, nm.nb * BN + half * WCOLS);
+                nm.img = -1;
+              }
+              if (lo == hi) {
+                if (nm.img < 0) {
+                  nm.img = lo;
+                  nm.nb = nb;
+                  nm.sx = __ldg(args.sx + lo);
+#pragma unroll
+                  for (int c = 0; c < NCH; ++c) {
+                    nm.sc[c] = fcol[c];
+                    nm.bi[c] = bcol[c];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) nm.w[c][k] = 0u;
+                  }
+                }
+                nm_mode = 1;
+              } else {
+                nm_mode = 2;  // the warp's pixels span two images
+              }
+            }
+          } else {
+            nm_mode = 2;
+          }
+        }
+      }
       if constexpr (kSmemFactors) {
         __syncwarp();  // this warp is done reading the previous tile's factors
 #pragma unroll
@@ -1179,7 +1289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (!mbar_wait<PAIR>(tfull + buf, bphase, abort_flag, args.err, 6)) break;
       tc_fence_after();
-      if (t + t_step < total) fac = load_factors(t + t_step);
+      if (t + t_inc < t_end) fac = load_factors(t + t_inc);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + half * WCOLS);
       if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
@@ -1302,9 +1412,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (n0 + 32 <= args.N && args.vec_ok)  // warp-uniform
               conv_deq_smem(args, px.s, n0, rc, col_sw + c * 32, col_bias + c * 32, pix_off, obuf);
             else
-              conv_chunk<EPI>(args, px, n0, rc, col_sw[c * 32 + lane], col_bias[c * 32 + lane], nullptr);
+              conv_chunk<EPI>(args, px, n0, rc, col_sw[c * 32 + lane], col_bias[c * 32 + lane], nullptr, 0, false,
+                              nm.w[c]);
           } else {
-            conv_chunk<EPI>(args, px, n0, rc, fcol[c], bcol[c], obuf);
+            conv_chunk<EPI>(args, px, n0, rc, fcol[c], bcol[c], obuf, nm_mode, nm_in, nm.w[c]);
           }
         }
         if (c + 1 < NCH) tmem_ld_wait();
@@ -1314,6 +1425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         buf = 0;
         bphase ^= 1;
       }
+    }
+    if constexpr (EPI == EPI_CONV_QNHWC) {
+      if (nm.img >= 0) next_max_flush(args, nm, nm.nb * BN + half * WCOLS);
     }
     if constexpr (TSTORE) {
       if (lane == 0) bulk_wait_all();
