@@ -74,7 +74,8 @@ def parse():
                          "(default: peer blocks copied over NVLink once, overlapping the GEMM), read by the GEMM's "
                          "TMA straight from peer memory, after an NCCL all-gather; or data-parallel with the sequences")
     ap.add_argument("--kernel", default=None,
-                    choices=["gemm_i8", "quant_rows", "conv3x3", "attention", "gemm_bf16", "gemm_bf16_qkv"],
+                    choices=["gemm_i8", "quant_rows", "conv3x3", "conv3x3_chain", "attention", "gemm_bf16",
+                             "gemm_bf16_qkv"],
                     help="time one kernel on --shape instead of a workload (profiling)")
     ap.add_argument("--shape", default="8192,6144,1024", help="--kernel shape, comma-separated")
     return ap.parse_args()
@@ -1212,6 +1213,19 @@ def run_kernel(args):
         y = torch.empty(N, C, H, H, device=dev, memory_format=torch.channels_last)
         fn = lambda: kernels.conv3x3(xp, lay.wp, N, C, C, H, H, kernels.CONV_DEQUANT, shift=10, scale=lay.scale,  # noqa
                                      sx=sx, bias=b, out=y)
+        work, unit = 2 * N * C * C * H * H * 9, "TOPS"
+    elif args.kernel == "conv3x3_chain":              # N, C, H: C -> C on H x H as a chain runs it: int8 codes
+        N, C, H = shp                                  # out, the next layer's pooled per-image maxima
+        w = torch.nn.Parameter(torch.randn(C, C, 3, 3, device=dev, generator=g) * (2 / (C * 9)) ** 0.5)
+        lay = xconv.ConvLayer(w, H, H, False)
+        lay.shift, lay.scale = 10, lay.sw * 1024.0
+        xp = torch.randint(-127, 128, (N, H + 2, H + 2, lay.cp), dtype=torch.int8, device=dev, generator=g)
+        sx, b = torch.rand(N, device=dev) + 0.5, torch.randn(C, device=dev) * 0.01
+        q = torch.empty(N, H, H, C, dtype=torch.int8, device=dev)
+        amax = torch.empty(N, dtype=torch.int32, device=dev)
+        mode = kernels.CONV_Q_NHWC | kernels.CONV_NEXT_AMAX | kernels.CONV_NEXT_RELU | kernels.CONV_NEXT_POOL
+        fn = lambda: kernels.conv3x3(xp, lay.wp, N, C, C, H, H, mode, shift=10, scale=lay.scale, sx=sx,  # noqa
+                                     bias=b, out=q, acc_max=amax)
         work, unit = 2 * N * C * C * H * H * 9, "TOPS"
     elif args.kernel == "attention":                  # B, L: causal, 16 q heads / 8 kv heads of 128
         B, L = shp

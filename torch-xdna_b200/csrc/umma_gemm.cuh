@@ -227,6 +227,26 @@ __device__ __forceinline__ int requant(int acc, int shift, int relu) {
   return relu ? min(max(q, 0), 255) : min(max(q, -128), 127);
 }
 
+// Four requantised codes in one word (byte i = code of acc[i]): the arithmetic shift of requant, the
+// saturation to [-128, 127] (or [0, 255] with relu) done by cvt.pack.sat, which converts two s32 to 8 bits
+// each into the word's low 16 bits (the first operand above the second) and copies its third operand's low
+// 16 bits above them.
+template <bool RELU>
+__device__ __forceinline__ uint32_t requant_pack4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, int rnd,
+                                                  int shift) {
+  const int q0 = (static_cast<int>(a0) + rnd) >> shift, q1 = (static_cast<int>(a1) + rnd) >> shift;
+  const int q2 = (static_cast<int>(a2) + rnd) >> shift, q3 = (static_cast<int>(a3) + rnd) >> shift;
+  uint32_t hi, w;
+  if constexpr (RELU) {
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(q3), "r"(q2));
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(q1), "r"(q0), "r"(hi));
+  } else {
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(q3), "r"(q2));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(q1), "r"(q0), "r"(hi));
+  }
+  return w;
+}
+
 // 32 accumulators of one row -> 32 dequantised floats. Column factors: lane j holds column j's.
 __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float srow, float sw_lane, float b_lane,
                                           bool has_bias, float (&v)[32]) {
@@ -551,22 +571,23 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     best = __reduce_max_sync(kFull, best);
     if (lane_id() == 0 && best > 0) atomicMax(a.acc_max, best);
   } else if constexpr (EPI == EPI_CONV_QNHWC) {
-    int qv[32];  // this pixel's codes
+    uint32_t w[8];  // this pixel's codes, four per word
+    const int rnd = 1 << (a.shift - 1);
+    if (a.relu) {  // warp-uniform
 #pragma unroll
-    for (int j = 0; j < 32; ++j) qv[j] = requant(static_cast<int>(r[j]), a.shift, a.relu);
-    uint32_t w[8];  // packed, four codes per word
+      for (int k = 0; k < 8; ++k) w[k] = requant_pack4<true>(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3], rnd, a.shift);
+    } else {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) word |= (static_cast<uint32_t>(qv[4 * k + b]) & 0xFFu) << (8 * b);
-      w[k] = word;
+      for (int k = 0; k < 8; ++k) w[k] = requant_pack4<false>(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3], rnd, a.shift);
     }
     if (nm_mode == 1) {  // warp-uniform
       const uint32_t flip = a.relu ? 0u : 0x80808080u;  // signed codes in unsigned order
 #pragma unroll
       for (int k = 0; k < 8; ++k) nm_acc[k] = __vmaxu4(nm_acc[k], nm_in ? (w[k] ^ flip) : 0u);
     } else if (nm_mode == 2) {
+      int qv[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) qv[j] = requant(static_cast<int>(r[j]), a.shift, a.relu);
       conv_next_amax(a, px, nvalid, qv, scale_lane, bias_lane);
     }
     if (!valid) return;
@@ -578,7 +599,7 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (j < nvalid) o[j] = static_cast<uint8_t>(qv[j] & 0xFF);
+        if (j < nvalid) o[j] = static_cast<uint8_t>(w[j >> 2] >> (8 * (j & 3)));
     }
   } else if constexpr (EPI == EPI_CONV_Q) {
     if (!valid) return;
