@@ -597,6 +597,93 @@ __global__ void __launch_bounds__(256) codes_to_bordered_kernel(const uint32_t* 
   }
 }
 
+// The same quantise, 16 bytes per thread, for C = Cp a power of two (16 .. 4096) and 16-byte aligned
+// tensors: a thread always handles the same 16 channels (256 threads x 16 bytes is a whole number of
+// pixels), so their factors t[c] = fl(scale[c] * sx_in[n]) and biases stay in registers, and a block
+// walks several bordered rows of one image. A code becomes a float exactly through the 2^23 bias (the
+// bit pattern 0x4B000000 + u is 2^23 + u; a signed code is stored as u = code + 128 first); then
+// y = fl(q * t[c]) + b[c] (+0 without a bias: the same quantised byte), the ReLU, round(y / s) as quant_t.
+template <bool POOL, bool USGN>
+__global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* __restrict__ q, int H, int W, int C,
+                                                                  const float* __restrict__ scale,
+                                                                  const float* __restrict__ sx_in,
+                                                                  const float* __restrict__ bias, int relu_after,
+                                                                  const uint32_t* __restrict__ amax,
+                                                                  uint4* __restrict__ xp, float* __restrict__ sx_out) {
+  const int n = blockIdx.y;
+  const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
+  const int Wp = Wo + 2;
+  const int C16 = C / 16;  // 16-byte chunks per pixel (a power of two <= 256)
+  const float s = scale_from_amax(__uint_as_float(amax[n]));
+  const float r = __frcp_rn(s);
+  if (blockIdx.x == 0 && threadIdx.x == 0) sx_out[n] = s;
+  const int chunk = threadIdx.x & (C16 - 1);
+  const float sxn = __ldg(sx_in + n);
+  float t[16], b[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int c = chunk * 16 + j;
+    t[j] = __fmul_rn(__ldg(scale + c), sxn);
+    b[j] = bias != nullptr ? __ldg(bias + c) : 0.f;
+  }
+  const float unbias = USGN ? 8388608.f : 8388736.f;  // 2^23 (+ 128: signed codes stored as code + 128)
+  const uint32_t flip = USGN ? 0u : 0x80808080u;
+  const int per_row = Wp * C16;
+  auto load = [&](int yb, int xb) {  // the pixel's 16 codes, signed ones as code + 128 (pooled: the 2x2 max)
+    if constexpr (!POOL) {
+      const uint4 u = __ldg(q + ((static_cast<int64_t>(n) * H + (yb - 1)) * W + (xb - 1)) * C16 + chunk);
+      return make_uint4(u.x ^ flip, u.y ^ flip, u.z ^ flip, u.w ^ flip);
+    } else {
+      const int64_t p0 = ((static_cast<int64_t>(n) * H + 2 * (yb - 1)) * W + 2 * (xb - 1)) * C16 + chunk;
+      const int64_t row = static_cast<int64_t>(W) * C16;
+      const uint4 a = __ldg(q + p0), bq = __ldg(q + p0 + C16), c = __ldg(q + p0 + row), d = __ldg(q + p0 + row + C16);
+      auto mx = [&](uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+        return __vmaxu4(__vmaxu4(w0 ^ flip, w1 ^ flip), __vmaxu4(w2 ^ flip, w3 ^ flip));
+      };
+      return make_uint4(mx(a.x, bq.x, c.x, d.x), mx(a.y, bq.y, c.y, d.y), mx(a.z, bq.z, c.z, d.z),
+                        mx(a.w, bq.w, c.w, d.w));
+    }
+  };
+  auto convert = [&](const uint4& u) {
+    const uint32_t wi[4] = {u.x, u.y, u.z, u.w};
+    uint32_t wo[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float qf = __fsub_rn(__uint_as_float(__byte_perm(wi[k], 0x4B000000u, 0x7540u + i)), unbias);
+        float y = __fadd_rn(__fmul_rn(qf, t[4 * k + i]), b[4 * k + i]);
+        if (relu_after) y = y > 0.f ? y : 0.f;
+        v[i] = quant_t(y, s, r);
+      }
+      wo[k] = pack_bytes(v[0], v[1], v[2], v[3]);
+    }
+    return make_uint4(wo[0], wo[1], wo[2], wo[3]);
+  };
+  constexpr int U = POOL ? 2 : 4;  // 16-byte vectors per thread in flight (a pooled one is four loads)
+  for (int yb = blockIdx.x; yb < Ho + 2; yb += gridDim.x) {
+    uint4* dst = xp + (static_cast<int64_t>(n) * (Ho + 2) + yb) * per_row;
+    const bool border_row = yb == 0 || yb == Ho + 1;
+    for (int e0 = threadIdx.x; e0 < per_row; e0 += U * blockDim.x) {
+      uint4 u[U];
+      bool in[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {  // all loads first
+        const int e = e0 + j * blockDim.x;
+        const int xb = e / C16;  // C16 a power of two: a shift
+        in[j] = e < per_row && !border_row && xb >= 1 && xb <= Wo;
+        u[j] = in[j] ? load(yb, xb) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int e = e0 + j * blockDim.x;
+        if (e < per_row) dst[e] = in[j] ? convert(u[j]) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
+}
+
 template <bool POOL, bool USGN>
 static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const float* scale, const float* sx_in,
                          const float* bias, int relu_after, int Cp, uint32_t* amax, int8_t* xp, float* sx_out,
@@ -606,8 +693,18 @@ static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const f
   const int chunks = static_cast<int>(std::min<int64_t>((per + 256 * 8 - 1) / (256 * 8), 1024));
   if (!amax_given)
     codes_amax_kernel<POOL, USGN><<<dim3(chunks, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, amax);
-  codes_to_bordered_kernel<POOL, USGN>
-      <<<dim3(Ho + 2, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, Cp, amax, xp, sx_out);
+  const int C = 4 * C4;
+  const bool pow2 = C >= 16 && C <= 4096 && (C & (C - 1)) == 0;
+  if (pow2 && Cp == C && reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(xp) % 16 == 0) {
+    // one wave: three resident blocks per SM over all images, each walking several rows
+    const int blocks = std::max(1, std::min(Ho + 2, 148 * 3 / std::max(N, 1)));
+    codes_to_bordered16_kernel<POOL, USGN><<<dim3(blocks, N), 256, 0, s>>>(
+        reinterpret_cast<const uint4*>(q), H, W, C, scale, sx_in, bias, relu_after, amax, reinterpret_cast<uint4*>(xp),
+        sx_out);
+  } else {
+    codes_to_bordered_kernel<POOL, USGN>
+        <<<dim3(Ho + 2, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, Cp, amax, xp, sx_out);
+  }
 }
 
 // wq [Co, Ci, 3, 3] -> wp [Co, 9, Cp], pad channels zero.
