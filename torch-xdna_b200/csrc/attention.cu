@@ -339,11 +339,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         // the row max of the raw scores (scale > 0 commutes with max), as 8 independent partial maxima so
         // that the reduction is not one 128-long dependent chain
+        // (three-input max.f32: two keys per instruction)
         float m8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(v[i]);
 #pragma unroll
-        for (int e = 8; e < 128; ++e) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(v[e]));
+        for (int e = 8; e + 16 <= 128; e += 16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], __uint_as_float(v[e + i]), __uint_as_float(v[e + 8 + i]));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], __uint_as_float(v[120 + i]));
         const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         const float m_blk = mx * sc;
         // raise the running max only when this block would push p above 2^8
@@ -378,17 +384,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // p = 2^(s * scale - m) as bf16 into the swizzled K-major P tile, and the row sum
         const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
         const bool none = m_use == -INFINITY;  // every key so far masked
-        float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial row sums
+        // two keys per instruction where the f32x2 pipe allows (the softmax is issue-bound): packed
+        // s * scale - m and packed partial row sums, the exponentials on the MUFU
+        float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(neg_m, neg_m);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t w[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            float p0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), sc, neg_m));
-            float p1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), sc, neg_m));
-            if (none) p0 = p1 = 0.f;
-            rs8[(e >> 1) & 7] += p0 + p1;
-            w[e / 2] = pack2_bf16(p0, p1);
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c * 32 + e]), __uint_as_float(v[c * 32 + e + 1])),
+                                        sc2, nm2);
+            float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            if (none) pp = make_float2(0.f, 0.f);
+            rs4[(e >> 1) & 3] = __fadd2_rn(rs4[(e >> 1) & 3], pp);
+            w[e / 2] = pack2_bf16(pp.x, pp.y);
           }
           // 32 keys = 64 bytes = 4 chunks of 16 bytes in k-block c / 2, chunk offset (c % 2) * 4
           uint8_t* rowp = myP + (c >> 1) * kTileBytes + r * 128;
@@ -399,7 +409,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
           }
         }
-        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+        l += ((rs4[0].x + rs4[0].y) + (rs4[1].x + rs4[1].y)) + ((rs4[2].x + rs4[2].y) + (rs4[3].x + rs4[3].y));
         // P (and the rescaled O) are ready for the MMA
         tc_fence_before();
         fence_async_smem();
