@@ -140,6 +140,49 @@ def test_image_strips_halo_and_combined_maxima(world):
         assert r[2:] == (True, True, True, True), r
 
 
+def _dead_peer_worker(rank, world, port, q):
+    """Rank 1 leaves (raises) between steps, before the strip exchange; rank 0's next collective must end
+    with an error within the process group's timeout instead of waiting for good."""
+    import datetime
+    import sys
+    import time
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "torch-xdna_b200"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    from torch_xdna import parallel
+
+    top = torch.tensor([5 + rank], dtype=torch.int32)
+    parallel.all_max_(top)  # a step both ranks complete
+    if rank == 1:
+        q.put((1, int(top), "left"))
+        raise SystemExit(3)  # the failure, on the host: this rank never joins the next exchange
+    t0 = time.monotonic()
+    xp = torch.zeros(1, 4, 6, 16, dtype=torch.int8)
+    try:
+        parallel.exchange_halo(xp)
+        outcome = "completed"
+    except Exception as e:  # the timeout surfaces as a RuntimeError from the backend
+        outcome = type(e).__name__
+    q.put((0, int(top), outcome, time.monotonic() - t0))
+
+
+def test_dead_peer_ends_the_exchange_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    assert procs[1].exitcode == 3
+    assert res[0][1] == res[1][1] == 6          # the step before the failure completed on both ranks
+    assert res[0][2] != "completed" and res[0][3] < 60, res[0]
+
+
 def test_shard_rejects_uneven():
     from torch_xdna import parallel
 
