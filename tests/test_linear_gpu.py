@@ -191,6 +191,49 @@ def test_gemm_dequant_bitexact(cuda, out, bias, M, N, K):
     assert bad == 0, f"{bad} of {want.size} dequantised values differ (max abs diff {np.abs(got - want).max()})"
 
 
+SMALL_M = [(1, 6144, 1024), (1, 1024, 3072), (2, 300, 200), (3, 4096, 1024), (5, 7, 7), (8, 1024, 3072),
+           (9, 33, 1040), (17, 520, 1000), (32, 6144, 1024), (31, 100, 16)]
+
+
+@pytest.mark.parametrize("out", ["int32", "float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("M,N,K", SMALL_M)
+def test_small_m_gemm_bitexact(cuda, out, M, N, K):
+    """M <= 8 rows take the dp4a path of xdna_gemm_i8 (larger M the tensor path): the same sums and the same
+    dequantise either way, bit for bit against the oracle. The rows' padding past K holds random bytes, which
+    must not count."""
+    x, w, b = mg.linear_inputs(M * 7 + N + K, M, K, N, bias=True)
+    xq, sx = orc.quant_rows(x)
+    wq, sw = orc.quant_rows(w)
+    g = mg.rng(M + 3 * N)
+    K16 = -(-K // 16) * 16
+    xp = g.integers(-128, 128, (M, K16), dtype=np.int8)
+    xp[:, :K] = xq
+    wp = g.integers(-128, 128, (N, K16), dtype=np.int8)
+    wp[:, :K] = wq
+    if out == "int32":
+        got = gemm_gpu(t(xp, cuda), t(wp, cuda), K, torch.int32).cpu().numpy()
+        want = orc.int_mm(xq, wq)
+    else:
+        bias_v = orc.cast(b, out) if M % 2 else None
+        y = gemm_gpu(t(xp, cuda), t(wp, cuda), K, TORCH_DT[out], t(sx, cuda), t(sw, cuda),
+                     t(bias_v, cuda, TORCH_DT[out]) if bias_v is not None else None)
+        got = y.float().cpu().numpy()
+        want = orc.dequant(orc.int_mm(xq, wq), sx, sw, bias_v, out)
+    bad = int((got != want).sum())
+    assert bad == 0, f"{bad} of {want.size} values differ"
+
+
+def test_small_m_extremes(cuda):
+    """All +-127 operands at M = 4: the largest sums in magnitude through dp4a."""
+    M, N, K = 4, 96, 4096
+    xq = np.full((M, K), 127, np.int8)
+    xq[::2] = -127
+    wq = np.full((N, K), 127, np.int8)
+    wq[:, ::3] = -127
+    acc = gemm_gpu(t(xq, cuda), t(wq, cuda), K, torch.int32).cpu().numpy()
+    assert np.array_equal(acc, orc.int_mm(xq, wq))
+
+
 @pytest.mark.parametrize("name", [c[0] for c in mg.LINEAR_CASES])
 def test_reference_golden_digests(cuda, golden, name):
     """The GPU's int32 sums and dequantised outputs hash to exactly what the reference produced."""

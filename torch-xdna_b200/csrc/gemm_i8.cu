@@ -59,6 +59,132 @@ static bool conv_window() {
   return on;
 }
 
+// ------------------------------------------------------------------ a few rows: dp4a dot products
+// For M <= kGemvMaxM rows the 128-row tensor-core tiles leave most SMs idle and stream the weights at a
+// fraction of HBM bandwidth. Here each warp owns CPW output columns: per step every lane reads 16
+// contiguous weight bytes of each of its columns (512 bytes per column and warp, coalesced) and the MR
+// activation rows' matching 16 bytes (from L1: every warp reads the same rows), and accumulates exact int32
+// sums with __dp4a, two steps' loads in flight. No byte past K of a row is read (the padding may hold
+// anything, or not exist for the last row). The warp then adds its lanes' partial sums (exact in int32) and lane
+// c * MR + m writes y[m, column c]: the sum itself (int32 out) or the GEMM epilogue's arithmetic,
+// fl(fl(float(acc) * sx[m]) * sw[n]) (+ bias[n]), rounded once to the output type.
+// (up to 8 rows: at 8 it matches the tensor path's time at 128 rows, at 32 it takes 2.8x as long)
+constexpr int kGemvMaxM = 8;
+
+// 16 bytes of a row from byte k: a vector load, or for the row's last partial chunk (k + 16 > K) the
+// bytes before K one by one and zeros after them (nothing past byte K of the row is read).
+__device__ __forceinline__ uint4 load_row16(const int8_t* row, int k, int K) {
+  if (k + 16 <= K) return __ldg(reinterpret_cast<const uint4*>(row + k));
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (k + i < K) w[i >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(__ldg(row + k + i))) << (8 * (i & 3));
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int MR, int CPW>
+__global__ void __launch_bounds__(256) gemv_i8_kernel(const int8_t* __restrict__ xq, int64_t ldx,
+                                                      const int8_t* __restrict__ wq, int64_t ldw, int M, int N, int K,
+                                                      const float* __restrict__ sx, const float* __restrict__ sw,
+                                                      const void* __restrict__ bias, int bias_dtype,
+                                                      void* __restrict__ y, int y_dtype, int64_t ldy) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = (blockIdx.x * 8 + warp) * CPW;
+  const int m0 = blockIdx.y * MR;
+  if (n0 >= N) return;  // the whole warp
+  int acc[CPW][MR];
+#pragma unroll
+  for (int c = 0; c < CPW; ++c)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[c][m] = 0;
+  auto step = [&](const uint4 (&wv)[CPW], int k) {
+    uint4 xv[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      xv[m] = m0 + m < M ? load_row16(xq + static_cast<int64_t>(m0 + m) * ldx, k, K) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int c = 0; c < CPW; ++c)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        int s = acc[c][m];
+        s = __dp4a(static_cast<int>(xv[m].x), static_cast<int>(wv[c].x), s);
+        s = __dp4a(static_cast<int>(xv[m].y), static_cast<int>(wv[c].y), s);
+        s = __dp4a(static_cast<int>(xv[m].z), static_cast<int>(wv[c].z), s);
+        s = __dp4a(static_cast<int>(xv[m].w), static_cast<int>(wv[c].w), s);
+        acc[c][m] = s;
+      }
+  };
+  auto load_w = [&](uint4 (&wv)[CPW], int k) {
+#pragma unroll
+    for (int c = 0; c < CPW; ++c)
+      wv[c] = (k < K && n0 + c < N) ? load_row16(wq + static_cast<int64_t>(n0 + c) * ldw, k, K)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+  };
+  for (int k = lane * 16; k < K; k += 1024) {
+    uint4 wa[CPW], wb[CPW];
+    load_w(wa, k);
+    load_w(wb, k + 512);
+    step(wa, k);
+    if (k + 512 < K) step(wb, k + 512);
+  }
+#pragma unroll
+  for (int c = 0; c < CPW; ++c)
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) acc[c][m] += __shfl_xor_sync(kFull, acc[c][m], s);
+  int mine = 0;
+#pragma unroll
+  for (int c = 0; c < CPW; ++c)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) mine = lane == c * MR + m ? acc[c][m] : mine;
+  const int c = lane / MR, m = lane % MR;
+  const int n = n0 + c, row = m0 + m;
+  if (c >= CPW || n >= N || row >= M) return;
+  const int64_t off = static_cast<int64_t>(row) * ldy + n;
+  if (y_dtype == XDNA_I32) {
+    static_cast<int32_t*>(y)[off] = mine;
+    return;
+  }
+  float v = __fmul_rn(__fmul_rn(__int2float_rn(mine), __ldg(sx + row)), __ldg(sw + n));
+  if (bias != nullptr) v = __fadd_rn(v, load_as_float(bias, bias_dtype, n));
+  store_one(y, y_dtype, off, v);
+}
+
+template <int MR>
+static int launch_gemv_mr(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, int M, int N, int K,
+                          const float* sx, const float* sw, const void* bias, int bias_dtype, void* y, int y_dtype,
+                          int64_t ldy, int sms, cudaStream_t s) {
+  const int passes = (M + MR - 1) / MR;
+  auto blocks = [&](int cpw) { return (N + 8 * cpw - 1) / (8 * cpw); };
+  // as many columns per warp as still fill the GPU (more loads in flight per lane)
+  // (at most 2 for 8 rows: 4 x 8 sums and their operands spill)
+  const int cpw = MR < 8 && static_cast<int64_t>(blocks(4)) * passes >= sms ? 4
+                  : static_cast<int64_t>(blocks(2)) * passes >= sms ? 2 : 1;
+  const dim3 grid(blocks(cpw), passes);
+  if constexpr (MR < 8) {
+    if (cpw == 4) {
+      gemv_i8_kernel<MR, 4><<<grid, 256, 0, s>>>(xq, ldx, wq, ldw, M, N, K, sx, sw, bias, bias_dtype, y, y_dtype, ldy);
+      return check_launch("gemv_i8_kernel");
+    }
+  }
+  if (cpw == 2)
+    gemv_i8_kernel<MR, 2><<<grid, 256, 0, s>>>(xq, ldx, wq, ldw, M, N, K, sx, sw, bias, bias_dtype, y, y_dtype, ldy);
+  else
+    gemv_i8_kernel<MR, 1><<<grid, 256, 0, s>>>(xq, ldx, wq, ldw, M, N, K, sx, sw, bias, bias_dtype, y, y_dtype, ldy);
+  return check_launch("gemv_i8_kernel");
+}
+
+static int launch_gemv(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, int M, int N, int K,
+                       const float* sx, const float* sw, const void* bias, int bias_dtype, void* y, int y_dtype,
+                       int64_t ldy, int sms, cudaStream_t s) {
+  if (M <= 1) return launch_gemv_mr<1>(xq, ldx, wq, ldw, M, N, K, sx, sw, bias, bias_dtype, y, y_dtype, ldy, sms, s);
+  if (M <= 2) return launch_gemv_mr<2>(xq, ldx, wq, ldw, M, N, K, sx, sw, bias, bias_dtype, y, y_dtype, ldy, sms, s);
+  if (M <= 4) return launch_gemv_mr<4>(xq, ldx, wq, ldw, M, N, K, sx, sw, bias, bias_dtype, y, y_dtype, ldy, sms, s);
+  return launch_gemv_mr<8>(xq, ldx, wq, ldw, M, N, K, sx, sw, bias, bias_dtype, y, y_dtype, ldy, sms, s);
+}
+
 // Widest tile that still gives every SM work; 64 for narrow outputs.
 static int choose_bn(int64_t m_tiles, int64_t N, int sms) {
   if (N <= 64) return 64;
@@ -99,6 +225,9 @@ int xdna_gemm_i8(const int8_t* xq, int64_t ldx, const int8_t* wq, int64_t ldw, i
     XDNA_CHECK_ARG(bias == nullptr || is_float_dtype(bias_dtype), "gemm_i8: bias dtype %d", bias_dtype);
   }
   XDNA_CHECK_ARG(ldx % 16 == 0 && ldw % 16 == 0, "gemm_i8: int8 row pitch must be a multiple of 16 bytes");
+  if (M <= kGemvMaxM && aligned16(xq) && aligned16(wq))
+    return launch_gemv(xq, ldx, wq, ldw, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), sx, sw, bias,
+                       bias_dtype, y, y_dtype, ldy, sms, s);
 
   GemmArgs a{};
   a.M = static_cast<int>(M);
