@@ -74,8 +74,8 @@ def parse():
                          "(default: peer blocks copied over NVLink once, overlapping the GEMM), read by the GEMM's "
                          "TMA straight from peer memory, after an NCCL all-gather; or data-parallel with the sequences")
     ap.add_argument("--kernel", default=None,
-                    choices=["gemm_i8", "quant_rows", "conv3x3", "conv3x3_chain", "attention", "gemm_bf16",
-                             "gemm_bf16_qkv"],
+                    choices=["gemm_i8", "quant_rows", "conv3x3", "conv3x3_chain", "conv_quant_codes", "attention",
+                             "gemm_bf16", "gemm_bf16_qkv"],
                     help="time one kernel on --shape instead of a workload (profiling)")
     ap.add_argument("--shape", default="8192,6144,1024", help="--kernel shape, comma-separated")
     return ap.parse_args()
@@ -125,6 +125,12 @@ def peaks():
 
 
 INT8_PEAK_NOTE = "int8 peak = 2 x the measured dense bf16 cuBLAS burst (B200's dense int8 rate is twice its bf16 rate)"
+
+
+# DRAM bytes of one launch of the chained conv1_2 (32 images, 64 -> 64, 224 x 224), from an ncu capture of
+# `bench.py --kernel conv3x3_chain --shape 32,64,224`: reads 109.06 MB + writes 59.85 MB (the rest of the
+# codes is still in L2 when the kernel ends)
+CONV_CHAIN_DRAM_BYTES_32 = 109_064_192 + 59_851_520
 
 
 def roof(bound, kernel, achieved, peak, unit, per_launch_ms, **extra):
@@ -646,7 +652,11 @@ def conv_record(args, rank, world, dev, flush):
            "gpu_launches": per_step * args.steps,
            "roofline": roof("tensor", "umma_gemm_kernel conv (conv 64->64 224x224 as chained: int8 codes out, next "
                             "layer's pooled per-image maxima in the epilogue)", conv_ops / ms / 1e9, int8_peak, "TOPS",
-                            ms, peak_source=INT8_PEAK_NOTE, traffic=None),
+                            ms, peak_source=INT8_PEAK_NOTE, traffic=round(CONV_CHAIN_DRAM_BYTES_32 * N / 32),
+                            traffic_source="ncu capture of bench.py --kernel conv3x3_chain --shape 32,64,224 "
+                                           "(dram__bytes_read.sum + dram__bytes_write.sum, scaled to this rank's "
+                                           "images), not measured by this run",
+                            algorithmic_bytes=N * (226 * 226 * 64 + 224 * 224 * 64)),
            "roofline_dequant_f32": roof("tensor", "umma_gemm_kernel conv (conv 64->64 224x224, f32 out, dequantise "
                                         "epilogue, bias + ReLU)", conv_ops / ms_f32 / 1e9, int8_peak, "TOPS", ms_f32,
                                         peak_source=INT8_PEAK_NOTE, traffic=None),
@@ -1227,6 +1237,19 @@ def run_kernel(args):
         fn = lambda: kernels.conv3x3(xp, lay.wp, N, C, C, H, H, mode, shift=10, scale=lay.scale, sx=sx,  # noqa
                                      bias=b, out=q, acc_max=amax)
         work, unit = 2 * N * C * C * H * H * 9, "TOPS"
+    elif args.kernel == "conv_quant_codes":           # N, C, H[, 1]: the chain's quantise from int8 codes [N, H, H, C]
+        N, C, H = shp[:3]                              # (ReLU after the bias, maxima given); 1: 2x2 pool first
+        pool = len(shp) > 3 and shp[3] == 1
+        q = torch.randint(-128, 128, (N, H, H, C), dtype=torch.int8, device=dev, generator=g)
+        scale = torch.rand(C, device=dev, generator=g) * 1e-3 + 1e-4
+        sx_in = torch.rand(N, device=dev, generator=g) + 0.5
+        b = torch.randn(C, device=dev, generator=g) * 0.05
+        Ho = H // 2 if pool else H
+        xp = torch.empty(N, Ho + 2, Ho + 2, xconv.channels_padded(C), dtype=torch.int8, device=dev)
+        sx = torch.empty(N, device=dev)
+        amax = torch.full((N,), 0x3F800000, dtype=torch.int32, device=dev)   # 1.0f
+        fn = lambda: kernels.conv_quant_codes_given_amax(q, scale, sx_in, b, True, pool, xp, sx, amax)  # noqa
+        work, unit = q.numel() + xp.numel(), "GB/s"
     elif args.kernel == "attention":                  # B, L: causal, 16 q heads / 8 kv heads of 128
         B, L = shp
         qk = torch.randn(B * L, 3072, device=dev, generator=g).to(torch.bfloat16)
