@@ -630,18 +630,22 @@ def conv_record(args, rank, world, dev, flush):
     # chain runs it: int8 codes out, the next layer's per-image maxima over the 2x2 pool's region in the epilogue
     lay = xconv._layer(params[1][0], 224, 224, False)
     xp = torch.randint(-127, 128, (N, 226, 226, lay.cp), dtype=torch.int8, device=dev)
+    xp2 = torch.randint(-127, 128, (N // 2, 226, 226, 128), dtype=torch.int8, device=dev) if N % 2 == 0 else None
     sx = torch.rand(N, device=dev) + 0.5
     bias = params[1][1].detach().float().contiguous()
     qo = torch.empty(N, 224, 224, 64, dtype=torch.int8, device=dev)
     amax = torch.empty(N, dtype=torch.int32, device=dev)
-    chain_mode = kernels.CONV_Q_NHWC | kernels.CONV_NEXT_AMAX | kernels.CONV_NEXT_RELU | kernels.CONV_NEXT_POOL
-    ms = event_ms(lambda: kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, chain_mode | lay.mode_flag,
+    # as the chain runs it: the input in image pairs when the rank holds an even number of images
+    chain_mode = (kernels.CONV_Q_NHWC | kernels.CONV_NEXT_AMAX | kernels.CONV_NEXT_RELU | kernels.CONV_NEXT_POOL
+                  | (kernels.CONV_PAIRS if xp2 is not None else 0))
+    ms = event_ms(lambda: kernels.conv3x3(xp2 if xp2 is not None else xp, lay.wp, N, 64, 64, 224, 224,
+                                          chain_mode | lay.mode_flag,
                                           shift=lay.shift, scale=lay.scale, sx=sx, bias=bias, out=qo, acc_max=amax), 5)
     yo = torch.empty(N, 64, 224, 224, device=dev, memory_format=torch.channels_last)
     ms_f32 = event_ms(lambda: kernels.conv3x3(xp, lay.wp, N, 64, 64, 224, 224, kernels.CONV_DEQUANT | lay.mode_flag,
                                               shift=lay.shift, scale=lay.scale, sx=sx, bias=params[1][1],
                                               relu=kernels.RELU_AFTER_BIAS, out=yo), 5)
-    del xp, yo, qo
+    del xp, xp2, yo, qo
     conv_ops = 2 * N * 224 * 224 * 64 * 64 * 9
     rec = {"metric": CONV_METRIC, "value": round(2 * vgg_macs(N_all) * args.steps / total_s / 1e12, 2), "unit": "TOPS",
            "ms_per_step": round(total_s * 1e3 / args.steps, 3), "scaling": "strong", "dtype": "int8",
@@ -650,8 +654,9 @@ def conv_record(args, rank, world, dev, flush):
                       else "int8 codes (pool on the codes)", "global_batch": N_all,
                       "parallelism": f"dp{world} (images)", "l2": "activations exceed L2"},
            "gpu_launches": per_step * args.steps,
-           "roofline": roof("tensor", "umma_gemm_kernel conv (conv 64->64 224x224 as chained: int8 codes out, next "
-                            "layer's pooled per-image maxima in the epilogue)", conv_ops / ms / 1e9, int8_peak, "TOPS",
+           "roofline": roof("tensor", "umma_gemm_kernel conv (conv 64->64 224x224 as chained: image pairs in, int8 "
+                            "codes out, next layer's pooled per-image maxima in the epilogue)", conv_ops / ms / 1e9,
+                            int8_peak, "TOPS",
                             ms, peak_source=INT8_PEAK_NOTE, traffic=round(CONV_CHAIN_DRAM_BYTES_32 * N / 32),
                             traffic_source="ncu capture of bench.py --kernel conv3x3_chain --shape 32,64,224 "
                                            "(dram__bytes_read.sum + dram__bytes_write.sum, scaled to this rank's "
@@ -1229,11 +1234,15 @@ def run_kernel(args):
         w = torch.nn.Parameter(torch.randn(C, C, 3, 3, device=dev, generator=g) * (2 / (C * 9)) ** 0.5)
         lay = xconv.ConvLayer(w, H, H, False)
         lay.shift, lay.scale = 10, lay.sw * 1024.0
-        xp = torch.randint(-127, 128, (N, H + 2, H + 2, lay.cp), dtype=torch.int8, device=dev, generator=g)
+        pairs = C == 64 and N % 2 == 0    # the chain's 64-channel input: two images per 128-byte row
+        xp = (torch.randint(-127, 128, (N // 2, H + 2, H + 2, 128), dtype=torch.int8, device=dev, generator=g)
+              if pairs else torch.randint(-127, 128, (N, H + 2, H + 2, lay.cp), dtype=torch.int8, device=dev,
+                                          generator=g))
         sx, b = torch.rand(N, device=dev) + 0.5, torch.randn(C, device=dev) * 0.01
         q = torch.empty(N, H, H, C, dtype=torch.int8, device=dev)
         amax = torch.empty(N, dtype=torch.int32, device=dev)
-        mode = kernels.CONV_Q_NHWC | kernels.CONV_NEXT_AMAX | kernels.CONV_NEXT_RELU | kernels.CONV_NEXT_POOL
+        mode = (kernels.CONV_Q_NHWC | kernels.CONV_NEXT_AMAX | kernels.CONV_NEXT_RELU | kernels.CONV_NEXT_POOL
+                | (kernels.CONV_PAIRS if pairs else 0))
         fn = lambda: kernels.conv3x3(xp, lay.wp, N, C, C, H, H, mode, shift=10, scale=lay.scale, sx=sx,  # noqa
                                      bias=b, out=q, acc_max=amax)
         work, unit = 2 * N * C * C * H * H * 9, "TOPS"

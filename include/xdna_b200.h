@@ -81,6 +81,10 @@ extern "C" {
  * image's sx), from xdna_conv_bias_int32; the sums become acc + bias[n][co] in every mode (the calibration's
  * max included), and DEQUANT adds no float bias. |acc| must stay below 2^31 - 3 * 2^29 (K * 127^2 < 5.3e8). */
 #define XDNA_CONV_BIAS_INT32 512
+/* Or'ed into XDNA_CONV_Q_NHWC for a stride-1 3x3 conv with Cp = 64, Co <= 128 and an even N: xp holds the
+ * images in pairs, [N/2, H+2, W+2, 128] (bytes 0..63 of a row: image 2i's channels, 64..127: image 2i+1's;
+ * xdna_conv_quant_codes_pairs writes it), which halves the TMA row requests of the conv's loads. */
+#define XDNA_CONV_PAIRS 1024
 /* `relu` of xdna_conv3x3_i8: 0 none; 1 fused into the requantise ([0,255] uint8, the reference's ReLU of
  * a bias-free conv); XDNA_RELU_AFTER_BIAS (DEQUANT only) applied to the dequantised output after the
  * bias, the requantise saturating to int8 — the same values as torch.relu on the DEQUANT output. */
@@ -199,6 +203,13 @@ int xdna_conv_quant_codes(const void* q, int q_unsigned, int64_t N, int64_t C, i
 
 /* xdna_conv_quant_codes with the per-image maxima already known (amax [N], the bit patterns the producing
  * conv wrote with XDNA_CONV_NEXT_AMAX, XDNA_CONV_NEXT_POOL iff pool): one pass over the codes instead of two. */
+/* xdna_conv_quant_codes into the image-pair layout XDNA_CONV_PAIRS reads: xp [N/2, H'+2, W'+2, 128], image n's
+ * channels at bytes 64 * (n % 2) .. of each pair row. C = 64, N even. amax: N words; with amax_given the
+ * per-image maxima the producing conv wrote (XDNA_CONV_NEXT_AMAX), else scratch this call fills. */
+int xdna_conv_quant_codes_pairs(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
+                                const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,
+                                int8_t* xp, float* sx_out, uint32_t* amax, int amax_given, void* stream);
+
 /* The int32 bias of XDNA_CONV_BIAS_INT32: out[n][co] = rint(bias[co] / (sw[co] * sx[n])) in f32 (the product
  * and the quotient correctly rounded, rint to nearest even), clamped to [-2^29, 2^29], NaN -> 0. bias: Co
  * values of bias_dtype (f32 / bf16 / f16); sw: the layer's weight scales [Co]; sx: the images' scales [N]. */

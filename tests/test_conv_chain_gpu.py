@@ -29,11 +29,14 @@ def _weights(dev, g, shapes, biased):
     return out
 
 
-# (channels per conv, bias per conv, pool before conv i, H, W)
+# (channels per conv, bias per conv, pool before conv i, H, W, images)
 CASES = [
-    ([(64, 3), (64, 64), (128, 64), (128, 128)], [True, True, True, False], [False, False, True, False], 32, 48),
+    ([(64, 3), (64, 64), (128, 64), (128, 128)], [True, True, True, False], [False, False, True, False], 32, 48, 3),
     # odd sizes: the pool rounds down (15 x 17 -> 7 x 8); 20 channels: scalar stores of the codes
-    ([(20, 8), (32, 20), (16, 32)], [True, False, True], [False, True, False], 15, 17),
+    ([(20, 8), (32, 20), (16, 32)], [True, False, True], [False, True, False], 15, 17, 3),
+    # an even batch: the 64-channel convs read their input in image pairs (XDNA_CONV_PAIRS), pooled or not
+    ([(64, 3), (64, 64), (128, 64), (64, 128), (64, 64)], [True, True, True, False, True],
+     [False, False, True, False, True], 30, 26, 4),
 ]
 
 
@@ -47,10 +50,10 @@ def test_chain_equals_unchained(cuda, case, verify, hint, bint):
     unpooled image and makes its own two passes. bint: Config(conv_bias_int32=True) on both routes."""
     from torch_xdna.conv import IN_CODES, IN_CODES_POOL, IN_FLOAT
 
-    shapes, biased, pools, H, W = CASES[case]
+    shapes, biased, pools, H, W, nimg = CASES[case]
     g = torch.Generator(device=cuda).manual_seed(7 + case)
     layers = _weights(cuda, g, shapes, biased)
-    x = torch.randn(3, shapes[0][1], H, W, device=cuda, generator=g)
+    x = torch.randn(nimg, shapes[0][1], H, W, device=cuda, generator=g)
     cid = _cid(verify=verify, conv_bias_int32=bint)
     # one by one: a biased conv's ReLU after its bias, a bias-free conv's ReLU in the requantise
     y = x
@@ -126,6 +129,53 @@ def test_next_layer_maxima_from_the_producer(cuda, shape, kind, pool):
     kernels.conv_quant_codes(*args, xa, sa, scratch)
     kernels.conv_quant_codes_given_amax(*args, xb, sb, amax)
     assert torch.equal(sa, sb) and torch.equal(xa, xb)
+
+
+@pytest.mark.parametrize("shape", [(2, 64, 15, 17), (4, 128, 30, 22), (6, 64, 3, 4), (2, 128, 112, 112)])
+@pytest.mark.parametrize("kind", ["relu_after_bias", "fused_relu", "signed"])
+def test_image_pairs_equal_the_plain_layout(cuda, shape, kind):
+    """XDNA_CONV_PAIRS: the same conv over the input interleaved two images per 128-byte row gives the same
+    codes and the same next-layer maxima as over the plain layout; conv_quant_codes_pairs writes exactly the
+    interleave of conv_quant_codes' output."""
+    from torch_xdna import conv as xconv
+    from torch_xdna import kernels
+
+    n, co, h, w = shape
+    g = torch.Generator(device=cuda).manual_seed(n + co + h + len(kind))
+    wt = torch.randn(co, 64, 3, 3, device=cuda, generator=g) * (2.0 / (64 * 9)) ** 0.5
+    fused = kind == "fused_relu"
+    bias = None if fused else torch.randn(co, device=cuda, generator=g) * 0.05
+    relu_after = kind == "relu_after_bias"
+    # the input: a previous conv's codes, quantised both ways
+    qin = torch.randint(0 if fused else -128, 256 if fused else 128, (n, h, w, 64), device=cuda, generator=g)
+    qin = qin.to(torch.uint8 if fused else torch.int8)
+    scale_in = torch.rand(64, device=cuda, generator=g) * 1e-3 + 1e-4
+    sx_in = torch.rand(n, device=cuda, generator=g) + 0.5
+    b_in = torch.randn(64, device=cuda, generator=g) * 0.05
+    xp = torch.empty(n, h + 2, w + 2, 64, dtype=torch.int8, device=cuda)
+    sx = torch.empty(n, device=cuda)
+    kernels.conv_quant_codes(qin, scale_in, sx_in, b_in, True, False, xp, sx, torch.empty(n, dtype=torch.int32,
+                                                                                           device=cuda))
+    xp2 = torch.empty(n // 2, h + 2, w + 2, 128, dtype=torch.int8, device=cuda)
+    sx2 = torch.empty(n, device=cuda)
+    kernels.conv_quant_codes_pairs(qin, scale_in, sx_in, b_in, True, False, xp2, sx2,
+                                   torch.empty(n, dtype=torch.int32, device=cuda), False)
+    assert torch.equal(sx, sx2)
+    assert torch.equal(xp2.view(n // 2, h + 2, w + 2, 2, 64).permute(0, 3, 1, 2, 4).reshape(xp.shape), xp)
+    layer = xconv.ConvLayer(wt, h, w, fused)
+    layer.calibrate(xp)
+    mode = kernels.CONV_Q_NHWC
+    if kind != "signed":
+        mode |= kernels.CONV_NEXT_AMAX | (kernels.CONV_NEXT_RELU if relu_after else 0)
+    outs = []
+    for src, extra in ((xp, 0), (xp2, kernels.CONV_PAIRS)):
+        q = torch.empty((n, h, w, co), dtype=torch.uint8 if fused else torch.int8, device=cuda)
+        amax = torch.zeros(n, dtype=torch.int32, device=cuda)
+        kernels.conv3x3(src, layer.wp, n, 64, co, h, w, mode | extra, shift=layer.shift, relu=fused,
+                        scale=layer.scale, sx=sx, bias=bias, out=q, acc_max=amax if kind != "signed" else None)
+        outs.append((q, amax))
+    assert torch.equal(outs[0][0], outs[1][0]), f"{int((outs[0][0] != outs[1][0]).sum())} codes differ"
+    assert torch.equal(outs[0][1], outs[1][1])
 
 
 def test_compiled_vgg_block_chained_equals_unchained(cuda):

@@ -324,8 +324,13 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   const bool next_relu = (mode & XDNA_CONV_NEXT_RELU) != 0;
   const bool next_pool = (mode & XDNA_CONV_NEXT_POOL) != 0;
   const bool bias_i32 = (mode & XDNA_CONV_BIAS_INT32) != 0;
+  const bool pimg = (mode & XDNA_CONV_PAIRS) != 0;
   mode &= ~(XDNA_CONV_SINGLE_TAP | XDNA_CONV_STRIDE2 | XDNA_CONV_NEXT_AMAX | XDNA_CONV_NEXT_RELU | XDNA_CONV_NEXT_POOL |
-            XDNA_CONV_BIAS_INT32);
+            XDNA_CONV_BIAS_INT32 | XDNA_CONV_PAIRS);
+  XDNA_CHECK_ARG(!pimg || (mode == XDNA_CONV_Q_NHWC && Cp == 64 && N % 2 == 0 && !single_tap && !stride2 && Co <= 128 &&
+                           conv_window()),
+                 "conv3x3: XDNA_CONV_PAIRS needs XDNA_CONV_Q_NHWC, Cp = 64, an even N, a stride-1 3x3 conv and "
+                 "Co <= 128");
   XDNA_CHECK_ARG(!bias_i32 || (bias != nullptr && bias_dtype == XDNA_I32),
                  "conv3x3: XDNA_CONV_BIAS_INT32 needs an int32 bias [N, Co]");
   XDNA_CHECK_ARG(bias_i32 || bias == nullptr || is_float_dtype(bias_dtype), "conv3x3: a float bias (or XDNA_CONV_BIAS_INT32)");
@@ -365,11 +370,11 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   // rows of the activation matrix: one bordered image per image, or for a stride-2 conv the phase planes
   // (4, or the even-even plane alone for the 1x1 conv), each n_in bordered images of the output's geometry
   const int planes = stride2 ? (single_tap ? 1 : 4) : 1;
-  const int64_t a_rows = stride2 ? planes * n_in * HWp : NP;
+  const int64_t a_rows = stride2 ? planes * n_in * HWp : pimg ? NP / 2 : NP;  // pairs: one row per two images
   XDNA_CHECK_ARG(a_rows < (1ll << 31) && Co * Cp * 9 < (1ll << 31), "conv3x3: problem exceeds 2^31 elements");
 
   GemmArgs a{};
-  a.M = static_cast<int>(NP);
+  a.M = static_cast<int>(pimg ? NP / 2 : NP);  // pairs: the tiles run over pair rows, each two images' pixel
   a.N = static_cast<int>(Co);
   const int kb = Cp <= 64 ? 64 : kBKBytes;  // K block bytes (= channels) per tap
   a.cblocks = static_cast<int>((Cp + kb - 1) / kb);
@@ -390,7 +395,7 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   // channels) loads one window of kBM + 2 rows per ky, which its three kx taps share (LOAD_CONV_WIN)
   const bool win = conv_window() && kb == 64 && a.cblocks == 1 && a.ntaps == 9 && !stride2 && Co <= 128;
   if (win) a.num_kb = 3;
-  a.m_tiles = static_cast<int>((NP + kBM - 1) / kBM);
+  a.m_tiles = static_cast<int>((a.M + kBM - 1) / kBM);
   const int bn = choose_bn(a.m_tiles, Co, sms);
   a.n_tiles = static_cast<int>((Co + bn - 1) / bn);
   // 256 x 256 tiles on CTA pairs for wide convs (not the calibration, which runs one image)
@@ -427,11 +432,13 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
 
   CUtensorMap ta, tb;
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(Cp), static_cast<uint64_t>(a_rows)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(Cp)};
-    const uint32_t box[2] = {static_cast<uint32_t>(kb), win ? kBM + 2 : kBM};
+    // pairs: rows of 128 bytes, images 2i and 2i + 1 side by side
+    const uint64_t row_bytes = pimg ? 2 * Cp : Cp;
+    const uint64_t dims[2] = {row_bytes, static_cast<uint64_t>(a_rows)};
+    const uint64_t strides[1] = {row_bytes};
+    const uint32_t box[2] = {static_cast<uint32_t>(pimg ? 128 : kb), win ? kBM + 2 : kBM};
     rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations",
-                    kb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+                    kb == 64 && !pimg ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != XDNA_OK) return rc;
   }
   {
@@ -449,6 +456,10 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
     case XDNA_CONV_DEQUANT:
       return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, pair, win, ta, tb, a, sms, s);
     case XDNA_CONV_Q_NHWC:
+      if (pimg) {
+        if (bn == 128) return launch_umma<128, LOAD_CONV_WIN2, EPI_CONV_QNHWC, false, XDNA_I8, 64>(ta, tb, ta, a, sms, s);
+        return launch_umma<64, LOAD_CONV_WIN2, EPI_CONV_QNHWC, false, XDNA_I8, 64>(ta, tb, ta, a, sms, s);
+      }
       return dispatch_conv<EPI_CONV_QNHWC, XDNA_I8>(kb, bn, pair, win, ta, tb, a, sms, s);
     default:
       return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, false, win, ta, tb, a, sms, s);

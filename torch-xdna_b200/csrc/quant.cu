@@ -603,7 +603,9 @@ __global__ void __launch_bounds__(256) codes_to_bordered_kernel(const uint32_t* 
 // walks several bordered rows of one image. A code becomes a float exactly through the 2^23 bias (the
 // bit pattern 0x4B000000 + u is 2^23 + u; a signed code is stored as u = code + 128 first); then
 // y = fl(q * t[c]) + b[c] (+0 without a bias: the same quantised byte), the ReLU, round(y / s) as quant_t.
-template <bool POOL, bool USGN>
+// PAIRS: xp holds the images in pairs, [N/2, Ho+2, Wo+2, 2 x C] (XDNA_CONV_PAIRS): image n's bytes of a pixel
+// are the (n % 2)-th C of the pair row.
+template <bool POOL, bool USGN, bool PAIRS = false>
 __global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* __restrict__ q, int H, int W, int C,
                                                                   const float* __restrict__ scale,
                                                                   const float* __restrict__ sx_in,
@@ -663,7 +665,9 @@ __global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* _
   };
   constexpr int U = POOL ? 2 : 4;  // 16-byte vectors per thread in flight (a pooled one is four loads)
   for (int yb = blockIdx.x; yb < Ho + 2; yb += gridDim.x) {
-    uint4* dst = xp + (static_cast<int64_t>(n) * (Ho + 2) + yb) * per_row;
+    // this image's row: plain, or every other C bytes of its pair's row
+    uint4* dst = PAIRS ? xp + (static_cast<int64_t>(n >> 1) * (Ho + 2) + yb) * 2 * per_row + (n & 1) * C16
+                       : xp + (static_cast<int64_t>(n) * (Ho + 2) + yb) * per_row;
     const bool border_row = yb == 0 || yb == Ho + 1;
     for (int e0 = threadIdx.x; e0 < per_row; e0 += U * blockDim.x) {
       uint4 u[U];
@@ -678,7 +682,7 @@ __global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* _
 #pragma unroll
       for (int j = 0; j < U; ++j) {
         const int e = e0 + j * blockDim.x;
-        if (e < per_row) dst[e] = in[j] ? convert(u[j]) : make_uint4(0u, 0u, 0u, 0u);
+        if (e < per_row) dst[PAIRS ? e + (e / C16) * C16 : e] = in[j] ? convert(u[j]) : make_uint4(0u, 0u, 0u, 0u);
       }
     }
   }
@@ -687,7 +691,7 @@ __global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* _
 template <bool POOL, bool USGN>
 static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const float* scale, const float* sx_in,
                          const float* bias, int relu_after, int Cp, uint32_t* amax, int8_t* xp, float* sx_out,
-                         cudaStream_t s, bool amax_given = false) {
+                         cudaStream_t s, bool amax_given = false, bool pairs = false) {
   const int Ho = POOL ? H / 2 : H;
   const int64_t per = static_cast<int64_t>(Ho) * (POOL ? W / 2 : W) * C4;
   const int chunks = static_cast<int>(std::min<int64_t>((per + 256 * 8 - 1) / (256 * 8), 1024));
@@ -698,9 +702,14 @@ static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const f
   if (pow2 && Cp == C && reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(xp) % 16 == 0) {
     // one wave: three resident blocks per SM over all images, each walking several rows
     const int blocks = std::max(1, std::min(Ho + 2, 148 * 3 / std::max(N, 1)));
-    codes_to_bordered16_kernel<POOL, USGN><<<dim3(blocks, N), 256, 0, s>>>(
-        reinterpret_cast<const uint4*>(q), H, W, C, scale, sx_in, bias, relu_after, amax, reinterpret_cast<uint4*>(xp),
-        sx_out);
+    if (pairs)
+      codes_to_bordered16_kernel<POOL, USGN, true><<<dim3(blocks, N), 256, 0, s>>>(
+          reinterpret_cast<const uint4*>(q), H, W, C, scale, sx_in, bias, relu_after, amax,
+          reinterpret_cast<uint4*>(xp), sx_out);
+    else
+      codes_to_bordered16_kernel<POOL, USGN><<<dim3(blocks, N), 256, 0, s>>>(
+          reinterpret_cast<const uint4*>(q), H, W, C, scale, sx_in, bias, relu_after, amax,
+          reinterpret_cast<uint4*>(xp), sx_out);
   } else {
     codes_to_bordered_kernel<POOL, USGN>
         <<<dim3(Ho + 2, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, Cp, amax, xp, sx_out);
@@ -987,6 +996,38 @@ int xdna_conv_bias_int32(const void* bias, int bias_dtype, const float* sw, cons
       return fail(XDNA_ERR_INVALID, "conv_bias_int32: bias_dtype %d is not f32/bf16/f16", bias_dtype);
   }
   return check_launch("conv bias to int32");
+}
+
+int xdna_conv_quant_codes_pairs(const void* q, int q_unsigned, int64_t N, int64_t C, int64_t H, int64_t W,
+                                const float* scale, const float* sx_in, const float* bias, int relu_after, int pool,
+                                int8_t* xp, float* sx_out, uint32_t* amax, int amax_given, void* stream) {
+  int rc = check_device(nullptr);
+  if (rc != XDNA_OK) return rc;
+  XDNA_CHECK_ARG(N >= 0 && N % 2 == 0 && C == 64 && H >= 1 && W >= 1,
+                 "conv_quant_codes_pairs: bad shape (64 channels, an even number of images)");
+  XDNA_CHECK_ARG(!pool || (H >= 2 && W >= 2), "conv_quant_codes_pairs: a 2x2 pool needs H, W >= 2");
+  XDNA_CHECK_ARG(N <= 65535 && H + 2 <= 65535 && N * H * W * C < (1ll << 40), "conv_quant_codes_pairs: too large");
+  if (N == 0) return XDNA_OK;
+  XDNA_CHECK_ARG(q && scale && sx_in && xp && sx_out && amax, "conv_quant_codes_pairs: null pointer");
+  XDNA_CHECK_ARG(aligned16(q) && aligned16(xp), "conv_quant_codes_pairs: q and xp must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint32_t* qw = static_cast<const uint32_t*>(q);
+  const int n = static_cast<int>(N), h = static_cast<int>(H), w = static_cast<int>(W), c4 = 16;
+  const int ra = relu_after ? 1 : 0;
+  const bool given = amax_given != 0;
+  if (!given) XDNA_CUDA(cudaMemsetAsync(amax, 0, N * sizeof(uint32_t), s));
+  if (pool) {
+    if (q_unsigned)
+      launch_codes<true, true>(qw, n, h, w, c4, scale, sx_in, bias, ra, 64, amax, xp, sx_out, s, given, true);
+    else
+      launch_codes<true, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, 64, amax, xp, sx_out, s, given, true);
+  } else {
+    if (q_unsigned)
+      launch_codes<false, true>(qw, n, h, w, c4, scale, sx_in, bias, ra, 64, amax, xp, sx_out, s, given, true);
+    else
+      launch_codes<false, false>(qw, n, h, w, c4, scale, sx_in, bias, ra, 64, amax, xp, sx_out, s, given, true);
+  }
+  return check_launch("conv quantise (int8 codes, image pairs)");
 }
 
 int xdna_conv_quant_channels_last(const void* x, int x_dtype, int64_t N, int64_t C, int64_t H, int64_t W,

@@ -389,6 +389,11 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// A 128-byte-swizzled matrix that starts some 128-byte rows (and K bytes) into a 1024-byte swizzle atom, as
+// smem_desc_k_sw64_at: the swizzle is a function of the absolute address, which TMA used when it wrote the
+// rows (checked bit for bit against the CPU integers by the conv tests).
+__device__ __forceinline__ uint64_t smem_desc_k_sw128_at(uint32_t smem_addr) { return smem_desc_k_sw128(smem_addr); }
+
 // Instruction descriptor, kind::i8: D s32, A/B signed 8-bit, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
   return (2u << 4)                               // D format: S32

@@ -34,7 +34,12 @@ namespace xdna {
 // LOAD_CONV_WIN: LOAD_CONV_RB for a stride-1 3x3 conv whose stages each hold one window of kBM + 2 activation
 // rows per ky: the ky's three kx taps read it at row offsets 0, 1 and 2 (their MMA descriptors start one or
 // two 64-byte rows into the window), so each row is requested from TMA once per ky instead of once per tap.
-enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1, LOAD_CONV_RB = 2, LOAD_CONV_WIN = 3 };
+// LOAD_CONV_WIN2: LOAD_CONV_WIN over an input whose images are interleaved in pairs ([N/2, H+2, W+2, 2 x 64]:
+// each 128-byte row holds one pixel of images 2i and 2i+1), so a window row request brings 128 bytes where
+// LOAD_CONV_WIN's brings 64: half the TMA row requests, the mainloop's bound for 64-channel convs. Each kx
+// tap issues the MMAs of both images, reading K bytes 0..63 (image 2i) and 64..127 (image 2i+1) of the
+// rows into two accumulators; the epilogue drains both (int8 codes out only).
+enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1, LOAD_CONV_RB = 2, LOAD_CONV_WIN = 3, LOAD_CONV_WIN2 = 4 };
 
 enum EpiMode {
   EPI_I32 = 0,         // int32 accumulators
@@ -141,13 +146,14 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
 }
 
 // RB: 0 -- A and B per stage; 1 -- conv weights resident (9 taps), A per stage; 2 -- resident weights and a
-// window of kBM + 2 A rows per stage that serves a ky's three kx taps, stored in whole 8-row swizzle atoms.
-__host__ __device__ constexpr int a_stage_rows(int RB) { return RB == 2 ? kBM + 8 : kBM; }
+// window of kBM + 2 A rows per stage that serves a ky's three kx taps, stored in whole 8-row swizzle atoms;
+// 3 -- the same with rows of two K blocks (an image pair, LOAD_CONV_WIN2).
+__host__ __device__ constexpr int a_stage_rows(int RB) { return RB >= 2 ? kBM + 8 : kBM; }
 
 // Operand bytes per stage (RB: A only, the weights are resident) and of the resident weights (9 taps).
 template <int BN, int KB, int RB>
 __host__ __device__ constexpr int stage_bytes() {
-  return (a_stage_rows(RB) + (RB ? 0 : BN)) * KB;
+  return (a_stage_rows(RB) * (RB == 3 ? 2 : 1) + (RB ? 0 : BN)) * KB;
 }
 template <int BN, int KB, int RB>
 __host__ __device__ constexpr int resident_bytes() {
@@ -522,6 +528,48 @@ __device__ __forceinline__ void next_max_flush(const GemmArgs& a, const NextMax<
   }
   best = __reduce_max_sync(kFull, best);
   if (lane == 0 && best != 0u) atomicMax(a.next_amax + nm.img, best);
+}
+
+// Per tile (the whole warp): how the next layer's maxima of this warp's pixels are taken -- *mode 1: folded
+// into nm (flushed first when nm holds another image or column tile), 2: reduced at once (pixels of two
+// images, or values that may be negative), 0: no pixel counts -- and whether this lane's pixel counts (*in).
+// col_base_held: the first column of the warp's chunks in the column tile nm holds; sc / bi: this lane's
+// channel factors in column tile nb.
+template <int NCH>
+__device__ __forceinline__ void next_max_prepare(const GemmArgs& a, const ConvPixel& px, NextMax<NCH>& nm, int nb,
+                                                 int col_base_held, const float (&sc)[NCH], const float (&bi)[NCH],
+                                                 int* mode, bool* in) {
+  *mode = 0;
+  *in = px.valid && px.yp - 1 < a.next_h && px.xp - 1 < a.next_w;
+  if (!next_nonneg(a)) {
+    *mode = 2;
+    return;
+  }
+  const int img = *in ? px.img : -1;
+  const int lo = __reduce_min_sync(kFull, *in ? img : INT_MAX);
+  const int hi = __reduce_max_sync(kFull, img);
+  if (hi < 0) return;  // no pixel of this warp counts
+  if (nm.img >= 0 && (lo != nm.img || hi != nm.img || nb != nm.nb)) {
+    next_max_flush(a, nm, col_base_held);
+    nm.img = -1;
+  }
+  if (lo != hi) {
+    *mode = 2;  // the warp's pixels span two images
+    return;
+  }
+  if (nm.img < 0) {
+    nm.img = lo;
+    nm.nb = nb;
+    nm.sx = __ldg(a.sx + lo);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      nm.sc[c] = sc[c];
+      nm.bi[c] = bi[c];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) nm.w[c][k] = 0u;
+    }
+  }
+  *mode = 1;
 }
 
 // XDNA_CONV_BIAS_INT32: the sums of this lane's pixel, channels n0..n0+31, plus the image's int32 bias row.
@@ -914,21 +962,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ GemmArgs args) {
   static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
   static_assert(!PAIR || (BN == 256 && KB == 128), "CTA pairs: 256 x 256 tiles of 128-byte K blocks");
-  constexpr int RBM = LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
+  constexpr int RBM = LOAD == LOAD_CONV_WIN2 ? 3 : LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
   constexpr bool RB = RBM != 0;               // conv weights resident in shared memory
-  constexpr bool WIN = RBM == 2;              // one A window per ky serves its three kx taps
+  constexpr bool WIN = RBM >= 2;              // one A window per ky serves its three kx taps
+  constexpr bool PIMG = RBM == 3;             // image pairs: two accumulators per tile
+  constexpr int A_ROW = PIMG ? 2 * KB : KB;   // bytes of one A row in shared memory
+  static_assert(!PIMG || (EPI == EPI_CONV_QNHWC && KB == 64 && !PAIR), "image pairs: 64-channel convs, codes out");
   constexpr bool kConv = LOAD != LOAD_GEMM;
   static_assert(!RB || (!PAIR && KB == 64 && BN <= 128), "resident conv weights: one 64-byte channel block, BN <= 128");
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (tile columns) this CTA loads
   constexpr int OUTB = stage_out_bytes<BROWS, KB, EPI, PAIR, RBM>();
   constexpr int STAGES = stages_for<BROWS, KB, OUTB, RBM>();
-  constexpr int A_BYTES = a_stage_rows(RBM) * KB;  // WIN: kBM + 2 rows used, whole swizzle atoms kept
+  constexpr int A_BYTES = a_stage_rows(RBM) * A_ROW;  // WIN: kBM + 2 rows used, whole swizzle atoms kept
   constexpr int B_BYTES = BROWS * KB;        // one K block of B (one tap, for the conv)
   constexpr int B_STAGE = RB ? 0 : B_BYTES;  // B bytes in each ring stage
   // a pair's stage: both CTAs' bytes; WIN: the window's kBM + 2 rows
-  constexpr uint32_t STAGE_TX = WIN ? (kBM + 2) * KB : (PAIR ? 2 : 1) * (A_BYTES + B_STAGE);
-  static_assert(!WIN || (A_BYTES % (8 * KB) == 0), "window stages in whole swizzle atoms");
-  constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
+  constexpr uint32_t STAGE_TX = WIN ? (kBM + 2) * A_ROW : (PAIR ? 2 : 1) * (A_BYTES + B_STAGE);
+  static_assert(!WIN || (A_BYTES % (8 * A_ROW) == 0), "window stages in whole swizzle atoms");
+  constexpr int NACC = 2;  // accumulator buffers (four for 64-column pair tiles measured no faster)
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(NACC * BN * (PIMG ? 2 : 1));
   constexpr int MMA_M = PAIR ? 2 * kBM : kBM;
   constexpr uint32_t IDESC = BF16 ? idesc_bf16(MMA_M, BN) : idesc_i8(MMA_M, BN);
   constexpr int KSTEPS = KB / 32;  // one MMA consumes 32 bytes of K (32 int8 or 16 bf16)
@@ -946,11 +998,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smOut + kEpiWarps * OUTB);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + NACC;
+  uint64_t* drain = tempty + NACC;
   uint64_t* bres = drain + 1;  // RB: the resident weights have landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres + 1);
-  static_assert((2 * STAGES + 6) * 8 + 8 <= 256, "barrier area");
+  static_assert((2 * STAGES + 2 * NACC + 2) * 8 + 8 <= 256, "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -968,7 +1020,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NACC; ++b) {
       mbar_init(tfull + b, 1);
       mbar_init(tempty + b, PAIR ? 2 * kEpiWarps : kEpiWarps);  // a pair: both CTAs' epilogue warps
     }
@@ -1106,7 +1158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = t_begin; t < t_end && ok; t += t_inc) {
         if (!mbar_wait<PAIR>(tempty + buf, bphase ^ 1, abort_flag, args.err, 3)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN * (PIMG ? 2 : 1));
         for (int kb = 0; kb < args.num_kb; ++kb) {
           if (!mbar_wait<PAIR>(full + stage, phase, abort_flag, args.err, 4)) {
             ok = false;
@@ -1118,10 +1170,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             // descriptor starts kx rows into the stage) and weights of tap 3 ky + kx
 #pragma unroll
             for (int kx = 0; kx < 3; ++kx) {
-              const uint64_t da = smem_desc_k_sw64_at(smem_u32(smA + stage * A_BYTES + kx * KB));
               const uint64_t db = smem_desc_k_sw64(smem_u32(smRes + (3 * kb + kx) * B_BYTES));
+              if constexpr (PIMG) {
+                // 128-byte rows (128-byte swizzle): image 2i's K bytes 0..63, then image 2i+1's 64..127
+                const uint64_t da = smem_desc_k_sw128_at(smem_u32(smA + stage * A_BYTES + kx * A_ROW));
 #pragma unroll
-              for (int k = 0; k < KSTEPS; ++k) umma_i8(d, da + 2 * k, db + 2 * k, IDESC, (kb | kx | k) != 0);
+                for (int w = 0; w < 2; ++w)
+#pragma unroll
+                  for (int k = 0; k < KSTEPS; ++k)
+                    umma_i8(d + w * BN, da + 4 * w + 2 * k, db + 2 * k, IDESC, (kb | kx | k) != 0);
+              } else {
+                const uint64_t da = smem_desc_k_sw64_at(smem_u32(smA + stage * A_BYTES + kx * KB));
+#pragma unroll
+                for (int k = 0; k < KSTEPS; ++k) umma_i8(d, da + 2 * k, db + 2 * k, IDESC, (kb | kx | k) != 0);
+              }
             }
           } else {
           const uint64_t da = KB == 128 ? smem_desc_k_sw128(smem_u32(smA + stage * A_BYTES))
@@ -1157,7 +1219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit_pair(tfull + buf, 0x3);
         else
           umma_commit(tfull + buf);
-        if (++buf == 2) {
+        if (++buf == NACC) {
           buf = 0;
           bphase ^= 1;
         }
@@ -1243,6 +1305,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     NextMax<NCH> nm;  // EPI_CONV_QNHWC with XDNA_CONV_NEXT_AMAX
     nm.img = -1;
     nm.nb = 0;
+    NextMax<NCH> nm1;  // PIMG: the odd images' maxima (nm: the even images')
+    nm1.img = -1;
+    nm1.nb = 0;
     for (int t = t_begin; t < t_end; t += t_inc) {
       int mb, nb;
       tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
@@ -1259,40 +1324,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const ConvPixel px = fac.px;
       int nm_mode = 0;
       bool nm_in = false;
-      if constexpr (EPI == EPI_CONV_QNHWC) {
-        if (args.next_amax != nullptr) {  // warp-uniform from here on
-          nm_in = px.valid && px.yp - 1 < args.next_h && px.xp - 1 < args.next_w;
-          if (next_nonneg(args)) {
-            const int img = nm_in ? px.img : -1;
-            const int lo = __reduce_min_sync(kFull, nm_in ? img : INT_MAX);
-            const int hi = __reduce_max_sync(kFull, img);
-            if (hi >= 0) {  // some pixel of this warp counts
-              if (nm.img >= 0 && (lo != nm.img || hi != nm.img || nb != nm.nb)) {
-                next_max_flush(args, nm, nm.nb * BN + half * WCOLS);
-                nm.img = -1;
-              }
-              if (lo == hi) {
-                if (nm.img < 0) {
-                  nm.img = lo;
-                  nm.nb = nb;
-                  nm.sx = __ldg(args.sx + lo);
-#pragma unroll
-                  for (int c = 0; c < NCH; ++c) {
-                    nm.sc[c] = fcol[c];
-                    nm.bi[c] = bcol[c];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) nm.w[c][k] = 0u;
-                  }
-                }
-                nm_mode = 1;
-              } else {
-                nm_mode = 2;  // the warp's pixels span two images
-              }
-            }
-          } else {
-            nm_mode = 2;
-          }
-        }
+      if constexpr (EPI == EPI_CONV_QNHWC && !PIMG) {
+        if (args.next_amax != nullptr)  // warp-uniform
+          next_max_prepare(args, px, nm, nb, nm.nb * BN + half * WCOLS, fcol, bcol, &nm_mode, &nm_in);
       }
       if constexpr (kSmemFactors) {
         __syncwarp();  // this warp is done reading the previous tile's factors
@@ -1323,6 +1357,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_accumulator(tempty + buf);
+      } else if constexpr (PIMG) {
+        // two accumulators: the tile's pixels of image 2i (columns buf * 2BN ..) and of image 2i + 1 (+ BN)
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          ConvPixel pw = px;
+          pw.img = 2 * px.img + w;
+          NextMax<NCH>& st = w == 0 ? nm : nm1;
+          int mode = 0;
+          bool in = false;
+          if (args.next_amax != nullptr)  // warp-uniform
+            next_max_prepare(args, pw, st, nb, st.nb * BN + half * WCOLS, fcol, bcol, &mode, &in);
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(taddr + buf * BN + w * BN + c * 32, r);
+            tmem_ld_wait();
+            if (w == 1 && c + 1 == NCH) {  // every column of both accumulators is in registers
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) release_accumulator(tempty + buf);
+            }
+            const int n0 = col0 + c * 32;
+            if (n0 < args.N) {  // warp-uniform
+              if (args.bias_i32 != nullptr) add_bias_i32(args, pw, n0, r);
+              conv_chunk<EPI>(args, pw, n0, r, fcol[c], bcol[c], obuf, mode, in, st.w[c]);
+            }
+          }
+        }
       } else {
       uint32_t r[2][32];
       __syncwarp();
@@ -1442,13 +1505,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c + 1 < NCH) tmem_ld_wait();
       }
       }  // generic chunk loop
-      if (++buf == 2) {
+      if (++buf == NACC) {
         buf = 0;
         bphase ^= 1;
       }
     }
     if constexpr (EPI == EPI_CONV_QNHWC) {
       if (nm.img >= 0) next_max_flush(args, nm, nm.nb * BN + half * WCOLS);
+      if constexpr (PIMG) {
+        if (nm1.img >= 0) next_max_flush(args, nm1, nm1.nb * BN + half * WCOLS);
+      }
     }
     if constexpr (TSTORE) {
       if (lane == 0) bulk_wait_all();
@@ -1477,7 +1543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB, bool PAIR>
 static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                               const CUtensorMap& td, const GemmArgs& args, int sms, cudaStream_t stream) {
-  constexpr int RB = LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
+  constexpr int RB = LOAD == LOAD_CONV_WIN2 ? 3 : LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
   constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB, stage_out_bytes<PAIR ? BN / 2 : BN, KB, EPI, PAIR, RB>(), RB>();
   auto kern = umma_gemm_kernel<BN, LOAD, EPI, BF16, TSTORE, ODT, KB, PAIR>;
   // per instantiation and device: resident pairs once the kernel is configured (0 = not yet). Two threads

@@ -441,10 +441,25 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
     t0 = time.perf_counter()
     with _lock:
         layer = _layer(weight, h, w, relu, taps=in_mode == IN_FLOAT and ci <= 7, bint=bint_mode)
-        xp = _bordered(n, h, w, layer.cp, x.device)
+        # image pairs (XDNA_CONV_PAIRS): a 64-channel input from codes, written two images per 128-byte row
+        pairs = in_mode != IN_FLOAT and out_q and ci == 64 and layer.cp == 64 and n % 2 == 0 and co <= 128
+        xp = None if pairs else _bordered(n, h, w, layer.cp, x.device)
         sx = torch.empty((n,), dtype=torch.float32, device=x.device)
         scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
-        if in_mode == IN_FLOAT:
+        if pairs:
+            xq = x.contiguous()
+            in_pool = in_mode == IN_CODES_POOL
+            xp2 = torch.empty((n // 2, h + 2, w + 2, 128), dtype=torch.int8, device=x.device)
+            given = xmeta.numel() == 2 * n + 2 * ci + (1 if in_pool else 0)
+            kernels.conv_quant_codes_pairs(xq, xmeta[n:n + ci], xmeta[:n], xmeta[n + ci:n + 2 * ci], in_relu_after,
+                                           in_pool, xp2, sx,
+                                           xmeta[n + 2 * ci:2 * n + 2 * ci].view(torch.int32) if given else scratch,
+                                           given)
+            float_in = lambda: codes_to_float(xq, xmeta, in_relu_after, in_pool)  # noqa: E731
+            if layer.shift is None or (cfg.verify != "off" and not (cfg.verify == "first" and layer.checked)):
+                # the plain layout, for the calibration and the CPU check (first calls)
+                xp = xp2.view(n // 2, h + 2, w + 2, 2, 64).permute(0, 3, 1, 2, 4).reshape(n, h + 2, w + 2, 64)
+        elif in_mode == IN_FLOAT:
             xc = x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
             _quantise_float(layer, xc, xp, sx, scratch)
             float_in = lambda: xc.float().cpu()  # noqa: E731
@@ -459,7 +474,7 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
                 kernels.conv_quant_codes(xq, xmeta[n:n + ci], xmeta[:n], xmeta[n + ci:n + 2 * ci], in_relu_after,
                                          in_pool, xp, sx, scratch)
             float_in = lambda: codes_to_float(xq, xmeta, in_relu_after, in_mode == IN_CODES_POOL)  # noqa: E731
-        stats.launches += 2
+        stats.launches += 1 if pairs else 2
         bint = layer.bias_int32(bias, sx) if bint_mode else None
         if layer.shift is None:
             layer.calibrate(xp, bint=bint)
@@ -475,14 +490,17 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
             if next_amax_ok(relu, fbias, post_relu, out_pool):
                 meta = codes_meta(sx, layer.scale, fbias, co, amax=True, pool=out_pool)
                 mode = (kernels.CONV_Q_NHWC | layer.flags(bint) | kernels.CONV_NEXT_AMAX
-                        | (kernels.CONV_NEXT_RELU if post_relu else 0) | (kernels.CONV_NEXT_POOL if out_pool else 0))
+                        | (kernels.CONV_NEXT_RELU if post_relu else 0) | (kernels.CONV_NEXT_POOL if out_pool else 0)
+                        | (kernels.CONV_PAIRS if pairs else 0))
                 kb = bint if bint is not None else (meta[n + co:n + 2 * co] if bias is not None else None)
-                kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, mode, shift=layer.shift, relu=relu,
+                kernels.conv3x3(xp2 if pairs else xp, layer.wp, n, layer.ci_k, co, h, w, mode, shift=layer.shift,
+                                relu=relu,
                                 scale=meta[n:n + co], sx=sx, bias=kb, out=q,
                                 acc_max=meta[n + 2 * co:2 * n + 2 * co].view(torch.int32))
                 out = (q, meta)
             else:
-                kernels.conv3x3(xp, layer.wp, n, layer.ci_k, co, h, w, kernels.CONV_Q_NHWC | layer.flags(bint),
+                kernels.conv3x3(xp2 if pairs else xp, layer.wp, n, layer.ci_k, co, h, w,
+                                kernels.CONV_Q_NHWC | layer.flags(bint) | (kernels.CONV_PAIRS if pairs else 0),
                                 shift=layer.shift, relu=relu, bias=bint, out=q)
                 out = (q, codes_meta(sx, layer.scale, fbias, co))
             stats.launches += 1

@@ -30,6 +30,7 @@ CONV_STRIDE2 = 32     # or'ed into a conv mode: stride 2, the input split into p
 # or'ed into CONV_Q_NHWC: the next layer's per-image maxima into acc_max (with its ReLU / 2x2 pool region)
 CONV_NEXT_AMAX, CONV_NEXT_RELU, CONV_NEXT_POOL = 64, 128, 256
 CONV_BIAS_INT32 = 512  # or'ed into any conv mode: `bias` is int32 [N, Co] (conv_bias_int32), added to the sums
+CONV_PAIRS = 1024      # or'ed into CONV_Q_NHWC: the input holds the images in pairs (conv_quant_codes_pairs)
 # status codes
 ERR_TIMEOUT = -4
 
@@ -68,6 +69,7 @@ def _load():
         "xdna_conv_quant_codes": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
         "xdna_conv_quant_codes_given_amax": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, I64, P, P, P], I),
         "xdna_conv_bias_int32": ([P, I, P, P, I64, I64, P, P], I),
+        "xdna_conv_quant_codes_pairs": ([P, I, I64, I64, I64, I64, P, P, P, I, I, P, P, P, I, P], I),
         "xdna_conv_quant_taps": ([P, I, I64, I64, I64, I64, P, I64, P, P, P], I),
         "xdna_conv_quant_phases": ([P, I, I, I64, I64, I64, I64, I, P, I64, P, P, P], I),
         "xdna_conv_image_amax": ([P, I, I64, I64, P, P], I),
@@ -297,6 +299,17 @@ def conv_quant_codes_given_amax(q, scale, sx_in, bias, relu_after, pool, xp, sx,
     _check("xdna_conv_quant_codes_given_amax", L.xdna_conv_quant_codes_given_amax(
         _p(q), int(q.dtype == torch.uint8), N, C, H, W, _p(scale), _p(sx_in), _p(bias), int(relu_after), int(pool),
         _p(xp), xp.shape[-1], _p(sx), _p(amax), _stream()))
+
+
+def conv_quant_codes_pairs(q, scale, sx_in, bias, relu_after, pool, xp2, sx, amax, amax_given):
+    """conv_quant_codes into the image-pair layout xp2 [N/2, H'+2, W'+2, 128] (64 channels): amax holds the
+    producing conv's maxima when amax_given, else it is scratch."""
+    L = require()
+    _cuda(q, scale, sx_in, bias, xp2, sx, amax)
+    N, H, W, C = q.shape
+    _check("xdna_conv_quant_codes_pairs", L.xdna_conv_quant_codes_pairs(
+        _p(q), int(q.dtype == torch.uint8), N, C, H, W, _p(scale), _p(sx_in), _p(bias), int(relu_after), int(pool),
+        _p(xp2), _p(sx), _p(amax), int(amax_given), _stream()))
 
 
 def conv_bias_int32(bias, sw, sx, out):
