@@ -436,7 +436,7 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
     const uint64_t row_bytes = pimg ? 2 * Cp : Cp;
     const uint64_t dims[2] = {row_bytes, static_cast<uint64_t>(a_rows)};
     const uint64_t strides[1] = {row_bytes};
-    const uint32_t box[2] = {static_cast<uint32_t>(pimg ? 128 : kb), win ? kBM + 2 : kBM};
+    const uint32_t box[2] = {static_cast<uint32_t>(pimg ? 128 : kb), static_cast<uint32_t>(win ? kBM + 2 : kBM)};
     rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations",
                     kb == 64 && !pimg ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != XDNA_OK) return rc;

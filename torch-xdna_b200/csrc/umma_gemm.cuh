@@ -483,15 +483,19 @@ __device__ __forceinline__ void conv_next_amax(const GemmArgs& a, const ConvPixe
 
 // XDNA_CONV_NEXT_AMAX for values >= 0 (next_nonneg), accumulated across tiles: each epilogue lane keeps, per
 // channel of its chunks, the largest code of its pixels over the tiles it drains of one image and one column
-// tile (four codes per word, in unsigned order: a signed code is stored as code + 128), and the warp combines
+// tile (in unsigned order: a signed code is stored as code + 128; with at most two chunks per warp two codes
+// per word as 16-bit lanes -- word 2k holding channels 4k and 4k + 2, word 2k + 1 channels 4k + 1 and 4k + 3 --
+// so that the merge is the packed 16-bit max; with four chunks, where registers are short, four codes per
+// word and __vmaxu4), and the warp combines
 // them and evaluates y once per channel when the image or the column tile changes and after the last tile --
 // instead of a warp reduction per channel per tile. img < 0: nothing held. sc / bi: this lane's channel
 // scale and bias for each chunk; sx: the image's scale.
 template <int NCH>
 struct NextMax {
+  static constexpr int kWords = NCH <= 2 ? 16 : 8;  // per chunk: 16-bit lanes, or 8-bit lanes
   int img, nb;
   float sx;
-  uint32_t w[NCH][8];
+  uint32_t w[NCH][kWords];
   float sc[NCH], bi[NCH];
 };
 
@@ -505,18 +509,23 @@ __device__ __forceinline__ void next_max_flush(const GemmArgs& a, const NextMax<
   for (int c = 0; c < NCH; ++c) {
     const int n0 = col0 + c * 32;
     if (n0 < a.N) {  // warp-uniform
-      uint32_t w[8];
+      constexpr int W = NextMax<NCH>::kWords;
+      uint32_t w[W];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) w[k] = nm.w[c][k];
+      for (int k = 0; k < W; ++k) w[k] = nm.w[c][k];
 #pragma unroll
       for (int s = 16; s >= 1; s >>= 1) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) w[k] = __vmaxu4(w[k], __shfl_xor_sync(kFull, w[k], s));
+        for (int k = 0; k < W; ++k)
+          w[k] = W == 16 ? __vmaxu2(w[k], __shfl_xor_sync(kFull, w[k], s)) : __vmaxu4(w[k], __shfl_xor_sync(kFull, w[k], s));
       }
-      uint32_t word = w[0];  // every lane holds the 32 channels' largest codes; lane j takes channel n0 + j
+      // every lane holds the 32 channels' largest codes; lane j takes channel n0 + j: 16-bit lanes: word
+      // 2 (j / 4) + j % 2, lane (j % 4) / 2; 8-bit lanes: word j / 4, byte j % 4
+      const int sel = W == 16 ? 2 * (lane >> 2) + (lane & 1) : lane >> 2;
+      uint32_t word = w[0];
 #pragma unroll
-      for (int k = 1; k < 8; ++k) word = (lane >> 2) == k ? w[k] : word;
-      const int u = static_cast<int>((word >> (8 * (lane & 3))) & 0xFFu);
+      for (int k = 1; k < W; ++k) word = sel == k ? w[k] : word;
+      const int u = static_cast<int>((word >> (W == 16 ? 16 * ((lane >> 1) & 1) : 8 * (lane & 3))) & 0xFFu);
       const int q = a.relu ? u : u - 128;
       if (lane < a.N - n0) {
         float y = __fmul_rn(static_cast<float>(q), __fmul_rn(nm.sc[c], nm.sx));
@@ -566,7 +575,7 @@ __device__ __forceinline__ void next_max_prepare(const GemmArgs& a, const ConvPi
       nm.sc[c] = sc[c];
       nm.bi[c] = bi[c];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) nm.w[c][k] = 0u;
+      for (int k = 0; k < NextMax<NCH>::kWords; ++k) nm.w[c][k] = 0u;
     }
   }
   *mode = 1;
@@ -596,10 +605,10 @@ __device__ __forceinline__ void add_bias_i32(const GemmArgs& a, const ConvPixel&
 // Conv epilogues: one thread, one bordered pixel, channels n0..n0+31 in r[].
 // nm_mode (EPI_CONV_QNHWC with XDNA_CONV_NEXT_AMAX): 1 fold the codes of the pixels in the next layer's
 // region (nm_in) into nm_acc (NextMax), 2 reduce this chunk's maxima at once (conv_next_amax), 0 neither.
-template <int EPI>
+template <int EPI, int NW>
 __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& px, int n0, const uint32_t (&r)[32],
                                            float scale_lane, float bias_lane, uint8_t* stage, int nm_mode,
-                                           bool nm_in, uint32_t (&nm_acc)[8]) {
+                                           bool nm_in, uint32_t (&nm_acc)[NW]) {
   const int img = px.img;
   const int yp = px.yp;
   const int xp = px.xp;
@@ -631,7 +640,15 @@ __device__ __forceinline__ void conv_chunk(const GemmArgs& a, const ConvPixel& p
     if (nm_mode == 1) {  // warp-uniform
       const uint32_t flip = a.relu ? 0u : 0x80808080u;  // signed codes in unsigned order
 #pragma unroll
-      for (int k = 0; k < 8; ++k) nm_acc[k] = __vmaxu4(nm_acc[k], nm_in ? (w[k] ^ flip) : 0u);
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t x = nm_in ? (w[k] ^ flip) : 0u;
+        if constexpr (NW == 16) {
+          nm_acc[2 * k] = __vmaxu2(nm_acc[2 * k], __byte_perm(x, 0u, 0x4240));          // bytes 0 and 2
+          nm_acc[2 * k + 1] = __vmaxu2(nm_acc[2 * k + 1], __byte_perm(x, 0u, 0x4341));  // bytes 1 and 3
+        } else {
+          nm_acc[k] = __vmaxu4(nm_acc[k], x);
+        }
+      }
     } else if (nm_mode == 2) {
       int qv[32];
 #pragma unroll
