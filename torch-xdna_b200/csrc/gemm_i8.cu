@@ -32,8 +32,13 @@ static int dispatch_bn(int bn, bool pair, const CUtensorMap& ta, const CUtensorM
 // The conv's kernel for one mode, with 64-byte K blocks when the input has at most 64 channels (a
 // 128-byte block would be half zero fill).
 template <int EPI, int ODT>
-static int dispatch_conv(int kb, int bn, bool pair, bool win, const CUtensorMap& ta, const CUtensorMap& tb,
+static int dispatch_conv(int kb, int bn, bool pair, bool win, bool winb, const CUtensorMap& ta, const CUtensorMap& tb,
                          const GemmArgs& args, int sms, cudaStream_t stream) {
+  if (winb) {  // 128-byte channel blocks: one window per (ky, block) with its three taps' weights (LOAD_CONV_WINB)
+    if (pair) return launch_gemm_kernel<256, LOAD_CONV_WINB, EPI, false, false, ODT, 128, true>(ta, tb, ta, ta, args, sms, stream);
+    if (bn == 128) return launch_umma<128, LOAD_CONV_WINB, EPI, false, ODT, 128>(ta, tb, ta, args, sms, stream);
+    return launch_umma<64, LOAD_CONV_WINB, EPI, false, ODT, 128>(ta, tb, ta, args, sms, stream);
+  }
   if (win) {  // resident weights, one window of 130 activation rows per ky (conv_window)
     if (bn == 128) return launch_umma<128, LOAD_CONV_WIN, EPI, false, ODT, 64>(ta, tb, ta, args, sms, stream);
     return launch_umma<64, LOAD_CONV_WIN, EPI, false, ODT, 64>(ta, tb, ta, args, sms, stream);
@@ -401,6 +406,12 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   // 256 x 256 tiles on CTA pairs for wide convs (not the calibration, which runs one image)
   const bool pair = kb == 128 && mode != XDNA_CONV_CALIBRATE && use_pairs(bn, a.m_tiles, a.n_tiles, sms);
   if (pair) a.m_tiles = static_cast<int>((NP + 2 * kBM - 1) / (2 * kBM));
+  // stride-1 3x3 convs of 128-byte channel blocks: one window per (ky, channel block) serving three taps, when
+  // a CTA's B tiles are at most 128 rows (three of them share the stage with the window); not for the
+  // dequantise, whose staged whole-line stores need the shared memory the window's stages take
+  const bool winb = conv_window() && kb == 128 && a.ntaps == 9 && !stride2 && (pair ? bn / 2 : bn) <= 128 &&
+                    mode != XDNA_CONV_DEQUANT;
+  if (winb) a.num_kb = 3 * a.cblocks;
   a.Wp = static_cast<int>(Wp);
   a.HWp = static_cast<int>(HWp);
   a.H = static_cast<int>(H);
@@ -436,7 +447,7 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
     const uint64_t row_bytes = pimg ? 2 * Cp : Cp;
     const uint64_t dims[2] = {row_bytes, static_cast<uint64_t>(a_rows)};
     const uint64_t strides[1] = {row_bytes};
-    const uint32_t box[2] = {static_cast<uint32_t>(pimg ? 128 : kb), static_cast<uint32_t>(win ? kBM + 2 : kBM)};
+    const uint32_t box[2] = {static_cast<uint32_t>(pimg ? 128 : kb), static_cast<uint32_t>(win || winb ? kBM + 2 : kBM)};
     rc = encode_tma(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xp, dims, strides, box, "conv3x3 activations",
                     kb == 64 && !pimg ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != XDNA_OK) return rc;
@@ -452,17 +463,17 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   }
   switch (mode) {
     case XDNA_CONV_Q:
-      return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, pair, win, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_Q, XDNA_I8>(kb, bn, pair, win, winb, ta, tb, a, sms, s);
     case XDNA_CONV_DEQUANT:
-      return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, pair, win, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_DEQ, XDNA_F32>(kb, bn, pair, win, winb, ta, tb, a, sms, s);
     case XDNA_CONV_Q_NHWC:
       if (pimg) {
         if (bn == 128) return launch_umma<128, LOAD_CONV_WIN2, EPI_CONV_QNHWC, false, XDNA_I8, 64>(ta, tb, ta, a, sms, s);
         return launch_umma<64, LOAD_CONV_WIN2, EPI_CONV_QNHWC, false, XDNA_I8, 64>(ta, tb, ta, a, sms, s);
       }
-      return dispatch_conv<EPI_CONV_QNHWC, XDNA_I8>(kb, bn, pair, win, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_QNHWC, XDNA_I8>(kb, bn, pair, win, winb, ta, tb, a, sms, s);
     default:
-      return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, false, win, ta, tb, a, sms, s);
+      return dispatch_conv<EPI_CONV_CALIB, XDNA_I32>(kb, bn, false, win, winb, ta, tb, a, sms, s);
   }
 }
 

@@ -39,7 +39,10 @@ namespace xdna {
 // LOAD_CONV_WIN's brings 64: half the TMA row requests, the mainloop's bound for 64-channel convs. Each kx
 // tap issues the MMAs of both images, reading K bytes 0..63 (image 2i) and 64..127 (image 2i+1) of the
 // rows into two accumulators; the epilogue drains both (int8 codes out only).
-enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1, LOAD_CONV_RB = 2, LOAD_CONV_WIN = 3, LOAD_CONV_WIN2 = 4 };
+// LOAD_CONV_WINB: the window for convs of 128-byte channel blocks whose weights do not stay resident: a stage
+// holds one window of kBM + 2 rows of one channel block for one ky and the three kx taps' weight tiles of that
+// block, so the A rows are requested once per ky instead of once per tap (B as before).
+enum LoadMode { LOAD_GEMM = 0, LOAD_CONV = 1, LOAD_CONV_RB = 2, LOAD_CONV_WIN = 3, LOAD_CONV_WIN2 = 4, LOAD_CONV_WINB = 5 };
 
 enum EpiMode {
   EPI_I32 = 0,         // int32 accumulators
@@ -147,17 +150,18 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
 
 // RB: 0 -- A and B per stage; 1 -- conv weights resident (9 taps), A per stage; 2 -- resident weights and a
 // window of kBM + 2 A rows per stage that serves a ky's three kx taps, stored in whole 8-row swizzle atoms;
-// 3 -- the same with rows of two K blocks (an image pair, LOAD_CONV_WIN2).
+// 3 -- the same with rows of two K blocks (an image pair, LOAD_CONV_WIN2); 4 -- a window and three taps' B
+// tiles per stage, nothing resident (LOAD_CONV_WINB).
 __host__ __device__ constexpr int a_stage_rows(int RB) { return RB >= 2 ? kBM + 8 : kBM; }
 
 // Operand bytes per stage (RB: A only, the weights are resident) and of the resident weights (9 taps).
 template <int BN, int KB, int RB>
 __host__ __device__ constexpr int stage_bytes() {
-  return (a_stage_rows(RB) * (RB == 3 ? 2 : 1) + (RB ? 0 : BN)) * KB;
+  return RB == 4 ? (a_stage_rows(RB) + 3 * BN) * KB : (a_stage_rows(RB) * (RB == 3 ? 2 : 1) + (RB ? 0 : BN)) * KB;
 }
 template <int BN, int KB, int RB>
 __host__ __device__ constexpr int resident_bytes() {
-  return RB ? 9 * BN * KB : 0;
+  return RB && RB != 4 ? 9 * BN * KB : 0;
 }
 
 // Operand stages in 224 KB less the epilogue's staging (8 x OUTB) and any resident weights, at most 12:
@@ -979,12 +983,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ GemmArgs args) {
   static_assert(KB == 128 || KB == 64, "K blocks of 128 or 64 bytes");
   static_assert(!PAIR || (BN == 256 && KB == 128), "CTA pairs: 256 x 256 tiles of 128-byte K blocks");
-  constexpr int RBM = LOAD == LOAD_CONV_WIN2 ? 3 : LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
-  constexpr bool RB = RBM != 0;               // conv weights resident in shared memory
+  constexpr int RBM = LOAD == LOAD_CONV_WINB ? 4 : LOAD == LOAD_CONV_WIN2 ? 3 : LOAD == LOAD_CONV_WIN ? 2
+                    : LOAD == LOAD_CONV_RB ? 1 : 0;
+  constexpr bool RB = RBM != 0 && RBM != 4;   // conv weights resident in shared memory
   constexpr bool WIN = RBM >= 2;              // one A window per ky serves its three kx taps
+  constexpr bool WINB = RBM == 4;             // ... with the three taps' B tiles in the stage
   constexpr bool PIMG = RBM == 3;             // image pairs: two accumulators per tile
   constexpr int A_ROW = PIMG ? 2 * KB : KB;   // bytes of one A row in shared memory
   static_assert(!PIMG || (EPI == EPI_CONV_QNHWC && KB == 64 && !PAIR), "image pairs: 64-channel convs, codes out");
+  static_assert(!WINB || (KB == 128 && (PAIR ? BN / 2 : BN) <= 128), "windows of 128-byte blocks, <= 128 B rows");
   constexpr bool kConv = LOAD != LOAD_GEMM;
   static_assert(!RB || (!PAIR && KB == 64 && BN <= 128), "resident conv weights: one 64-byte channel block, BN <= 128");
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (tile columns) this CTA loads
@@ -992,9 +999,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGES = stages_for<BROWS, KB, OUTB, RBM>();
   constexpr int A_BYTES = a_stage_rows(RBM) * A_ROW;  // WIN: kBM + 2 rows used, whole swizzle atoms kept
   constexpr int B_BYTES = BROWS * KB;        // one K block of B (one tap, for the conv)
-  constexpr int B_STAGE = RB ? 0 : B_BYTES;  // B bytes in each ring stage
+  constexpr int B_STAGE = RB ? 0 : WINB ? 3 * B_BYTES : B_BYTES;  // B bytes in each ring stage
   // a pair's stage: both CTAs' bytes; WIN: the window's kBM + 2 rows
-  constexpr uint32_t STAGE_TX = WIN ? (kBM + 2) * A_ROW : (PAIR ? 2 : 1) * (A_BYTES + B_STAGE);
+  constexpr uint32_t STAGE_TX = WINB ? (PAIR ? 2 : 1) * ((kBM + 2) * KB + B_STAGE)
+                                : WIN ? (kBM + 2) * A_ROW : (PAIR ? 2 : 1) * (A_BYTES + B_STAGE);
   static_assert(!WIN || (A_BYTES % (8 * A_ROW) == 0), "window stages in whole swizzle atoms");
   constexpr int NACC = 2;  // accumulator buffers (four for 64-column pair tiles measured no faster)
   constexpr uint32_t TMEM_COLS = tmem_cols_for(NACC * BN * (PIMG ? 2 : 1));
@@ -1115,6 +1123,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               else
                 tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, kb * K_ELEMS, ar);
               tma_load_2d_pair(smB + stage * B_BYTES, &tmB, fb, kb * K_ELEMS, b_row);
+            } else if constexpr (WINB) {
+              // K block kb: ky = kb / cblocks and channel block cb; the window from the row of tap (ky, 0),
+              // the weights of taps 3 ky + 0, 1, 2
+              const int ky = kb / args.cblocks;
+              const int cb = kb - ky * args.cblocks;
+              tma_load_2d_pair(smA + stage * A_BYTES, &tmA, fb, cb * K_ELEMS, tile_row0(mb) + args.tap_off[3 * ky]);
+#pragma unroll
+              for (int kx = 0; kx < 3; ++kx)
+                tma_load_3d_pair(smB + stage * B_STAGE + kx * B_BYTES, &tmB, fb, cb * K_ELEMS, 3 * ky + kx, b_row);
             } else {
               const int tap = kb / args.cblocks;
               const int cb = kb - tap * args.cblocks;
@@ -1130,6 +1147,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             else
               tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, kb * K_ELEMS, mb * kBM);
             tma_load_2d(smB + stage * B_BYTES, &tmB, full + stage, kb * K_ELEMS, nb * BN);
+          } else if constexpr (WINB) {
+            mbar_arrive_expect_tx(full + stage, STAGE_TX);
+            const int ky = kb / args.cblocks;
+            const int cb = kb - ky * args.cblocks;
+            tma_load_2d(smA + stage * A_BYTES, &tmA, full + stage, cb * K_ELEMS, mb * kBM + args.tap_off[3 * ky]);
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx)
+              tma_load_3d(smB + stage * B_STAGE + kx * B_BYTES, &tmB, full + stage, cb * K_ELEMS, 3 * ky + kx, nb * BN);
           } else {
             mbar_arrive_expect_tx(full + stage, STAGE_TX);
             // WIN: K block kb is ky = kb, its window starting at the row of tap (ky, kx = 0)
@@ -1182,7 +1207,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          if constexpr (WIN) {
+          if constexpr (WINB) {
+            // the three kx taps read the window from row kx on (128-byte rows) with their own weight tiles
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) {
+              const uint64_t da = smem_desc_k_sw128_at(smem_u32(smA + stage * A_BYTES + kx * KB));
+              const uint64_t db = smem_desc_k_sw128(smem_u32(smB + stage * B_STAGE + kx * B_BYTES));
+#pragma unroll
+              for (int k = 0; k < KSTEPS; ++k) {
+                const uint32_t acc = (kb | kx | k) != 0;
+                if constexpr (PAIR)
+                  umma_i8_pair(d, da + 2 * k, db + 2 * k, IDESC, acc);
+                else
+                  umma_i8(d, da + 2 * k, db + 2 * k, IDESC, acc);
+              }
+            }
+          } else if constexpr (WIN) {
             // K block kb is ky = kb; its three kx taps read the window from row kx on (64-byte rows, so the
             // descriptor starts kx rows into the stage) and weights of tap 3 ky + kx
 #pragma unroll
@@ -1560,7 +1600,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, int LOAD, int EPI, bool BF16, bool TSTORE, int ODT, int KB, bool PAIR>
 static int launch_gemm_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                               const CUtensorMap& td, const GemmArgs& args, int sms, cudaStream_t stream) {
-  constexpr int RB = LOAD == LOAD_CONV_WIN2 ? 3 : LOAD == LOAD_CONV_WIN ? 2 : LOAD == LOAD_CONV_RB ? 1 : 0;
+  constexpr int RB = LOAD == LOAD_CONV_WINB ? 4 : LOAD == LOAD_CONV_WIN2 ? 3 : LOAD == LOAD_CONV_WIN ? 2
+                   : LOAD == LOAD_CONV_RB ? 1 : 0;
   constexpr int smem = smem_bytes_for<PAIR ? BN / 2 : BN, KB, stage_out_bytes<PAIR ? BN / 2 : BN, KB, EPI, PAIR, RB>(), RB>();
   auto kern = umma_gemm_kernel<BN, LOAD, EPI, BF16, TSTORE, ODT, KB, PAIR>;
   // per instantiation and device: resident pairs once the kernel is configured (0 = not yet). Two threads
