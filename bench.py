@@ -128,9 +128,9 @@ INT8_PEAK_NOTE = "int8 peak = 2 x the measured dense bf16 cuBLAS burst (B200's d
 
 
 # DRAM bytes of one launch of the chained conv1_2 (32 images, 64 -> 64, 224 x 224), from an ncu capture of
-# `bench.py --kernel conv3x3_chain --shape 32,64,224`: reads 109.06 MB + writes 59.85 MB (the rest of the
-# codes is still in L2 when the kernel ends)
-CONV_CHAIN_DRAM_BYTES_32 = 109_064_192 + 59_851_520
+# `bench.py --kernel conv3x3_chain --shape 32,64,224` (input in image pairs): reads 113.36 MB + writes 57.53 MB
+# (the rest of the codes is still in L2 when the kernel ends)
+CONV_CHAIN_DRAM_BYTES_32 = 113_359_360 + 57_533_952
 
 
 def roof(bound, kernel, achieved, peak, unit, per_launch_ms, **extra):
