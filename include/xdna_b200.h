@@ -7,10 +7,14 @@
  *     comment says "host";
  *   - `stream` is a cudaStream_t (NULL = legacy default stream); calls only enqueue work and
  *     never synchronise, except xdna_take_device_error();
- *   - no entry point allocates device memory on its hot path; the only allocation the library
- *     ever makes is nothing -- scratch is passed in by the caller;
+ *   - no entry point allocates device memory except xdna_ipc_alloc (the shareable buffer a caller
+ *     asks for); scratch is passed in by the caller;
  *   - leading dimensions (`ld*`) are in elements; int8 operands read by TMA need their row
- *     pitch in bytes to be a multiple of 16 and their base 16-byte aligned.
+ *     pitch in bytes to be a multiple of 16 and their base 16-byte aligned;
+ *   - the library caches, per device, the device addresses of its own globals (the error word,
+ *     the no-allocation scratch) on first use: it must not be used on a device after a
+ *     cudaDeviceReset of that device (the cached addresses would point into the destroyed
+ *     context); load the library again in a new process instead.
  *
  * The reference (AyaSakura-comp/torch-xdna) reaches its device through Python calls into
  * Triton-XDNA; each entry point below names the reference call it replaces.
