@@ -401,7 +401,11 @@ int xdna_conv3x3_i8(const int8_t* xp, const int8_t* wp, int64_t N, int64_t Ci, i
   const bool win = conv_window() && kb == 64 && a.cblocks == 1 && a.ntaps == 9 && !stride2 && Co <= 128;
   if (win) a.num_kb = 3;
   a.m_tiles = static_cast<int>((a.M + kBM - 1) / kBM);
-  const int bn = choose_bn(a.m_tiles, Co, sms);
+  int bn = choose_bn(a.m_tiles, Co, sms);
+  // a small conv of 128-byte channel blocks (a few images per GPU, deep layers): 64-column tiles while
+  // 128-column ones leave SMs idle (not for <= 64 input channels, whose resident-weight paths take one
+  // column tile of all the output channels)
+  if (kb == 128 && bn == 128 && Co > 64 && a.m_tiles * ((Co + 127) / 128) < sms) bn = 64;
   a.n_tiles = static_cast<int>((Co + bn - 1) / bn);
   // 256 x 256 tiles on CTA pairs for wide convs (not the calibration, which runs one image)
   const bool pair = kb == 128 && mode != XDNA_CONV_CALIBRATE && use_pairs(bn, a.m_tiles, a.n_tiles, sms);
