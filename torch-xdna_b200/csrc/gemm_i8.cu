@@ -54,8 +54,9 @@ static int dispatch_conv(int kb, int bn, bool pair, bool win, bool winb, const C
   return dispatch_bn<LOAD_CONV, EPI, false, ODT, 128>(bn, pair, ta, tb, ta, args, sms, stream);
 }
 
-// Whether stride-1 3x3 convs of <= 64 input channels use the window load (LOAD_CONV_WIN); XDNA_CONV_WINDOW=0
-// in the environment turns it off (the per-tap loads of LOAD_CONV_RB), e.g. to compare the two.
+// Whether stride-1 3x3 convs use the window loads (LOAD_CONV_WIN, LOAD_CONV_WIN2, LOAD_CONV_WINB);
+// XDNA_CONV_WINDOW=0 in the environment turns them off (per-tap loads), e.g. to compare the two; image pairs
+// (XDNA_CONV_PAIRS), which only the window reads, are then refused.
 static bool conv_window() {
   static const bool on = [] {
     const char* e = std::getenv("XDNA_CONV_WINDOW");

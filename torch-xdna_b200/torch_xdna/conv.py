@@ -19,6 +19,7 @@ conv with the dequantise (or requantise) in its epilogue.
 
 import logging
 import math
+import os
 import threading
 import time
 import weakref
@@ -441,8 +442,10 @@ def conv3x3_chain(cfg, x, xmeta, weight, bias, relu, post_relu, in_mode, in_relu
     t0 = time.perf_counter()
     with _lock:
         layer = _layer(weight, h, w, relu, taps=in_mode == IN_FLOAT and ci <= 7, bint=bint_mode)
-        # image pairs (XDNA_CONV_PAIRS): a 64-channel input from codes, written two images per 128-byte row
-        pairs = in_mode != IN_FLOAT and out_q and ci == 64 and layer.cp == 64 and n % 2 == 0 and co <= 128
+        # image pairs (XDNA_CONV_PAIRS): a 64-channel input from codes, written two images per 128-byte row (they
+        # read through the window loads, which XDNA_CONV_WINDOW=0 turns off for comparisons)
+        pairs = (in_mode != IN_FLOAT and out_q and ci == 64 and layer.cp == 64 and n % 2 == 0 and co <= 128
+                 and os.environ.get("XDNA_CONV_WINDOW", "1") != "0")
         xp = None if pairs else _bordered(n, h, w, layer.cp, x.device)
         sx = torch.empty((n,), dtype=torch.float32, device=x.device)
         scratch = torch.empty((n,), dtype=torch.int32, device=x.device)
