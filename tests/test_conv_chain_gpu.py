@@ -178,6 +178,43 @@ def test_image_pairs_equal_the_plain_layout(cuda, shape, kind):
     assert torch.equal(outs[0][1], outs[1][1])
 
 
+@pytest.mark.parametrize("pool", [False, True])
+@pytest.mark.parametrize("relu_after", [True, False])
+@pytest.mark.parametrize("pairs", [False, True])
+def test_quantise_from_codes_matches_the_cpu(cuda, pool, relu_after, pairs):
+    """The quantise from codes on millions of values against the CPU: y rebuilt with torch's f32 operations
+    in the epilogue's order (codes_to_float), the per-image max, and round(y / s) by IEEE division -- bit
+    for bit. Large enough that a rounding difference of a few codes in 10^5 shows."""
+    from torch_xdna import conv as xconv
+    from torch_xdna import kernels
+
+    n, h, w, c = 4, 96, 104, 64
+    g = torch.Generator(device=cuda).manual_seed(3 + pool + 2 * relu_after + 4 * pairs)
+    q = torch.randint(-128, 128, (n, h, w, c), device=cuda, generator=g).to(torch.int8)
+    scale = torch.rand(c, device=cuda, generator=g) * 1e-3 + 1e-4
+    sx_in = torch.rand(n, device=cuda, generator=g) + 0.5
+    bias = torch.randn(c, device=cuda, generator=g) * 0.02
+    meta = xconv.codes_meta(sx_in, scale, bias, c)
+    ho, wo = (h // 2, w // 2) if pool else (h, w)
+    sx = torch.empty(n, device=cuda)
+    scratch = torch.empty(n, dtype=torch.int32, device=cuda)
+    if pairs:
+        xp2 = torch.empty(n // 2, ho + 2, wo + 2, 128, dtype=torch.int8, device=cuda)
+        kernels.conv_quant_codes_pairs(q, scale, sx_in, bias, relu_after, pool, xp2, sx, scratch, False)
+        xp = xp2.view(n // 2, ho + 2, wo + 2, 2, 64).permute(0, 3, 1, 2, 4).reshape(n, ho + 2, wo + 2, 64)
+    else:
+        xp = torch.empty(n, ho + 2, wo + 2, 64, dtype=torch.int8, device=cuda)
+        kernels.conv_quant_codes(q, scale, sx_in, bias, relu_after, pool, xp, sx, scratch)
+    y = xconv.codes_to_float(q, meta, relu_after, pool)                    # CPU, NCHW
+    s = (y.abs().amax(dim=(1, 2, 3)).clamp(min=1e-8) / 127).float()
+    want = torch.round(y / s[:, None, None, None]).clamp(-127, 127).to(torch.int8).permute(0, 2, 3, 1)
+    assert torch.equal(sx.cpu(), s)
+    got = xp[:, 1:ho + 1, 1:wo + 1].cpu()
+    bad = int((got != want).sum())
+    assert bad == 0, f"{bad} of {want.numel()} quantised values differ"
+    assert int(xp[:, 0].abs().sum()) == 0 and int(xp[:, :, 0].abs().sum()) == 0   # the zero border
+
+
 def test_compiled_vgg_block_chained_equals_unchained(cuda):
     """torch.compile(backend="xdna"): the chained graph (default) and the unchained one (fuse=False, ReLU
     and max-pool left to torch) give identical outputs."""
