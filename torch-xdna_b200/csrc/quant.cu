@@ -474,10 +474,12 @@ __global__ void __launch_bounds__(256) to_phases_kernel(const T* __restrict__ x,
 // One thread per bordered pixel (yb, xb), i.e. output pixel (yb - 1, xb - 1): the 3x3 stencil's taps of
 // C <= 7 channels as 9 C quantised bytes of its Kp-byte row, tap t = 3 dy + dx reading input pixel
 // (yb - 2 + dy, xb - 2 + dx); zeros outside the image and past byte 9 C. grid (ceil((H+2)(W+2) / 256), N).
-template <typename T>
-__global__ void __launch_bounds__(256) to_taps_kernel(const T* __restrict__ x, int C, int H, int W, int Kp,
+// C is a template parameter, so the tap and channel loops unroll and the row's words stay in registers.
+template <typename T, int C>
+__global__ void __launch_bounds__(256) to_taps_kernel(const T* __restrict__ x, int H, int W,
                                                       const uint32_t* __restrict__ amax, int8_t* __restrict__ xp,
                                                       float* __restrict__ sx) {
+  constexpr int Kp = (9 * C + 15) / 16 * 16;
   const int n = blockIdx.y;
   const int Wp = W + 2, HWp = (H + 2) * Wp;
   const int p = blockIdx.x * blockDim.x + threadIdx.x;
@@ -486,19 +488,23 @@ __global__ void __launch_bounds__(256) to_taps_kernel(const T* __restrict__ x, i
   if (blockIdx.x == 0 && threadIdx.x == 0) sx[n] = s;
   if (p >= HWp) return;
   const int yb = p / Wp, xb = p - yb * Wp;
-  uint32_t words[16];
+  uint32_t words[Kp / 4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) words[i] = 0;
+  for (int i = 0; i < Kp / 4; ++i) words[i] = 0;
+#pragma unroll
   for (int t = 0; t < 9; ++t) {
     const int y = yb - 2 + t / 3, xx = xb - 2 + t % 3;
-    if (y < 0 || y >= H || xx < 0 || xx >= W) continue;
+    const bool in = y >= 0 && y < H && xx >= 0 && xx < W;
+#pragma unroll
     for (int c = 0; c < C; ++c) {
-      const uint32_t q = quant_byte(to_f32(x[((static_cast<int64_t>(n) * C + c) * H + y) * W + xx]), s, r) & 0xFFu;
+      const uint32_t q =
+          in ? quant_byte(to_f32(x[((static_cast<int64_t>(n) * C + c) * H + y) * W + xx]), s, r) & 0xFFu : 0u;
       const int k = t * C + c;
       words[k >> 2] |= q << (8 * (k & 3));
     }
   }
   uint4* dst = reinterpret_cast<uint4*>(xp + (static_cast<int64_t>(n) * HWp + p) * Kp);
+#pragma unroll
   for (int i = 0; i < Kp / 16; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
 }
 
@@ -756,6 +762,20 @@ __global__ void __launch_bounds__(256) bias_int32_kernel(const T* __restrict__ b
   }
 }
 
+template <typename T>
+static void launch_taps(const T* x, int C, int H, int W, dim3 g, const uint32_t* amax, int8_t* xp, float* sx,
+                        cudaStream_t s) {
+  switch (C) {
+    case 1: to_taps_kernel<T, 1><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
+    case 2: to_taps_kernel<T, 2><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
+    case 3: to_taps_kernel<T, 3><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
+    case 4: to_taps_kernel<T, 4><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
+    case 5: to_taps_kernel<T, 5><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
+    case 6: to_taps_kernel<T, 6><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
+    default: to_taps_kernel<T, 7><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
+  }
+}
+
 }  // namespace xdna
 
 using namespace xdna;
@@ -872,7 +892,7 @@ int xdna_conv_quant_taps(const void* x, int x_dtype, int64_t N, int64_t C, int64
   int rc = check_device(nullptr);
   if (rc != XDNA_OK) return rc;
   XDNA_CHECK_ARG(N >= 0 && C >= 1 && C <= 7 && H >= 1 && W >= 1, "conv_quant_taps: bad shape (1 <= C <= 7)");
-  XDNA_CHECK_ARG(Kp >= 9 * C && Kp % 16 == 0 && Kp <= 64, "conv_quant_taps: Kp must cover 9 C, a multiple of 16");
+  XDNA_CHECK_ARG(Kp == (9 * C + 15) / 16 * 16, "conv_quant_taps: Kp must be 9 C rounded up to a multiple of 16");
   XDNA_CHECK_ARG(N <= 65535 && (H + 2) * (W + 2) < (1ll << 31), "conv_quant_taps: too large");
   if (N == 0) return XDNA_OK;
   XDNA_CHECK_ARG(x && xp && sx && amax_scratch, "conv_quant_taps: null pointer");
@@ -884,20 +904,20 @@ int xdna_conv_quant_taps(const void* x, int x_dtype, int64_t N, int64_t C, int64
   dim3 g_amax(chunks, static_cast<unsigned>(N));
   dim3 g(static_cast<unsigned>(((H + 2) * (W + 2) + 255) / 256), static_cast<unsigned>(N));
   const int c = static_cast<int>(C), h = static_cast<int>(H), w = static_cast<int>(W), kp = static_cast<int>(Kp);
+  (void)kp;
   switch (x_dtype) {
     case XDNA_F32:
       image_amax_kernel<float><<<g_amax, 256, 0, s>>>(static_cast<const float*>(x), per_image, amax_scratch);
-      to_taps_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), c, h, w, kp, amax_scratch, xp, sx);
+      launch_taps<float>(static_cast<const float*>(x), c, h, w, g, amax_scratch, xp, sx, s);
       break;
     case XDNA_BF16:
       image_amax_kernel<__nv_bfloat16>
           <<<g_amax, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), per_image, amax_scratch);
-      to_taps_kernel<__nv_bfloat16>
-          <<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), c, h, w, kp, amax_scratch, xp, sx);
+      launch_taps<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), c, h, w, g, amax_scratch, xp, sx, s);
       break;
     case XDNA_F16:
       image_amax_kernel<__half><<<g_amax, 256, 0, s>>>(static_cast<const __half*>(x), per_image, amax_scratch);
-      to_taps_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(x), c, h, w, kp, amax_scratch, xp, sx);
+      launch_taps<__half>(static_cast<const __half*>(x), c, h, w, g, amax_scratch, xp, sx, s);
       break;
     default:
       return fail(XDNA_ERR_INVALID, "conv_quant_taps: x_dtype %d is not f32/bf16/f16", x_dtype);
