@@ -95,3 +95,36 @@ def test_codes_rebuild_the_oracle_conv_output(bias, relu, pool):
                            torch.from_numpy(b) if bias else None, 16)
     got = conv.codes_to_float(q, meta, relu_after=bias, pool=pool)
     assert got.dtype == torch.float32 and torch.equal(got, y)
+
+
+@pytest.mark.parametrize("bint", [False, True])
+@pytest.mark.parametrize("out_pool", [False, True])
+@pytest.mark.parametrize("kind", ["relu_after_bias", "fused_relu", "signed_biased"])
+def test_chain_fake_matches_the_op(kind, out_pool, bint):
+    """xdna::conv3x3_chain's shape function (what torch.compile traces with) gives the codes' dtype and the
+    meta vector's length the op produces: [sx, scale, bias] plus the next layer's maxima (one word more when
+    the next conv pools) exactly when the producer can compute them (conv.next_amax_ok), the int32-bias
+    option turning a ReLU after the bias into uint8 codes."""
+    import torch_xdna
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    n, ci, co, h, w = 2, 64, 32, 10, 12
+    relu, post_relu = (False, True) if kind == "relu_after_bias" else (True, False) if kind == "fused_relu" \
+        else (False, False)
+    has_bias = kind != "fused_relu"
+    cid = torch_xdna.ops.config_id(torch_xdna.Config(conv_bias_int32=bint))
+    cfg = torch_xdna.ops._configs[cid]
+    with FakeTensorMode():
+        x = torch.empty((n, h, w, ci), dtype=torch.int8)
+        xmeta = torch.empty((n + 2 * ci,), dtype=torch.float32)
+        wt = torch.empty((co, ci, 3, 3))
+        b = torch.empty((co,)) if has_bias else None
+        q, meta = torch.ops.xdna.conv3x3_chain(x, xmeta, wt, b, relu, cid, post_relu, conv.IN_CODES, True, True,
+                                               out_pool)
+    erelu, epost = conv.effective_relu(cfg, relu, b, post_relu)
+    fbias = None if conv.int32_bias(cfg, b) else b
+    assert q.shape == (n, h, w, co) and q.dtype == (torch.uint8 if erelu else torch.int8)
+    extra = n + (1 if out_pool else 0) if conv.next_amax_ok(erelu, fbias, epost, out_pool) else 0
+    assert meta.numel() == n + 2 * co + extra
+    # the consumer tells from the length alone whether the maxima are there (and cover a pool's region)
+    assert (meta.numel() == 2 * n + 2 * co + (1 if out_pool else 0)) == bool(extra)
