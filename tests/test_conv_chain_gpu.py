@@ -178,18 +178,21 @@ def test_image_pairs_equal_the_plain_layout(cuda, shape, kind):
     assert torch.equal(outs[0][1], outs[1][1])
 
 
+@pytest.mark.parametrize("c", [64, 256])
 @pytest.mark.parametrize("pool", [False, True])
 @pytest.mark.parametrize("relu_after", [True, False])
 @pytest.mark.parametrize("pairs", [False, True])
-def test_quantise_from_codes_matches_the_cpu(cuda, pool, relu_after, pairs):
+def test_quantise_from_codes_matches_the_cpu(cuda, c, pool, relu_after, pairs):
     """The quantise from codes on millions of values against the CPU: y rebuilt with torch's f32 operations
     in the epilogue's order (codes_to_float), the per-image max, and round(y / s) by IEEE division -- bit
     for bit. Large enough that a rounding difference of a few codes in 10^5 shows."""
     from torch_xdna import conv as xconv
     from torch_xdna import kernels
 
-    n, h, w, c = 4, 96, 104, 64
-    g = torch.Generator(device=cuda).manual_seed(3 + pool + 2 * relu_after + 4 * pairs)
+    if pairs and c != 64:
+        pytest.skip("image pairs are 64-channel layouts")
+    n, h, w = 4, 96, 104
+    g = torch.Generator(device=cuda).manual_seed(3 + pool + 2 * relu_after + 4 * pairs + c)
     q = torch.randint(-128, 128, (n, h, w, c), device=cuda, generator=g).to(torch.int8)
     scale = torch.rand(c, device=cuda, generator=g) * 1e-3 + 1e-4
     sx_in = torch.rand(n, device=cuda, generator=g) + 0.5
@@ -203,7 +206,7 @@ def test_quantise_from_codes_matches_the_cpu(cuda, pool, relu_after, pairs):
         kernels.conv_quant_codes_pairs(q, scale, sx_in, bias, relu_after, pool, xp2, sx, scratch, False)
         xp = xp2.view(n // 2, ho + 2, wo + 2, 2, 64).permute(0, 3, 1, 2, 4).reshape(n, ho + 2, wo + 2, 64)
     else:
-        xp = torch.empty(n, ho + 2, wo + 2, 64, dtype=torch.int8, device=cuda)
+        xp = torch.empty(n, ho + 2, wo + 2, c, dtype=torch.int8, device=cuda)
         kernels.conv_quant_codes(q, scale, sx_in, bias, relu_after, pool, xp, sx, scratch)
     y = xconv.codes_to_float(q, meta, relu_after, pool)                    # CPU, NCHW
     s = (y.abs().amax(dim=(1, 2, 3)).clamp(min=1e-8) / 127).float()
@@ -213,6 +216,25 @@ def test_quantise_from_codes_matches_the_cpu(cuda, pool, relu_after, pairs):
     bad = int((got != want).sum())
     assert bad == 0, f"{bad} of {want.numel()} quantised values differ"
     assert int(xp[:, 0].abs().sum()) == 0 and int(xp[:, :, 0].abs().sum()) == 0   # the zero border
+
+
+def test_quantise_through_the_table():
+    """The table kernel for the quantise from codes (chosen by size: large batches of large images) run
+    wherever it applies (XDNA_CODES_LUT=2, a fresh process since the library reads it once) through this
+    file's bit-exact tests of the quantise, the image pairs, the producers' maxima and the chain; and the
+    direct kernel alone (XDNA_CODES_LUT=0) through the quantise test."""
+    import os
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    for mode, sel in (("2", "quantise_from_codes or image_pairs or next_layer_maxima or chain_equals_unchained"),
+                      ("0", "quantise_from_codes")):
+        env = dict(os.environ, XDNA_CODES_LUT=mode)
+        out = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-p", "no:cacheprovider", "-m", "gpu",
+                              "-k", sel, os.path.join(here, "test_conv_chain_gpu.py")],
+                             env=env, capture_output=True, text=True, timeout=900)
+        assert out.returncode == 0, f"XDNA_CODES_LUT={mode}:\n{out.stdout[-3000:]}\n{out.stderr[-2000:]}"
 
 
 def test_compiled_vgg_block_chained_equals_unchained(cuda):

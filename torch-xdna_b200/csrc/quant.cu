@@ -694,6 +694,116 @@ __global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* _
   }
 }
 
+// The same quantise through a table, for C a multiple of 64: within one image a code's next-layer byte
+// depends only on the code's byte u (signed codes stored as code + 128) and its channel c, so a block
+// first evaluates byte(c, u) for its 64 channels (grid z: the channel slice) and all 256 u into 16 KB of
+// shared memory, with the arithmetic of codes_to_bordered16_kernel operation for operation (so the bytes
+// are the same), then maps each code with one byte permute and one shared-memory byte load instead of
+// ~11 floating-point operations. Row c of the table holds u at column u ^ (32 * (c / 16)): the four
+// 16-channel chunks a warp reads at once start 8 banks apart, and the XOR is applied to a whole word of
+// codes before the bytes are taken out. A block covers a contiguous range of bordered rows, flattened
+// into (row, pixel, chunk) elements; the row of an element comes from a multiply-high by wp_magic =
+// ceil(2^32 / Wp), exact while (rows x Wp) x (Wp - 1) < 2^32 (checked by the host).
+template <bool POOL, bool USGN, bool PAIRS = false>
+__global__ void __launch_bounds__(256, 5) codes_lut_kernel(const uint4* __restrict__ q, int H, int W, int C,
+                                                        const float* __restrict__ scale,
+                                                        const float* __restrict__ sx_in,
+                                                        const float* __restrict__ bias, int relu_after,
+                                                        const uint32_t* __restrict__ amax, uint4* __restrict__ xp,
+                                                        float* __restrict__ sx_out, uint32_t wp_magic) {
+  __shared__ __align__(16) uint8_t tbl[64 * 256];
+  const int n = blockIdx.y, sl = blockIdx.z;
+  const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
+  const int Wp = Wo + 2;
+  const int C16 = C / 16;
+  const float s = scale_from_amax(__uint_as_float(amax[n]));
+  const float r = __frcp_rn(s);
+  if (blockIdx.x == 0 && sl == 0 && threadIdx.x == 0) sx_out[n] = s;
+  const float sxn = __ldg(sx_in + n);
+  const float unbias = USGN ? 8388608.f : 8388736.f;  // 2^23 (+ 128: signed codes stored as code + 128)
+  for (int e = threadIdx.x; e < 64 * 64; e += 256) {  // four bytes u0 .. u0 + 3 of channel c per step
+    const int c = e >> 6, u0 = (e & 63) * 4;
+    const float t = __fmul_rn(__ldg(scale + sl * 64 + c), sxn);
+    const float b = bias != nullptr ? __ldg(bias + sl * 64 + c) : 0.f;
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float qf = __fsub_rn(__uint_as_float(0x4B000000u | static_cast<uint32_t>(u0 + i)), unbias);
+      float y = __fadd_rn(__fmul_rn(qf, t), b);
+      if (relu_after) y = y > 0.f ? y : 0.f;
+      v[i] = quant_t(y, s, r);
+    }
+    *reinterpret_cast<uint32_t*>(tbl + c * 256 + (u0 ^ ((c >> 4) << 5))) = pack_bytes(v[0], v[1], v[2], v[3]);
+  }
+  __syncthreads();
+
+  const int chunk = threadIdx.x & 3;  // a thread keeps one 16-channel chunk of the slice
+  const uint32_t flip = USGN ? 0u : 0x80808080u;
+  const uint32_t swz = 0x20202020u * static_cast<uint32_t>(chunk);
+  const uint32_t rowb = static_cast<uint32_t>(chunk) << 12;  // row 16 * chunk of the table, << 8
+  const int col = sl * 4 + chunk;                             // 16-byte column within a pixel
+  const int rows = Ho + 2;
+  const int y0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * rows / gridDim.x);
+  const int y1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * rows / gridDim.x);
+  const int total = (y1 - y0) * Wp * 4;
+  auto load = [&](int yb, int xb) {  // the chunk's 16 codes as stored bytes (pooled: the 2x2 max)
+    if constexpr (!POOL) {
+      const uint4 u = __ldg(q + ((static_cast<int64_t>(n) * H + (yb - 1)) * W + (xb - 1)) * C16 + col);
+      return make_uint4(u.x ^ flip, u.y ^ flip, u.z ^ flip, u.w ^ flip);
+    } else {
+      const int64_t p0 = ((static_cast<int64_t>(n) * H + 2 * (yb - 1)) * W + 2 * (xb - 1)) * C16 + col;
+      const int64_t row = static_cast<int64_t>(W) * C16;
+      const uint4 a = __ldg(q + p0), bq = __ldg(q + p0 + C16), c = __ldg(q + p0 + row), d = __ldg(q + p0 + row + C16);
+      auto mx = [&](uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+        return __vmaxu4(__vmaxu4(w0 ^ flip, w1 ^ flip), __vmaxu4(w2 ^ flip, w3 ^ flip));
+      };
+      return make_uint4(mx(a.x, bq.x, c.x, d.x), mx(a.y, bq.y, c.y, d.y), mx(a.z, bq.z, c.z, d.z),
+                        mx(a.w, bq.w, c.w, d.w));
+    }
+  };
+  auto convert = [&](const uint4& u) {
+    const uint32_t wi[4] = {u.x ^ swz, u.y ^ swz, u.z ^ swz, u.w ^ swz};
+    uint32_t wo[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = tbl[__byte_perm(wi[k], rowb, 0x7650u + i) + (4 * k + i) * 256];
+      wo[k] = __byte_perm(__byte_perm(o[0], o[1], 0x0040), __byte_perm(o[2], o[3], 0x0040), 0x5410);
+    }
+    return make_uint4(wo[0], wo[1], wo[2], wo[3]);
+  };
+  constexpr int U = POOL ? 2 : 4;  // 16-byte vectors per thread in flight (a pooled one is four loads)
+  for (int g0 = threadIdx.x; g0 < total; g0 += U * blockDim.x) {
+    uint4 u[U];
+    bool in[U];
+    int64_t at[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {  // all loads first
+      const int g = g0 + j * blockDim.x;
+      const uint32_t px = static_cast<uint32_t>(g) >> 2;
+      const int yl = static_cast<int>(__umulhi(px, wp_magic));
+      const int xb = static_cast<int>(px) - yl * Wp, yb = y0 + yl;
+      in[j] = g < total && yb >= 1 && yb <= Ho && xb >= 1 && xb <= Wo;
+      at[j] = PAIRS ? ((static_cast<int64_t>(n >> 1) * rows + yb) * Wp + xb) * 2 * C16 + (n & 1) * C16 + col
+                    : ((static_cast<int64_t>(n) * rows + yb) * Wp + xb) * C16 + col;
+      u[j] = in[j] ? load(yb, xb) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      if (g0 + j * static_cast<int>(blockDim.x) < total) xp[at[j]] = in[j] ? convert(u[j]) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// XDNA_CODES_LUT: 0 = never the table kernel, 2 = wherever it applies, else (default) where it pays.
+static int codes_lut() {
+  static const int mode = [] {
+    const char* e = std::getenv("XDNA_CODES_LUT");
+    return e == nullptr ? 1 : e[0] == '0' ? 0 : e[0] == '2' ? 2 : 1;
+  }();
+  return mode;
+}
+
 template <bool POOL, bool USGN>
 static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const float* scale, const float* sx_in,
                          const float* bias, int relu_after, int Cp, uint32_t* amax, int8_t* xp, float* sx_out,
@@ -705,7 +815,30 @@ static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const f
     codes_amax_kernel<POOL, USGN><<<dim3(chunks, N), 256, 0, s>>>(q, H, W, C4, scale, sx_in, bias, relu_after, amax);
   const int C = 4 * C4;
   const bool pow2 = C >= 16 && C <= 4096 && (C & (C - 1)) == 0;
-  if (pow2 && Cp == C && reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(xp) % 16 == 0) {
+  const bool al16 = reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(xp) % 16 == 0;
+  const int Wp = (POOL ? W / 2 : W) + 2;
+  const int slices = C / 64;
+  // the table kernel: five blocks per SM over all (image, slice) pairs (its 48 registers and 16 KB allow it;
+  // warps, not bytes in flight, hide its load -> table -> store latency). It pays where a block maps at
+  // least one table's worth of codes, or where many (image, slice) pairs leave each block few rows (the
+  // direct kernel is then worse still); a small batch of large images keeps the direct kernel.
+  const int pairs_ns = N * std::max(slices, 1);
+  const int parts = std::max(1, std::min(Ho + 2, 148 * 5 / std::max(pairs_ns, 1)));
+  const int64_t codes_per_block = static_cast<int64_t>(Ho) * (Wp - 2) * 64 / parts;
+  if (codes_lut() != 0 && C % 64 == 0 && slices <= 65535 && Cp == C && al16 &&
+      (codes_lut() == 2 || codes_per_block >= 16384 || pairs_ns >= 128) &&
+      static_cast<int64_t>(Ho + 2) * Wp * (Wp - 1) < (int64_t{1} << 32)) {
+    const uint32_t magic = static_cast<uint32_t>(((uint64_t{1} << 32) + Wp - 1) / Wp);
+    const dim3 grid(parts, N, slices);
+    if (pairs)
+      codes_lut_kernel<POOL, USGN, true><<<grid, 256, 0, s>>>(reinterpret_cast<const uint4*>(q), H, W, C, scale,
+                                                               sx_in, bias, relu_after, amax,
+                                                               reinterpret_cast<uint4*>(xp), sx_out, magic);
+    else
+      codes_lut_kernel<POOL, USGN><<<grid, 256, 0, s>>>(reinterpret_cast<const uint4*>(q), H, W, C, scale, sx_in,
+                                                         bias, relu_after, amax, reinterpret_cast<uint4*>(xp),
+                                                         sx_out, magic);
+  } else if (pow2 && Cp == C && al16) {
     // one wave: three resident blocks per SM over all images, each walking several rows
     const int blocks = std::max(1, std::min(Ho + 2, 148 * 3 / std::max(N, 1)));
     if (pairs)
