@@ -188,3 +188,32 @@ def test_compiled_cnn(cuda):
     with torch.no_grad():
         want = net.down(torch.from_numpy(r3["y"]).to(cuda))
     assert torch.equal(y, want)
+
+
+@pytest.mark.parametrize("c", [1, 2, 3, 4, 5, 7])
+@pytest.mark.parametrize("n,h,w", [(2, 9, 13), (3, 33, 47), (1, 4, 300)])
+def test_quant_taps_layout(cuda, c, n, h, w):
+    """The first layer's input with the 3x3 stencil's taps packed into each bordered pixel's row, byte for
+    byte: row (yb, xb) holds, for tap t = 3 dy + dx and channel ch, the oracle's int8 of input pixel
+    (yb - 2 + dy, xb - 2 + dx) at byte C t + ch (zero outside the image and past byte 9 C). C <= 4 takes
+    the row-per-block kernel, C >= 5 the pixel-per-thread one."""
+    from torch_xdna import kernels
+
+    x, _, _ = mg.conv_inputs(300 + c + h, n, c, 8, h, w)
+    kp = (9 * c + 15) // 16 * 16
+    xp = torch.full((n, h + 2, w + 2, kp), 77, dtype=torch.int8, device=cuda)
+    sx = torch.empty((n,), dtype=torch.float32, device=cuda)
+    scratch = torch.empty((n,), dtype=torch.int32, device=cuda)
+    kernels.conv_quant_taps(t(x, cuda), xp, sx, scratch)
+    q, s = orc.conv_quant(x)
+    assert np.array_equal(sx.cpu().numpy(), s)
+    pad = np.zeros((n, c, h + 4, w + 4), dtype=np.int8)     # input pixel (y, x) at (y + 2, x + 2)
+    pad[:, :, 2:h + 2, 2:w + 2] = q
+    want = np.zeros((n, h + 2, w + 2, kp), dtype=np.int8)
+    for tap in range(9):
+        dy, dx = divmod(tap, 3)
+        # bordered pixel (yb, xb) reads input (yb - 2 + dy, xb - 2 + dx) = pad[yb + dy, xb + dx]
+        want[..., tap * c:(tap + 1) * c] = pad[:, :, dy:dy + h + 2, dx:dx + w + 2].transpose(0, 2, 3, 1)
+    got = xp.cpu().numpy()
+    bad = int((got != want).sum())
+    assert bad == 0, f"{bad} of {got.size} bytes differ"

@@ -895,9 +895,68 @@ __global__ void __launch_bounds__(256) bias_int32_kernel(const T* __restrict__ b
   }
 }
 
+// The same taps, one block per bordered row yb for C <= 4: the three input rows yb - 2 .. yb that the row's
+// stencils read are quantised once into shared memory, one word per pixel (channel c in byte c, zero
+// outside the image; columns -2 .. W + 1), and each pixel's 9 C bytes are assembled from nine of those
+// words with constant shifts. An input value is quantised three times (once per row block reading it)
+// instead of nine, and loaded as one coalesced row instead of per stencil. grid (H + 2, N), shared memory
+// 3 (W + 4) words.
+template <typename T, int C>
+__global__ void __launch_bounds__(256) to_taps_rows_kernel(const T* __restrict__ x, int H, int W,
+                                                           const uint32_t* __restrict__ amax,
+                                                           int8_t* __restrict__ xp, float* __restrict__ sx) {
+  static_assert(C >= 1 && C <= 4, "one word per pixel");
+  constexpr int Kp = (9 * C + 15) / 16 * 16;
+  extern __shared__ uint32_t rows_sm[];  // [3][W + 4]
+  const int n = blockIdx.y, yb = blockIdx.x;
+  const int Wp = W + 2, Ws = W + 4;
+  const float s = scale_from_amax(__uint_as_float(amax[n]));
+  const float r = __frcp_rn(s);
+  if (yb == 0 && threadIdx.x == 0) sx[n] = s;
+  for (int e = threadIdx.x; e < 3 * Ws; e += blockDim.x) {
+    const int dy = e / Ws, xi = e - dy * Ws;
+    const int y = yb - 2 + dy, xx = xi - 2;
+    uint32_t word = 0;
+    if (y >= 0 && y < H && xx >= 0 && xx < W) {
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+        word |= (quant_byte(to_f32(x[((static_cast<int64_t>(n) * C + c) * H + y) * W + xx]), s, r) & 0xFFu) << (8 * c);
+    }
+    rows_sm[e] = word;
+  }
+  __syncthreads();
+  for (int xb = threadIdx.x; xb < Wp; xb += blockDim.x) {
+    uint32_t words[Kp / 4];
+#pragma unroll
+    for (int i = 0; i < Kp / 4; ++i) words[i] = 0;
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {  // tap t's C bytes at byte C t of the row: input column xb - 2 + t % 3
+      const uint32_t p = rows_sm[(t / 3) * Ws + xb + t % 3];
+      constexpr int kBits = 8 * C;
+      const int bit = kBits * t, i = bit >> 5, sh = bit & 31;
+      words[i] |= p << sh;
+      if (sh + kBits > 32) words[i + 1] |= p >> (32 - sh);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(xp + (static_cast<int64_t>(n) * (H + 2) * Wp + static_cast<int64_t>(yb) * Wp + xb) * Kp);
+#pragma unroll
+    for (int i = 0; i < Kp / 16; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+  }
+}
+
 template <typename T>
 static void launch_taps(const T* x, int C, int H, int W, dim3 g, const uint32_t* amax, int8_t* xp, float* sx,
                         cudaStream_t s) {
+  const size_t rows_smem = static_cast<size_t>(3) * (W + 4) * sizeof(uint32_t);
+  if (C <= 4 && rows_smem <= 48 * 1024 && H + 2 <= 2147483647) {
+    const dim3 gr(static_cast<unsigned>(H + 2), g.y);
+    switch (C) {
+      case 1: to_taps_rows_kernel<T, 1><<<gr, 256, rows_smem, s>>>(x, H, W, amax, xp, sx); break;
+      case 2: to_taps_rows_kernel<T, 2><<<gr, 256, rows_smem, s>>>(x, H, W, amax, xp, sx); break;
+      case 3: to_taps_rows_kernel<T, 3><<<gr, 256, rows_smem, s>>>(x, H, W, amax, xp, sx); break;
+      default: to_taps_rows_kernel<T, 4><<<gr, 256, rows_smem, s>>>(x, H, W, amax, xp, sx); break;
+    }
+    return;
+  }
   switch (C) {
     case 1: to_taps_kernel<T, 1><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
     case 2: to_taps_kernel<T, 2><<<g, 256, 0, s>>>(x, H, W, amax, xp, sx); break;
