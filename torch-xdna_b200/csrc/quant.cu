@@ -694,6 +694,13 @@ __global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* _
   }
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t smem, const void* gmem, bool fill) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem), "l"(gmem), "r"(fill ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // The same quantise through a table, for C a multiple of 64: within one image a code's next-layer byte
 // depends only on the code's byte u (signed codes stored as code + 128) and its channel c, so a block
 // first evaluates byte(c, u) for its 64 channels (grid z: the channel slice) and all 256 u into 16 KB of
@@ -704,14 +711,27 @@ __global__ void __launch_bounds__(256) codes_to_bordered16_kernel(const uint4* _
 // codes before the bytes are taken out. A block covers a contiguous range of bordered rows, flattened
 // into (row, pixel, chunk) elements; the row of an element comes from a multiply-high by wp_magic =
 // ceil(2^32 / Wp), exact while (rows x Wp) x (Wp - 1) < 2^32 (checked by the host).
+// The codes are prefetched into shared memory, not registers: each thread owns a ring of kRingStages x 4
+// sixteen-byte slots (slot (stage, v) of thread t at [(stage * 4 + v) * 256 + t], so a warp's slot reads
+// are conflict-free) and fills them with cp.async, zero-filling what lies outside the image; two stages
+// are in flight while it converts the third, the first two while the block builds its table. A thread
+// reads only its own slots and waits only on its own copies (cp.async.wait_group), so the ring needs no
+// barrier; a slot is refilled one iteration after it was read, once the stores that used its codes have
+// issued. Pooled, a stage holds the four codes vectors of one output vector. Dynamic shared memory: the
+// 16 KB table, then the 48 KB ring (three blocks per SM).
+constexpr int kRingStages = 3;
+constexpr size_t kRingSmem = 64 * 256 + static_cast<size_t>(kRingStages) * 4 * 256 * 16;
+
 template <bool POOL, bool USGN, bool PAIRS = false>
-__global__ void __launch_bounds__(256, 5) codes_lut_kernel(const uint4* __restrict__ q, int H, int W, int C,
-                                                        const float* __restrict__ scale,
-                                                        const float* __restrict__ sx_in,
-                                                        const float* __restrict__ bias, int relu_after,
-                                                        const uint32_t* __restrict__ amax, uint4* __restrict__ xp,
-                                                        float* __restrict__ sx_out, uint32_t wp_magic) {
-  __shared__ __align__(16) uint8_t tbl[64 * 256];
+__global__ void __launch_bounds__(256, 3) codes_lut_kernel(const uint4* __restrict__ q, int H, int W, int C,
+                                                           const float* __restrict__ scale,
+                                                           const float* __restrict__ sx_in,
+                                                           const float* __restrict__ bias, int relu_after,
+                                                           const uint32_t* __restrict__ amax, uint4* __restrict__ xp,
+                                                           float* __restrict__ sx_out, uint32_t wp_magic) {
+  extern __shared__ __align__(16) uint8_t ring_sm[];
+  uint8_t* tbl = ring_sm;
+  uint4* ring = reinterpret_cast<uint4*>(ring_sm + 64 * 256);
   const int n = blockIdx.y, sl = blockIdx.z;
   const int Ho = POOL ? H / 2 : H, Wo = POOL ? W / 2 : W;
   const int Wp = Wo + 2;
@@ -719,9 +739,52 @@ __global__ void __launch_bounds__(256, 5) codes_lut_kernel(const uint4* __restri
   const float s = scale_from_amax(__uint_as_float(amax[n]));
   const float r = __frcp_rn(s);
   if (blockIdx.x == 0 && sl == 0 && threadIdx.x == 0) sx_out[n] = s;
+  const int chunk = threadIdx.x & 3;
+  const uint32_t flip = USGN ? 0u : 0x80808080u;
+  const uint32_t swz = 0x20202020u * static_cast<uint32_t>(chunk);
+  const uint32_t rowb = static_cast<uint32_t>(chunk) << 12;
+  const int col = sl * 4 + chunk;
+  const int rows = Ho + 2;
+  const int y0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * rows / gridDim.x);
+  const int y1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * rows / gridDim.x);
+  const int total = (y1 - y0) * Wp * 4;
+  constexpr int U = POOL ? 1 : 4;  // output vectors per stage (a pooled one reads four)
+  const int step = U * static_cast<int>(blockDim.x);
+  auto pixel = [&](int g, int& yb, int& xb, bool& in) {
+    const uint32_t px = static_cast<uint32_t>(g) >> 2;
+    const int yl = static_cast<int>(__umulhi(px, wp_magic));
+    xb = static_cast<int>(px) - yl * Wp;
+    yb = y0 + yl;
+    in = g < total && yb >= 1 && yb <= Ho && xb >= 1 && xb <= Wo;
+  };
+  const uint32_t ring_base = static_cast<uint32_t>(__cvta_generic_to_shared(ring)) + threadIdx.x * 16;
+  auto issue = [&](int g0, int stage) {  // the codes of elements g0, g0 + 256, ... into the stage's slots
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      int yb, xb;
+      bool in;
+      pixel(g0 + j * static_cast<int>(blockDim.x), yb, xb, in);
+      if constexpr (!POOL) {
+        const uint4* src = in ? q + ((static_cast<int64_t>(n) * H + (yb - 1)) * W + (xb - 1)) * C16 + col : q;
+        cp_async16(ring_base + (stage * 4 + j) * 256 * 16, src, in);
+      } else {
+        const int64_t p0 = in ? ((static_cast<int64_t>(n) * H + 2 * (yb - 1)) * W + 2 * (xb - 1)) * C16 + col : 0;
+        const int64_t row = in ? static_cast<int64_t>(W) * C16 : 0;
+        const int64_t off[4] = {p0, p0 + (in ? C16 : 0), p0 + row, p0 + row + (in ? C16 : 0)};
+#pragma unroll
+        for (int v = 0; v < 4; ++v) cp_async16(ring_base + (stage * 4 + v) * 256 * 16, q + off[v], in);
+      }
+    }
+    cp_async_commit();
+  };
+  // the first stages' copies are in flight while the block builds its table
+  int g_issue = threadIdx.x;
+#pragma unroll
+  for (int st = 0; st < kRingStages - 1; ++st, g_issue += step) issue(g_issue, st);
+
   const float sxn = __ldg(sx_in + n);
-  const float unbias = USGN ? 8388608.f : 8388736.f;  // 2^23 (+ 128: signed codes stored as code + 128)
-  for (int e = threadIdx.x; e < 64 * 64; e += 256) {  // four bytes u0 .. u0 + 3 of channel c per step
+  const float unbias = USGN ? 8388608.f : 8388736.f;
+  for (int e = threadIdx.x; e < 64 * 64; e += 256) {
     const int c = e >> 6, u0 = (e & 63) * 4;
     const float t = __fmul_rn(__ldg(scale + sl * 64 + c), sxn);
     const float b = bias != nullptr ? __ldg(bias + sl * 64 + c) : 0.f;
@@ -737,30 +800,6 @@ __global__ void __launch_bounds__(256, 5) codes_lut_kernel(const uint4* __restri
   }
   __syncthreads();
 
-  const int chunk = threadIdx.x & 3;  // a thread keeps one 16-channel chunk of the slice
-  const uint32_t flip = USGN ? 0u : 0x80808080u;
-  const uint32_t swz = 0x20202020u * static_cast<uint32_t>(chunk);
-  const uint32_t rowb = static_cast<uint32_t>(chunk) << 12;  // row 16 * chunk of the table, << 8
-  const int col = sl * 4 + chunk;                             // 16-byte column within a pixel
-  const int rows = Ho + 2;
-  const int y0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * rows / gridDim.x);
-  const int y1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * rows / gridDim.x);
-  const int total = (y1 - y0) * Wp * 4;
-  auto load = [&](int yb, int xb) {  // the chunk's 16 codes as stored bytes (pooled: the 2x2 max)
-    if constexpr (!POOL) {
-      const uint4 u = __ldg(q + ((static_cast<int64_t>(n) * H + (yb - 1)) * W + (xb - 1)) * C16 + col);
-      return make_uint4(u.x ^ flip, u.y ^ flip, u.z ^ flip, u.w ^ flip);
-    } else {
-      const int64_t p0 = ((static_cast<int64_t>(n) * H + 2 * (yb - 1)) * W + 2 * (xb - 1)) * C16 + col;
-      const int64_t row = static_cast<int64_t>(W) * C16;
-      const uint4 a = __ldg(q + p0), bq = __ldg(q + p0 + C16), c = __ldg(q + p0 + row), d = __ldg(q + p0 + row + C16);
-      auto mx = [&](uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
-        return __vmaxu4(__vmaxu4(w0 ^ flip, w1 ^ flip), __vmaxu4(w2 ^ flip, w3 ^ flip));
-      };
-      return make_uint4(mx(a.x, bq.x, c.x, d.x), mx(a.y, bq.y, c.y, d.y), mx(a.z, bq.z, c.z, d.z),
-                        mx(a.w, bq.w, c.w, d.w));
-    }
-  };
   auto convert = [&](const uint4& u) {
     const uint32_t wi[4] = {u.x ^ swz, u.y ^ swz, u.z ^ swz, u.w ^ swz};
     uint32_t wo[4];
@@ -773,26 +812,42 @@ __global__ void __launch_bounds__(256, 5) codes_lut_kernel(const uint4* __restri
     }
     return make_uint4(wo[0], wo[1], wo[2], wo[3]);
   };
-  constexpr int U = POOL ? 2 : 4;  // 16-byte vectors per thread in flight (a pooled one is four loads)
-  for (int g0 = threadIdx.x; g0 < total; g0 += U * blockDim.x) {
+  int stage = 0;
+  for (int g0 = threadIdx.x; g0 < total; g0 += step) {
+    cp_async_wait<kRingStages - 2>();  // this stage's group has landed
     uint4 u[U];
-    bool in[U];
-    int64_t at[U];
 #pragma unroll
-    for (int j = 0; j < U; ++j) {  // all loads first
-      const int g = g0 + j * blockDim.x;
-      const uint32_t px = static_cast<uint32_t>(g) >> 2;
-      const int yl = static_cast<int>(__umulhi(px, wp_magic));
-      const int xb = static_cast<int>(px) - yl * Wp, yb = y0 + yl;
-      in[j] = g < total && yb >= 1 && yb <= Ho && xb >= 1 && xb <= Wo;
-      at[j] = PAIRS ? ((static_cast<int64_t>(n >> 1) * rows + yb) * Wp + xb) * 2 * C16 + (n & 1) * C16 + col
-                    : ((static_cast<int64_t>(n) * rows + yb) * Wp + xb) * C16 + col;
-      u[j] = in[j] ? load(yb, xb) : make_uint4(0u, 0u, 0u, 0u);
+    for (int j = 0; j < U; ++j) {
+      const uint4* slot = ring + (stage * 4 + j) * 256 + threadIdx.x;
+      if constexpr (!POOL) {
+        const uint4 a = slot[0];
+        u[j] = make_uint4(a.x ^ flip, a.y ^ flip, a.z ^ flip, a.w ^ flip);
+      } else {
+        const uint4 a = slot[0], b = slot[256], c = slot[512], d = slot[768];
+        auto mx = [&](uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+          return __vmaxu4(__vmaxu4(w0 ^ flip, w1 ^ flip), __vmaxu4(w2 ^ flip, w3 ^ flip));
+        };
+        u[j] = make_uint4(mx(a.x, b.x, c.x, d.x), mx(a.y, b.y, c.y, d.y), mx(a.z, b.z, c.z, d.z), mx(a.w, b.w, c.w, d.w));
+      }
     }
+    // refill the slots read one iteration ago (an empty group past the end keeps the count uniform)
+    issue(g_issue, (stage + kRingStages - 1) % kRingStages);
+    g_issue += step;
 #pragma unroll
-    for (int j = 0; j < U; ++j)
-      if (g0 + j * static_cast<int>(blockDim.x) < total) xp[at[j]] = in[j] ? convert(u[j]) : make_uint4(0u, 0u, 0u, 0u);
+    for (int j = 0; j < U; ++j) {
+      const int g = g0 + j * static_cast<int>(blockDim.x);
+      int yb, xb;
+      bool in;
+      pixel(g, yb, xb, in);
+      if (g < total) {
+        const int64_t at = PAIRS ? ((static_cast<int64_t>(n >> 1) * rows + yb) * Wp + xb) * 2 * C16 + (n & 1) * C16 + col
+                                 : ((static_cast<int64_t>(n) * rows + yb) * Wp + xb) * C16 + col;
+        xp[at] = in ? convert(u[j]) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    stage = stage + 1 == kRingStages ? 0 : stage + 1;
   }
+  cp_async_wait<0>();  // no copy outlives the block
 }
 
 // XDNA_CODES_LUT: 0 = never the table kernel, 2 = wherever it applies, else (default) where it pays.
@@ -818,26 +873,34 @@ static void launch_codes(const uint32_t* q, int N, int H, int W, int C4, const f
   const bool al16 = reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(xp) % 16 == 0;
   const int Wp = (POOL ? W / 2 : W) + 2;
   const int slices = C / 64;
-  // the table kernel: five blocks per SM over all (image, slice) pairs (its 48 registers and 16 KB allow it;
-  // warps, not bytes in flight, hide its load -> table -> store latency). It pays where a block maps at
-  // least one table's worth of codes, or where many (image, slice) pairs leave each block few rows (the
-  // direct kernel is then worse still); a small batch of large images keeps the direct kernel.
+  // the table kernel: three blocks per SM (64 KB of shared memory each) over all (image, slice) pairs. It
+  // pays where a block maps at least one table's worth of codes, or where many (image, slice) pairs leave
+  // each block few rows (the direct kernel is then worse still); a small batch of large images keeps the
+  // direct kernel.
   const int pairs_ns = N * std::max(slices, 1);
-  const int parts = std::max(1, std::min(Ho + 2, 148 * 5 / std::max(pairs_ns, 1)));
+  const int parts = std::max(1, std::min(Ho + 2, 148 * 3 / std::max(pairs_ns, 1)));
   const int64_t codes_per_block = static_cast<int64_t>(Ho) * (Wp - 2) * 64 / parts;
   if (codes_lut() != 0 && C % 64 == 0 && slices <= 65535 && Cp == C && al16 &&
       (codes_lut() == 2 || codes_per_block >= 16384 || pairs_ns >= 128) &&
       static_cast<int64_t>(Ho + 2) * Wp * (Wp - 1) < (int64_t{1} << 32)) {
     const uint32_t magic = static_cast<uint32_t>(((uint64_t{1} << 32) + Wp - 1) / Wp);
     const dim3 grid(parts, N, slices);
+    static const bool attr = [] {  // 64 KB of dynamic shared memory
+      cudaFuncSetAttribute(codes_lut_kernel<POOL, USGN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kRingSmem));
+      cudaFuncSetAttribute(codes_lut_kernel<POOL, USGN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kRingSmem));
+      return true;
+    }();
+    (void)attr;
     if (pairs)
-      codes_lut_kernel<POOL, USGN, true><<<grid, 256, 0, s>>>(reinterpret_cast<const uint4*>(q), H, W, C, scale,
+      codes_lut_kernel<POOL, USGN, true><<<grid, 256, kRingSmem, s>>>(reinterpret_cast<const uint4*>(q), H, W, C,
+                                                                     scale, sx_in, bias, relu_after, amax,
+                                                                     reinterpret_cast<uint4*>(xp), sx_out, magic);
+    else
+      codes_lut_kernel<POOL, USGN><<<grid, 256, kRingSmem, s>>>(reinterpret_cast<const uint4*>(q), H, W, C, scale,
                                                                sx_in, bias, relu_after, amax,
                                                                reinterpret_cast<uint4*>(xp), sx_out, magic);
-    else
-      codes_lut_kernel<POOL, USGN><<<grid, 256, 0, s>>>(reinterpret_cast<const uint4*>(q), H, W, C, scale, sx_in,
-                                                         bias, relu_after, amax, reinterpret_cast<uint4*>(xp),
-                                                         sx_out, magic);
   } else if (pow2 && Cp == C && al16) {
     // one wave: three resident blocks per SM over all images, each walking several rows
     const int blocks = std::max(1, std::min(Ho + 2, 148 * 3 / std::max(N, 1)));
