@@ -1010,8 +1010,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t IDESC = BF16 ? idesc_bf16(MMA_M, BN) : idesc_i8(MMA_M, BN);
   constexpr int KSTEPS = KB / 32;  // one MMA consumes 32 bytes of K (32 int8 or 16 bf16)
   constexpr int K_ELEMS = BF16 ? KB / 2 : KB;
-  constexpr int WCOLS = BN / 2;          // columns per epilogue warp
-  constexpr int NCH = WCOLS / 32;        // 32-column chunks per epilogue warp
+  // Epilogue groups: for the conv with resident weights, 64 output channels and int8 codes out (the first
+  // layers of an image net: a tile is one or a few K blocks, so the epilogue sets the pace), warps 2-5 and
+  // 6-9 drain alternate tiles, each group its own accumulator (group g: buffer g) and each warp all 64
+  // columns of its 32 rows, so two tiles' epilogues overlap; an accumulator is released by four warps.
+  constexpr bool kGroups = EPI == EPI_CONV_QNHWC && RBM == 1 && BN == 64 && !PAIR;
+  constexpr int WCOLS = kGroups ? BN : BN / 2;  // columns per epilogue warp
+  constexpr int NCH = WCOLS / 32;               // 32-column chunks per epilogue warp
   static_assert(NCH >= 1 && NCH <= 4, "BN must be 64, 128 or 256");
 
   extern __shared__ uint8_t smem_raw[];
@@ -1047,7 +1052,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < NACC; ++b) {
       mbar_init(tfull + b, 1);
-      mbar_init(tempty + b, PAIR ? 2 * kEpiWarps : kEpiWarps);  // a pair: both CTAs' epilogue warps
+      mbar_init(tempty + b, PAIR ? 2 * kEpiWarps : kGroups ? kEpiWarps / 2 : kEpiWarps);  // a pair: both CTAs' warps
     }
     mbar_init(drain, 1);
     mbar_init(bres, 1);
@@ -1295,7 +1300,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..9)
     const int ew = warp - 2;
     const int q = warp & 3;          // the TMEM lane quadrant this warp may read
-    const int half = ew >> 2;        // which half of the tile's columns
+    const int half = kGroups ? 0 : ew >> 2;   // which half of the tile's columns
+    const int group = kGroups ? ew >> 2 : 0;  // with epilogue groups: which of the alternate tiles
+    const int t_first_e = t_begin + group * t_inc;
+    const int t_next = (kGroups ? 2 : 1) * t_inc;
     uint8_t* obuf = smOut + ew * OUTB;
     // The tile's column factors in shared memory: EPI_DEQ through TMA (with 4 KB per warp one staging
     // slot and the factors in the second 2 KB; with 8 KB two slots and the factors behind them) and
@@ -1322,7 +1330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(bar);
     };
     const bool has_bias = args.bias != nullptr;
-    int buf = 0;
+    int buf = group;
     uint32_t bphase = 0;
     // Per-row and per-column factors of a tile (and, for the conv, where its pixel sits). Loaded one
     // tile ahead: right after this warp's accumulator for tile t is ready, the loads for the next
@@ -1358,14 +1366,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       return f;
     };
     Factors fac{};
-    if (t_begin < t_end) fac = load_factors(t_begin);
+    if (t_first_e < t_end) fac = load_factors(t_first_e);
     NextMax<NCH> nm;  // EPI_CONV_QNHWC with XDNA_CONV_NEXT_AMAX
     nm.img = -1;
     nm.nb = 0;
     NextMax<NCH> nm1;  // PIMG: the odd images' maxima (nm: the even images')
     nm1.img = -1;
     nm1.nb = 0;
-    for (int t = t_begin; t < t_end; t += t_inc) {
+    for (int t = t_first_e; t < t_end; t += t_next) {
       int mb, nb;
       tile_coords(t, args.m_tiles, args.n_tiles, mb, nb);
       const int row0 = tile_row0(mb) + q * 32;
@@ -1401,7 +1409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (!mbar_wait<PAIR>(tfull + buf, bphase, abort_flag, args.err, 6)) break;
       tc_fence_after();
-      if (t + t_inc < t_end) fac = load_factors(t + t_inc);
+      if (t + t_next < t_end) fac = load_factors(t + t_next);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + half * WCOLS);
       if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
@@ -1562,7 +1570,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c + 1 < NCH) tmem_ld_wait();
       }
       }  // generic chunk loop
-      if (++buf == NACC) {
+      if constexpr (kGroups) {
+        bphase ^= 1;  // this group's accumulator comes back every other tile
+      } else if (++buf == NACC) {
         buf = 0;
         bphase ^= 1;
       }
