@@ -37,6 +37,9 @@ CASES = [
     # an even batch: the 64-channel convs read their input in image pairs (XDNA_CONV_PAIRS), pooled or not
     ([(64, 3), (64, 64), (128, 64), (64, 128), (64, 64)], [True, True, True, False, True],
      [False, False, True, False, True], 30, 26, 4),
+    # ~420 tiles of the first conv (taps packed, codes out) over 148 SMs: two or three per CTA, so both of
+    # its epilogue warp groups drain tiles, unevenly, and images change inside a CTA's range
+    ([(64, 3), (64, 64)], [True, True], [False, False], 80, 80, 8),
 ]
 
 
